@@ -1,0 +1,527 @@
+"""Benchmark: NF4 decode GEMV GB/s on B200 (one replica per GPU).
+
+Workload (`config.workload`): the decode-time NF4 projections of the S2-Pro
+slow AR - per layer wqkv 6144x2560, wo 2560x4096 (+residual), w1 9728x2560,
+w3 9728x2560 (silu-gate epilogue on w1's output), w2 2560x9728 (+residual),
+blocksize 64 with double-quantised scales - at M=1, in the decode block's
+launch order. A step is one pass over 36 distinct layers (1.87 GB of NF4
+weights, far larger than the 126 MB L2, so every step streams from HBM),
+captured once as a CUDA graph of C-ABI calls. Weights ~ N(0, 0.02) and
+activations ~ N(0, 1), seeded per layer and rank (synthetic; no checkpoint).
+
+value  = algorithmic bytes of all ranks' steps / max-over-ranks device time
+e2e    = the same metric through the C ABI with host buffers: every step
+         copies its inputs from pinned host memory, replays the calls and
+         reads every output back to pinned host memory, inside the timed region.
+
+`--impl reference` times the reference's own CPU NF4 kernel (nf4cpu.nf4_gemv,
+built into oracle/_ref) on the host cores over the same workload definition.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "nf4_decode_gemv_GBps"
+UNIT = "GB/s"
+N_LAYERS = 36
+# (name, out, in, epilogue): epilogue 0 none, 1 residual, 2 silu-gate on the previous output
+PROJ = [("wqkv", 6144, 2560, 0), ("wo", 2560, 4096, 1), ("w1", 9728, 2560, 0),
+        ("w3", 9728, 2560, 2), ("w2", 2560, 9728, 1)]
+BS, BS2 = 64, 256
+
+
+def algorithmic_bytes(n: int, k: int, rows: int = 1, epi: int = 0, nested: bool = True) -> int:
+    """Bytes a matmul must move: packed codes + scales + x + y (+ operand)."""
+    nb = n * k // BS
+    scales = (nb + 4 * math.ceil(nb / BS2) + 1024) if nested else 4 * nb
+    return n * k // 2 + scales + 2 * rows * k + 2 * rows * n + (2 * rows * n if epi else 0)
+
+
+STEP_BYTES = N_LAYERS * sum(algorithmic_bytes(n, k, 1, e) for _, n, k, e in PROJ)
+LAUNCHES_PER_STEP = N_LAYERS * len(PROJ)
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# --------------------------------------------------------------------------
+# distributed plumbing (one process per GPU; replicas, no data-path collective)
+# --------------------------------------------------------------------------
+
+
+def dist_init(backend: str):
+    import torch.distributed as dist
+
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws > 1 and not dist.is_initialized():
+        from datetime import timedelta
+
+        dist.init_process_group(backend=backend, timeout=timedelta(seconds=300))
+    return int(os.environ.get("RANK", "0")), ws, int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def max_over_ranks(v: float, device) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier():
+    import torch.distributed as dist
+
+    if dist.is_initialized():
+        dist.barrier()
+
+
+# --------------------------------------------------------------------------
+# clocks during the timed region
+# --------------------------------------------------------------------------
+
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.idx = set(gpu_indices)
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in open(self.path):
+                f = [c.strip() for c in line.split(",")]
+                if len(f) < 9 or not f[0].isdigit() or int(f[0]) not in self.idx:
+                    continue
+                rows.append(f)
+        except Exception:  # noqa: BLE001
+            pass
+        finally:
+            if self.path:
+                os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        load = [s for s in sm if mx and s > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(load) if load else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows),
+                "power_w_max": max((num(r[3]) or 0.0) for r in rows)}
+
+
+# --------------------------------------------------------------------------
+# the GPU arm
+# --------------------------------------------------------------------------
+
+
+def make_layers(device, rank: int):
+    """36 layers x 5 NF4 projections (nested scales), generated on the device."""
+    import torch
+
+    from ttspipe_b200 import nf4gemv
+    from ttspipe_b200.quant import Linear4bit
+
+    layers = []
+    for li in range(N_LAYERS):
+        mods = []
+        for pi, (_, n, k, _) in enumerate(PROJ):
+            g = torch.Generator(device=device).manual_seed(1_000_003 * rank + 100 * li + pi)
+            w = torch.randn(n, k, generator=g, device=device) * 0.02
+            lin = Linear4bit.from_float(w, double_quant=True)
+            del w
+            assert nf4gemv.prepare(lin)
+            mods.append(lin)
+        layers.append(mods)
+    torch.cuda.synchronize(device)
+    return layers
+
+
+class StepIO:
+    """All of a step's inputs and outputs in two flat device buffers (and
+    pinned host mirrors for the end-to-end measurement)."""
+
+    def __init__(self, device, rank: int):
+        import torch
+
+        self.in_specs, self.out_specs = [], []
+        off_in = off_out = 0
+        for _ in range(N_LAYERS):
+            for _, n, k, e in PROJ:
+                x_off = off_in
+                off_in += k
+                op_off = None
+                if e == 1:
+                    op_off = off_in
+                    off_in += n
+                self.in_specs.append((x_off, k, op_off, n))
+                self.out_specs.append((off_out, n))
+                off_out += n
+        g = torch.Generator(device=device).manual_seed(77 + rank)
+        self.dev_in = torch.randn(off_in, generator=g, device=device).to(torch.bfloat16)
+        self.dev_out = torch.zeros(off_out, dtype=torch.bfloat16, device=device)
+        self.host_in = torch.empty(off_in, dtype=torch.bfloat16, pin_memory=True)
+        self.host_in.copy_(self.dev_in.cpu())
+        self.host_out = torch.empty(off_out, dtype=torch.bfloat16, pin_memory=True)
+        self.h2d_bytes = self.dev_in.numel() * 2
+        self.d2h_bytes = self.dev_out.numel() * 2
+
+
+def issue_step(layers, io: StepIO, ws, stream_ptr):
+    """One step through the C ABI: 36 layers x 5 nf4b_gemm calls."""
+    from ttspipe_b200 import _lib
+
+    L = _lib.lib()
+    i = 0
+    ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
+    in_base, out_base = io.dev_in.data_ptr(), io.dev_out.data_ptr()
+    for mods in layers:
+        prev_out = None
+        for lin, (_, n, k, e) in zip(mods, PROJ):
+            x_off, _, op_off, _ = io.in_specs[i]
+            y_off, _ = io.out_specs[i]
+            y_ptr = out_base + 2 * y_off
+            operand = None
+            if e == 1:
+                operand = in_base + 2 * op_off
+            elif e == 2:
+                operand = prev_out
+            desc = lin._nf4_fast["desc"]
+            st = L.nf4b_gemm(ctypes.byref(desc), in_base + 2 * x_off, y_ptr, 1, e, operand,
+                             ws_ptr, ws_bytes, stream_ptr)
+            if st != 0:
+                raise RuntimeError(f"nf4b_gemm failed: {_lib.last_error()}")
+            prev_out = y_ptr
+            i += 1
+
+
+def roofline_traffic():
+    """Per-launch DRAM traffic of the GEMV from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "nf4_gemv_decode_traffic.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["dram_bytes_per_launch"])
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def measured_peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except Exception:  # noqa: BLE001
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def run_gpu(args):
+    import torch
+
+    from ttspipe_b200 import _lib, nf4gemv
+
+    rank, world, local = dist_init("nccl")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    assert nf4gemv.available(), "libnf4b200.so must load on a B200"
+
+    t0 = time.time()
+    layers = make_layers(device, rank)
+    io = StepIO(device, rank)
+    need = max(int(_lib.lib().nf4b_gemm_workspace_size(ctypes.byref(m._nf4_fast["desc"]), 1))
+               for m in layers[0])
+    ws = torch.zeros(need, dtype=torch.uint8, device=device)
+    log(f"[rank {rank}] built {N_LAYERS} layers in {time.time() - t0:.1f}s; step bytes {STEP_BYTES / 1e9:.3f} GB")
+
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        issue_step(layers, io, ws, stream.cuda_stream)   # eager warm-up of every call
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        graph.capture_begin()
+        issue_step(layers, io, ws, stream.cuda_stream)
+        graph.capture_end()
+    stream.synchronize()
+
+    def timed(fn, steps):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize(device)
+        start.record(stream)
+        for _ in range(steps):
+            fn()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+        return start.elapsed_time(end) / 1e3  # seconds
+
+    def step_graph():
+        with torch.cuda.stream(stream):
+            graph.replay()
+
+    def step_e2e():
+        with torch.cuda.stream(stream):
+            io.dev_in.copy_(io.host_in, non_blocking=True)
+            graph.replay()
+            io.host_out.copy_(io.dev_out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step_graph()
+    torch.cuda.synchronize(device)
+
+    with ClockSampler([local] if world == 1 else list(range(world))) as clocks:
+        secs = timed(step_graph, args.steps)
+    clock = clocks.summary()
+    for _ in range(max(1, args.warmup)):
+        step_e2e()
+    e2e_secs = timed(step_e2e, args.steps)
+
+    secs_max = max_over_ranks(secs, device)
+    e2e_max = max_over_ranks(e2e_secs, device)
+    value = world * STEP_BYTES * args.steps / secs_max / 1e9
+    e2e_value = world * STEP_BYTES * args.steps / e2e_max / 1e9
+    per_rank = STEP_BYTES * args.steps / secs / 1e9
+
+    # per-projection timing (eager, events around 20 launches of one shape over
+    # rotating layers) - printed to stderr for the profile notes only
+    if rank == 0 and args.detail:
+        for pi, (name, n, k, e) in enumerate(PROJ):
+            st, en = torch.cuda.Event(True), torch.cuda.Event(True)
+            reps = 36
+            with torch.cuda.stream(stream):
+                st.record(stream)
+                for r in range(reps):
+                    lin = layers[r % N_LAYERS][pi]
+                    x_off, _, op_off, _ = io.in_specs[(r % N_LAYERS) * len(PROJ) + pi]
+                    desc = lin._nf4_fast["desc"]
+                    opnd = io.dev_in.data_ptr() + 2 * op_off if e == 1 else (io.dev_out.data_ptr() if e == 2 else None)
+                    _lib.lib().nf4b_gemm(ctypes.byref(desc), io.dev_in.data_ptr() + 2 * x_off,
+                                         io.dev_out.data_ptr(), 1, e, opnd, ws.data_ptr(), ws.numel(),
+                                         stream.cuda_stream)
+                en.record(stream)
+            torch.cuda.synchronize(device)
+            us = st.elapsed_time(en) * 1e3 / reps
+            b = algorithmic_bytes(n, k, 1, e)
+            log(f"  {name} {n}x{k}: {us:.2f} us/launch, {b / us / 1e3:.0f} GB/s (eager, back to back)")
+
+    peaks, peak_kind = measured_peaks()
+    hbm = float(peaks["hbm_gbs"])
+    achieved = STEP_BYTES / (secs / args.steps) / 1e9
+    traffic = roofline_traffic()
+    result = None
+    if rank == 0:
+        result = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(secs_max / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init NF4 weights N(0,0.02), activations N(0,1), seeded per rank)",
+            "config": {"workload": "S2-Pro slow-AR decode projections: 36 layers x [wqkv 6144x2560, "
+                                   "wo 2560x4096 +res, w1 9728x2560, w3 9728x2560 silu-gate, w2 2560x9728 +res], "
+                                   "M=1, NF4 bs64 + double-quant (bs2 256)",
+                       "baseline_config": "configs[1] (one slow-AR layer's linears at M=1) x 36 distinct layers",
+                       "bytes_per_step": STEP_BYTES, "rows": 1,
+                       "l2": "inputs larger than L2 (1.87 GB of weights per step per GPU)",
+                       "parallelism": f"replicas x{world} (no collective on the data path)"},
+            "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": io.h2d_bytes,
+                    "d2h_bytes_per_step": io.d2h_bytes,
+                    "path": "C ABI nf4b_gemm calls (CUDA graph) + pinned H2D inputs + D2H outputs per step"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "peak_source": peak_kind,
+                         "traffic": traffic,
+                         "algorithmic_bytes_per_launch": STEP_BYTES // LAUNCHES_PER_STEP,
+                         "kernel": "nf4_gemv_kernel<1> (all launches of the step)"},
+            "clocks": clock,
+            "per_rank_GBps": round(per_rank, 1),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    del graph
+    import torch.distributed as dist
+
+    if dist.is_initialized():
+        barrier()
+        dist.destroy_process_group()
+    return result
+
+
+# --------------------------------------------------------------------------
+# the CPU reference: the reference's own nf4cpu kernels (oracle/_ref)
+# --------------------------------------------------------------------------
+
+
+def _cpu_layers(count: int):
+    """Random packed NF4 bytes and bf16 absmax for `count` layers, generated
+    directly as the reference's own CPU test does (tests/test_nf4cpu.py:31-35);
+    the kernel's speed does not depend on the values."""
+    import torch
+
+    layers = []
+    for li in range(count):
+        g = torch.Generator().manual_seed(li)
+        mods = []
+        for _, n, k, _ in PROJ:
+            packed = torch.randint(0, 255, (n, k // 2), dtype=torch.uint8, generator=g)
+            absmax = (torch.rand(n, k // 64, generator=g) * 0.1).to(torch.bfloat16)
+            mods.append((packed, absmax, n, k))
+        layers.append(mods)
+    return layers
+
+
+def _reference_ext():
+    from oracle import build_ref
+
+    return build_ref.load()
+
+
+def cpu_gemv_runner():
+    """(callable(x, packed, absmax, n) -> y, kind, note)."""
+    import torch
+
+    from oracle import nf4_oracle as orc
+
+    code16 = torch.tensor(orc.NF4_CODE).to(torch.bfloat16)
+    try:
+        ext = _reference_ext()
+        return (lambda x, p, a, n: ext.nf4_gemv(x, p, a, code16, n)), "reference", \
+            "reference app/engine/nf4cpu.py nf4_gemv (AVX-512 BF16), built by oracle/build_ref.py"
+    except Exception as exc:  # noqa: BLE001
+        def port(x, p, a, n):
+            y = orc.nf4cpu_gemv(x.view(torch.int16).numpy().view("uint16"), p.numpy(),
+                                a.view(torch.int16).numpy().view("uint16"),
+                                code16.view(torch.int16).numpy().view("uint16"))
+            return torch.from_numpy(y.view("int16")).view(torch.bfloat16)
+        return port, "port", f"oracle port (numpy), reference unavailable: {exc}"
+
+
+def cpu_baseline(seconds: float) -> dict:
+    import torch
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    run, kind, note = cpu_gemv_runner()
+    layers = _cpu_layers(4)
+    xs = {k: torch.randn(1, k).to(torch.bfloat16) for _, _, k, _ in PROJ}
+    for mods in layers[:1]:
+        for p, a, n, k in mods:
+            run(xs[k], p, a, n)
+    done_bytes, t0 = 0, time.perf_counter()
+    li = 0
+    while time.perf_counter() - t0 < seconds:
+        for p, a, n, k in layers[li % len(layers)]:
+            run(xs[k], p, a, n)
+        done_bytes += sum(algorithmic_bytes(n, k, 1, e) for _, n, k, e in PROJ)
+        li += 1
+    el = time.perf_counter() - t0
+    return {"value": round(done_bytes / el / 1e9, 2), "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{li} layer passes (5 projections each, 4 distinct layers cycled, M=1) in {el:.1f}s; {note}"}
+
+
+def run_reference(args):
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    run, kind, note = cpu_gemv_runner()
+    n_layers = N_LAYERS if kind == "reference" else 2
+    layers = _cpu_layers(n_layers)
+    xs = {k: torch.randn(1, k).to(torch.bfloat16) for _, _, k, _ in PROJ}
+
+    def step():
+        for mods in layers:
+            for p, a, n, k in mods:
+                run(xs[k], p, a, n)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    step_bytes = n_layers * sum(algorithmic_bytes(n, k, 1, e) for _, n, k, e in PROJ)
+    value = step_bytes * args.steps / el / 1e9
+    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1, "impl": "reference",
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random packed NF4 bytes, bf16 absmax, x N(0,1))",
+            "config": {"workload": f"{n_layers} layers x [wqkv 6144x2560, wo 2560x4096, w1/w3 9728x2560, "
+                                   "w2 2560x9728], M=1, NF4 bs64 (bf16 absmax, as the reference's CPU path)",
+                       "bytes_per_step": step_bytes},
+            "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads, "kind": kind,
+                             "sample": f"{args.steps} steps of {n_layers} layers; {note}"},
+            "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--detail", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        res = run_reference(args)
+    else:
+        res = run_gpu(args)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

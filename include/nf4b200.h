@@ -1,0 +1,159 @@
+/*
+ * nf4b200.h - C ABI of the B200 (sm_100a) NF4 hot-path library (libnf4b200.so).
+ *
+ * The reference (bitNtech/ttspipe) reaches its kernels through Python ctypes
+ * and the CUDA driver API (app/engine/nvrtc.py:184-199). This library replaces
+ * those NVRTC-compiled kernels with nvcc-built sm_100a ones behind plain C
+ * entry points: pointers and sizes only, no torch types, no exceptions.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor pointers are device pointers, contiguous, row-major.
+ *   - Activations are bf16 (uint16 bit patterns); accumulation is fp32.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Nothing here
+ *     synchronises the host or allocates device memory, so every call can be
+ *     captured into a CUDA graph.
+ *   - Return 0 on success or a negative NF4B_ERR_* code; the message of the
+ *     last failure on the calling thread is nf4b_last_error().
+ */
+#ifndef NF4B200_H
+#define NF4B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. Argument errors are detected on the host before any launch. */
+#define NF4B_OK 0
+#define NF4B_ERR_ARG (-1)         /* null pointer or out-of-range scalar      */
+#define NF4B_ERR_SHAPE (-2)       /* shape the kernels do not serve           */
+#define NF4B_ERR_ALIGN (-3)       /* pointer not aligned as required          */
+#define NF4B_ERR_DTYPE (-4)       /* dtype the kernels do not serve           */
+#define NF4B_ERR_WORKSPACE (-5)   /* workspace missing or too small           */
+#define NF4B_ERR_LAUNCH (-6)      /* CUDA launch / runtime error              */
+#define NF4B_ERR_DEVICE (-7)      /* current device is not sm_100             */
+
+/* Epilogues fused into the matmul's store (app/engine/nf4gemv.py:424). */
+#define NF4B_EPI_NONE 0
+#define NF4B_EPI_RESIDUAL 1   /* y = operand + x W^T                          */
+#define NF4B_EPI_SILU_GATE 2  /* y = silu(operand) * x W^T                    */
+
+/* Element types of the rotary table (app/engine/fusedops.py:96-101). */
+#define NF4B_F32 0
+#define NF4B_F16 1
+#define NF4B_BF16 2
+
+/*
+ * One bitsandbytes NF4 weight, read in place (app/engine/nf4gemv.py:343-377
+ * lists the QuantState fields the reference reads).
+ *   packed      uint8 [n_out, k_in/2]; byte j = (q[2j] << 4) | q[2j+1]
+ *   nested = 0: absmax fp32 [n_out * k_in / blocksize]; absmax_code, code2 unused
+ *   nested = 1: absmax_code uint8 [n_out * k_in / blocksize] (QuantState.absmax),
+ *               absmax fp32 [ceil(nblocks / blocksize2)] (state2.absmax),
+ *               code2 fp32 [256] (state2.code), offset (QuantState.offset);
+ *               scale[b] = code2[absmax_code[b]] * absmax[b / blocksize2] + offset
+ *   blocksize, blocksize2: powers of two; blocksize >= 64; k_in % blocksize == 0
+ */
+typedef struct nf4b_weight {
+  const uint8_t* packed;
+  const uint8_t* absmax_code;
+  const float* absmax;
+  const float* code2;
+  float offset;
+  int32_t n_out;
+  int32_t k_in;
+  int32_t blocksize;
+  int32_t blocksize2;
+  int32_t nested;
+} nf4b_weight;
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int nf4b_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* nf4b_last_error(void);
+
+/*
+ * The library's device error word: non-zero after a kernel gave up on a
+ * bounded wait (a pipeline barrier that never completed). Synchronises the
+ * device to read it; `clear` resets it. No counterpart in the reference,
+ * whose kernels have no waits.
+ */
+int nf4b_device_error(int clear);
+
+/*
+ * Y[rows, n_out] = epi(X[rows, k_in] . dequant(W)^T).
+ * Replaces the `nf4_mma` launch of nf4gemv.matmul (app/engine/nf4gemv.py:427-479):
+ * rows <= 32 (decode and batched decode) run the streaming GEMV, larger row
+ * counts the tcgen05 GEMM. `operand` has Y's shape (epi != NONE).
+ * `workspace` must hold nf4b_gemm_workspace_size(w, rows) bytes and be zeroed
+ * once before its first use; every call leaves it zeroed again. One workspace
+ * per stream: calls that overlap on the GPU must not share one.
+ */
+int nf4b_gemm(const nf4b_weight* w, const void* x, void* y, int rows, int epi,
+              const void* operand, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace nf4b_gemm needs for this weight and row count. */
+size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows);
+
+/*
+ * out[n_out, k_in] = RNE_bf16(NF4[q] * scale) - bitsandbytes' dequantize_4bit
+ * to bf16 (the per-element value of app/engine/nf4gemv.py:185-188 in bf16).
+ */
+int nf4b_dequantize(const nf4b_weight* w, void* out, void* stream);
+
+/*
+ * y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * weight) over the last axis of
+ * x[rows, width]. Replaces fusedops.rms_norm (app/engine/fusedops.py:61-95,
+ * :169-196).
+ */
+int nf4b_rms_norm(const void* x, const void* weight, void* y, int rows, int width, float eps,
+                  void* stream);
+
+/*
+ * Interleaved-pair rotary embedding of x[batch, seq, heads, head_dim] against
+ * freqs[seq, head_dim/2, 2] = (cos, sin) of type freqs_dtype. Bit-exact to the
+ * unfused fp32 formula. Replaces fusedops.rope (app/engine/fusedops.py:103-132,
+ * :199-236).
+ */
+int nf4b_rope(const void* x, const void* freqs, int freqs_dtype, void* y, int batch, int seq,
+              int heads, int head_dim, void* stream);
+
+/*
+ * One decode position: optional per-head RMSNorm of q and k (q_norm_w/k_norm_w
+ * may be NULL), rotary on q and k, q -> q_out[n_head, head_dim], k and v into
+ * the caches [n_kv, max_len, head_dim] at row *pos (read on the device, so a
+ * captured graph serves every position). Replaces fusedlayer's `qk_rope_kv`
+ * (app/engine/fusedlayer.py:56-92). head_dim must be 128.
+ */
+int nf4b_qk_rope_kv(const void* qkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                    const void* freqs, int freqs_dtype, const int64_t* pos, void* q_out,
+                    void* k_cache, void* v_cache, int n_head, int n_kv, int head_dim, int max_len,
+                    void* stream);
+
+/*
+ * Grouped-query attention of one query position over cache rows [0, L) with
+ * L = min(*pos + 1, window) when `pos` is given (read on the device, so one
+ * captured graph serves every position) and L = window otherwise; rows whose
+ * `mask` byte is 0 are skipped (mask may be NULL = all visible). Query head h
+ * reads KV head h / (n_head / n_kv). Caches are [n_kv, max_len, head_dim]
+ * (max_len = the head stride in rows). out is bf16 [n_head, head_dim].
+ * Replaces fusedlayer's attn_partial + attn_combine (app/engine/fusedlayer.py:95-157)
+ * and fastpath.decode_attention for one query (app/engine/fastpath.py:133-174).
+ * `workspace` must hold nf4b_decode_attention_workspace_size(...) bytes, zeroed
+ * once before first use; calls leave it zeroed.
+ */
+int nf4b_decode_attention(const void* q, const void* k_cache, const void* v_cache,
+                          const int64_t* pos, const uint8_t* mask, void* out, int n_head, int n_kv,
+                          int head_dim, int max_len, int window, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+size_t nf4b_decode_attention_workspace_size(int n_head, int head_dim, int window);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NF4B200_H */

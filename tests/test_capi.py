@@ -1,0 +1,111 @@
+"""The C ABI library loads on a CPU-only machine, exports every symbol the
+header declares, and rejects bad arguments on the host with a status and a
+message - before it ever needs a GPU."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from ttspipe_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "nf4b200.h"
+
+
+def declared_symbols() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"^\w[\w\s\*]*?\b(nf4b_\w+)\s*\(", text, flags=re.M))
+
+
+def test_header_and_binding_agree():
+    assert declared_symbols() == set(_lib.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (nf4b_\w+)", out))
+    missing = declared_symbols() - exported
+    assert not missing, missing
+    assert lib.nf4b_version() >= 100
+
+
+def _weight(**kw):
+    w = _lib.Nf4Weight()
+    buf = ctypes.create_string_buffer(4096 + 16)
+    base = (ctypes.addressof(buf) + 15) // 16 * 16
+    w.packed, w.absmax = base, base
+    w.n_out, w.k_in, w.blocksize, w.blocksize2, w.nested = 64, 256, 64, 256, 0
+    for k, v in kw.items():
+        setattr(w, k, v)
+    return w, buf
+
+
+@pytest.mark.parametrize("field,value,status", [
+    ("blocksize", 96, -2),      # not a power of two (tests/test_nf4gemv.py:207-221)
+    ("blocksize", 32, -2),      # below 64
+    ("k_in", 100, -2),          # not a multiple of the blocksize
+    ("n_out", 0, -2),           # empty
+    ("nested", 1, -1),          # nested without codes
+])
+def test_gemm_rejects_bad_weights_on_the_host(field, value, status):
+    w, _keep = _weight(**{field: value})
+    x = ctypes.create_string_buffer(1024)
+    st = _lib.lib().nf4b_gemm(ctypes.byref(w), ctypes.addressof(x), ctypes.addressof(x), 1, 0,
+                              None, None, 0, None)
+    assert st == status
+    assert _lib.last_error()
+
+
+def test_gemm_rejects_misaligned_packed_weight():
+    w, _keep = _weight()
+    w.packed = w.packed + 1
+    st = _lib.lib().nf4b_gemm(ctypes.byref(w), w.absmax, w.absmax, 1, 0, None, None, 0, None)
+    assert st == _lib_err("ALIGN")
+
+
+def _lib_err(name):
+    return {"ARG": -1, "SHAPE": -2, "ALIGN": -3, "DTYPE": -4, "WORKSPACE": -5, "LAUNCH": -6,
+            "DEVICE": -7}[name]
+
+
+def test_gemm_rejects_null_and_unknown_epilogue():
+    w, _keep = _weight()
+    L = _lib.lib()
+    assert L.nf4b_gemm(None, None, None, 1, 0, None, None, 0, None) == -1
+    assert L.nf4b_gemm(ctypes.byref(w), None, w.absmax, 1, 0, None, None, 0, None) == -1
+    assert L.nf4b_gemm(ctypes.byref(w), w.absmax, w.absmax, 1, 7, None, None, 0, None) == -1
+    assert L.nf4b_gemm(ctypes.byref(w), w.absmax, w.absmax, 1, 1, None, None, 0, None) == -1
+    assert L.nf4b_gemm(ctypes.byref(w), w.absmax, w.absmax, 0, 0, None, None, 0, None) == -2
+
+
+def test_workspace_size_grows_with_rows_and_is_zero_for_the_gemm_path():
+    w, _keep = _weight(n_out=9728, k_in=2560)
+    L = _lib.lib()
+    s1 = L.nf4b_gemm_workspace_size(ctypes.byref(w), 1)
+    s32 = L.nf4b_gemm_workspace_size(ctypes.byref(w), 32)
+    assert 0 < s1 < s32
+    assert L.nf4b_gemm_workspace_size(ctypes.byref(w), 33) == 0
+    assert L.nf4b_decode_attention_workspace_size(32, 128, 2048) > 0
+
+
+def test_other_entry_points_reject_bad_arguments():
+    L = _lib.lib()
+    buf = ctypes.create_string_buffer(4096 + 16)
+    p = (ctypes.addressof(buf) + 15) // 16 * 16
+    assert L.nf4b_rms_norm(None, p, p, 1, 8, 1e-6, None) == -1
+    assert L.nf4b_rms_norm(p, p, p, 0, 8, 1e-6, None) == -2
+    assert L.nf4b_rope(p, p, 9, p, 1, 1, 1, 8, None) == -4
+    assert L.nf4b_rope(p, p, 0, p, 1, 1, 1, 7, None) == -2
+    assert L.nf4b_qk_rope_kv(p, None, None, 1e-6, p, 2, p, p, p, p, 32, 8, 64, 16, None) == -2
+    assert L.nf4b_qk_rope_kv(p, p, None, 1e-6, p, 2, p, p, p, p, 32, 8, 128, 16, None) == -1
+    assert L.nf4b_decode_attention(p, p, p, p, None, p, 32, 8, 64, 16, 16, p, 1 << 20, None) == -2
+    assert L.nf4b_decode_attention(p, p, p, p, None, p, 12, 8, 128, 16, 16, p, 1 << 20, None) == -2
+    assert L.nf4b_decode_attention(p, p, p, p, None, p, 32, 8, 128, 16, 32, p, 1 << 20, None) == -2
+    assert L.nf4b_decode_attention(p, p, p, p, None, p, 32, 8, 128, 16, 16, p, 16, None) == -5
+    assert L.nf4b_dequantize(None, p, None) == -1

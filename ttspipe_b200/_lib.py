@@ -1,0 +1,110 @@
+"""ctypes binding of ``libnf4b200.so`` (the C ABI in ``include/nf4b200.h``).
+
+The library is the only compute path: if it is missing or fails to load, every
+entry point here raises instead of falling back to anything else.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libnf4b200.so"
+
+NF4B_OK = 0
+NF4B_EPI_NONE, NF4B_EPI_RESIDUAL, NF4B_EPI_SILU_GATE = 0, 1, 2
+NF4B_F32, NF4B_F16, NF4B_BF16 = 0, 1, 2
+
+#: Every symbol the header declares; the CPU tests check the library exports all of them.
+EXPORTS = (
+    "nf4b_version",
+    "nf4b_last_error",
+    "nf4b_device_error",
+    "nf4b_gemm",
+    "nf4b_gemm_workspace_size",
+    "nf4b_dequantize",
+    "nf4b_rms_norm",
+    "nf4b_rope",
+    "nf4b_qk_rope_kv",
+    "nf4b_decode_attention",
+    "nf4b_decode_attention_workspace_size",
+)
+
+
+class Nf4Weight(ctypes.Structure):
+    """`nf4b_weight`: one bitsandbytes NF4 weight, by pointer."""
+
+    _fields_ = [
+        ("packed", ctypes.c_void_p),
+        ("absmax_code", ctypes.c_void_p),
+        ("absmax", ctypes.c_void_p),
+        ("code2", ctypes.c_void_p),
+        ("offset", ctypes.c_float),
+        ("n_out", ctypes.c_int32),
+        ("k_in", ctypes.c_int32),
+        ("blocksize", ctypes.c_int32),
+        ("blocksize2", ctypes.c_int32),
+        ("nested", ctypes.c_int32),
+    ]
+
+
+class Nf4bError(RuntimeError):
+    """A non-zero status from the library, with its message."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"nf4b status {status}: {message}")
+        self.status = status
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def _declare(lib) -> None:
+    vp, i32, f32, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+    wp = ctypes.POINTER(Nf4Weight)
+    sig = {
+        "nf4b_version": (i32, []),
+        "nf4b_last_error": (ctypes.c_char_p, []),
+        "nf4b_device_error": (i32, [i32]),
+        "nf4b_gemm": (i32, [wp, vp, vp, i32, i32, vp, vp, sz, vp]),
+        "nf4b_gemm_workspace_size": (sz, [wp, i32]),
+        "nf4b_dequantize": (i32, [wp, vp, vp]),
+        "nf4b_rms_norm": (i32, [vp, vp, vp, i32, i32, f32, vp]),
+        "nf4b_rope": (i32, [vp, vp, i32, vp, i32, i32, i32, i32, vp]),
+        "nf4b_qk_rope_kv": (i32, [vp, vp, vp, f32, vp, i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
+        "nf4b_decode_attention": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, sz, vp]),
+        "nf4b_decode_attention_workspace_size": (sz, [i32, i32, i32]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+
+
+def lib():
+    """The loaded library. Raises if it has not been built or cannot load."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{LIB_PATH.name} is not built; run `python -m ttspipe_b200.build` "
+                    "(the NF4 kernels have no other implementation)")
+            handle = ctypes.CDLL(str(LIB_PATH))
+            _declare(handle)
+            _lib = handle
+    return _lib
+
+
+def check(status: int) -> None:
+    """Raise Nf4bError for a non-zero status."""
+    if status != NF4B_OK:
+        raise Nf4bError(status, lib().nf4b_last_error().decode(errors="replace"))
+
+
+def last_error() -> str:
+    return lib().nf4b_last_error().decode(errors="replace")

@@ -1,0 +1,290 @@
+// The C ABI of libnf4b200.so (declared in include/nf4b200.h).
+//
+// Every entry point validates its arguments on the host and returns a status
+// instead of throwing: shape, alignment and dtype problems are reported before
+// anything is launched, so a caller can decline and fall back exactly where the
+// reference returns None (app/engine/nf4gemv.py:315-376, :436-455). A launch
+// failure returns NF4B_ERR_LAUNCH, the analogue of the reference's RuntimeError
+// on a non-zero cuLaunchKernel status (app/engine/nf4gemv.py:476-477).
+
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace nf4b {
+int read_device_error(int clear);
+}
+
+using namespace nf4b;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int ok() {
+  g_err[0] = '\0';
+  return NF4B_OK;
+}
+
+bool is_pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
+int log2i(int v) {
+  int s = 0;
+  while ((1 << s) < v) ++s;
+  return s;
+}
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_device() {
+  static int checked[64] = {};  // 0 unknown, 1 ok, -1 bad
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(NF4B_ERR_DEVICE, "no current CUDA device");
+  if (checked[dev] == 0) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    checked[dev] = (major == 10 && minor == 0) ? 1 : -1;
+  }
+  if (checked[dev] < 0)
+    return fail(NF4B_ERR_DEVICE, "device %d is not sm_100 (this library is built for sm_100a)", dev);
+  return NF4B_OK;
+}
+
+int check_weight(const nf4b_weight* w) {
+  if (w == nullptr || w->packed == nullptr || w->absmax == nullptr)
+    return fail(NF4B_ERR_ARG, "weight descriptor or its packed/absmax pointer is null");
+  if (w->n_out <= 0 || w->k_in <= 0) return fail(NF4B_ERR_SHAPE, "empty weight %dx%d", w->n_out, w->k_in);
+  if (!is_pow2(w->blocksize) || w->blocksize < 64)
+    return fail(NF4B_ERR_SHAPE, "blocksize %d is not a power of two >= 64", w->blocksize);
+  if (w->k_in % w->blocksize || w->k_in % 64)
+    return fail(NF4B_ERR_SHAPE, "in_features %d is not a multiple of 64 and of the blocksize %d",
+                w->k_in, w->blocksize);
+  if (!aligned(w->packed, 16)) return fail(NF4B_ERR_ALIGN, "packed weight is not 16-byte aligned");
+  if (w->nested) {
+    if (w->absmax_code == nullptr || w->code2 == nullptr)
+      return fail(NF4B_ERR_ARG, "nested weight without absmax codes or code2 table");
+    if (!is_pow2(w->blocksize2))
+      return fail(NF4B_ERR_SHAPE, "second-level blocksize %d is not a power of two", w->blocksize2);
+  }
+  return NF4B_OK;
+}
+
+int launch_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(NF4B_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+int current_sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  return gemv_sm_count(dev);
+}
+
+}  // namespace
+
+extern "C" {
+
+int nf4b_version(void) { return 100; }
+
+const char* nf4b_last_error(void) { return g_err; }
+
+int nf4b_device_error(int clear) { return read_device_error(clear); }
+
+size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows) {
+  if (w == nullptr || rows <= 0 || w->n_out <= 0 || w->k_in <= 0) return 0;
+  if (rows > GEMV_MAX_ROWS) return 0;
+  GemvPlan plan;
+  gemv_plan(w->n_out, w->k_in, rows, current_sm_count(), &plan);
+  return plan.counter_bytes + plan.partial_bytes;
+}
+
+int nf4b_gemm(const nf4b_weight* w, const void* x, void* y, int rows, int epi, const void* operand,
+              void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_weight(w);
+  if (st) return st;
+  if (x == nullptr || y == nullptr) return fail(NF4B_ERR_ARG, "x or y is null");
+  if (rows <= 0) return fail(NF4B_ERR_SHAPE, "rows must be positive (got %d)", rows);
+  if (epi < NF4B_EPI_NONE || epi > NF4B_EPI_SILU_GATE) return fail(NF4B_ERR_ARG, "unknown epilogue %d", epi);
+  if (epi != NF4B_EPI_NONE && operand == nullptr)
+    return fail(NF4B_ERR_ARG, "epilogue %d needs an operand", epi);
+  if (!aligned(x, 16)) return fail(NF4B_ERR_ALIGN, "x is not 16-byte aligned");
+  if (!aligned(y, 2) || (operand && !aligned(operand, 2)))
+    return fail(NF4B_ERR_ALIGN, "y/operand not 2-byte aligned");
+  if ((st = check_device())) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+
+  if (rows <= GEMV_MAX_ROWS) {
+    GemvPlan plan;
+    gemv_plan(w->n_out, w->k_in, rows, current_sm_count(), &plan);
+    const size_t need = plan.counter_bytes + plan.partial_bytes;
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(NF4B_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need,
+                  workspace ? workspace_bytes : (size_t)0);
+    if (!aligned(workspace, 256)) return fail(NF4B_ERR_ALIGN, "workspace is not 256-byte aligned");
+    GemvParams p;
+    p.packed = w->packed;
+    p.a8 = w->absmax_code;
+    p.absmax = w->absmax;
+    p.code2 = w->code2;
+    p.offset = w->offset;
+    p.N = w->n_out;
+    p.K = w->k_in;
+    p.nested = w->nested ? 1 : 0;
+    p.bs_shift = log2i(w->blocksize);
+    p.bs2_shift = w->nested ? log2i(w->blocksize2) : 0;
+    p.x = static_cast<const uint16_t*>(x);
+    p.y = static_cast<uint16_t*>(y);
+    p.operand = static_cast<const uint16_t*>(operand);
+    p.M = rows;
+    p.epi = epi;
+    p.counters = static_cast<int*>(workspace);
+    p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.counter_bytes);
+    p.units = plan.units;
+    p.warps_total = plan.warps_total;
+    p.blocks_per_tile = w->k_in / 64;
+    return launch_status(launch_gemv(p, plan.grid, s), "nf4 gemv launch");
+  }
+
+  GemmParams p;
+  p.packed = w->packed;
+  p.a8 = w->absmax_code;
+  p.absmax = w->absmax;
+  p.code2 = w->code2;
+  p.offset = w->offset;
+  p.N = w->n_out;
+  p.K = w->k_in;
+  p.nested = w->nested ? 1 : 0;
+  p.bs_shift = log2i(w->blocksize);
+  p.bs2_shift = w->nested ? log2i(w->blocksize2) : 0;
+  p.x = static_cast<const uint16_t*>(x);
+  p.y = static_cast<uint16_t*>(y);
+  p.operand = static_cast<const uint16_t*>(operand);
+  p.M = rows;
+  p.epi = epi;
+  return launch_status(launch_gemm_tc(p, s), "nf4 tcgen05 gemm launch");
+}
+
+int nf4b_dequantize(const nf4b_weight* w, void* out, void* stream) {
+  int st = check_weight(w);
+  if (st) return st;
+  if (out == nullptr) return fail(NF4B_ERR_ARG, "out is null");
+  if (!aligned(out, 16)) return fail(NF4B_ERR_ALIGN, "out is not 16-byte aligned");
+  if ((st = check_device())) return st;
+  DequantParams p;
+  p.packed = w->packed;
+  p.a8 = w->absmax_code;
+  p.absmax = w->absmax;
+  p.code2 = w->code2;
+  p.offset = w->offset;
+  p.N = w->n_out;
+  p.K = w->k_in;
+  p.nested = w->nested ? 1 : 0;
+  p.bs_shift = log2i(w->blocksize);
+  p.bs2_shift = w->nested ? log2i(w->blocksize2) : 0;
+  p.out = static_cast<uint16_t*>(out);
+  return launch_status(launch_dequant(p, reinterpret_cast<cudaStream_t>(stream)), "nf4 dequantize launch");
+}
+
+int nf4b_rms_norm(const void* x, const void* weight, void* y, int rows, int width, float eps,
+                  void* stream) {
+  if (x == nullptr || weight == nullptr || y == nullptr) return fail(NF4B_ERR_ARG, "null pointer");
+  if (rows <= 0 || width <= 0) return fail(NF4B_ERR_SHAPE, "empty input %dx%d", rows, width);
+  if (!(eps >= 0.f)) return fail(NF4B_ERR_ARG, "eps must be >= 0");
+  int st = check_device();
+  if (st) return st;
+  return launch_status(
+      launch_rms_norm(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(weight),
+                      static_cast<uint16_t*>(y), rows, width, eps,
+                      reinterpret_cast<cudaStream_t>(stream)),
+      "rms_norm launch");
+}
+
+int nf4b_rope(const void* x, const void* freqs, int freqs_dtype, void* y, int batch, int seq,
+              int heads, int head_dim, void* stream) {
+  if (x == nullptr || freqs == nullptr || y == nullptr) return fail(NF4B_ERR_ARG, "null pointer");
+  if (batch <= 0 || seq <= 0 || heads <= 0 || head_dim <= 0 || head_dim % 2)
+    return fail(NF4B_ERR_SHAPE, "bad rotary shape (%d,%d,%d,%d)", batch, seq, heads, head_dim);
+  if (freqs_dtype < NF4B_F32 || freqs_dtype > NF4B_BF16)
+    return fail(NF4B_ERR_DTYPE, "unknown freqs dtype %d", freqs_dtype);
+  int st = check_device();
+  if (st) return st;
+  const long long pairs = (long long)batch * seq * heads * head_dim / 2;
+  return launch_status(launch_rope(static_cast<const uint16_t*>(x), freqs, freqs_dtype,
+                                   static_cast<uint16_t*>(y), pairs, head_dim / 2, heads, seq,
+                                   reinterpret_cast<cudaStream_t>(stream)),
+                       "rope launch");
+}
+
+int nf4b_qk_rope_kv(const void* qkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                    const void* freqs, int freqs_dtype, const int64_t* pos, void* q_out,
+                    void* k_cache, void* v_cache, int n_head, int n_kv, int head_dim, int max_len,
+                    void* stream) {
+  if (!qkv || !freqs || !pos || !q_out || !k_cache || !v_cache)
+    return fail(NF4B_ERR_ARG, "null pointer");
+  if (head_dim != 128) return fail(NF4B_ERR_SHAPE, "head_dim must be 128 (got %d)", head_dim);
+  if (n_head <= 0 || n_kv <= 0 || max_len <= 0) return fail(NF4B_ERR_SHAPE, "bad head counts");
+  if ((q_norm_w == nullptr) != (k_norm_w == nullptr))
+    return fail(NF4B_ERR_ARG, "q and k norm weights must both be given or both be null");
+  if (freqs_dtype < NF4B_F32 || freqs_dtype > NF4B_BF16)
+    return fail(NF4B_ERR_DTYPE, "unknown freqs dtype %d", freqs_dtype);
+  int st = check_device();
+  if (st) return st;
+  return launch_status(
+      launch_qk_rope_kv(static_cast<const uint16_t*>(qkv), static_cast<const uint16_t*>(q_norm_w),
+                        static_cast<const uint16_t*>(k_norm_w), eps, freqs, freqs_dtype, pos,
+                        static_cast<uint16_t*>(q_out), static_cast<uint16_t*>(k_cache),
+                        static_cast<uint16_t*>(v_cache), n_head, n_kv, max_len,
+                        reinterpret_cast<cudaStream_t>(stream)),
+      "qk_rope_kv launch");
+}
+
+size_t nf4b_decode_attention_workspace_size(int n_head, int head_dim, int window) {
+  if (n_head <= 0 || head_dim <= 0 || window <= 0) return 0;
+  AttnPlan plan;
+  attn_plan(n_head, head_dim, window, &plan);
+  return plan.counter_bytes + plan.partial_bytes;
+}
+
+int nf4b_decode_attention(const void* q, const void* k_cache, const void* v_cache,
+                          const int64_t* pos, const uint8_t* mask, void* out, int n_head, int n_kv,
+                          int head_dim, int max_len, int window, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  if (!q || !k_cache || !v_cache || !out) return fail(NF4B_ERR_ARG, "null pointer");
+  if (head_dim != 128) return fail(NF4B_ERR_SHAPE, "head_dim must be 128 (got %d)", head_dim);
+  if (n_head <= 0 || n_kv <= 0 || n_head % n_kv)
+    return fail(NF4B_ERR_SHAPE, "n_head %d is not a multiple of n_kv %d", n_head, n_kv);
+  const int groups = n_head / n_kv;
+  if (groups != 1 && groups != 2 && groups != 4 && groups != 8)
+    return fail(NF4B_ERR_SHAPE, "query groups of %d are not served (1, 2, 4 or 8)", groups);
+  if (window <= 0 || window > max_len) return fail(NF4B_ERR_SHAPE, "window %d outside [1, %d]", window, max_len);
+  if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16))
+    return fail(NF4B_ERR_ALIGN, "q / caches not 16-byte aligned");
+  AttnPlan plan;
+  attn_plan(n_head, head_dim, window, &plan);
+  const size_t need = plan.counter_bytes + plan.partial_bytes;
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(NF4B_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
+  if (!aligned(workspace, 256)) return fail(NF4B_ERR_ALIGN, "workspace is not 256-byte aligned");
+  int st = check_device();
+  if (st) return st;
+  float* partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.counter_bytes);
+  return launch_status(
+      launch_decode_attention(static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k_cache),
+                              static_cast<const uint16_t*>(v_cache), pos, mask, static_cast<uint16_t*>(out),
+                              n_head, n_kv, max_len, window, partial, static_cast<int*>(workspace),
+                              reinterpret_cast<cudaStream_t>(stream)),
+      "decode attention launch");
+}
+
+}  // extern "C"

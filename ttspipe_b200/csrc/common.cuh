@@ -1,0 +1,83 @@
+// Shared device helpers for the sm_100a NF4 hot-path kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "nf4b200.h"
+
+namespace nf4b {
+
+typedef uint16_t bf16_t;  // bf16 bit pattern; arithmetic is always fp32
+
+// bitsandbytes' NF4 code points in index order (app/engine/nf4gemv.py:69-86).
+static __constant__ float c_nf4_code[16] = {
+    -1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f,
+    -0.28444138169288635f, -0.18477343022823334f, -0.09105003625154495f, 0.0f,
+    0.07958029955625534f, 0.16093020141124725f, 0.24611230194568634f, 0.33791524171829224f,
+    0.44070982933044434f, 0.5626170039176941f, 0.7229568362236023f, 1.0f};
+
+__device__ __forceinline__ float bf2f(bf16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
+
+// Round to nearest even; NaN stays NaN (cvt handles it).
+__device__ __forceinline__ bf16_t f2bf(float f) {
+  uint16_t r;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(f));
+  return r;
+}
+
+__device__ __forceinline__ float round_bf(float f) { return bf2f(f2bf(f)); }
+
+// Two fp32 -> one bf16x2 register, `lo` in the low half (lower address).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Streaming read of data used once (packed weights): no L1 allocation, and a
+// 256-byte L2 prefetch so the neighbouring sectors of the row arrive with it.
+__device__ __forceinline__ uint2 ld_stream_u2(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v2.u32 {%0, %1}, [%2];"
+               : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue, and wait for the previous kernel's results before reading them.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// The per-block scale of a bitsandbytes NF4 weight: plain fp32 absmax, or the
+// doubly quantised code2[a8] * absmax2 + offset as two separately rounded
+// fp32 operations (the reconstruction bitsandbytes and the reference do).
+__device__ __forceinline__ float nested_scale(float code2_val, float absmax2_val, float offset) {
+  return __fadd_rn(__fmul_rn(code2_val, absmax2_val), offset);
+}
+
+// Epilogue applied to one fp32 accumulator: the matmul output is rounded to
+// bf16 first, then the fused op rounds again where the unfused model does.
+__device__ __forceinline__ bf16_t epilogue(float acc, int epi, const bf16_t* operand, size_t idx) {
+  const float y = round_bf(acc);
+  if (epi == NF4B_EPI_RESIDUAL) {
+    return f2bf(__fadd_rn(bf2f(operand[idx]), y));
+  } else if (epi == NF4B_EPI_SILU_GATE) {
+    const float a = bf2f(operand[idx]);
+    const float s = round_bf(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))));
+    return f2bf(__fmul_rn(s, y));
+  }
+  return f2bf(y);
+}
+
+}  // namespace nf4b

@@ -1,0 +1,117 @@
+// Host-side declarations shared by the kernel files and the C ABI (capi.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace nf4b {
+
+// ---- streaming GEMV (nf4_gemv.cu) ----------------------------------------
+
+constexpr int GEMV_WARPS = 8;                  // warps per CTA
+constexpr int GEMV_CTAS_PER_SM = 2;            // persistent grid: CTAs per SM
+constexpr int GEMV_LUT_BYTES = 256 * 256;      // pair table, 256 B stride, one copy per lane
+constexpr int GEMV_SMEM_BYTES = GEMV_LUT_BYTES + 256 * 4;  // + code2 copy
+constexpr int GEMV_MAX_ROWS = 32;              // activation rows one launch takes
+
+struct GemvParams {
+  const uint8_t* packed;
+  const uint8_t* a8;
+  const float* absmax;
+  const float* code2;
+  float offset;
+  int N, K;
+  int nested;
+  int bs_shift;
+  int bs2_shift;
+  const uint16_t* x;
+  uint16_t* y;
+  const uint16_t* operand;
+  int M;
+  int epi;
+  float* partial;
+  int* counters;
+  long long units;
+  int warps_total;
+  int blocks_per_tile;
+};
+
+struct GemvPlan {
+  long long tiles;
+  long long units;
+  int warps_total;
+  int grid;
+  int slots;
+  size_t counter_bytes;
+  size_t partial_bytes;
+};
+
+int gemv_sm_count(int dev);
+void gemv_plan(int N, int K, int M, int sm_count, GemvPlan* plan);
+cudaError_t launch_gemv(const GemvParams& p, int grid, cudaStream_t stream);
+
+// ---- dequantisation (nf4_dequant.cu) ---------------------------------------
+
+struct DequantParams {
+  const uint8_t* packed;
+  const uint8_t* a8;
+  const float* absmax;
+  const float* code2;
+  float offset;
+  int N, K;
+  int nested;
+  int bs_shift;
+  int bs2_shift;
+  uint16_t* out;
+};
+cudaError_t launch_dequant(const DequantParams& p, cudaStream_t stream);
+
+// ---- tcgen05 GEMM (nf4_gemm_tc.cu) -----------------------------------------
+
+constexpr int GEMM_MIN_ROWS = 33;  // rows above GEMV_MAX_ROWS go to the GEMM
+
+struct GemmParams {
+  const uint8_t* packed;
+  const uint8_t* a8;
+  const float* absmax;
+  const float* code2;
+  float offset;
+  int N, K;
+  int nested;
+  int bs_shift;
+  int bs2_shift;
+  const uint16_t* x;
+  uint16_t* y;
+  const uint16_t* operand;
+  int M;
+  int epi;
+};
+cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream);
+
+// ---- fused elementwise (fused_ops.cu) -------------------------------------
+
+cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows,
+                            int width, float eps, cudaStream_t stream);
+cudaError_t launch_rope(const uint16_t* x, const void* freqs, int ftype, uint16_t* y,
+                        long long pairs, int half_dim, int heads, int seq, cudaStream_t stream);
+cudaError_t launch_qk_rope_kv(const uint16_t* qkv, const uint16_t* qw, const uint16_t* kw,
+                              float eps, const void* freqs, int ftype, const int64_t* pos,
+                              uint16_t* q_out, uint16_t* kc, uint16_t* vc, int nh, int nkv,
+                              int max_len, cudaStream_t stream);
+
+// ---- decode attention (decode_attention.cu) ---------------------------------
+
+constexpr int ATTN_CHUNK = 64;  // cache rows per CTA
+struct AttnPlan {
+  int chunks;
+  size_t counter_bytes;
+  size_t partial_bytes;
+};
+void attn_plan(int n_head, int head_dim, int window, AttnPlan* plan);
+cudaError_t launch_decode_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
+                                    const int64_t* pos, const uint8_t* mask, uint16_t* out, int nh, int nkv,
+                                    int max_len, int window, float* partial, int* counters,
+                                    cudaStream_t stream);
+
+}  // namespace nf4b

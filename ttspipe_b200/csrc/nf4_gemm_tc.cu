@@ -1,0 +1,384 @@
+// NF4 GEMM for prefill and batched decode (more than 32 activation rows) on
+// the sm_100a tensor cores: tcgen05.mma with TMEM accumulators.
+//
+// The reference has no large-row kernel: it slices a prompt into 32-row
+// launches of the same mma.sync kernel (app/engine/nf4gemv.py:460-478), and
+// bitsandbytes itself dequantises the whole weight into a dense GEMM
+// (app/engine/nf4gemv.py:10-13). Here one CTA computes a 128-weight-row x BT
+// activation-row tile of Y^T (weights on the MMA's M side, activations on its
+// N side, so each dequantised weight tile feeds BT rows at once):
+//
+//   warp 0     TMA producer: X tile [BT x 64] bf16 (128-byte swizzle) and the
+//              packed weight tile [128 x 32 B] per 64-wide k block, into a
+//              STAGES-deep ring, completion via mbarrier transaction counts.
+//   warp 1     allocates TMEM (BT fp32 columns) and, from one thread, issues
+//              4 x tcgen05.mma (M=128, N=BT, K=16) per k block, committing each
+//              stage back to the producer and the whole tile to the epilogue.
+//   warps 2-5  dequantise: thread r owns weight row r of the tile; it forms the
+//              block's scale (plain fp32, or code2[a8] * absmax2 + offset as two
+//              rounded fp32 ops) and writes bf16(NF4[q] * scale) - bit-exact to
+//              bitsandbytes' dequantisation - into the K-major 128-byte-swizzled
+//              A tile the MMA reads. After the last k block the same warps read
+//              the accumulator back (tcgen05.ld, 32 lanes x 32 columns at a
+//              time), round to bf16, apply the epilogue and store Y.
+//
+// Every mbarrier wait is bounded: a wait that outlives kWaitNs sets the
+// library's device error word and a CTA-wide abort flag, after which every
+// role drains out, TMEM is released and the kernel returns.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace nf4b {
+
+__device__ int g_device_error = 0;
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int kThreads = 192;
+constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
+
+template <int BT>
+struct __align__(1024) TileSmem {
+  uint8_t x[STAGES][BT * 128];
+  uint8_t a[STAGES][BM * 128];
+  uint8_t w[STAGES][BM * 32];
+  float code2[256];
+  float nf4[16];
+  unsigned long long tma_full[STAGES];
+  unsigned long long a_full[STAGES];
+  unsigned long long mma_done[STAGES];
+  unsigned long long accum_full;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+// Bounded wait on an mbarrier phase. Returns false if the CTA is aborting.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  unsigned long long start = 0;
+  for (uint32_t i = 0;; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((i & 255u) == 0u) {
+      if (*abort_flag) return false;
+      const unsigned long long now = globaltimer();
+      if (i == 0) {
+        start = now;
+      } else if (now - start > kWaitNs) {
+        *abort_flag = 1;
+        atomicOr(&g_device_error, 1);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// K-major, 128-byte-swizzled operand: rows of 128 B, 8-row atoms of 1024 B.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  uint64_t d = (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;             // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+
+template <int BT>
+__host__ __device__ constexpr uint32_t instr_desc() {
+  return (1u << 4)                      // D: fp32
+         | (1u << 7)                    // A: bf16
+         | (1u << 10)                   // B: bf16
+         | ((uint32_t)(BT >> 3) << 17)  // N
+         | ((uint32_t)(BM >> 4) << 24); // M
+}
+
+template <int BT>
+__global__ void __launch_bounds__(kThreads, 1)
+    nf4_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                       const __grid_constant__ CUtensorMap tmap_w, const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  TileSmem<BT>& sm = *reinterpret_cast<TileSmem<BT>*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * BM;
+  const int tok0 = blockIdx.y * BT;
+  const int KB = p.K / BK;
+  volatile int* abort_flag = &sm.abort_flag;
+
+  if (tid == 0) {
+    sm.abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&sm.tma_full[s]), 1);
+      mbar_init(smem_u32(&sm.a_full[s]), 4);
+      mbar_init(smem_u32(&sm.mma_done[s]), 1);
+    }
+    mbar_init(smem_u32(&sm.accum_full), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&sm.tmem_base)),
+                 "r"((uint32_t)BT)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid < 16) sm.nf4[tid] = c_nf4_code[tid];
+  if (p.nested)
+    for (int i = tid; i < 256; i += kThreads) sm.code2[i] = p.code2[i];
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = sm.tmem_base;
+
+  pdl_wait();  // X and Y belong to the stream's previous work
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % STAGES;
+        if (kb >= STAGES &&
+            !mbar_wait(smem_u32(&sm.mma_done[s]), ((kb / STAGES) - 1) & 1, abort_flag))
+          break;
+        const uint32_t bar = smem_u32(&sm.tma_full[s]);
+        mbar_expect_tx(bar, BT * 128 + BM * 32);
+        tma_load_2d(smem_u32(sm.x[s]), &tmap_x, kb * BK, tok0, bar);
+        tma_load_2d(smem_u32(sm.w[s]), &tmap_w, kb * (BK / 2), n0, bar);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc<BT>();
+      bool ok = true;
+      for (int kb = 0; kb < KB && ok; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        ok = mbar_wait(smem_u32(&sm.tma_full[s]), ph, abort_flag) &&
+             mbar_wait(smem_u32(&sm.a_full[s]), ph, abort_flag);
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_addr = smem_u32(sm.a[s]), x_addr = smem_u32(sm.x[s]);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t ad = smem_desc(a_addr + k * 32), bd = smem_desc(x_addr + k * 32);
+          const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+          asm volatile(
+              "{\n\t.reg .pred p;\n\t"
+              "setp.ne.b32 p, %4, 0;\n\t"
+              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+              "l"(ad), "l"(bd), "r"(idesc), "r"(accumulate)
+              : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
+                         "r"(smem_u32(&sm.mma_done[s]))
+                     : "memory");
+      }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
+                       "r"(smem_u32(&sm.accum_full))
+                   : "memory");
+    }
+  } else {
+    // Dequantise: thread r owns weight row n0 + r.
+    const int r = tid - 64;
+    const int row = n0 + r;
+    const bool valid = row < p.N;
+    const int rsw = r & 7;
+    for (int kb = 0; kb < KB; ++kb) {
+      const int s = kb % STAGES;
+      float scale = 0.f;
+      if (valid) {
+        const size_t b = ((size_t)row * p.K + (size_t)kb * BK) >> p.bs_shift;
+        if (p.nested)
+          scale = nested_scale(sm.code2[__ldg(p.a8 + b)], __ldg(p.absmax + (b >> p.bs2_shift)),
+                               p.offset);
+        else
+          scale = __ldg(p.absmax + b);
+      }
+      if (!mbar_wait(smem_u32(&sm.tma_full[s]), (kb / STAGES) & 1, abort_flag)) break;
+      const uint4* wp = reinterpret_cast<const uint4*>(sm.w[s] + r * 32);
+      const uint4 u0 = wp[0], u1 = wp[1];
+      const uint32_t words[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      uint8_t* arow = sm.a[s] + (r >> 3) * 1024 + rsw * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t byte = (words[c] >> (8 * j)) & 0xFFu;
+          o[j] = pack_bf16x2(__fmul_rn(sm.nf4[byte >> 4], scale),
+                             __fmul_rn(sm.nf4[byte & 15], scale));
+        }
+        *reinterpret_cast<uint4*>(arow + ((c ^ rsw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sm.a_full[s]));
+    }
+
+    // Epilogue: TMEM lane quarter (warp % 4) holds weight rows 32q..32q+31.
+    if (mbar_wait(smem_u32(&sm.accum_full), 0, abort_flag)) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int q = warp & 3;
+      const int n = n0 + q * 32 + lane;
+      for (int cb = 0; cb < BT / 32; ++cb) {
+        uint32_t v[32];
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * 32);
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+            "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+              "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
+              "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
+              "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+              "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
+              "=r"(v[30]), "=r"(v[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (n < p.N) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int tok = tok0 + cb * 32 + i;
+            if (tok < p.M) {
+              const size_t o = (size_t)tok * p.N + n;
+              p.y[o] = epilogue(__uint_as_float(v[i]), p.epi, p.operand, o);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  pdl_launch_dependents();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"((uint32_t)BT)
+                 : "memory");
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+                 uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swizzle) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BT>
+cudaError_t launch_bt(const GemmParams& p, cudaStream_t stream) {
+  CUtensorMap mx, mw;
+  if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.x, (uint64_t)p.K, (uint64_t)p.M,
+                   (uint64_t)p.K * 2, BK, BT, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  if (!make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.packed, (uint64_t)p.K / 2, (uint64_t)p.N,
+                   (uint64_t)p.K / 2, BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  const size_t smem = sizeof(TileSmem<BT>) + 1024;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(nf4_gemm_tc_kernel<BT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.N + BM - 1) / BM, (p.M + BT - 1) / BT);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, nf4_gemm_tc_kernel<BT>, mx, mw, p);
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream) {
+  if (p.M <= 64) return launch_bt<64>(p, stream);
+  if (p.M <= 128) return launch_bt<128>(p, stream);
+  return launch_bt<256>(p, stream);
+}
+
+int read_device_error(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace nf4b

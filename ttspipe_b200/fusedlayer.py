@@ -1,0 +1,136 @@
+"""One decode position through a transformer block, on the sm_100a kernels.
+
+Drop-in for the reference's ``app/engine/fusedlayer.py`` (``decode_block``,
+``install``, ``stats``): same launch order and rounding points
+(app/engine/fusedlayer.py:212-269):
+
+    rms_norm -> wqkv -> qk_rope_kv -> decode_attention -> wo(+x)
+             -> rms_norm -> w1 -> w3(silu(w1) * .) -> w2(+h)
+
+The reference's two attention launches (attn_partial + attn_combine) are one
+here (the last CTA of each KV head merges the partials). The position is read
+on the device from ``input_pos`` and the attended window is the mask's width,
+so one captured CUDA graph per window serves every position in it. Anything
+that is not a single bf16 position of an eligible block returns None and
+runs the block's own forward.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+from ttspipe_b200 import _lib
+
+HEAD_DIM = 128
+_stats = {"fused": 0, "fallback": 0}
+_installed = False
+_FTYPE = {"torch.float32": _lib.NF4B_F32, "torch.float16": _lib.NF4B_F16,
+          "torch.bfloat16": _lib.NF4B_BF16}
+
+
+def stats() -> dict:
+    from ttspipe_b200 import nf4gemv
+
+    return {**_stats, "ready": nf4gemv.available() and _installed}
+
+
+def _eligible(block, x, mask, input_pos) -> bool:
+    import torch
+
+    from ttspipe_b200 import nf4gemv
+
+    a, ff = block.attention, block.feed_forward
+    if x.dim() != 3 or x.shape[0] != 1 or x.shape[1] != 1 or x.dtype != torch.bfloat16 or not x.is_cuda:
+        return False
+    if mask is None or input_pos is None or input_pos.numel() != 1 or a.kv_cache is None:
+        return False
+    if input_pos.dtype != torch.long or not input_pos.is_cuda:
+        return False
+    if a.head_dim != HEAD_DIM or a.n_head % a.n_local_heads:
+        return False
+    if (a.n_head // a.n_local_heads) not in (1, 2, 4, 8):
+        return False
+    kc = a.kv_cache.k_cache
+    if kc.dtype != torch.bfloat16 or not kc.is_contiguous() or not a.kv_cache.v_cache.is_contiguous():
+        return False
+    if mask.shape[-1] > kc.shape[2]:
+        return False
+    for linear in (a.wqkv, a.wo, ff.w1, ff.w2, ff.w3):
+        if getattr(linear, "bias", None) is not None or not nf4gemv.prepare(linear):
+            return False
+    return True
+
+
+def decode_block(block, x, freqs_cis, mask, input_pos):
+    """`TransformerBlock.forward` for one position, or None if it cannot."""
+    import torch
+
+    from ttspipe_b200 import fastpath, fusedops, nf4gemv
+
+    if not nf4gemv.available() or not _eligible(block, x, mask, input_pos):
+        return None
+    if str(freqs_cis.dtype) not in _FTYPE or not freqs_cis.is_contiguous() or not freqs_cis.is_cuda:
+        return None
+    a, ff = block.attention, block.feed_forward
+    xn = fusedops.rms_norm(x, block.attention_norm.weight, block.attention_norm.eps)
+    if xn is None:
+        return None
+    qkv = nf4gemv.matmul(a.wqkv, xn)
+    if qkv is None:
+        return None
+    nh, nkv = a.n_head, a.n_local_heads
+    max_len = a.kv_cache.k_cache.shape[2]
+    qn = getattr(a, "q_norm", None) if a.attention_qk_norm else None
+    kn = getattr(a, "k_norm", None) if a.attention_qk_norm else None
+    eps = float(qn.eps if qn is not None and qn.eps is not None else 1e-6)
+    q = torch.empty(nh * HEAD_DIM, dtype=torch.bfloat16, device=x.device)
+    st = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+    _lib.check(_lib.lib().nf4b_qk_rope_kv(
+        qkv.data_ptr(), None if qn is None else qn.weight.data_ptr(),
+        None if kn is None else kn.weight.data_ptr(), eps, freqs_cis.data_ptr(),
+        _FTYPE[str(freqs_cis.dtype)], input_pos.data_ptr(), q.data_ptr(),
+        a.kv_cache.k_cache.data_ptr(), a.kv_cache.v_cache.data_ptr(), nh, nkv, HEAD_DIM, max_len, st))
+    y = torch.empty((1, 1, nh * HEAD_DIM), dtype=torch.bfloat16, device=x.device)
+    fastpath.kernel_attention(q, a.kv_cache.k_cache, a.kv_cache.v_cache, y, n_head=nh, n_kv=nkv,
+                              pos=input_pos, mask=None, window=int(mask.shape[-1]), max_len=max_len)
+    h = nf4gemv.matmul(a.wo, y, epi=nf4gemv.EPI_RESIDUAL, operand=x)
+    hn = fusedops.rms_norm(h, block.ffn_norm.weight, block.ffn_norm.eps)
+    g1 = nf4gemv.matmul(ff.w1, hn)
+    g = nf4gemv.matmul(ff.w3, hn, epi=nf4gemv.EPI_SILU_GATE, operand=g1)
+    out = nf4gemv.matmul(ff.w2, g, epi=nf4gemv.EPI_RESIDUAL, operand=h)
+    _stats["fused"] += 1
+    return out
+
+
+def install() -> bool:
+    """Route single-position ``TransformerBlock.forward`` calls through ``decode_block``."""
+    global _installed
+    from ttspipe_b200 import model, nf4gemv
+
+    if not nf4gemv.available():
+        return False
+    classes = [model.TransformerBlock]
+    try:
+        from fish_speech.models.text2semantic.llama import TransformerBlock as ForkBlock
+
+        classes.append(ForkBlock)
+    except Exception:  # noqa: BLE001 - the fork is optional
+        pass
+    for cls in classes:
+        if getattr(cls, "_fused_patched", False):
+            continue
+        original = cls.forward
+
+        def forward(self, x, freqs_cis, mask, input_pos=None, _orig=original):
+            out = decode_block(self, x, freqs_cis, mask, input_pos)
+            if out is not None:
+                return out
+            if x.shape[1] == 1:
+                _stats["fallback"] += 1
+            return _orig(self, x, freqs_cis, mask, input_pos)
+
+        cls.forward = forward
+        cls._fused_patched = True
+        cls._fused_original_forward = original
+    _installed = True
+    return True

@@ -1,0 +1,307 @@
+"""The NF4 matmul for decode and prefill, on sm_100a, reading bitsandbytes' weights in place.
+
+Drop-in for the reference's ``app/engine/nf4gemv.py``: same entry points
+(``available``, ``prepare``, ``matmul``, ``install``, ``stats``, ``EPI_*``,
+``MAX_N``, ``NF4_CODE``), same argument meaning and the same "None means
+declined" convention (app/engine/nf4gemv.py:315-376, :427-479). The kernels
+are nvcc-built sm_100a code in ``libnf4b200.so`` behind a C ABI
+(``include/nf4b200.h``) instead of NVRTC + ctypes driver launches:
+
+* up to ``MAX_N`` (32) activation rows: the streaming GEMV (mma.sync fragments
+  fed from a shared-memory NF4 pair table, persistent SM-balanced grid);
+* more rows: the tcgen05 GEMM (TMA, bit-exact bf16 dequantisation into shared
+  memory, TMEM accumulators) - one launch for the whole prompt, where the
+  reference slices it into 32-row launches (app/engine/nf4gemv.py:460-478).
+
+Activations are bf16 (the reference's GPU path is fp16-only; this build's
+primary dtype is bf16, see app/engine/nf4cpu.py for the bf16 rounding points).
+fp16 inputs are declined (None), as the reference declines non-fp16 ones.
+There is no CPU or bitsandbytes fallback inside: a missing library raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import logging
+import threading
+
+from ttspipe_b200 import _lib
+from ttspipe_b200.quant import NF4_CODE  # noqa: F401 - part of the reference's API
+
+logger = logging.getLogger(__name__)
+
+#: Rows one GEMV launch takes; more rows go to the tensor-core GEMM in ONE launch.
+MAX_N = 32
+
+#: Epilogues `matmul` can fold into the kernel's store (app/engine/nf4gemv.py:424).
+EPI_NONE, EPI_RESIDUAL, EPI_SILU_GATE = 0, 1, 2
+
+_lock = threading.Lock()
+_stats = {"fast": 0, "fallback": 0, "layers": 0}
+_unavailable: str | None = None
+_checked = False
+_workspaces: dict = {}   # device index -> zeroed uint8 tensor
+
+
+def stats() -> dict:
+    """Calls served by the kernel, calls handed back, layers covered."""
+    return dict(_stats)
+
+
+def available() -> bool:
+    """Whether the library loads and the current device is a B200 (sm_100)."""
+    global _checked, _unavailable
+    if _checked:
+        return _unavailable is None
+    with _lock:
+        if not _checked:
+            try:
+                import torch
+
+                _lib.lib()
+                if not torch.cuda.is_available():
+                    raise RuntimeError("no CUDA device")
+                cap = torch.cuda.get_device_capability()
+                if cap != (10, 0):
+                    raise RuntimeError(f"device capability {cap} is not sm_100")
+            except Exception as exc:  # noqa: BLE001 - reported, never swallowed silently
+                _unavailable = str(exc)
+                logger.warning("nf4 kernels unavailable: %s", exc)
+            _checked = True
+    return _unavailable is None
+
+
+def _workspace(device, nbytes: int):
+    """The zeroed, 256-byte aligned GEMV workspace of this device.
+
+    One per device, like the reference's single worker stream
+    (app/engine/worker.py:1-12): GEMVs issued concurrently on two streams of
+    one device must not overlap. Grown only outside CUDA-graph capture;
+    `prepare` sizes it for the largest GEMV a layer can issue so captured
+    calls never need to grow it.
+    """
+    import torch
+
+    key = torch.device(device).index if torch.device(device).index is not None else torch.cuda.current_device()
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("nf4 workspace must be sized before graph capture (call prepare())")
+        size = max(nbytes, 32 << 20, 0 if ws is None else 2 * ws.numel())
+        ws = torch.zeros(size, dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def _to_desc(packed, qs) -> tuple[_lib.Nf4Weight, tuple]:
+    import torch
+
+    out_f, in_f = (int(v) for v in qs.shape)
+    desc = _lib.Nf4Weight()
+    desc.packed = packed.data_ptr()
+    desc.n_out, desc.k_in = out_f, in_f
+    desc.blocksize = int(qs.blocksize)
+    if getattr(qs, "nested", False):
+        st2 = qs.state2
+        code2 = st2.code.to(device=packed.device, dtype=torch.float32).contiguous()
+        am2 = st2.absmax.contiguous()
+        a8 = qs.absmax.contiguous()
+        desc.absmax_code = a8.data_ptr()
+        desc.absmax = am2.data_ptr()
+        desc.code2 = code2.data_ptr()
+        off = qs.offset
+        desc.offset = float(off.item() if hasattr(off, "item") else off)
+        desc.blocksize2 = int(st2.blocksize)
+        desc.nested = 1
+        held = (packed, a8, am2, code2)
+    else:
+        am = qs.absmax.contiguous()
+        desc.absmax = am.data_ptr()
+        desc.absmax_code = None
+        desc.code2 = None
+        desc.offset = 0.0
+        desc.blocksize2 = 0
+        desc.nested = 0
+        held = (packed, am)
+    return desc, held
+
+
+def prepare(module) -> bool:
+    """Attach what the kernels need to one NF4 linear, or say they cannot serve it.
+
+    Idempotent and cached on ``module._nf4_fast`` (None = declined), reading
+    only ``weight.quant_state`` fields and the weight's pointer/device, as the
+    reference does (app/engine/nf4gemv.py:315-421). Nothing is copied except
+    the nested scales' 1 KB code table when it is not fp32 on the device.
+    """
+    import torch
+
+    cached = getattr(module, "_nf4_fast", -1)
+    if cached != -1:
+        return cached is not None
+
+    def reject(why: str) -> bool:
+        module._nf4_fast = None
+        logger.debug("nf4 kernel declines %s: %s", type(module).__name__, why)
+        return False
+
+    weight = getattr(module, "weight", None)
+    qs = getattr(weight, "quant_state", None)
+    if qs is None:
+        return reject("weight is not quantised yet")
+    if getattr(qs, "quant_type", None) != "nf4":
+        return reject(f"quant_type={getattr(qs, 'quant_type', None)}")
+    if weight.device.type != "cuda":
+        return reject("weight is not on a CUDA device")
+    out_f, in_f = (int(v) for v in qs.shape)
+    bs = int(qs.blocksize)
+    if bs < 64 or bs & (bs - 1):
+        return reject(f"blocksize {bs} is not a power of two >= 64")
+    if in_f % bs or in_f % 64:
+        return reject(f"in_features {in_f} is not a multiple of 64 and {bs}")
+    if weight.data_ptr() % 16:
+        return reject("packed weight is not 16-byte aligned")
+    nblk = out_f * in_f // bs
+    if qs.absmax.numel() != nblk:
+        return reject("scales do not form a rectangle over the weight rows")
+    if getattr(qs, "nested", False):
+        st2 = qs.state2
+        bs2 = int(st2.blocksize)
+        if bs2 <= 0 or bs2 & (bs2 - 1):
+            return reject(f"second-level blocksize {bs2} is not a power of two")
+        if qs.absmax.dtype != torch.uint8 or st2.absmax.dtype != torch.float32:
+            return reject("second-level scales are not the uint8/fp32 pair the kernel reads")
+    elif qs.absmax.dtype != torch.float32:
+        return reject(f"scales are {qs.absmax.dtype}, not float32")
+    packed = weight.data if weight.data.dim() == 2 else weight.data.reshape(out_f, in_f // 2)
+    desc, held = _to_desc(packed, qs)
+    module._nf4_fast = {"desc": desc, "held": held, "M": out_f, "K": in_f,
+                        "nested": bool(getattr(qs, "nested", False))}
+    if available():
+        ws = _lib.lib().nf4b_gemm_workspace_size(ctypes.byref(desc), MAX_N)
+        _workspace(weight.device, int(ws))
+    _stats["layers"] += 1
+    return True
+
+
+def matmul(module, x, *, epi: int = EPI_NONE, operand=None):
+    """``x @ module.weight.T`` for any number of input rows, or None if not applicable.
+
+    `epi` fuses ``operand + xW`` (EPI_RESIDUAL) or ``silu(operand) * xW``
+    (EPI_SILU_GATE); `operand` has the output's shape, bf16, on x's device.
+    Launches on ``torch.cuda.current_stream()``.
+    """
+    import torch
+
+    fast = getattr(module, "_nf4_fast", None)
+    if fast is None:
+        return None
+    if x.dtype != torch.bfloat16 or x.device.type != "cuda":
+        return None
+    K, N = fast["K"], fast["M"]
+    if x.shape[-1] != K:
+        return None
+    flat = x.reshape(-1, K)
+    if not flat.is_contiguous() or flat.data_ptr() % 16:
+        flat = flat.contiguous()
+        if flat.data_ptr() % 16:
+            return None
+    rows = flat.shape[0]
+    if rows == 0:
+        return x.new_empty((*x.shape[:-1], N))
+    op_ptr = None
+    if epi != EPI_NONE:
+        if operand is None or operand.numel() != rows * N or operand.dtype != torch.bfloat16:
+            return None
+        operand = operand.reshape(rows, N)
+        if not operand.is_contiguous():
+            return None
+        op_ptr = operand.data_ptr()
+    if not available():
+        raise RuntimeError(f"nf4 kernels unavailable: {_unavailable}")
+    out = torch.empty((rows, N), dtype=torch.bfloat16, device=x.device)
+    stream = torch.cuda.current_stream(x.device)
+    L = _lib.lib()
+    desc = fast["desc"]
+    ws_ptr, ws_bytes = None, 0
+    if rows <= MAX_N:
+        need = int(L.nf4b_gemm_workspace_size(ctypes.byref(desc), rows))
+        ws = _workspace(x.device, need)
+        ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
+    _lib.check(L.nf4b_gemm(ctypes.byref(desc), flat.data_ptr(), out.data_ptr(), rows, int(epi),
+                           op_ptr, ws_ptr, ws_bytes, ctypes.c_void_p(stream.cuda_stream)))
+    _stats["fast"] += 1
+    return out.view(*x.shape[:-1], N)
+
+
+def dequantize(module):
+    """The bf16 dense weight [out, in] the kernels multiply by (bit-exact
+    bitsandbytes dequantisation), computed on the device."""
+    import torch
+
+    if not prepare(module):
+        return None
+    fast = module._nf4_fast
+    out = torch.empty((fast["M"], fast["K"]), dtype=torch.bfloat16, device=module.weight.device)
+    _lib.check(_lib.lib().nf4b_dequantize(ctypes.byref(fast["desc"]), out.data_ptr(),
+                                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    return out
+
+
+def _linear_classes():
+    classes = []
+    from ttspipe_b200 import quant
+
+    classes.append(quant.Linear4bit)
+    try:
+        import bitsandbytes as bnb  # optional: real bitsandbytes layers are served too
+
+        classes.append(bnb.nn.Linear4bit)
+    except Exception:  # noqa: BLE001
+        pass
+    return classes
+
+
+def install(model=None) -> bool:
+    """Route 4-bit linear forwards through the kernels (class-level patch).
+
+    Patches ``ttspipe_b200.quant.Linear4bit`` and, when importable,
+    ``bitsandbytes.nn.Linear4bit`` (app/engine/nf4gemv.py:482-517). A declined
+    call counts as a fallback and goes to the class's original forward.
+    """
+    if not available():
+        return False
+    for cls in _linear_classes():
+        if getattr(cls, "_nf4_patched", False):
+            continue
+        original_forward = cls.forward
+
+        def forward(self, x, _orig=original_forward):
+            if prepare(self):
+                out = matmul(self, x)
+                if out is not None:
+                    if self.bias is not None:
+                        out = out + self.bias
+                    return out
+            _stats["fallback"] += 1
+            return _orig(self, x)
+
+        cls.forward = forward
+        cls._nf4_patched = True
+        cls._nf4_original_forward = original_forward
+    if model is not None:
+        _prepare_all(model)
+    return True
+
+
+def _prepare_all(model) -> None:
+    """Build every layer's descriptor now, so no step pays for it mid-utterance."""
+    classes = tuple(_linear_classes())
+    served = declined = 0
+    for module in model.modules():
+        if isinstance(module, classes):
+            if prepare(module):
+                served += 1
+            else:
+                declined += 1
+    logger.info("nf4 kernels ready for %d of %d 4-bit layers", served, served + declined)
