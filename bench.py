@@ -217,15 +217,18 @@ class StepIO:
         self.d2h_bytes = self.dev_out.numel() * 2
 
 
-def issue_step(layers, io: StepIO, ws, stream_ptr):
-    """One step through the C ABI: 36 layers x 5 nf4b_gemm calls."""
+def issue_step(layers, io: StepIO, ws, stream_ptr, prefetch: bool = True):
+    """One step through the C ABI: 36 layers x 5 nf4b_gemm_ex calls, each
+    naming the weight of the call after it (the next projection, and the next
+    layer's wqkv after w2) for L2 prefetch."""
     from ttspipe_b200 import _lib
 
     L = _lib.lib()
     i = 0
     ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
     in_base, out_base = io.dev_in.data_ptr(), io.dev_out.data_ptr()
-    for mods in layers:
+    chain = [lin for mods in layers for lin in mods]
+    for li, mods in enumerate(layers):
         prev_out = None
         for lin, (_, n, k, e) in zip(mods, PROJ):
             x_off, _, op_off, _ = io.in_specs[i]
@@ -237,8 +240,12 @@ def issue_step(layers, io: StepIO, ws, stream_ptr):
             elif e == 2:
                 operand = prev_out
             desc = lin._nf4_fast["desc"]
-            st = L.nf4b_gemm(ctypes.byref(desc), in_base + 2 * x_off, y_ptr, 1, e, operand,
-                             ws_ptr, ws_bytes, stream_ptr)
+            opts = None
+            if prefetch:
+                nxt = chain[(i + 1) % len(chain)]._nf4_fast["desc"]
+                opts = ctypes.byref(_lib.GemmOpts(ctypes.pointer(nxt)))
+            st = L.nf4b_gemm_ex(ctypes.byref(desc), in_base + 2 * x_off, y_ptr, 1, e, operand,
+                                ws_ptr, ws_bytes, opts, stream_ptr)
             if st != 0:
                 raise RuntimeError(f"nf4b_gemm failed: {_lib.last_error()}")
             prev_out = y_ptr
@@ -260,6 +267,64 @@ def measured_peaks():
         return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
     except Exception:  # noqa: BLE001
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def detail(layers, io, ws, stream, device):
+    """Per-projection and whole-step timings (graph replay of 36 launches of
+    one shape over the 36 layers, with and without the L2 prefetch chain),
+    printed to stderr for the profile notes; not part of the JSON line."""
+    import torch
+
+    from ttspipe_b200 import _lib
+
+    L = _lib.lib()
+
+    def graph_of(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            fn()
+            torch.cuda.synchronize(device)
+            g.capture_begin()
+            fn()
+            g.capture_end()
+        torch.cuda.synchronize(device)
+        return g
+
+    def time_graph(g, reps=5):
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            g.replay()
+            st.record(stream)
+            for _ in range(reps):
+                g.replay()
+            en.record(stream)
+        torch.cuda.synchronize(device)
+        return st.elapsed_time(en) / reps * 1e3  # us per replay
+
+    for pi, (name, n, k, e) in enumerate(PROJ):
+        for pf in (False, True):
+            def fn(pi=pi, e=e, pf=pf):
+                for li in range(N_LAYERS):
+                    lin = layers[li][pi]
+                    x_off, _, op_off, _ = io.in_specs[li * len(PROJ) + pi]
+                    opnd = io.dev_in.data_ptr() + 2 * op_off if e == 1 else (io.dev_out.data_ptr() if e == 2 else None)
+                    opts = None
+                    if pf:
+                        nxt = layers[(li + 1) % N_LAYERS][pi]._nf4_fast["desc"]
+                        opts = ctypes.byref(_lib.GemmOpts(ctypes.pointer(nxt)))
+                    L.nf4b_gemm_ex(ctypes.byref(lin._nf4_fast["desc"]), io.dev_in.data_ptr() + 2 * x_off,
+                                   io.dev_out.data_ptr(), 1, e, opnd, ws.data_ptr(), ws.numel(), opts,
+                                   stream.cuda_stream)
+            g = graph_of(fn)
+            us = time_graph(g) / N_LAYERS
+            b = algorithmic_bytes(n, k, 1, e)
+            log(f"  {name} {n}x{k} prefetch={int(pf)}: {us:.2f} us/launch, {b / us / 1e3:.0f} GB/s (graph)")
+            del g
+    for pf in (False, True):
+        g = graph_of(lambda pf=pf: issue_step(layers, io, ws, stream.cuda_stream, prefetch=pf))
+        us = time_graph(g)
+        log(f"  step prefetch={int(pf)}: {us:.1f} us, {STEP_BYTES / us / 1e3:.0f} GB/s (graph)")
+        del g
 
 
 def run_gpu(args):
@@ -333,24 +398,7 @@ def run_gpu(args):
     # per-projection timing (eager, events around 20 launches of one shape over
     # rotating layers) - printed to stderr for the profile notes only
     if rank == 0 and args.detail:
-        for pi, (name, n, k, e) in enumerate(PROJ):
-            st, en = torch.cuda.Event(True), torch.cuda.Event(True)
-            reps = 36
-            with torch.cuda.stream(stream):
-                st.record(stream)
-                for r in range(reps):
-                    lin = layers[r % N_LAYERS][pi]
-                    x_off, _, op_off, _ = io.in_specs[(r % N_LAYERS) * len(PROJ) + pi]
-                    desc = lin._nf4_fast["desc"]
-                    opnd = io.dev_in.data_ptr() + 2 * op_off if e == 1 else (io.dev_out.data_ptr() if e == 2 else None)
-                    _lib.lib().nf4b_gemm(ctypes.byref(desc), io.dev_in.data_ptr() + 2 * x_off,
-                                         io.dev_out.data_ptr(), 1, e, opnd, ws.data_ptr(), ws.numel(),
-                                         stream.cuda_stream)
-                en.record(stream)
-            torch.cuda.synchronize(device)
-            us = st.elapsed_time(en) * 1e3 / reps
-            b = algorithmic_bytes(n, k, 1, e)
-            log(f"  {name} {n}x{k}: {us:.2f} us/launch, {b / us / 1e3:.0f} GB/s (eager, back to back)")
+        detail(layers, io, ws, stream, device)
 
     peaks, peak_kind = measured_peaks()
     hbm = float(peaks["hbm_gbs"])

@@ -95,6 +95,20 @@ int nf4b_device_error(int clear);
 int nf4b_gemm(const nf4b_weight* w, const void* x, void* y, int rows, int epi,
               const void* operand, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Options of nf4b_gemm_ex. No counterpart in the reference. */
+typedef struct nf4b_gemm_opts {
+  /* The weight the NEXT call on this stream will read, or NULL. Its packed
+   * codes and first-level scales are streamed into L2 by the GEMV's warps as
+   * they finish, so the next launch starts on L2 hits instead of waiting on
+   * HBM. Purely a hint: results do not depend on it. */
+  const nf4b_weight* prefetch_next;
+} nf4b_gemm_opts;
+
+/* nf4b_gemm with options (opts may be NULL). */
+int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi,
+                 const void* operand, void* workspace, size_t workspace_bytes,
+                 const nf4b_gemm_opts* opts, void* stream);
+
 /* Bytes of workspace nf4b_gemm needs for this weight and row count. */
 size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows);
 

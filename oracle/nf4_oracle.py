@@ -227,6 +227,15 @@ def epilogue(acc, epi: int = EPI_NONE, operand=None) -> np.ndarray:
     raise ValueError(f"unknown epilogue {epi}")
 
 
+def matmul_exact(x_bits, w_bits) -> np.ndarray:
+    """X @ Wᵀ of bf16 inputs, accumulated in fp64 and NOT rounded: the value a
+    bf16-output kernel approximates (its error = accumulation + its own final
+    rounding, at most half a bf16 ulp when the accumulation is exact)."""
+    x = bf16_to_f32(x_bits).astype(np.float64)
+    w = bf16_to_f32(w_bits).astype(np.float64)
+    return x.reshape(-1, w.shape[1]) @ w.T
+
+
 def matmul_dequant(x_bits, w_bits, epi: int = EPI_NONE, operand=None) -> np.ndarray:
     """Y = X @ Wᵀ from the dequantised bf16 weight, accumulated exactly (fp64)
     and rounded once: the reference's "dequantise then matmul"

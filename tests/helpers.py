@@ -43,8 +43,14 @@ def oracle_dequant(layer) -> np.ndarray:
 
 def make_linear(out_f: int, in_f: int, *, seed: int, nested: bool = True, device="cuda",
                 std: float = 0.02, blocksize: int = 64):
+    """A seeded NF4 Linear4bit; on a GPU it is also `prepare`d, as the
+    reference's install does for every layer of a model."""
+    from ttspipe_b200 import nf4gemv
     from ttspipe_b200.quant import Linear4bit
 
     g = torch.Generator(device="cpu").manual_seed(seed)
     w = (torch.randn(out_f, in_f, generator=g) * std).to(device)
-    return Linear4bit.from_float(w, double_quant=nested, blocksize=blocksize)
+    layer = Linear4bit.from_float(w, double_quant=nested, blocksize=blocksize)
+    if layer.weight.device.type == "cuda":
+        nf4gemv.prepare(layer)
+    return layer

@@ -10,7 +10,11 @@ import ctypes
 import threading
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libnf4b200.so"
+import os
+
+#: The library; NF4B_LIBRARY overrides the in-tree path (as the reference's
+#: TTS_NVRTC_PATH does for NVRTC, app/engine/nvrtc.py:49-51).
+LIB_PATH = Path(os.environ.get("NF4B_LIBRARY") or Path(__file__).resolve().parent / "libnf4b200.so")
 
 NF4B_OK = 0
 NF4B_EPI_NONE, NF4B_EPI_RESIDUAL, NF4B_EPI_SILU_GATE = 0, 1, 2
@@ -22,6 +26,7 @@ EXPORTS = (
     "nf4b_last_error",
     "nf4b_device_error",
     "nf4b_gemm",
+    "nf4b_gemm_ex",
     "nf4b_gemm_workspace_size",
     "nf4b_dequantize",
     "nf4b_rms_norm",
@@ -49,6 +54,12 @@ class Nf4Weight(ctypes.Structure):
     ]
 
 
+class GemmOpts(ctypes.Structure):
+    """`nf4b_gemm_opts`."""
+
+    _fields_ = [("prefetch_next", ctypes.POINTER(Nf4Weight))]
+
+
 class Nf4bError(RuntimeError):
     """A non-zero status from the library, with its message."""
 
@@ -69,6 +80,7 @@ def _declare(lib) -> None:
         "nf4b_last_error": (ctypes.c_char_p, []),
         "nf4b_device_error": (i32, [i32]),
         "nf4b_gemm": (i32, [wp, vp, vp, i32, i32, vp, vp, sz, vp]),
+        "nf4b_gemm_ex": (i32, [wp, vp, vp, i32, i32, vp, vp, sz, ctypes.POINTER(GemmOpts), vp]),
         "nf4b_gemm_workspace_size": (sz, [wp, i32]),
         "nf4b_dequantize": (i32, [wp, vp, vp]),
         "nf4b_rms_norm": (i32, [vp, vp, vp, i32, i32, f32, vp]),

@@ -85,6 +85,30 @@ int launch_status(cudaError_t e, const char* what) {
   return ok();
 }
 
+// The pair GEMV reads two adjacent 64-block scales at once (a 2-byte code pair
+// or an 8-byte fp32 pair) and assumes an even block and its successor share a
+// second-level block.
+bool use_pairs(const nf4b_weight* w, int rows) {
+  if (rows > 4 || w->k_in % 128) return false;
+  if (w->blocksize == 64) {
+    if (w->nested) return aligned(w->absmax_code, 2) && w->blocksize2 >= 2;
+    return aligned(w->absmax, 8);
+  }
+  return !w->nested || w->blocksize2 >= 1;
+}
+
+size_t gemv_workspace_bytes(const nf4b_weight* w, int rows, int sms) {
+  GemvPlan a;
+  gemv_plan(w->n_out, w->k_in, rows, sms, false, &a);
+  size_t bytes = a.partial_bytes;
+  if (rows <= 4 && w->k_in % 128 == 0) {  // the pair kernel may serve this call
+    GemvPlan b;
+    gemv_plan(w->n_out, w->k_in, rows, sms, true, &b);
+    if (b.partial_bytes > bytes) bytes = b.partial_bytes;
+  }
+  return GEMV_COUNTER_BYTES + bytes;
+}
+
 int current_sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
@@ -104,13 +128,17 @@ int nf4b_device_error(int clear) { return read_device_error(clear); }
 size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows) {
   if (w == nullptr || rows <= 0 || w->n_out <= 0 || w->k_in <= 0) return 0;
   if (rows > GEMV_MAX_ROWS) return 0;
-  GemvPlan plan;
-  gemv_plan(w->n_out, w->k_in, rows, current_sm_count(), &plan);
-  return plan.counter_bytes + plan.partial_bytes;
+  return gemv_workspace_bytes(w, rows, current_sm_count());
 }
 
 int nf4b_gemm(const nf4b_weight* w, const void* x, void* y, int rows, int epi, const void* operand,
               void* workspace, size_t workspace_bytes, void* stream) {
+  return nf4b_gemm_ex(w, x, y, rows, epi, operand, workspace, workspace_bytes, nullptr, stream);
+}
+
+int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi,
+                 const void* operand, void* workspace, size_t workspace_bytes,
+                 const nf4b_gemm_opts* opts, void* stream) {
   int st = check_weight(w);
   if (st) return st;
   if (x == nullptr || y == nullptr) return fail(NF4B_ERR_ARG, "x or y is null");
@@ -125,9 +153,13 @@ int nf4b_gemm(const nf4b_weight* w, const void* x, void* y, int rows, int epi, c
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
   if (rows <= GEMV_MAX_ROWS) {
+    if ((long long)(w->n_out + 15) / 16 > GEMV_MAX_TILES)
+      return fail(NF4B_ERR_SHAPE, "n_out %d exceeds the GEMV's %lld-row limit", w->n_out,
+                  GEMV_MAX_TILES * 16);
+    const bool pairs = use_pairs(w, rows);
     GemvPlan plan;
-    gemv_plan(w->n_out, w->k_in, rows, current_sm_count(), &plan);
-    const size_t need = plan.counter_bytes + plan.partial_bytes;
+    gemv_plan(w->n_out, w->k_in, rows, current_sm_count(), pairs, &plan);
+    const size_t need = gemv_workspace_bytes(w, rows, current_sm_count());
     if (workspace == nullptr || workspace_bytes < need)
       return fail(NF4B_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need,
                   workspace ? workspace_bytes : (size_t)0);
@@ -152,8 +184,26 @@ int nf4b_gemm(const nf4b_weight* w, const void* x, void* y, int rows, int epi, c
     p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.counter_bytes);
     p.units = plan.units;
     p.warps_total = plan.warps_total;
-    p.blocks_per_tile = w->k_in / 64;
-    return launch_status(launch_gemv(p, plan.grid, s), "nf4 gemv launch");
+    p.uq = (int)(plan.units / plan.warps_total);
+    p.ur = (int)(plan.units % plan.warps_total);
+    p.blocks_per_tile = plan.blocks_per_tile;
+    p.pf_ptr = nullptr;
+    p.pf_bytes = 0;
+    p.pf2_ptr = nullptr;
+    p.pf2_bytes = 0;
+    const nf4b_weight* nx = opts ? opts->prefetch_next : nullptr;
+    if (nx != nullptr && nx->packed != nullptr && aligned(nx->packed, 16) && nx->n_out > 0 &&
+        nx->k_in > 0 && nx->blocksize > 0) {
+      p.pf_ptr = nx->packed;
+      p.pf_bytes = ((long long)nx->n_out * nx->k_in / 2) & ~15LL;
+      const long long nb = (long long)nx->n_out * nx->k_in / nx->blocksize;
+      const void* sc = nx->nested ? (const void*)nx->absmax_code : (const void*)nx->absmax;
+      if (sc != nullptr && aligned(sc, 16)) {
+        p.pf2_ptr = static_cast<const uint8_t*>(sc);
+        p.pf2_bytes = (nb * (nx->nested ? 1 : 4)) & ~15LL;
+      }
+    }
+    return launch_status(launch_gemv(p, plan.grid, pairs, s), "nf4 gemv launch");
   }
 
   GemmParams p;
@@ -264,6 +314,8 @@ int nf4b_decode_attention(const void* q, const void* k_cache, const void* v_cach
   if (head_dim != 128) return fail(NF4B_ERR_SHAPE, "head_dim must be 128 (got %d)", head_dim);
   if (n_head <= 0 || n_kv <= 0 || n_head % n_kv)
     return fail(NF4B_ERR_SHAPE, "n_head %d is not a multiple of n_kv %d", n_head, n_kv);
+  if ((size_t)n_kv * sizeof(int) > ATTN_COUNTER_BYTES)
+    return fail(NF4B_ERR_SHAPE, "more than %zu KV heads", ATTN_COUNTER_BYTES / sizeof(int));
   const int groups = n_head / n_kv;
   if (groups != 1 && groups != 2 && groups != 4 && groups != 8)
     return fail(NF4B_ERR_SHAPE, "query groups of %d are not served (1, 2, 4 or 8)", groups);

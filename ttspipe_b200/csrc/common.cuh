@@ -52,6 +52,18 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
   return v;
 }
 
+// Stream [ptr, ptr + bytes) into L2 (fire and forget). Both must be 16-byte
+// multiples; issued in pieces of at most 32 KB.
+__device__ __forceinline__ void prefetch_l2(const void* ptr, long long bytes) {
+  const char* p = static_cast<const char*>(ptr);
+  while (bytes > 0) {
+    const uint32_t n = bytes > 32768 ? 32768u : (uint32_t)bytes;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(n) : "memory");
+    p += n;
+    bytes -= n;
+  }
+}
+
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue, and wait for the previous kernel's results before reading them.
 __device__ __forceinline__ void pdl_launch_dependents() {
@@ -64,6 +76,53 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // fp32 operations (the reconstruction bitsandbytes and the reference do).
 __device__ __forceinline__ float nested_scale(float code2_val, float absmax2_val, float offset) {
   return __fadd_rn(__fmul_rn(code2_val, absmax2_val), offset);
+}
+
+// One 64-block's dequantisation table: entry i = RNE_bf16(NF4[i] * scale) (the
+// fp32 product, so bit-exact), stored as byte planes - lo[j] holds the low
+// bytes of entries 4j..4j+3, hi[j] their high bytes - so that byte permutes
+// can look entries up without memory.
+struct ScaledLut {
+  uint32_t lo[4], hi[4];
+};
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+__device__ __forceinline__ ScaledLut scaled_lut(float scale) {
+  uint32_t pair[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    pair[i] = pack_bf16x2(__fmul_rn(c_nf4_code[2 * i], scale), __fmul_rn(c_nf4_code[2 * i + 1], scale));
+  ScaledLut t;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    t.lo[j] = prmt(pair[2 * j], pair[2 * j + 1], 0x6420u);
+    t.hi[j] = prmt(pair[2 * j], pair[2 * j + 1], 0x7531u);
+  }
+  return t;
+}
+
+// Dequantise one 32-bit word of packed codes (8 weights, byte j = codes 2j
+// (high nibble) and 2j+1) into four bf16x2 words in k order. Per nibble: a
+// 3-bit permute into each half of the table, a select on the nibble's top
+// bit (a mask made with the permute's sign-replicating mode), then the low
+// and high byte planes are interleaved back into bf16 values.
+__device__ __forceinline__ void lut_dequant8(const ScaledLut& t, uint32_t w, uint32_t (&o)[4]) {
+  const uint32_t w4 = w << 4;
+  const uint32_t m_lo = prmt(w4, w, 0xD9C8u), m_hi = prmt(w4, w, 0xFBEAu);
+  const uint32_t s_lo = w & 0x7777u, s_hi = (w >> 16) & 0x7777u;
+  uint32_t l = (prmt(t.lo[0], t.lo[1], s_lo) & ~m_lo) | (prmt(t.lo[2], t.lo[3], s_lo) & m_lo);
+  uint32_t h = (prmt(t.hi[0], t.hi[1], s_lo) & ~m_lo) | (prmt(t.hi[2], t.hi[3], s_lo) & m_lo);
+  o[0] = prmt(l, h, 0x4051u);
+  o[1] = prmt(l, h, 0x6273u);
+  l = (prmt(t.lo[0], t.lo[1], s_hi) & ~m_hi) | (prmt(t.lo[2], t.lo[3], s_hi) & m_hi);
+  h = (prmt(t.hi[0], t.hi[1], s_hi) & ~m_hi) | (prmt(t.hi[2], t.hi[3], s_hi) & m_hi);
+  o[2] = prmt(l, h, 0x4051u);
+  o[3] = prmt(l, h, 0x6273u);
 }
 
 // Epilogue applied to one fp32 accumulator: the matmul output is rounded to

@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(
 
 void attn_plan(int n_head, int head_dim, int window, AttnPlan* plan) {
   plan->chunks = (window + ATTN_CHUNK - 1) / ATTN_CHUNK;
-  plan->counter_bytes = (size_t)((n_head * sizeof(int) + 255) / 256 * 256);
+  plan->counter_bytes = ATTN_COUNTER_BYTES;
   plan->partial_bytes = (size_t)n_head * plan->chunks * (head_dim + 2) * sizeof(float);
 }
 

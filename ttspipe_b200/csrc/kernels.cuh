@@ -9,11 +9,22 @@ namespace nf4b {
 
 // ---- streaming GEMV (nf4_gemv.cu) ----------------------------------------
 
-constexpr int GEMV_WARPS = 8;                  // warps per CTA
-constexpr int GEMV_CTAS_PER_SM = 2;            // persistent grid: CTAs per SM
+#ifndef NF4B_GEMV_WARPS
+#define NF4B_GEMV_WARPS 8
+#endif
+#ifndef NF4B_GEMV_CTAS
+#define NF4B_GEMV_CTAS 2
+#endif
+constexpr int GEMV_WARPS = NF4B_GEMV_WARPS;    // warps per CTA
+constexpr int GEMV_CTAS_PER_SM = NF4B_GEMV_CTAS;  // persistent grid: CTAs per SM
 constexpr int GEMV_LUT_BYTES = 256 * 256;      // pair table, 256 B stride, one copy per lane
 constexpr int GEMV_SMEM_BYTES = GEMV_LUT_BYTES + 256 * 4;  // + code2 copy
 constexpr int GEMV_MAX_ROWS = 32;              // activation rows one launch takes
+// The workspace starts with a fixed-size region of per-tile arrival counters,
+// so calls on weights of different shapes never alias one another's counters
+// with their partial sums. 16384 tiles of 16 rows: n_out <= 262144.
+constexpr size_t GEMV_COUNTER_BYTES = 64 * 1024;
+constexpr long long GEMV_MAX_TILES = GEMV_COUNTER_BYTES / 4;
 
 struct GemvParams {
   const uint8_t* packed;
@@ -35,11 +46,21 @@ struct GemvParams {
   long long units;
   int warps_total;
   int blocks_per_tile;
+  // Warp w owns units [w*uq + min(w, ur), (w+1)*uq + min(w+1, ur)): uq = units /
+  // warps, ur = units % warps (computed on the host; 32-bit arithmetic on the device).
+  int uq, ur;
+  // Optional L2 prefetch of the weight the NEXT call reads (packed codes and
+  // its first-level scales), issued by each warp once its own loads are done.
+  const uint8_t* pf_ptr;
+  long long pf_bytes;
+  const uint8_t* pf2_ptr;
+  long long pf2_bytes;
 };
 
 struct GemvPlan {
   long long tiles;
   long long units;
+  int blocks_per_tile;  // units per row tile (k_in / 128 for the pair kernel, / 64 otherwise)
   int warps_total;
   int grid;
   int slots;
@@ -48,8 +69,10 @@ struct GemvPlan {
 };
 
 int gemv_sm_count(int dev);
-void gemv_plan(int N, int K, int M, int sm_count, GemvPlan* plan);
-cudaError_t launch_gemv(const GemvParams& p, int grid, cudaStream_t stream);
+// `pairs`: use the pair kernel (units of 128 codes; up to 4 activation rows,
+// k_in % 128 == 0, scale arrays aligned for its paired loads).
+void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan);
+cudaError_t launch_gemv(const GemvParams& p, int grid, bool pairs, cudaStream_t stream);
 
 // ---- dequantisation (nf4_dequant.cu) ---------------------------------------
 
@@ -103,6 +126,7 @@ cudaError_t launch_qk_rope_kv(const uint16_t* qkv, const uint16_t* qw, const uin
 // ---- decode attention (decode_attention.cu) ---------------------------------
 
 constexpr int ATTN_CHUNK = 64;  // cache rows per CTA
+constexpr size_t ATTN_COUNTER_BYTES = 4096;  // fixed counter region: up to 1024 KV heads
 struct AttnPlan {
   int chunks;
   size_t counter_bytes;

@@ -41,7 +41,11 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int STAGES = 4;
-constexpr int kThreads = 192;
+// Warp 0: TMA producer; warp 1: TMEM owner + MMA issuer; then DQ groups of
+// four dequantisation/epilogue warps (group g serves k blocks g, g + DQ, ...).
+template <int DQ>
+constexpr int gemm_threads() { return 64 + 128 * DQ; }
+constexpr int kDequantGroups = 2;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 
 template <int BT>
@@ -137,8 +141,8 @@ __host__ __device__ constexpr uint32_t instr_desc() {
          | ((uint32_t)(BM >> 4) << 24); // M
 }
 
-template <int BT>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BT, int DQ>
+__global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
     nf4_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                        const __grid_constant__ CUtensorMap tmap_w, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -169,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (tid < 16) sm.nf4[tid] = c_nf4_code[tid];
   if (p.nested)
-    for (int i = tid; i < 256; i += kThreads) sm.code2[i] = p.code2[i];
+    for (int i = tid; i < 256; i += gemm_threads<DQ>()) sm.code2[i] = p.code2[i];
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -222,12 +226,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                    : "memory");
     }
   } else {
-    // Dequantise: thread r owns weight row n0 + r.
-    const int r = tid - 64;
+    // Dequantise: thread r of group grp owns weight row n0 + r.
+    const int grp = (warp - 2) >> 2;
+    const int r = (tid - 64) & 127;
     const int row = n0 + r;
     const bool valid = row < p.N;
     const int rsw = r & 7;
-    for (int kb = 0; kb < KB; ++kb) {
+    for (int kb = grp; kb < KB; kb += DQ) {
       const int s = kb % STAGES;
       float scale = 0.f;
       if (valid) {
@@ -243,15 +248,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint4 u0 = wp[0], u1 = wp[1];
       const uint32_t words[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
       uint8_t* arow = sm.a[s] + (r >> 3) * 1024 + rsw * 128;
+      const ScaledLut lut = scaled_lut(scale);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint32_t o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t byte = (words[c] >> (8 * j)) & 0xFFu;
-          o[j] = pack_bf16x2(__fmul_rn(sm.nf4[byte >> 4], scale),
-                             __fmul_rn(sm.nf4[byte & 15], scale));
-        }
+        lut_dequant8(lut, words[c], o);
         *reinterpret_cast<uint4*>(arow + ((c ^ rsw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -264,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int q = warp & 3;
       const int n = n0 + q * 32 + lane;
-      for (int cb = 0; cb < BT / 32; ++cb) {
+      for (int cb = grp; cb < BT / 32; cb += DQ) {
         uint32_t v[32];
         const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * 32);
         asm volatile(
@@ -345,14 +346,14 @@ cudaError_t launch_bt(const GemmParams& p, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(nf4_gemm_tc_kernel<BT>,
+    cudaError_t e = cudaFuncSetAttribute(nf4_gemm_tc_kernel<BT, kDequantGroups>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((p.N + BM - 1) / BM, (p.M + BT - 1) / BT);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(gemm_threads<kDequantGroups>());
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -360,7 +361,7 @@ cudaError_t launch_bt(const GemmParams& p, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, nf4_gemm_tc_kernel<BT>, mx, mw, p);
+  return cudaLaunchKernelEx(&cfg, nf4_gemm_tc_kernel<BT, kDequantGroups>, mx, mw, p);
 }
 
 }  // namespace

@@ -3,32 +3,44 @@
 // Replaces the reference's `nf4_mma` kernel for N <= 32 inputs
 // (app/engine/nf4gemv.py:108-231, launch configs :234-248).
 //
-// Work decomposition. A "unit" is 16 weight rows x one 64-wide k block. Units
-// are numbered row-tile-major and split into equal contiguous runs, one run
-// per warp of a persistent grid sized to the SM count, so every SM streams the
-// same number of bytes whatever the weight shape. A warp that owns a whole row
-// tile stores its outputs directly; tiles split between warps are reduced
-// through a workspace: each contributor writes its fp32 partial into its own
-// slot, and the last to arrive (an atomic counter per tile) sums the slots in
-// slot order - deterministic - applies the epilogue and re-zeroes the counter.
+// Work decomposition. A "unit" is 16 weight rows x a k span (128 codes for
+// the pair kernel, 64 for the block kernel). Units are numbered row-tile-major
+// and split into equal contiguous runs, one run per warp of a persistent grid
+// sized to the SM count, so every SM streams the same number of bytes whatever
+// the weight shape. A warp that owns a whole row tile stores its outputs
+// directly; tiles split between warps are reduced through a workspace: each
+// contributor writes its fp32 partial into its own slot, and the last to
+// arrive (an atomic counter per tile) sums the slots in slot order -
+// deterministic - applies the epilogue and re-zeroes the counter. No warp ever
+// waits on another.
 //
-// Inner loop, per warp and unit: each lane loads 8 packed bytes of two rows
-// (g and g+8; the four lanes of a group cover the block's 32 bytes), turns every
-// byte into a bf16x2 pair of NF4 code values with one shared-memory lookup
-// (a 256-entry pair table, one copy per lane so all 32 lanes hit different
-// banks; the address is built with a single byte-permute), and feeds the pairs
-// as the A fragment of mma.m16n8k16 with x as B. The block's scale multiplies
-// the block's fp32 partial afterwards: y = sum_b s_b * sum_k code[q_k] x_k,
-// the factorisation the reference's CPU kernel uses (app/engine/nf4cpu.py:104-131).
-// Weights are read with 256-byte L2 prefetch and no L1 allocation, PREFETCH
-// units ahead; x is read through L1.
+// Inner loop. Each lane loads packed bytes of two rows (g and g+8), turns every
+// byte into a bf16x2 pair of NF4 code values with ONE shared-memory load (a
+// 256-entry pair table with one copy per lane, so the 32 lanes always hit 32
+// different banks; the address is built with a single byte-permute), and
+// feeds the pairs as the A fragment of mma.m16n8k16 with x as B. The scale
+// of each 64-block multiplies that block's fp32 partial afterwards:
+// y = sum_b s_b * sum_k code[q_k] x_k, the factorisation of the reference's
+// CPU kernel (app/engine/nf4cpu.py:104-131).
 //
-// Programmatic dependent launch: the prologue (tables, first weight loads)
-// runs before `griddepcontrol.wait`, overlapping the previous kernel's tail;
-// nothing the previous kernel writes (x, the workspace, y) is touched before it.
+//  * pair kernel (rows <= 4, k_in % 128 == 0): a lane loads 16 bytes of each of
+//    its two rows (two 64-blocks per 4-lane group); the MMA's 8 columns carry
+//    (activation row, block parity), so one MMA sums both blocks into separate
+//    columns and each block still gets its own scale.
+//  * block kernel (rows <= 32): a lane loads 8 bytes per row (the group covers
+//    one 64-block); columns are activation rows, up to 4 column tiles.
+//
+// Weights are read with 256-byte L2 prefetch and no L1 allocation, several
+// units ahead; x through L1. Programmatic dependent launch: the tables and
+// the first weight loads are issued before `griddepcontrol.wait`, overlapping
+// the previous kernel's tail; x, the workspace and y are touched only after it.
 
 #include "common.cuh"
 #include "kernels.cuh"
+
+#ifndef NF4B_GEMV_PAIR_DEPTH
+#define NF4B_GEMV_PAIR_DEPTH 3  // 128-code units each warp keeps in flight
+#endif
 
 namespace nf4b {
 
@@ -39,10 +51,13 @@ constexpr int kThreads = kWarps * 32;
 
 __device__ __forceinline__ uint32_t lut_lookup(const uint8_t* lut, uint32_t word, uint32_t sel,
                                                uint32_t lane_base) {
-  // Byte permute: result = {lane_base.b0, word.b[j], 0, 0} -> entry * 256 + lane * 4.
+  // Byte permute: {lane_base.b0, word.b[j], 0, 0} = entry * 256 + lane * 4.
   const uint32_t off = __byte_perm(word, lane_base, sel);
   return *reinterpret_cast<const uint32_t*>(lut + off);
 }
+
+// Selector that picks byte j of the word (see lut_lookup).
+__host__ __device__ constexpr uint32_t lut_sel(int j) { return 0x5504u | ((uint32_t)j << 4); }
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
                                                uint32_t a2, uint32_t a3, uint32_t b0,
@@ -54,56 +69,299 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-struct Slot {
-  uint2 wa, wb;     // 8 packed bytes of rows g and g+8
-  float sa, sb;     // plain: the absmax; nested: absmax2
-  uint32_t qa, qb;  // nested: the 8-bit scale codes
-};
-
-__device__ __forceinline__ long long warp_of(long long u, long long U, long long W) {
-  return ((u + 1) * W - 1) / U;
+// The warp whose unit run contains unit u (runs of uq + 1 units for the first
+// ur warps, uq after them).
+__device__ __forceinline__ int warp_of(int u, int uq, int ur) {
+  const int big = ur * (uq + 1);
+  return u < big ? u / (uq + 1) : ur + (u - big) / uq;
 }
 
-template <int NT>
-__global__ void __launch_bounds__(kThreads, 2) nf4_gemv_kernel(const GemvParams p) {
-  constexpr int P = (NT == 1) ? 4 : 2;
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* lut = smem;
-  float* code2_s = reinterpret_cast<float*>(smem + GEMV_LUT_BYTES);
+__device__ __forceinline__ int atomic_add_acq_rel(int* addr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
 
-  for (int i = threadIdx.x; i < 256 * 32; i += kThreads) {
-    const int e = i >> 5, l = i & 31;
-    reinterpret_cast<uint32_t*>(lut)[e * 64 + l] =
-        pack_bf16x2(c_nf4_code[e >> 4], c_nf4_code[e & 15]);
+// Shared-memory tables: the NF4 pair table and (nested scales) code2. Entry
+// e's 32 per-lane copies are 128 contiguous bytes (stride 256), written eight
+// copies per 16-byte store.
+__device__ __forceinline__ void build_tables(uint8_t* smem, const GemvParams& p) {
+  for (int i = threadIdx.x; i < 256 * 8; i += kThreads) {
+    const int e = i >> 3, part = i & 7;
+    const uint32_t v = pack_bf16x2(c_nf4_code[e >> 4], c_nf4_code[e & 15]);
+    *reinterpret_cast<uint4*>(smem + e * 256 + part * 16) = make_uint4(v, v, v, v);
   }
-  if (p.nested)
+  if (p.nested) {
+    float* code2_s = reinterpret_cast<float*>(smem + GEMV_LUT_BYTES);
     for (int i = threadIdx.x; i < 256; i += kThreads) code2_s[i] = p.code2[i];
-  __syncthreads();
-  pdl_launch_dependents();
+  }
+}
+
+// Finish row tile `rt`: every lane holds NV (row, activation row, value)
+// triples. A warp that covered the whole tile stores directly; otherwise the
+// split-tile protocol described at the top of this file.
+template <int NV>
+__device__ __forceinline__ void finish_tile(const GemvParams& p, int rt, int u0, int u1, int gw,
+                                            const int (&row)[NV], const int (&tok)[NV],
+                                            const float (&val)[NV], int lane) {
+  const int t0 = rt * p.blocks_per_tile, t1 = t0 + p.blocks_per_tile - 1;
+  const bool whole = (t0 >= u0) && (t1 < u1);
+  const int N = p.N, M = p.M;
+  int n_contrib = 1;
+  if (!whole) {
+    const int w_lo = warp_of(t0, p.uq, p.ur);
+    n_contrib = warp_of(t1, p.uq, p.ur) - w_lo + 1;
+    float* slot = p.partial + (size_t)(gw - w_lo) * M * N;
+#pragma unroll
+    for (int e = 0; e < NV; ++e)
+      if (row[e] < N && tok[e] < M) slot[(size_t)tok[e] * N + row[e]] = val[e];
+    // The warp barrier orders every lane's partial before lane 0's release
+    // (fence + arrival); the last arriver's acquire orders the reads after it.
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) {
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
+      old = atomic_add_acq_rel(p.counters + rt, 1);
+    }
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old != n_contrib - 1) return;
+    if (lane == 0) p.counters[rt] = 0;
+    __syncwarp();
+  }
+#pragma unroll
+  for (int e = 0; e < NV; ++e) {
+    if (row[e] < N && tok[e] < M) {
+      float v = val[e];
+      if (!whole) {
+        v = 0.f;
+        for (int c = 0; c < n_contrib; ++c)
+          v += __ldcg(p.partial + (size_t)c * M * N + (size_t)tok[e] * N + row[e]);
+      }
+      const size_t o = (size_t)tok[e] * N + row[e];
+      p.y[o] = epilogue(v, p.epi, p.operand, o);
+    }
+  }
+}
+
+// This warp's share of the next call's weight, streamed into L2.
+__device__ __forceinline__ void prefetch_next(const GemvParams& p, int gw, int lane) {
+  if (lane != 0) return;
+  const long long W = p.warps_total;
+  if (p.pf_bytes > 0) {
+    const long long a = (gw * (p.pf_bytes >> 4) / W) << 4, b = ((gw + 1) * (p.pf_bytes >> 4) / W) << 4;
+    if (b > a) prefetch_l2(p.pf_ptr + a, b - a);
+  }
+  if (p.pf2_bytes > 0) {
+    const long long a = (gw * (p.pf2_bytes >> 4) / W) << 4, b = ((gw + 1) * (p.pf2_bytes >> 4) / W) << 4;
+    if (b > a) prefetch_l2(p.pf2_ptr + a, b - a);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// pair kernel: units of 16 rows x 128 codes, activation rows <= 4
+// ---------------------------------------------------------------------------
+
+struct PairSlot {
+  uint4 wa, wb;     // 16 packed bytes of rows g and g+8 (two 64-blocks per group)
+  uint32_t qa, qb;  // nested: 8-bit scale codes, even block in bits 0-7, odd in 8-15;
+                    // plain: the odd block's fp32 absmax bits
+  float sa, sb;     // plain: even-block absmax; nested: absmax2
+};
+
+template <int P>
+__global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint8_t* lut = smem;
+  const float* code2_s = reinterpret_cast<const float*>(smem + GEMV_LUT_BYTES);
 
   const int lane = threadIdx.x & 31;
-  const long long gw = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
-  const long long U = p.units, W = p.warps_total;
-  if (gw >= W) {
-    pdl_wait();
-    return;
-  }
-  const long long u0 = gw * U / W, u1 = (gw + 1) * U / W;
+  const int gw = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const bool active = gw < p.warps_total;
+  const int u0 = active ? gw * p.uq + min(gw, p.ur) : 0;
+  const int u1 = active ? u0 + p.uq + (gw < p.ur ? 1 : 0) : 0;
   const int g = lane >> 2, t = lane & 3;
-  const int B = p.blocks_per_tile;
+  const int B = p.blocks_per_tile;  // 128-code units per row tile
   const int N = p.N, K = p.K, M = p.M;
-  const size_t row_bytes = (size_t)K >> 1;
+  const int row_bytes = K >> 1;
   const uint32_t lane_base = (uint32_t)lane * 4u;
+  const bool bs64 = p.bs_shift == 6;
+  const int nblk = K >> p.bs_shift;  // scale blocks per weight row
 
-  Slot ring[P];
-  auto load = [&](long long u, Slot& s) {
-    const long long rt = u / B;
-    const int kb = (int)(u - rt * B);
-    const int ra = min((int)(rt * 16) + g, N - 1), rb = min((int)(rt * 16) + g + 8, N - 1);
-    s.wa = ld_stream_u2(p.packed + (size_t)ra * row_bytes + kb * 32 + t * 8);
-    s.wb = ld_stream_u2(p.packed + (size_t)rb * row_bytes + kb * 32 + t * 8);
-    const size_t ba = ((size_t)ra * K + (size_t)kb * 64) >> p.bs_shift;
-    const size_t bb = ((size_t)rb * K + (size_t)kb * 64) >> p.bs_shift;
+  int lt = u0 / B, lk = u0 - (u0 / B) * B;
+  int ct = lt, ck = lk;
+
+  // Row pointers of the tile being loaded, refreshed when the tile changes.
+  const uint8_t* pa = nullptr;
+  const uint8_t* pb = nullptr;
+  int ra = 0, rb = 0;
+  auto set_rows = [&](int rt) {
+    ra = min(rt * 16 + g, N - 1);
+    rb = min(rt * 16 + g + 8, N - 1);
+    pa = p.packed + (size_t)ra * row_bytes + t * 16;
+    pb = p.packed + (size_t)rb * row_bytes + t * 16;
+  };
+  set_rows(lt);
+
+  auto load = [&](int kb2, PairSlot& s) {
+    s.wa = ld_stream_u4(pa + kb2 * 64);
+    s.wb = ld_stream_u4(pb + kb2 * 64);
+    // 64-blocks 2*kb2 and 2*kb2+1 of each row.
+    const int be_a = ra * nblk + ((kb2 * 128) >> p.bs_shift);
+    const int be_b = rb * nblk + ((kb2 * 128) >> p.bs_shift);
+    if (p.nested) {
+      if (bs64) {  // two adjacent codes; even index, so 2-byte aligned
+        s.qa = __ldg(reinterpret_cast<const uint16_t*>(p.a8 + be_a));
+        s.qb = __ldg(reinterpret_cast<const uint16_t*>(p.a8 + be_b));
+      } else {     // both halves share one scale
+        s.qa = __ldg(p.a8 + be_a) * 0x101u;
+        s.qb = __ldg(p.a8 + be_b) * 0x101u;
+      }
+      // an even block and the next share their second-level block
+      s.sa = __ldg(p.absmax + (be_a >> p.bs2_shift));
+      s.sb = __ldg(p.absmax + (be_b >> p.bs2_shift));
+    } else if (bs64) {
+      const float2 va = __ldg(reinterpret_cast<const float2*>(p.absmax + be_a));
+      const float2 vb = __ldg(reinterpret_cast<const float2*>(p.absmax + be_b));
+      s.sa = va.x; s.qa = __float_as_uint(va.y);
+      s.sb = vb.x; s.qb = __float_as_uint(vb.y);
+    } else {
+      s.sa = __ldg(p.absmax + be_a); s.qa = __float_as_uint(s.sa);
+      s.sb = __ldg(p.absmax + be_b); s.qb = __float_as_uint(s.sb);
+    }
+  };
+
+  PairSlot ring[P];
+#pragma unroll
+  for (int i = 0; i < P; ++i)
+    if (u0 + i < u1) {
+      load(lk, ring[i]);
+      if (++lk == B) { lk = 0; ++lt; set_rows(lt); }
+    }
+  // The tables are built while the first weight loads are in flight.
+  build_tables(smem, p);
+  __syncthreads();
+  pdl_launch_dependents();
+  if (!active) return;
+
+  pdl_wait();
+
+  // x: column c of the MMA is (activation row c >> 1, block parity c & 1);
+  // lane (g, t) supplies column g for codes of block parity t >> 1.
+  const int xtok = g >> 1;
+  const bool xlane = (xtok < M) && ((g & 1) == (t >> 1));
+  const uint4* xrow = reinterpret_cast<const uint4*>(p.x + (size_t)(xlane ? xtok : 0) * K) + t * 4;
+
+  float acc_a = 0.f, acc_b = 0.f;  // rows g, g+8 for activation row t
+  for (int base = u0; base < u1; base += P) {
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      const int u = base + i;
+      if (u >= u1) break;
+      const PairSlot cur = ring[i];
+      if (u + P < u1) {
+        load(lk, ring[i]);
+        if (++lk == B) { lk = 0; ++lt; set_rows(lt); }
+      }
+      const int rt = ct, kb2 = ck;
+      if (++ck == B) { ck = 0; ++ct; }
+
+      float se_a, so_a, se_b, so_b;
+      if (p.nested) {
+        se_a = nested_scale(code2_s[cur.qa & 0xFFu], cur.sa, p.offset);
+        so_a = nested_scale(code2_s[(cur.qa >> 8) & 0xFFu], cur.sa, p.offset);
+        se_b = nested_scale(code2_s[cur.qb & 0xFFu], cur.sb, p.offset);
+        so_b = nested_scale(code2_s[(cur.qb >> 8) & 0xFFu], cur.sb, p.offset);
+      } else {
+        se_a = cur.sa; so_a = __uint_as_float(cur.qa); se_b = cur.sb; so_b = __uint_as_float(cur.qb);
+      }
+
+      uint4 xv[4];
+      if (xlane) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xv[j] = __ldg(xrow + kb2 * 16 + j);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xv[j] = make_uint4(0, 0, 0, 0);
+      }
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t wa[4] = {cur.wa.x, cur.wa.y, cur.wa.z, cur.wa.w};
+      const uint32_t wb[4] = {cur.wb.x, cur.wb.y, cur.wb.z, cur.wb.w};
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        const uint32_t w0 = wa[s >> 1], w1 = wb[s >> 1];
+        const int j0 = 2 * (s & 1);
+        const uint32_t a0 = lut_lookup(lut, w0, lut_sel(j0), lane_base);
+        const uint32_t a2 = lut_lookup(lut, w0, lut_sel(j0 + 1), lane_base);
+        const uint32_t a1 = lut_lookup(lut, w1, lut_sel(j0), lane_base);
+        const uint32_t a3 = lut_lookup(lut, w1, lut_sel(j0 + 1), lane_base);
+        const uint4& xs = xv[s >> 1];
+        const uint32_t b0 = (s & 1) ? xs.z : xs.x;
+        const uint32_t b1 = (s & 1) ? xs.w : xs.y;
+        mma_bf16_16816(d, a0, a1, a2, a3, b0, b1);
+      }
+      // d0 = (row g, col 2t) = even block, d1 = odd block; d2/d3 for row g+8.
+      acc_a = fmaf(se_a, d[0], acc_a);
+      acc_a = fmaf(so_a, d[1], acc_a);
+      acc_b = fmaf(se_b, d[2], acc_b);
+      acc_b = fmaf(so_b, d[3], acc_b);
+
+      if (kb2 == B - 1 || u == u1 - 1) {
+        const int rows[2] = {rt * 16 + g, rt * 16 + g + 8};
+        const int toks[2] = {t, t};
+        const float vals[2] = {acc_a, acc_b};
+        finish_tile<2>(p, rt, u0, u1, gw, rows, toks, vals, lane);
+        acc_a = acc_b = 0.f;
+      }
+    }
+  }
+  prefetch_next(p, gw, lane);
+}
+
+// ---------------------------------------------------------------------------
+// block kernel: units of 16 rows x 64 codes, up to 4 column tiles of 8 rows
+// ---------------------------------------------------------------------------
+
+struct BlockSlot {
+  uint2 wa, wb;
+  float sa, sb;
+  uint32_t qa, qb;
+};
+
+template <int NT, int P>
+__global__ void __launch_bounds__(kThreads, 2) nf4_gemv_block_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint8_t* lut = smem;
+  const float* code2_s = reinterpret_cast<const float*>(smem + GEMV_LUT_BYTES);
+
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const bool active = gw < p.warps_total;
+  const int u0 = active ? gw * p.uq + min(gw, p.ur) : 0;
+  const int u1 = active ? u0 + p.uq + (gw < p.ur ? 1 : 0) : 0;
+  const int g = lane >> 2, t = lane & 3;
+  const int B = p.blocks_per_tile;  // 64-code units per row tile
+  const int N = p.N, K = p.K, M = p.M;
+  const int row_bytes = K >> 1;
+  const uint32_t lane_base = (uint32_t)lane * 4u;
+  const int nblk = K >> p.bs_shift;
+
+  int lt = u0 / B, lk = u0 - (u0 / B) * B;
+  int ct = lt, ck = lk;
+  const uint8_t* pa = nullptr;
+  const uint8_t* pb = nullptr;
+  int ra = 0, rb = 0;
+  auto set_rows = [&](int rt) {
+    ra = min(rt * 16 + g, N - 1);
+    rb = min(rt * 16 + g + 8, N - 1);
+    pa = p.packed + (size_t)ra * row_bytes + t * 8;
+    pb = p.packed + (size_t)rb * row_bytes + t * 8;
+  };
+  set_rows(lt);
+  auto load = [&](int kb, BlockSlot& s) {
+    s.wa = ld_stream_u2(pa + kb * 32);
+    s.wb = ld_stream_u2(pb + kb * 32);
+    const int ba = ra * nblk + ((kb * 64) >> p.bs_shift);
+    const int bb = rb * nblk + ((kb * 64) >> p.bs_shift);
     if (p.nested) {
       s.qa = __ldg(p.a8 + ba);
       s.qb = __ldg(p.a8 + bb);
@@ -115,73 +373,36 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_kernel(const GemvParams 
     }
   };
 
+  BlockSlot ring[P];
 #pragma unroll
   for (int i = 0; i < P; ++i)
-    if (u0 + i < u1) load(u0 + i, ring[i]);
+    if (u0 + i < u1) {
+      load(lk, ring[i]);
+      if (++lk == B) { lk = 0; ++lt; set_rows(lt); }
+    }
+  build_tables(smem, p);
+  __syncthreads();
+  pdl_launch_dependents();
+  if (!active) return;
 
-  pdl_wait();  // x, the workspace and y belong to the stream's previous work
+  pdl_wait();
 
   float acc[NT][4];
 #pragma unroll
   for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 
-  auto flush = [&](long long rt) {
-    const long long t0 = rt * B, t1 = t0 + B - 1;
-    const bool whole = (t0 >= u0) && (t1 < u1);
-    int n_contrib = 1, last = 1;
-    if (!whole) {
-      const long long w_lo = warp_of(t0, U, W);
-      n_contrib = (int)(warp_of(t1, U, W) - w_lo + 1);
-      float* slot = p.partial + (size_t)(gw - w_lo) * M * N;
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int row = (int)(rt * 16) + g + ((e & 2) ? 8 : 0);
-          const int tok = j * 8 + 2 * t + (e & 1);
-          if (row < N && tok < M) slot[(size_t)tok * N + row] = acc[j][e];
-        }
-      __threadfence();
-      __syncwarp();
-      int old = 0;
-      if (lane == 0) old = atomicAdd(p.counters + rt, 1);
-      old = __shfl_sync(0xffffffffu, old, 0);
-      last = (old == n_contrib - 1);
-      if (last) {
-        if (lane == 0) p.counters[rt] = 0;
-        __threadfence();
-      }
-    }
-    if (!last) return;
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int row = (int)(rt * 16) + g + ((e & 2) ? 8 : 0);
-        const int tok = j * 8 + 2 * t + (e & 1);
-        if (row < N && tok < M) {
-          float v = acc[j][e];
-          if (!whole) {
-            v = 0.f;
-            for (int c = 0; c < n_contrib; ++c)
-              v += __ldcg(p.partial + (size_t)c * M * N + (size_t)tok * N + row);
-          }
-          const size_t o = (size_t)tok * N + row;
-          p.y[o] = epilogue(v, p.epi, p.operand, o);
-        }
-      }
-  };
-
-  for (long long base = u0; base < u1; base += P) {
+  for (int base = u0; base < u1; base += P) {
 #pragma unroll
     for (int i = 0; i < P; ++i) {
-      const long long u = base + i;
+      const int u = base + i;
       if (u >= u1) break;
-      const Slot cur = ring[i];
-      if (u + P < u1) load(u + P, ring[i]);
-
-      const long long rt = u / B;
-      const int kb = (int)(u - rt * B);
+      const BlockSlot cur = ring[i];
+      if (u + P < u1) {
+        load(lk, ring[i]);
+        if (++lk == B) { lk = 0; ++lt; set_rows(lt); }
+      }
+      const int rt = ct, kb = ck;
+      if (++ck == B) { ck = 0; ++ct; }
       float sa = cur.sa, sb = cur.sb;
       if (p.nested) {
         sa = nested_scale(code2_s[cur.qa], cur.sa, p.offset);
@@ -208,12 +429,11 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_kernel(const GemvParams 
       for (int s = 0; s < 4; ++s) {
         const uint32_t wa = (s < 2) ? cur.wa.x : cur.wa.y;
         const uint32_t wb = (s < 2) ? cur.wb.x : cur.wb.y;
-        const uint32_t sel0 = 0x5504u | ((uint32_t)(2 * (s & 1)) << 4);
-        const uint32_t sel1 = 0x5504u | ((uint32_t)(2 * (s & 1) + 1) << 4);
-        const uint32_t a0 = lut_lookup(lut, wa, sel0, lane_base);
-        const uint32_t a2 = lut_lookup(lut, wa, sel1, lane_base);
-        const uint32_t a1 = lut_lookup(lut, wb, sel0, lane_base);
-        const uint32_t a3 = lut_lookup(lut, wb, sel1, lane_base);
+        const int j0 = 2 * (s & 1);
+        const uint32_t a0 = lut_lookup(lut, wa, lut_sel(j0), lane_base);
+        const uint32_t a2 = lut_lookup(lut, wa, lut_sel(j0 + 1), lane_base);
+        const uint32_t a1 = lut_lookup(lut, wb, lut_sel(j0), lane_base);
+        const uint32_t a3 = lut_lookup(lut, wb, lut_sel(j0 + 1), lane_base);
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
           const uint4& xs = xr[j][s >> 1];
@@ -230,12 +450,47 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_kernel(const GemvParams 
         acc[j][3] = fmaf(sb, blk[j][3], acc[j][3]);
       }
       if (kb == B - 1 || u == u1 - 1) {
-        flush(rt);
+        int rows[NT * 4], toks[NT * 4];
+        float vals[NT * 4];
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            rows[j * 4 + e] = rt * 16 + g + ((e & 2) ? 8 : 0);
+            toks[j * 4 + e] = j * 8 + 2 * t + (e & 1);
+            vals[j * 4 + e] = acc[j][e];
+          }
+        finish_tile<NT * 4>(p, rt, u0, u1, gw, rows, toks, vals, lane);
 #pragma unroll
         for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
       }
     }
   }
+  prefetch_next(p, gw, lane);
+}
+
+template <typename Kernel>
+cudaError_t launch_kernel(Kernel kernel, const GemvParams& p, int grid, cudaStream_t stream,
+                          bool* configured) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = GEMV_SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
 }  // namespace
@@ -253,55 +508,33 @@ int gemv_sm_count(int dev) {
   return g_sm_count[dev];
 }
 
-void gemv_plan(int N, int K, int M, int sm_count, GemvPlan* plan) {
+void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan) {
   const long long tiles = (N + 15) / 16;
-  const long long B = K / 64;
+  const long long B = pairs ? K / 128 : K / 64;
   const long long U = tiles * B;
   const long long ctas = (long long)sm_count * GEMV_CTAS_PER_SM;
   long long W = ctas * kWarps;
   if (W > U) W = U;
   plan->tiles = tiles;
   plan->units = U;
+  plan->blocks_per_tile = (int)B;
   plan->warps_total = (int)W;
   plan->grid = (int)((W + kWarps - 1) / kWarps);
-  // The longest run of warps that can share one tile: every warp owns at
-  // least floor(U / W) units, so a tile of B units meets at most
-  // ceil(B / floor(U / W)) + 1 of them.
+  // Every warp owns at least floor(U / W) units, so a tile of B units meets at
+  // most ceil(B / floor(U / W)) + 1 of them.
   const long long per = U / W;
   plan->slots = (int)((B + per - 1) / per + 1);
-  plan->counter_bytes = (size_t)((tiles * sizeof(int) + 255) / 256 * 256);
+  plan->counter_bytes = GEMV_COUNTER_BYTES;
   plan->partial_bytes = (size_t)plan->slots * M * N * sizeof(float);
 }
 
-template <int NT>
-static cudaError_t launch_nt(const GemvParams& p, int grid, cudaStream_t stream) {
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(nf4_gemv_kernel<NT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         GEMV_SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = GEMV_SMEM_BYTES;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, nf4_gemv_kernel<NT>, p);
-}
-
-cudaError_t launch_gemv(const GemvParams& p, int grid, cudaStream_t stream) {
-  if (p.M <= 8) return launch_nt<1>(p, grid, stream);
-  if (p.M <= 16) return launch_nt<2>(p, grid, stream);
-  return launch_nt<4>(p, grid, stream);
+cudaError_t launch_gemv(const GemvParams& p, int grid, bool pairs, cudaStream_t stream) {
+  static bool cfg_pair[64] = {}, cfg1[64] = {}, cfg2[64] = {}, cfg4[64] = {};
+  if (pairs)
+    return launch_kernel(nf4_gemv_pair_kernel<NF4B_GEMV_PAIR_DEPTH>, p, grid, stream, cfg_pair);
+  if (p.M <= 8) return launch_kernel(nf4_gemv_block_kernel<1, 4>, p, grid, stream, cfg1);
+  if (p.M <= 16) return launch_kernel(nf4_gemv_block_kernel<2, 2>, p, grid, stream, cfg2);
+  return launch_kernel(nf4_gemv_block_kernel<4, 2>, p, grid, stream, cfg4);
 }
 
 }  // namespace nf4b

@@ -61,8 +61,12 @@ def _eligible(block, x, mask, input_pos) -> bool:
     return True
 
 
-def decode_block(block, x, freqs_cis, mask, input_pos):
-    """`TransformerBlock.forward` for one position, or None if it cannot."""
+def decode_block(block, x, freqs_cis, mask, input_pos, next_block=None):
+    """`TransformerBlock.forward` for one position, or None if it cannot.
+
+    `next_block` (optional, not in the reference's signature): the block that
+    runs next, whose first weight is streamed into L2 during this block's
+    last matmul."""
     import torch
 
     from ttspipe_b200 import fastpath, fusedops, nf4gemv
@@ -75,7 +79,7 @@ def decode_block(block, x, freqs_cis, mask, input_pos):
     xn = fusedops.rms_norm(x, block.attention_norm.weight, block.attention_norm.eps)
     if xn is None:
         return None
-    qkv = nf4gemv.matmul(a.wqkv, xn)
+    qkv = nf4gemv.matmul(a.wqkv, xn, prefetch=a.wo)
     if qkv is None:
         return None
     nh, nkv = a.n_head, a.n_local_heads
@@ -93,11 +97,12 @@ def decode_block(block, x, freqs_cis, mask, input_pos):
     y = torch.empty((1, 1, nh * HEAD_DIM), dtype=torch.bfloat16, device=x.device)
     fastpath.kernel_attention(q, a.kv_cache.k_cache, a.kv_cache.v_cache, y, n_head=nh, n_kv=nkv,
                               pos=input_pos, mask=None, window=int(mask.shape[-1]), max_len=max_len)
-    h = nf4gemv.matmul(a.wo, y, epi=nf4gemv.EPI_RESIDUAL, operand=x)
+    h = nf4gemv.matmul(a.wo, y, epi=nf4gemv.EPI_RESIDUAL, operand=x, prefetch=ff.w1)
     hn = fusedops.rms_norm(h, block.ffn_norm.weight, block.ffn_norm.eps)
-    g1 = nf4gemv.matmul(ff.w1, hn)
-    g = nf4gemv.matmul(ff.w3, hn, epi=nf4gemv.EPI_SILU_GATE, operand=g1)
-    out = nf4gemv.matmul(ff.w2, g, epi=nf4gemv.EPI_RESIDUAL, operand=h)
+    g1 = nf4gemv.matmul(ff.w1, hn, prefetch=ff.w3)
+    g = nf4gemv.matmul(ff.w3, hn, epi=nf4gemv.EPI_SILU_GATE, operand=g1, prefetch=ff.w2)
+    nxt = next_block.attention.wqkv if next_block is not None else None
+    out = nf4gemv.matmul(ff.w2, g, epi=nf4gemv.EPI_RESIDUAL, operand=h, prefetch=nxt)
     _stats["fused"] += 1
     return out
 

@@ -184,12 +184,14 @@ def prepare(module) -> bool:
     return True
 
 
-def matmul(module, x, *, epi: int = EPI_NONE, operand=None):
+def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None):
     """``x @ module.weight.T`` for any number of input rows, or None if not applicable.
 
     `epi` fuses ``operand + xW`` (EPI_RESIDUAL) or ``silu(operand) * xW``
     (EPI_SILU_GATE); `operand` has the output's shape, bf16, on x's device.
-    Launches on ``torch.cuda.current_stream()``.
+    `prefetch` (an extension; None in the reference's API) names the prepared
+    linear the next call will read: its weights are streamed into L2 while
+    this call finishes. Launches on ``torch.cuda.current_stream()``.
     """
     import torch
 
@@ -228,8 +230,12 @@ def matmul(module, x, *, epi: int = EPI_NONE, operand=None):
         need = int(L.nf4b_gemm_workspace_size(ctypes.byref(desc), rows))
         ws = _workspace(x.device, need)
         ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
-    _lib.check(L.nf4b_gemm(ctypes.byref(desc), flat.data_ptr(), out.data_ptr(), rows, int(epi),
-                           op_ptr, ws_ptr, ws_bytes, ctypes.c_void_p(stream.cuda_stream)))
+    opts = None
+    nxt = getattr(prefetch, "_nf4_fast", None) if prefetch is not None else None
+    if nxt is not None:
+        opts = ctypes.byref(_lib.GemmOpts(ctypes.pointer(nxt["desc"])))
+    _lib.check(L.nf4b_gemm_ex(ctypes.byref(desc), flat.data_ptr(), out.data_ptr(), rows, int(epi),
+                              op_ptr, ws_ptr, ws_bytes, opts, ctypes.c_void_p(stream.cuda_stream)))
     _stats["fast"] += 1
     return out.view(*x.shape[:-1], N)
 
