@@ -112,6 +112,25 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
 /* Bytes of workspace nf4b_gemm needs for this weight and row count. */
 size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows);
 
+/* Size of the device scratch compiled into the library for nf4b_gemm_noalloc. */
+#define NF4B_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/*
+ * nf4b_gemm for callers that cannot allocate device memory (a real-time audio
+ * callback that must not touch an allocator, a cgo/JNI host holding only raw
+ * device pointers from another runtime, a graph being recorded): the GEMV's
+ * partial sums and counters live in a 4 MiB scratch array built into the
+ * library, which every GPU that loads it keeps until exit. No counterpart in
+ * the reference. Limits: calls whose scratch need (nf4b_gemm_workspace_size)
+ * exceeds NF4B_NOALLOC_SCRATCH_BYTES fail with NF4B_ERR_WORKSPACE; more than
+ * 32 rows run the GEMM, which needs no scratch. The first call on a device
+ * looks the scratch's device address up, so make it before any stream
+ * capture. All calls share the scratch: each clears its counters first, and
+ * calls that overlap on the GPU (other streams or threads) race.
+ */
+int nf4b_gemm_noalloc(const nf4b_weight* w, const void* x, void* y, int rows, int epi,
+                      const void* operand, void* stream);
+
 /*
  * out[n_out, k_in] = RNE_bf16(NF4[q] * scale) - bitsandbytes' dequantize_4bit
  * to bf16 (the per-element value of app/engine/nf4gemv.py:185-188 in bf16).

@@ -28,6 +28,7 @@ EXPORTS = (
     "nf4b_gemm",
     "nf4b_gemm_ex",
     "nf4b_gemm_workspace_size",
+    "nf4b_gemm_noalloc",
     "nf4b_dequantize",
     "nf4b_rms_norm",
     "nf4b_rope",
@@ -82,6 +83,7 @@ def _declare(lib) -> None:
         "nf4b_gemm": (i32, [wp, vp, vp, i32, i32, vp, vp, sz, vp]),
         "nf4b_gemm_ex": (i32, [wp, vp, vp, i32, i32, vp, vp, sz, ctypes.POINTER(GemmOpts), vp]),
         "nf4b_gemm_workspace_size": (sz, [wp, i32]),
+        "nf4b_gemm_noalloc": (i32, [wp, vp, vp, i32, i32, vp, vp]),
         "nf4b_dequantize": (i32, [wp, vp, vp]),
         "nf4b_rms_norm": (i32, [vp, vp, vp, i32, i32, f32, vp]),
         "nf4b_rope": (i32, [vp, vp, i32, vp, i32, i32, i32, i32, vp]),

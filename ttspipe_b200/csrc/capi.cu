@@ -20,6 +20,16 @@ int read_device_error(int clear);
 using namespace nf4b;
 
 namespace {
+int fail(int code, const char* fmt, ...);
+}
+
+namespace nf4b {
+// Record `msg` as this thread's last error and return `code` (for entry points
+// defined in other files).
+int report_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace nf4b
+
+namespace {
 
 thread_local char g_err[512] = "";
 
