@@ -1,13 +1,16 @@
 """Benchmark: NF4 decode GEMV GB/s on B200 (one replica per GPU).
 
-Workload (`config.workload`): the decode-time NF4 projections of the S2-Pro
-slow AR - per layer wqkv 6144x2560, wo 2560x4096 (+residual), w1 9728x2560,
-w3 9728x2560 (silu-gate epilogue on w1's output), w2 2560x9728 (+residual),
-blocksize 64 with double-quantised scales - at M=1, in the decode block's
-launch order. A step is one pass over 36 distinct layers (1.87 GB of NF4
-weights, far larger than the 126 MB L2, so every step streams from HBM),
-captured once as a CUDA graph of C-ABI calls. Weights ~ N(0, 0.02) and
-activations ~ N(0, 1), seeded per layer and rank (synthetic; no checkpoint).
+Workload (`config.workload`): the decode-time NF4 matmuls of the S2-Pro slow AR
+at M=1 (blocksize 64, double-quantised scales), per layer: wqkv 6144x2560,
+wo 2560x4096 (+residual), the FeedForward gate silu(x W1^T) * (x W3^T) with
+W1, W3 9728x2560, and w2 2560x9728 (+residual). A step is one pass over 36
+distinct layers (1.87 GB of NF4 weights, far larger than the 126 MB L2, so
+every step streams from HBM). Each layer issues its matmuls in stream order as
+a decode step does: wqkv, wo (+residual), the gate (one nf4b_gemm_gated
+launch), w2 (+residual) - 4 C-ABI launches per layer, captured once as a CUDA
+graph. Each launch names the weights of a later launch as an L2 prefetch hint
+(`--prefetch-distance`). Weights ~ N(0, 0.02) and activations ~ N(0, 1),
+seeded per layer and rank (synthetic; no checkpoint).
 
 value  = algorithmic bytes of all ranks' steps / max-over-ranks device time
 e2e    = the same metric through the C ABI with host buffers: every step
@@ -38,9 +41,11 @@ sys.path.insert(0, str(ROOT))
 METRIC = "nf4_decode_gemv_GBps"
 UNIT = "GB/s"
 N_LAYERS = 36
-# (name, out, in, epilogue): epilogue 0 none, 1 residual, 2 silu-gate on the previous output
+# The layer's weights (name, out, in) and its matmul jobs: (name, weights, epilogue)
+# with epilogue 0 none, 1 residual, "gated" = silu(x W1^T) * (x W3^T).
 PROJ = [("wqkv", 6144, 2560, 0), ("wo", 2560, 4096, 1), ("w1", 9728, 2560, 0),
         ("w3", 9728, 2560, 2), ("w2", 2560, 9728, 1)]
+JOBS = [("wqkv", (0,), 0), ("wo", (1,), 1), ("w13", (2, 3), "gated"), ("w2", (4,), 1)]
 BS, BS2 = 64, 256
 
 
@@ -51,8 +56,22 @@ def algorithmic_bytes(n: int, k: int, rows: int = 1, epi: int = 0, nested: bool 
     return n * k // 2 + scales + 2 * rows * k + 2 * rows * n + (2 * rows * n if epi else 0)
 
 
-STEP_BYTES = N_LAYERS * sum(algorithmic_bytes(n, k, 1, e) for _, n, k, e in PROJ)
-LAUNCHES_PER_STEP = N_LAYERS * len(PROJ)
+def weight_bytes(n: int, k: int, nested: bool = True) -> int:
+    nb = n * k // BS
+    return n * k // 2 + ((nb + 4 * math.ceil(nb / BS2) + 1024) if nested else 4 * nb)
+
+
+def job_bytes(job, rows: int = 1) -> int:
+    """Weights + x + y (+ operand) of one job; a gated pair reads x once and
+    writes only the gated product."""
+    _, widx, epi = job
+    n, k = PROJ[widx[0]][1], PROJ[widx[0]][2]
+    b = sum(weight_bytes(PROJ[i][1], PROJ[i][2]) for i in widx) + 2 * rows * k + 2 * rows * n
+    return b + (2 * rows * n if epi == 1 else 0)
+
+
+LAYER_BYTES = sum(job_bytes(j) for j in JOBS)
+STEP_BYTES = N_LAYERS * LAYER_BYTES
 
 
 def log(*a):
@@ -189,27 +208,27 @@ def make_layers(device, rank: int):
 
 class StepIO:
     """All of a step's inputs and outputs in two flat device buffers (and
-    pinned host mirrors for the end-to-end measurement)."""
+    pinned host mirrors for the end-to-end measurement). Per layer and job:
+    x (and the residual operand) in `dev_in`, y in `dev_out`."""
 
     def __init__(self, device, rank: int):
         import torch
 
-        self.in_specs, self.out_specs = [], []
+        self.specs = []   # per (layer, job): (x_off, op_off or None, y_off, n, k)
         off_in = off_out = 0
         for _ in range(N_LAYERS):
-            for _, n, k, e in PROJ:
-                x_off = off_in
-                off_in += k
+            for _, widx, epi in JOBS:
+                n, k = PROJ[widx[0]][1], PROJ[widx[0]][2]
+                x_off, off_in = off_in, off_in + k
                 op_off = None
-                if e == 1:
-                    op_off = off_in
-                    off_in += n
-                self.in_specs.append((x_off, k, op_off, n))
-                self.out_specs.append((off_out, n))
+                if epi == 1:
+                    op_off, off_in = off_in, off_in + n
+                self.specs.append((x_off, op_off, off_out, n, k))
                 off_out += n
         g = torch.Generator(device=device).manual_seed(77 + rank)
         self.dev_in = torch.randn(off_in, generator=g, device=device).to(torch.bfloat16)
         self.dev_out = torch.zeros(off_out, dtype=torch.bfloat16, device=device)
+        self.scratch = torch.zeros(9728, dtype=torch.bfloat16, device=device)  # w1 output (single mode)
         self.host_in = torch.empty(off_in, dtype=torch.bfloat16, pin_memory=True)
         self.host_in.copy_(self.dev_in.cpu())
         self.host_out = torch.empty(off_out, dtype=torch.bfloat16, pin_memory=True)
@@ -217,39 +236,83 @@ class StepIO:
         self.d2h_bytes = self.dev_out.numel() * 2
 
 
-def issue_step(layers, io: StepIO, ws, stream_ptr, prefetch: bool = True):
-    """One step through the C ABI: 36 layers x 5 nf4b_gemm_ex calls, each
-    naming the weight of the call after it (the next projection, and the next
-    layer's wqkv after w2) for L2 prefetch."""
+def step_workspace(layers, io, device):
+    import torch
+
     from ttspipe_b200 import _lib
 
     L = _lib.lib()
-    i = 0
-    ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
-    in_base, out_base = io.dev_in.data_ptr(), io.dev_out.data_ptr()
-    chain = [lin for mods in layers for lin in mods]
-    for li, mods in enumerate(layers):
-        prev_out = None
-        for lin, (_, n, k, e) in zip(mods, PROJ):
-            x_off, _, op_off, _ = io.in_specs[i]
-            y_off, _ = io.out_specs[i]
-            y_ptr = out_base + 2 * y_off
-            operand = None
-            if e == 1:
-                operand = in_base + 2 * op_off
-            elif e == 2:
-                operand = prev_out
-            desc = lin._nf4_fast["desc"]
-            opts = None
-            if prefetch:
-                nxt = chain[(i + 1) % len(chain)]._nf4_fast["desc"]
-                opts = ctypes.byref(_lib.GemmOpts(ctypes.pointer(nxt)))
-            st = L.nf4b_gemm_ex(ctypes.byref(desc), in_base + 2 * x_off, y_ptr, 1, e, operand,
-                                ws_ptr, ws_bytes, opts, stream_ptr)
+    need = max(int(L.nf4b_gemm_workspace_size(ctypes.byref(m._nf4_fast["desc"]), 1)) for m in layers[0])
+    return torch.zeros(need, dtype=torch.uint8, device=device)
+
+
+MODES = {
+    "decode": "per layer wqkv, wo(+res), the gated w1/w3 pair in one launch (nf4b_gemm_gated), w2(+res): "
+              "4 launches per layer in stream order, each naming the weights of a later launch for L2 prefetch",
+    "single": "one launch per projection (w1, then w3 with the silu-gate epilogue on w1's output): "
+              "5 launches per layer",
+}
+
+
+class StepPlan:
+    """The launches of one step through the C ABI, built once (ctypes structs
+    kept alive here) and issued on a stream; CUDA-graph capturable.
+
+    Each launch names the weights of the launch `distance` places later as an
+    L2 prefetch hint (0: no hints)."""
+
+    def __init__(self, layers, io: StepIO, ws, mode: str = "decode", distance: int = 2):
+        from ttspipe_b200 import _lib
+
+        self.L = _lib.lib()
+        self.ws_ptr, self.ws_bytes = ws.data_ptr(), ws.numel()
+        self.mode = mode
+        self.launches = []   # ("gemm", desc, x, y, epi, operand) | ("gated", d1, d3, x, y)
+        weights = []         # per launch: descriptors it reads
+        in_base, out_base = io.dev_in.data_ptr(), io.dev_out.data_ptr()
+        for li, mods in enumerate(layers):
+            for ji, (_, widx, epi) in enumerate(JOBS):
+                x_off, op_off, y_off, _, _ = io.specs[li * len(JOBS) + ji]
+                x, y = in_base + 2 * x_off, out_base + 2 * y_off
+                op = in_base + 2 * op_off if op_off is not None else None
+                descs = [mods[w]._nf4_fast["desc"] for w in widx]
+                if epi == "gated" and mode == "decode":
+                    self.launches.append(("gated", descs[0], descs[1], x, y))
+                    weights.append(descs)
+                elif epi == "gated":
+                    scratch = io.scratch.data_ptr()
+                    self.launches.append(("gemm", descs[0], x, scratch, 0, None))
+                    weights.append([descs[0]])
+                    self.launches.append(("gemm", descs[1], x, y, 2, scratch))
+                    weights.append([descs[1]])
+                else:
+                    self.launches.append(("gemm", descs[0], x, y, epi, op))
+                    weights.append(descs)
+        n = len(self.launches)
+        self.opts = []
+        for i in range(n):
+            hint = weights[(i + distance) % n][:2] if distance > 0 else []
+            self.opts.append(_lib.GemmOpts(*[ctypes.pointer(d) for d in hint]) if hint else None)
+
+    def __len__(self):
+        return len(self.launches)
+
+    def issue(self, stream_ptr):
+        from ttspipe_b200 import _lib
+
+        L = self.L
+        for launch, opts in zip(self.launches, self.opts):
+            o = ctypes.byref(opts) if opts is not None else None
+            if launch[0] == "gated":
+                _, d1, d3, x, y = launch
+                st = L.nf4b_gemm_gated(ctypes.byref(d1), ctypes.byref(d3), x, y, 1, self.ws_ptr, self.ws_bytes,
+                                       o, stream_ptr)
+            else:
+                _, desc, x, y, epi, op = launch
+                st = L.nf4b_gemm_ex(ctypes.byref(desc), x, y, 1, epi, op, self.ws_ptr, self.ws_bytes, o,
+                                    stream_ptr)
             if st != 0:
-                raise RuntimeError(f"nf4b_gemm failed: {_lib.last_error()}")
-            prev_out = y_ptr
-            i += 1
+                raise RuntimeError(f"{launch[0]} launch failed: {_lib.last_error()}")
 
 
 def roofline_traffic():
@@ -270,14 +333,9 @@ def measured_peaks():
 
 
 def detail(layers, io, ws, stream, device):
-    """Per-projection and whole-step timings (graph replay of 36 launches of
-    one shape over the 36 layers, with and without the L2 prefetch chain),
-    printed to stderr for the profile notes; not part of the JSON line."""
+    """Whole-step timings of every issue mode and prefetch distance (graph
+    replay), printed to stderr for the profile notes; not part of the JSON line."""
     import torch
-
-    from ttspipe_b200 import _lib
-
-    L = _lib.lib()
 
     def graph_of(fn):
         g = torch.cuda.CUDAGraph()
@@ -301,29 +359,13 @@ def detail(layers, io, ws, stream, device):
         torch.cuda.synchronize(device)
         return st.elapsed_time(en) / reps * 1e3  # us per replay
 
-    for pi, (name, n, k, e) in enumerate(PROJ):
-        for pf in (False, True):
-            def fn(pi=pi, e=e, pf=pf):
-                for li in range(N_LAYERS):
-                    lin = layers[li][pi]
-                    x_off, _, op_off, _ = io.in_specs[li * len(PROJ) + pi]
-                    opnd = io.dev_in.data_ptr() + 2 * op_off if e == 1 else (io.dev_out.data_ptr() if e == 2 else None)
-                    opts = None
-                    if pf:
-                        nxt = layers[(li + 1) % N_LAYERS][pi]._nf4_fast["desc"]
-                        opts = ctypes.byref(_lib.GemmOpts(ctypes.pointer(nxt)))
-                    L.nf4b_gemm_ex(ctypes.byref(lin._nf4_fast["desc"]), io.dev_in.data_ptr() + 2 * x_off,
-                                   io.dev_out.data_ptr(), 1, e, opnd, ws.data_ptr(), ws.numel(), opts,
-                                   stream.cuda_stream)
-            g = graph_of(fn)
-            us = time_graph(g) / N_LAYERS
-            b = algorithmic_bytes(n, k, 1, e)
-            log(f"  {name} {n}x{k} prefetch={int(pf)}: {us:.2f} us/launch, {b / us / 1e3:.0f} GB/s (graph)")
-            del g
-    for pf in (False, True):
-        g = graph_of(lambda pf=pf: issue_step(layers, io, ws, stream.cuda_stream, prefetch=pf))
+    cases = [("decode", d) for d in (0, 1, 2)] + [("single", d) for d in (0, 1)]
+    for mode, dist in cases:
+        plan = StepPlan(layers, io, ws, mode, dist)
+        g = graph_of(lambda: plan.issue(stream.cuda_stream))
         us = time_graph(g)
-        log(f"  step prefetch={int(pf)}: {us:.1f} us, {STEP_BYTES / us / 1e3:.0f} GB/s (graph)")
+        log(f"  step mode={mode} prefetch_distance={dist}: {len(plan)} launches, {us:.1f} us, "
+            f"{STEP_BYTES / us / 1e3:.0f} GB/s (graph)")
         del g
 
 
@@ -340,19 +382,18 @@ def run_gpu(args):
     t0 = time.time()
     layers = make_layers(device, rank)
     io = StepIO(device, rank)
-    need = max(int(_lib.lib().nf4b_gemm_workspace_size(ctypes.byref(m._nf4_fast["desc"]), 1))
-               for m in layers[0])
-    ws = torch.zeros(need, dtype=torch.uint8, device=device)
+    ws = step_workspace(layers, io, device)
+    plan = StepPlan(layers, io, ws, args.mode, args.prefetch_distance)
     log(f"[rank {rank}] built {N_LAYERS} layers in {time.time() - t0:.1f}s; step bytes {STEP_BYTES / 1e9:.3f} GB")
 
     stream = torch.cuda.Stream(device)
     with torch.cuda.stream(stream):
-        issue_step(layers, io, ws, stream.cuda_stream)   # eager warm-up of every call
+        plan.issue(stream.cuda_stream)   # eager warm-up of every call
     stream.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         graph.capture_begin()
-        issue_step(layers, io, ws, stream.cuda_stream)
+        plan.issue(stream.cuda_stream)
         graph.capture_end()
     stream.synchronize()
 
@@ -412,22 +453,25 @@ def run_gpu(args):
             "ms_per_step": round(secs_max / args.steps * 1e3, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init NF4 weights N(0,0.02), activations N(0,1), seeded per rank)",
-            "config": {"workload": "S2-Pro slow-AR decode projections: 36 layers x [wqkv 6144x2560, "
-                                   "wo 2560x4096 +res, w1 9728x2560, w3 9728x2560 silu-gate, w2 2560x9728 +res], "
+            "config": {"workload": "S2-Pro slow-AR decode matmuls: 36 layers x [wqkv 6144x2560, "
+                                   "wo 2560x4096 +res, silu(x W1)*(x W3) W1,W3 9728x2560, w2 2560x9728 +res], "
                                    "M=1, NF4 bs64 + double-quant (bs2 256)",
+                       "schedule": f"{args.mode}: {MODES[args.mode]}",
+                       "prefetch_distance": args.prefetch_distance,
                        "baseline_config": "configs[1] (one slow-AR layer's linears at M=1) x 36 distinct layers",
                        "bytes_per_step": STEP_BYTES, "rows": 1,
                        "l2": "inputs larger than L2 (1.87 GB of weights per step per GPU)",
                        "parallelism": f"replicas x{world} (no collective on the data path)"},
-            "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+            "gpu_launches": len(plan) * args.steps,
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": io.h2d_bytes,
                     "d2h_bytes_per_step": io.d2h_bytes,
                     "path": "C ABI nf4b_gemm calls (CUDA graph) + pinned H2D inputs + D2H outputs per step"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "peak_source": peak_kind,
                          "traffic": traffic,
-                         "algorithmic_bytes_per_launch": STEP_BYTES // LAUNCHES_PER_STEP,
-                         "kernel": "nf4_gemv_kernel<1> (all launches of the step)"},
+                         "algorithmic_bytes_per_launch": STEP_BYTES // len(plan),
+                         "kernel": "nf4_gemv_pair_kernel, plain and gated (every launch of the step; "
+                                   "achieved = step bytes / step time, i.e. launch gaps included)"},
             "clocks": clock,
             "per_rank_GBps": round(per_rank, 1),
         }
@@ -447,17 +491,21 @@ def run_gpu(args):
 # --------------------------------------------------------------------------
 
 
+CPU_SHAPES = [(6144, 2560), (2560, 4096), (19456, 2560), (2560, 9728)]  # wqkv, wo, w13, w2
+
+
 def _cpu_layers(count: int):
     """Random packed NF4 bytes and bf16 absmax for `count` layers, generated
     directly as the reference's own CPU test does (tests/test_nf4cpu.py:31-35);
-    the kernel's speed does not depend on the values."""
+    the kernel's speed does not depend on the values. w1 and w3 are one fused
+    w13 matmul, as the reference's CPU path serves them (app/engine/cpu.py:98-126)."""
     import torch
 
     layers = []
     for li in range(count):
         g = torch.Generator().manual_seed(li)
         mods = []
-        for _, n, k, _ in PROJ:
+        for n, k in CPU_SHAPES:
             packed = torch.randint(0, 255, (n, k // 2), dtype=torch.uint8, generator=g)
             absmax = (torch.rand(n, k // 64, generator=g) * 0.1).to(torch.bfloat16)
             mods.append((packed, absmax, n, k))
@@ -498,7 +546,7 @@ def cpu_baseline(seconds: float) -> dict:
     torch.set_num_threads(threads)
     run, kind, note = cpu_gemv_runner()
     layers = _cpu_layers(4)
-    xs = {k: torch.randn(1, k).to(torch.bfloat16) for _, _, k, _ in PROJ}
+    xs = {k: torch.randn(1, k).to(torch.bfloat16) for _, k in CPU_SHAPES}
     for mods in layers[:1]:
         for p, a, n, k in mods:
             run(xs[k], p, a, n)
@@ -507,11 +555,11 @@ def cpu_baseline(seconds: float) -> dict:
     while time.perf_counter() - t0 < seconds:
         for p, a, n, k in layers[li % len(layers)]:
             run(xs[k], p, a, n)
-        done_bytes += sum(algorithmic_bytes(n, k, 1, e) for _, n, k, e in PROJ)
+        done_bytes += LAYER_BYTES
         li += 1
     el = time.perf_counter() - t0
     return {"value": round(done_bytes / el / 1e9, 2), "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{li} layer passes (5 projections each, 4 distinct layers cycled, M=1) in {el:.1f}s; {note}"}
+            "sample": f"{li} layer passes (wqkv, wo, w13, w2 at M=1; 4 distinct layers cycled) in {el:.1f}s; {note}"}
 
 
 def run_reference(args):
@@ -525,7 +573,7 @@ def run_reference(args):
     run, kind, note = cpu_gemv_runner()
     n_layers = N_LAYERS if kind == "reference" else 2
     layers = _cpu_layers(n_layers)
-    xs = {k: torch.randn(1, k).to(torch.bfloat16) for _, _, k, _ in PROJ}
+    xs = {k: torch.randn(1, k).to(torch.bfloat16) for _, k in CPU_SHAPES}
 
     def step():
         for mods in layers:
@@ -538,13 +586,13 @@ def run_reference(args):
     for _ in range(args.steps):
         step()
     el = time.perf_counter() - t0
-    step_bytes = n_layers * sum(algorithmic_bytes(n, k, 1, e) for _, n, k, e in PROJ)
+    step_bytes = n_layers * LAYER_BYTES
     value = step_bytes * args.steps / el / 1e9
     return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1, "impl": "reference",
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random packed NF4 bytes, bf16 absmax, x N(0,1))",
-            "config": {"workload": f"{n_layers} layers x [wqkv 6144x2560, wo 2560x4096, w1/w3 9728x2560, "
+            "config": {"workload": f"{n_layers} layers x [wqkv 6144x2560, wo 2560x4096, w13 19456x2560, "
                                    "w2 2560x9728], M=1, NF4 bs64 (bf16 absmax, as the reference's CPU path)",
                        "bytes_per_step": step_bytes},
             "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads, "kind": kind,
@@ -561,6 +609,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--detail", action="store_true")
+    ap.add_argument("--mode", default="decode", choices=sorted(MODES))
+    ap.add_argument("--prefetch-distance", type=int, default=2,
+                    help="launches ahead whose weights each launch streams into L2 (0: none)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

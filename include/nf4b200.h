@@ -97,17 +97,31 @@ int nf4b_gemm(const nf4b_weight* w, const void* x, void* y, int rows, int epi,
 
 /* Options of nf4b_gemm_ex. No counterpart in the reference. */
 typedef struct nf4b_gemm_opts {
-  /* The weight the NEXT call on this stream will read, or NULL. Its packed
-   * codes and first-level scales are streamed into L2 by the GEMV's warps as
-   * they finish, so the next launch starts on L2 hits instead of waiting on
-   * HBM. Purely a hint: results do not depend on it. */
+  /* Weights a LATER call on this stream will read, or NULL. Their packed
+   * codes and first-level scales are streamed into L2 by the GEMV's warps
+   * while it runs, so those launches find their weights in L2 instead of
+   * waiting on HBM. Purely a hint: results do not depend on it. */
   const nf4b_weight* prefetch_next;
+  const nf4b_weight* prefetch_next2;
 } nf4b_gemm_opts;
 
 /* nf4b_gemm with options (opts may be NULL). */
 int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi,
                  const void* operand, void* workspace, size_t workspace_bytes,
                  const nf4b_gemm_opts* opts, void* stream);
+
+/*
+ * The FeedForward gate of a W1/W3 pair sharing x in ONE launch:
+ * y = bf16(bf16(silu(bf16(x W1^T))) * bf16(x W3^T)), the rounding points of the
+ * fork's w2(F.silu(w1(x)) * w3(x)) (app/engine/fusedlayer.py:265-266, where it
+ * is two nf4gemv.matmul launches, the second with EPI_SILU_GATE). x W1^T is
+ * never written out. Serves 1..4 rows with k_in % 128 == 0 (NF4B_ERR_SHAPE
+ * otherwise: the caller then issues the two matmuls). w1 and w3 must agree in
+ * shape and quantisation. Workspace as nf4b_gemm (nf4b_gemm_workspace_size of
+ * w1 covers it). No reference counterpart as a single call.
+ */
+int nf4b_gemm_gated(const nf4b_weight* w1, const nf4b_weight* w3, const void* x, void* y, int rows,
+                    void* workspace, size_t workspace_bytes, const nf4b_gemm_opts* opts, void* stream);
 
 /* Bytes of workspace nf4b_gemm needs for this weight and row count. */
 size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows);

@@ -98,7 +98,7 @@ def test_config2_projections_at_m1(idx):
     check_matmul(y, x, layer)
 
 
-@pytest.mark.parametrize("rows", [2, 5, 8, 9, 16, 19, 32])
+@pytest.mark.parametrize("rows", [2, 3, 4, 5, 8, 9, 16, 19, 32])
 @pytest.mark.parametrize("shape", [(6144, 2560), (2560, 9728), (1544, 2560)])
 def test_rows_match_the_oracle(shape, rows):
     """Batched decode and prefill, including row counts that do not fill a

@@ -29,6 +29,7 @@ EXPORTS = (
     "nf4b_gemm_ex",
     "nf4b_gemm_workspace_size",
     "nf4b_gemm_noalloc",
+    "nf4b_gemm_gated",
     "nf4b_dequantize",
     "nf4b_rms_norm",
     "nf4b_rope",
@@ -58,7 +59,7 @@ class Nf4Weight(ctypes.Structure):
 class GemmOpts(ctypes.Structure):
     """`nf4b_gemm_opts`."""
 
-    _fields_ = [("prefetch_next", ctypes.POINTER(Nf4Weight))]
+    _fields_ = [("prefetch_next", ctypes.POINTER(Nf4Weight)), ("prefetch_next2", ctypes.POINTER(Nf4Weight))]
 
 
 class Nf4bError(RuntimeError):
@@ -82,6 +83,7 @@ def _declare(lib) -> None:
         "nf4b_device_error": (i32, [i32]),
         "nf4b_gemm": (i32, [wp, vp, vp, i32, i32, vp, vp, sz, vp]),
         "nf4b_gemm_ex": (i32, [wp, vp, vp, i32, i32, vp, vp, sz, ctypes.POINTER(GemmOpts), vp]),
+        "nf4b_gemm_gated": (i32, [wp, wp, vp, vp, i32, vp, sz, ctypes.POINTER(GemmOpts), vp]),
         "nf4b_gemm_workspace_size": (sz, [wp, i32]),
         "nf4b_gemm_noalloc": (i32, [wp, vp, vp, i32, i32, vp, vp]),
         "nf4b_dequantize": (i32, [wp, vp, vp]),

@@ -98,6 +98,31 @@ int launch_status(cudaError_t e, const char* what) {
 // The pair GEMV reads two adjacent 64-block scales at once (a 2-byte code pair
 // or an 8-byte fp32 pair) and assumes an even block and its successor share a
 // second-level block.
+// The byte ranges of an L2 prefetch hint: the packed codes and the first-level
+// scales of each named weight (16-byte aligned, whole 16-byte chunks).
+void prefetch_ranges(const nf4b_gemm_opts* opts, PrefetchHint* h) {
+  for (int i = 0; i < 4; ++i) {
+    h->ptr[i] = nullptr;
+    h->bytes[i] = 0;
+  }
+  if (opts == nullptr) return;
+  const nf4b_weight* ws[2] = {opts->prefetch_next, opts->prefetch_next2};
+  for (int i = 0; i < 2; ++i) {
+    const nf4b_weight* nx = ws[i];
+    if (nx == nullptr || nx->packed == nullptr || !aligned(nx->packed, 16) || nx->n_out <= 0 ||
+        nx->k_in <= 0 || nx->blocksize <= 0)
+      continue;
+    h->ptr[2 * i] = nx->packed;
+    h->bytes[2 * i] = ((long long)nx->n_out * nx->k_in / 2) & ~15LL;
+    const long long nb = (long long)nx->n_out * nx->k_in / nx->blocksize;
+    const void* sc = nx->nested ? (const void*)nx->absmax_code : (const void*)nx->absmax;
+    if (sc != nullptr && aligned(sc, 16)) {
+      h->ptr[2 * i + 1] = static_cast<const uint8_t*>(sc);
+      h->bytes[2 * i + 1] = (nb * (nx->nested ? 1 : 4)) & ~15LL;
+    }
+  }
+}
+
 bool use_pairs(const nf4b_weight* w, int rows) {
   if (rows > 4 || w->k_in % 128) return false;
   if (w->blocksize == 64) {
@@ -111,10 +136,12 @@ size_t gemv_workspace_bytes(const nf4b_weight* w, int rows, int sms) {
   GemvPlan a;
   gemv_plan(w->n_out, w->k_in, rows, sms, false, &a);
   size_t bytes = a.partial_bytes;
-  if (rows <= 4 && w->k_in % 128 == 0) {  // the pair kernel may serve this call
-    GemvPlan b;
-    gemv_plan(w->n_out, w->k_in, rows, sms, true, &b);
-    if (b.partial_bytes > bytes) bytes = b.partial_bytes;
+  if (rows <= 4 && w->k_in % 128 == 0) {  // the pair kernel may serve this call, plain or gated
+    for (int gated = 0; gated < 2; ++gated) {
+      GemvPlan b;
+      gemv_plan(w->n_out, w->k_in, rows, sms, true, &b, gated != 0);
+      if (b.partial_bytes > bytes) bytes = b.partial_bytes;
+    }
   }
   return GEMV_COUNTER_BYTES + bytes;
 }
@@ -123,6 +150,61 @@ int current_sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
   return gemv_sm_count(dev);
+}
+
+// One GEMV launch (rows <= GEMV_MAX_ROWS): plain, or the gated pair (w, w3)
+// of the pair kernel. Arguments already checked by the caller except the
+// workspace and the GEMV-specific limits.
+int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* y, int rows, int epi,
+              const void* operand, void* workspace, size_t workspace_bytes, const nf4b_gemm_opts* opts,
+              cudaStream_t s) {
+  if ((long long)(w->n_out + 15) / 16 > GEMV_MAX_TILES)
+    return fail(NF4B_ERR_SHAPE, "n_out %d exceeds the GEMV's %lld-row limit", w->n_out, GEMV_MAX_TILES * 16);
+  const bool pairs = use_pairs(w, rows);
+  const bool gated = w3 != nullptr;
+  if (gated && !(pairs && use_pairs(w3, rows)))
+    return fail(NF4B_ERR_SHAPE, "the gated GEMV serves 1..4 rows with k_in %% 128 == 0 (got %d rows, k_in %d)",
+                rows, w->k_in);
+  const int sms = current_sm_count();
+  GemvPlan plan;
+  gemv_plan(w->n_out, w->k_in, rows, sms, pairs, &plan, gated);
+  const size_t need = gemv_workspace_bytes(w, rows, sms);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(NF4B_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need,
+                workspace ? workspace_bytes : (size_t)0);
+  if (!aligned(workspace, 256)) return fail(NF4B_ERR_ALIGN, "workspace is not 256-byte aligned");
+  GemvParams p;
+  p.packed = w->packed;
+  p.a8 = w->absmax_code;
+  p.absmax = w->absmax;
+  p.code2 = w->code2;
+  p.offset = w->offset;
+  p.packed3 = gated ? w3->packed : nullptr;
+  p.a8_3 = gated ? w3->absmax_code : nullptr;
+  p.absmax3 = gated ? w3->absmax : nullptr;
+  p.code2_3 = gated && w3->nested ? w3->code2 : nullptr;
+  p.offset3 = gated ? w3->offset : 0.f;
+  p.gated = gated ? 1 : 0;
+  p.x_staged = (pairs && (long long)rows * w->k_in * 2 <= GEMV_PAIR_X_MAX) ? 1 : 0;
+  p.N = w->n_out;
+  p.K = w->k_in;
+  p.nested = w->nested ? 1 : 0;
+  p.bs_shift = log2i(w->blocksize);
+  p.bs2_shift = w->nested ? log2i(w->blocksize2) : 0;
+  p.x = static_cast<const uint16_t*>(x);
+  p.y = static_cast<uint16_t*>(y);
+  p.operand = static_cast<const uint16_t*>(operand);
+  p.M = rows;
+  p.epi = gated ? NF4B_EPI_NONE : epi;
+  p.counters = static_cast<int*>(workspace);
+  p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.counter_bytes);
+  p.units = plan.units;
+  p.warps_total = plan.warps_total;
+  p.uq = (int)(plan.units / plan.warps_total);
+  p.ur = (int)(plan.units % plan.warps_total);
+  p.blocks_per_tile = plan.blocks_per_tile;
+  prefetch_ranges(opts, &p.pf);
+  return launch_status(launch_gemv(p, plan.grid, pairs, s), "nf4 gemv launch");
 }
 
 }  // namespace
@@ -162,59 +244,8 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
   if ((st = check_device())) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
-  if (rows <= GEMV_MAX_ROWS) {
-    if ((long long)(w->n_out + 15) / 16 > GEMV_MAX_TILES)
-      return fail(NF4B_ERR_SHAPE, "n_out %d exceeds the GEMV's %lld-row limit", w->n_out,
-                  GEMV_MAX_TILES * 16);
-    const bool pairs = use_pairs(w, rows);
-    GemvPlan plan;
-    gemv_plan(w->n_out, w->k_in, rows, current_sm_count(), pairs, &plan);
-    const size_t need = gemv_workspace_bytes(w, rows, current_sm_count());
-    if (workspace == nullptr || workspace_bytes < need)
-      return fail(NF4B_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need,
-                  workspace ? workspace_bytes : (size_t)0);
-    if (!aligned(workspace, 256)) return fail(NF4B_ERR_ALIGN, "workspace is not 256-byte aligned");
-    GemvParams p;
-    p.packed = w->packed;
-    p.a8 = w->absmax_code;
-    p.absmax = w->absmax;
-    p.code2 = w->code2;
-    p.offset = w->offset;
-    p.N = w->n_out;
-    p.K = w->k_in;
-    p.nested = w->nested ? 1 : 0;
-    p.bs_shift = log2i(w->blocksize);
-    p.bs2_shift = w->nested ? log2i(w->blocksize2) : 0;
-    p.x = static_cast<const uint16_t*>(x);
-    p.y = static_cast<uint16_t*>(y);
-    p.operand = static_cast<const uint16_t*>(operand);
-    p.M = rows;
-    p.epi = epi;
-    p.counters = static_cast<int*>(workspace);
-    p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.counter_bytes);
-    p.units = plan.units;
-    p.warps_total = plan.warps_total;
-    p.uq = (int)(plan.units / plan.warps_total);
-    p.ur = (int)(plan.units % plan.warps_total);
-    p.blocks_per_tile = plan.blocks_per_tile;
-    p.pf_ptr = nullptr;
-    p.pf_bytes = 0;
-    p.pf2_ptr = nullptr;
-    p.pf2_bytes = 0;
-    const nf4b_weight* nx = opts ? opts->prefetch_next : nullptr;
-    if (nx != nullptr && nx->packed != nullptr && aligned(nx->packed, 16) && nx->n_out > 0 &&
-        nx->k_in > 0 && nx->blocksize > 0) {
-      p.pf_ptr = nx->packed;
-      p.pf_bytes = ((long long)nx->n_out * nx->k_in / 2) & ~15LL;
-      const long long nb = (long long)nx->n_out * nx->k_in / nx->blocksize;
-      const void* sc = nx->nested ? (const void*)nx->absmax_code : (const void*)nx->absmax;
-      if (sc != nullptr && aligned(sc, 16)) {
-        p.pf2_ptr = static_cast<const uint8_t*>(sc);
-        p.pf2_bytes = (nb * (nx->nested ? 1 : 4)) & ~15LL;
-      }
-    }
-    return launch_status(launch_gemv(p, plan.grid, pairs, s), "nf4 gemv launch");
-  }
+  if (rows <= GEMV_MAX_ROWS)
+    return gemv_call(w, nullptr, x, y, rows, epi, operand, workspace, workspace_bytes, opts, s);
 
   GemmParams p;
   p.packed = w->packed;
@@ -235,7 +266,24 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
   return launch_status(launch_gemm_tc(p, s), "nf4 tcgen05 gemm launch");
 }
 
-int nf4b_dequantize(const nf4b_weight* w, void* out, void* stream) {
+int nf4b_gemm_gated(const nf4b_weight* w1, const nf4b_weight* w3, const void* x, void* y, int rows,
+                    void* workspace, size_t workspace_bytes, const nf4b_gemm_opts* opts, void* stream) {
+  int st = check_weight(w1);
+  if (st) return st;
+  if ((st = check_weight(w3))) return st;
+  if (w3->n_out != w1->n_out || w3->k_in != w1->k_in || w3->blocksize != w1->blocksize ||
+      w3->nested != w1->nested || (w1->nested && w3->blocksize2 != w1->blocksize2))
+    return fail(NF4B_ERR_SHAPE, "w1 and w3 differ in shape or quantisation");
+  if (x == nullptr || y == nullptr) return fail(NF4B_ERR_ARG, "x or y is null");
+  if (rows <= 0) return fail(NF4B_ERR_SHAPE, "rows must be positive (got %d)", rows);
+  if (!aligned(x, 16)) return fail(NF4B_ERR_ALIGN, "x is not 16-byte aligned");
+  if (!aligned(y, 2)) return fail(NF4B_ERR_ALIGN, "y is not 2-byte aligned");
+  if ((st = check_device())) return st;
+  return gemv_call(w1, w3, x, y, rows, NF4B_EPI_NONE, nullptr, workspace, workspace_bytes, opts,
+                   reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nf4b_dequantize(const nf4b_weight* w, void* out, void* stream) {
   int st = check_weight(w);
   if (st) return st;
   if (out == nullptr) return fail(NF4B_ERR_ARG, "out is null");

@@ -52,17 +52,6 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
   return v;
 }
 
-// Stream [ptr, ptr + bytes) into L2 (fire and forget). Both must be 16-byte
-// multiples; issued in pieces of at most 32 KB.
-__device__ __forceinline__ void prefetch_l2(const void* ptr, long long bytes) {
-  const char* p = static_cast<const char*>(ptr);
-  while (bytes > 0) {
-    const uint32_t n = bytes > 32768 ? 32768u : (uint32_t)bytes;
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(n) : "memory");
-    p += n;
-    bytes -= n;
-  }
-}
 
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue, and wait for the previous kernel's results before reading them.

@@ -19,6 +19,12 @@ constexpr int GEMV_WARPS = NF4B_GEMV_WARPS;    // warps per CTA
 constexpr int GEMV_CTAS_PER_SM = NF4B_GEMV_CTAS;  // persistent grid: CTAs per SM
 constexpr int GEMV_LUT_BYTES = 256 * 256;      // pair table, 256 B stride, one copy per lane
 constexpr int GEMV_SMEM_BYTES = GEMV_LUT_BYTES + 256 * 4;  // + code2 copy
+// Pair kernel: pair table, code2 of W and of a gated pair's W3, then x staged
+// whole when it fits (rows * k_in * 2 <= GEMV_PAIR_X_MAX), so that two CTAs
+// still fit on an SM.
+constexpr int GEMV_PAIR_X_OFFSET = GEMV_LUT_BYTES + 2 * 256 * 4;
+constexpr int GEMV_PAIR_X_MAX = 40 * 1024;
+constexpr int GEMV_PAIR_SMEM_MAX = GEMV_PAIR_X_OFFSET + GEMV_PAIR_X_MAX;
 constexpr int GEMV_MAX_ROWS = 32;              // activation rows one launch takes
 // The workspace starts with a fixed-size region of per-tile arrival counters,
 // so calls on weights of different shapes never alias one another's counters
@@ -26,12 +32,47 @@ constexpr int GEMV_MAX_ROWS = 32;              // activation rows one launch tak
 constexpr size_t GEMV_COUNTER_BYTES = 64 * 1024;
 constexpr long long GEMV_MAX_TILES = GEMV_COUNTER_BYTES / 4;
 
+// Byte ranges (16-byte aligned, whole 16-byte chunks) that a launch streams
+// into L2 for later launches: packed codes and first-level scales of up to
+// two weights. Each warp of the persistent grid takes an equal share.
+struct PrefetchHint {
+  const uint8_t* ptr[4];
+  long long bytes[4];
+};
+
+// Warp gw's share (of W) of every hinted range, streamed into L2 with bulk
+// prefetches (fire and forget; at most 32 KB each).
+__device__ __forceinline__ void prefetch_share(const PrefetchHint& h, long long gw, long long W) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const long long chunks = h.bytes[i] >> 4;
+    if (chunks <= 0) continue;
+    const long long a = (gw * chunks / W) << 4, b = ((gw + 1) * chunks / W) << 4;
+    const char* ptr = reinterpret_cast<const char*>(h.ptr[i]) + a;
+    for (long long left = b - a; left > 0;) {
+      const uint32_t n = left > 32768 ? 32768u : (uint32_t)left;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(n) : "memory");
+      ptr += n;
+      left -= n;
+    }
+  }
+}
+
 struct GemvParams {
   const uint8_t* packed;
   const uint8_t* a8;
   const float* absmax;
   const float* code2;
   float offset;
+  // Gated pair (pair kernel only): W3, same shape and quantisation as W; the
+  // output is the FeedForward gate of x W^T and x W3^T. code2_3 is null otherwise.
+  const uint8_t* packed3;
+  const uint8_t* a8_3;
+  const float* absmax3;
+  const float* code2_3;
+  float offset3;
+  int gated;
+  int x_staged;  // pair kernel: x is copied whole into shared memory first
   int N, K;
   int nested;
   int bs_shift;
@@ -51,10 +92,7 @@ struct GemvParams {
   int uq, ur;
   // Optional L2 prefetch of the weight the NEXT call reads (packed codes and
   // its first-level scales), issued by each warp once its own loads are done.
-  const uint8_t* pf_ptr;
-  long long pf_bytes;
-  const uint8_t* pf2_ptr;
-  long long pf2_bytes;
+  PrefetchHint pf;
 };
 
 struct GemvPlan {
@@ -71,7 +109,8 @@ struct GemvPlan {
 int gemv_sm_count(int dev);
 // `pairs`: use the pair kernel (units of 128 codes; up to 4 activation rows,
 // k_in % 128 == 0, scale arrays aligned for its paired loads).
-void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan);
+// `gated`: the pair kernel's gated mode (tiles of 2 * k_in / 128 units).
+void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan, bool gated = false);
 cudaError_t launch_gemv(const GemvParams& p, int grid, bool pairs, cudaStream_t stream);
 
 // ---- dequantisation (nf4_dequant.cu) ---------------------------------------

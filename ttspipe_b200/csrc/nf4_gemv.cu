@@ -41,6 +41,9 @@
 #ifndef NF4B_GEMV_PAIR_DEPTH
 #define NF4B_GEMV_PAIR_DEPTH 3  // 128-code units each warp keeps in flight
 #endif
+#ifndef NF4B_GEMV_PREFETCH_EARLY
+#define NF4B_GEMV_PREFETCH_EARLY 1  // stream the hinted weight into L2 at kernel start (0: at the end)
+#endif
 
 namespace nf4b {
 
@@ -94,6 +97,8 @@ __device__ __forceinline__ void build_tables(uint8_t* smem, const GemvParams& p)
   if (p.nested) {
     float* code2_s = reinterpret_cast<float*>(smem + GEMV_LUT_BYTES);
     for (int i = threadIdx.x; i < 256; i += kThreads) code2_s[i] = p.code2[i];
+    if (p.code2_3 != nullptr)
+      for (int i = threadIdx.x; i < 256; i += kThreads) code2_s[256 + i] = p.code2_3[i];
   }
 }
 
@@ -143,18 +148,9 @@ __device__ __forceinline__ void finish_tile(const GemvParams& p, int rt, int u0,
   }
 }
 
-// This warp's share of the next call's weight, streamed into L2.
+// This warp's share of the hinted ranges, streamed into L2.
 __device__ __forceinline__ void prefetch_next(const GemvParams& p, int gw, int lane) {
-  if (lane != 0) return;
-  const long long W = p.warps_total;
-  if (p.pf_bytes > 0) {
-    const long long a = (gw * (p.pf_bytes >> 4) / W) << 4, b = ((gw + 1) * (p.pf_bytes >> 4) / W) << 4;
-    if (b > a) prefetch_l2(p.pf_ptr + a, b - a);
-  }
-  if (p.pf2_bytes > 0) {
-    const long long a = (gw * (p.pf2_bytes >> 4) / W) << 4, b = ((gw + 1) * (p.pf2_bytes >> 4) / W) << 4;
-    if (b > a) prefetch_l2(p.pf2_ptr + a, b - a);
-  }
+  if (lane == 0) prefetch_share(p.pf, gw, p.warps_total);
 }
 
 // ---------------------------------------------------------------------------
@@ -168,11 +164,99 @@ struct PairSlot {
   float sa, sb;     // plain: even-block absmax; nested: absmax2
 };
 
-template <int P>
+// Sum of `n` partial slots (stride `stride` floats) in slot order, four loads
+// in flight at a time; the association is ((0 + s0) + s1) + ... whatever n is.
+__device__ __forceinline__ float sum_slots(const float* p, size_t stride, int n) {
+  float v = 0.f;
+  int c = 0;
+  for (; c + 4 <= n; c += 4) {
+    const float a = __ldcg(p + c * stride), b = __ldcg(p + (c + 1) * stride);
+    const float d = __ldcg(p + (c + 2) * stride), e = __ldcg(p + (c + 3) * stride);
+    v += a;
+    v += b;
+    v += d;
+    v += e;
+  }
+  for (; c < n; ++c) v += __ldcg(p + c * stride);
+  return v;
+}
+
+// The gate of a W1/W3 pair at the fork's rounding points:
+// bf16(bf16(silu(bf16(x W1))) * bf16(x W3)) (app/engine/fusedlayer.py:265-266).
+__device__ __forceinline__ uint16_t gate_bf16(float v1, float v3) {
+  const float a = round_bf(v1);
+  const float s = round_bf(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))));
+  return f2bf(__fmul_rn(s, round_bf(v3)));
+}
+
+// Finish row tile `rt` of the pair kernel. Lane (g, t) holds rows g and g+8 of
+// activation row t for each half H (W, and W3 of a gated pair). Split tiles go
+// through the workspace: slot layout [slot][half][activation row][N].
+template <bool kGated>
+__device__ __forceinline__ void finish_pair_tile(const GemvParams& p, int rt, int u0, int u1, int gw,
+                                                 int g, int t, int lane, float a0, float b0, float a1,
+                                                 float b1) {
+  constexpr int H = kGated ? 2 : 1;
+  const int per_tile = p.blocks_per_tile * H;
+  const int t0 = rt * per_tile, t1 = t0 + per_tile - 1;
+  const bool whole = (t0 >= u0) && (t1 < u1);
+  const int N = p.N, M = p.M;
+  const int ra = rt * 16 + g, rb = ra + 8;
+  float v[2][2] = {{a0, b0}, {a1, b1}};  // [half][row g / g + 8]
+  if (!whole) {
+    const int w_lo = warp_of(t0, p.uq, p.ur);
+    const int n_contrib = warp_of(t1, p.uq, p.ur) - w_lo + 1;
+    const size_t MN = (size_t)M * N;
+    float* slot = p.partial + (size_t)(gw - w_lo) * H * MN + (size_t)t * N;
+    if (t < M) {
+#pragma unroll
+      for (int h = 0; h < H; ++h) {
+        if (ra < N) __stcg(slot + h * MN + ra, v[h][0]);
+        if (rb < N) __stcg(slot + h * MN + rb, v[h][1]);
+      }
+    }
+    // The warp barrier orders every lane's partial before lane 0's release
+    // (fence + arrival); the last arriver's acquire orders the reads after it.
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) {
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
+      old = atomic_add_acq_rel(p.counters + rt, 1);
+    }
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old != n_contrib - 1) return;
+    if (lane == 0) p.counters[rt] = 0;
+    __syncwarp();
+    if (t < M) {
+      const float* base = p.partial + (size_t)t * N;
+#pragma unroll
+      for (int h = 0; h < H; ++h) {
+        v[h][0] = ra < N ? sum_slots(base + h * MN + ra, H * MN, n_contrib) : 0.f;
+        v[h][1] = rb < N ? sum_slots(base + h * MN + rb, H * MN, n_contrib) : 0.f;
+      }
+    }
+  }
+  if (t >= M) return;
+  const size_t oa = (size_t)t * N + ra, ob = (size_t)t * N + rb;
+  if (kGated) {
+    if (ra < N) p.y[oa] = gate_bf16(v[0][0], v[1][0]);
+    if (rb < N) p.y[ob] = gate_bf16(v[0][1], v[1][1]);
+  } else {
+    if (ra < N) p.y[oa] = epilogue(v[0][0], p.epi, p.operand, oa);
+    if (rb < N) p.y[ob] = epilogue(v[0][1], p.epi, p.operand, ob);
+  }
+}
+
+// Pair kernel. Units are numbered tile-major; within a tile, the k units of W
+// and then (gated pair) those of W3, so one warp run covers both halves of a
+// tile where it can and the finisher sees both.
+template <int P, bool kGated>
 __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const uint8_t* lut = smem;
   const float* code2_s = reinterpret_cast<const float*>(smem + GEMV_LUT_BYTES);
+  const float* code2_s3 = code2_s + 256;
+  const uint8_t* xs = smem + GEMV_PAIR_X_OFFSET;
 
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * kWarps + (threadIdx.x >> 5);
@@ -180,27 +264,50 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvPa
   const int u0 = active ? gw * p.uq + min(gw, p.ur) : 0;
   const int u1 = active ? u0 + p.uq + (gw < p.ur ? 1 : 0) : 0;
   const int g = lane >> 2, t = lane & 3;
-  const int B = p.blocks_per_tile;  // 128-code units per row tile
+  const int B = p.blocks_per_tile;  // 128-code units per row tile and half
+  const int per_tile = kGated ? 2 * B : B;
   const int N = p.N, K = p.K, M = p.M;
   const int row_bytes = K >> 1;
   const uint32_t lane_base = (uint32_t)lane * 4u;
   const bool bs64 = p.bs_shift == 6;
   const int nblk = K >> p.bs_shift;  // scale blocks per weight row
 
-  int lt = u0 / B, lk = u0 - (u0 / B) * B;
-  int ct = lt, ck = lk;
+  // Load cursor: tile lt, half lh, k unit lk (incremental, no divisions).
+  int lt = u0 / per_tile, lk = u0 - lt * per_tile, lh = 0;
+  if (kGated && lk >= B) {
+    lh = 1;
+    lk -= B;
+  }
+  int ct = lt, ch = lh, ck = lk;
 
-  // Row pointers of the tile being loaded, refreshed when the tile changes.
+  // Row pointers and scale arrays of the tile/half being loaded.
   const uint8_t* pa = nullptr;
   const uint8_t* pb = nullptr;
+  const uint8_t* a8 = p.a8;
+  const float* absmax = p.absmax;
   int ra = 0, rb = 0;
-  auto set_rows = [&](int rt) {
+  auto set_rows = [&](int rt, int h) {
     ra = min(rt * 16 + g, N - 1);
     rb = min(rt * 16 + g + 8, N - 1);
-    pa = p.packed + (size_t)ra * row_bytes + t * 16;
-    pb = p.packed + (size_t)rb * row_bytes + t * 16;
+    const uint8_t* base = (kGated && h) ? p.packed3 : p.packed;
+    a8 = (kGated && h) ? p.a8_3 : p.a8;
+    absmax = (kGated && h) ? p.absmax3 : p.absmax;
+    pa = base + (size_t)ra * row_bytes + t * 16;
+    pb = base + (size_t)rb * row_bytes + t * 16;
   };
-  set_rows(lt);
+  set_rows(lt, lh);
+  auto step_load = [&]() {
+    if (++lk == B) {
+      lk = 0;
+      if (kGated && lh == 0) {
+        lh = 1;
+      } else {
+        lh = 0;
+        ++lt;
+      }
+      set_rows(lt, lh);
+    }
+  };
 
   auto load = [&](int kb2, PairSlot& s) {
     s.wa = ld_stream_u4(pa + kb2 * 64);
@@ -210,23 +317,23 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvPa
     const int be_b = rb * nblk + ((kb2 * 128) >> p.bs_shift);
     if (p.nested) {
       if (bs64) {  // two adjacent codes; even index, so 2-byte aligned
-        s.qa = __ldg(reinterpret_cast<const uint16_t*>(p.a8 + be_a));
-        s.qb = __ldg(reinterpret_cast<const uint16_t*>(p.a8 + be_b));
+        s.qa = __ldg(reinterpret_cast<const uint16_t*>(a8 + be_a));
+        s.qb = __ldg(reinterpret_cast<const uint16_t*>(a8 + be_b));
       } else {     // both halves share one scale
-        s.qa = __ldg(p.a8 + be_a) * 0x101u;
-        s.qb = __ldg(p.a8 + be_b) * 0x101u;
+        s.qa = __ldg(a8 + be_a) * 0x101u;
+        s.qb = __ldg(a8 + be_b) * 0x101u;
       }
       // an even block and the next share their second-level block
-      s.sa = __ldg(p.absmax + (be_a >> p.bs2_shift));
-      s.sb = __ldg(p.absmax + (be_b >> p.bs2_shift));
+      s.sa = __ldg(absmax + (be_a >> p.bs2_shift));
+      s.sb = __ldg(absmax + (be_b >> p.bs2_shift));
     } else if (bs64) {
-      const float2 va = __ldg(reinterpret_cast<const float2*>(p.absmax + be_a));
-      const float2 vb = __ldg(reinterpret_cast<const float2*>(p.absmax + be_b));
+      const float2 va = __ldg(reinterpret_cast<const float2*>(absmax + be_a));
+      const float2 vb = __ldg(reinterpret_cast<const float2*>(absmax + be_b));
       s.sa = va.x; s.qa = __float_as_uint(va.y);
       s.sb = vb.x; s.qb = __float_as_uint(vb.y);
     } else {
-      s.sa = __ldg(p.absmax + be_a); s.qa = __float_as_uint(s.sa);
-      s.sb = __ldg(p.absmax + be_b); s.qb = __float_as_uint(s.sb);
+      s.sa = __ldg(absmax + be_a); s.qa = __float_as_uint(s.sa);
+      s.sb = __ldg(absmax + be_b); s.qb = __float_as_uint(s.sb);
     }
   };
 
@@ -235,23 +342,35 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvPa
   for (int i = 0; i < P; ++i)
     if (u0 + i < u1) {
       load(lk, ring[i]);
-      if (++lk == B) { lk = 0; ++lt; set_rows(lt); }
+      step_load();
     }
   // The tables are built while the first weight loads are in flight.
   build_tables(smem, p);
   __syncthreads();
   pdl_launch_dependents();
-  if (!active) return;
-
+  if (active && NF4B_GEMV_PREFETCH_EARLY) prefetch_next(p, gw, lane);
   pdl_wait();
+  // x, written by earlier work on the stream, is staged once per CTA so that
+  // no unit waits on an L2 round trip for its slice of it.
+  if (p.x_staged) {
+    const int n16 = (M * K) >> 3;
+    const uint4* src = reinterpret_cast<const uint4*>(p.x);
+    uint4* dst = reinterpret_cast<uint4*>(smem + GEMV_PAIR_X_OFFSET);
+    for (int i = threadIdx.x; i < n16; i += kThreads) dst[i] = __ldcg(src + i);
+    __syncthreads();
+  }
+  if (!active) return;
 
   // x: column c of the MMA is (activation row c >> 1, block parity c & 1);
   // lane (g, t) supplies column g for codes of block parity t >> 1.
   const int xtok = g >> 1;
   const bool xlane = (xtok < M) && ((g & 1) == (t >> 1));
-  const uint4* xrow = reinterpret_cast<const uint4*>(p.x + (size_t)(xlane ? xtok : 0) * K) + t * 4;
+  const size_t xrow_off = (size_t)(xlane ? xtok : 0) * K * 2 + t * 64;  // bytes
+  const uint4* xrow = reinterpret_cast<const uint4*>(
+      (p.x_staged ? xs : reinterpret_cast<const uint8_t*>(p.x)) + xrow_off);
 
-  float acc_a = 0.f, acc_b = 0.f;  // rows g, g+8 for activation row t
+  float acc_a = 0.f, acc_b = 0.f;    // W (or W1): rows g, g+8 for activation row t
+  float acc3_a = 0.f, acc3_b = 0.f;  // gated pair: W3
   for (int base = u0; base < u1; base += P) {
 #pragma unroll
     for (int i = 0; i < P; ++i) {
@@ -260,25 +379,35 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvPa
       const PairSlot cur = ring[i];
       if (u + P < u1) {
         load(lk, ring[i]);
-        if (++lk == B) { lk = 0; ++lt; set_rows(lt); }
+        step_load();
       }
-      const int rt = ct, kb2 = ck;
-      if (++ck == B) { ck = 0; ++ct; }
+      const int rt = ct, kb2 = ck, hh = ch;
+      if (++ck == B) {
+        ck = 0;
+        if (kGated && ch == 0) {
+          ch = 1;
+        } else {
+          ch = 0;
+          ++ct;
+        }
+      }
 
       float se_a, so_a, se_b, so_b;
       if (p.nested) {
-        se_a = nested_scale(code2_s[cur.qa & 0xFFu], cur.sa, p.offset);
-        so_a = nested_scale(code2_s[(cur.qa >> 8) & 0xFFu], cur.sa, p.offset);
-        se_b = nested_scale(code2_s[cur.qb & 0xFFu], cur.sb, p.offset);
-        so_b = nested_scale(code2_s[(cur.qb >> 8) & 0xFFu], cur.sb, p.offset);
+        const float* c2 = (kGated && hh) ? code2_s3 : code2_s;
+        const float off = (kGated && hh) ? p.offset3 : p.offset;
+        se_a = nested_scale(c2[cur.qa & 0xFFu], cur.sa, off);
+        so_a = nested_scale(c2[(cur.qa >> 8) & 0xFFu], cur.sa, off);
+        se_b = nested_scale(c2[cur.qb & 0xFFu], cur.sb, off);
+        so_b = nested_scale(c2[(cur.qb >> 8) & 0xFFu], cur.sb, off);
       } else {
         se_a = cur.sa; so_a = __uint_as_float(cur.qa); se_b = cur.sb; so_b = __uint_as_float(cur.qb);
       }
 
       uint4 xv[4];
-      if (xlane) {
+      if (xlane) {  // shared memory when staged, else global (generic loads)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) xv[j] = __ldg(xrow + kb2 * 16 + j);
+        for (int j = 0; j < 4; ++j) xv[j] = xrow[kb2 * 16 + j];
       } else {
 #pragma unroll
         for (int j = 0; j < 4; ++j) xv[j] = make_uint4(0, 0, 0, 0);
@@ -294,27 +423,31 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvPa
         const uint32_t a2 = lut_lookup(lut, w0, lut_sel(j0 + 1), lane_base);
         const uint32_t a1 = lut_lookup(lut, w1, lut_sel(j0), lane_base);
         const uint32_t a3 = lut_lookup(lut, w1, lut_sel(j0 + 1), lane_base);
-        const uint4& xs = xv[s >> 1];
-        const uint32_t b0 = (s & 1) ? xs.z : xs.x;
-        const uint32_t b1 = (s & 1) ? xs.w : xs.y;
+        const uint4& xq = xv[s >> 1];
+        const uint32_t b0 = (s & 1) ? xq.z : xq.x;
+        const uint32_t b1 = (s & 1) ? xq.w : xq.y;
         mma_bf16_16816(d, a0, a1, a2, a3, b0, b1);
       }
       // d0 = (row g, col 2t) = even block, d1 = odd block; d2/d3 for row g+8.
-      acc_a = fmaf(se_a, d[0], acc_a);
-      acc_a = fmaf(so_a, d[1], acc_a);
-      acc_b = fmaf(se_b, d[2], acc_b);
-      acc_b = fmaf(so_b, d[3], acc_b);
+      if (kGated && hh) {
+        acc3_a = fmaf(se_a, d[0], acc3_a);
+        acc3_a = fmaf(so_a, d[1], acc3_a);
+        acc3_b = fmaf(se_b, d[2], acc3_b);
+        acc3_b = fmaf(so_b, d[3], acc3_b);
+      } else {
+        acc_a = fmaf(se_a, d[0], acc_a);
+        acc_a = fmaf(so_a, d[1], acc_a);
+        acc_b = fmaf(se_b, d[2], acc_b);
+        acc_b = fmaf(so_b, d[3], acc_b);
+      }
 
-      if (kb2 == B - 1 || u == u1 - 1) {
-        const int rows[2] = {rt * 16 + g, rt * 16 + g + 8};
-        const int toks[2] = {t, t};
-        const float vals[2] = {acc_a, acc_b};
-        finish_tile<2>(p, rt, u0, u1, gw, rows, toks, vals, lane);
-        acc_a = acc_b = 0.f;
+      if ((kb2 == B - 1 && (!kGated || hh == 1)) || u == u1 - 1) {
+        finish_pair_tile<kGated>(p, rt, u0, u1, gw, g, t, lane, acc_a, acc_b, acc3_a, acc3_b);
+        acc_a = acc_b = acc3_a = acc3_b = 0.f;
       }
     }
   }
-  prefetch_next(p, gw, lane);
+  if (!NF4B_GEMV_PREFETCH_EARLY) prefetch_next(p, gw, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -384,6 +517,7 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_block_kernel(const GemvP
   __syncthreads();
   pdl_launch_dependents();
   if (!active) return;
+  if (NF4B_GEMV_PREFETCH_EARLY) prefetch_next(p, gw, lane);
 
   pdl_wait();
 
@@ -466,24 +600,23 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_block_kernel(const GemvP
       }
     }
   }
-  prefetch_next(p, gw, lane);
+  if (!NF4B_GEMV_PREFETCH_EARLY) prefetch_next(p, gw, lane);
 }
 
 template <typename Kernel>
 cudaError_t launch_kernel(Kernel kernel, const GemvParams& p, int grid, cudaStream_t stream,
-                          bool* configured) {
+                          bool* configured, int smem = GEMV_SMEM_BYTES, int smem_max = GEMV_SMEM_BYTES) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = GEMV_SMEM_BYTES;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -508,10 +641,11 @@ int gemv_sm_count(int dev) {
   return g_sm_count[dev];
 }
 
-void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan) {
+void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan, bool gated) {
   const long long tiles = (N + 15) / 16;
   const long long B = pairs ? K / 128 : K / 64;
-  const long long U = tiles * B;
+  const long long H = (pairs && gated) ? 2 : 1;  // halves per tile
+  const long long U = tiles * B * H;
   const long long ctas = (long long)sm_count * GEMV_CTAS_PER_SM;
   long long W = ctas * kWarps;
   if (W > U) W = U;
@@ -520,18 +654,24 @@ void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan) {
   plan->blocks_per_tile = (int)B;
   plan->warps_total = (int)W;
   plan->grid = (int)((W + kWarps - 1) / kWarps);
-  // Every warp owns at least floor(U / W) units, so a tile of B units meets at
-  // most ceil(B / floor(U / W)) + 1 of them.
+  // Every warp owns at least floor(U / W) units, so a tile of B * H units
+  // meets at most ceil(B * H / floor(U / W)) + 1 of them.
   const long long per = U / W;
-  plan->slots = (int)((B + per - 1) / per + 1);
+  plan->slots = (int)((B * H + per - 1) / per + 1);
   plan->counter_bytes = GEMV_COUNTER_BYTES;
-  plan->partial_bytes = (size_t)plan->slots * M * N * sizeof(float);
+  plan->partial_bytes = (size_t)plan->slots * H * M * N * sizeof(float);
 }
 
 cudaError_t launch_gemv(const GemvParams& p, int grid, bool pairs, cudaStream_t stream) {
-  static bool cfg_pair[64] = {}, cfg1[64] = {}, cfg2[64] = {}, cfg4[64] = {};
-  if (pairs)
-    return launch_kernel(nf4_gemv_pair_kernel<NF4B_GEMV_PAIR_DEPTH>, p, grid, stream, cfg_pair);
+  static bool cfg_pair[64] = {}, cfg_gated[64] = {}, cfg1[64] = {}, cfg2[64] = {}, cfg4[64] = {};
+  if (pairs) {
+    const int smem = GEMV_PAIR_X_OFFSET + (p.x_staged ? p.M * p.K * 2 : 0);
+    if (p.gated)
+      return launch_kernel(nf4_gemv_pair_kernel<NF4B_GEMV_PAIR_DEPTH, true>, p, grid, stream, cfg_gated,
+                           smem, GEMV_PAIR_SMEM_MAX);
+    return launch_kernel(nf4_gemv_pair_kernel<NF4B_GEMV_PAIR_DEPTH, false>, p, grid, stream, cfg_pair,
+                         smem, GEMV_PAIR_SMEM_MAX);
+  }
   if (p.M <= 8) return launch_kernel(nf4_gemv_block_kernel<1, 4>, p, grid, stream, cfg1);
   if (p.M <= 16) return launch_kernel(nf4_gemv_block_kernel<2, 2>, p, grid, stream, cfg2);
   return launch_kernel(nf4_gemv_block_kernel<4, 2>, p, grid, stream, cfg4);

@@ -5,10 +5,11 @@ Drop-in for the reference's ``app/engine/fusedlayer.py`` (``decode_block``,
 (app/engine/fusedlayer.py:212-269):
 
     rms_norm -> wqkv -> qk_rope_kv -> decode_attention -> wo(+x)
-             -> rms_norm -> w1 -> w3(silu(w1) * .) -> w2(+h)
+             -> rms_norm -> [w1, w3: silu(w1) * w3] -> w2(+h)
 
 The reference's two attention launches (attn_partial + attn_combine) are one
-here (the last CTA of each KV head merges the partials). The position is read
+here (the last CTA of each KV head merges the partials), and so are its w1 and
+w3 launches (``nf4gemv.matmul_gated``, same rounding points). The position is read
 on the device from ``input_pos`` and the attended window is the mask's width,
 so one captured CUDA graph per window serves every position in it. Anything
 that is not a single bf16 position of an eligible block returns None and
@@ -99,8 +100,12 @@ def decode_block(block, x, freqs_cis, mask, input_pos, next_block=None):
                               pos=input_pos, mask=None, window=int(mask.shape[-1]), max_len=max_len)
     h = nf4gemv.matmul(a.wo, y, epi=nf4gemv.EPI_RESIDUAL, operand=x, prefetch=ff.w1)
     hn = fusedops.rms_norm(h, block.ffn_norm.weight, block.ffn_norm.eps)
-    g1 = nf4gemv.matmul(ff.w1, hn, prefetch=ff.w3)
-    g = nf4gemv.matmul(ff.w3, hn, epi=nf4gemv.EPI_SILU_GATE, operand=g1, prefetch=ff.w2)
+    # w1 and w3 read the same input: one launch computes the gate
+    # silu(hn W1^T) * (hn W3^T) without writing hn W1^T out.
+    g = nf4gemv.matmul_gated(ff.w1, ff.w3, hn, prefetch=ff.w2)
+    if g is None:
+        g1 = nf4gemv.matmul(ff.w1, hn, prefetch=ff.w3)
+        g = nf4gemv.matmul(ff.w3, hn, epi=nf4gemv.EPI_SILU_GATE, operand=g1, prefetch=ff.w2)
     nxt = next_block.attention.wqkv if next_block is not None else None
     out = nf4gemv.matmul(ff.w2, g, epi=nf4gemv.EPI_RESIDUAL, operand=h, prefetch=nxt)
     _stats["fused"] += 1

@@ -184,14 +184,26 @@ def prepare(module) -> bool:
     return True
 
 
+def _prefetch_opts(prefetch):
+    """`nf4b_gemm_opts` naming up to two prepared linears to stream into L2, or None."""
+    if prefetch is None:
+        return None
+    mods = list(prefetch) if isinstance(prefetch, (list, tuple)) else [prefetch]
+    descs = [m._nf4_fast["desc"] for m in mods[:2] if getattr(m, "_nf4_fast", None) is not None]
+    if not descs:
+        return None
+    opts = _lib.GemmOpts(*[ctypes.pointer(d) for d in descs])
+    return ctypes.byref(opts)
+
+
 def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None):
     """``x @ module.weight.T`` for any number of input rows, or None if not applicable.
 
     `epi` fuses ``operand + xW`` (EPI_RESIDUAL) or ``silu(operand) * xW``
     (EPI_SILU_GATE); `operand` has the output's shape, bf16, on x's device.
-    `prefetch` (an extension; None in the reference's API) names the prepared
-    linear the next call will read: its weights are streamed into L2 while
-    this call finishes. Launches on ``torch.cuda.current_stream()``.
+    `prefetch` (an extension; None in the reference's API) names one or two
+    prepared linears that later calls will read: their weights are streamed
+    into L2 while this call runs. Launches on ``torch.cuda.current_stream()``.
     """
     import torch
 
@@ -230,12 +242,47 @@ def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None):
         need = int(L.nf4b_gemm_workspace_size(ctypes.byref(desc), rows))
         ws = _workspace(x.device, need)
         ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
-    opts = None
-    nxt = getattr(prefetch, "_nf4_fast", None) if prefetch is not None else None
-    if nxt is not None:
-        opts = ctypes.byref(_lib.GemmOpts(ctypes.pointer(nxt["desc"])))
+    opts = _prefetch_opts(prefetch)
     _lib.check(L.nf4b_gemm_ex(ctypes.byref(desc), flat.data_ptr(), out.data_ptr(), rows, int(epi),
                               op_ptr, ws_ptr, ws_bytes, opts, ctypes.c_void_p(stream.cuda_stream)))
+    _stats["fast"] += 1
+    return out.view(*x.shape[:-1], N)
+
+
+def matmul_gated(w1, w3, x, *, prefetch=None):
+    """``silu(x @ w1.weight.T) * (x @ w3.weight.T)`` in ONE launch, with the
+    fork's rounding points (app/engine/fusedlayer.py:265-266: two ``matmul``
+    launches there, the second with EPI_SILU_GATE); x W1^T is never written
+    out. An extension of the reference's API. Serves 1..4 rows with
+    in_features % 128 == 0; returns None otherwise (the caller then issues the
+    two matmuls) or if either linear is not prepared.
+    """
+    import torch
+
+    f1, f3 = getattr(w1, "_nf4_fast", None), getattr(w3, "_nf4_fast", None)
+    if f1 is None or f3 is None or x.dtype != torch.bfloat16 or x.device.type != "cuda":
+        return None
+    K, N = f1["K"], f1["M"]
+    if (f3["K"], f3["M"]) != (K, N) or x.shape[-1] != K or K % 128:
+        return None
+    flat = x.reshape(-1, K)
+    if not flat.is_contiguous() or flat.data_ptr() % 16:
+        flat = flat.contiguous()
+        if flat.data_ptr() % 16:
+            return None
+    rows = flat.shape[0]
+    if rows < 1 or rows > 4:
+        return None
+    if not available():
+        raise RuntimeError(f"nf4 kernels unavailable: {_unavailable}")
+    L = _lib.lib()
+    need = int(L.nf4b_gemm_workspace_size(ctypes.byref(f1["desc"]), rows))
+    ws = _workspace(x.device, need)
+    out = torch.empty((rows, N), dtype=torch.bfloat16, device=x.device)
+    stream = torch.cuda.current_stream(x.device)
+    _lib.check(L.nf4b_gemm_gated(ctypes.byref(f1["desc"]), ctypes.byref(f3["desc"]), flat.data_ptr(),
+                                 out.data_ptr(), rows, ws.data_ptr(), ws.numel(), _prefetch_opts(prefetch),
+                                 ctypes.c_void_p(stream.cuda_stream)))
     _stats["fast"] += 1
     return out.view(*x.shape[:-1], N)
 
