@@ -261,7 +261,7 @@ class StepPlan:
     Each launch names the weights of the launch `distance` places later as an
     L2 prefetch hint (0: no hints)."""
 
-    def __init__(self, layers, io: StepIO, ws, mode: str = "decode", distance: int = 2):
+    def __init__(self, layers, io: StepIO, ws, mode: str = "decode", distance: int = 0):
         from ttspipe_b200 import _lib
 
         self.L = _lib.lib()
@@ -315,12 +315,14 @@ class StepPlan:
                 raise RuntimeError(f"{launch[0]} launch failed: {_lib.last_error()}")
 
 
-def roofline_traffic():
-    """Per-launch DRAM traffic of the GEMV from the committed ncu summary, if any."""
+def roofline_traffic(alg_bytes_per_launch: float):
+    """DRAM bytes per launch of the GEMV: the traffic/algorithmic ratio of the
+    committed ncu capture (a 9728x2560 launch, small enough to capture) scaled to
+    this workload's algorithmic bytes per launch; None without the capture."""
     p = ROOT / "profiles" / "nf4_gemv_decode_traffic.json"
     try:
         d = json.loads(p.read_text())
-        return float(d["dram_bytes_per_launch"])
+        return round(float(d["traffic_to_algorithmic"]) * alg_bytes_per_launch)
     except Exception:  # noqa: BLE001
         return None
 
@@ -444,7 +446,7 @@ def run_gpu(args):
     peaks, peak_kind = measured_peaks()
     hbm = float(peaks["hbm_gbs"])
     achieved = STEP_BYTES / (secs / args.steps) / 1e9
-    traffic = roofline_traffic()
+    traffic = roofline_traffic(STEP_BYTES / len(plan))
     result = None
     if rank == 0:
         result = {
@@ -610,8 +612,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--detail", action="store_true")
     ap.add_argument("--mode", default="decode", choices=sorted(MODES))
-    ap.add_argument("--prefetch-distance", type=int, default=2,
-                    help="launches ahead whose weights each launch streams into L2 (0: none)")
+    ap.add_argument("--prefetch-distance", type=int, default=0,
+                    help="launches ahead whose weights each launch streams into L2 (0: none; "
+                         "measured slower at 1-3 on B200, so off by default)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

@@ -125,11 +125,12 @@ void prefetch_ranges(const nf4b_gemm_opts* opts, PrefetchHint* h) {
 
 bool use_pairs(const nf4b_weight* w, int rows) {
   if (rows > 4 || w->k_in % 128) return false;
-  if (w->blocksize == 64) {
-    if (w->nested) return aligned(w->absmax_code, 2) && w->blocksize2 >= 2;
-    return aligned(w->absmax, 8);
-  }
-  return !w->nested || w->blocksize2 >= 1;
+  // The pair kernel copies scales with 4- and 8-byte cp.async: the 8-bit codes
+  // as 4-byte aligned windows, fp32 scales at their natural alignment (paired
+  // when blocks are 64 codes).
+  if (w->nested)
+    return aligned(w->absmax_code, 4) && aligned(w->absmax, 4) && w->blocksize2 >= (w->blocksize == 64 ? 2 : 1);
+  return aligned(w->absmax, w->blocksize == 64 ? 8 : 4);
 }
 
 size_t gemv_workspace_bytes(const nf4b_weight* w, int rows, int sms) {

@@ -19,12 +19,27 @@ constexpr int GEMV_WARPS = NF4B_GEMV_WARPS;    // warps per CTA
 constexpr int GEMV_CTAS_PER_SM = NF4B_GEMV_CTAS;  // persistent grid: CTAs per SM
 constexpr int GEMV_LUT_BYTES = 256 * 256;      // pair table, 256 B stride, one copy per lane
 constexpr int GEMV_SMEM_BYTES = GEMV_LUT_BYTES + 256 * 4;  // + code2 copy
-// Pair kernel: pair table, code2 of W and of a gated pair's W3, then x staged
-// whole when it fits (rows * k_in * 2 <= GEMV_PAIR_X_MAX), so that two CTAs
-// still fit on an SM.
-constexpr int GEMV_PAIR_X_OFFSET = GEMV_LUT_BYTES + 2 * 256 * 4;
+// Pair kernel: one CTA of GEMV_PAIR_WARPS warps per SM. Shared memory: the pair
+// table, code2 of W and of a gated pair's W3, each warp's ring of
+// GEMV_PAIR_STAGES unit stages (filled by cp.async), then x staged whole when
+// it fits (rows * k_in * 2 <= GEMV_PAIR_X_MAX).
+#ifndef NF4B_GEMV_PAIR_WARPS
+#define NF4B_GEMV_PAIR_WARPS 16
+#endif
+#ifndef NF4B_GEMV_PAIR_STAGES
+#define NF4B_GEMV_PAIR_STAGES 5
+#endif
+constexpr int GEMV_PAIR_WARPS = NF4B_GEMV_PAIR_WARPS;
+constexpr int GEMV_PAIR_STAGES = NF4B_GEMV_PAIR_STAGES;
+// One stage: rows g (512 B) and g + 8 (512 B) of a 16 x 128-code unit, then
+// 8 bytes of scale data for each of the 16 rows.
+constexpr int GEMV_PAIR_STAGE_BYTES = 1024 + 16 * 8;
+constexpr int GEMV_PAIR_STAGE_OFFSET = GEMV_LUT_BYTES + 2 * 256 * 4;
+constexpr int GEMV_PAIR_X_OFFSET =
+    GEMV_PAIR_STAGE_OFFSET + GEMV_PAIR_WARPS * GEMV_PAIR_STAGES * GEMV_PAIR_STAGE_BYTES;
 constexpr int GEMV_PAIR_X_MAX = 40 * 1024;
 constexpr int GEMV_PAIR_SMEM_MAX = GEMV_PAIR_X_OFFSET + GEMV_PAIR_X_MAX;
+static_assert(GEMV_PAIR_SMEM_MAX <= 227 * 1024, "pair kernel shared memory exceeds one CTA's limit");
 constexpr int GEMV_MAX_ROWS = 32;              // activation rows one launch takes
 // The workspace starts with a fixed-size region of per-tile arrival counters,
 // so calls on weights of different shapes never alias one another's counters

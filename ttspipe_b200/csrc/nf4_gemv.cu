@@ -38,9 +38,6 @@
 #include "common.cuh"
 #include "kernels.cuh"
 
-#ifndef NF4B_GEMV_PAIR_DEPTH
-#define NF4B_GEMV_PAIR_DEPTH 3  // 128-code units each warp keeps in flight
-#endif
 #ifndef NF4B_GEMV_PREFETCH_EARLY
 #define NF4B_GEMV_PREFETCH_EARLY 1  // stream the hinted weight into L2 at kernel start (0: at the end)
 #endif
@@ -88,17 +85,18 @@ __device__ __forceinline__ int atomic_add_acq_rel(int* addr, int v) {
 // Shared-memory tables: the NF4 pair table and (nested scales) code2. Entry
 // e's 32 per-lane copies are 128 contiguous bytes (stride 256), written eight
 // copies per 16-byte store.
+template <int THREADS = kThreads>
 __device__ __forceinline__ void build_tables(uint8_t* smem, const GemvParams& p) {
-  for (int i = threadIdx.x; i < 256 * 8; i += kThreads) {
+  for (int i = threadIdx.x; i < 256 * 8; i += THREADS) {
     const int e = i >> 3, part = i & 7;
     const uint32_t v = pack_bf16x2(c_nf4_code[e >> 4], c_nf4_code[e & 15]);
     *reinterpret_cast<uint4*>(smem + e * 256 + part * 16) = make_uint4(v, v, v, v);
   }
   if (p.nested) {
     float* code2_s = reinterpret_cast<float*>(smem + GEMV_LUT_BYTES);
-    for (int i = threadIdx.x; i < 256; i += kThreads) code2_s[i] = p.code2[i];
+    for (int i = threadIdx.x; i < 256; i += THREADS) code2_s[i] = p.code2[i];
     if (p.code2_3 != nullptr)
-      for (int i = threadIdx.x; i < 256; i += kThreads) code2_s[256 + i] = p.code2_3[i];
+      for (int i = threadIdx.x; i < 256; i += THREADS) code2_s[256 + i] = p.code2_3[i];
   }
 }
 
@@ -156,13 +154,6 @@ __device__ __forceinline__ void prefetch_next(const GemvParams& p, int gw, int l
 // ---------------------------------------------------------------------------
 // pair kernel: units of 16 rows x 128 codes, activation rows <= 4
 // ---------------------------------------------------------------------------
-
-struct PairSlot {
-  uint4 wa, wb;     // 16 packed bytes of rows g and g+8 (two 64-blocks per group)
-  uint32_t qa, qb;  // nested: 8-bit scale codes, even block in bits 0-7, odd in 8-15;
-                    // plain: the odd block's fp32 absmax bits
-  float sa, sb;     // plain: even-block absmax; nested: absmax2
-};
 
 // Sum of `n` partial slots (stride `stride` floats) in slot order, four loads
 // in flight at a time; the association is ((0 + s0) + s1) + ... whatever n is.
@@ -247,11 +238,43 @@ __device__ __forceinline__ void finish_pair_tile(const GemvParams& p, int rt, in
   }
 }
 
+// cp.async helpers (sm_80+ asynchronous global -> shared copies, tracked per
+// thread in commit groups).
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_8(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+// 4-byte copy of which only the first `src_bytes` (1..4) are read; the rest is
+// zero-filled.
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
 // Pair kernel. Units are numbered tile-major; within a tile, the k units of W
 // and then (gated pair) those of W3, so one warp run covers both halves of a
 // tile where it can and the finisher sees both.
-template <int P, bool kGated>
-__global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvParams p) {
+//
+// Each warp streams its run through a private ring of GEMV_PAIR_STAGES stages
+// in shared memory: unit u + S - 1 is requested (cp.async, one commit group
+// per unit) before unit u is computed, and `cp.async.wait_group S-1` releases
+// exactly unit u's group, so S - 1 units are always in flight regardless of
+// how the compiler schedules the arithmetic. Lane (g, t) copies the 16 bytes
+// of rows g and g + 8 it will multiply; lanes t = 0 and t = 1 also copy the
+// scale data of rows g and g + 8 for the whole warp.
+template <bool kGated>
+__global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1) nf4_gemv_pair_kernel(const GemvParams p) {
+  constexpr int S = GEMV_PAIR_STAGES;
+  constexpr int kT = GEMV_PAIR_WARPS * 32;
   extern __shared__ __align__(128) uint8_t smem[];
   const uint8_t* lut = smem;
   const float* code2_s = reinterpret_cast<const float*>(smem + GEMV_LUT_BYTES);
@@ -259,7 +282,8 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvPa
   const uint8_t* xs = smem + GEMV_PAIR_X_OFFSET;
 
   const int lane = threadIdx.x & 31;
-  const int gw = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int wib = threadIdx.x >> 5;  // warp in block
+  const int gw = blockIdx.x * GEMV_PAIR_WARPS + wib;
   const bool active = gw < p.warps_total;
   const int u0 = active ? gw * p.uq + min(gw, p.ur) : 0;
   const int u1 = active ? u0 + p.uq + (gw < p.ur ? 1 : 0) : 0;
@@ -271,6 +295,10 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvPa
   const uint32_t lane_base = (uint32_t)lane * 4u;
   const bool bs64 = p.bs_shift == 6;
   const int nblk = K >> p.bs_shift;  // scale blocks per weight row
+  const long long a8_total = (long long)N * nblk;
+
+  uint8_t* ring = smem + GEMV_PAIR_STAGE_OFFSET + wib * (S * GEMV_PAIR_STAGE_BYTES);
+  const uint32_t ring_s = smem_addr(ring);
 
   // Load cursor: tile lt, half lh, k unit lk (incremental, no divisions).
   int lt = u0 / per_tile, lk = u0 - lt * per_tile, lh = 0;
@@ -280,15 +308,17 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvPa
   }
   int ct = lt, ch = lh, ck = lk;
 
-  // Row pointers and scale arrays of the tile/half being loaded.
+  // Row pointers and scale arrays of the tile/half being loaded. Lanes t = 0
+  // and t = 1 copy the scales of row g and g + 8 respectively (row `sr`).
   const uint8_t* pa = nullptr;
   const uint8_t* pb = nullptr;
   const uint8_t* a8 = p.a8;
   const float* absmax = p.absmax;
-  int ra = 0, rb = 0;
+  int sr = 0;
   auto set_rows = [&](int rt, int h) {
-    ra = min(rt * 16 + g, N - 1);
-    rb = min(rt * 16 + g + 8, N - 1);
+    const int ra = min(rt * 16 + g, N - 1);
+    const int rb = min(rt * 16 + g + 8, N - 1);
+    sr = t == 0 ? ra : rb;
     const uint8_t* base = (kGated && h) ? p.packed3 : p.packed;
     a8 = (kGated && h) ? p.a8_3 : p.a8;
     absmax = (kGated && h) ? p.absmax3 : p.absmax;
@@ -308,44 +338,41 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvPa
       set_rows(lt, lh);
     }
   };
-
-  auto load = [&](int kb2, PairSlot& s) {
-    s.wa = ld_stream_u4(pa + kb2 * 64);
-    s.wb = ld_stream_u4(pb + kb2 * 64);
-    // 64-blocks 2*kb2 and 2*kb2+1 of each row.
-    const int be_a = ra * nblk + ((kb2 * 128) >> p.bs_shift);
-    const int be_b = rb * nblk + ((kb2 * 128) >> p.bs_shift);
-    if (p.nested) {
-      if (bs64) {  // two adjacent codes; even index, so 2-byte aligned
-        s.qa = __ldg(reinterpret_cast<const uint16_t*>(a8 + be_a));
-        s.qb = __ldg(reinterpret_cast<const uint16_t*>(a8 + be_b));
-      } else {     // both halves share one scale
-        s.qa = __ldg(a8 + be_a) * 0x101u;
-        s.qb = __ldg(a8 + be_b) * 0x101u;
+  // Request unit (cursor) into stage `st`: weights, and (lanes t < 2) scales.
+  auto issue = [&](int st) {
+    const uint32_t d = ring_s + st * GEMV_PAIR_STAGE_BYTES;
+    cp_async_16(d + lane * 16, pa + lk * 64);
+    cp_async_16(d + 512 + lane * 16, pb + lk * 64);
+    if (t < 2) {
+      const uint32_t ds = d + 1024 + (g + 8 * t) * 8;
+      const long long be = (long long)sr * nblk + ((lk * 128) >> p.bs_shift);
+      if (p.nested) {
+        // the 4-byte aligned window holding this unit's one or two 8-bit codes
+        const long long w0 = be & ~3LL;
+        const long long left = a8_total - w0;
+        cp_async_4(ds, a8 + w0, (uint32_t)(left < 4 ? left : 4));
+        // an even block and the next share their second-level block
+        cp_async_4(ds + 4, absmax + (be >> p.bs2_shift), 4u);
+      } else if (bs64) {
+        cp_async_8(ds, absmax + be);
+      } else {
+        cp_async_4(ds, absmax + be, 4u);
+        cp_async_4(ds + 4, absmax + be, 4u);
       }
-      // an even block and the next share their second-level block
-      s.sa = __ldg(absmax + (be_a >> p.bs2_shift));
-      s.sb = __ldg(absmax + (be_b >> p.bs2_shift));
-    } else if (bs64) {
-      const float2 va = __ldg(reinterpret_cast<const float2*>(absmax + be_a));
-      const float2 vb = __ldg(reinterpret_cast<const float2*>(absmax + be_b));
-      s.sa = va.x; s.qa = __float_as_uint(va.y);
-      s.sb = vb.x; s.qb = __float_as_uint(vb.y);
-    } else {
-      s.sa = __ldg(absmax + be_a); s.qa = __float_as_uint(s.sa);
-      s.sb = __ldg(absmax + be_b); s.qb = __float_as_uint(s.sb);
     }
   };
 
-  PairSlot ring[P];
+  // Prologue: S - 1 units requested (one group each, empty past the run).
 #pragma unroll
-  for (int i = 0; i < P; ++i)
+  for (int i = 0; i < S - 1; ++i) {
     if (u0 + i < u1) {
-      load(lk, ring[i]);
+      issue(i);
       step_load();
     }
-  // The tables are built while the first weight loads are in flight.
-  build_tables(smem, p);
+    cp_async_commit();
+  }
+  // The tables are built while the first units are in flight.
+  build_tables<kT>(smem, p);
   __syncthreads();
   pdl_launch_dependents();
   if (active && NF4B_GEMV_PREFETCH_EARLY) prefetch_next(p, gw, lane);
@@ -356,10 +383,13 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvPa
     const int n16 = (M * K) >> 3;
     const uint4* src = reinterpret_cast<const uint4*>(p.x);
     uint4* dst = reinterpret_cast<uint4*>(smem + GEMV_PAIR_X_OFFSET);
-    for (int i = threadIdx.x; i < n16; i += kThreads) dst[i] = __ldcg(src + i);
+    for (int i = threadIdx.x; i < n16; i += kT) dst[i] = __ldcg(src + i);
     __syncthreads();
   }
-  if (!active) return;
+  if (!active) {
+    cp_async_wait<0>();
+    return;
+  }
 
   // x: column c of the MMA is (activation row c >> 1, block parity c & 1);
   // lane (g, t) supplies column g for codes of block parity t >> 1.
@@ -371,82 +401,108 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_pair_kernel(const GemvPa
 
   float acc_a = 0.f, acc_b = 0.f;    // W (or W1): rows g, g+8 for activation row t
   float acc3_a = 0.f, acc3_b = 0.f;  // gated pair: W3
-  for (int base = u0; base < u1; base += P) {
-#pragma unroll
-    for (int i = 0; i < P; ++i) {
-      const int u = base + i;
-      if (u >= u1) break;
-      const PairSlot cur = ring[i];
-      if (u + P < u1) {
-        load(lk, ring[i]);
-        step_load();
-      }
-      const int rt = ct, kb2 = ck, hh = ch;
-      if (++ck == B) {
-        ck = 0;
-        if (kGated && ch == 0) {
-          ch = 1;
-        } else {
-          ch = 0;
-          ++ct;
-        }
-      }
+  int st_use = 0, st_fill = S - 1;
+  for (int u = u0; u < u1; ++u) {
+    // Request unit u + S - 1 into the stage computed last iteration (the warp
+    // barrier orders every lane's reads of it before the overwrite).
+    __syncwarp();
+    if (u + S - 1 < u1) {
+      issue(st_fill);
+      step_load();
+    }
+    cp_async_commit();
+    cp_async_wait<S - 1>();  // unit u's group has landed (for this lane)
+    __syncwarp();            // ... and every lane's, so the scales are visible
+    const uint8_t* stage = ring + st_use * GEMV_PAIR_STAGE_BYTES;
+    st_use = st_use + 1 == S ? 0 : st_use + 1;
+    st_fill = st_fill + 1 == S ? 0 : st_fill + 1;
 
-      float se_a, so_a, se_b, so_b;
-      if (p.nested) {
-        const float* c2 = (kGated && hh) ? code2_s3 : code2_s;
-        const float off = (kGated && hh) ? p.offset3 : p.offset;
-        se_a = nested_scale(c2[cur.qa & 0xFFu], cur.sa, off);
-        so_a = nested_scale(c2[(cur.qa >> 8) & 0xFFu], cur.sa, off);
-        se_b = nested_scale(c2[cur.qb & 0xFFu], cur.sb, off);
-        so_b = nested_scale(c2[(cur.qb >> 8) & 0xFFu], cur.sb, off);
+    const int rt = ct, kb2 = ck, hh = ch;
+    if (++ck == B) {
+      ck = 0;
+      if (kGated && ch == 0) {
+        ch = 1;
       } else {
-        se_a = cur.sa; so_a = __uint_as_float(cur.qa); se_b = cur.sb; so_b = __uint_as_float(cur.qb);
-      }
-
-      uint4 xv[4];
-      if (xlane) {  // shared memory when staged, else global (generic loads)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) xv[j] = xrow[kb2 * 16 + j];
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) xv[j] = make_uint4(0, 0, 0, 0);
-      }
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint32_t wa[4] = {cur.wa.x, cur.wa.y, cur.wa.z, cur.wa.w};
-      const uint32_t wb[4] = {cur.wb.x, cur.wb.y, cur.wb.z, cur.wb.w};
-#pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        const uint32_t w0 = wa[s >> 1], w1 = wb[s >> 1];
-        const int j0 = 2 * (s & 1);
-        const uint32_t a0 = lut_lookup(lut, w0, lut_sel(j0), lane_base);
-        const uint32_t a2 = lut_lookup(lut, w0, lut_sel(j0 + 1), lane_base);
-        const uint32_t a1 = lut_lookup(lut, w1, lut_sel(j0), lane_base);
-        const uint32_t a3 = lut_lookup(lut, w1, lut_sel(j0 + 1), lane_base);
-        const uint4& xq = xv[s >> 1];
-        const uint32_t b0 = (s & 1) ? xq.z : xq.x;
-        const uint32_t b1 = (s & 1) ? xq.w : xq.y;
-        mma_bf16_16816(d, a0, a1, a2, a3, b0, b1);
-      }
-      // d0 = (row g, col 2t) = even block, d1 = odd block; d2/d3 for row g+8.
-      if (kGated && hh) {
-        acc3_a = fmaf(se_a, d[0], acc3_a);
-        acc3_a = fmaf(so_a, d[1], acc3_a);
-        acc3_b = fmaf(se_b, d[2], acc3_b);
-        acc3_b = fmaf(so_b, d[3], acc3_b);
-      } else {
-        acc_a = fmaf(se_a, d[0], acc_a);
-        acc_a = fmaf(so_a, d[1], acc_a);
-        acc_b = fmaf(se_b, d[2], acc_b);
-        acc_b = fmaf(so_b, d[3], acc_b);
-      }
-
-      if ((kb2 == B - 1 && (!kGated || hh == 1)) || u == u1 - 1) {
-        finish_pair_tile<kGated>(p, rt, u0, u1, gw, g, t, lane, acc_a, acc_b, acc3_a, acc3_b);
-        acc_a = acc_b = acc3_a = acc3_b = 0.f;
+        ch = 0;
+        ++ct;
       }
     }
+
+    const uint4 wav = *reinterpret_cast<const uint4*>(stage + lane * 16);
+    const uint4 wbv = *reinterpret_cast<const uint4*>(stage + 512 + lane * 16);
+    const uint2 sca = *reinterpret_cast<const uint2*>(stage + 1024 + g * 8);
+    const uint2 scb = *reinterpret_cast<const uint2*>(stage + 1024 + (g + 8) * 8);
+
+    float se_a, so_a, se_b, so_b;
+    if (p.nested) {
+      const float* c2 = (kGated && hh) ? code2_s3 : code2_s;
+      const float off = (kGated && hh) ? p.offset3 : p.offset;
+      // the unit's first block sits at byte (block index & 3) of the window
+      const int be0 = ((kb2 * 128) >> p.bs_shift);
+      const uint32_t sha = (uint32_t)(((rt * 16 + g < N ? rt * 16 + g : N - 1) * nblk + be0) & 3) * 8;
+      const uint32_t shb = (uint32_t)(((rt * 16 + g + 8 < N ? rt * 16 + g + 8 : N - 1) * nblk + be0) & 3) * 8;
+      const uint32_t ea = (sca.x >> sha) & 0xFFu, eb = (scb.x >> shb) & 0xFFu;
+      const uint32_t oa = bs64 ? (sca.x >> (sha + 8)) & 0xFFu : ea;
+      const uint32_t ob = bs64 ? (scb.x >> (shb + 8)) & 0xFFu : eb;
+      const float s2a = __uint_as_float(sca.y), s2b = __uint_as_float(scb.y);
+      se_a = nested_scale(c2[ea], s2a, off);
+      so_a = nested_scale(c2[oa], s2a, off);
+      se_b = nested_scale(c2[eb], s2b, off);
+      so_b = nested_scale(c2[ob], s2b, off);
+    } else {
+      se_a = __uint_as_float(sca.x); so_a = __uint_as_float(sca.y);
+      se_b = __uint_as_float(scb.x); so_b = __uint_as_float(scb.y);
+    }
+
+    uint4 xv[4];
+    if (xlane) {  // shared memory when staged, else global (generic loads)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xv[j] = xrow[kb2 * 16 + j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xv[j] = make_uint4(0, 0, 0, 0);
+    }
+    // Two independent MMA chains (even and odd k steps) halve the dependent
+    // accumulate latency per unit.
+    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t wa[4] = {wav.x, wav.y, wav.z, wav.w};
+    const uint32_t wb[4] = {wbv.x, wbv.y, wbv.z, wbv.w};
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      const uint32_t w0 = wa[s >> 1], w1 = wb[s >> 1];
+      const int j0 = 2 * (s & 1);
+      const uint32_t a0 = lut_lookup(lut, w0, lut_sel(j0), lane_base);
+      const uint32_t a2 = lut_lookup(lut, w0, lut_sel(j0 + 1), lane_base);
+      const uint32_t a1 = lut_lookup(lut, w1, lut_sel(j0), lane_base);
+      const uint32_t a3 = lut_lookup(lut, w1, lut_sel(j0 + 1), lane_base);
+      const uint4& xq = xv[s >> 1];
+      const uint32_t b0 = (s & 1) ? xq.z : xq.x;
+      const uint32_t b1 = (s & 1) ? xq.w : xq.y;
+      if (s & 1)
+        mma_bf16_16816(d1, a0, a1, a2, a3, b0, b1);
+      else
+        mma_bf16_16816(d0, a0, a1, a2, a3, b0, b1);
+    }
+    const float e0 = d0[0] + d1[0], e1 = d0[1] + d1[1], e2 = d0[2] + d1[2], e3 = d0[3] + d1[3];
+    // e0 = (row g, col 2t) = even block, e1 = odd block; e2/e3 for row g+8.
+    if (kGated && hh) {
+      acc3_a = fmaf(se_a, e0, acc3_a);
+      acc3_a = fmaf(so_a, e1, acc3_a);
+      acc3_b = fmaf(se_b, e2, acc3_b);
+      acc3_b = fmaf(so_b, e3, acc3_b);
+    } else {
+      acc_a = fmaf(se_a, e0, acc_a);
+      acc_a = fmaf(so_a, e1, acc_a);
+      acc_b = fmaf(se_b, e2, acc_b);
+      acc_b = fmaf(so_b, e3, acc_b);
+    }
+
+    if ((kb2 == B - 1 && (!kGated || hh == 1)) || u == u1 - 1) {
+      finish_pair_tile<kGated>(p, rt, u0, u1, gw, g, t, lane, acc_a, acc_b, acc3_a, acc3_b);
+      acc_a = acc_b = acc3_a = acc3_b = 0.f;
+    }
   }
+  cp_async_wait<0>();
   if (!NF4B_GEMV_PREFETCH_EARLY) prefetch_next(p, gw, lane);
 }
 
@@ -605,7 +661,8 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_block_kernel(const GemvP
 
 template <typename Kernel>
 cudaError_t launch_kernel(Kernel kernel, const GemvParams& p, int grid, cudaStream_t stream,
-                          bool* configured, int smem = GEMV_SMEM_BYTES, int smem_max = GEMV_SMEM_BYTES) {
+                          bool* configured, int smem = GEMV_SMEM_BYTES, int smem_max = GEMV_SMEM_BYTES,
+                          int threads = kThreads) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
@@ -615,7 +672,7 @@ cudaError_t launch_kernel(Kernel kernel, const GemvParams& p, int grid, cudaStre
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -646,14 +703,15 @@ void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan, bo
   const long long B = pairs ? K / 128 : K / 64;
   const long long H = (pairs && gated) ? 2 : 1;  // halves per tile
   const long long U = tiles * B * H;
-  const long long ctas = (long long)sm_count * GEMV_CTAS_PER_SM;
-  long long W = ctas * kWarps;
+  const int wpc = pairs ? GEMV_PAIR_WARPS : kWarps;              // warps per CTA
+  const long long ctas = (long long)sm_count * (pairs ? 1 : GEMV_CTAS_PER_SM);
+  long long W = ctas * wpc;
   if (W > U) W = U;
   plan->tiles = tiles;
   plan->units = U;
   plan->blocks_per_tile = (int)B;
   plan->warps_total = (int)W;
-  plan->grid = (int)((W + kWarps - 1) / kWarps);
+  plan->grid = (int)((W + wpc - 1) / wpc);
   // Every warp owns at least floor(U / W) units, so a tile of B * H units
   // meets at most ceil(B * H / floor(U / W)) + 1 of them.
   const long long per = U / W;
@@ -667,10 +725,10 @@ cudaError_t launch_gemv(const GemvParams& p, int grid, bool pairs, cudaStream_t 
   if (pairs) {
     const int smem = GEMV_PAIR_X_OFFSET + (p.x_staged ? p.M * p.K * 2 : 0);
     if (p.gated)
-      return launch_kernel(nf4_gemv_pair_kernel<NF4B_GEMV_PAIR_DEPTH, true>, p, grid, stream, cfg_gated,
-                           smem, GEMV_PAIR_SMEM_MAX);
-    return launch_kernel(nf4_gemv_pair_kernel<NF4B_GEMV_PAIR_DEPTH, false>, p, grid, stream, cfg_pair,
-                         smem, GEMV_PAIR_SMEM_MAX);
+      return launch_kernel(nf4_gemv_pair_kernel<true>, p, grid, stream, cfg_gated, smem, GEMV_PAIR_SMEM_MAX,
+                           GEMV_PAIR_WARPS * 32);
+    return launch_kernel(nf4_gemv_pair_kernel<false>, p, grid, stream, cfg_pair, smem, GEMV_PAIR_SMEM_MAX,
+                         GEMV_PAIR_WARPS * 32);
   }
   if (p.M <= 8) return launch_kernel(nf4_gemv_block_kernel<1, 4>, p, grid, stream, cfg1);
   if (p.M <= 16) return launch_kernel(nf4_gemv_block_kernel<2, 2>, p, grid, stream, cfg2);
