@@ -15,6 +15,7 @@
 
 namespace nf4b {
 int read_device_error(int clear);
+int read_gemv_error(int clear);
 }
 
 using namespace nf4b;
@@ -140,7 +141,7 @@ size_t gemv_workspace_bytes(const nf4b_weight* w, int rows, int sms) {
   if (rows <= 4 && w->k_in % 128 == 0) {  // the pair kernel may serve this call, plain or gated
     for (int gated = 0; gated < 2; ++gated) {
       GemvPlan b;
-      gemv_plan(w->n_out, w->k_in, rows, sms, true, &b, gated != 0);
+      gemv_plan(w->n_out, w->k_in, rows, sms, true, &b, gated != 0, gemv_pair_su(w->k_in, w->blocksize));
       if (b.partial_bytes > bytes) bytes = b.partial_bytes;
     }
   }
@@ -167,8 +168,9 @@ int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* 
     return fail(NF4B_ERR_SHAPE, "the gated GEMV serves 1..4 rows with k_in %% 128 == 0 (got %d rows, k_in %d)",
                 rows, w->k_in);
   const int sms = current_sm_count();
+  const int su = pairs ? gemv_pair_su(w->k_in, w->blocksize) : 1;
   GemvPlan plan;
-  gemv_plan(w->n_out, w->k_in, rows, sms, pairs, &plan, gated);
+  gemv_plan(w->n_out, w->k_in, rows, sms, pairs, &plan, gated, su);
   const size_t need = gemv_workspace_bytes(w, rows, sms);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(NF4B_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need,
@@ -186,6 +188,7 @@ int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* 
   p.code2_3 = gated && w3->nested ? w3->code2 : nullptr;
   p.offset3 = gated ? w3->offset : 0.f;
   p.gated = gated ? 1 : 0;
+  p.su = su;
   p.x_staged = (pairs && (long long)rows * w->k_in * 2 <= GEMV_PAIR_X_MAX) ? 1 : 0;
   p.N = w->n_out;
   p.K = w->k_in;
@@ -216,7 +219,11 @@ int nf4b_version(void) { return 100; }
 
 const char* nf4b_last_error(void) { return g_err; }
 
-int nf4b_device_error(int clear) { return read_device_error(clear); }
+int nf4b_device_error(int clear) {
+  const int gemm = read_device_error(clear), gemv = read_gemv_error(clear);
+  if (gemm < 0 || gemv < 0) return -1;
+  return (gemm ? 1 : 0) | (gemv ? 2 : 0);
+}
 
 size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows) {
   if (w == nullptr || rows <= 0 || w->n_out <= 0 || w->k_in <= 0) return 0;

@@ -1,6 +1,7 @@
 // Host-side declarations shared by the kernel files and the C ABI (capi.cu).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -21,24 +22,25 @@ constexpr int GEMV_LUT_BYTES = 256 * 256;      // pair table, 256 B stride, one 
 constexpr int GEMV_SMEM_BYTES = GEMV_LUT_BYTES + 256 * 4;  // + code2 copy
 // Pair kernel: one CTA of GEMV_PAIR_WARPS warps per SM. Shared memory: the pair
 // table, code2 of W and of a gated pair's W3, each warp's ring of
-// GEMV_PAIR_STAGES unit stages (filled by cp.async), then x staged whole when
-// it fits (rows * k_in * 2 <= GEMV_PAIR_X_MAX).
+// unit stages (a 16-row weight box written by TMA, 8 bytes of scale data per
+// row and 128-code sub-unit written by cp.async, one mbarrier), then x staged
+// whole when it fits (rows * k_in * 2 <= GEMV_PAIR_X_MAX).
 #ifndef NF4B_GEMV_PAIR_WARPS
 #define NF4B_GEMV_PAIR_WARPS 16
 #endif
-#ifndef NF4B_GEMV_PAIR_STAGES
-#define NF4B_GEMV_PAIR_STAGES 5
+#ifndef NF4B_GEMV_PAIR_STAGE_KB
+#define NF4B_GEMV_PAIR_STAGE_KB 6  // KB of weight ring per warp (stages = this / unit KB)
 #endif
 constexpr int GEMV_PAIR_WARPS = NF4B_GEMV_PAIR_WARPS;
-constexpr int GEMV_PAIR_STAGES = NF4B_GEMV_PAIR_STAGES;
-// One stage: rows g (512 B) and g + 8 (512 B) of a 16 x 128-code unit, then
-// 8 bytes of scale data for each of the 16 rows.
-constexpr int GEMV_PAIR_STAGE_BYTES = 1024 + 16 * 8;
-constexpr int GEMV_PAIR_STAGE_OFFSET = GEMV_LUT_BYTES + 2 * 256 * 4;
-constexpr int GEMV_PAIR_X_OFFSET =
-    GEMV_PAIR_STAGE_OFFSET + GEMV_PAIR_WARPS * GEMV_PAIR_STAGES * GEMV_PAIR_STAGE_BYTES;
+constexpr int GEMV_PAIR_STAGE_KB = NF4B_GEMV_PAIR_STAGE_KB;
+constexpr int GEMV_PAIR_SLOTS = GEMV_PAIR_WARPS * GEMV_PAIR_STAGE_KB;  // 1 KB weight slots
+constexpr int GEMV_PAIR_W_OFFSET = GEMV_LUT_BYTES + 2 * 256 * 4;           // 1024-aligned boxes
+constexpr int GEMV_PAIR_SC_OFFSET = GEMV_PAIR_W_OFFSET + GEMV_PAIR_SLOTS * 1024;
+constexpr int GEMV_PAIR_BAR_OFFSET = GEMV_PAIR_SC_OFFSET + GEMV_PAIR_SLOTS * 128;
+constexpr int GEMV_PAIR_X_OFFSET = GEMV_PAIR_BAR_OFFSET + GEMV_PAIR_SLOTS * 8;
 constexpr int GEMV_PAIR_X_MAX = 40 * 1024;
 constexpr int GEMV_PAIR_SMEM_MAX = GEMV_PAIR_X_OFFSET + GEMV_PAIR_X_MAX;
+static_assert(GEMV_PAIR_W_OFFSET % 1024 == 0, "TMA boxes must be aligned");
 static_assert(GEMV_PAIR_SMEM_MAX <= 227 * 1024, "pair kernel shared memory exceeds one CTA's limit");
 constexpr int GEMV_MAX_ROWS = 32;              // activation rows one launch takes
 // The workspace starts with a fixed-size region of per-tile arrival counters,
@@ -73,7 +75,7 @@ __device__ __forceinline__ void prefetch_share(const PrefetchHint& h, long long 
   }
 }
 
-struct GemvParams {
+struct alignas(64) GemvParams {
   const uint8_t* packed;
   const uint8_t* a8;
   const float* absmax;
@@ -87,7 +89,12 @@ struct GemvParams {
   const float* code2_3;
   float offset3;
   int gated;
+  int su;        // pair kernel: 128-code sub-units per unit (1 or 2)
   int x_staged;  // pair kernel: x is copied whole into shared memory first
+  // Pair kernel: TMA maps of the packed weights (W, and W3 of a gated pair) as
+  // [n_out rows, k_in / 2 bytes], boxes of 64 bytes x 16 rows.
+  CUtensorMap wmap;
+  CUtensorMap wmap3;
   int N, K;
   int nested;
   int bs_shift;
@@ -124,8 +131,10 @@ struct GemvPlan {
 int gemv_sm_count(int dev);
 // `pairs`: use the pair kernel (units of 128 codes; up to 4 activation rows,
 // k_in % 128 == 0, scale arrays aligned for its paired loads).
-// `gated`: the pair kernel's gated mode (tiles of 2 * k_in / 128 units).
-void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan, bool gated = false);
+// `gated`: the pair kernel's gated mode (tiles of W units then W3 units).
+// `su`: 128-code sub-units per pair-kernel unit (gemv_pair_su).
+void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan, bool gated = false, int su = 1);
+int gemv_pair_su(int K, int blocksize);
 cudaError_t launch_gemv(const GemvParams& p, int grid, bool pairs, cudaStream_t stream);
 
 // ---- dequantisation (nf4_dequant.cu) ---------------------------------------

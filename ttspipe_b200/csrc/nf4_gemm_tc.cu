@@ -31,6 +31,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tmap.cuh"
 
 namespace nf4b {
 
@@ -303,33 +304,6 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
                  "r"((uint32_t)BT)
                  : "memory");
   }
-}
-
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
-  return fn;
-}
-
-bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
-                 uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
-                 CUtensorMapSwizzle swizzle) {
-  auto fn = encode_fn();
-  if (fn == nullptr) return false;
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  return fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int BT>

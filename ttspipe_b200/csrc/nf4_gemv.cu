@@ -37,6 +37,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tmap.cuh"
 
 #ifndef NF4B_GEMV_PREFETCH_EARLY
 #define NF4B_GEMV_PREFETCH_EARLY 1  // stream the hinted weight into L2 at kernel start (0: at the end)
@@ -240,9 +241,6 @@ __device__ __forceinline__ void finish_pair_tile(const GemvParams& p, int rt, in
 
 // cp.async helpers (sm_80+ asynchronous global -> shared copies, tracked per
 // thread in commit groups).
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
 __device__ __forceinline__ void cp_async_8(uint32_t dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
 }
@@ -260,22 +258,83 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
 
-// Pair kernel. Units are numbered tile-major; within a tile, the k units of W
-// and then (gated pair) those of W3, so one warp run covers both halves of a
-// tile where it can and the finisher sees both.
+// TMA and mbarrier helpers for the pair kernel.
+__device__ int g_gemv_error = 0;  // bit 0: a bounded wait gave up (read by nf4b_device_error)
+
+__device__ __forceinline__ unsigned long long gemv_globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init1(uint32_t bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// Box (x bytes, y rows) of a 2-D uint8 map into shared memory; completion
+// counted on `bar`. x is a multiple of 64 (16-byte aligned as TMA requires).
+__device__ __forceinline__ void tma_box(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+// Bounded wait for phase `parity` of `bar` (2 s by %globaltimer); false after
+// recording the timeout in g_gemv_error.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  unsigned long long start = 0;
+  for (uint32_t i = 0;; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((i & 63u) == 0u) {
+      const unsigned long long now = gemv_globaltimer();
+      if (i == 0) {
+        start = now;
+      } else if (now - start > 2000000000ull) {
+        atomicOr(&g_gemv_error, 1);
+        return false;
+      }
+    }
+  }
+}
+
+// Pair kernel. A unit is 16 weight rows x SU * 128 codes (SU = 2 for
+// blocksize-64 weights with k_in % 256 == 0, else 1). Units are numbered
+// tile-major; within a tile, the k units of W and then (gated pair) those of
+// W3, so one warp run covers both halves of a tile where it can and the
+// finisher sees both.
 //
-// Each warp streams its run through a private ring of GEMV_PAIR_STAGES stages
-// in shared memory: unit u + S - 1 is requested (cp.async, one commit group
-// per unit) before unit u is computed, and `cp.async.wait_group S-1` releases
-// exactly unit u's group, so S - 1 units are always in flight regardless of
-// how the compiler schedules the arithmetic. Lane (g, t) copies the 16 bytes
-// of rows g and g + 8 it will multiply; lanes t = 0 and t = 1 also copy the
-// scale data of rows g and g + 8 for the whole warp.
-template <bool kGated>
-__global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1) nf4_gemv_pair_kernel(const GemvParams p) {
-  constexpr int S = GEMV_PAIR_STAGES;
+// Each warp streams its run through a private ring of R = 6 / SU stages,
+// R - 1 units ahead. Lane 0 requests a unit's 16 rows x SU * 64 bytes as one
+// TMA box (completion on the stage's mbarrier); lanes t = 0 and t = 1 copy the
+// scale data of rows g and g + 8 with cp.async (one commit group per unit,
+// released by `cp.async.wait_group R-1`). A box lands row-major, so lane (g, t)
+// reads the 16 bytes of rows g and g + 8 it multiplies for each 128-code
+// sub-unit, and every 8-lane phase of those 128-bit loads covers 128
+// contiguous bytes (no bank conflicts) when SU = 1, 2-way when SU = 2.
+//
+// Scale data per row and unit (8 * SU bytes): nested - the 4-byte aligned
+// window(s) holding the unit's 8-bit codes, then one second-level scale per
+// 128-code sub-unit (its two 64-blocks share it); plain - the fp32 scales of
+// the unit's blocks.
+template <bool kGated, int SU>
+__global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
+    nf4_gemv_pair_kernel(const __grid_constant__ GemvParams p) {
+  constexpr int R = GEMV_PAIR_STAGE_KB / SU;
+  constexpr int WB = 1024 * SU;  // weight bytes per stage
+  constexpr int SB = 128 * SU;   // scale bytes per stage
+  static_assert(R >= 2, "ring too short");
   constexpr int kT = GEMV_PAIR_WARPS * 32;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(1024) uint8_t smem[];
   const uint8_t* lut = smem;
   const float* code2_s = reinterpret_cast<const float*>(smem + GEMV_LUT_BYTES);
   const float* code2_s3 = code2_s + 256;
@@ -288,17 +347,25 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1) nf4_gemv_pair_kernel(
   const int u0 = active ? gw * p.uq + min(gw, p.ur) : 0;
   const int u1 = active ? u0 + p.uq + (gw < p.ur ? 1 : 0) : 0;
   const int g = lane >> 2, t = lane & 3;
-  const int B = p.blocks_per_tile;  // 128-code units per row tile and half
+  const int B = p.blocks_per_tile;  // units per row tile and half
   const int per_tile = kGated ? 2 * B : B;
   const int N = p.N, K = p.K, M = p.M;
-  const int row_bytes = K >> 1;
   const uint32_t lane_base = (uint32_t)lane * 4u;
-  const bool bs64 = p.bs_shift == 6;
-  const int nblk = K >> p.bs_shift;  // scale blocks per weight row
+  const int bs_shift = p.bs_shift;
+  const bool bs64 = bs_shift == 6;
+  const int nblk = K >> bs_shift;  // scale blocks per weight row
   const long long a8_total = (long long)N * nblk;
 
-  uint8_t* ring = smem + GEMV_PAIR_STAGE_OFFSET + wib * (S * GEMV_PAIR_STAGE_BYTES);
-  const uint32_t ring_s = smem_addr(ring);
+  const uint8_t* wring = smem + GEMV_PAIR_W_OFFSET + wib * (R * WB);
+  const uint8_t* sring = smem + GEMV_PAIR_SC_OFFSET + wib * (R * SB);
+  const uint32_t wring_s = smem_addr(wring), sring_s = smem_addr(sring);
+  const uint32_t bar_s = smem_addr(smem + GEMV_PAIR_BAR_OFFSET + wib * (R * 8));
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < R; ++i) mbar_init1(bar_s + 8 * i);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
 
   // Load cursor: tile lt, half lh, k unit lk (incremental, no divisions).
   int lt = u0 / per_tile, lk = u0 - lt * per_tile, lh = 0;
@@ -308,22 +375,15 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1) nf4_gemv_pair_kernel(
   }
   int ct = lt, ch = lh, ck = lk;
 
-  // Row pointers and scale arrays of the tile/half being loaded. Lanes t = 0
-  // and t = 1 copy the scales of row g and g + 8 respectively (row `sr`).
-  const uint8_t* pa = nullptr;
-  const uint8_t* pb = nullptr;
+  // Scale arrays of the tile/half being loaded; lanes t = 0 and t = 1 copy the
+  // scales of row g and g + 8 respectively (`sbase` = that row's first block).
   const uint8_t* a8 = p.a8;
   const float* absmax = p.absmax;
-  int sr = 0;
+  long long sbase = 0;
   auto set_rows = [&](int rt, int h) {
-    const int ra = min(rt * 16 + g, N - 1);
-    const int rb = min(rt * 16 + g + 8, N - 1);
-    sr = t == 0 ? ra : rb;
-    const uint8_t* base = (kGated && h) ? p.packed3 : p.packed;
+    sbase = (long long)min(rt * 16 + g + 8 * t, N - 1) * nblk;
     a8 = (kGated && h) ? p.a8_3 : p.a8;
     absmax = (kGated && h) ? p.absmax3 : p.absmax;
-    pa = base + (size_t)ra * row_bytes + t * 16;
-    pb = base + (size_t)rb * row_bytes + t * 16;
   };
   set_rows(lt, lh);
   auto step_load = [&]() {
@@ -338,21 +398,36 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1) nf4_gemv_pair_kernel(
       set_rows(lt, lh);
     }
   };
-  // Request unit (cursor) into stage `st`: weights, and (lanes t < 2) scales.
+  // Request the load cursor's unit into stage `st`.
   auto issue = [&](int st) {
-    const uint32_t d = ring_s + st * GEMV_PAIR_STAGE_BYTES;
-    cp_async_16(d + lane * 16, pa + lk * 64);
-    cp_async_16(d + 512 + lane * 16, pb + lk * 64);
+    if (lane == 0) {
+      const uint32_t bar = bar_s + 8 * st;
+      mbar_expect(bar, (uint32_t)WB);
+      // rows past n_out read as zeros (TMA bounds); their outputs are never stored
+      tma_box(wring_s + st * WB, (kGated && lh) ? &p.wmap3 : &p.wmap, lk * 64 * SU, lt * 16, bar);
+    }
     if (t < 2) {
-      const uint32_t ds = d + 1024 + (g + 8 * t) * 8;
-      const long long be = (long long)sr * nblk + ((lk * 128) >> p.bs_shift);
+      const uint32_t ds = sring_s + st * SB + (g + 8 * t) * (8 * SU);
+      const long long be = sbase + ((lk * 128 * SU) >> bs_shift);
       if (p.nested) {
-        // the 4-byte aligned window holding this unit's one or two 8-bit codes
+        // the 4-byte aligned window(s) holding this unit's 8-bit codes
         const long long w0 = be & ~3LL;
         const long long left = a8_total - w0;
         cp_async_4(ds, a8 + w0, (uint32_t)(left < 4 ? left : 4));
-        // an even block and the next share their second-level block
-        cp_async_4(ds + 4, absmax + (be >> p.bs2_shift), 4u);
+        if (SU == 2) {
+          // a second word only when the codes run past the first (left > 4 then)
+          const long long w1 = left > 4 ? w0 + 4 : w0;
+          const long long l1 = left > 4 ? a8_total - w1 : 0;
+          cp_async_4(ds + 4, a8 + w1, (uint32_t)(l1 < 4 ? l1 : 4));
+          // each 128-code sub-unit's two 64-blocks share a second-level block
+          cp_async_4(ds + 8, absmax + (be >> p.bs2_shift), 4u);
+          cp_async_4(ds + 12, absmax + ((be + 2) >> p.bs2_shift), 4u);
+        } else {
+          cp_async_4(ds + 4, absmax + (be >> p.bs2_shift), 4u);
+        }
+      } else if (SU == 2) {
+        cp_async_8(ds, absmax + be);
+        cp_async_8(ds + 8, absmax + be + 2);
       } else if (bs64) {
         cp_async_8(ds, absmax + be);
       } else {
@@ -361,10 +436,18 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1) nf4_gemv_pair_kernel(
       }
     }
   };
+  // Compute cursor and the byte phase (row * nblk) & 3 of rows g and g+8
+  // within their 4-byte scale-code windows.
+  int ph_a = 0, ph_b = 0;
+  auto set_phase = [&](int rt) {
+    ph_a = (int)(((long long)min(rt * 16 + g, N - 1) * nblk) & 3);
+    ph_b = (int)(((long long)min(rt * 16 + g + 8, N - 1) * nblk) & 3);
+  };
+  set_phase(ct);
 
-  // Prologue: S - 1 units requested (one group each, empty past the run).
+  // Prologue: R - 1 units requested (one cp.async group each, empty past the run).
 #pragma unroll
-  for (int i = 0; i < S - 1; ++i) {
+  for (int i = 0; i < R - 1; ++i) {
     if (u0 + i < u1) {
       issue(i);
       step_load();
@@ -386,10 +469,6 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1) nf4_gemv_pair_kernel(
     for (int i = threadIdx.x; i < n16; i += kT) dst[i] = __ldcg(src + i);
     __syncthreads();
   }
-  if (!active) {
-    cp_async_wait<0>();
-    return;
-  }
 
   // x: column c of the MMA is (activation row c >> 1, block parity c & 1);
   // lane (g, t) supplies column g for codes of block parity t >> 1.
@@ -401,23 +480,28 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1) nf4_gemv_pair_kernel(
 
   float acc_a = 0.f, acc_b = 0.f;    // W (or W1): rows g, g+8 for activation row t
   float acc3_a = 0.f, acc3_b = 0.f;  // gated pair: W3
-  int st_use = 0, st_fill = S - 1;
+  int st_use = 0, st_fill = R - 1;
+  uint32_t phase = 0;  // bit s: parity of stage s's next completion
   for (int u = u0; u < u1; ++u) {
-    // Request unit u + S - 1 into the stage computed last iteration (the warp
+    // Request unit u + R - 1 into the stage computed last iteration (the warp
     // barrier orders every lane's reads of it before the overwrite).
     __syncwarp();
-    if (u + S - 1 < u1) {
+    if (u + R - 1 < u1) {
       issue(st_fill);
       step_load();
     }
     cp_async_commit();
-    cp_async_wait<S - 1>();  // unit u's group has landed (for this lane)
-    __syncwarp();            // ... and every lane's, so the scales are visible
-    const uint8_t* stage = ring + st_use * GEMV_PAIR_STAGE_BYTES;
-    st_use = st_use + 1 == S ? 0 : st_use + 1;
-    st_fill = st_fill + 1 == S ? 0 : st_fill + 1;
+    st_fill = st_fill + 1 == R ? 0 : st_fill + 1;
+    cp_async_wait<R - 1>();  // unit u's scales (this lane's copies)
+    if (!mbar_wait_bounded(bar_s + 8 * st_use, (phase >> st_use) & 1u)) break;
+    phase ^= 1u << st_use;
+    __syncwarp();            // every lane's scale copies are visible
+    const uint8_t* wst = wring + st_use * WB;
+    const uint8_t* sst = sring + st_use * SB;
+    st_use = st_use + 1 == R ? 0 : st_use + 1;
 
-    const int rt = ct, kb2 = ck, hh = ch;
+    const int rt = ct, kb = ck, hh = ch;
+    const int pha = ph_a, phb = ph_b;
     if (++ck == B) {
       ck = 0;
       if (kGated && ch == 0) {
@@ -425,79 +509,105 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1) nf4_gemv_pair_kernel(
       } else {
         ch = 0;
         ++ct;
+        set_phase(ct);
       }
     }
 
-    const uint4 wav = *reinterpret_cast<const uint4*>(stage + lane * 16);
-    const uint4 wbv = *reinterpret_cast<const uint4*>(stage + 512 + lane * 16);
-    const uint2 sca = *reinterpret_cast<const uint2*>(stage + 1024 + g * 8);
-    const uint2 scb = *reinterpret_cast<const uint2*>(stage + 1024 + (g + 8) * 8);
-
-    float se_a, so_a, se_b, so_b;
-    if (p.nested) {
-      const float* c2 = (kGated && hh) ? code2_s3 : code2_s;
-      const float off = (kGated && hh) ? p.offset3 : p.offset;
-      // the unit's first block sits at byte (block index & 3) of the window
-      const int be0 = ((kb2 * 128) >> p.bs_shift);
-      const uint32_t sha = (uint32_t)(((rt * 16 + g < N ? rt * 16 + g : N - 1) * nblk + be0) & 3) * 8;
-      const uint32_t shb = (uint32_t)(((rt * 16 + g + 8 < N ? rt * 16 + g + 8 : N - 1) * nblk + be0) & 3) * 8;
-      const uint32_t ea = (sca.x >> sha) & 0xFFu, eb = (scb.x >> shb) & 0xFFu;
-      const uint32_t oa = bs64 ? (sca.x >> (sha + 8)) & 0xFFu : ea;
-      const uint32_t ob = bs64 ? (scb.x >> (shb + 8)) & 0xFFu : eb;
-      const float s2a = __uint_as_float(sca.y), s2b = __uint_as_float(scb.y);
-      se_a = nested_scale(c2[ea], s2a, off);
-      so_a = nested_scale(c2[oa], s2a, off);
-      se_b = nested_scale(c2[eb], s2b, off);
-      so_b = nested_scale(c2[ob], s2b, off);
+    // Scale data of rows g and g + 8 for this unit.
+    uint32_t sa[2 * SU], sb[2 * SU];
+    if (SU == 2) {
+      const uint4 va = *reinterpret_cast<const uint4*>(sst + g * 16);
+      const uint4 vb = *reinterpret_cast<const uint4*>(sst + (g + 8) * 16);
+      sa[0] = va.x; sa[1] = va.y; sa[2 % (2 * SU)] = va.z; sa[3 % (2 * SU)] = va.w;
+      sb[0] = vb.x; sb[1] = vb.y; sb[2 % (2 * SU)] = vb.z; sb[3 % (2 * SU)] = vb.w;
     } else {
-      se_a = __uint_as_float(sca.x); so_a = __uint_as_float(sca.y);
-      se_b = __uint_as_float(scb.x); so_b = __uint_as_float(scb.y);
+      const uint2 va = *reinterpret_cast<const uint2*>(sst + g * 8);
+      const uint2 vb = *reinterpret_cast<const uint2*>(sst + (g + 8) * 8);
+      sa[0] = va.x; sa[1] = va.y;
+      sb[0] = vb.x; sb[1] = vb.y;
     }
-
-    uint4 xv[4];
-    if (xlane) {  // shared memory when staged, else global (generic loads)
+    float ya = 0.f, yb = 0.f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) xv[j] = xrow[kb2 * 16 + j];
-    } else {
+    for (int i = 0; i < SU; ++i) {
+      const int kb2 = kb * SU + i;  // 128-code sub-unit index within the row
+      float se_a, so_a, se_b, so_b;
+      if (p.nested) {
+        const float* c2 = (kGated && hh) ? code2_s3 : code2_s;
+        const float off = (kGated && hh) ? p.offset3 : p.offset;
+        uint32_t ea, oa, eb, ob;
+        float s2a, s2b;
+        if (SU == 2) {
+          // blocks 2i, 2i+1 of the unit sit at bytes (row phase + 2i) and +1 of the 8-byte window
+          const unsigned long long wa8 = ((unsigned long long)sa[1] << 32) | sa[0];
+          const unsigned long long wb8 = ((unsigned long long)sb[1] << 32) | sb[0];
+          const uint32_t sha = (uint32_t)(pha + 2 * i) * 8, shb = (uint32_t)(phb + 2 * i) * 8;
+          ea = (uint32_t)(wa8 >> sha) & 0xFFu;
+          oa = (uint32_t)(wa8 >> (sha + 8)) & 0xFFu;
+          eb = (uint32_t)(wb8 >> shb) & 0xFFu;
+          ob = (uint32_t)(wb8 >> (shb + 8)) & 0xFFu;
+          s2a = __uint_as_float(sa[(2 + i) % (2 * SU)]);
+          s2b = __uint_as_float(sb[(2 + i) % (2 * SU)]);
+        } else {
+          // the unit's first block sits at byte (row phase + block index) & 3 of the window
+          const int be0 = (kb2 * 128) >> bs_shift;
+          const uint32_t sha = (uint32_t)((pha + be0) & 3) * 8, shb = (uint32_t)((phb + be0) & 3) * 8;
+          ea = (sa[0] >> sha) & 0xFFu;
+          eb = (sb[0] >> shb) & 0xFFu;
+          oa = bs64 ? (sa[0] >> (sha + 8)) & 0xFFu : ea;
+          ob = bs64 ? (sb[0] >> (shb + 8)) & 0xFFu : eb;
+          s2a = __uint_as_float(sa[1]);
+          s2b = __uint_as_float(sb[1]);
+        }
+        se_a = nested_scale(c2[ea], s2a, off);
+        so_a = nested_scale(c2[oa], s2a, off);
+        se_b = nested_scale(c2[eb], s2b, off);
+        so_b = nested_scale(c2[ob], s2b, off);
+      } else {
+        se_a = __uint_as_float(sa[(2 * i) % (2 * SU)]); so_a = __uint_as_float(sa[(2 * i + 1) % (2 * SU)]);
+        se_b = __uint_as_float(sb[(2 * i) % (2 * SU)]); so_b = __uint_as_float(sb[(2 * i + 1) % (2 * SU)]);
+      }
+      uint4 xv[4];
+      if (xlane) {  // shared memory when staged, else global (generic loads)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) xv[j] = make_uint4(0, 0, 0, 0);
+        for (int j = 0; j < 4; ++j) xv[j] = xrow[kb2 * 16 + j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xv[j] = make_uint4(0, 0, 0, 0);
+      }
+      const uint4 wav = *reinterpret_cast<const uint4*>(wst + g * (64 * SU) + i * 64 + t * 16);
+      const uint4 wbv = *reinterpret_cast<const uint4*>(wst + (g + 8) * (64 * SU) + i * 64 + t * 16);
+      // Two independent MMA chains (even and odd k steps).
+      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t wa[4] = {wav.x, wav.y, wav.z, wav.w};
+      const uint32_t wb[4] = {wbv.x, wbv.y, wbv.z, wbv.w};
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        const uint32_t w0 = wa[s >> 1], w1 = wb[s >> 1];
+        const int j0 = 2 * (s & 1);
+        const uint32_t a0 = lut_lookup(lut, w0, lut_sel(j0), lane_base);
+        const uint32_t a2 = lut_lookup(lut, w0, lut_sel(j0 + 1), lane_base);
+        const uint32_t a1 = lut_lookup(lut, w1, lut_sel(j0), lane_base);
+        const uint32_t a3 = lut_lookup(lut, w1, lut_sel(j0 + 1), lane_base);
+        const uint4& xq = xv[s >> 1];
+        const uint32_t b0 = (s & 1) ? xq.z : xq.x;
+        const uint32_t b1 = (s & 1) ? xq.w : xq.y;
+        if (s & 1)
+          mma_bf16_16816(d1, a0, a1, a2, a3, b0, b1);
+        else
+          mma_bf16_16816(d0, a0, a1, a2, a3, b0, b1);
+      }
+      // d[0] = (row g, col 2t) = even block, d[1] = odd block; d[2]/d[3] for row g+8.
+      ya += fmaf(so_a, d0[1] + d1[1], (d0[0] + d1[0]) * se_a);
+      yb += fmaf(so_b, d0[3] + d1[3], (d0[2] + d1[2]) * se_b);
     }
-    // Two independent MMA chains (even and odd k steps) halve the dependent
-    // accumulate latency per unit.
-    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint32_t wa[4] = {wav.x, wav.y, wav.z, wav.w};
-    const uint32_t wb[4] = {wbv.x, wbv.y, wbv.z, wbv.w};
-#pragma unroll
-    for (int s = 0; s < 8; ++s) {
-      const uint32_t w0 = wa[s >> 1], w1 = wb[s >> 1];
-      const int j0 = 2 * (s & 1);
-      const uint32_t a0 = lut_lookup(lut, w0, lut_sel(j0), lane_base);
-      const uint32_t a2 = lut_lookup(lut, w0, lut_sel(j0 + 1), lane_base);
-      const uint32_t a1 = lut_lookup(lut, w1, lut_sel(j0), lane_base);
-      const uint32_t a3 = lut_lookup(lut, w1, lut_sel(j0 + 1), lane_base);
-      const uint4& xq = xv[s >> 1];
-      const uint32_t b0 = (s & 1) ? xq.z : xq.x;
-      const uint32_t b1 = (s & 1) ? xq.w : xq.y;
-      if (s & 1)
-        mma_bf16_16816(d1, a0, a1, a2, a3, b0, b1);
-      else
-        mma_bf16_16816(d0, a0, a1, a2, a3, b0, b1);
-    }
-    const float e0 = d0[0] + d1[0], e1 = d0[1] + d1[1], e2 = d0[2] + d1[2], e3 = d0[3] + d1[3];
-    // e0 = (row g, col 2t) = even block, e1 = odd block; e2/e3 for row g+8.
     if (kGated && hh) {
-      acc3_a = fmaf(se_a, e0, acc3_a);
-      acc3_a = fmaf(so_a, e1, acc3_a);
-      acc3_b = fmaf(se_b, e2, acc3_b);
-      acc3_b = fmaf(so_b, e3, acc3_b);
+      acc3_a += ya;
+      acc3_b += yb;
     } else {
-      acc_a = fmaf(se_a, e0, acc_a);
-      acc_a = fmaf(so_a, e1, acc_a);
-      acc_b = fmaf(se_b, e2, acc_b);
-      acc_b = fmaf(so_b, e3, acc_b);
+      acc_a += ya;
+      acc_b += yb;
     }
-
-    if ((kb2 == B - 1 && (!kGated || hh == 1)) || u == u1 - 1) {
+    if ((kb == B - 1 && (!kGated || hh == 1)) || u == u1 - 1) {
       finish_pair_tile<kGated>(p, rt, u0, u1, gw, g, t, lane, acc_a, acc_b, acc3_a, acc3_b);
       acc_a = acc_b = acc3_a = acc3_b = 0.f;
     }
@@ -518,7 +628,7 @@ struct BlockSlot {
 
 template <int NT, int P>
 __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_block_kernel(const GemvParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(1024) uint8_t smem[];
   const uint8_t* lut = smem;
   const float* code2_s = reinterpret_cast<const float*>(smem + GEMV_LUT_BYTES);
 
@@ -687,6 +797,16 @@ cudaError_t launch_kernel(Kernel kernel, const GemvParams& p, int grid, cudaStre
 
 static int g_sm_count[64];
 
+int read_gemv_error(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemv_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_gemv_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
 int gemv_sm_count(int dev) {
   if (dev < 0 || dev >= 64) return 148;
   if (g_sm_count[dev] == 0) {
@@ -698,9 +818,11 @@ int gemv_sm_count(int dev) {
   return g_sm_count[dev];
 }
 
-void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan, bool gated) {
+int gemv_pair_su(int K, int blocksize) { return (blocksize == 64 && K % 256 == 0) ? 2 : 1; }
+
+void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan, bool gated, int su) {
   const long long tiles = (N + 15) / 16;
-  const long long B = pairs ? K / 128 : K / 64;
+  const long long B = pairs ? K / (128 * su) : K / 64;
   const long long H = (pairs && gated) ? 2 : 1;  // halves per tile
   const long long U = tiles * B * H;
   const int wpc = pairs ? GEMV_PAIR_WARPS : kWarps;              // warps per CTA
@@ -721,14 +843,28 @@ void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan, bo
 }
 
 cudaError_t launch_gemv(const GemvParams& p, int grid, bool pairs, cudaStream_t stream) {
-  static bool cfg_pair[64] = {}, cfg_gated[64] = {}, cfg1[64] = {}, cfg2[64] = {}, cfg4[64] = {};
+  static bool cfg_pair[64] = {}, cfg_gated[64] = {}, cfg_pair2[64] = {}, cfg_gated2[64] = {};
+  static bool cfg1[64] = {}, cfg2[64] = {}, cfg4[64] = {};
   if (pairs) {
+    GemvParams q = p;
+    const uint64_t rb = (uint64_t)p.K / 2;
+    const uint32_t box = 64u * (uint32_t)p.su;
+    if (!make_map_2d(&q.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.packed, rb, (uint64_t)p.N, rb, box, 16,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        (p.gated && !make_map_2d(&q.wmap3, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.packed3, rb, (uint64_t)p.N, rb, box,
+                                 16, CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return cudaErrorInvalidValue;
     const int smem = GEMV_PAIR_X_OFFSET + (p.x_staged ? p.M * p.K * 2 : 0);
-    if (p.gated)
-      return launch_kernel(nf4_gemv_pair_kernel<true>, p, grid, stream, cfg_gated, smem, GEMV_PAIR_SMEM_MAX,
-                           GEMV_PAIR_WARPS * 32);
-    return launch_kernel(nf4_gemv_pair_kernel<false>, p, grid, stream, cfg_pair, smem, GEMV_PAIR_SMEM_MAX,
-                         GEMV_PAIR_WARPS * 32);
+    const int nt = GEMV_PAIR_WARPS * 32;
+    if (p.su == 2)
+      return p.gated ? launch_kernel(nf4_gemv_pair_kernel<true, 2>, q, grid, stream, cfg_gated2, smem,
+                                     GEMV_PAIR_SMEM_MAX, nt)
+                     : launch_kernel(nf4_gemv_pair_kernel<false, 2>, q, grid, stream, cfg_pair2, smem,
+                                     GEMV_PAIR_SMEM_MAX, nt);
+    return p.gated ? launch_kernel(nf4_gemv_pair_kernel<true, 1>, q, grid, stream, cfg_gated, smem,
+                                   GEMV_PAIR_SMEM_MAX, nt)
+                   : launch_kernel(nf4_gemv_pair_kernel<false, 1>, q, grid, stream, cfg_pair, smem,
+                                   GEMV_PAIR_SMEM_MAX, nt);
   }
   if (p.M <= 8) return launch_kernel(nf4_gemv_block_kernel<1, 4>, p, grid, stream, cfg1);
   if (p.M <= 16) return launch_kernel(nf4_gemv_block_kernel<2, 2>, p, grid, stream, cfg2);
