@@ -128,9 +128,10 @@ bool use_pairs(const nf4b_weight* w, int rows) {
   if (rows > 4 || w->k_in % 128) return false;
   // The pair kernel copies scales with 4- and 8-byte cp.async: the 8-bit codes
   // as 4-byte aligned windows, fp32 scales at their natural alignment (paired
-  // when blocks are 64 codes).
+  // when blocks are 64 codes), and the 1 KB code2 table in 16-byte pieces.
   if (w->nested)
-    return aligned(w->absmax_code, 4) && aligned(w->absmax, 4) && w->blocksize2 >= (w->blocksize == 64 ? 2 : 1);
+    return aligned(w->absmax_code, 4) && aligned(w->absmax, 4) && aligned(w->code2, 16) &&
+           w->blocksize2 >= (w->blocksize == 64 ? 2 : 1);
   return aligned(w->absmax, w->blocksize == 64 ? 8 : 4);
 }
 

@@ -86,6 +86,16 @@ __device__ __forceinline__ int atomic_add_acq_rel(int* addr, int v) {
 // Shared-memory tables: the NF4 pair table and (nested scales) code2. Entry
 // e's 32 per-lane copies are 128 contiguous bytes (stride 256), written eight
 // copies per 16-byte store.
+// The pair table alone (entry e's 32 per-lane copies at e * 256).
+template <int THREADS>
+__device__ __forceinline__ void build_pair_lut(uint8_t* smem) {
+  for (int i = threadIdx.x; i < 256 * 8; i += THREADS) {
+    const int e = i >> 3, part = i & 7;
+    const uint32_t v = pack_bf16x2(c_nf4_code[e >> 4], c_nf4_code[e & 15]);
+    *reinterpret_cast<uint4*>(smem + e * 256 + part * 16) = make_uint4(v, v, v, v);
+  }
+}
+
 template <int THREADS = kThreads>
 __device__ __forceinline__ void build_tables(uint8_t* smem, const GemvParams& p) {
   for (int i = threadIdx.x; i < 256 * 8; i += THREADS) {
@@ -181,66 +191,11 @@ __device__ __forceinline__ uint16_t gate_bf16(float v1, float v3) {
   return f2bf(__fmul_rn(s, round_bf(v3)));
 }
 
-// Finish row tile `rt` of the pair kernel. Lane (g, t) holds rows g and g+8 of
-// activation row t for each half H (W, and W3 of a gated pair). Split tiles go
-// through the workspace: slot layout [slot][half][activation row][N].
-template <bool kGated>
-__device__ __forceinline__ void finish_pair_tile(const GemvParams& p, int rt, int u0, int u1, int gw,
-                                                 int g, int t, int lane, float a0, float b0, float a1,
-                                                 float b1) {
-  constexpr int H = kGated ? 2 : 1;
-  const int per_tile = p.blocks_per_tile * H;
-  const int t0 = rt * per_tile, t1 = t0 + per_tile - 1;
-  const bool whole = (t0 >= u0) && (t1 < u1);
-  const int N = p.N, M = p.M;
-  const int ra = rt * 16 + g, rb = ra + 8;
-  float v[2][2] = {{a0, b0}, {a1, b1}};  // [half][row g / g + 8]
-  if (!whole) {
-    const int w_lo = warp_of(t0, p.uq, p.ur);
-    const int n_contrib = warp_of(t1, p.uq, p.ur) - w_lo + 1;
-    const size_t MN = (size_t)M * N;
-    float* slot = p.partial + (size_t)(gw - w_lo) * H * MN + (size_t)t * N;
-    if (t < M) {
-#pragma unroll
-      for (int h = 0; h < H; ++h) {
-        if (ra < N) __stcg(slot + h * MN + ra, v[h][0]);
-        if (rb < N) __stcg(slot + h * MN + rb, v[h][1]);
-      }
-    }
-    // The warp barrier orders every lane's partial before lane 0's release
-    // (fence + arrival); the last arriver's acquire orders the reads after it.
-    __syncwarp();
-    int old = 0;
-    if (lane == 0) {
-      asm volatile("fence.acq_rel.gpu;" ::: "memory");
-      old = atomic_add_acq_rel(p.counters + rt, 1);
-    }
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != n_contrib - 1) return;
-    if (lane == 0) p.counters[rt] = 0;
-    __syncwarp();
-    if (t < M) {
-      const float* base = p.partial + (size_t)t * N;
-#pragma unroll
-      for (int h = 0; h < H; ++h) {
-        v[h][0] = ra < N ? sum_slots(base + h * MN + ra, H * MN, n_contrib) : 0.f;
-        v[h][1] = rb < N ? sum_slots(base + h * MN + rb, H * MN, n_contrib) : 0.f;
-      }
-    }
-  }
-  if (t >= M) return;
-  const size_t oa = (size_t)t * N + ra, ob = (size_t)t * N + rb;
-  if (kGated) {
-    if (ra < N) p.y[oa] = gate_bf16(v[0][0], v[1][0]);
-    if (rb < N) p.y[ob] = gate_bf16(v[0][1], v[1][1]);
-  } else {
-    if (ra < N) p.y[oa] = epilogue(v[0][0], p.epi, p.operand, oa);
-    if (rb < N) p.y[ob] = epilogue(v[0][1], p.epi, p.operand, ob);
-  }
-}
-
 // cp.async helpers (sm_80+ asynchronous global -> shared copies, tracked per
 // thread in commit groups).
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
 __device__ __forceinline__ void cp_async_8(uint32_t dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
 }
@@ -259,7 +214,7 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
 }
 
 // TMA and mbarrier helpers for the pair kernel.
-__device__ int g_gemv_error = 0;  // bit 0: a bounded wait gave up (read by nf4b_device_error)
+__device__ int g_gemv_error = 0;  // a bounded wait gave up: bit 0 weight stream, bit 1 split-tile reduce
 
 __device__ __forceinline__ unsigned long long gemv_globaltimer() {
   unsigned long long t;
@@ -305,6 +260,110 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
       }
     }
   }
+}
+
+// Store the outputs of row tile `rt` (rows g, g + 8 of activation row t):
+// the gate of the two halves for a gated pair, else the epilogue of half 0.
+template <bool kGated>
+__device__ __forceinline__ void store_pair_tile(const GemvParams& p, int rt, int g, int t,
+                                                const float (&v)[2][2]) {
+  const int N = p.N;
+  const int ra = rt * 16 + g, rb = ra + 8;
+  if (t >= p.M) return;
+  const size_t oa = (size_t)t * N + ra, ob = (size_t)t * N + rb;
+  if (kGated) {
+    if (ra < N) p.y[oa] = gate_bf16(v[0][0], v[1][0]);
+    if (rb < N) p.y[ob] = gate_bf16(v[0][1], v[1][1]);
+  } else {
+    if (ra < N) p.y[oa] = epilogue(v[0][0], p.epi, p.operand, oa);
+    if (rb < N) p.y[ob] = epilogue(v[0][1], p.epi, p.operand, ob);
+  }
+}
+
+// Finish row tile `rt` of the pair kernel from this warp's partial sums
+// v[half][row g / g + 8]. A tile inside the warp's run is stored at once.
+// A split tile is reduced by the warp owning its last unit; the others each
+// publish their partial in their own workspace slot, count themselves in with
+// a release increment and move on (no round trip). Returns true when this
+// warp is the reducer: it then finishes the tile later with reduce_pair_tile,
+// after the rest of its run, by when its contributors (the warps before it,
+// whose runs end in this tile) are done too. Each warp reduces at most one
+// tile: the one its run starts in.
+template <bool kGated>
+__device__ __forceinline__ bool finish_pair_tile(const GemvParams& p, int rt, int u0, int u1, int gw, int g,
+                                                 int t, int lane, const float (&v)[2][2]) {
+  constexpr int H = kGated ? 2 : 1;
+  const int per_tile = p.blocks_per_tile * H;
+  const int t0 = rt * per_tile, t1 = t0 + per_tile - 1;
+  if (t0 >= u0 && t1 < u1) {
+    store_pair_tile<kGated>(p, rt, g, t, v);
+    return false;
+  }
+  const int w_lo = warp_of(t0, p.uq, p.ur), w_hi = warp_of(t1, p.uq, p.ur);
+  if (gw == w_hi) return true;
+  const int N = p.N, M = p.M;
+  const int ra = rt * 16 + g, rb = ra + 8;
+  const size_t MN = (size_t)M * N;
+  float* slot = p.partial + (size_t)(gw - w_lo) * H * MN + (size_t)t * N;
+  if (t < M) {
+#pragma unroll
+    for (int h = 0; h < H; ++h) {
+      if (ra < N) __stcg(slot + h * MN + ra, v[h][0]);
+      if (rb < N) __stcg(slot + h * MN + rb, v[h][1]);
+    }
+  }
+  // The warp barrier orders every lane's partial before lane 0's release.
+  __syncwarp();
+  if (lane == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.counters + rt) : "memory");
+  return false;
+}
+
+// The reducer's half of a split tile: wait (bounded) for the other
+// contributors, sum their slots in slot order and its own partial last
+// (deterministic), re-zero the counter, store.
+template <bool kGated>
+__device__ __forceinline__ void reduce_pair_tile(const GemvParams& p, int rt, int gw, int g, int t, int lane,
+                                                 float (&v)[2][2]) {
+  constexpr int H = kGated ? 2 : 1;
+  const int per_tile = p.blocks_per_tile * H;
+  const int t0 = rt * per_tile;
+  const int others = gw - warp_of(t0, p.uq, p.ur);
+  int* ctr = p.counters + rt;
+  int ok = 1;
+  if (lane == 0) {
+    unsigned long long start = 0;
+    for (uint32_t i = 0;; ++i) {
+      int seen;
+      asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(ctr) : "memory");
+      if (seen == others) break;
+      if ((i & 15u) == 0u) {
+        const unsigned long long now = gemv_globaltimer();
+        if (i == 0) {
+          start = now;
+        } else if (now - start > 2000000000ull) {
+          atomicOr(&g_gemv_error, 2);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    *ctr = 0;
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();  // lane 0's acquire orders every lane's reads of the slots
+  if (!ok) return;
+  const int N = p.N, M = p.M;
+  const int ra = rt * 16 + g, rb = ra + 8;
+  const size_t MN = (size_t)M * N;
+  if (t < M) {
+    const float* base = p.partial + (size_t)t * N;
+#pragma unroll
+    for (int h = 0; h < H; ++h) {
+      if (ra < N) v[h][0] = sum_slots(base + h * MN + ra, H * MN, others) + v[h][0];
+      if (rb < N) v[h][1] = sum_slots(base + h * MN + rb, H * MN, others) + v[h][1];
+    }
+  }
+  store_pair_tile<kGated>(p, rt, g, t, v);
 }
 
 // Pair kernel. A unit is 16 weight rows x SU * 128 codes (SU = 2 for
@@ -445,6 +504,17 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   };
   set_phase(ct);
 
+  // The nested scales' code2 tables (1 KB each) are copied asynchronously as
+  // the first commit group, so the table build below never waits on memory.
+  if (p.nested) {
+    if (threadIdx.x < 64) {
+      cp_async_16(smem_addr(smem + GEMV_LUT_BYTES) + threadIdx.x * 16, p.code2 + threadIdx.x * 4);
+    } else if (kGated && threadIdx.x < 128) {
+      const int i = threadIdx.x - 64;
+      cp_async_16(smem_addr(smem + GEMV_LUT_BYTES + 1024) + i * 16, p.code2_3 + i * 4);
+    }
+  }
+  cp_async_commit();
   // Prologue: R - 1 units requested (one cp.async group each, empty past the run).
 #pragma unroll
   for (int i = 0; i < R - 1; ++i) {
@@ -454,9 +524,8 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     }
     cp_async_commit();
   }
-  // The tables are built while the first units are in flight.
-  build_tables<kT>(smem, p);
-  __syncthreads();
+  // The pair table is built while the first units are in flight.
+  build_pair_lut<kT>(smem);
   pdl_launch_dependents();
   if (active && NF4B_GEMV_PREFETCH_EARLY) prefetch_next(p, gw, lane);
   pdl_wait();
@@ -467,8 +536,9 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     const uint4* src = reinterpret_cast<const uint4*>(p.x);
     uint4* dst = reinterpret_cast<uint4*>(smem + GEMV_PAIR_X_OFFSET);
     for (int i = threadIdx.x; i < n16; i += kT) dst[i] = __ldcg(src + i);
-    __syncthreads();
   }
+  cp_async_wait<R - 1>();  // this thread's code2 copy (R - 1 unit groups were committed after it)
+  __syncthreads();         // the pair table, code2 and x are visible to every warp
 
   // x: column c of the MMA is (activation row c >> 1, block parity c & 1);
   // lane (g, t) supplies column g for codes of block parity t >> 1.
@@ -480,6 +550,8 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
 
   float acc_a = 0.f, acc_b = 0.f;    // W (or W1): rows g, g+8 for activation row t
   float acc3_a = 0.f, acc3_b = 0.f;  // gated pair: W3
+  int pend_rt = -1;                  // the split tile this warp reduces, after its run
+  float pend[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
   int st_use = 0, st_fill = R - 1;
   uint32_t phase = 0;  // bit s: parity of stage s's next completion
   for (int u = u0; u < u1; ++u) {
@@ -608,10 +680,15 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       acc_b += yb;
     }
     if ((kb == B - 1 && (!kGated || hh == 1)) || u == u1 - 1) {
-      finish_pair_tile<kGated>(p, rt, u0, u1, gw, g, t, lane, acc_a, acc_b, acc3_a, acc3_b);
+      const float v[2][2] = {{acc_a, acc_b}, {acc3_a, acc3_b}};
+      if (finish_pair_tile<kGated>(p, rt, u0, u1, gw, g, t, lane, v)) {
+        pend_rt = rt;
+        pend[0][0] = acc_a; pend[0][1] = acc_b; pend[1][0] = acc3_a; pend[1][1] = acc3_b;
+      }
       acc_a = acc_b = acc3_a = acc3_b = 0.f;
     }
   }
+  if (pend_rt >= 0) reduce_pair_tile<kGated>(p, pend_rt, gw, g, t, lane, pend);
   cp_async_wait<0>();
   if (!NF4B_GEMV_PREFETCH_EARLY) prefetch_next(p, gw, lane);
 }
