@@ -243,6 +243,7 @@ def step_workspace(layers, io, device):
 
     L = _lib.lib()
     need = max(int(L.nf4b_gemm_workspace_size(ctypes.byref(m._nf4_fast["desc"]), 1)) for m in layers[0])
+    need = max(need, 64 << 20)   # covers every chain of S2-Pro layers at M=1 (each launch checks)
     return torch.zeros(need, dtype=torch.uint8, device=device)
 
 
@@ -251,6 +252,8 @@ MODES = {
               "4 launches per layer in stream order, each naming the weights of a later launch for L2 prefetch",
     "single": "one launch per projection (w1, then w3 with the silu-gate epilogue on w1's output): "
               "5 launches per layer",
+    "chain": "the same 4 matmuls per layer with the same data dependencies, issued as nf4b_gemv_chain "
+             "launches of --chain-layers layers each (job j reads its inputs only after jobs < j are done)",
 }
 
 
@@ -261,7 +264,7 @@ class StepPlan:
     Each launch names the weights of the launch `distance` places later as an
     L2 prefetch hint (0: no hints)."""
 
-    def __init__(self, layers, io: StepIO, ws, mode: str = "decode", distance: int = 0):
+    def __init__(self, layers, io: StepIO, ws, mode: str = "decode", distance: int = 0, chain_layers: int = 9):
         from ttspipe_b200 import _lib
 
         self.L = _lib.lib()
@@ -270,7 +273,25 @@ class StepPlan:
         self.launches = []   # ("gemm", desc, x, y, epi, operand) | ("gated", d1, d3, x, y)
         weights = []         # per launch: descriptors it reads
         in_base, out_base = io.dev_in.data_ptr(), io.dev_out.data_ptr()
-        for li, mods in enumerate(layers):
+        if mode == "chain":
+            for first in range(0, len(layers), chain_layers):
+                ids = list(range(first, min(first + chain_layers, len(layers))))
+                arr = (_lib.ChainJob * (len(ids) * len(JOBS)))()
+                i = 0
+                for li in ids:
+                    mods = layers[li]
+                    for ji, (_, widx, epi) in enumerate(JOBS):
+                        x_off, op_off, y_off, _, _ = io.specs[li * len(JOBS) + ji]
+                        arr[i].w = ctypes.pointer(mods[widx[0]]._nf4_fast["desc"])
+                        arr[i].w3 = ctypes.pointer(mods[widx[1]]._nf4_fast["desc"]) if epi == "gated" else None
+                        arr[i].x, arr[i].y = in_base + 2 * x_off, out_base + 2 * y_off
+                        arr[i].operand = in_base + 2 * op_off if op_off is not None else None
+                        arr[i].epi = 1 if epi == 1 else 0
+                        arr[i].norm_weight, arr[i].norm_eps = None, 0.0
+                        i += 1
+                self.launches.append(("chain", arr))
+                weights.append([])
+        for li, mods in enumerate(layers if mode != "chain" else []):
             for ji, (_, widx, epi) in enumerate(JOBS):
                 x_off, op_off, y_off, _, _ = io.specs[li * len(JOBS) + ji]
                 x, y = in_base + 2 * x_off, out_base + 2 * y_off
@@ -303,7 +324,10 @@ class StepPlan:
         L = self.L
         for launch, opts in zip(self.launches, self.opts):
             o = ctypes.byref(opts) if opts is not None else None
-            if launch[0] == "gated":
+            if launch[0] == "chain":
+                arr = launch[1]
+                st = L.nf4b_gemv_chain(arr, len(arr), 1, self.ws_ptr, self.ws_bytes, stream_ptr)
+            elif launch[0] == "gated":
                 _, d1, d3, x, y = launch
                 st = L.nf4b_gemm_gated(ctypes.byref(d1), ctypes.byref(d3), x, y, 1, self.ws_ptr, self.ws_bytes,
                                        o, stream_ptr)
@@ -361,12 +385,12 @@ def detail(layers, io, ws, stream, device):
         torch.cuda.synchronize(device)
         return st.elapsed_time(en) / reps * 1e3  # us per replay
 
-    cases = [("decode", d) for d in (0, 1, 2)] + [("single", d) for d in (0, 1)]
-    for mode, dist in cases:
-        plan = StepPlan(layers, io, ws, mode, dist)
+    cases = [("decode", 0, 0), ("decode", 2, 0), ("single", 0, 0)] + [("chain", 0, c) for c in (1, 4, 9)]
+    for mode, dist, cl in cases:
+        plan = StepPlan(layers, io, ws, mode, dist, cl or 9)
         g = graph_of(lambda: plan.issue(stream.cuda_stream))
         us = time_graph(g)
-        log(f"  step mode={mode} prefetch_distance={dist}: {len(plan)} launches, {us:.1f} us, "
+        log(f"  step mode={mode} prefetch_distance={dist} chain_layers={cl}: {len(plan)} launches, {us:.1f} us, "
             f"{STEP_BYTES / us / 1e3:.0f} GB/s (graph)")
         del g
 
@@ -385,7 +409,7 @@ def run_gpu(args):
     layers = make_layers(device, rank)
     io = StepIO(device, rank)
     ws = step_workspace(layers, io, device)
-    plan = StepPlan(layers, io, ws, args.mode, args.prefetch_distance)
+    plan = StepPlan(layers, io, ws, args.mode, args.prefetch_distance, args.chain_layers)
     log(f"[rank {rank}] built {N_LAYERS} layers in {time.time() - t0:.1f}s; step bytes {STEP_BYTES / 1e9:.3f} GB")
 
     stream = torch.cuda.Stream(device)
@@ -460,11 +484,13 @@ def run_gpu(args):
                                    "M=1, NF4 bs64 + double-quant (bs2 256)",
                        "schedule": f"{args.mode}: {MODES[args.mode]}",
                        "prefetch_distance": args.prefetch_distance,
+                       "chain_layers": args.chain_layers if args.mode == "chain" else None,
                        "baseline_config": "configs[1] (one slow-AR layer's linears at M=1) x 36 distinct layers",
                        "bytes_per_step": STEP_BYTES, "rows": 1,
                        "l2": "inputs larger than L2 (1.87 GB of weights per step per GPU)",
                        "parallelism": f"replicas x{world} (no collective on the data path)"},
             "gpu_launches": len(plan) * args.steps,
+            "launches_per_step": len(plan),
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": io.h2d_bytes,
                     "d2h_bytes_per_step": io.d2h_bytes,
                     "path": "C ABI nf4b_gemm calls (CUDA graph) + pinned H2D inputs + D2H outputs per step"},
@@ -612,6 +638,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--detail", action="store_true")
     ap.add_argument("--mode", default="decode", choices=sorted(MODES))
+    ap.add_argument("--chain-layers", type=int, default=9, help="layers per nf4b_gemv_chain launch (--mode chain)")
     ap.add_argument("--prefetch-distance", type=int, default=0,
                     help="launches ahead whose weights each launch streams into L2 (0: none; "
                          "measured slower at 1-3 on B200, so off by default)")

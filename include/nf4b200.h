@@ -124,6 +124,40 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
 int nf4b_gemm_gated(const nf4b_weight* w1, const nf4b_weight* w3, const void* x, void* y, int rows,
                     void* workspace, size_t workspace_bytes, const nf4b_gemm_opts* opts, void* stream);
 
+/* One job of nf4b_gemv_chain. */
+typedef struct nf4b_chain_job {
+  const nf4b_weight* w;     /* the weight; for a gated pair, W1                      */
+  const nf4b_weight* w3;    /* gated pair: W3 (same shape and quantisation); else NULL */
+  const void* x;            /* [rows, k_in] bf16, 16-byte aligned; may be an earlier job's y */
+  void* y;                  /* [rows, n_out] bf16                                     */
+  const void* operand;      /* epilogue operand [rows, n_out] bf16 (may be an earlier job's y), or NULL */
+  int32_t epi;              /* NF4B_EPI_*; ignored for gated pairs                    */
+  const void* norm_weight;  /* non-NULL: x is first RMS-normalised with this bf16 [k_in] weight, exactly
+                               as nf4b_rms_norm (then the matmul reads the normalised x) */
+  float norm_eps;
+} nf4b_chain_job;
+
+#define NF4B_MAX_CHAIN_JOBS 40
+
+/*
+ * Up to NF4B_MAX_CHAIN_JOBS decode GEMVs that depend on one another, in ONE
+ * persistent launch: job j reads its x and operand only after every output of
+ * jobs 0..j-1 is written, so a transformer block's matmul sequence
+ * (wo + residual -> RMSNorm -> the W1/W3 gate -> w2 + residual, and so on) runs
+ * without a launch between its steps. Each job computes what nf4b_gemm (or
+ * nf4b_gemm_gated, after nf4b_rms_norm when norm_weight is given) computes,
+ * within the GEMV's rounding. Serves 1..4 rows of blocksize-64 NF4 weights
+ * with k_in % 256 == 0 and rows * k_in * 2 <= 40 KB (NF4B_ERR_SHAPE
+ * otherwise). The workspace (nf4b_gemv_chain_workspace_size) is zeroed once
+ * by the caller and left zeroed by every call. No reference counterpart: the
+ * reference launches every matmul, norm and gate separately
+ * (app/engine/fusedlayer.py:212-269).
+ */
+int nf4b_gemv_chain(const nf4b_chain_job* jobs, int n_jobs, int rows, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+size_t nf4b_gemv_chain_workspace_size(const nf4b_chain_job* jobs, int n_jobs, int rows);
+
 /* Bytes of workspace nf4b_gemm needs for this weight and row count. */
 size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows);
 

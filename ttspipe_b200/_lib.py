@@ -30,6 +30,8 @@ EXPORTS = (
     "nf4b_gemm_workspace_size",
     "nf4b_gemm_noalloc",
     "nf4b_gemm_gated",
+    "nf4b_gemv_chain",
+    "nf4b_gemv_chain_workspace_size",
     "nf4b_dequantize",
     "nf4b_rms_norm",
     "nf4b_rope",
@@ -53,6 +55,21 @@ class Nf4Weight(ctypes.Structure):
         ("blocksize", ctypes.c_int32),
         ("blocksize2", ctypes.c_int32),
         ("nested", ctypes.c_int32),
+    ]
+
+
+class ChainJob(ctypes.Structure):
+    """`nf4b_chain_job`."""
+
+    _fields_ = [
+        ("w", ctypes.POINTER(Nf4Weight)),
+        ("w3", ctypes.POINTER(Nf4Weight)),
+        ("x", ctypes.c_void_p),
+        ("y", ctypes.c_void_p),
+        ("operand", ctypes.c_void_p),
+        ("epi", ctypes.c_int32),
+        ("norm_weight", ctypes.c_void_p),
+        ("norm_eps", ctypes.c_float),
     ]
 
 
@@ -84,6 +101,8 @@ def _declare(lib) -> None:
         "nf4b_gemm": (i32, [wp, vp, vp, i32, i32, vp, vp, sz, vp]),
         "nf4b_gemm_ex": (i32, [wp, vp, vp, i32, i32, vp, vp, sz, ctypes.POINTER(GemmOpts), vp]),
         "nf4b_gemm_gated": (i32, [wp, wp, vp, vp, i32, vp, sz, ctypes.POINTER(GemmOpts), vp]),
+        "nf4b_gemv_chain": (i32, [ctypes.POINTER(ChainJob), i32, i32, vp, sz, vp]),
+        "nf4b_gemv_chain_workspace_size": (sz, [ctypes.POINTER(ChainJob), i32, i32]),
         "nf4b_gemm_workspace_size": (sz, [wp, i32]),
         "nf4b_gemm_noalloc": (i32, [wp, vp, vp, i32, i32, vp, vp]),
         "nf4b_dequantize": (i32, [wp, vp, vp]),

@@ -12,6 +12,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tmap.cuh"
 
 namespace nf4b {
 int read_device_error(int clear);
@@ -124,6 +125,16 @@ void prefetch_ranges(const nf4b_gemm_opts* opts, PrefetchHint* h) {
   }
 }
 
+// 128-code sub-units per pair-kernel unit: 2 when a unit's four 64-blocks
+// start at a multiple of 4 (k_in % 256 == 0) so their scale data is one
+// aligned copy - nested with second-level blocks of >= 4 (one shared
+// second-level scale), or fp32 scales 16-byte aligned - and x can be staged.
+int pair_su(const nf4b_weight* w, int rows) {
+  if (w->blocksize != 64 || w->k_in % 256 || (long long)rows * w->k_in * 2 > GEMV_PAIR_X_MAX) return 1;
+  if (w->nested) return w->blocksize2 >= 4 ? 2 : 1;
+  return aligned(w->absmax, 16) ? 2 : 1;
+}
+
 bool use_pairs(const nf4b_weight* w, int rows) {
   if (rows > 4 || w->k_in % 128) return false;
   // The pair kernel copies scales with 4- and 8-byte cp.async: the 8-bit codes
@@ -140,11 +151,12 @@ size_t gemv_workspace_bytes(const nf4b_weight* w, int rows, int sms) {
   gemv_plan(w->n_out, w->k_in, rows, sms, false, &a);
   size_t bytes = a.partial_bytes;
   if (rows <= 4 && w->k_in % 128 == 0) {  // the pair kernel may serve this call, plain or gated
-    for (int gated = 0; gated < 2; ++gated) {
-      GemvPlan b;
-      gemv_plan(w->n_out, w->k_in, rows, sms, true, &b, gated != 0, gemv_pair_su(w->k_in, w->blocksize));
-      if (b.partial_bytes > bytes) bytes = b.partial_bytes;
-    }
+    for (int gated = 0; gated < 2; ++gated)
+      for (int su = 1; su <= pair_su(w, rows); ++su) {
+        GemvPlan b;
+        gemv_plan(w->n_out, w->k_in, rows, sms, true, &b, gated != 0, su);
+        if (b.partial_bytes > bytes) bytes = b.partial_bytes;
+      }
   }
   return GEMV_COUNTER_BYTES + bytes;
 }
@@ -169,7 +181,7 @@ int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* 
     return fail(NF4B_ERR_SHAPE, "the gated GEMV serves 1..4 rows with k_in %% 128 == 0 (got %d rows, k_in %d)",
                 rows, w->k_in);
   const int sms = current_sm_count();
-  const int su = pairs ? gemv_pair_su(w->k_in, w->blocksize) : 1;
+  const int su = pairs ? (gated ? (pair_su(w, rows) == 2 && pair_su(w3, rows) == 2 ? 2 : 1) : pair_su(w, rows)) : 1;
   GemvPlan plan;
   gemv_plan(w->n_out, w->k_in, rows, sms, pairs, &plan, gated, su);
   const size_t need = gemv_workspace_bytes(w, rows, sms);
@@ -290,6 +302,102 @@ int nf4b_gemm_gated(const nf4b_weight* w1, const nf4b_weight* w3, const void* x,
   if ((st = check_device())) return st;
   return gemv_call(w1, w3, x, y, rows, NF4B_EPI_NONE, nullptr, workspace, workspace_bytes, opts,
                    reinterpret_cast<cudaStream_t>(stream));
+}
+
+namespace {
+
+// Validate a chain and fill the kernel parameters (pointers, maps, plan).
+int build_chain(const nf4b_chain_job* jobs, int n_jobs, int rows, ChainParams* cp, size_t* partial_bytes) {
+  if (jobs == nullptr || n_jobs <= 0) return fail(NF4B_ERR_ARG, "empty job list");
+  if (n_jobs > CHAIN_MAX_JOBS)
+    return fail(NF4B_ERR_SHAPE, "%d jobs exceed the chain limit of %d", n_jobs, CHAIN_MAX_JOBS);
+  if (rows < 1 || rows > 4) return fail(NF4B_ERR_SHAPE, "the GEMV chain serves 1..4 rows (got %d)", rows);
+  cp->n_jobs = n_jobs;
+  cp->M = rows;
+  for (int i = 0; i < n_jobs; ++i) {
+    const nf4b_chain_job& jb = jobs[i];
+    int st = check_weight(jb.w);
+    if (st) return st;
+    const nf4b_weight* w = jb.w;
+    if (w->blocksize != 64 || w->k_in % 256)
+      return fail(NF4B_ERR_SHAPE, "job %d: the chain needs blocksize 64 and k_in %% 256 == 0", i);
+    if ((long long)rows * w->k_in * 2 > GEMV_PAIR_X_MAX)
+      return fail(NF4B_ERR_SHAPE, "job %d: %d rows x k_in %d do not fit the staged x", i, rows, w->k_in);
+    if ((long long)(w->n_out + 15) / 16 > CHAIN_MAX_TILES) return fail(NF4B_ERR_SHAPE, "job %d too large", i);
+    if (!use_pairs(w, rows)) return fail(NF4B_ERR_ALIGN, "job %d: scales not aligned for the copies", i);
+    if (jb.x == nullptr || jb.y == nullptr) return fail(NF4B_ERR_ARG, "job %d: x or y is null", i);
+    if (!aligned(jb.x, 16)) return fail(NF4B_ERR_ALIGN, "job %d: x is not 16-byte aligned", i);
+    if (!aligned(jb.y, 2) || (jb.operand && !aligned(jb.operand, 2)) || (jb.norm_weight && !aligned(jb.norm_weight, 2)))
+      return fail(NF4B_ERR_ALIGN, "job %d: y/operand/norm weight not 2-byte aligned", i);
+    if (jb.norm_weight != nullptr && !(jb.norm_eps >= 0.f))
+      return fail(NF4B_ERR_ARG, "job %d: norm eps must be >= 0", i);
+    ChainJob& J = cp->jobs[i];
+    J.gated = jb.w3 != nullptr ? 1 : 0;
+    if (J.gated) {
+      const nf4b_weight* w3 = jb.w3;
+      if ((st = check_weight(w3))) return st;
+      if (w3->n_out != w->n_out || w3->k_in != w->k_in || w3->blocksize != w->blocksize ||
+          w3->nested != w->nested || (w->nested && w3->blocksize2 != w->blocksize2) || !use_pairs(w3, rows))
+        return fail(NF4B_ERR_SHAPE, "job %d: the gated pair's weights differ in shape or quantisation", i);
+    } else {
+      if (jb.epi < NF4B_EPI_NONE || jb.epi > NF4B_EPI_SILU_GATE)
+        return fail(NF4B_ERR_ARG, "job %d: unknown epilogue %d", i, jb.epi);
+      if (jb.epi != NF4B_EPI_NONE && jb.operand == nullptr)
+        return fail(NF4B_ERR_ARG, "job %d: epilogue %d needs an operand", i, jb.epi);
+    }
+    const uint64_t rb = (uint64_t)w->k_in / 2;
+    if (!make_map_2d(&J.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->packed, rb, (uint64_t)w->n_out, rb, 128, 16,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        (J.gated && !make_map_2d(&J.wmap3, CU_TENSOR_MAP_DATA_TYPE_UINT8, jb.w3->packed, rb, (uint64_t)w->n_out,
+                                 rb, 128, 16, CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return fail(NF4B_ERR_ARG, "job %d: cannot describe the weight to the TMA unit", i);
+    J.a8 = w->absmax_code;
+    J.absmax = w->absmax;
+    J.code2 = w->code2;
+    J.offset = w->offset;
+    J.a8_3 = J.gated ? jb.w3->absmax_code : nullptr;
+    J.absmax3 = J.gated ? jb.w3->absmax : nullptr;
+    J.code2_3 = J.gated ? jb.w3->code2 : nullptr;
+    J.offset3 = J.gated ? jb.w3->offset : 0.f;
+    J.x = static_cast<const uint16_t*>(jb.x);
+    J.y = static_cast<uint16_t*>(jb.y);
+    J.operand = static_cast<const uint16_t*>(jb.operand);
+    J.norm_w = static_cast<const uint16_t*>(jb.norm_weight);
+    J.norm_eps = jb.norm_eps;
+    J.N = w->n_out;
+    J.K = w->k_in;
+    J.nested = w->nested ? 1 : 0;
+    J.bs2_shift = w->nested ? log2i(w->blocksize2) : 0;
+    J.epi = J.gated ? NF4B_EPI_NONE : jb.epi;
+  }
+  *partial_bytes = chain_plan(cp, current_sm_count());
+  return NF4B_OK;
+}
+
+}  // namespace
+
+extern "C" size_t nf4b_gemv_chain_workspace_size(const nf4b_chain_job* jobs, int n_jobs, int rows) {
+  static thread_local ChainParams cp;
+  size_t partial = 0;
+  if (build_chain(jobs, n_jobs, rows, &cp, &partial)) return 0;
+  return GEMV_COUNTER_BYTES + partial;
+}
+
+extern "C" int nf4b_gemv_chain(const nf4b_chain_job* jobs, int n_jobs, int rows, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  static thread_local ChainParams cp;
+  size_t partial = 0;
+  int st = build_chain(jobs, n_jobs, rows, &cp, &partial);
+  if (st) return st;
+  const size_t need = GEMV_COUNTER_BYTES + partial;
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(NF4B_ERR_WORKSPACE, "chain workspace of %zu bytes needed, %zu given", need,
+                workspace ? workspace_bytes : (size_t)0);
+  if (!aligned(workspace, 256)) return fail(NF4B_ERR_ALIGN, "workspace is not 256-byte aligned");
+  if ((st = check_device())) return st;
+  cp.counters = static_cast<int*>(workspace);
+  cp.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + GEMV_COUNTER_BYTES);
+  return launch_status(launch_gemv_chain(cp, reinterpret_cast<cudaStream_t>(stream)), "nf4 gemv chain launch");
 }
 
 extern "C" int nf4b_dequantize(const nf4b_weight* w, void* out, void* stream) {

@@ -38,7 +38,10 @@ constexpr int GEMV_PAIR_W_OFFSET = GEMV_LUT_BYTES + 2 * 256 * 4;           // 10
 constexpr int GEMV_PAIR_SC_OFFSET = GEMV_PAIR_W_OFFSET + GEMV_PAIR_SLOTS * 1024;
 constexpr int GEMV_PAIR_BAR_OFFSET = GEMV_PAIR_SC_OFFSET + GEMV_PAIR_SLOTS * 128;
 constexpr int GEMV_PAIR_X_OFFSET = GEMV_PAIR_BAR_OFFSET + GEMV_PAIR_SLOTS * 8;
-constexpr int GEMV_PAIR_X_MAX = 40 * 1024;
+#ifndef NF4B_GEMV_PAIR_X_KB
+#define NF4B_GEMV_PAIR_X_KB 40
+#endif
+constexpr int GEMV_PAIR_X_MAX = NF4B_GEMV_PAIR_X_KB * 1024;
 constexpr int GEMV_PAIR_SMEM_MAX = GEMV_PAIR_X_OFFSET + GEMV_PAIR_X_MAX;
 static_assert(GEMV_PAIR_W_OFFSET % 1024 == 0, "TMA boxes must be aligned");
 static_assert(GEMV_PAIR_SMEM_MAX <= 227 * 1024, "pair kernel shared memory exceeds one CTA's limit");
@@ -132,10 +135,53 @@ int gemv_sm_count(int dev);
 // `pairs`: use the pair kernel (units of 128 codes; up to 4 activation rows,
 // k_in % 128 == 0, scale arrays aligned for its paired loads).
 // `gated`: the pair kernel's gated mode (tiles of W units then W3 units).
-// `su`: 128-code sub-units per pair-kernel unit (gemv_pair_su).
+// `su`: 128-code sub-units per pair-kernel unit (2 for blocksize-64 weights
+// with k_in % 256 == 0 whose x fits the shared-memory stage, else 1).
 void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan, bool gated = false, int su = 1);
-int gemv_pair_su(int K, int blocksize);
 cudaError_t launch_gemv(const GemvParams& p, int grid, bool pairs, cudaStream_t stream);
+
+// ---- GEMV chain (nf4_gemv.cu): dependent decode GEMVs in one persistent launch
+
+constexpr int CHAIN_MAX_JOBS = 40;
+// The done counters (one per job) and the CTA exit counter sit at the end of
+// the workspace's counter region; split-tile counters use its start.
+constexpr int CHAIN_DONE_INTS = 64;
+constexpr long long CHAIN_MAX_TILES = GEMV_MAX_TILES - CHAIN_DONE_INTS;
+
+struct alignas(64) ChainJob {
+  CUtensorMap wmap;   // packed W, boxes of 128 bytes x 16 rows
+  CUtensorMap wmap3;  // gated pair: W3
+  const uint8_t* a8;
+  const float* absmax;
+  const float* code2;
+  const uint8_t* a8_3;
+  const float* absmax3;
+  const float* code2_3;
+  const uint16_t* x;
+  uint16_t* y;
+  const uint16_t* operand;
+  const uint16_t* norm_w;  // RMS-normalise x with this weight first, or null
+  float offset, offset3, norm_eps;
+  int N, K;
+  int nested, bs2_shift, gated, epi;
+  int B;      // 256-code units per row tile and half
+  int tiles;  // row tiles of 16
+  int uq, ur; // warp w's run: [w*uq + min(w, ur), ...) of tiles * B * (gated ? 2 : 1) units
+};
+
+struct alignas(64) ChainParams {
+  int n_jobs;
+  int M;
+  int warps_total;
+  float* partial;
+  int* counters;
+  ChainJob jobs[CHAIN_MAX_JOBS];
+};
+
+// Units and warp runs of every job (fields B, tiles, uq, ur); returns the
+// partial-sum bytes the split tiles need (the largest job's).
+size_t chain_plan(ChainParams* p, int sm_count);
+cudaError_t launch_gemv_chain(const ChainParams& p, cudaStream_t stream);
 
 // ---- dequantisation (nf4_dequant.cu) ---------------------------------------
 

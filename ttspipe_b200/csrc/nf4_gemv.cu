@@ -468,25 +468,22 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     if (t < 2) {
       const uint32_t ds = sring_s + st * SB + (g + 8 * t) * (8 * SU);
       const long long be = sbase + ((lk * 128 * SU) >> bs_shift);
-      if (p.nested) {
-        // the 4-byte aligned window(s) holding this unit's 8-bit codes
+      if (SU == 2) {
+        // k_in % 256 == 0, so a unit's four blocks start at a multiple of 4:
+        // nested - their codes are one aligned word and (second-level blocks
+        // of >= 4) share one second-level scale; plain - 16 aligned bytes.
+        if (p.nested) {
+          cp_async_4(ds, a8 + be, 4u);
+          cp_async_4(ds + 4, absmax + (be >> p.bs2_shift), 4u);
+        } else {
+          cp_async_16(ds, absmax + be);
+        }
+      } else if (p.nested) {
+        // the 4-byte aligned window holding this unit's one or two 8-bit codes
         const long long w0 = be & ~3LL;
         const long long left = a8_total - w0;
         cp_async_4(ds, a8 + w0, (uint32_t)(left < 4 ? left : 4));
-        if (SU == 2) {
-          // a second word only when the codes run past the first (left > 4 then)
-          const long long w1 = left > 4 ? w0 + 4 : w0;
-          const long long l1 = left > 4 ? a8_total - w1 : 0;
-          cp_async_4(ds + 4, a8 + w1, (uint32_t)(l1 < 4 ? l1 : 4));
-          // each 128-code sub-unit's two 64-blocks share a second-level block
-          cp_async_4(ds + 8, absmax + (be >> p.bs2_shift), 4u);
-          cp_async_4(ds + 12, absmax + ((be + 2) >> p.bs2_shift), 4u);
-        } else {
-          cp_async_4(ds + 4, absmax + (be >> p.bs2_shift), 4u);
-        }
-      } else if (SU == 2) {
-        cp_async_8(ds, absmax + be);
-        cp_async_8(ds + 8, absmax + be + 2);
+        cp_async_4(ds + 4, absmax + (be >> p.bs2_shift), 4u);
       } else if (bs64) {
         cp_async_8(ds, absmax + be);
       } else {
@@ -547,6 +544,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   const size_t xrow_off = (size_t)(xlane ? xtok : 0) * K * 2 + t * 64;  // bytes
   const uint4* xrow = reinterpret_cast<const uint4*>(
       (p.x_staged ? xs : reinterpret_cast<const uint8_t*>(p.x)) + xrow_off);
+  const uint4* xrow_s = reinterpret_cast<const uint4*>(xs + xrow_off);
 
   float acc_a = 0.f, acc_b = 0.f;    // W (or W1): rows g, g+8 for activation row t
   float acc3_a = 0.f, acc3_b = 0.f;  // gated pair: W3
@@ -609,16 +607,13 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
         uint32_t ea, oa, eb, ob;
         float s2a, s2b;
         if (SU == 2) {
-          // blocks 2i, 2i+1 of the unit sit at bytes (row phase + 2i) and +1 of the 8-byte window
-          const unsigned long long wa8 = ((unsigned long long)sa[1] << 32) | sa[0];
-          const unsigned long long wb8 = ((unsigned long long)sb[1] << 32) | sb[0];
-          const uint32_t sha = (uint32_t)(pha + 2 * i) * 8, shb = (uint32_t)(phb + 2 * i) * 8;
-          ea = (uint32_t)(wa8 >> sha) & 0xFFu;
-          oa = (uint32_t)(wa8 >> (sha + 8)) & 0xFFu;
-          eb = (uint32_t)(wb8 >> shb) & 0xFFu;
-          ob = (uint32_t)(wb8 >> (shb + 8)) & 0xFFu;
-          s2a = __uint_as_float(sa[(2 + i) % (2 * SU)]);
-          s2b = __uint_as_float(sb[(2 + i) % (2 * SU)]);
+          // blocks 2i, 2i+1 of the unit are bytes 2i, 2i+1 of the code word
+          ea = (sa[0] >> (16 * i)) & 0xFFu;
+          oa = (sa[0] >> (16 * i + 8)) & 0xFFu;
+          eb = (sb[0] >> (16 * i)) & 0xFFu;
+          ob = (sb[0] >> (16 * i + 8)) & 0xFFu;
+          s2a = __uint_as_float(sa[1]);
+          s2b = __uint_as_float(sb[1]);
         } else {
           // the unit's first block sits at byte (row phase + block index) & 3 of the window
           const int be0 = (kb2 * 128) >> bs_shift;
@@ -639,9 +634,10 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
         se_b = __uint_as_float(sb[(2 * i) % (2 * SU)]); so_b = __uint_as_float(sb[(2 * i + 1) % (2 * SU)]);
       }
       uint4 xv[4];
-      if (xlane) {  // shared memory when staged, else global (generic loads)
+      if (xlane) {  // SU = 2: x is always staged (shared loads); SU = 1: staged or global
+        const uint4* xr = SU == 2 ? xrow_s : xrow;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) xv[j] = xrow[kb2 * 16 + j];
+        for (int j = 0; j < 4; ++j) xv[j] = xr[kb2 * 16 + j];
       } else {
 #pragma unroll
         for (int j = 0; j < 4; ++j) xv[j] = make_uint4(0, 0, 0, 0);
@@ -846,6 +842,452 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_block_kernel(const GemvP
   if (!NF4B_GEMV_PREFETCH_EARLY) prefetch_next(p, gw, lane);
 }
 
+// ---------------------------------------------------------------------------
+// GEMV chain: dependent decode GEMVs (rows <= 4, blocksize-64 weights with
+// k_in % 256 == 0, x staged in shared memory) in ONE persistent launch
+// ---------------------------------------------------------------------------
+//
+// Job j reads its x (and epilogue operand) only after every row tile of jobs
+// 0..j-1 is stored, so x may be an earlier job's y. Units and runs per job
+// are those of the pair kernel (256-code units, equal contiguous runs per
+// warp); each warp's TMA ring runs straight across job boundaries, so the next
+// job's weights are already in shared memory while the current job finishes.
+// At a job boundary each CTA waits (thread 0, bounded) until the previous
+// job's completion count equals its tile count, then stages the job's code2
+// table and x - RMS-normalised first when the job asks for it, with the
+// arithmetic of nf4b_rms_norm - behind a CTA barrier. Every stored row tile
+// adds one to its job's count (release). The last CTA out re-zeroes the
+// counts, so the workspace is left as it was found.
+
+__device__ __forceinline__ float rms_rsqrt(double ss, int width, float eps) {
+  const float t = __fadd_rn((float)(ss / (double)width), eps);
+  return (float)(1.0 / sqrt((double)t));
+}
+
+__device__ __forceinline__ void chain_store_tile(const ChainJob& J, int M, int rt, int g, int t,
+                                                 const float (&v)[2][2]) {
+  const int N = J.N;
+  const int ra = rt * 16 + g, rb = ra + 8;
+  if (t >= M) return;
+  const size_t oa = (size_t)t * N + ra, ob = (size_t)t * N + rb;
+  if (J.gated) {
+    if (ra < N) J.y[oa] = gate_bf16(v[0][0], v[1][0]);
+    if (rb < N) J.y[ob] = gate_bf16(v[0][1], v[1][1]);
+    return;
+  }
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int row = e ? rb : ra;
+    const size_t o = e ? ob : oa;
+    if (row >= N) continue;
+    const float y = round_bf(v[0][e]);
+    float out = y;
+    if (J.epi == NF4B_EPI_RESIDUAL) {
+      out = __fadd_rn(bf2f(__ldcg(J.operand + o)), y);
+    } else if (J.epi == NF4B_EPI_SILU_GATE) {
+      const float a = bf2f(__ldcg(J.operand + o));
+      out = __fmul_rn(round_bf(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a)))), y);
+    }
+    J.y[o] = f2bf(out);
+  }
+}
+
+__global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
+    nf4_gemv_chain_kernel(const __grid_constant__ ChainParams p) {
+  constexpr int SU = 2;
+  constexpr int R = GEMV_PAIR_STAGE_KB / SU;
+  constexpr int WB = 1024 * SU, SB = 128 * SU;
+  constexpr int kT = GEMV_PAIR_WARPS * 32;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ double red[GEMV_PAIR_WARPS];
+  __shared__ int s_ok;
+  const uint8_t* lut = smem;
+  float* code2_s = reinterpret_cast<float*>(smem + GEMV_LUT_BYTES);
+  float* code2_s3 = code2_s + 256;
+  uint8_t* xs = smem + GEMV_PAIR_X_OFFSET;
+
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  const int gw = blockIdx.x * GEMV_PAIR_WARPS + wib;
+  const int g = lane >> 2, t = lane & 3;
+  const int M = p.M, n_jobs = p.n_jobs;
+  const uint32_t lane_base = (uint32_t)lane * 4u;
+  int* done = p.counters + (GEMV_MAX_TILES - CHAIN_DONE_INTS);
+  int* exit_ctr = done + (CHAIN_DONE_INTS - 1);
+
+  const uint8_t* wring = smem + GEMV_PAIR_W_OFFSET + wib * (R * WB);
+  const uint8_t* sring = smem + GEMV_PAIR_SC_OFFSET + wib * (R * SB);
+  const uint32_t wring_s = smem_addr(wring), sring_s = smem_addr(sring);
+  const uint32_t bar_s = smem_addr(smem + GEMV_PAIR_BAR_OFFSET + wib * (R * 8));
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < R; ++i) mbar_init1(bar_s + 8 * i);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncwarp();
+
+  auto run_of = [&](int j, int& a, int& b) {
+    const ChainJob& J = p.jobs[j];
+    a = gw * J.uq + min(gw, J.ur);
+    b = a + J.uq + (gw < J.ur ? 1 : 0);
+  };
+
+  // Load cursor: job lj, unit lu of this warp's run [lu, lend) in it, and the
+  // unit's tile lt, half lh, k unit lk.
+  int lj = -1, lu = 0, lend = 0, lt = 0, lh = 0, lk = 0;
+  long long sbase = 0;
+  auto load_rows = [&]() {
+    const ChainJob& J = p.jobs[lj];
+    sbase = (long long)min(lt * 16 + g + 8 * t, J.N - 1) * (J.K >> 6);
+  };
+  auto next_job = [&]() {
+    while (++lj < n_jobs) {
+      run_of(lj, lu, lend);
+      if (lu < lend) {
+        const ChainJob& J = p.jobs[lj];
+        const int per_tile = J.gated ? 2 * J.B : J.B;
+        lt = lu / per_tile;
+        lk = lu - lt * per_tile;
+        lh = 0;
+        if (J.gated && lk >= J.B) {
+          lh = 1;
+          lk -= J.B;
+        }
+        load_rows();
+        return;
+      }
+    }
+  };
+  next_job();
+  auto step_load = [&]() {
+    if (++lu == lend) {
+      next_job();
+      return;
+    }
+    const ChainJob& J = p.jobs[lj];
+    if (++lk == J.B) {
+      lk = 0;
+      if (J.gated && lh == 0) {
+        lh = 1;
+      } else {
+        lh = 0;
+        ++lt;
+      }
+      load_rows();
+    }
+  };
+  auto issue = [&](int st) {
+    const ChainJob& J = p.jobs[lj];
+    const bool h3 = J.gated && lh;
+    if (lane == 0) {
+      const uint32_t bar = bar_s + 8 * st;
+      mbar_expect(bar, (uint32_t)WB);
+      tma_box(wring_s + st * WB, h3 ? &J.wmap3 : &J.wmap, lk * 64 * SU, lt * 16, bar);
+    }
+    if (t < 2) {
+      const uint32_t ds = sring_s + st * SB + (g + 8 * t) * (8 * SU);
+      const long long be = sbase + lk * 4;  // four 64-blocks per unit
+      const float* absmax = h3 ? J.absmax3 : J.absmax;
+      if (J.nested) {
+        const uint8_t* a8 = h3 ? J.a8_3 : J.a8;
+        const long long total = (long long)J.N * (J.K >> 6);
+        const long long w0 = be & ~3LL;
+        const long long left = total - w0;
+        cp_async_4(ds, a8 + w0, (uint32_t)(left < 4 ? left : 4));
+        const long long w1 = left > 4 ? w0 + 4 : w0;
+        const long long l1 = left > 4 ? total - w1 : 0;
+        cp_async_4(ds + 4, a8 + w1, (uint32_t)(l1 < 4 ? l1 : 4));
+        cp_async_4(ds + 8, absmax + (be >> J.bs2_shift), 4u);
+        cp_async_4(ds + 12, absmax + ((be + 2) >> J.bs2_shift), 4u);
+      } else {
+        cp_async_8(ds, absmax + be);
+        cp_async_8(ds + 8, absmax + be + 2);
+      }
+    }
+  };
+
+#pragma unroll
+  for (int i = 0; i < R - 1; ++i) {
+    if (lj < n_jobs) {
+      issue(i);
+      step_load();
+    }
+    cp_async_commit();
+  }
+  build_pair_lut<kT>(smem);
+  pdl_launch_dependents();
+  pdl_wait();
+
+  int st_use = 0, st_fill = R - 1;
+  uint32_t phase = 0;
+  for (int j = 0; j < n_jobs; ++j) {
+    const ChainJob& J = p.jobs[j];
+    // ---- job boundary: every warp of this CTA is done with the last job's x and code2
+    __syncthreads();
+    if (j > 0 && threadIdx.x == 0) {
+      const int need = p.jobs[j - 1].tiles;
+      unsigned long long start = 0;
+      for (uint32_t i = 0;; ++i) {
+        int seen;
+        asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(done + (j - 1)) : "memory");
+        if (seen >= need) break;
+        if ((i & 15u) == 0u) {
+          const unsigned long long now = gemv_globaltimer();
+          if (i == 0) {
+            start = now;
+          } else if (now - start > 2000000000ull) {
+            atomicOr(&g_gemv_error, 4);
+            s_ok = 0;
+            break;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (!s_ok) break;
+    const int K = J.K, N = J.N;
+    if (J.nested) {
+      for (int i = threadIdx.x; i < 256; i += kT) {
+        code2_s[i] = __ldcg(J.code2 + i);
+        if (J.gated) code2_s3[i] = __ldcg(J.code2_3 + i);
+      }
+    }
+    {
+      const int n16 = (M * K) >> 3;
+      const uint4* src = reinterpret_cast<const uint4*>(J.x);
+      uint4* dst = reinterpret_cast<uint4*>(xs);
+      for (int i = threadIdx.x; i < n16; i += kT) dst[i] = __ldcg(src + i);
+    }
+    __syncthreads();
+    if (J.norm_w != nullptr) {
+      uint16_t* xr = reinterpret_cast<uint16_t*>(xs);
+      for (int m = 0; m < M; ++m) {
+        double ss = 0.0;
+        for (int i = threadIdx.x; i < K; i += kT) {
+          const double v = bf2f(xr[m * K + i]);
+          ss += v * v;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        if (lane == 0) red[wib] = ss;
+        __syncthreads();
+        double tot = 0.0;
+#pragma unroll
+        for (int w = 0; w < GEMV_PAIR_WARPS; ++w) tot += red[w];
+        const float r = rms_rsqrt(tot, K, J.norm_eps);
+        for (int i = threadIdx.x; i < K; i += kT) {
+          const float normed = round_bf(__fmul_rn(bf2f(xr[m * K + i]), r));
+          xr[m * K + i] = f2bf(__fmul_rn(normed, bf2f(__ldg(J.norm_w + i))));
+        }
+        __syncthreads();
+      }
+    }
+
+    // ---- this warp's units of job j
+    const int nblk = K >> 6;
+    const int B = J.B, per_tile = J.gated ? 2 * B : B;
+    int u0, u1;
+    run_of(j, u0, u1);
+    int ct = u0 / per_tile, ck = u0 - ct * per_tile, ch = 0;
+    if (J.gated && ck >= B) {
+      ch = 1;
+      ck -= B;
+    }
+    int ph_a = (int)(((long long)min(ct * 16 + g, N - 1) * nblk) & 3);
+    int ph_b = (int)(((long long)min(ct * 16 + g + 8, N - 1) * nblk) & 3);
+    const int xtok = g >> 1;
+    const bool xlane = (xtok < M) && ((g & 1) == (t >> 1));
+    const uint4* xrow = reinterpret_cast<const uint4*>(xs + (size_t)(xlane ? xtok : 0) * K * 2 + t * 64);
+    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [half][row g / g + 8]
+    int pend_rt = -1;
+    float pend[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    for (int u = u0; u < u1; ++u) {
+      __syncwarp();
+      if (lj < n_jobs) {
+        issue(st_fill);
+        step_load();
+      }
+      cp_async_commit();
+      st_fill = st_fill + 1 == R ? 0 : st_fill + 1;
+      cp_async_wait<R - 1>();
+      if (!mbar_wait_bounded(bar_s + 8 * st_use, (phase >> st_use) & 1u)) {
+        s_ok = 0;
+        break;
+      }
+      phase ^= 1u << st_use;
+      __syncwarp();
+      const uint8_t* wst = wring + st_use * WB;
+      const uint8_t* sst = sring + st_use * SB;
+      st_use = st_use + 1 == R ? 0 : st_use + 1;
+
+      const int rt = ct, kb = ck, hh = ch;
+      const int pha = ph_a, phb = ph_b;
+      if (++ck == B) {
+        ck = 0;
+        if (J.gated && ch == 0) {
+          ch = 1;
+        } else {
+          ch = 0;
+          ++ct;
+          ph_a = (int)(((long long)min(ct * 16 + g, N - 1) * nblk) & 3);
+          ph_b = (int)(((long long)min(ct * 16 + g + 8, N - 1) * nblk) & 3);
+        }
+      }
+      const uint4 va = *reinterpret_cast<const uint4*>(sst + g * 16);
+      const uint4 vb = *reinterpret_cast<const uint4*>(sst + (g + 8) * 16);
+      const bool h3 = J.gated && hh;
+      float ya = 0.f, yb = 0.f;
+#pragma unroll
+      for (int i = 0; i < SU; ++i) {
+        const int kb2 = kb * SU + i;
+        float se_a, so_a, se_b, so_b;
+        if (J.nested) {
+          const float* c2 = h3 ? code2_s3 : code2_s;
+          const float off = h3 ? J.offset3 : J.offset;
+          const unsigned long long wa8 = ((unsigned long long)va.y << 32) | va.x;
+          const unsigned long long wb8 = ((unsigned long long)vb.y << 32) | vb.x;
+          const uint32_t sha = (uint32_t)(pha + 2 * i) * 8, shb = (uint32_t)(phb + 2 * i) * 8;
+          const float s2a = __uint_as_float(i ? va.w : va.z), s2b = __uint_as_float(i ? vb.w : vb.z);
+          se_a = nested_scale(c2[(uint32_t)(wa8 >> sha) & 0xFFu], s2a, off);
+          so_a = nested_scale(c2[(uint32_t)(wa8 >> (sha + 8)) & 0xFFu], s2a, off);
+          se_b = nested_scale(c2[(uint32_t)(wb8 >> shb) & 0xFFu], s2b, off);
+          so_b = nested_scale(c2[(uint32_t)(wb8 >> (shb + 8)) & 0xFFu], s2b, off);
+        } else {
+          se_a = __uint_as_float(i ? va.z : va.x); so_a = __uint_as_float(i ? va.w : va.y);
+          se_b = __uint_as_float(i ? vb.z : vb.x); so_b = __uint_as_float(i ? vb.w : vb.y);
+        }
+        uint4 xv[4];
+        if (xlane) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) xv[q] = xrow[kb2 * 16 + q];
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) xv[q] = make_uint4(0, 0, 0, 0);
+        }
+        const uint4 wav = *reinterpret_cast<const uint4*>(wst + g * (64 * SU) + i * 64 + t * 16);
+        const uint4 wbv = *reinterpret_cast<const uint4*>(wst + (g + 8) * (64 * SU) + i * 64 + t * 16);
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t wa[4] = {wav.x, wav.y, wav.z, wav.w};
+        const uint32_t wb[4] = {wbv.x, wbv.y, wbv.z, wbv.w};
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          const uint32_t w0 = wa[s >> 1], w1 = wb[s >> 1];
+          const int j0 = 2 * (s & 1);
+          const uint32_t a0 = lut_lookup(lut, w0, lut_sel(j0), lane_base);
+          const uint32_t a2 = lut_lookup(lut, w0, lut_sel(j0 + 1), lane_base);
+          const uint32_t a1 = lut_lookup(lut, w1, lut_sel(j0), lane_base);
+          const uint32_t a3 = lut_lookup(lut, w1, lut_sel(j0 + 1), lane_base);
+          const uint4& xq = xv[s >> 1];
+          const uint32_t b0 = (s & 1) ? xq.z : xq.x;
+          const uint32_t b1 = (s & 1) ? xq.w : xq.y;
+          if (s & 1)
+            mma_bf16_16816(d1, a0, a1, a2, a3, b0, b1);
+          else
+            mma_bf16_16816(d0, a0, a1, a2, a3, b0, b1);
+        }
+        ya += fmaf(so_a, d0[1] + d1[1], (d0[0] + d1[0]) * se_a);
+        yb += fmaf(so_b, d0[3] + d1[3], (d0[2] + d1[2]) * se_b);
+      }
+      if (h3) {
+        acc[1][0] += ya;
+        acc[1][1] += yb;
+      } else {
+        acc[0][0] += ya;
+        acc[0][1] += yb;
+      }
+      if ((kb == B - 1 && (!J.gated || hh == 1)) || u == u1 - 1) {
+        // finish row tile rt (see finish_pair_tile; here every stored tile also
+        // counts toward the job's completion)
+        const int H = J.gated ? 2 : 1;
+        const int t0 = rt * per_tile, t1 = t0 + per_tile - 1;
+        if (t0 >= u0 && t1 < u1) {
+          chain_store_tile(J, M, rt, g, t, acc);
+          __syncwarp();
+          if (lane == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(done + j) : "memory");
+        } else {
+          const int w_lo = warp_of(t0, J.uq, J.ur), w_hi = warp_of(t1, J.uq, J.ur);
+          if (gw == w_hi) {
+            pend_rt = rt;
+            pend[0][0] = acc[0][0]; pend[0][1] = acc[0][1]; pend[1][0] = acc[1][0]; pend[1][1] = acc[1][1];
+          } else {
+            const int ra = rt * 16 + g, rb = ra + 8;
+            const size_t MN = (size_t)M * N;
+            float* slot = p.partial + (size_t)(gw - w_lo) * H * MN + (size_t)t * N;
+            if (t < M) {
+              for (int h = 0; h < H; ++h) {
+                if (ra < N) __stcg(slot + h * MN + ra, acc[h][0]);
+                if (rb < N) __stcg(slot + h * MN + rb, acc[h][1]);
+              }
+            }
+            __syncwarp();
+            if (lane == 0)
+              asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.counters + rt) : "memory");
+          }
+        }
+        acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.f;
+      }
+    }
+    if (pend_rt >= 0 && s_ok) {
+      // this warp reduces the split tile its run started in (see reduce_pair_tile)
+      const int H = J.gated ? 2 : 1;
+      const int rt = pend_rt;
+      const int others = gw - warp_of(rt * per_tile, J.uq, J.ur);
+      int* ctr = p.counters + rt;
+      int ok = 1;
+      if (lane == 0) {
+        unsigned long long start = 0;
+        for (uint32_t i = 0;; ++i) {
+          int seen;
+          asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(ctr) : "memory");
+          if (seen == others) break;
+          if ((i & 15u) == 0u) {
+            const unsigned long long now = gemv_globaltimer();
+            if (i == 0) {
+              start = now;
+            } else if (now - start > 2000000000ull) {
+              atomicOr(&g_gemv_error, 2);
+              ok = 0;
+              break;
+            }
+          }
+        }
+        *ctr = 0;
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      __syncwarp();
+      if (ok) {
+        const int ra = rt * 16 + g, rb = ra + 8;
+        const size_t MN = (size_t)M * N;
+        if (t < M) {
+          const float* base = p.partial + (size_t)t * N;
+          for (int h = 0; h < H; ++h) {
+            if (ra < N) pend[h][0] = sum_slots(base + h * MN + ra, H * MN, others) + pend[h][0];
+            if (rb < N) pend[h][1] = sum_slots(base + h * MN + rb, H * MN, others) + pend[h][1];
+          }
+        }
+        chain_store_tile(J, M, rt, g, t, pend);
+        __syncwarp();
+        if (lane == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(done + j) : "memory");
+      } else {
+        s_ok = 0;
+      }
+    }
+  }
+  cp_async_wait<0>();
+  // The last CTA out re-zeroes the completion counts for the next launch.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int old = atomicAdd(exit_ctr, 1);
+    if (old == (int)gridDim.x - 1) {
+      __threadfence();
+      for (int j = 0; j < n_jobs; ++j) done[j] = 0;
+      *exit_ctr = 0;
+    }
+  }
+}
+
 template <typename Kernel>
 cudaError_t launch_kernel(Kernel kernel, const GemvParams& p, int grid, cudaStream_t stream,
                           bool* configured, int smem = GEMV_SMEM_BYTES, int smem_max = GEMV_SMEM_BYTES,
@@ -895,7 +1337,7 @@ int gemv_sm_count(int dev) {
   return g_sm_count[dev];
 }
 
-int gemv_pair_su(int K, int blocksize) { return (blocksize == 64 && K % 256 == 0) ? 2 : 1; }
+
 
 void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan, bool gated, int su) {
   const long long tiles = (N + 15) / 16;
@@ -917,6 +1359,52 @@ void gemv_plan(int N, int K, int M, int sm_count, bool pairs, GemvPlan* plan, bo
   plan->slots = (int)((B * H + per - 1) / per + 1);
   plan->counter_bytes = GEMV_COUNTER_BYTES;
   plan->partial_bytes = (size_t)plan->slots * H * M * N * sizeof(float);
+}
+
+size_t chain_plan(ChainParams* p, int sm_count) {
+  const long long W = (long long)sm_count * GEMV_PAIR_WARPS;
+  p->warps_total = (int)W;
+  size_t partial = 0;
+  for (int i = 0; i < p->n_jobs; ++i) {
+    ChainJob& J = p->jobs[i];
+    const long long H = J.gated ? 2 : 1;
+    J.B = J.K / 256;
+    J.tiles = (J.N + 15) / 16;
+    const long long U = (long long)J.tiles * J.B * H;
+    J.uq = (int)(U / W);
+    J.ur = (int)(U % W);
+    // a tile of B * H units meets at most ceil(B * H / floor(U / W)) + 1 warps
+    const long long per = J.uq > 0 ? J.uq : 1;
+    const long long slots = (J.B * H + per - 1) / per + 1;
+    const size_t bytes = (size_t)slots * H * p->M * J.N * sizeof(float);
+    if (bytes > partial) partial = bytes;
+  }
+  return partial;
+}
+
+cudaError_t launch_gemv_chain(const ChainParams& p, cudaStream_t stream) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(nf4_gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         GEMV_PAIR_SMEM_MAX);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  int kmax = 0;
+  for (int i = 0; i < p.n_jobs; ++i) kmax = p.jobs[i].K > kmax ? p.jobs[i].K : kmax;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.warps_total / GEMV_PAIR_WARPS));
+  cfg.blockDim = dim3(GEMV_PAIR_WARPS * 32);
+  cfg.dynamicSmemBytes = GEMV_PAIR_X_OFFSET + p.M * kmax * 2;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, nf4_gemv_chain_kernel, p);
 }
 
 cudaError_t launch_gemv(const GemvParams& p, int grid, bool pairs, cudaStream_t stream) {

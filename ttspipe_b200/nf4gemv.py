@@ -287,6 +287,89 @@ def matmul_gated(w1, w3, x, *, prefetch=None):
     return out.view(*x.shape[:-1], N)
 
 
+def matmul_chain(steps):
+    """Dependent decode matmuls in ONE launch (an extension of the reference's
+    API, which launches each matmul, norm and gate separately,
+    app/engine/fusedlayer.py:212-269).
+
+    `steps`: a list of dicts, run in order, each with
+      ``w`` (prepared linear), ``x`` (bf16 tensor [..., in] or the int index of
+      an earlier step, whose output is then the input), optional ``w3`` (the
+      FeedForward gate silu(x W^T) * (x W3^T)), ``epi`` / ``operand`` (tensor
+      or step index) as for ``matmul``, and ``norm`` = (weight, eps) to
+      RMS-normalise x first exactly as ``fusedops.rms_norm``.
+    Returns the list of step outputs, or None if any step is outside the
+    chain's envelope (1..4 rows, blocksize 64, in_features % 256 == 0,
+    rows * in_features * 2 <= 40 KB); then nothing was launched.
+    """
+    import torch
+
+    if not steps or len(steps) > 40:
+        return None
+    arr = (_lib.ChainJob * len(steps))()
+    outs, keep = [], []
+    rows = dev = None
+    for i, st in enumerate(steps):
+        w, w3 = st["w"], st.get("w3")
+        fasts = [getattr(m, "_nf4_fast", None) for m in ((w, w3) if w3 is not None else (w,))]
+        if any(f is None for f in fasts):
+            return None
+        K, N = fasts[0]["K"], fasts[0]["M"]
+        x = st["x"]
+        if isinstance(x, int):
+            if not 0 <= x < i:
+                return None
+            x = outs[x]
+        if x.dtype != torch.bfloat16 or not x.is_cuda or x.shape[-1] != K:
+            return None
+        flat = x.reshape(-1, K)
+        if not flat.is_contiguous() or flat.data_ptr() % 16:
+            return None
+        if rows is None:
+            rows, dev = flat.shape[0], x.device
+        if flat.shape[0] != rows:
+            return None
+        epi = int(st.get("epi", EPI_NONE))
+        operand = st.get("operand")
+        if isinstance(operand, int):
+            if not 0 <= operand < i:
+                return None
+            operand = outs[operand]
+        if w3 is None and epi != EPI_NONE:
+            if operand is None or operand.numel() != rows * N or operand.dtype != torch.bfloat16 \
+                    or not operand.is_contiguous():
+                return None
+        out = torch.empty((rows, N), dtype=torch.bfloat16, device=dev)
+        arr[i].w = ctypes.pointer(fasts[0]["desc"])
+        arr[i].w3 = ctypes.pointer(fasts[1]["desc"]) if w3 is not None else None
+        arr[i].x, arr[i].y = flat.data_ptr(), out.data_ptr()
+        arr[i].epi = epi if w3 is None else EPI_NONE
+        arr[i].operand = operand.data_ptr() if (w3 is None and epi != EPI_NONE) else None
+        norm = st.get("norm")
+        if norm is not None:
+            nw, eps = norm
+            if nw.dtype != torch.bfloat16 or nw.numel() != K or not nw.is_contiguous():
+                return None
+            arr[i].norm_weight, arr[i].norm_eps = nw.data_ptr(), float(eps)
+            keep.append(nw)
+        else:
+            arr[i].norm_weight, arr[i].norm_eps = None, 0.0
+        keep += [flat, operand]
+        outs.append(out)
+    if not available():
+        raise RuntimeError(f"nf4 kernels unavailable: {_unavailable}")
+    L = _lib.lib()
+    need = int(L.nf4b_gemv_chain_workspace_size(arr, len(steps), rows))
+    if need == 0:
+        return None
+    ws = _workspace(dev, need)
+    stream = torch.cuda.current_stream(dev)
+    _lib.check(L.nf4b_gemv_chain(arr, len(steps), rows, ws.data_ptr(), ws.numel(),
+                                 ctypes.c_void_p(stream.cuda_stream)))
+    _stats["fast"] += len(steps)
+    return outs
+
+
 def dequantize(module):
     """The bf16 dense weight [out, in] the kernels multiply by (bit-exact
     bitsandbytes dequantisation), computed on the device."""
