@@ -78,7 +78,7 @@ const char* nf4b_last_error(void);
 /*
  * The library's device error word: non-zero after a kernel gave up on a
  * bounded wait (a pipeline barrier that never completed): bit 0 the GEMM,
- * bit 1 the GEMV's weight stream. Synchronises the device to read it; `clear`
+ * bit 1 the GEMV, bit 2 decode attention's KV copies. Synchronises the device to read it; `clear`
  * resets it; -1 if it cannot be read. No counterpart in the reference, whose
  * kernels have no waits.
  */

@@ -17,6 +17,7 @@
 namespace nf4b {
 int read_device_error(int clear);
 int read_gemv_error(int clear);
+int read_attn_error(int clear);
 }
 
 using namespace nf4b;
@@ -233,9 +234,9 @@ int nf4b_version(void) { return 100; }
 const char* nf4b_last_error(void) { return g_err; }
 
 int nf4b_device_error(int clear) {
-  const int gemm = read_device_error(clear), gemv = read_gemv_error(clear);
-  if (gemm < 0 || gemv < 0) return -1;
-  return (gemm ? 1 : 0) | (gemv ? 2 : 0);
+  const int gemm = read_device_error(clear), gemv = read_gemv_error(clear), attn = read_attn_error(clear);
+  if (gemm < 0 || gemv < 0 || attn < 0) return -1;
+  return (gemm ? 1 : 0) | (gemv ? 2 : 0) | (attn ? 4 : 0);
 }
 
 size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows) {

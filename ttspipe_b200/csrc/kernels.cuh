@@ -242,6 +242,11 @@ struct AttnPlan {
   size_t partial_bytes;
 };
 void attn_plan(int n_head, int head_dim, int window, AttnPlan* plan);
+// One thread-block cluster of 8 CTAs per KV head; cudaErrorNotSupported when
+// such a cluster cannot be resident on the device.
+cudaError_t launch_cluster_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int64_t* pos,
+                                     const uint8_t* mask, uint16_t* out, int nh, int nkv, int max_len, int window,
+                                     cudaStream_t stream);
 cudaError_t launch_decode_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
                                     const int64_t* pos, const uint8_t* mask, uint16_t* out, int nh, int nkv,
                                     int max_len, int window, float* partial, int* counters,
