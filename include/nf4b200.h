@@ -181,6 +181,33 @@ int nf4b_gemm_noalloc(const nf4b_weight* w, const void* x, void* y, int rows, in
                       const void* operand, void* stream);
 
 /*
+ * y[n_out] = bf16(x W^T) for a dense bf16 weight W[n_out, k_in] (row-major)
+ * and one activation row x[k_in], fp32 accumulation - the fork's bf16 output
+ * heads (the slow AR's LM head, the fast AR's codebook heads), which the
+ * reference runs through torch. k_in in {1024, 2048, 2560, 4096}; w and x
+ * 16-byte aligned.
+ */
+int nf4b_dense_gemv(const void* w, const void* x, void* y, int n_out, int k_in, void* stream);
+
+/*
+ * Draw one token id from a bf16 logit row, on the device (graph-capturable):
+ * the fork's sampler as the reference calls it (app/engine/graphs.py:55-73;
+ * fused in app/engine/fusedsample.py) - logits sorted descending, positions
+ * past top_k (<= 64) or past cumulative softmax probability top_p (softmax of
+ * the unscaled logits over the whole vocabulary) dropped except the first,
+ * the kept logits divided by max(temperature, 1e-5), softmax, one draw. The
+ * draw uses one uniform from a counter-based hash of (seed, *step) (step may
+ * be NULL: 0), so a run is reproducible from its seed. Writes out[0] (int64).
+ * vocab <= 262144. The workspace (nf4b_sample_workspace_size) is zeroed once
+ * by the caller and left zeroed.
+ */
+int nf4b_sample(const void* logits, int vocab, float temperature, float top_p, int top_k,
+                unsigned long long seed, const int64_t* step, int64_t* out, void* workspace,
+                size_t workspace_bytes, void* stream);
+
+size_t nf4b_sample_workspace_size(int vocab);
+
+/*
  * out[n_out, k_in] = RNE_bf16(NF4[q] * scale) - bitsandbytes' dequantize_4bit
  * to bf16 (the per-element value of app/engine/nf4gemv.py:185-188 in bf16).
  */

@@ -442,6 +442,65 @@ def decode_block(x_bits, weights: dict, k_cache_bits, v_cache_bits, pos: int, fr
 # --------------------------------------------------------------------------
 
 
+# --------------------------------------------------------------------------
+# output heads and sampling (the frame's tail)
+# --------------------------------------------------------------------------
+
+
+def dense_gemv_exact(x_bits, w_bits) -> np.ndarray:
+    """x W^T of a bf16 row and a dense bf16 weight [N, K] in fp64, unrounded:
+    the fork's bf16 output heads (app/engine/graphs.py:205-217 replays them)."""
+    x = bf16_to_f32(np.asarray(x_bits).reshape(-1)).astype(np.float64)
+    w = bf16_to_f32(w_bits).astype(np.float64)
+    return w @ x
+
+
+_MASK64 = (1 << 64) - 1
+
+
+def splitmix64(z: int) -> int:
+    """The counter-based hash the device sampler draws its uniform from."""
+    z = (z + 0x9E3779B97F4A7C15) & _MASK64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _MASK64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _MASK64
+    return z ^ (z >> 31)
+
+
+def sample_uniform(seed: int, step: int) -> float:
+    """u in [0, 1) for (seed, step), 24 bits, as the device computes it."""
+    h = splitmix64((seed ^ ((step * 0xD1B54A32D192ED03) & _MASK64)) & _MASK64)
+    return float(np.float32((h >> 40) * (1.0 / 16777216.0)))
+
+
+def sample_token(logit_bits, temperature: float, top_p: float, top_k: int, seed: int, step: int):
+    """The fork's sampler as the reference calls it (app/engine/graphs.py:55-73):
+    sort descending (ties: smaller index first); p = softmax of the sorted,
+    unscaled logits over the WHOLE vocabulary; drop position i if
+    cumsum(p)[i] > top_p or i >= top_k, never i = 0; divide the kept logits by
+    max(temperature, 1e-5); softmax; one inverse-CDF draw with
+    sample_uniform(seed, step). Returns (token, kept ids, their probabilities).
+    """
+    v = bf16_to_f32(np.asarray(logit_bits).reshape(-1)).astype(np.float64)
+    order = np.lexsort((np.arange(v.size), -v))
+    sv = v[order]
+    p = np.exp(sv - sv[0])
+    p /= p.sum()
+    cum = np.cumsum(p)
+    k = max(1, min(int(top_k), 64, v.size))
+    keep = 1
+    for i in range(1, k):
+        if cum[i] > top_p:
+            break
+        keep = i + 1
+    z = sv[:keep] / max(float(temperature), 1e-5)
+    q = np.exp(z - z[0])
+    q /= q.sum()
+    u = sample_uniform(seed, step)
+    pick = int(np.searchsorted(np.cumsum(q), u, side="right"))
+    pick = min(pick, keep - 1)
+    return int(order[pick]), order[:keep].copy(), q
+
+
 def relative_error(got, ref) -> float:
     """max|got - ref| / max|ref| (tests/test_nf4gemv.py:59-62)."""
     got = np.asarray(got, dtype=np.float64)

@@ -104,3 +104,22 @@ def test_attention_matches_the_references_torch_attention(att, case):
     if q.shape[1] == 1:
         y1 = orc.attention(q[:, 0], k, v, k.shape[1], nh, nkv)
         assert np.array_equal(y1, want[:, 0])
+
+
+def test_sampler_oracle_follows_the_reference_rule():
+    """Hand-checkable case of the fork's rule: cumulative probability cut,
+    first position always kept, temperature after the cut."""
+    logits = np.array([2.0, 1.0, 0.0, -1.0, 3.0], dtype=np.float32)
+    bits = orc.f32_to_bf16(logits)
+    p = np.exp(np.sort(logits.astype(np.float64))[::-1] - 3.0)
+    p /= p.sum()                     # 0.6364, 0.2341, 0.0861, 0.0317, 0.0117
+    tok, kept, q = orc.sample_token(bits, 1.0, 0.9, 64, 0, 0)
+    assert list(kept) == [4, 0]      # cumsum 0.870 <= 0.9, then 0.956 > 0.9 cuts the rest
+    assert tok in (4, 0)
+    tok, kept, _ = orc.sample_token(bits, 1.0, 0.8, 64, 0, 0)
+    assert list(kept) == [4]         # 0.870 > 0.8 already at position 1
+    tok, kept, _ = orc.sample_token(bits, 1.0, 0.5, 64, 0, 0)
+    assert list(kept) == [4]         # position 0 is always kept
+    tok, kept, _ = orc.sample_token(bits, 1.0, 1.0, 3, 0, 0)
+    assert list(kept) == [4, 0, 1]   # top_k
+    assert 0.0 <= orc.sample_uniform(7, 3) < 1.0

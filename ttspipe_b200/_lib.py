@@ -31,6 +31,9 @@ EXPORTS = (
     "nf4b_gemm_noalloc",
     "nf4b_gemm_gated",
     "nf4b_gemv_chain",
+    "nf4b_dense_gemv",
+    "nf4b_sample",
+    "nf4b_sample_workspace_size",
     "nf4b_gemv_chain_workspace_size",
     "nf4b_dequantize",
     "nf4b_rms_norm",
@@ -102,6 +105,9 @@ def _declare(lib) -> None:
         "nf4b_gemm_ex": (i32, [wp, vp, vp, i32, i32, vp, vp, sz, ctypes.POINTER(GemmOpts), vp]),
         "nf4b_gemm_gated": (i32, [wp, wp, vp, vp, i32, vp, sz, ctypes.POINTER(GemmOpts), vp]),
         "nf4b_gemv_chain": (i32, [ctypes.POINTER(ChainJob), i32, i32, vp, sz, vp]),
+        "nf4b_dense_gemv": (i32, [vp, vp, vp, i32, i32, vp]),
+        "nf4b_sample": (i32, [vp, i32, ctypes.c_float, ctypes.c_float, i32, ctypes.c_uint64, vp, vp, vp, sz, vp]),
+        "nf4b_sample_workspace_size": (sz, [i32]),
         "nf4b_gemv_chain_workspace_size": (sz, [ctypes.POINTER(ChainJob), i32, i32]),
         "nf4b_gemm_workspace_size": (sz, [wp, i32]),
         "nf4b_gemm_noalloc": (i32, [wp, vp, vp, i32, i32, vp, vp]),

@@ -401,6 +401,47 @@ extern "C" int nf4b_gemv_chain(const nf4b_chain_job* jobs, int n_jobs, int rows,
   return launch_status(launch_gemv_chain(cp, reinterpret_cast<cudaStream_t>(stream)), "nf4 gemv chain launch");
 }
 
+extern "C" int nf4b_dense_gemv(const void* w, const void* x, void* y, int n_out, int k_in, void* stream) {
+  if (w == nullptr || x == nullptr || y == nullptr) return fail(NF4B_ERR_ARG, "null pointer");
+  if (n_out <= 0) return fail(NF4B_ERR_SHAPE, "n_out must be positive (got %d)", n_out);
+  if (k_in != 1024 && k_in != 2048 && k_in != 2560 && k_in != 4096)
+    return fail(NF4B_ERR_SHAPE, "k_in %d is not one of 1024, 2048, 2560, 4096", k_in);
+  if (!aligned(w, 16) || !aligned(x, 16) || !aligned(y, 2)) return fail(NF4B_ERR_ALIGN, "w/x not 16-byte aligned");
+  int st = check_device();
+  if (st) return st;
+  return launch_status(launch_dense_gemv(static_cast<const uint16_t*>(w), static_cast<const uint16_t*>(x),
+                                         static_cast<uint16_t*>(y), n_out, k_in, current_sm_count(),
+                                         reinterpret_cast<cudaStream_t>(stream)),
+                       "dense gemv launch");
+}
+
+extern "C" size_t nf4b_sample_workspace_size(int vocab) {
+  if (vocab <= 0 || vocab > SAMPLER_MAX_VOCAB) return 0;
+  return sampler_workspace_bytes(vocab);
+}
+
+extern "C" int nf4b_sample(const void* logits, int vocab, float temperature, float top_p, int top_k,
+                           unsigned long long seed, const int64_t* step, int64_t* out, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (logits == nullptr || out == nullptr) return fail(NF4B_ERR_ARG, "null pointer");
+  if (vocab <= 0 || vocab > SAMPLER_MAX_VOCAB)
+    return fail(NF4B_ERR_SHAPE, "vocabulary %d outside [1, %d]", vocab, SAMPLER_MAX_VOCAB);
+  if (!(temperature >= 0.f) || !(top_p >= 0.f) || top_k < 1)
+    return fail(NF4B_ERR_ARG, "bad sampling parameters (temperature %g, top_p %g, top_k %d)", temperature, top_p,
+                top_k);
+  const size_t need = sampler_workspace_bytes(vocab);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(NF4B_ERR_WORKSPACE, "sampler workspace of %zu bytes needed, %zu given", need,
+                workspace ? workspace_bytes : (size_t)0);
+  if (!aligned(workspace, 256) || !aligned(logits, 2) || !aligned(out, 8))
+    return fail(NF4B_ERR_ALIGN, "workspace/logits/out misaligned");
+  int st = check_device();
+  if (st) return st;
+  return launch_status(launch_sampler(static_cast<const uint16_t*>(logits), vocab, temperature, top_p, top_k, seed,
+                                      step, out, workspace, reinterpret_cast<cudaStream_t>(stream)),
+                       "sampler launch");
+}
+
 extern "C" int nf4b_dequantize(const nf4b_weight* w, void* out, void* stream) {
   int st = check_weight(w);
   if (st) return st;

@@ -183,6 +183,19 @@ struct alignas(64) ChainParams {
 size_t chain_plan(ChainParams* p, int sm_count);
 cudaError_t launch_gemv_chain(const ChainParams& p, cudaStream_t stream);
 
+// ---- dense bf16 GEMV for the output heads (dense_gemv.cu) -----------------
+// k_in in {1024, 2048, 2560, 4096}; one activation row.
+cudaError_t launch_dense_gemv(const uint16_t* w, const uint16_t* x, uint16_t* y, int n_out, int k_in, int sms,
+                              cudaStream_t stream);
+
+// ---- fused top-k / top-p sampler (sampler.cu) -------------------------------
+// V <= 8192 * 2048 / 64 logits (the last CTA sorts <= 8192 slice winners).
+constexpr int SAMPLER_MAX_VOCAB = 262144;
+size_t sampler_workspace_bytes(int V);
+cudaError_t launch_sampler(const uint16_t* logits, int V, float temperature, float top_p, int top_k,
+                           unsigned long long seed, const int64_t* step, int64_t* out, void* workspace,
+                           cudaStream_t stream);
+
 // ---- dequantisation (nf4_dequant.cu) ---------------------------------------
 
 struct DequantParams {
