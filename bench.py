@@ -395,6 +395,59 @@ def detail(layers, io, ws, stream, device):
         del g
 
 
+def run_dualar(args, device, rank: int, world: int):
+    """BASELINE config 5 on this rank's GPU: a random-init Dual-AR model, a
+    512-token prompt prefilled, then `args.dualar_frames` frames replayed from
+    one captured CUDA graph (device-timed, max over ranks)."""
+    import torch
+
+    from ttspipe_b200.dualar import DualARConfig, DualARDecoder
+
+    t0 = time.time()
+    dec = DualARDecoder(DualARConfig(), device, seed=17 + rank)
+    g = torch.Generator().manual_seed(rank)
+    dec.prefill(torch.randint(0, dec.cfg.vocab, (512,), generator=g).to(device))
+    dec.capture()
+    build_s = time.time() - t0
+    for _ in range(3):
+        dec.replay()
+    torch.cuda.synchronize(device)
+    n = args.dualar_frames
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(device)
+    start.record()
+    for _ in range(n):
+        dec.replay()
+    end.record()
+    torch.cuda.synchronize(device)
+    barrier()
+    secs = max_over_ranks(start.elapsed_time(end) / 1e3, device)
+    per_layer = 52_159_552
+    kv = 36 * 2 * 8 * 128 * 2 * (512 + 3 + n / 2)                 # mean cache rows read per frame
+    wqkv = weight_bytes(6144, 2560)
+    # slow stack + LM head + fast prime (3 blocks and the last block's wqkv) +
+    # 9 fast steps x 4 blocks + their codebook heads + the slow KV reads
+    frame_bytes = (36 * per_layer + 2560 * 155136 * 2 + 3 * per_layer + wqkv + 36 * per_layer
+                   + 9 * 2560 * 4096 * 2 + kv)
+    peaks, kind = measured_peaks()
+    fps = n / secs
+    dec.release()
+    del dec
+    torch.cuda.empty_cache()
+    return {
+        "workload": "config 5: random-init NF4 Dual-AR (36 slow layers + bf16 LM head 2560x155136, 4 fast layers x 9 "
+                    "steps + 2560x4096 codebook heads), 512-token prompt, frames 516.., temperature 0.7, top-p 0.8, "
+                    "top-k 64, repetition-aware resample; one CUDA graph per frame",
+        "frames": n, "frames_per_s_per_replica": round(fps, 1), "frames_per_s": round(world * fps, 1),
+        "codebook_tokens_per_s": round(world * fps * 10, 1), "ms_per_frame": round(1e3 / fps, 3),
+        "bytes_per_frame": int(frame_bytes),
+        "roofline": {"bound": "hbm", "achieved_GBps": round(frame_bytes * fps / 1e9, 1), "peak": peaks["hbm_gbs"],
+                     "frac": round(frame_bytes * fps / 1e9 / float(peaks["hbm_gbs"]), 4), "peak_source": kind},
+        "setup_s": round(build_s, 1),
+    }
+
+
 def run_gpu(args):
     import torch
 
@@ -506,6 +559,10 @@ def run_gpu(args):
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     del graph
+    if args.dualar_frames > 0:
+        dual = run_dualar(args, device, rank, world)
+        if rank == 0:
+            result["dualar"] = dual
     import torch.distributed as dist
 
     if dist.is_initialized():
@@ -639,6 +696,8 @@ def main():
     ap.add_argument("--detail", action="store_true")
     ap.add_argument("--mode", default="decode", choices=sorted(MODES))
     ap.add_argument("--chain-layers", type=int, default=9, help="layers per nf4b_gemv_chain launch (--mode chain)")
+    ap.add_argument("--dualar-frames", type=int, default=128,
+                    help="Dual-AR frames timed after the GEMV step (config 5; 0: skip)")
     ap.add_argument("--prefetch-distance", type=int, default=0,
                     help="launches ahead whose weights each launch streams into L2 (0: none; "
                          "measured slower at 1-3 on B200, so off by default)")

@@ -1,0 +1,201 @@
+"""Dual-AR decode frame driver on the device.
+
+One frame is the reference's ``DecodeGraphs.decode`` + ``sample_frame``
+(app/engine/graphs.py:92-132, :205-217, :348-355), replayed as ONE captured
+CUDA graph with no host round trip:
+
+  slow AR: 36 decode blocks at the device-side position  (fusedlayer.decode_block)
+  final RMSNorm, bf16 LM head over the vocabulary         (heads.dense_linear)
+  main token: top-k / top-p sample; repetition-aware resample with a hotter
+  setting when the main token repeats within the window   (heads.sample)
+  fast AR prime at fast position 0 with the slow hidden state: every fast
+  block but the last, and the last block's q/k/v projection + rotary + KV
+  write only (its attention output feeds nothing: app/engine/graphs.py:76-89)
+  9 fast steps: codebook embedding -> 4 fast blocks -> norm -> codebook head
+  -> sample
+  next frame's input: semantic embedding + the frame's codebook embeddings;
+  position and draw counters advance on the device.
+
+The model is random-init NF4 with S2-Pro dimensions (the checkpoint is not
+available): weights N(0, 0.02), norm weights N(1, 0.1), embeddings N(0, 1)
+scaled by 0.02. The prompt is prefilled through the same blocks (GEMM path,
+the grouped attention of app/engine/fastpath.py:158-174).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import torch
+
+from ttspipe_b200 import _lib, fusedlayer, fusedops, heads, nf4gemv
+from ttspipe_b200.model import ModelArgs, precompute_freqs_cis, random_block
+
+
+@dataclass
+class DualARConfig:
+    slow: ModelArgs = field(default_factory=lambda: ModelArgs(n_layer=36, max_seq_len=2048))
+    n_fast_layer: int = 4
+    vocab: int = 155136
+    num_codebooks: int = 10
+    codebook_size: int = 4096
+    semantic_begin_id: int = 151040        # the codebook-0 tokens: [begin, begin + codebook_size)
+    temperature: float = 0.7
+    top_p: float = 0.8
+    top_k: int = 64
+    high_temperature: float = 1.0          # repetition-aware resample (app/engine/graphs.py:105-116)
+    high_top_p: float = 0.9
+    ras_window: int = 16
+
+
+class DualARDecoder:
+    """A random-init Dual-AR model on one GPU and its captured frame graph."""
+
+    def __init__(self, cfg: DualARConfig, device, seed: int = 0, n_slow: int | None = None):
+        if not (nf4gemv.available() and nf4gemv.install() and fusedlayer.install() and fusedops.install()):
+            raise RuntimeError("the sm_100a kernels are not available")
+        self.cfg, self.device, self.seed = cfg, torch.device(device), seed
+        sc = cfg.slow
+        n_slow = sc.n_layer if n_slow is None else n_slow
+        g = torch.Generator(device=self.device).manual_seed(seed)
+
+        def randn(*shape, std=0.02):
+            return (torch.randn(*shape, generator=g, device=self.device) * std).to(torch.bfloat16)
+
+        def norm_w():
+            return (1.0 + 0.1 * torch.randn(sc.dim, generator=g, device=self.device)).to(torch.bfloat16)
+
+        self.slow = [random_block(sc, device=self.device, seed=seed * 1000 + i) for i in range(n_slow)]
+        fast_args = ModelArgs(dim=sc.dim, n_head=sc.n_head, n_local_heads=sc.n_local_heads, head_dim=sc.head_dim,
+                              intermediate_size=sc.intermediate_size, max_seq_len=16, n_layer=cfg.n_fast_layer)
+        self.fast = [random_block(fast_args, device=self.device, seed=seed * 1000 + 500 + i)
+                     for i in range(cfg.n_fast_layer)]
+        for blk in self.slow + self.fast:
+            for lin in (blk.attention.wqkv, blk.attention.wo, blk.feed_forward.w1, blk.feed_forward.w3,
+                        blk.feed_forward.w2):
+                assert nf4gemv.prepare(lin)
+        self.norm_w, self.fast_norm_w = norm_w(), norm_w()
+        self.lm_head = randn(cfg.vocab, sc.dim)
+        self.cb_heads = [randn(cfg.codebook_size, sc.dim) for _ in range(cfg.num_codebooks)]
+        self.sem_emb = randn(cfg.vocab, sc.dim)
+        self.cb_emb = randn(cfg.num_codebooks, cfg.codebook_size, sc.dim)
+        self.fast_emb = randn(cfg.codebook_size, sc.dim)
+        self.freqs = precompute_freqs_cis(sc.max_seq_len, sc.head_dim, sc.rope_base, device=self.device)
+        self.fast_freqs = precompute_freqs_cis(16, sc.head_dim, sc.rope_base, device=self.device)
+        self.mask = torch.ones(1, 1, 1, sc.max_seq_len, dtype=torch.bool, device=self.device)
+        self.fast_mask = torch.ones(1, 1, 1, 16, dtype=torch.bool, device=self.device)
+        # device state of the frame loop
+        self.pos = torch.zeros(1, dtype=torch.long, device=self.device)
+        self.step = torch.zeros(1, dtype=torch.long, device=self.device)
+        self.fast_pos = [torch.full((1,), i, dtype=torch.long, device=self.device)
+                         for i in range(cfg.num_codebooks)]
+        self.draw = [torch.zeros(1, dtype=torch.long, device=self.device) for _ in range(cfg.num_codebooks + 1)]
+        self.x = torch.zeros(1, 1, sc.dim, dtype=torch.bfloat16, device=self.device)
+        self.tokens = torch.zeros(cfg.num_codebooks + 1, dtype=torch.long, device=self.device)
+        self.recent = torch.full((cfg.ras_window,), -1, dtype=torch.long, device=self.device)
+        self.graph = None
+
+    # ------------------------------------------------------------------ prompt
+    @torch.no_grad()
+    def prefill(self, prompt_ids: torch.Tensor) -> None:
+        """Run the prompt through the slow stack (filling its KV caches) and set
+        the first frame's input to the last prompt position's embedding."""
+        n = prompt_ids.numel()
+        sc = self.cfg.slow
+        x = self.sem_emb.index_select(0, prompt_ids.to(self.device)).view(1, n, sc.dim)
+        pos = torch.arange(n, device=self.device)
+        mask = torch.tril(torch.ones(n, sc.max_seq_len, dtype=torch.bool, device=self.device)).view(1, 1, n, -1)
+        freqs = self.freqs[:n]
+        for blk in self.slow:
+            x = blk(x, freqs, mask, pos)
+        self.x.copy_(self.sem_emb[prompt_ids[-1]].view(1, 1, -1))
+        self.pos.fill_(n)
+        self.step.zero_()
+
+    # ------------------------------------------------------------------ frame
+    def _fast_prime(self, hidden) -> None:
+        """Fast position 0 for its KV entries only: the last block's attention
+        output and feed-forward feed nothing, so only its q/k/v projection,
+        rotary and KV write run."""
+        x = hidden
+        for blk in self.fast[:-1]:
+            x = fusedlayer.decode_block(blk, x, self.fast_freqs, self.fast_mask, self.fast_pos[0])
+        last = self.fast[-1]
+        a = last.attention
+        xn = fusedops.rms_norm(x, last.attention_norm.weight, last.attention_norm.eps)
+        qkv = nf4gemv.matmul(a.wqkv, xn)
+        q = torch.empty(a.n_head * a.head_dim, dtype=torch.bfloat16, device=self.device)
+        st = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(_lib.lib().nf4b_qk_rope_kv(
+            qkv.data_ptr(), None, None, 1e-6, self.fast_freqs.data_ptr(), _lib.NF4B_BF16, self.fast_pos[0].data_ptr(),
+            q.data_ptr(), a.kv_cache.k_cache.data_ptr(), a.kv_cache.v_cache.data_ptr(), a.n_head, a.n_local_heads,
+            a.head_dim, a.kv_cache.k_cache.shape[2], st))
+
+    @torch.no_grad()
+    def frame(self) -> None:
+        """Issue one frame on the current stream (capturable)."""
+        cfg = self.cfg
+        x = self.x
+        for i, blk in enumerate(self.slow):
+            nxt = self.slow[i + 1] if i + 1 < len(self.slow) else None
+            x = fusedlayer.decode_block(blk, x, self.freqs, self.mask, self.pos, next_block=nxt)
+            assert x is not None, "a slow block fell back"
+        hidden = fusedops.rms_norm(x, self.norm_w, cfg.slow.norm_eps)
+        logits = heads.dense_linear(self.lm_head, hidden)
+        main = heads.sample(logits, temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k,
+                            seed=self.seed * 7919 + 1, step=self.step)
+        high = heads.sample(logits, temperature=cfg.high_temperature, top_p=cfg.high_top_p, top_k=cfg.top_k,
+                            seed=self.seed * 7919 + 2, step=self.step)
+        semantic = (main >= cfg.semantic_begin_id) & (main < cfg.semantic_begin_id + cfg.codebook_size)
+        repeat = (self.recent == main).any() & semantic
+        main = torch.where(repeat, high, main)
+        self.tokens[0:1].copy_(main)
+        self._fast_prime(hidden)
+        a = torch.clamp(main - cfg.semantic_begin_id, min=0, max=cfg.codebook_size - 1)
+        self.tokens[1:2].copy_(a)
+        h = self.fast_emb.index_select(0, a).view(1, 1, -1)
+        for i in range(1, cfg.num_codebooks):
+            y = h
+            for blk in self.fast:
+                y = fusedlayer.decode_block(blk, y, self.fast_freqs, self.fast_mask, self.fast_pos[i])
+                assert y is not None, "a fast block fell back"
+            yn = fusedops.rms_norm(y, self.fast_norm_w, cfg.slow.norm_eps)
+            logits_i = heads.dense_linear(self.cb_heads[i], yn)
+            a = heads.sample(logits_i, temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k,
+                             seed=self.seed * 7919 + 10 + i, step=self.step)
+            self.tokens[i + 1:i + 2].copy_(a)
+            h = self.fast_emb.index_select(0, a).view(1, 1, -1)
+        # next frame's input and counters
+        emb = self.sem_emb.index_select(0, self.tokens[0:1]).float()
+        codes = self.tokens[1:]
+        emb = emb + self.cb_emb[torch.arange(cfg.num_codebooks, device=self.device), codes].float().sum(0, keepdim=True)
+        self.x.copy_(emb.to(torch.bfloat16).view(1, 1, -1))
+        self.recent.copy_(torch.roll(self.recent, 1))
+        self.recent[0:1].copy_(self.tokens[0:1])
+        self.pos.add_(1)
+        self.step.add_(1)
+
+    def capture(self) -> None:
+        """Record one frame as a CUDA graph (state lives in device tensors)."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        saved = (self.pos.clone(), self.step.clone(), self.x.clone(), self.recent.clone())
+        with torch.cuda.stream(s):
+            self.frame()              # eager pass: sizes every workspace before capture
+            torch.cuda.synchronize(self.device)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=s):
+                self.frame()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        self.pos.copy_(saved[0])
+        self.step.copy_(saved[1])
+        self.x.copy_(saved[2])
+        self.recent.copy_(saved[3])
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+    def release(self) -> None:
+        self.graph = None
