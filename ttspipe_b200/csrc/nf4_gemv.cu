@@ -83,6 +83,23 @@ __device__ __forceinline__ int atomic_add_acq_rel(int* addr, int v) {
   return old;
 }
 
+// NF4 code point q (0..15) from immediates (a select tree): the tables below
+// are built without a constant-bank load, which misses in a fresh launch.
+__device__ __forceinline__ float nf4_code_imm(uint32_t q) {
+  const bool b0 = q & 1u, b1 = q & 2u, b2 = q & 4u, b3 = q & 8u;
+  const float l0 = b0 ? -0.6961928009986877f : -1.0f;
+  const float l1 = b0 ? -0.39491748809814453f : -0.5250730514526367f;
+  const float l2 = b0 ? -0.18477343022823334f : -0.28444138169288635f;
+  const float l3 = b0 ? 0.0f : -0.09105003625154495f;
+  const float l4 = b0 ? 0.16093020141124725f : 0.07958029955625534f;
+  const float l5 = b0 ? 0.33791524171829224f : 0.24611230194568634f;
+  const float l6 = b0 ? 0.5626170039176941f : 0.44070982933044434f;
+  const float l7 = b0 ? 1.0f : 0.7229568362236023f;
+  const float m0 = b1 ? l1 : l0, m1 = b1 ? l3 : l2, m2 = b1 ? l5 : l4, m3 = b1 ? l7 : l6;
+  const float n0 = b2 ? m1 : m0, n1 = b2 ? m3 : m2;
+  return b3 ? n1 : n0;
+}
+
 // Shared-memory tables: the NF4 pair table and (nested scales) code2. Entry
 // e's 32 per-lane copies are 128 contiguous bytes (stride 256), written eight
 // copies per 16-byte store.
@@ -91,7 +108,7 @@ template <int THREADS>
 __device__ __forceinline__ void build_pair_lut(uint8_t* smem) {
   for (int i = threadIdx.x; i < 256 * 8; i += THREADS) {
     const int e = i >> 3, part = i & 7;
-    const uint32_t v = pack_bf16x2(c_nf4_code[e >> 4], c_nf4_code[e & 15]);
+    const uint32_t v = pack_bf16x2(nf4_code_imm((uint32_t)e >> 4), nf4_code_imm((uint32_t)e & 15u));
     *reinterpret_cast<uint4*>(smem + e * 256 + part * 16) = make_uint4(v, v, v, v);
   }
 }
@@ -100,7 +117,7 @@ template <int THREADS = kThreads>
 __device__ __forceinline__ void build_tables(uint8_t* smem, const GemvParams& p) {
   for (int i = threadIdx.x; i < 256 * 8; i += THREADS) {
     const int e = i >> 3, part = i & 7;
-    const uint32_t v = pack_bf16x2(c_nf4_code[e >> 4], c_nf4_code[e & 15]);
+    const uint32_t v = pack_bf16x2(nf4_code_imm((uint32_t)e >> 4), nf4_code_imm((uint32_t)e & 15u));
     *reinterpret_cast<uint4*>(smem + e * 256 + part * 16) = make_uint4(v, v, v, v);
   }
   if (p.nested) {
@@ -166,21 +183,46 @@ __device__ __forceinline__ void prefetch_next(const GemvParams& p, int gw, int l
 // pair kernel: units of 16 rows x 128 codes, activation rows <= 4
 // ---------------------------------------------------------------------------
 
-// Sum of `n` partial slots (stride `stride` floats) in slot order, four loads
-// in flight at a time; the association is ((0 + s0) + s1) + ... whatever n is.
-__device__ __forceinline__ float sum_slots(const float* p, size_t stride, int n) {
-  float v = 0.f;
-  int c = 0;
-  for (; c + 4 <= n; c += 4) {
-    const float a = __ldcg(p + c * stride), b = __ldcg(p + (c + 1) * stride);
-    const float d = __ldcg(p + (c + 2) * stride), e = __ldcg(p + (c + 3) * stride);
-    v += a;
-    v += b;
-    v += d;
-    v += e;
+// Sums of the `n` partial slots (stride `stride` floats) of one split tile,
+// for rows ra and rb of each of the H halves (`base` = slot 0, half h at
+// + h * MN): v[h][e] = (((0 + s0) + s1) + ... + s(n-1)) + v[h][e], slot order
+// whatever n is. All loads of a chunk of CH slots are issued before the first
+// add, so a tile reduced over <= CH slots costs one L2 round trip.
+template <int H>
+__device__ __forceinline__ void sum_tile_slots(const float* base, size_t MN, size_t stride, int n, int ra, int rb,
+                                               int N, float (&v)[2][2]) {
+  constexpr int CH = 16 / H;
+  float acc[H][2];
+#pragma unroll
+  for (int h = 0; h < H; ++h) acc[h][0] = acc[h][1] = 0.f;
+  for (int c0 = 0; c0 < n; c0 += CH) {
+    float s[H][2][CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const bool live = c0 + c < n;
+      const float* q = base + (size_t)(c0 + c) * stride;
+#pragma unroll
+      for (int h = 0; h < H; ++h) {
+        s[h][0][c] = (live && ra < N) ? __ldcg(q + h * MN + ra) : 0.f;
+        s[h][1][c] = (live && rb < N) ? __ldcg(q + h * MN + rb) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      if (c0 + c < n) {
+#pragma unroll
+        for (int h = 0; h < H; ++h) {
+          acc[h][0] += s[h][0][c];
+          acc[h][1] += s[h][1][c];
+        }
+      }
+    }
   }
-  for (; c < n; ++c) v += __ldcg(p + c * stride);
-  return v;
+#pragma unroll
+  for (int h = 0; h < H; ++h) {
+    if (ra < N) v[h][0] = acc[h][0] + v[h][0];
+    if (rb < N) v[h][1] = acc[h][1] + v[h][1];
+  }
 }
 
 // The gate of a W1/W3 pair at the fork's rounding points:
@@ -355,14 +397,7 @@ __device__ __forceinline__ void reduce_pair_tile(const GemvParams& p, int rt, in
   const int N = p.N, M = p.M;
   const int ra = rt * 16 + g, rb = ra + 8;
   const size_t MN = (size_t)M * N;
-  if (t < M) {
-    const float* base = p.partial + (size_t)t * N;
-#pragma unroll
-    for (int h = 0; h < H; ++h) {
-      if (ra < N) v[h][0] = sum_slots(base + h * MN + ra, H * MN, others) + v[h][0];
-      if (rb < N) v[h][1] = sum_slots(base + h * MN + rb, H * MN, others) + v[h][1];
-    }
-  }
+  if (t < M) sum_tile_slots<H>(p.partial + (size_t)t * N, MN, H * MN, others, ra, rb, N, v);
   store_pair_tile<kGated>(p, rt, g, t, v);
 }
 
@@ -1261,10 +1296,10 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
         const size_t MN = (size_t)M * N;
         if (t < M) {
           const float* base = p.partial + (size_t)t * N;
-          for (int h = 0; h < H; ++h) {
-            if (ra < N) pend[h][0] = sum_slots(base + h * MN + ra, H * MN, others) + pend[h][0];
-            if (rb < N) pend[h][1] = sum_slots(base + h * MN + rb, H * MN, others) + pend[h][1];
-          }
+          if (H == 2)
+            sum_tile_slots<2>(base, MN, 2 * MN, others, ra, rb, N, pend);
+          else
+            sum_tile_slots<1>(base, MN, MN, others, ra, rb, N, pend);
         }
         chain_store_tile(J, M, rt, g, t, pend);
         __syncwarp();
