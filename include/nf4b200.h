@@ -104,6 +104,14 @@ typedef struct nf4b_gemm_opts {
    * waiting on HBM. Purely a hint: results do not depend on it. */
   const nf4b_weight* prefetch_next;
   const nf4b_weight* prefetch_next2;
+  /* Non-NULL: x is first RMS-normalised with this bf16 [k_in] weight and
+   * norm_eps inside the launch, with exactly the arithmetic of nf4b_rms_norm,
+   * and the matmul reads the normalised x (it is never written out): the
+   * reference's attention_norm / ffn_norm before wqkv / w1,w3 as one launch.
+   * Served when x fits the decode GEMV's shared-memory staging (1..4 rows,
+   * k_in % 128 == 0, rows * k_in * 2 <= 40 KB); NF4B_ERR_SHAPE otherwise. */
+  const void* norm_weight;
+  float norm_eps;
 } nf4b_gemm_opts;
 
 /* nf4b_gemm with options (opts may be NULL). */

@@ -17,6 +17,8 @@ import os
 LIB_PATH = Path(os.environ.get("NF4B_LIBRARY") or Path(__file__).resolve().parent / "libnf4b200.so")
 
 NF4B_OK = 0
+NF4B_ERR_ARG, NF4B_ERR_SHAPE, NF4B_ERR_ALIGN, NF4B_ERR_DTYPE = -1, -2, -3, -4
+NF4B_ERR_WORKSPACE, NF4B_ERR_LAUNCH, NF4B_ERR_DEVICE = -5, -6, -7
 NF4B_EPI_NONE, NF4B_EPI_RESIDUAL, NF4B_EPI_SILU_GATE = 0, 1, 2
 NF4B_F32, NF4B_F16, NF4B_BF16 = 0, 1, 2
 
@@ -79,7 +81,8 @@ class ChainJob(ctypes.Structure):
 class GemmOpts(ctypes.Structure):
     """`nf4b_gemm_opts`."""
 
-    _fields_ = [("prefetch_next", ctypes.POINTER(Nf4Weight)), ("prefetch_next2", ctypes.POINTER(Nf4Weight))]
+    _fields_ = [("prefetch_next", ctypes.POINTER(Nf4Weight)), ("prefetch_next2", ctypes.POINTER(Nf4Weight)),
+                ("norm_weight", ctypes.c_void_p), ("norm_eps", ctypes.c_float)]
 
 
 class Nf4bError(RuntimeError):

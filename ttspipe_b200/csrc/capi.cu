@@ -190,7 +190,7 @@ int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* 
     return fail(NF4B_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need,
                 workspace ? workspace_bytes : (size_t)0);
   if (!aligned(workspace, 256)) return fail(NF4B_ERR_ALIGN, "workspace is not 256-byte aligned");
-  GemvParams p;
+  GemvParams p = {};
   p.packed = w->packed;
   p.a8 = w->absmax_code;
   p.absmax = w->absmax;
@@ -204,6 +204,12 @@ int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* 
   p.gated = gated ? 1 : 0;
   p.su = su;
   p.x_staged = (pairs && (long long)rows * w->k_in * 2 <= GEMV_PAIR_X_MAX) ? 1 : 0;
+  p.norm_w = opts ? static_cast<const uint16_t*>(opts->norm_weight) : nullptr;
+  p.norm_eps = opts ? opts->norm_eps : 0.f;
+  if (p.norm_w != nullptr && !p.x_staged)
+    return fail(NF4B_ERR_SHAPE, "a fused RMSNorm needs x staged (1..4 rows, k_in %% 128 == 0, rows * k_in * 2 <= %d)",
+                GEMV_PAIR_X_MAX);
+  if (p.norm_w != nullptr && !aligned(p.norm_w, 2)) return fail(NF4B_ERR_ALIGN, "norm weight not 2-byte aligned");
   p.N = w->n_out;
   p.K = w->k_in;
   p.nested = w->nested ? 1 : 0;
@@ -268,6 +274,8 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
 
   if (rows <= GEMV_MAX_ROWS)
     return gemv_call(w, nullptr, x, y, rows, epi, operand, workspace, workspace_bytes, opts, s);
+  if (opts != nullptr && opts->norm_weight != nullptr)
+    return fail(NF4B_ERR_SHAPE, "a fused RMSNorm is served for 1..4 rows (got %d)", rows);
 
   GemmParams p;
   p.packed = w->packed;

@@ -94,6 +94,8 @@ struct alignas(64) GemvParams {
   int gated;
   int su;        // pair kernel: 128-code sub-units per unit (1 or 2)
   int x_staged;  // pair kernel: x is copied whole into shared memory first
+  const uint16_t* norm_w;  // pair kernel, staged x: RMS-normalise x with this weight first (or null)
+  float norm_eps;
   // Pair kernel: TMA maps of the packed weights (W, and W3 of a gated pair) as
   // [n_out rows, k_in / 2 bytes], boxes of 64 bytes x 16 rows.
   CUtensorMap wmap;

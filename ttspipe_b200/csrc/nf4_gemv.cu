@@ -233,6 +233,44 @@ __device__ __forceinline__ uint16_t gate_bf16(float v1, float v3) {
   return f2bf(__fmul_rn(s, round_bf(v3)));
 }
 
+__device__ __forceinline__ float rms_rsqrt(double ss, int width, float eps) {
+  const float t = __fadd_rn((float)(ss / (double)width), eps);
+  return (float)(1.0 / sqrt((double)t));
+}
+
+// RMS-normalise the M rows of K bf16 values staged at xr (shared memory) in
+// place with weight w, with the arithmetic of nf4b_rms_norm: fp64 sum of
+// squares (exact for bf16 inputs, so its order does not matter),
+// r = 1 / sqrt(fp32(ss / K) + eps), y = bf16(bf16(x * r) * w). Called by every
+// thread of the CTA after a barrier that made x visible; ends with a barrier.
+// `red` holds one double per warp.
+template <int THREADS>
+__device__ __forceinline__ void rms_normalise_staged(uint16_t* xr, int M, int K, const uint16_t* __restrict__ w,
+                                                     float eps, double* red) {
+  constexpr int NW = THREADS / 32;
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  for (int m = 0; m < M; ++m) {
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < K; i += THREADS) {
+      const double v = bf2f(xr[m * K + i]);
+      ss += v * v;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (lane == 0) red[wib] = ss;
+    __syncthreads();
+    double tot = 0.0;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) tot += red[k];
+    const float r = rms_rsqrt(tot, K, eps);
+    for (int i = threadIdx.x; i < K; i += THREADS) {
+      const float normed = round_bf(__fmul_rn(bf2f(xr[m * K + i]), r));
+      xr[m * K + i] = f2bf(__fmul_rn(normed, bf2f(__ldg(w + i))));
+    }
+    __syncthreads();
+  }
+}
+
 // cp.async helpers (sm_80+ asynchronous global -> shared copies, tracked per
 // thread in commit groups).
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
@@ -429,6 +467,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   static_assert(R >= 2, "ring too short");
   constexpr int kT = GEMV_PAIR_WARPS * 32;
   extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ double norm_red[GEMV_PAIR_WARPS];
   const uint8_t* lut = smem;
   const float* code2_s = reinterpret_cast<const float*>(smem + GEMV_LUT_BYTES);
   const float* code2_s3 = code2_s + 256;
@@ -571,6 +610,10 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   }
   cp_async_wait<R - 1>();  // this thread's code2 copy (R - 1 unit groups were committed after it)
   __syncthreads();         // the pair table, code2 and x are visible to every warp
+  // the fused RMSNorm (x is staged whenever it is requested)
+  if (p.norm_w != nullptr)
+    rms_normalise_staged<kT>(reinterpret_cast<uint16_t*>(smem + GEMV_PAIR_X_OFFSET), M, K, p.norm_w, p.norm_eps,
+                             norm_red);
 
   // x: column c of the MMA is (activation row c >> 1, block parity c & 1);
   // lane (g, t) supplies column g for codes of block parity t >> 1.
@@ -894,11 +937,6 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_block_kernel(const GemvP
 // adds one to its job's count (release). The last CTA out re-zeroes the
 // counts, so the workspace is left as it was found.
 
-__device__ __forceinline__ float rms_rsqrt(double ss, int width, float eps) {
-  const float t = __fadd_rn((float)(ss / (double)width), eps);
-  return (float)(1.0 / sqrt((double)t));
-}
-
 __device__ __forceinline__ void chain_store_tile(const ChainJob& J, int M, int rt, int g, int t,
                                                  const float (&v)[2][2]) {
   const int N = J.N;
@@ -1095,29 +1133,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       for (int i = threadIdx.x; i < n16; i += kT) dst[i] = __ldcg(src + i);
     }
     __syncthreads();
-    if (J.norm_w != nullptr) {
-      uint16_t* xr = reinterpret_cast<uint16_t*>(xs);
-      for (int m = 0; m < M; ++m) {
-        double ss = 0.0;
-        for (int i = threadIdx.x; i < K; i += kT) {
-          const double v = bf2f(xr[m * K + i]);
-          ss += v * v;
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-        if (lane == 0) red[wib] = ss;
-        __syncthreads();
-        double tot = 0.0;
-#pragma unroll
-        for (int w = 0; w < GEMV_PAIR_WARPS; ++w) tot += red[w];
-        const float r = rms_rsqrt(tot, K, J.norm_eps);
-        for (int i = threadIdx.x; i < K; i += kT) {
-          const float normed = round_bf(__fmul_rn(bf2f(xr[m * K + i]), r));
-          xr[m * K + i] = f2bf(__fmul_rn(normed, bf2f(__ldg(J.norm_w + i))));
-        }
-        __syncthreads();
-      }
-    }
+    if (J.norm_w != nullptr) rms_normalise_staged<kT>(reinterpret_cast<uint16_t*>(xs), M, K, J.norm_w, J.norm_eps, red);
 
     // ---- this warp's units of job j
     const int nblk = K >> 6;

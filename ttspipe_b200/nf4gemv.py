@@ -184,26 +184,46 @@ def prepare(module) -> bool:
     return True
 
 
-def _prefetch_opts(prefetch):
-    """`nf4b_gemm_opts` naming up to two prepared linears to stream into L2, or None."""
-    if prefetch is None:
-        return None
-    mods = list(prefetch) if isinstance(prefetch, (list, tuple)) else [prefetch]
-    descs = [m._nf4_fast["desc"] for m in mods[:2] if getattr(m, "_nf4_fast", None) is not None]
-    if not descs:
-        return None
-    opts = _lib.GemmOpts(*[ctypes.pointer(d) for d in descs])
-    return ctypes.byref(opts)
+#: Largest x (rows * in_features * 2 bytes) the decode GEMV stages in shared
+#: memory, and so the largest a fused RMSNorm serves.
+NORM_X_MAX = 40 * 1024
 
 
-def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None):
+def _norm_ok(norm, rows: int, K: int, device) -> bool:
+    """Whether `norm` = (weight, eps) can be fused into a decode GEMV of this shape."""
+    import torch
+
+    w = norm[0]
+    return (1 <= rows <= 4 and K % 128 == 0 and rows * K * 2 <= NORM_X_MAX and w.dtype == torch.bfloat16
+            and w.is_contiguous() and w.numel() == K and w.device == device)
+
+
+def _opts(prefetch=None, norm=None):
+    """`nf4b_gemm_opts`: up to two prepared linears to stream into L2 and a
+    fused RMSNorm (weight, eps) of x; None when neither is given."""
+    descs = []
+    if prefetch is not None:
+        mods = list(prefetch) if isinstance(prefetch, (list, tuple)) else [prefetch]
+        descs = [m._nf4_fast["desc"] for m in mods[:2] if getattr(m, "_nf4_fast", None) is not None]
+    if not descs and norm is None:
+        return None
+    ptrs = [ctypes.pointer(d) for d in descs] + [None] * (2 - len(descs))
+    nw, eps = (norm[0].data_ptr(), float(norm[1])) if norm is not None else (None, 0.0)
+    return ctypes.byref(_lib.GemmOpts(ptrs[0], ptrs[1], nw, eps))
+
+
+def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None, norm=None):
     """``x @ module.weight.T`` for any number of input rows, or None if not applicable.
 
     `epi` fuses ``operand + xW`` (EPI_RESIDUAL) or ``silu(operand) * xW``
     (EPI_SILU_GATE); `operand` has the output's shape, bf16, on x's device.
     `prefetch` (an extension; None in the reference's API) names one or two
     prepared linears that later calls will read: their weights are streamed
-    into L2 while this call runs. Launches on ``torch.cuda.current_stream()``.
+    into L2 while this call runs. `norm` (an extension) = (weight, eps):
+    ``rms_norm(x) @ W.T`` in the same launch, bit-exact to
+    ``fusedops.rms_norm`` then ``matmul``; served for 1..4 rows with
+    in_features % 128 == 0 and x within NORM_X_MAX bytes (None otherwise).
+    Launches on ``torch.cuda.current_stream()``.
     """
     import torch
 
@@ -223,6 +243,8 @@ def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None):
     rows = flat.shape[0]
     if rows == 0:
         return x.new_empty((*x.shape[:-1], N))
+    if norm is not None and not _norm_ok(norm, rows, K, x.device):
+        return None
     op_ptr = None
     if epi != EPI_NONE:
         if operand is None or operand.numel() != rows * N or operand.dtype != torch.bfloat16:
@@ -242,20 +264,20 @@ def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None):
         need = int(L.nf4b_gemm_workspace_size(ctypes.byref(desc), rows))
         ws = _workspace(x.device, need)
         ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
-    opts = _prefetch_opts(prefetch)
+    opts = _opts(prefetch, norm)
     _lib.check(L.nf4b_gemm_ex(ctypes.byref(desc), flat.data_ptr(), out.data_ptr(), rows, int(epi),
                               op_ptr, ws_ptr, ws_bytes, opts, ctypes.c_void_p(stream.cuda_stream)))
     _stats["fast"] += 1
     return out.view(*x.shape[:-1], N)
 
 
-def matmul_gated(w1, w3, x, *, prefetch=None):
+def matmul_gated(w1, w3, x, *, prefetch=None, norm=None):
     """``silu(x @ w1.weight.T) * (x @ w3.weight.T)`` in ONE launch, with the
     fork's rounding points (app/engine/fusedlayer.py:265-266: two ``matmul``
     launches there, the second with EPI_SILU_GATE); x W1^T is never written
     out. An extension of the reference's API. Serves 1..4 rows with
     in_features % 128 == 0; returns None otherwise (the caller then issues the
-    two matmuls) or if either linear is not prepared.
+    two matmuls) or if either linear is not prepared. `norm` as in ``matmul``.
     """
     import torch
 
@@ -273,6 +295,8 @@ def matmul_gated(w1, w3, x, *, prefetch=None):
     rows = flat.shape[0]
     if rows < 1 or rows > 4:
         return None
+    if norm is not None and not _norm_ok(norm, rows, K, x.device):
+        return None
     if not available():
         raise RuntimeError(f"nf4 kernels unavailable: {_unavailable}")
     L = _lib.lib()
@@ -281,7 +305,7 @@ def matmul_gated(w1, w3, x, *, prefetch=None):
     out = torch.empty((rows, N), dtype=torch.bfloat16, device=x.device)
     stream = torch.cuda.current_stream(x.device)
     _lib.check(L.nf4b_gemm_gated(ctypes.byref(f1["desc"]), ctypes.byref(f3["desc"]), flat.data_ptr(),
-                                 out.data_ptr(), rows, ws.data_ptr(), ws.numel(), _prefetch_opts(prefetch),
+                                 out.data_ptr(), rows, ws.data_ptr(), ws.numel(), _opts(prefetch, norm),
                                  ctypes.c_void_p(stream.cuda_stream)))
     _stats["fast"] += 1
     return out.view(*x.shape[:-1], N)
