@@ -503,7 +503,9 @@ def run_gpu(args):
     torch.cuda.synchronize(device)
 
     with ClockSampler([local] if world == 1 else list(range(world))) as clocks:
+        torch.cuda.profiler.start()   # bounds an `ncu --profile-from-start off` launch list to the timed steps
         secs = timed(step_graph, args.steps)
+        torch.cuda.profiler.stop()
     clock = clocks.summary()
     for _ in range(max(1, args.warmup)):
         step_e2e()

@@ -299,6 +299,20 @@ def test_decode_attention_by_position(length):
     assert orc.relative_error(orc.bf16_to_f32(to_bits(out)), orc.bf16_to_f32(want)) < ATTN_TOL
 
 
+@pytest.mark.parametrize("max_len,length", [(16, 1), (16, 5), (16, 16), (100, 64), (100, 65), (100, 100),
+                                            (300, 130), (300, 300)])
+def test_decode_attention_short_windows(max_len, length):
+    """Windows of 1..4 chunks: one CTA per KV head, or clusters of 2..5."""
+    nh, nkv = 32, 8
+    k, v = _cache(nkv, max_len, seed=max_len + length)
+    q = randn_bf16((nh, 128), seed=length + 3, device="cuda")
+    out = torch.empty((nh, 128), dtype=torch.bfloat16, device="cuda")
+    pos = torch.tensor([length - 1], dtype=torch.long, device="cuda")
+    fastpath.kernel_attention(q, k, v, out, n_head=nh, n_kv=nkv, pos=pos, window=max_len, max_len=max_len)
+    want = orc.attention(to_bits(q), to_bits(k), to_bits(v), length, nh, nkv)
+    assert orc.relative_error(orc.bf16_to_f32(to_bits(out)), orc.bf16_to_f32(want)) < ATTN_TOL
+
+
 @pytest.mark.parametrize("kv_len", [1, 10, 17, 401, 2048])
 def test_decode_attention_api_matches_the_oracle(kv_len):
     """fastpath.decode_attention's signature (tests/test_nf4gemv.py:224-242)."""

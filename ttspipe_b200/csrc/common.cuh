@@ -116,6 +116,18 @@ __device__ __forceinline__ void lut_dequant8(const ScaledLut& t, uint32_t w, uin
 
 // Epilogue applied to one fp32 accumulator: the matmul output is rounded to
 // bf16 first, then the fused op rounds again where the unfused model does.
+// The epilogue with the operand value already loaded (ignored for NF4B_EPI_NONE).
+__device__ __forceinline__ bf16_t epilogue_value(float acc, int epi, float opv) {
+  const float y = round_bf(acc);
+  if (epi == NF4B_EPI_RESIDUAL) {
+    return f2bf(__fadd_rn(opv, y));
+  } else if (epi == NF4B_EPI_SILU_GATE) {
+    const float s = round_bf(__fdiv_rn(opv, __fadd_rn(1.0f, expf(-opv))));
+    return f2bf(__fmul_rn(s, y));
+  }
+  return f2bf(y);
+}
+
 __device__ __forceinline__ bf16_t epilogue(float acc, int epi, const bf16_t* operand, size_t idx) {
   const float y = round_bf(acc);
   if (epi == NF4B_EPI_RESIDUAL) {

@@ -584,7 +584,9 @@ cudaError_t launch_cluster_attention(const uint16_t* q, const uint16_t* kc, cons
                                      const uint8_t* mask, uint16_t* out, int nh, int nkv, int max_len, int window,
                                      cudaStream_t stream) {
   // Clusters of 8 (the portable size): measured as fast as 16 at 2048 rows
-  // and faster below. chosen: 0 unknown, 1 launches, -1 cannot be resident.
+  // and faster below; fewer when the window has fewer 64-row chunks (a
+  // window of one chunk - the fast AR's - runs one CTA per KV head, no
+  // cross-CTA merge). chosen: 0 unknown, 1 launches, -1 cannot be resident.
   static int chosen[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -592,7 +594,8 @@ cudaError_t launch_cluster_attention(const uint16_t* q, const uint16_t* kc, cons
   const int idx = (dev >= 0 && dev < 64) ? dev : 0;
   if (chosen[idx] < 0) return cudaErrorNotSupported;
   {
-    const int C = 8;
+    const int chunks = (window + ATTN_CHUNK - 1) / ATTN_CHUNK;
+    const int C = chunks < 8 ? (chunks < 1 ? 1 : chunks) : 8;
     const bool check = chosen[idx] == 0;
     cudaError_t e;
     switch (groups) {

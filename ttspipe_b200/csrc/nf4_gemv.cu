@@ -361,17 +361,17 @@ __device__ __forceinline__ void store_pair_tile(const GemvParams& p, int rt, int
 }
 
 // Finish row tile `rt` of the pair kernel from this warp's partial sums
-// v[half][row g / g + 8]. A tile inside the warp's run is stored at once.
-// A split tile is reduced by the warp owning its last unit; the others each
-// publish their partial in their own workspace slot, count themselves in with
-// a release increment and move on (no round trip). Returns true when this
-// warp is the reducer: it then finishes the tile later with reduce_pair_tile,
-// after the rest of its run, by when its contributors (the warps before it,
-// whose runs end in this tile) are done too. Each warp reduces at most one
-// tile: the one its run starts in.
+// v[half][row g / g + 8]. A tile inside the warp's run is stored at once
+// (returns false). A split tile is published as soon as the warp's part of it
+// is done: the partial goes to this warp's slot (slot = warp - first
+// contributing warp) and lane 0 counts the warp in with an acquire-release
+// atomic whose result (`old`, lane 0) is only looked at after the warp's run,
+// by finish_split_tile: no warp waits for another, and the last to arrive
+// reduces (returns true). (Publishing every split tile only after the run was
+// measured slower: the first tile's reduction then no longer overlaps the run.)
 template <bool kGated>
-__device__ __forceinline__ bool finish_pair_tile(const GemvParams& p, int rt, int u0, int u1, int gw, int g,
-                                                 int t, int lane, const float (&v)[2][2]) {
+__device__ __forceinline__ bool publish_pair_tile(const GemvParams& p, int rt, int u0, int u1, int gw, int g,
+                                                  int t, int lane, const float (&v)[2][2], int& old) {
   constexpr int H = kGated ? 2 : 1;
   const int per_tile = p.blocks_per_tile * H;
   const int t0 = rt * per_tile, t1 = t0 + per_tile - 1;
@@ -379,8 +379,7 @@ __device__ __forceinline__ bool finish_pair_tile(const GemvParams& p, int rt, in
     store_pair_tile<kGated>(p, rt, g, t, v);
     return false;
   }
-  const int w_lo = warp_of(t0, p.uq, p.ur), w_hi = warp_of(t1, p.uq, p.ur);
-  if (gw == w_hi) return true;
+  const int w_lo = warp_of(t0, p.uq, p.ur);
   const int N = p.N, M = p.M;
   const int ra = rt * 16 + g, rb = ra + 8;
   const size_t MN = (size_t)M * N;
@@ -394,49 +393,40 @@ __device__ __forceinline__ bool finish_pair_tile(const GemvParams& p, int rt, in
   }
   // The warp barrier orders every lane's partial before lane 0's release.
   __syncwarp();
-  if (lane == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.counters + rt) : "memory");
-  return false;
+  if (lane == 0) old = atomic_add_acq_rel(p.counters + rt, 1);
+  return true;
 }
 
-// The reducer's half of a split tile: wait (bounded) for the other
-// contributors, sum their slots in slot order and its own partial last
-// (deterministic), re-zero the counter, store.
+// After the warp's run: if it was the last of split tile rt's contributors to
+// arrive, sum every slot in slot order, (((0 + s0) + s1) + ...), and store -
+// the residual or gate operand is fetched in the same round trip as the
+// slots - then re-zero the counter for the next launch.
 template <bool kGated>
-__device__ __forceinline__ void reduce_pair_tile(const GemvParams& p, int rt, int gw, int g, int t, int lane,
-                                                 float (&v)[2][2]) {
+__device__ __forceinline__ void finish_split_tile(const GemvParams& p, int rt, int old, int g, int t, int lane) {
   constexpr int H = kGated ? 2 : 1;
   const int per_tile = p.blocks_per_tile * H;
   const int t0 = rt * per_tile;
-  const int others = gw - warp_of(t0, p.uq, p.ur);
-  int* ctr = p.counters + rt;
-  int ok = 1;
-  if (lane == 0) {
-    unsigned long long start = 0;
-    for (uint32_t i = 0;; ++i) {
-      int seen;
-      asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(ctr) : "memory");
-      if (seen == others) break;
-      if ((i & 15u) == 0u) {
-        const unsigned long long now = gemv_globaltimer();
-        if (i == 0) {
-          start = now;
-        } else if (now - start > 2000000000ull) {
-          atomicOr(&g_gemv_error, 2);
-          ok = 0;
-          break;
-        }
-      }
-    }
-    *ctr = 0;
-  }
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();  // lane 0's acquire orders every lane's reads of the slots
-  if (!ok) return;
+  const int n = warp_of(t0 + per_tile - 1, p.uq, p.ur) - warp_of(t0, p.uq, p.ur) + 1;
+  old = __shfl_sync(0xffffffffu, old, 0);  // lane 0's acquire; the shuffle orders the lanes' reads after it
+  if (old != n - 1) return;
   const int N = p.N, M = p.M;
   const int ra = rt * 16 + g, rb = ra + 8;
   const size_t MN = (size_t)M * N;
-  if (t < M) sum_tile_slots<H>(p.partial + (size_t)t * N, MN, H * MN, others, ra, rb, N, v);
-  store_pair_tile<kGated>(p, rt, g, t, v);
+  if (lane == 0) p.counters[rt] = 0;
+  if (t >= M) return;
+  const size_t oa = (size_t)t * N + ra, ob = (size_t)t * N + rb;
+  const bool opnd = !kGated && p.epi != NF4B_EPI_NONE;
+  const uint16_t opa = (opnd && ra < N) ? __ldcg(p.operand + oa) : (uint16_t)0;
+  const uint16_t opb = (opnd && rb < N) ? __ldcg(p.operand + ob) : (uint16_t)0;
+  float v[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+  sum_tile_slots<H>(p.partial + (size_t)t * N, MN, H * MN, n, ra, rb, N, v);
+  if (kGated) {
+    if (ra < N) p.y[oa] = gate_bf16(v[0][0], v[1][0]);
+    if (rb < N) p.y[ob] = gate_bf16(v[0][1], v[1][1]);
+  } else {
+    if (ra < N) p.y[oa] = epilogue_value(v[0][0], p.epi, bf2f(opa));
+    if (rb < N) p.y[ob] = epilogue_value(v[0][1], p.epi, bf2f(opb));
+  }
 }
 
 // Pair kernel. A unit is 16 weight rows x SU * 128 codes (SU = 2 for
@@ -626,8 +616,8 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
 
   float acc_a = 0.f, acc_b = 0.f;    // W (or W1): rows g, g+8 for activation row t
   float acc3_a = 0.f, acc3_b = 0.f;  // gated pair: W3
-  int pend_rt = -1;                  // the split tile this warp reduces, after its run
-  float pend[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+  // split tiles this warp published (at most two: its run's first and last)
+  int split_a = -1, split_b = -1, old_a = 0, old_b = 0;
   int st_use = 0, st_fill = R - 1;
   uint32_t phase = 0;  // bit s: parity of stage s's next completion
   for (int u = u0; u < u1; ++u) {
@@ -755,14 +745,21 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     }
     if ((kb == B - 1 && (!kGated || hh == 1)) || u == u1 - 1) {
       const float v[2][2] = {{acc_a, acc_b}, {acc3_a, acc3_b}};
-      if (finish_pair_tile<kGated>(p, rt, u0, u1, gw, g, t, lane, v)) {
-        pend_rt = rt;
-        pend[0][0] = acc_a; pend[0][1] = acc_b; pend[1][0] = acc3_a; pend[1][1] = acc3_b;
+      int old = 0;
+      if (publish_pair_tile<kGated>(p, rt, u0, u1, gw, g, t, lane, v, old)) {
+        if (split_a < 0) {
+          split_a = rt;
+          old_a = old;
+        } else {
+          split_b = rt;
+          old_b = old;
+        }
       }
       acc_a = acc_b = acc3_a = acc3_b = 0.f;
     }
   }
-  if (pend_rt >= 0) reduce_pair_tile<kGated>(p, pend_rt, gw, g, t, lane, pend);
+  if (split_a >= 0) finish_split_tile<kGated>(p, split_a, old_a, g, t, lane);
+  if (split_b >= 0) finish_split_tile<kGated>(p, split_b, old_b, g, t, lane);
   cp_async_wait<0>();
   if (!NF4B_GEMV_PREFETCH_EARLY) prefetch_next(p, gw, lane);
 }
@@ -1248,8 +1245,10 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
         acc[0][1] += yb;
       }
       if ((kb == B - 1 && (!J.gated || hh == 1)) || u == u1 - 1) {
-        // finish row tile rt (see finish_pair_tile; here every stored tile also
-        // counts toward the job's completion)
+        // finish row tile rt: stored at once when it lies inside this warp's
+        // run; a split tile is reduced by the warp owning its last unit, after
+        // that warp's run, once the others have published their partials.
+        // Every stored tile counts toward the job's completion.
         const int H = J.gated ? 2 : 1;
         const int t0 = rt * per_tile, t1 = t0 + per_tile - 1;
         if (t0 >= u0 && t1 < u1) {
@@ -1280,7 +1279,8 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       }
     }
     if (pend_rt >= 0 && s_ok) {
-      // this warp reduces the split tile its run started in (see reduce_pair_tile)
+      // this warp reduces the split tile its run started in: bounded wait for
+      // the earlier contributors, then their slots in slot order and its own last
       const int H = J.gated ? 2 : 1;
       const int rt = pend_rt;
       const int others = gw - warp_of(rt * per_tile, J.uq, J.ur);

@@ -8,13 +8,16 @@
 //   divide the kept logits by max(temperature, 1e-5), softmax over them,
 //   draw one.
 //
-// One launch. CTA s sorts a 2048-logit slice (bitonic network on 64-bit
-// (value, index) keys: larger value first, then smaller index), publishes its
-// 64 best keys and its (max, sum of exp) for the full-vocabulary softmax; the
-// last CTA (atomic counter, reset after use) sorts the slices' winners and
-// draws. The draw is inverse-CDF with one uniform from a counter-based hash
-// of (seed, *step) - the same distribution as the fork's exponential race,
-// reproducible from the seed.
+// One launch. CTA s takes a 2048-logit slice: each of its 32 warps sorts 64
+// (value, index) keys (larger value first, then smaller index) in registers,
+// and the warps' lists are merged pairwise - the top 64 of two sorted lists
+// is max(A[i], B[63 - i]), a bitonic sequence, then a 6-stage bitonic merge -
+// down to the slice's 64 best, published with the slice's (max, sum of exp)
+// for the full-vocabulary softmax. The last CTA (atomic counter, reset after
+// use) merges the slices' lists the same way and draws. The draw is
+// inverse-CDF with one uniform from a counter-based hash of (seed, *step) -
+// the same distribution as the fork's exponential race, reproducible from the
+// seed.
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -26,6 +29,8 @@ namespace {
 constexpr int kSlice = 2048;
 constexpr int kSThreads = 1024;
 constexpr int kTop = 64;
+constexpr int kMaxSlices = (SAMPLER_MAX_VOCAB + kSlice - 1) / kSlice;
+static_assert(kSThreads == 32 * 32 && kSlice == 64 * 32, "one 64-key list per warp, 32 warps");
 
 __device__ __forceinline__ unsigned long long make_key(float v, uint32_t idx) {
   uint32_t b = __float_as_uint(v);
@@ -39,24 +44,88 @@ __device__ __forceinline__ float key_value(unsigned long long k) {
 }
 __device__ __forceinline__ uint32_t key_index(unsigned long long k) { return 0xFFFFFFFFu - (uint32_t)k; }
 
-// Descending bitonic sort of n (power of two) keys in shared memory.
-__device__ void bitonic_desc(unsigned long long* a, int n) {
-  for (int size = 2; size <= n; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      __syncthreads();
-      for (int i = threadIdx.x; i < n / 2; i += blockDim.x) {
-        const int lo = 2 * i - (i & (stride - 1));
-        const int hi = lo + stride;
-        const bool desc = ((lo & size) == 0);
-        const unsigned long long x = a[lo], y = a[hi];
-        if ((x < y) == desc) {
-          a[lo] = y;
-          a[hi] = x;
-        }
+// A sorted (descending) list of 64 keys held by one warp: lane l holds
+// L[l] in x0 and L[l + 32] in x1.
+__device__ __forceinline__ unsigned long long kmax(unsigned long long a, unsigned long long b) { return a > b ? a : b; }
+__device__ __forceinline__ unsigned long long kmin(unsigned long long a, unsigned long long b) { return a < b ? a : b; }
+
+// Sort 64 arbitrary keys into that layout (bitonic network; strides below 32
+// between lanes, stride 32 within a lane).
+__device__ __forceinline__ void warp_sort64(unsigned long long& x0, unsigned long long& x1, int lane) {
+#pragma unroll
+  for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j == 32) {  // k == 64: element i against i + 32, descending
+        const unsigned long long hi = kmax(x0, x1), lo = kmin(x0, x1);
+        x0 = hi;
+        x1 = lo;
+        continue;
       }
+      const bool lower = (lane & j) == 0;
+      const bool d0 = (lane & k) == 0, d1 = ((lane + 32) & k) == 0;  // block of element i sorted descending?
+      const unsigned long long p0 = __shfl_xor_sync(0xffffffffu, x0, j);
+      const unsigned long long p1 = __shfl_xor_sync(0xffffffffu, x1, j);
+      x0 = (lower == d0) ? kmax(x0, p0) : kmin(x0, p0);
+      x1 = (lower == d1) ? kmax(x1, p1) : kmin(x1, p1);
+    }
+  }
+}
+
+// (a0, a1) <- the top 64 of the sorted lists A = (a0, a1) and B = (b0, b1), sorted.
+__device__ __forceinline__ void warp_merge64(unsigned long long& a0, unsigned long long& a1, unsigned long long b0,
+                                             unsigned long long b1, int lane) {
+  const unsigned long long r0 = __shfl_sync(0xffffffffu, b1, 31 - lane);  // B[63 - lane]
+  const unsigned long long r1 = __shfl_sync(0xffffffffu, b0, 31 - lane);  // B[31 - lane]
+  unsigned long long c0 = kmax(a0, r0), c1 = kmax(a1, r1);              // bitonic
+  const unsigned long long hi = kmax(c0, c1), lo = kmin(c0, c1);
+  c0 = hi;
+  c1 = lo;
+#pragma unroll
+  for (int j = 16; j > 0; j >>= 1) {
+    const bool lower = (lane & j) == 0;
+    const unsigned long long p0 = __shfl_xor_sync(0xffffffffu, c0, j);
+    const unsigned long long p1 = __shfl_xor_sync(0xffffffffu, c1, j);
+    c0 = lower ? kmax(c0, p0) : kmin(c0, p0);
+    c1 = lower ? kmax(c1, p1) : kmin(c1, p1);
+  }
+  a0 = c0;
+  a1 = c1;
+}
+
+// Merge the 32 warps' lists (registers) down to warp 0's; lists[32][64] is
+// shared scratch. Leaves the result in lists[0] too. Every thread calls it.
+__device__ __forceinline__ void block_merge(unsigned long long (*lists)[kTop], unsigned long long& x0,
+                                            unsigned long long& x1, int warp, int lane) {
+  lists[warp][lane] = x0;
+  lists[warp][lane + 32] = x1;
+#pragma unroll
+  for (int lvl = 1; lvl < 32; lvl <<= 1) {
+    __syncthreads();
+    if ((warp & (2 * lvl - 1)) == 0) {
+      warp_merge64(x0, x1, lists[warp + lvl][lane], lists[warp + lvl][lane + 32], lane);
+      lists[warp][lane] = x0;
+      lists[warp][lane + 32] = x1;
     }
   }
   __syncthreads();
+}
+
+// Inclusive prefix sum across the warp's lanes.
+__device__ __forceinline__ float warp_scan(float v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
+// The first position set in the 64-bit mask (lo: positions 0-31, hi: 32-63), or `none`.
+__device__ __forceinline__ int first_set(uint32_t lo, uint32_t hi, int none) {
+  if (lo) return __ffs(lo) - 1;
+  if (hi) return 32 + __ffs(hi) - 1;
+  return none;
 }
 
 __device__ __forceinline__ unsigned long long splitmix64(unsigned long long z) {
@@ -71,41 +140,36 @@ __global__ void __launch_bounds__(kSThreads) sample_kernel(const uint16_t* __res
                                                            unsigned long long seed, const int64_t* __restrict__ step,
                                                            int64_t* __restrict__ out, unsigned long long* __restrict__ ws_keys,
                                                            float* __restrict__ ws_stats, int* __restrict__ counter) {
-  extern __shared__ __align__(16) unsigned long long keys[];
+  __shared__ unsigned long long lists[kSThreads / 32][kTop];
   __shared__ float red_m[kSThreads / 32], red_s[kSThreads / 32];
+  __shared__ float sm_max[kMaxSlices], sm_term[kMaxSlices];
   __shared__ int last;
   pdl_wait();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int s = blockIdx.x, S = gridDim.x;
   const int base = s * kSlice;
-  // this slice's keys and its max / sum of exp
-  float m = -INFINITY;
-  for (int i = tid; i < kSlice; i += kSThreads) {
-    const int j = base + i;
-    if (j < V) {
-      const float v = bf2f(logits[j]);
-      keys[i] = make_key(v, (uint32_t)j);
-      m = fmaxf(m, v);
-    } else {
-      keys[i] = 0ull;  // below every real key
-    }
-  }
+  // this slice's keys (64 per warp, sorted in registers) and its max / sum of exp
+  const int j0 = base + warp * 64 + lane, j1 = j0 + 32;
+  const float v0 = j0 < V ? bf2f(logits[j0]) : -INFINITY, v1 = j1 < V ? bf2f(logits[j1]) : -INFINITY;
+  unsigned long long x0 = j0 < V ? make_key(v0, (uint32_t)j0) : 0ull;  // 0: below every real key
+  unsigned long long x1 = j1 < V ? make_key(v1, (uint32_t)j1) : 0ull;
+  float m = fmaxf(v0, v1);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
   if (lane == 0) red_m[warp] = m;
+  warp_sort64(x0, x1, lane);
   __syncthreads();
   m = -INFINITY;
   for (int w = 0; w < kSThreads / 32; ++w) m = fmaxf(m, red_m[w]);
-  float sum = 0.f;
-  for (int i = tid; i < kSlice; i += kSThreads) {
-    const int j = base + i;
-    if (j < V) sum += expf(bf2f(logits[j]) - m);
-  }
+  float sum = expf(v0 - m) + expf(v1 - m);  // exp(-inf) = 0 past the vocabulary
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
   if (lane == 0) red_s[warp] = sum;
-  bitonic_desc(keys, kSlice);
-  if (tid < kTop) ws_keys[(size_t)s * kTop + tid] = keys[tid];
+  block_merge(lists, x0, x1, warp, lane);
+  if (warp == 0) {
+    ws_keys[(size_t)s * kTop + lane] = x0;
+    ws_keys[(size_t)s * kTop + lane + 32] = x1;
+  }
   if (tid == 0) {
     float t = 0.f;
     for (int w = 0; w < kSThreads / 32; ++w) t += red_s[w];  // fixed order
@@ -126,43 +190,47 @@ __global__ void __launch_bounds__(kSThreads) sample_kernel(const uint16_t* __res
   }
   __threadfence();
   // ---- the last CTA: global top keys, full-vocabulary softmax statistics, draw
-  int P = kTop;
-  while (P < S * kTop) P <<= 1;
-  for (int i = tid; i < P; i += kSThreads) keys[i] = i < S * kTop ? __ldcg(ws_keys + i) : 0ull;
-  bitonic_desc(keys, P);
-  if (tid == 0) {
+  x0 = x1 = 0ull;
+  for (int c = warp; c < S; c += kSThreads / 32) {
+    const unsigned long long b0 = __ldcg(ws_keys + (size_t)c * kTop + lane);
+    const unsigned long long b1 = __ldcg(ws_keys + (size_t)c * kTop + lane + 32);
+    warp_merge64(x0, x1, b0, b1, lane);
+  }
+  for (int c = tid; c < S; c += kSThreads) sm_max[c] = __ldcg(ws_stats + 2 * c);
+  block_merge(lists, x0, x1, warp, lane);  // its barriers also publish sm_max
+  const unsigned long long* keys = lists[0];
+  if (warp == 0) {
     float M = -INFINITY;
-    for (int c = 0; c < S; ++c) M = fmaxf(M, __ldcg(ws_stats + 2 * c));
+    for (int c = lane; c < S; c += 32) M = fmaxf(M, sm_max[c]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    for (int c = lane; c < S; c += 32) sm_term[c] = __ldcg(ws_stats + 2 * c + 1) * expf(sm_max[c] - M);
+    __syncwarp();
     float Z = 0.f;
-    for (int c = 0; c < S; ++c) Z += __ldcg(ws_stats + 2 * c + 1) * expf(__ldcg(ws_stats + 2 * c) - M);
+    for (int c = 0; c < S; ++c) Z += sm_term[c];  // slice order (every lane, same value)
     const int kk = top_k < kTop ? (top_k < 1 ? 1 : top_k) : kTop;
     const int n = kk < V ? kk : V;
     const float inv_t = 1.0f / fmaxf(temperature, 1e-5f);
-    // kept positions: a prefix of the sorted list (cumsum is increasing)
-    float cum = 0.f;
-    int keep = 0;
-    for (int i = 0; i < n; ++i) {
-      cum += expf(key_value(keys[i]) - M) / Z;
-      if (i > 0 && cum > top_p) break;
-      keep = i + 1;
-    }
+    const float kv0 = key_value(keys[lane]), kv1 = key_value(keys[lane + 32]);
+    // kept positions: i = 0, then up to the first i with cumsum(p)[i] > top_p
+    const float p0 = lane < n ? expf(kv0 - M) / Z : 0.f, p1 = lane + 32 < n ? expf(kv1 - M) / Z : 0.f;
+    const float c0 = warp_scan(p0, lane);
+    const float c1 = warp_scan(p1, lane) + __shfl_sync(0xffffffffu, c0, 31);
+    const int keep = first_set(__ballot_sync(0xffffffffu, lane >= 1 && lane < n && c0 > top_p),
+                               __ballot_sync(0xffffffffu, lane + 32 < n && c1 > top_p), n);
     // softmax of the kept logits / temperature, then the inverse-CDF draw
     const float m0 = key_value(keys[0]) * inv_t;
-    float tot = 0.f;
-    for (int i = 0; i < keep; ++i) tot += expf(key_value(keys[i]) * inv_t - m0);
+    const float q0 = lane < keep ? expf(kv0 * inv_t - m0) : 0.f;
+    const float q1 = lane + 32 < keep ? expf(kv1 * inv_t - m0) : 0.f;
+    const float a0 = warp_scan(q0, lane);
+    const float a1 = warp_scan(q1, lane) + __shfl_sync(0xffffffffu, a0, 31);
+    const float tot = __shfl_sync(0xffffffffu, a1, 31);
     const unsigned long long st = step != nullptr ? (unsigned long long)step[0] : 0ull;
     const float u = (float)(splitmix64(seed ^ (st * 0xD1B54A32D192ED03ull)) >> 40) * (1.0f / 16777216.0f);
     const float target = u * tot;
-    float acc = 0.f;
-    int pick = keep - 1;
-    for (int i = 0; i < keep; ++i) {
-      acc += expf(key_value(keys[i]) * inv_t - m0);
-      if (acc > target) {
-        pick = i;
-        break;
-      }
-    }
-    out[0] = (int64_t)key_index(keys[pick]);
+    const int pick = first_set(__ballot_sync(0xffffffffu, lane < keep && a0 > target),
+                               __ballot_sync(0xffffffffu, lane + 32 < keep && a1 > target), keep - 1);
+    if (lane == 0) out[0] = (int64_t)key_index(keys[pick]);
   }
   pdl_launch_dependents();
 }
@@ -178,24 +246,13 @@ cudaError_t launch_sampler(const uint16_t* logits, int V, float temperature, flo
                            unsigned long long seed, const int64_t* step, int64_t* out, void* workspace,
                            cudaStream_t stream) {
   const int S = (V + kSlice - 1) / kSlice;
-  int P = kTop;
-  while (P < S * kTop) P <<= 1;
-  const int smem = (P > kSlice ? P : kSlice) * 8;
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
   int* counter = static_cast<int*>(workspace);
   unsigned long long* keys = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(workspace) + 256);
   float* stats = reinterpret_cast<float*>(keys + (size_t)S * kTop);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(S);
   cfg.blockDim = dim3(kSThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -9,7 +9,9 @@ prints CUDA-event timings (never under a profiler).
 
 kernels: gemv (M rows <= 32), gated (the W1/W3 gate, M <= 4), gemm (tcgen05, M > 32), attention (decode,
 qk_rope_kv + split-KV attention at a given cache length), prefill (the seven
-S2-Pro projections at M rows through the GEMM, TFLOP/s).
+S2-Pro projections at M rows through the GEMM, TFLOP/s), dualar (the config-5
+frame graph: `--frames` replays between cudaProfilerStart/Stop, for an
+`ncu --profile-from-start off` launch list; with --time, ms per frame).
 """
 
 from __future__ import annotations
@@ -141,9 +143,38 @@ def run_attention(length: int, launches: int, timed: bool) -> None:
     torch.cuda.synchronize()
 
 
+def run_dualar(frames: int, timed: bool) -> None:
+    """The Dual-AR frame graph (random-init model, 512-token prompt, 3 warm replays)."""
+    from ttspipe_b200.dualar import DualARConfig, DualARDecoder
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    dec = DualARDecoder(DualARConfig(), dev, seed=17)
+    g = torch.Generator().manual_seed(0)
+    dec.prefill(torch.randint(0, dec.cfg.vocab, (512,), generator=g).to(dev))
+    dec.capture()
+    for _ in range(3):
+        dec.replay()
+    torch.cuda.synchronize()
+    if timed:
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        for _ in range(frames):
+            dec.replay()
+        en.record()
+        torch.cuda.synchronize()
+        print(f"dual-AR frame: {st.elapsed_time(en) / frames:.3f} ms")
+    else:
+        torch.cuda.profiler.start()
+        for _ in range(frames):
+            dec.replay()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+    dec.release()
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemv", "gated", "gemm", "attention", "prefill"])
+    ap.add_argument("kernel", choices=["gemv", "gated", "gemm", "attention", "prefill", "dualar"])
     ap.add_argument("--n", type=int, default=9728)
     ap.add_argument("--k", type=int, default=2560)
     ap.add_argument("--rows", type=int, default=1)
@@ -152,6 +183,7 @@ def main(argv=None) -> None:
     ap.add_argument("--plain", action="store_true", help="fp32 absmax instead of double quant")
     ap.add_argument("--length", type=int, default=2048)
     ap.add_argument("--time", action="store_true", help="time from a CUDA graph instead")
+    ap.add_argument("--frames", type=int, default=2, help="dualar: frames replayed")
     a = ap.parse_args(argv)
     from ttspipe_b200 import nf4gemv
 
@@ -163,6 +195,8 @@ def main(argv=None) -> None:
         run_prefill(a.rows)
     elif a.kernel == "gated":
         run_gated(a.n, a.k, a.rows, a.copies, a.launches, a.time)
+    elif a.kernel == "dualar":
+        run_dualar(a.frames, a.time)
     else:
         run_attention(a.length, a.launches, a.time)
     print("ok", file=sys.stderr)
