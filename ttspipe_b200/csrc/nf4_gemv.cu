@@ -317,27 +317,27 @@ __device__ __forceinline__ void tma_box(uint32_t dst, const CUtensorMap* map, in
       : "memory");
 }
 // Bounded wait for phase `parity` of `bar` (2 s by %globaltimer); false after
-// recording the timeout in g_gemv_error.
+// recording the timeout in g_gemv_error. The clock is read only once the
+// first probe finds the phase incomplete.
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-  unsigned long long start = 0;
-  for (uint32_t i = 0;; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if ((i & 63u) == 0u) {
-      const unsigned long long now = gemv_globaltimer();
-      if (i == 0) {
-        start = now;
-      } else if (now - start > 2000000000ull) {
-        atomicOr(&g_gemv_error, 1);
-        return false;
-      }
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long start = gemv_globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 63u) == 0u && gemv_globaltimer() - start > 2000000000ull) {
+      atomicOr(&g_gemv_error, 1);
+      return false;
     }
   }
 }
