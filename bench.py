@@ -675,7 +675,9 @@ def run_reference(args):
     el = time.perf_counter() - t0
     step_bytes = n_layers * LAYER_BYTES
     value = step_bytes * args.steps / el / 1e9
-    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": 1, "impl": "reference",
+    # n_gpus: the N of the run this line stands beside (the reference's NF4 path is
+    # CPU-only: rank 0 times it on the host cores, the GPUs stay idle)
+    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus, "impl": "reference",
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random packed NF4 bytes, bf16 absmax, x N(0,1))",
