@@ -10,7 +10,9 @@ from __future__ import annotations
 import pytest
 import torch
 
-from ttspipe_b200 import nf4gemv
+from oracle import nf4_oracle as orc
+from tests.helpers import to_bits
+from ttspipe_b200 import model, nf4gemv
 from ttspipe_b200.dualar import DualARConfig, DualARDecoder
 
 pytestmark = pytest.mark.gpu
@@ -76,3 +78,38 @@ def test_tokens_are_in_range_and_frames_differ(decoder):
         assert 0 <= int(t[0]) < cfg.vocab
         assert bool(((t[1:] >= 0) & (t[1:] < cfg.codebook_size)).all())
     assert len({tuple(t.tolist()) for t in frames}) > 1
+
+
+def test_slow_stack_matches_the_reference_blocks_at_the_frame_position(decoder):
+    """The frame's fused slow stack at device position p equals the model's own
+    block forward (separate norm / wqkv / rotary / KV write / attention / wo /
+    norm / w1, w3 / w2 launches) fed freqs_cis[p], the reference's convention:
+    q and k are rotated for p, not for position 0."""
+    dec = decoder
+    snap = snapshot(dec)
+    torch.cuda.synchronize()
+    p = int(dec.pos.item())
+    assert p > 0
+    fused = dec.slow_stack(dec.x.clone())
+    torch.cuda.synchronize()
+    restore(dec, snap)
+    forward = getattr(model.TransformerBlock, "_fused_original_forward", model.TransformerBlock.forward)
+    x = dec.x.clone()
+    ip = torch.tensor([p], dtype=torch.long, device="cuda")
+    mask = torch.zeros_like(dec.mask)
+    mask[..., :p + 1] = True  # causal row of position p, as the reference's model builds it
+    for blk in dec.slow:
+        x = forward(blk, x, dec.freqs[p:p + 1], mask, ip)
+    torch.cuda.synchronize()
+    restore(dec, snap)
+    got, want = orc.bf16_to_f32(to_bits(fused)), orc.bf16_to_f32(to_bits(x))
+    err = orc.rms_relative_max_error(got, want)
+    assert err < 2e-2
+    # and the position matters: position 0's rotation lands measurably further away
+    x0 = dec.x.clone()
+    for blk in dec.slow:
+        x0 = forward(blk, x0, dec.freqs[0:1], mask, ip)
+    torch.cuda.synchronize()
+    restore(dec, snap)
+    err0 = orc.rms_relative_max_error(orc.bf16_to_f32(to_bits(x0)), want)
+    assert err0 > max(5 * err, 1e-4), (err, err0)

@@ -120,7 +120,7 @@ class DualARDecoder:
         rotary and KV write run."""
         x = hidden
         for blk in self.fast[:-1]:
-            x = fusedlayer.decode_block(blk, x, self.fast_freqs, self.fast_mask, self.fast_pos[0])
+            x = fusedlayer.decode_block(blk, x, self.fast_freqs[0:1], self.fast_mask, self.fast_pos[0])
         last = self.fast[-1]
         a = last.attention
         xn = fusedops.rms_norm(x, last.attention_norm.weight, last.attention_norm.eps)
@@ -133,14 +133,23 @@ class DualARDecoder:
             a.head_dim, a.kv_cache.k_cache.shape[2], st))
 
     @torch.no_grad()
+    def slow_stack(self, x):
+        """The slow blocks at the device-side position `self.pos` (capturable):
+        the rotary row is gathered on the device, so a replayed graph rotates
+        q and k for the position of the frame it runs, the way the
+        reference's model indexes ``freqs_cis[input_pos]`` before its layers."""
+        fr = self.freqs.index_select(0, self.pos)
+        for i, blk in enumerate(self.slow):
+            nxt = self.slow[i + 1] if i + 1 < len(self.slow) else None
+            x = fusedlayer.decode_block(blk, x, fr, self.mask, self.pos, next_block=nxt)
+            assert x is not None, "a slow block fell back"
+        return x
+
+    @torch.no_grad()
     def frame(self) -> None:
         """Issue one frame on the current stream (capturable)."""
         cfg = self.cfg
-        x = self.x
-        for i, blk in enumerate(self.slow):
-            nxt = self.slow[i + 1] if i + 1 < len(self.slow) else None
-            x = fusedlayer.decode_block(blk, x, self.freqs, self.mask, self.pos, next_block=nxt)
-            assert x is not None, "a slow block fell back"
+        x = self.slow_stack(self.x)
         hidden = fusedops.rms_norm(x, self.norm_w, cfg.slow.norm_eps)
         logits = heads.dense_linear(self.lm_head, hidden)
         main = heads.sample(logits, temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k,
@@ -158,7 +167,7 @@ class DualARDecoder:
         for i in range(1, cfg.num_codebooks):
             y = h
             for blk in self.fast:
-                y = fusedlayer.decode_block(blk, y, self.fast_freqs, self.fast_mask, self.fast_pos[i])
+                y = fusedlayer.decode_block(blk, y, self.fast_freqs[i:i + 1], self.fast_mask, self.fast_pos[i])
                 assert y is not None, "a fast block fell back"
             yn = fusedops.rms_norm(y, self.fast_norm_w, cfg.slow.norm_eps)
             logits_i = heads.dense_linear(self.cb_heads[i], yn)
