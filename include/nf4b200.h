@@ -269,6 +269,23 @@ int nf4b_decode_attention(const void* q, const void* k_cache, const void* v_cach
 
 size_t nf4b_decode_attention_workspace_size(int n_head, int head_dim, int window);
 
+/*
+ * nf4b_qk_rope_kv then nf4b_decode_attention (pos given, no mask) in ONE
+ * launch: the attention kernel reads q, k, v straight from the wqkv output,
+ * applies the q/k norm and rotary with nf4b_qk_rope_kv's arithmetic, writes
+ * the new k, v rows to the caches at *pos and attends over rows
+ * [0, min(*pos + 1, window)) - the reference's qk_rope_kv + attn_partial +
+ * attn_combine (app/engine/fusedlayer.py:56-157) as one call, results equal to
+ * the two separate calls. Where the device cannot make the attention cluster
+ * resident it issues the two calls, using q_scratch (n_head * head_dim bf16)
+ * for the rotated q. Arguments as those two functions; workspace as
+ * nf4b_decode_attention. No reference counterpart as a single call.
+ */
+int nf4b_qkv_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                       const void* freqs, int freqs_dtype, const int64_t* pos, void* q_scratch,
+                       void* k_cache, void* v_cache, void* out, int n_head, int n_kv, int head_dim, int max_len,
+                       int window, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

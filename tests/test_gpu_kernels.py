@@ -372,3 +372,44 @@ def test_prefill_attention_uses_the_grouped_formulation():
     want = orc.attention_masked(to_bits(q)[0], to_bits(k)[0], to_bits(v)[0],
                                 mask[0, 0].cpu().numpy(), nh, nkv)
     assert orc.relative_error(orc.bf16_to_f32(to_bits(y)[0]), orc.bf16_to_f32(want)) < ATTN_TOL
+
+
+# --------------------------------------------------------------------------
+# q/k norm + rotary + KV write fused into the attention launch
+# --------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("max_len,pos", [(2048, 0), (2048, 5), (2048, 63), (2048, 64), (2048, 700), (16, 0),
+                                         (16, 9), (16, 15)])
+@pytest.mark.parametrize("qk_norm", [False, True])
+@pytest.mark.parametrize("fdtype", [torch.bfloat16, torch.float32])
+def test_qkv_attention_equals_qk_rope_kv_then_attention(max_len, pos, qk_norm, fdtype):
+    from ttspipe_b200 import _lib, model
+
+    nh, nkv = 32, 8
+    ftype = {torch.bfloat16: _lib.NF4B_BF16, torch.float32: _lib.NF4B_F32}[fdtype]
+    qkv = randn_bf16(((nh + 2 * nkv) * 128,), seed=pos + 11, device="cuda")
+    k0, v0 = _cache(nkv, max_len, seed=pos + 12)
+    freqs = model.precompute_freqs_cis(max_len, 128, 1e6, device="cuda").to(fdtype)[pos:pos + 1].contiguous()
+    g = torch.Generator().manual_seed(pos)
+    qw = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16).cuda() if qk_norm else None
+    kw = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16).cuda() if qk_norm else None
+    p = torch.tensor([pos], dtype=torch.long, device="cuda")
+    # separate launches
+    k1, v1 = k0.clone(), v0.clone()
+    q = torch.empty(nh * 128, dtype=torch.bfloat16, device="cuda")
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _lib.check(_lib.lib().nf4b_qk_rope_kv(
+        qkv.data_ptr(), None if qw is None else qw.data_ptr(), None if kw is None else kw.data_ptr(), 1e-6,
+        freqs.data_ptr(), ftype, p.data_ptr(), q.data_ptr(), k1.data_ptr(), v1.data_ptr(), nh, nkv, 128, max_len, st))
+    want = torch.empty((nh, 128), dtype=torch.bfloat16, device="cuda")
+    fastpath.kernel_attention(q.view(nh, 128), k1, v1, want, n_head=nh, n_kv=nkv, pos=p, window=max_len,
+                              max_len=max_len)
+    # one launch
+    k2, v2 = k0.clone(), v0.clone()
+    got = torch.empty((nh, 128), dtype=torch.bfloat16, device="cuda")
+    fastpath.qkv_attention(qkv, k2, v2, got, n_head=nh, n_kv=nkv, pos=p, window=max_len, max_len=max_len,
+                           freqs=freqs, freqs_dtype=ftype, q_norm_w=qw, k_norm_w=kw, eps=1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(k2, k1) and torch.equal(v2, v1)
+    assert torch.equal(got, want)

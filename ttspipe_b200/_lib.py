@@ -43,6 +43,7 @@ EXPORTS = (
     "nf4b_qk_rope_kv",
     "nf4b_decode_attention",
     "nf4b_decode_attention_workspace_size",
+    "nf4b_qkv_attention",
 )
 
 
@@ -120,6 +121,8 @@ def _declare(lib) -> None:
         "nf4b_qk_rope_kv": (i32, [vp, vp, vp, f32, vp, i32, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
         "nf4b_decode_attention": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, sz, vp]),
         "nf4b_decode_attention_workspace_size": (sz, [i32, i32, i32]),
+        "nf4b_qkv_attention": (i32, [vp, vp, vp, f32, vp, i32, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, sz,
+                                     vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

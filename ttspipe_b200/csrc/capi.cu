@@ -564,4 +564,48 @@ int nf4b_decode_attention(const void* q, const void* k_cache, const void* v_cach
       "decode attention launch");
 }
 
+int nf4b_qkv_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                       const void* freqs, int freqs_dtype, const int64_t* pos, void* q_scratch,
+                       void* k_cache, void* v_cache, void* out, int n_head, int n_kv, int head_dim, int max_len,
+                       int window, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!qkv || !freqs || !pos || !q_scratch || !k_cache || !v_cache || !out) return fail(NF4B_ERR_ARG, "null pointer");
+  if (head_dim != 128) return fail(NF4B_ERR_SHAPE, "head_dim must be 128 (got %d)", head_dim);
+  if (n_head <= 0 || n_kv <= 0 || n_head % n_kv)
+    return fail(NF4B_ERR_SHAPE, "n_head %d is not a multiple of n_kv %d", n_head, n_kv);
+  if ((size_t)n_kv * sizeof(int) > ATTN_COUNTER_BYTES)
+    return fail(NF4B_ERR_SHAPE, "more than %zu KV heads", ATTN_COUNTER_BYTES / sizeof(int));
+  const int groups = n_head / n_kv;
+  if (groups != 1 && groups != 2 && groups != 4 && groups != 8)
+    return fail(NF4B_ERR_SHAPE, "query groups of %d are not served (1, 2, 4 or 8)", groups);
+  if (window <= 0 || window > max_len) return fail(NF4B_ERR_SHAPE, "window %d outside [1, %d]", window, max_len);
+  if ((q_norm_w == nullptr) != (k_norm_w == nullptr))
+    return fail(NF4B_ERR_ARG, "q and k norm weights must both be given or both be null");
+  if (freqs_dtype < NF4B_F32 || freqs_dtype > NF4B_BF16)
+    return fail(NF4B_ERR_DTYPE, "unknown freqs dtype %d", freqs_dtype);
+  if (!aligned(q_scratch, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16))
+    return fail(NF4B_ERR_ALIGN, "q scratch / caches not 16-byte aligned");
+  AttnPlan plan;
+  attn_plan(n_head, head_dim, window, &plan);
+  const size_t need = plan.counter_bytes + plan.partial_bytes;
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(NF4B_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
+  if (!aligned(workspace, 256)) return fail(NF4B_ERR_ALIGN, "workspace is not 256-byte aligned");
+  int st = check_device();
+  if (st) return st;
+  QkvIn in;
+  in.qkv = static_cast<const uint16_t*>(qkv);
+  in.qw = static_cast<const uint16_t*>(q_norm_w);
+  in.kw = static_cast<const uint16_t*>(k_norm_w);
+  in.eps = eps;
+  in.freqs = freqs;
+  in.ftype = freqs_dtype;
+  in.n_head = n_head;
+  float* partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.counter_bytes);
+  return launch_status(
+      launch_qkv_attention(in, pos, static_cast<uint16_t*>(q_scratch), static_cast<uint16_t*>(k_cache),
+                           static_cast<uint16_t*>(v_cache), static_cast<uint16_t*>(out), n_head, n_kv, max_len,
+                           window, partial, static_cast<int*>(workspace), reinterpret_cast<cudaStream_t>(stream)),
+      "qkv attention launch");
+}
+
 }  // extern "C"

@@ -116,6 +116,20 @@ __device__ __forceinline__ void lut_dequant8(const ScaledLut& t, uint32_t w, uin
 
 // Epilogue applied to one fp32 accumulator: the matmul output is rounded to
 // bf16 first, then the fused op rounds again where the unfused model does.
+// Element i of a rotary table of dtype NF4B_F32 / NF4B_F16 / NF4B_BF16.
+__device__ __forceinline__ float load_freq(const void* f, long long i, int ftype) {
+  if (ftype == NF4B_F32) return reinterpret_cast<const float*>(f)[i];
+  if (ftype == NF4B_F16) return __half2float(reinterpret_cast<const __half*>(f)[i]);
+  return bf2f(reinterpret_cast<const bf16_t*>(f)[i]);
+}
+
+// RMSNorm's scale from an fp64 sum of squares: the correctly rounded fp32
+// 1 / sqrt(fp32(ss / width) + eps).
+__device__ __forceinline__ float rsqrt_exact(double ss, int width, float eps) {
+  const float t = __fadd_rn((float)(ss / (double)width), eps);
+  return (float)(1.0 / sqrt((double)t));
+}
+
 // The epilogue with the operand value already loaded (ignored for NF4B_EPI_NONE).
 __device__ __forceinline__ bf16_t epilogue_value(float acc, int epi, float opv) {
   const float y = round_bf(acc);

@@ -293,6 +293,10 @@ struct ClusterSmem {
   float alpha[G];
   float run_m[G], run_l[G];
   unsigned long long bar[2];
+  // the fused q/k norm + rotary prologue (QkvIn)
+  float sx[2][kD];
+  double nred[kCThreads / 32];
+  uint16_t knew[kD], vnew[kD];
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -316,11 +320,47 @@ __device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t ran
   return v;
 }
 
+// One 128-wide row per half-CTA (threads 0-127: half 0, 128-255: half 1)
+// with qk_rope_kv's arithmetic: RMSNorm with this half's weight w (none when
+// null) - fp64 sum of squares, reduced exactly as block_sum over 4 warps -
+// then the rotary pair (x0 c - x1 s, x1 c + x0 s) at the freqs row when
+// `rope`. Every thread calls it (uniform barriers); `any_norm` is uniform.
+template <int G>
+__device__ __forceinline__ float norm_rope_half(ClusterSmem<G>& sm, float x, bool has_w, float wd, bool rope,
+                                                bool any_norm, float eps, float c, float sn) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int d = tid & (kD - 1), half = tid >> 7;
+  if (any_norm) {
+    double sq = has_w ? (double)x * (double)x : 0.0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+    if (lane == 0) sm.nred[warp] = sq;
+    __syncthreads();
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ss += sm.nred[4 * half + i];
+    if (has_w) {
+      const float r = rsqrt_exact(ss, kD, eps);
+      x = round_bf(__fmul_rn(__fmul_rn(x, r), wd));
+    }
+    __syncthreads();
+  }
+  sm.sx[half][d] = x;
+  __syncthreads();
+  float y = x;
+  if (rope) {
+    const float x0 = sm.sx[half][d & ~1], x1 = sm.sx[half][d | 1];
+    y = (d & 1) ? __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)) : __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+  }
+  __syncthreads();
+  return y;
+}
+
 template <int G>
 __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
     const bf16_t* __restrict__ q, const bf16_t* __restrict__ kc, const bf16_t* __restrict__ vc,
     const int64_t* __restrict__ pos_ptr, const uint8_t* __restrict__ mask, bf16_t* __restrict__ out,
-    int max_len, int window, float scale) {
+    int max_len, int window, float scale, const QkvIn in) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   ClusterSmem<G>& sm = *reinterpret_cast<ClusterSmem<G>*>(smem_raw);
   const int kh = blockIdx.x;
@@ -363,7 +403,43 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     for (int ci = 0; ci < 2 && ci < my_chunks; ++ci) issue(ci);
   }
-  for (int i = tid; i < G * kD; i += kCThreads) sm.q[i / kD][i % kD] = bf2f(q[(size_t)kh * G * kD + i]);
+  const bool fused = in.qkv != nullptr;  // q/k/v from the wqkv output (pos given, no mask)
+  const long long p_new = fused ? pos_ptr[0] : -1;
+  if (!fused) {
+    for (int i = tid; i < G * kD; i += kCThreads) sm.q[i / kD][i % kD] = bf2f(q[(size_t)kh * G * kD + i]);
+  } else {
+    // This KV head's query heads, two per pass, then k (half 0) and v (half 1):
+    // the arithmetic of qk_rope_kv. The new rows reach the cache through rank 0;
+    // the CTA whose chunk holds row p_new patches them into its shared copy.
+    const int d = tid & (kD - 1), half = tid >> 7;
+    const bf16_t* qkv = in.qkv;
+    const bool norm = in.qw != nullptr;  // q and k norm weights come together
+    // every global load first (one round trip), then the passes
+    constexpr int P = (G + 1) / 2;
+    float xq[P];
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      const int h = 2 * i + half;
+      xq[i] = h < G ? bf2f(qkv[(size_t)(kh * G + h) * kD + d]) : 0.f;
+    }
+    const int nkv = (int)gridDim.x;
+    const float xkv = bf2f(qkv[(size_t)(in.n_head + (half ? nkv : 0) + kh) * kD + d]);
+    const float c = load_freq(in.freqs, d & ~1, in.ftype), sn = load_freq(in.freqs, d | 1, in.ftype);
+    const float qwd = norm ? bf2f(in.qw[d]) : 0.f, kwd = norm ? bf2f(in.kw[d]) : 0.f;
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      const int h = 2 * i + half;
+      const float y = norm_rope_half<G>(sm, xq[i], norm, qwd, true, norm, in.eps, c, sn);
+      if (h < G) sm.q[h][d] = bf2f(f2bf(y));
+    }
+    const float y = norm_rope_half<G>(sm, xkv, norm && half == 0, kwd, half == 0, norm, in.eps, c, sn);
+    const bf16_t nb = f2bf(y);
+    (half ? sm.vnew : sm.knew)[d] = nb;
+    if (rank == 0 && p_new < max_len) {
+      bf16_t* cache = const_cast<bf16_t*>(half ? vc : kc);
+      cache[((size_t)kh * max_len + p_new) * kD + d] = nb;
+    }
+  }
   if (tid < G) {
     sm.run_m[tid] = -INFINITY;
     sm.run_l[tid] = 0.f;
@@ -381,6 +457,12 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
     ok = ok && wait_bar_parity(sm_u32(&sm.bar[ci & 1]), (uint32_t)(ci >> 1) & 1u);
     const long long j0 = r0 + (long long)ci * ATTN_CHUNK;
     const int rows = (int)((r1 - j0 < ATTN_CHUNK) ? r1 - j0 : ATTN_CHUNK);
+    if (fused && p_new >= j0 && p_new < j0 + rows) {
+      // the copy may predate rank 0's store of the new row: use the computed one
+      const int d = tid & (kD - 1), half = tid >> 7;
+      sm.kv[ci & 1][half][(int)(p_new - j0) * kD + d] = (half ? sm.vnew : sm.knew)[d];
+      __syncthreads();
+    }
     const uint16_t* ks = sm.kv[ci & 1][0];
     const uint16_t* vs = sm.kv[ci & 1][1];
     // Scores: a warp takes 8 rows, four at a time, eight lanes per row.
@@ -542,7 +624,7 @@ namespace {
 template <int G>
 cudaError_t launch_cluster_g(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int64_t* pos,
                              const uint8_t* mask, uint16_t* out, int nkv, int max_len, int window, int C,
-                             bool check, cudaStream_t stream) {
+                             bool check, const QkvIn& in, cudaStream_t stream) {
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -575,14 +657,14 @@ cudaError_t launch_cluster_g(const uint16_t* q, const uint16_t* kc, const uint16
   }
   const float scale = 1.0f / sqrtf((float)kD);
   return cudaLaunchKernelEx(&cfg, decode_attention_cluster_kernel<G>, (const bf16_t*)q, (const bf16_t*)kc,
-                            (const bf16_t*)vc, pos, mask, (bf16_t*)out, max_len, window, scale);
+                            (const bf16_t*)vc, pos, mask, (bf16_t*)out, max_len, window, scale, in);
 }
 
 }  // namespace
 
 cudaError_t launch_cluster_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int64_t* pos,
                                      const uint8_t* mask, uint16_t* out, int nh, int nkv, int max_len, int window,
-                                     cudaStream_t stream) {
+                                     cudaStream_t stream, const QkvIn& in) {
   // Clusters of 8 (the portable size): measured as fast as 16 at 2048 rows
   // and faster below; fewer when the window has fewer 64-row chunks (a
   // window of one chunk - the fast AR's - runs one CTA per KV head, no
@@ -599,10 +681,10 @@ cudaError_t launch_cluster_attention(const uint16_t* q, const uint16_t* kc, cons
     const bool check = chosen[idx] == 0;
     cudaError_t e;
     switch (groups) {
-      case 1: e = launch_cluster_g<1>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, stream); break;
-      case 2: e = launch_cluster_g<2>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, stream); break;
-      case 4: e = launch_cluster_g<4>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, stream); break;
-      case 8: e = launch_cluster_g<8>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, stream); break;
+      case 1: e = launch_cluster_g<1>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream); break;
+      case 2: e = launch_cluster_g<2>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream); break;
+      case 4: e = launch_cluster_g<4>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream); break;
+      case 8: e = launch_cluster_g<8>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream); break;
       default: return cudaErrorInvalidValue;
     }
     if (e == cudaSuccess) {
@@ -624,7 +706,8 @@ cudaError_t launch_decode_attention(const uint16_t* q, const uint16_t* kc, const
   {
     // One cluster of 8 CTAs per KV head; the split-KV kernel below if the
     // device cannot make such a cluster resident.
-    cudaError_t e = launch_cluster_attention(q, kc, vc, pos, mask, out, nh, nkv, max_len, window, stream);
+    const QkvIn none = {};
+    cudaError_t e = launch_cluster_attention(q, kc, vc, pos, mask, out, nh, nkv, max_len, window, stream, none);
     if (e == cudaSuccess) return e;
     (void)cudaGetLastError();
   }
@@ -665,6 +748,19 @@ cudaError_t launch_decode_attention(const uint16_t* q, const uint16_t* kc, const
       return cudaErrorInvalidValue;
   }
 #undef NF4B_ATTN_CASE
+}
+
+cudaError_t launch_qkv_attention(const QkvIn& in, const int64_t* pos, uint16_t* q_scratch, uint16_t* kc,
+                                 uint16_t* vc, uint16_t* out, int nh, int nkv, int max_len, int window,
+                                 float* partial, int* counters, cudaStream_t stream) {
+  cudaError_t e = launch_cluster_attention(nullptr, kc, vc, pos, nullptr, out, nh, nkv, max_len, window, stream, in);
+  if (e == cudaSuccess) return e;
+  (void)cudaGetLastError();
+  e = launch_qk_rope_kv(in.qkv, in.qw, in.kw, in.eps, in.freqs, in.ftype, pos, q_scratch, kc, vc, nh, nkv, max_len,
+                        stream);
+  if (e != cudaSuccess) return e;
+  return launch_decode_attention(q_scratch, kc, vc, pos, nullptr, out, nh, nkv, max_len, window, partial, counters,
+                                 stream);
 }
 
 }  // namespace nf4b

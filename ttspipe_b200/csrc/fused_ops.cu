@@ -16,17 +16,6 @@ namespace nf4b {
 
 namespace {
 
-__device__ __forceinline__ float load_freq(const void* f, long long i, int ftype) {
-  if (ftype == NF4B_F32) return reinterpret_cast<const float*>(f)[i];
-  if (ftype == NF4B_F16) return __half2float(reinterpret_cast<const __half*>(f)[i]);
-  return bf2f(reinterpret_cast<const bf16_t*>(f)[i]);
-}
-
-__device__ __forceinline__ float rsqrt_exact(double ss, int width, float eps) {
-  const float t = __fadd_rn((float)(ss / (double)width), eps);
-  return (float)(1.0 / sqrt((double)t));
-}
-
 template <int THREADS>
 __device__ __forceinline__ double block_sum(double v, double* red) {
 #pragma unroll

@@ -259,12 +259,29 @@ struct AttnPlan {
 void attn_plan(int n_head, int head_dim, int window, AttnPlan* plan);
 // One thread-block cluster of 8 CTAs per KV head; cudaErrorNotSupported when
 // such a cluster cannot be resident on the device.
+struct QkvIn;
 cudaError_t launch_cluster_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int64_t* pos,
                                      const uint8_t* mask, uint16_t* out, int nh, int nkv, int max_len, int window,
-                                     cudaStream_t stream);
+                                     cudaStream_t stream, const QkvIn& in);
 cudaError_t launch_decode_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
                                     const int64_t* pos, const uint8_t* mask, uint16_t* out, int nh, int nkv,
                                     int max_len, int window, float* partial, int* counters,
                                     cudaStream_t stream);
+// The decode step's q/k norm + rotary + KV write (qk_rope_kv's arithmetic)
+// taken by the cluster attention kernel from the wqkv output directly.
+struct QkvIn {
+  const uint16_t* qkv;  // [n_head + 2 n_kv, 128] bf16
+  const uint16_t* qw;   // q_norm weight [128] or null
+  const uint16_t* kw;   // k_norm weight [128] or null
+  float eps;
+  const void* freqs;    // the position's rotary row [64, 2]
+  int ftype;
+  int n_head;
+};
+// One launch when a cluster can be resident; otherwise launch_qk_rope_kv into
+// q_scratch then launch_decode_attention (needs partial/counters).
+cudaError_t launch_qkv_attention(const QkvIn& in, const int64_t* pos, uint16_t* q_scratch, uint16_t* kc,
+                                 uint16_t* vc, uint16_t* out, int nh, int nkv, int max_len, int window,
+                                 float* partial, int* counters, cudaStream_t stream);
 
 }  // namespace nf4b

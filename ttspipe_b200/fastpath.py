@@ -61,6 +61,24 @@ def kernel_attention(q, k_cache, v_cache, out, *, n_head: int, n_kv: int, pos=No
         ctypes.c_void_p(st.cuda_stream)))
 
 
+def qkv_attention(qkv, k_cache, v_cache, out, *, n_head: int, n_kv: int, pos, window: int, max_len: int,
+                  freqs, freqs_dtype: int, q_norm_w=None, k_norm_w=None, eps: float = 1e-6, q_scratch=None):
+    """q/k norm + rotary + KV write + decode attention in one launch
+    (nf4b_qkv_attention) from the wqkv output `qkv` [n_head + 2 n_kv, 128];
+    `freqs` is the position's rotary row, `pos` the int64 device position."""
+    import torch
+
+    ws = attention_workspace(qkv.device, n_head, 128, window)
+    if q_scratch is None:
+        q_scratch = torch.empty(n_head * 128, dtype=torch.bfloat16, device=qkv.device)
+    st = torch.cuda.current_stream(qkv.device)
+    _lib.check(_lib.lib().nf4b_qkv_attention(
+        qkv.data_ptr(), None if q_norm_w is None else q_norm_w.data_ptr(),
+        None if k_norm_w is None else k_norm_w.data_ptr(), float(eps), freqs.data_ptr(), int(freqs_dtype),
+        pos.data_ptr(), q_scratch.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
+        n_head, n_kv, 128, max_len, window, ws.data_ptr(), ws.numel(), ctypes.c_void_p(st.cuda_stream)))
+
+
 def _grouped_torch(q, k, v, mask, n_head, n_local_heads, head_dim):
     """The reference's grouped formulation (app/engine/fastpath.py:158-174)."""
     import torch

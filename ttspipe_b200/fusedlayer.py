@@ -18,11 +18,14 @@ runs the block's own forward.
 
 from __future__ import annotations
 
-import ctypes
 
 from ttspipe_b200 import _lib
 
 HEAD_DIM = 128
+#: One launch for q/k norm + rotary + KV write + attention (nf4b_qkv_attention)
+#: instead of nf4b_qk_rope_kv then nf4b_decode_attention. Off: measured 3% slower
+#: per Dual-AR frame than the two launches chained by programmatic dependent launch.
+FUSED_QKV_ATTENTION = False
 #: Pass L2 prefetch hints (the next weight of the block) to each matmul: off,
 #: measured 1.5% slower per Dual-AR frame with them.
 PREFETCH = False
@@ -96,16 +99,24 @@ def decode_block(block, x, freqs_cis, mask, input_pos, next_block=None):
     qn = getattr(a, "q_norm", None) if a.attention_qk_norm else None
     kn = getattr(a, "k_norm", None) if a.attention_qk_norm else None
     eps = float(qn.eps if qn is not None and qn.eps is not None else 1e-6)
-    q = torch.empty(nh * HEAD_DIM, dtype=torch.bfloat16, device=x.device)
-    st = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
-    _lib.check(_lib.lib().nf4b_qk_rope_kv(
-        qkv.data_ptr(), None if qn is None else qn.weight.data_ptr(),
-        None if kn is None else kn.weight.data_ptr(), eps, freqs_cis.data_ptr(),
-        _FTYPE[str(freqs_cis.dtype)], input_pos.data_ptr(), q.data_ptr(),
-        a.kv_cache.k_cache.data_ptr(), a.kv_cache.v_cache.data_ptr(), nh, nkv, HEAD_DIM, max_len, st))
     y = torch.empty((1, 1, nh * HEAD_DIM), dtype=torch.bfloat16, device=x.device)
-    fastpath.kernel_attention(q, a.kv_cache.k_cache, a.kv_cache.v_cache, y, n_head=nh, n_kv=nkv,
-                              pos=input_pos, mask=None, window=int(mask.shape[-1]), max_len=max_len)
+    if not FUSED_QKV_ATTENTION:
+        q = torch.empty(nh * HEAD_DIM, dtype=torch.bfloat16, device=x.device)
+        _lib.check(_lib.lib().nf4b_qk_rope_kv(
+            qkv.data_ptr(), None if qn is None else qn.weight.data_ptr(),
+            None if kn is None else kn.weight.data_ptr(), eps, freqs_cis.data_ptr(),
+            _FTYPE[str(freqs_cis.dtype)], input_pos.data_ptr(), q.data_ptr(),
+            a.kv_cache.k_cache.data_ptr(), a.kv_cache.v_cache.data_ptr(), nh, nkv, HEAD_DIM, max_len,
+            torch.cuda.current_stream(x.device).cuda_stream))
+        fastpath.kernel_attention(q, a.kv_cache.k_cache, a.kv_cache.v_cache, y, n_head=nh, n_kv=nkv,
+                                  pos=input_pos, mask=None, window=int(mask.shape[-1]), max_len=max_len)
+    else:
+        # q/k norm, rotary, the KV write and the attention itself: one launch
+        fastpath.qkv_attention(qkv, a.kv_cache.k_cache, a.kv_cache.v_cache, y, n_head=nh, n_kv=nkv, pos=input_pos,
+                               window=int(mask.shape[-1]), max_len=max_len, freqs=freqs_cis,
+                               freqs_dtype=_FTYPE[str(freqs_cis.dtype)],
+                               q_norm_w=None if qn is None else qn.weight,
+                               k_norm_w=None if kn is None else kn.weight, eps=eps)
     h = nf4gemv.matmul(a.wo, y, epi=nf4gemv.EPI_RESIDUAL, operand=x, prefetch=pf(ff.w1))
     # w1 and w3 read the same input: one launch normalises h (ffn_norm) and
     # computes the gate silu(hn W1^T) * (hn W3^T) without writing hn or hn W1^T out.
