@@ -342,6 +342,26 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
   }
 }
 
+// Bounded wait (2 s by %globaltimer) until the global count at `ctr` reaches
+// `need`, acquire; false after recording the timeout in g_gemv_error (bit 2).
+__device__ __forceinline__ bool mbar_free_wait_count(const int* ctr, int need) {
+  unsigned long long start = 0;
+  for (uint32_t i = 0;; ++i) {
+    int seen;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(ctr) : "memory");
+    if (seen >= need) return true;
+    if ((i & 15u) == 0u) {
+      const unsigned long long now = gemv_globaltimer();
+      if (i == 0) {
+        start = now;
+      } else if (now - start > 2000000000ull) {
+        atomicOr(&g_gemv_error, 4);
+        return false;
+      }
+    }
+  }
+}
+
 // Store the outputs of row tile `rt` (rows g, g + 8 of activation row t):
 // the gate of the two halves for a gated pair, else the epilogue of half 0.
 template <bool kGated>
@@ -923,43 +943,31 @@ __global__ void __launch_bounds__(kThreads, 2) nf4_gemv_block_kernel(const GemvP
 // ---------------------------------------------------------------------------
 //
 // Job j reads its x (and epilogue operand) only after every row tile of jobs
-// 0..j-1 is stored, so x may be an earlier job's y. Units and runs per job
-// are those of the pair kernel (256-code units, equal contiguous runs per
-// warp); each warp's TMA ring runs straight across job boundaries, so the next
-// job's weights are already in shared memory while the current job finishes.
-// At a job boundary each CTA waits (thread 0, bounded) until the previous
-// job's completion count equals its tile count, then stages the job's code2
-// table and x - RMS-normalised first when the job asks for it, with the
-// arithmetic of nf4b_rms_norm - behind a CTA barrier. Every stored row tile
-// adds one to its job's count (release). The last CTA out re-zeroes the
-// counts, so the workspace is left as it was found.
+// 0..j-1 is stored, so x may be an earlier job's y. Units, runs, the unit
+// loop and the split-tile protocol are the pair kernel's (256-code units,
+// equal contiguous runs per warp, the last contributor to arrive reduces), so
+// every job equals the separate call bit for bit. Each warp's TMA ring runs
+// straight across job boundaries: the next job's first units are in flight
+// while the current one finishes. A CTA counts itself into the job's
+// completion count once all its warps are done with the job (reductions
+// included); at the next boundary thread 0 waits (bounded) for the count to
+// reach the grid size, then the CTA stages the job's code2 table(s) and x in
+// one round trip - RMS-normalised first when the job asks for it, with the
+// arithmetic of nf4b_rms_norm - behind a CTA barrier. The last CTA out
+// re-zeroes the counts, so the workspace is left as it was found.
 
-__device__ __forceinline__ void chain_store_tile(const ChainJob& J, int M, int rt, int g, int t,
-                                                 const float (&v)[2][2]) {
-  const int N = J.N;
-  const int ra = rt * 16 + g, rb = ra + 8;
-  if (t >= M) return;
-  const size_t oa = (size_t)t * N + ra, ob = (size_t)t * N + rb;
-  if (J.gated) {
-    if (ra < N) J.y[oa] = gate_bf16(v[0][0], v[1][0]);
-    if (rb < N) J.y[ob] = gate_bf16(v[0][1], v[1][1]);
-    return;
-  }
-#pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    const int row = e ? rb : ra;
-    const size_t o = e ? ob : oa;
-    if (row >= N) continue;
-    const float y = round_bf(v[0][e]);
-    float out = y;
-    if (J.epi == NF4B_EPI_RESIDUAL) {
-      out = __fadd_rn(bf2f(__ldcg(J.operand + o)), y);
-    } else if (J.epi == NF4B_EPI_SILU_GATE) {
-      const float a = bf2f(__ldcg(J.operand + o));
-      out = __fmul_rn(round_bf(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a)))), y);
-    }
-    J.y[o] = f2bf(out);
-  }
+// The chain's view of a job as the pair kernel's split-tile helpers see it.
+__device__ __forceinline__ void chain_as_params(const ChainJob& J, const ChainParams& cp, GemvParams& q) {
+  q.N = J.N;
+  q.M = cp.M;
+  q.blocks_per_tile = J.B;
+  q.uq = J.uq;
+  q.ur = J.ur;
+  q.partial = cp.partial;
+  q.counters = cp.counters;
+  q.y = J.y;
+  q.operand = J.operand;
+  q.epi = J.epi;
 }
 
 __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
@@ -968,6 +976,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   constexpr int R = GEMV_PAIR_STAGE_KB / SU;
   constexpr int WB = 1024 * SU, SB = 128 * SU;
   constexpr int kT = GEMV_PAIR_WARPS * 32;
+  constexpr int XR = (GEMV_PAIR_X_MAX / 16 + kT - 1) / kT;  // x uint4s per thread at most
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ double red[GEMV_PAIR_WARPS];
   __shared__ int s_ok;
@@ -1006,7 +1015,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   // Load cursor: job lj, unit lu of this warp's run [lu, lend) in it, and the
   // unit's tile lt, half lh, k unit lk.
   int lj = -1, lu = 0, lend = 0, lt = 0, lh = 0, lk = 0;
-  long long sbase = 0;
+  long long sbase = 0;  // first scale block of row g + 8t of tile lt
   auto load_rows = [&]() {
     const ChainJob& J = p.jobs[lj];
     sbase = (long long)min(lt * 16 + g + 8 * t, J.N - 1) * (J.K >> 6);
@@ -1047,6 +1056,9 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       load_rows();
     }
   };
+  // The pair kernel's 256-code unit request: one TMA box, and per row one
+  // aligned word of four scale codes plus the shared second-level scale (or
+  // 16 bytes of fp32 scales).
   auto issue = [&](int st) {
     const ChainJob& J = p.jobs[lj];
     const bool h3 = J.gated && lh;
@@ -1057,22 +1069,13 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     }
     if (t < 2) {
       const uint32_t ds = sring_s + st * SB + (g + 8 * t) * (8 * SU);
-      const long long be = sbase + lk * 4;  // four 64-blocks per unit
+      const long long be = sbase + lk * 4;  // four 64-blocks per unit, a multiple of 4
       const float* absmax = h3 ? J.absmax3 : J.absmax;
       if (J.nested) {
-        const uint8_t* a8 = h3 ? J.a8_3 : J.a8;
-        const long long total = (long long)J.N * (J.K >> 6);
-        const long long w0 = be & ~3LL;
-        const long long left = total - w0;
-        cp_async_4(ds, a8 + w0, (uint32_t)(left < 4 ? left : 4));
-        const long long w1 = left > 4 ? w0 + 4 : w0;
-        const long long l1 = left > 4 ? total - w1 : 0;
-        cp_async_4(ds + 4, a8 + w1, (uint32_t)(l1 < 4 ? l1 : 4));
-        cp_async_4(ds + 8, absmax + (be >> J.bs2_shift), 4u);
-        cp_async_4(ds + 12, absmax + ((be + 2) >> J.bs2_shift), 4u);
+        cp_async_4(ds, (h3 ? J.a8_3 : J.a8) + be, 4u);
+        cp_async_4(ds + 4, absmax + (be >> J.bs2_shift), 4u);
       } else {
-        cp_async_8(ds, absmax + be);
-        cp_async_8(ds + 8, absmax + be + 2);
+        cp_async_16(ds, absmax + be);
       }
     }
   };
@@ -1093,47 +1096,46 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   uint32_t phase = 0;
   for (int j = 0; j < n_jobs; ++j) {
     const ChainJob& J = p.jobs[j];
-    // ---- job boundary: every warp of this CTA is done with the last job's x and code2
-    __syncthreads();
+    GemvParams q;
+    chain_as_params(J, p, q);
+    // ---- job boundary: every CTA has stored its tiles of job j - 1
     if (j > 0 && threadIdx.x == 0) {
-      const int need = p.jobs[j - 1].tiles;
-      unsigned long long start = 0;
-      for (uint32_t i = 0;; ++i) {
-        int seen;
-        asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(done + (j - 1)) : "memory");
-        if (seen >= need) break;
-        if ((i & 15u) == 0u) {
-          const unsigned long long now = gemv_globaltimer();
-          if (i == 0) {
-            start = now;
-          } else if (now - start > 2000000000ull) {
-            atomicOr(&g_gemv_error, 4);
-            s_ok = 0;
-            break;
-          }
-        }
-      }
+      const int need = (int)gridDim.x;
+      if (!mbar_free_wait_count(done + (j - 1), need)) s_ok = 0;
     }
     __syncthreads();
     if (!s_ok) break;
-    const int K = J.K, N = J.N;
-    if (J.nested) {
-      for (int i = threadIdx.x; i < 256; i += kT) {
-        code2_s[i] = __ldcg(J.code2 + i);
-        if (J.gated) code2_s3[i] = __ldcg(J.code2_3 + i);
-      }
-    }
+    const int K = J.K;
     {
+      // code2 and x in one round trip: every load issued before the stores
       const int n16 = (M * K) >> 3;
       const uint4* src = reinterpret_cast<const uint4*>(J.x);
+      uint4 xv[XR];
+#pragma unroll
+      for (int r = 0; r < XR; ++r) {
+        const int i = threadIdx.x + r * kT;
+        if (i < n16) xv[r] = __ldcg(src + i);
+      }
+      float c2a = 0.f, c2b = 0.f;
+      if (J.nested && threadIdx.x < 256) {
+        c2a = __ldcg(J.code2 + threadIdx.x);
+        if (J.gated) c2b = __ldcg(J.code2_3 + threadIdx.x);
+      }
       uint4* dst = reinterpret_cast<uint4*>(xs);
-      for (int i = threadIdx.x; i < n16; i += kT) dst[i] = __ldcg(src + i);
+#pragma unroll
+      for (int r = 0; r < XR; ++r) {
+        const int i = threadIdx.x + r * kT;
+        if (i < n16) dst[i] = xv[r];
+      }
+      if (J.nested && threadIdx.x < 256) {
+        code2_s[threadIdx.x] = c2a;
+        if (J.gated) code2_s3[threadIdx.x] = c2b;
+      }
     }
     __syncthreads();
     if (J.norm_w != nullptr) rms_normalise_staged<kT>(reinterpret_cast<uint16_t*>(xs), M, K, J.norm_w, J.norm_eps, red);
 
-    // ---- this warp's units of job j
-    const int nblk = K >> 6;
+    // ---- this warp's units of job j (the pair kernel's unit loop)
     const int B = J.B, per_tile = J.gated ? 2 * B : B;
     int u0, u1;
     run_of(j, u0, u1);
@@ -1142,14 +1144,11 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       ch = 1;
       ck -= B;
     }
-    int ph_a = (int)(((long long)min(ct * 16 + g, N - 1) * nblk) & 3);
-    int ph_b = (int)(((long long)min(ct * 16 + g + 8, N - 1) * nblk) & 3);
     const int xtok = g >> 1;
     const bool xlane = (xtok < M) && ((g & 1) == (t >> 1));
     const uint4* xrow = reinterpret_cast<const uint4*>(xs + (size_t)(xlane ? xtok : 0) * K * 2 + t * 64);
-    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [half][row g / g + 8]
-    int pend_rt = -1;
-    float pend[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    float acc_a = 0.f, acc_b = 0.f, acc3_a = 0.f, acc3_b = 0.f;
+    int split_a = -1, split_b = -1, old_a = 0, old_b = 0;
     for (int u = u0; u < u1; ++u) {
       __syncwarp();
       if (lj < n_jobs) {
@@ -1170,7 +1169,6 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       st_use = st_use + 1 == R ? 0 : st_use + 1;
 
       const int rt = ct, kb = ck, hh = ch;
-      const int pha = ph_a, phb = ph_b;
       if (++ck == B) {
         ck = 0;
         if (J.gated && ch == 0) {
@@ -1178,40 +1176,37 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
         } else {
           ch = 0;
           ++ct;
-          ph_a = (int)(((long long)min(ct * 16 + g, N - 1) * nblk) & 3);
-          ph_b = (int)(((long long)min(ct * 16 + g + 8, N - 1) * nblk) & 3);
         }
       }
       const uint4 va = *reinterpret_cast<const uint4*>(sst + g * 16);
       const uint4 vb = *reinterpret_cast<const uint4*>(sst + (g + 8) * 16);
-      const bool h3 = J.gated && hh;
+      const uint32_t sa[4] = {va.x, va.y, va.z, va.w}, sb[4] = {vb.x, vb.y, vb.z, vb.w};
       float ya = 0.f, yb = 0.f;
 #pragma unroll
       for (int i = 0; i < SU; ++i) {
         const int kb2 = kb * SU + i;
         float se_a, so_a, se_b, so_b;
         if (J.nested) {
-          const float* c2 = h3 ? code2_s3 : code2_s;
-          const float off = h3 ? J.offset3 : J.offset;
-          const unsigned long long wa8 = ((unsigned long long)va.y << 32) | va.x;
-          const unsigned long long wb8 = ((unsigned long long)vb.y << 32) | vb.x;
-          const uint32_t sha = (uint32_t)(pha + 2 * i) * 8, shb = (uint32_t)(phb + 2 * i) * 8;
-          const float s2a = __uint_as_float(i ? va.w : va.z), s2b = __uint_as_float(i ? vb.w : vb.z);
-          se_a = nested_scale(c2[(uint32_t)(wa8 >> sha) & 0xFFu], s2a, off);
-          so_a = nested_scale(c2[(uint32_t)(wa8 >> (sha + 8)) & 0xFFu], s2a, off);
-          se_b = nested_scale(c2[(uint32_t)(wb8 >> shb) & 0xFFu], s2b, off);
-          so_b = nested_scale(c2[(uint32_t)(wb8 >> (shb + 8)) & 0xFFu], s2b, off);
+          const float* c2 = (J.gated && hh) ? code2_s3 : code2_s;
+          const float off = (J.gated && hh) ? J.offset3 : J.offset;
+          const uint32_t ea = (sa[0] >> (16 * i)) & 0xFFu, oa = (sa[0] >> (16 * i + 8)) & 0xFFu;
+          const uint32_t eb = (sb[0] >> (16 * i)) & 0xFFu, ob = (sb[0] >> (16 * i + 8)) & 0xFFu;
+          const float s2a = __uint_as_float(sa[1]), s2b = __uint_as_float(sb[1]);
+          se_a = nested_scale(c2[ea], s2a, off);
+          so_a = nested_scale(c2[oa], s2a, off);
+          se_b = nested_scale(c2[eb], s2b, off);
+          so_b = nested_scale(c2[ob], s2b, off);
         } else {
-          se_a = __uint_as_float(i ? va.z : va.x); so_a = __uint_as_float(i ? va.w : va.y);
-          se_b = __uint_as_float(i ? vb.z : vb.x); so_b = __uint_as_float(i ? vb.w : vb.y);
+          se_a = __uint_as_float(sa[2 * i]); so_a = __uint_as_float(sa[2 * i + 1]);
+          se_b = __uint_as_float(sb[2 * i]); so_b = __uint_as_float(sb[2 * i + 1]);
         }
-        uint4 xv[4];
+        uint4 xq4[4];
         if (xlane) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) xv[q] = xrow[kb2 * 16 + q];
+          for (int jj = 0; jj < 4; ++jj) xq4[jj] = xrow[kb2 * 16 + jj];
         } else {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) xv[q] = make_uint4(0, 0, 0, 0);
+          for (int jj = 0; jj < 4; ++jj) xq4[jj] = make_uint4(0, 0, 0, 0);
         }
         const uint4 wav = *reinterpret_cast<const uint4*>(wst + g * (64 * SU) + i * 64 + t * 16);
         const uint4 wbv = *reinterpret_cast<const uint4*>(wst + (g + 8) * (64 * SU) + i * 64 + t * 16);
@@ -1226,7 +1221,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
           const uint32_t a2 = lut_lookup(lut, w0, lut_sel(j0 + 1), lane_base);
           const uint32_t a1 = lut_lookup(lut, w1, lut_sel(j0), lane_base);
           const uint32_t a3 = lut_lookup(lut, w1, lut_sel(j0 + 1), lane_base);
-          const uint4& xq = xv[s >> 1];
+          const uint4& xq = xq4[s >> 1];
           const uint32_t b0 = (s & 1) ? xq.z : xq.x;
           const uint32_t b1 = (s & 1) ? xq.w : xq.y;
           if (s & 1)
@@ -1237,92 +1232,44 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
         ya += fmaf(so_a, d0[1] + d1[1], (d0[0] + d1[0]) * se_a);
         yb += fmaf(so_b, d0[3] + d1[3], (d0[2] + d1[2]) * se_b);
       }
-      if (h3) {
-        acc[1][0] += ya;
-        acc[1][1] += yb;
+      if (J.gated && hh) {
+        acc3_a += ya;
+        acc3_b += yb;
       } else {
-        acc[0][0] += ya;
-        acc[0][1] += yb;
+        acc_a += ya;
+        acc_b += yb;
       }
       if ((kb == B - 1 && (!J.gated || hh == 1)) || u == u1 - 1) {
-        // finish row tile rt: stored at once when it lies inside this warp's
-        // run; a split tile is reduced by the warp owning its last unit, after
-        // that warp's run, once the others have published their partials.
-        // Every stored tile counts toward the job's completion.
-        const int H = J.gated ? 2 : 1;
-        const int t0 = rt * per_tile, t1 = t0 + per_tile - 1;
-        if (t0 >= u0 && t1 < u1) {
-          chain_store_tile(J, M, rt, g, t, acc);
-          __syncwarp();
-          if (lane == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(done + j) : "memory");
-        } else {
-          const int w_lo = warp_of(t0, J.uq, J.ur), w_hi = warp_of(t1, J.uq, J.ur);
-          if (gw == w_hi) {
-            pend_rt = rt;
-            pend[0][0] = acc[0][0]; pend[0][1] = acc[0][1]; pend[1][0] = acc[1][0]; pend[1][1] = acc[1][1];
+        const float v[2][2] = {{acc_a, acc_b}, {acc3_a, acc3_b}};
+        int old = 0;
+        const bool split = J.gated ? publish_pair_tile<true>(q, rt, u0, u1, gw, g, t, lane, v, old)
+                                   : publish_pair_tile<false>(q, rt, u0, u1, gw, g, t, lane, v, old);
+        if (split) {
+          if (split_a < 0) {
+            split_a = rt;
+            old_a = old;
           } else {
-            const int ra = rt * 16 + g, rb = ra + 8;
-            const size_t MN = (size_t)M * N;
-            float* slot = p.partial + (size_t)(gw - w_lo) * H * MN + (size_t)t * N;
-            if (t < M) {
-              for (int h = 0; h < H; ++h) {
-                if (ra < N) __stcg(slot + h * MN + ra, acc[h][0]);
-                if (rb < N) __stcg(slot + h * MN + rb, acc[h][1]);
-              }
-            }
-            __syncwarp();
-            if (lane == 0)
-              asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.counters + rt) : "memory");
+            split_b = rt;
+            old_b = old;
           }
         }
-        acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.f;
+        acc_a = acc_b = acc3_a = acc3_b = 0.f;
       }
     }
-    if (pend_rt >= 0 && s_ok) {
-      // this warp reduces the split tile its run started in: bounded wait for
-      // the earlier contributors, then their slots in slot order and its own last
-      const int H = J.gated ? 2 : 1;
-      const int rt = pend_rt;
-      const int others = gw - warp_of(rt * per_tile, J.uq, J.ur);
-      int* ctr = p.counters + rt;
-      int ok = 1;
-      if (lane == 0) {
-        unsigned long long start = 0;
-        for (uint32_t i = 0;; ++i) {
-          int seen;
-          asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(ctr) : "memory");
-          if (seen == others) break;
-          if ((i & 15u) == 0u) {
-            const unsigned long long now = gemv_globaltimer();
-            if (i == 0) {
-              start = now;
-            } else if (now - start > 2000000000ull) {
-              atomicOr(&g_gemv_error, 2);
-              ok = 0;
-              break;
-            }
-          }
-        }
-        *ctr = 0;
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      __syncwarp();
-      if (ok) {
-        const int ra = rt * 16 + g, rb = ra + 8;
-        const size_t MN = (size_t)M * N;
-        if (t < M) {
-          const float* base = p.partial + (size_t)t * N;
-          if (H == 2)
-            sum_tile_slots<2>(base, MN, 2 * MN, others, ra, rb, N, pend);
-          else
-            sum_tile_slots<1>(base, MN, MN, others, ra, rb, N, pend);
-        }
-        chain_store_tile(J, M, rt, g, t, pend);
-        __syncwarp();
-        if (lane == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(done + j) : "memory");
+    if (s_ok) {
+      if (J.gated) {
+        if (split_a >= 0) finish_split_tile<true>(q, split_a, old_a, g, t, lane);
+        if (split_b >= 0) finish_split_tile<true>(q, split_b, old_b, g, t, lane);
       } else {
-        s_ok = 0;
+        if (split_a >= 0) finish_split_tile<false>(q, split_a, old_a, g, t, lane);
+        if (split_b >= 0) finish_split_tile<false>(q, split_b, old_b, g, t, lane);
       }
+    }
+    // ---- this CTA is done with job j: count it in (release after the barrier)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(done + j) : "memory");
     }
   }
   cp_async_wait<0>();
