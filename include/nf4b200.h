@@ -91,7 +91,11 @@ int nf4b_device_error(int clear);
  * counts the tcgen05 GEMM. `operand` has Y's shape (epi != NONE).
  * `workspace` must hold nf4b_gemm_workspace_size(w, rows) bytes and be zeroed
  * once before its first use; every call leaves it zeroed again. One workspace
- * per stream: calls that overlap on the GPU must not share one.
+ * per stream: calls that overlap on the GPU must not share one. For the GEMM
+ * the workspace holds split-K partial sums (the k range is split across CTAs
+ * when the output tiles alone cannot fill the GPU, and each tile's last CTA
+ * sums the splits in order); a GEMM given no (or too small a) workspace runs
+ * unsplit, with the same results up to fp32 summation order.
  */
 int nf4b_gemm(const nf4b_weight* w, const void* x, void* y, int rows, int epi,
               const void* operand, void* workspace, size_t workspace_bytes, void* stream);

@@ -78,3 +78,40 @@ def test_repeated_calls_are_deterministic():
     b = nf4gemv.matmul(layer, x)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("n,k,rows", [(2560, 4096, 64), (2560, 9728, 64), (6144, 2560, 64), (1024, 2560, 64),
+                                      (1024, 2560, 40), (2560, 4096, 33)])
+def test_split_k_matches_the_unsplit_gemm(n, k, rows):
+    """Given a workspace the GEMM splits the k range across CTAs when its 64-row
+    tiles cannot fill the GPU (batched decode, M <= 64); the splits' sums (in
+    split order, so repeatable) equal the one-pass GEMM up to fp32 summation
+    order, and the workspace's tile counters are left at zero."""
+    import ctypes
+
+    lin = make_linear(n, k, seed=n + k + rows)
+    x = randn_bf16((rows, k), seed=7000 + rows, device="cuda")
+    L = _lib.lib()
+    desc = lin._nf4_fast["desc"]
+    need = int(L.nf4b_gemm_workspace_size(ctypes.byref(desc), rows))
+    assert need > 0, "a 148-SM B200 splits this shape"
+    ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    y_split = torch.empty(rows, n, dtype=torch.bfloat16, device="cuda")
+    y_again = torch.empty_like(y_split)
+    y_one = torch.empty_like(y_split)
+    assert L.nf4b_gemm(ctypes.byref(desc), x.data_ptr(), y_split.data_ptr(), rows, 0, None, ws.data_ptr(), need, st) == 0
+    assert L.nf4b_gemm(ctypes.byref(desc), x.data_ptr(), y_again.data_ptr(), rows, 0, None, ws.data_ptr(), need, st) == 0
+    assert L.nf4b_gemm(ctypes.byref(desc), x.data_ptr(), y_one.data_ptr(), rows, 0, None, None, 0, st) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(y_split, y_again)
+    assert int(ws[:4096].count_nonzero()) == 0
+    got, one = orc.bf16_to_f32(to_bits(y_split)), orc.bf16_to_f32(to_bits(y_one))
+    # the fp32 sums differ only in order (~1e-5 absolute here): after the bf16
+    # rounding at most one ulp apart, or a hair apart near zero
+    import numpy as np
+    rms = float(np.sqrt((one.astype(np.float64) ** 2).mean()))
+    assert np.all(np.abs(got - one) <= np.maximum(np.abs(got), np.abs(one)) * 2.0 ** -7 + 1e-4 * rms)
+    check_matmul(y_split.view(1, rows, n), x.view(1, rows, k), lin)
+    check_matmul(y_one.view(1, rows, n), x.view(1, rows, k), lin)
+    assert L.nf4b_device_error(0) == 0

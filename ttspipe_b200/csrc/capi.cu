@@ -247,7 +247,7 @@ int nf4b_device_error(int clear) {
 
 size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows) {
   if (w == nullptr || rows <= 0 || w->n_out <= 0 || w->k_in <= 0) return 0;
-  if (rows > GEMV_MAX_ROWS) return 0;
+  if (rows > GEMV_MAX_ROWS) return gemm_workspace_bytes(w->n_out, rows, w->k_in, current_sm_count());
   return gemv_workspace_bytes(w, rows, current_sm_count());
 }
 
@@ -277,7 +277,7 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
   if (opts != nullptr && opts->norm_weight != nullptr)
     return fail(NF4B_ERR_SHAPE, "a fused RMSNorm is served for 1..4 rows (got %d)", rows);
 
-  GemmParams p;
+  GemmParams p = {};
   p.packed = w->packed;
   p.a8 = w->absmax_code;
   p.absmax = w->absmax;
@@ -293,6 +293,13 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
   p.operand = static_cast<const uint16_t*>(operand);
   p.M = rows;
   p.epi = epi;
+  // split-K when the caller's workspace holds the partial sums (else one pass)
+  int splits = gemm_splits(w->n_out, rows, w->k_in, current_sm_count());
+  const size_t need = splits > 1 ? GEMM_COUNTER_BYTES + (size_t)splits * rows * w->n_out * sizeof(float) : 0;
+  if (splits > 1 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256))) splits = 1;
+  p.splits = splits;
+  p.counters = static_cast<int*>(workspace);
+  p.partial = splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + GEMM_COUNTER_BYTES) : nullptr;
   return launch_status(launch_gemm_tc(p, s), "nf4 tcgen05 gemm launch");
 }
 

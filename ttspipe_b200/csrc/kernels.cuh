@@ -233,7 +233,17 @@ struct GemmParams {
   const uint16_t* operand;
   int M;
   int epi;
+  // split-K (grid z = splits > 1): fp32 partial sums [splits, M, N] and one
+  // counter per output tile; the last CTA of a tile sums the splits in order
+  int splits;
+  float* partial;
+  int* counters;
 };
+constexpr size_t GEMM_COUNTER_BYTES = 4096;  // tile counters of a split-K launch (<= 1024 tiles)
+// Split-K factor the GEMM would use for this shape on `sms` SMs (1: none), and
+// the workspace it then needs (0 when 1).
+int gemm_splits(int N, int M, int K, int sms);
+size_t gemm_workspace_bytes(int N, int M, int K, int sms);
 cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream);
 
 // ---- fused elementwise (fused_ops.cu) -------------------------------------

@@ -62,6 +62,7 @@ struct __align__(1024) TileSmem {
   unsigned long long accum_full;
   uint32_t tmem_base;
   int abort_flag;
+  int last;  // split-K: this CTA finishes its tile
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -142,7 +143,7 @@ __host__ __device__ constexpr uint32_t instr_desc() {
          | ((uint32_t)(BM >> 4) << 24); // M
 }
 
-template <int BT, int DQ>
+template <int BT, int DQ, bool kSplit>
 __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
     nf4_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                        const __grid_constant__ CUtensorMap tmap_w, const GemmParams p) {
@@ -153,6 +154,10 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
   const int n0 = blockIdx.x * BM;
   const int tok0 = blockIdx.y * BT;
   const int KB = p.K / BK;
+  // split-K: this CTA's k blocks [kb_lo, kb_lo + nkb)
+  const int S = kSplit ? (int)gridDim.z : 1, z = kSplit ? (int)blockIdx.z : 0;
+  const int kb_lo = kSplit ? (int)((long long)KB * z / S) : 0;
+  const int nkb = kSplit ? (int)((long long)KB * (z + 1) / S) - kb_lo : KB;
   volatile int* abort_flag = &sm.abort_flag;
 
   if (tid == 0) {
@@ -184,10 +189,10 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % STAGES;
-        if (kb >= STAGES &&
-            !mbar_wait(smem_u32(&sm.mma_done[s]), ((kb / STAGES) - 1) & 1, abort_flag))
+      for (int i = 0; i < nkb; ++i) {
+        const int kb = kb_lo + i, s = i % STAGES;
+        if (i >= STAGES &&
+            !mbar_wait(smem_u32(&sm.mma_done[s]), ((i / STAGES) - 1) & 1, abort_flag))
           break;
         const uint32_t bar = smem_u32(&sm.tma_full[s]);
         mbar_expect_tx(bar, BT * 128 + BM * 32);
@@ -199,9 +204,9 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
     if (lane == 0) {
       constexpr uint32_t idesc = instr_desc<BT>();
       bool ok = true;
-      for (int kb = 0; kb < KB && ok; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
+      for (int i = 0; i < nkb && ok; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
         ok = mbar_wait(smem_u32(&sm.tma_full[s]), ph, abort_flag) &&
              mbar_wait(smem_u32(&sm.a_full[s]), ph, abort_flag);
         if (!ok) break;
@@ -210,7 +215,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k) {
           const uint64_t ad = smem_desc(a_addr + k * 32), bd = smem_desc(x_addr + k * 32);
-          const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+          const uint32_t accumulate = (i > 0 || k > 0) ? 1u : 0u;
           asm volatile(
               "{\n\t.reg .pred p;\n\t"
               "setp.ne.b32 p, %4, 0;\n\t"
@@ -233,8 +238,8 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
     const int row = n0 + r;
     const bool valid = row < p.N;
     const int rsw = r & 7;
-    for (int kb = grp; kb < KB; kb += DQ) {
-      const int s = kb % STAGES;
+    for (int i = grp; i < nkb; i += DQ) {
+      const int kb = kb_lo + i, s = i % STAGES;
       float scale = 0.f;
       if (valid) {
         const size_t b = ((size_t)row * p.K + (size_t)kb * BK) >> p.bs_shift;
@@ -244,7 +249,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
         else
           scale = __ldg(p.absmax + b);
       }
-      if (!mbar_wait(smem_u32(&sm.tma_full[s]), (kb / STAGES) & 1, abort_flag)) break;
+      if (!mbar_wait(smem_u32(&sm.tma_full[s]), (i / STAGES) & 1, abort_flag)) break;
       const uint4* wp = reinterpret_cast<const uint4*>(sm.w[s] + r * 32);
       const uint4 u0 = wp[0], u1 = wp[1];
       const uint32_t words[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
@@ -281,7 +286,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
               "=r"(v[30]), "=r"(v[31])
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (n < p.N) {
+        if (n < p.N && !kSplit) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int tok = tok0 + cb * 32 + i;
@@ -290,12 +295,20 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
               p.y[o] = epilogue(__uint_as_float(v[i]), p.epi, p.operand, o);
             }
           }
+        } else if (n < p.N) {
+          float* part = p.partial + (size_t)z * p.M * p.N + n;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int tok = tok0 + cb * 32 + i;
+            if (tok < p.M) __stcg(part + (size_t)tok * p.N, __uint_as_float(v[i]));
+          }
         }
       }
     }
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  if (kSplit) __threadfence();  // this thread's partial stores, before the tile's count below
   __syncthreads();
   pdl_launch_dependents();
   if (warp == 1) {
@@ -304,9 +317,55 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
                  "r"((uint32_t)BT)
                  : "memory");
   }
+  if (kSplit) {
+    // The tile's last CTA to finish sums the S partials in split order
+    // (deterministic) and stores Y; the counter is re-zeroed for the next launch.
+    int* ctr = p.counters + blockIdx.y * gridDim.x + blockIdx.x;
+    if (tid == 0) {
+      __threadfence();
+      const int old = atomicAdd(ctr, 1);
+      sm.last = (old == S - 1);
+      if (sm.last) *ctr = 0;
+    }
+    __syncthreads();
+    if (!sm.last || *abort_flag) return;
+    __threadfence();
+    // four elements per thread in flight, each with all its splits' loads issued
+    // before the in-order sum
+    const size_t MN = (size_t)p.M * p.N;
+    constexpr int T = gemm_threads<DQ>();
+    for (int base = tid; base < BT * BM; base += 4 * T) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      size_t o[4];
+      bool live[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int idx = base + e * T;
+        const int tok = tok0 + idx / BM, n = n0 + idx % BM;
+        live[e] = idx < BT * BM && tok < p.M && n < p.N;
+        o[e] = live[e] ? (size_t)tok * p.N + n : 0;
+      }
+      for (int z0 = 0; z0 < S; z0 += 4) {
+        float v[4][4];
+#pragma unroll
+        for (int zz = 0; zz < 4; ++zz)
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            v[zz][e] = (live[e] && z0 + zz < S) ? __ldcg(p.partial + (z0 + zz) * MN + o[e]) : 0.f;
+#pragma unroll
+        for (int zz = 0; zz < 4; ++zz)
+          if (z0 + zz < S)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[e] += v[zz][e];
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (live[e]) p.y[o[e]] = epilogue(acc[e], p.epi, p.operand, o[e]);
+    }
+  }
 }
 
-template <int BT>
+template <int BT, bool kSplit>
 cudaError_t launch_bt(const GemmParams& p, cudaStream_t stream) {
   CUtensorMap mx, mw;
   if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.x, (uint64_t)p.K, (uint64_t)p.M,
@@ -320,13 +379,13 @@ cudaError_t launch_bt(const GemmParams& p, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(nf4_gemm_tc_kernel<BT, kDequantGroups>,
+    cudaError_t e = cudaFuncSetAttribute(nf4_gemm_tc_kernel<BT, kDequantGroups, kSplit>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((p.N + BM - 1) / BM, (p.M + BT - 1) / BT);
+  cfg.gridDim = dim3((p.N + BM - 1) / BM, (p.M + BT - 1) / BT, kSplit ? p.splits : 1);
   cfg.blockDim = dim3(gemm_threads<kDequantGroups>());
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -335,15 +394,63 @@ cudaError_t launch_bt(const GemmParams& p, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, nf4_gemm_tc_kernel<BT, kDequantGroups>, mx, mw, p);
+  return cudaLaunchKernelEx(&cfg, nf4_gemm_tc_kernel<BT, kDequantGroups, kSplit>, mx, mw, p);
 }
 
 }  // namespace
 
+// Activation rows per tile for M rows.
+static int gemm_bt(int M) { return M <= 64 ? 64 : (M <= 128 ? 128 : 256); }
+
+template <int BT, bool kSplit>
+static int gemm_ctas_per_sm() {
+  static int occ[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int i = (dev >= 0 && dev < 64) ? dev : 0;
+  if (occ[i] == 0) {
+    const int smem = (int)(sizeof(TileSmem<BT>) + 1024);
+    int n = 0;
+    if (cudaFuncSetAttribute(nf4_gemm_tc_kernel<BT, kDequantGroups, kSplit>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, nf4_gemm_tc_kernel<BT, kDequantGroups, kSplit>,
+                                                      gemm_threads<kDequantGroups>(), smem) != cudaSuccess ||
+        n < 1) {
+      (void)cudaGetLastError();
+      n = 1;
+    }
+    occ[i] = n;
+  }
+  return occ[i];
+}
+
+// Split the k range when the output tiles alone cannot fill the GPU: as many
+// splits as keep every resident CTA slot busy, each of at least 4 k blocks.
+// Only 64-row tiles (M <= 64): measured, the partial sums' traffic costs more
+// than the extra CTAs win for 128- and 256-row tiles.
+int gemm_splits(int N, int M, int K, int sms) {
+  const int bt = gemm_bt(M);
+  if (bt != 64) return 1;
+  const long long tiles = (long long)((N + BM - 1) / BM) * ((M + bt - 1) / bt);
+  if (tiles * (long long)sizeof(int) > (long long)GEMM_COUNTER_BYTES) return 1;
+  const int occ = gemm_ctas_per_sm<64, true>();
+  long long s = (long long)sms * occ / tiles;
+  const long long kmax = (K / BK) / 4;
+  if (s > kmax) s = kmax;
+  if (s > 16) s = 16;
+  return s >= 2 ? (int)s : 1;
+}
+
+size_t gemm_workspace_bytes(int N, int M, int K, int sms) {
+  const int s = gemm_splits(N, M, K, sms);
+  return s > 1 ? GEMM_COUNTER_BYTES + (size_t)s * M * N * sizeof(float) : 0;
+}
+
 cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream) {
-  if (p.M <= 64) return launch_bt<64>(p, stream);
-  if (p.M <= 128) return launch_bt<128>(p, stream);
-  return launch_bt<256>(p, stream);
+  const int bt = gemm_bt(p.M);
+  if (bt == 64) return p.splits > 1 ? launch_bt<64, true>(p, stream) : launch_bt<64, false>(p, stream);
+  if (bt == 128) return launch_bt<128, false>(p, stream);
+  return launch_bt<256, false>(p, stream);
 }
 
 int read_device_error(int clear) {

@@ -22,8 +22,10 @@
 // (cudaMemsetAsync on the call's stream) before launching, so stale contents
 // are harmless for calls ordered on one stream; calls that overlap on the GPU
 // (other streams, other threads) race on the same bytes and must not be issued.
-// Calls whose partial sums would not fit are rejected; more than 32 activation
-// rows run the tensor-core GEMM, which needs no scratch at all.
+// GEMV calls whose partial sums would not fit are rejected. More than 32
+// activation rows run the tensor-core GEMM: it takes the scratch for its
+// split-K partial sums when they fit (so it splits exactly as nf4b_gemm with a
+// workspace does) and otherwise runs unsplit.
 
 #include <mutex>
 #include <stdio.h>
@@ -46,10 +48,10 @@ void* g_scratch_ptr[64];  // device address of g_gemv_scratch, per device
 
 extern "C" int nf4b_gemm_noalloc(const nf4b_weight* w, const void* x, void* y, int rows, int epi,
                                  const void* operand, void* stream) {
-  if (rows > nf4b::GEMV_MAX_ROWS)  // the tensor-core path uses no scratch
-    return nf4b_gemm(w, x, y, rows, epi, operand, nullptr, 0, stream);
   const size_t need = nf4b_gemm_workspace_size(w, rows);
-  if (need == 0)  // invalid weight or row count: nf4b_gemm reports why
+  if (need == 0)  // an unsplit GEMM, or an invalid weight / row count that nf4b_gemm reports
+    return nf4b_gemm(w, x, y, rows, epi, operand, nullptr, 0, stream);
+  if (rows > nf4b::GEMV_MAX_ROWS && need > (size_t)NF4B_NOALLOC_SCRATCH_BYTES)  // GEMM: run unsplit
     return nf4b_gemm(w, x, y, rows, epi, operand, nullptr, 0, stream);
   if (need > (size_t)NF4B_NOALLOC_SCRATCH_BYTES) {
     char msg[256];
@@ -78,7 +80,8 @@ extern "C" int nf4b_gemm_noalloc(const nf4b_weight* w, const void* x, void* y, i
     }
     scratch = g_scratch_ptr[dev];
   }
-  // The per-tile arrival counters at the start of the scratch must read zero.
+  // The per-tile arrival counters at the start of the scratch must read zero
+  // (GEMV_COUNTER_BYTES covers the GEMM's GEMM_COUNTER_BYTES too).
   const cudaError_t e = cudaMemsetAsync(scratch, 0, nf4b::GEMV_COUNTER_BYTES,
                                         reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {

@@ -71,8 +71,11 @@ def available() -> bool:
     return _unavailable is None
 
 
-def _workspace(device, nbytes: int):
-    """The zeroed, 256-byte aligned GEMV workspace of this device.
+def _workspace(device, nbytes: int, kind: str = "gemv"):
+    """The zeroed, 256-byte aligned GEMV workspace of this device (kind
+    "gemm": the tensor-core GEMM's split-K workspace, kept apart so that
+    growing it for a large prefill never moves the buffer a captured decode
+    graph points at).
 
     One per device, like the reference's single worker stream
     (app/engine/worker.py:1-12): GEMVs issued concurrently on two streams of
@@ -82,7 +85,8 @@ def _workspace(device, nbytes: int):
     """
     import torch
 
-    key = torch.device(device).index if torch.device(device).index is not None else torch.cuda.current_device()
+    idx = torch.device(device).index if torch.device(device).index is not None else torch.cuda.current_device()
+    key = idx if kind == "gemv" else (kind, idx)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         if torch.cuda.is_current_stream_capturing():
@@ -260,9 +264,9 @@ def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None, norm=
     L = _lib.lib()
     desc = fast["desc"]
     ws_ptr, ws_bytes = None, 0
-    if rows <= MAX_N:
-        need = int(L.nf4b_gemm_workspace_size(ctypes.byref(desc), rows))
-        ws = _workspace(x.device, need)
+    need = int(L.nf4b_gemm_workspace_size(ctypes.byref(desc), rows))   # GEMV slots or GEMM split-K sums
+    if need > 0:
+        ws = _workspace(x.device, need, "gemv" if rows <= MAX_N else "gemm")
         ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
     opts = _opts(prefetch, norm)
     _lib.check(L.nf4b_gemm_ex(ctypes.byref(desc), flat.data_ptr(), out.data_ptr(), rows, int(epi),
