@@ -113,3 +113,25 @@ def test_slow_stack_matches_the_reference_blocks_at_the_frame_position(decoder):
     restore(dec, snap)
     err0 = orc.rms_relative_max_error(orc.bf16_to_f32(to_bits(x0)), want)
     assert err0 > max(5 * err, 1e-4), (err, err0)
+
+
+def test_state_dict_round_trip_reproduces_the_model():
+    """A decoder built from another's state dict (NF4 blocks in bitsandbytes'
+    serialisation) computes exactly what the original computes; a decoder
+    with other random weights does not."""
+    cfg = DualARConfig()
+    a = DualARDecoder(cfg, "cuda", seed=5, n_slow=2)
+    sd = a.state_dict()
+    b = DualARDecoder(cfg, "cuda", seed=6, n_slow=2, state_dict=sd)
+    c = DualARDecoder(cfg, "cuda", seed=6, n_slow=2)
+    prompt = torch.randint(0, cfg.vocab, (40,), generator=torch.Generator().manual_seed(1)).cuda()
+    outs = []
+    for d in (a, b, c):
+        d.prefill(prompt)
+        h = d.slow_stack(d.x.clone())
+        outs.append((h, torch.matmul(h.view(1, -1).float(), d.lm_head.float().t())))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    assert not torch.equal(outs[0][0], outs[2][0])
+    for d in (a, b, c):
+        d.release()

@@ -18,7 +18,9 @@ CUDA graph with no host round trip:
 
 The model is random-init NF4 with S2-Pro dimensions (the checkpoint is not
 available): weights N(0, 0.02), norm weights N(1, 0.1), embeddings N(0, 1)
-scaled by 0.02. The prompt is prefilled through the same blocks (GEMM path,
+scaled by 0.02 - or loaded from a state dict (``state_dict()`` /
+``DualARDecoder(..., state_dict=sd)``), whose NF4 blocks use bitsandbytes'
+serialisation (ttspipe_b200.checkpoint). The prompt is prefilled through the same blocks (GEMM path,
 the grouped attention of app/engine/fastpath.py:158-174).
 """
 
@@ -29,7 +31,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from ttspipe_b200 import _lib, fusedlayer, fusedops, heads, nf4gemv
+from ttspipe_b200 import _lib, checkpoint, fusedlayer, fusedops, heads, nf4gemv
 from ttspipe_b200.model import ModelArgs, precompute_freqs_cis, random_block
 
 
@@ -50,9 +52,11 @@ class DualARConfig:
 
 
 class DualARDecoder:
-    """A random-init Dual-AR model on one GPU and its captured frame graph."""
+    """A Dual-AR model on one GPU (random-init, or from a state dict) and its
+    captured frame graph. `seed` also seeds the draws."""
 
-    def __init__(self, cfg: DualARConfig, device, seed: int = 0, n_slow: int | None = None):
+    def __init__(self, cfg: DualARConfig, device, seed: int = 0, n_slow: int | None = None,
+                 state_dict: dict | None = None):
         if not (nf4gemv.available() and nf4gemv.install() and fusedlayer.install() and fusedops.install()):
             raise RuntimeError("the sm_100a kernels are not available")
         self.cfg, self.device, self.seed = cfg, torch.device(device), seed
@@ -66,11 +70,18 @@ class DualARDecoder:
         def norm_w():
             return (1.0 + 0.1 * torch.randn(sc.dim, generator=g, device=self.device)).to(torch.bfloat16)
 
-        self.slow = [random_block(sc, device=self.device, seed=seed * 1000 + i) for i in range(n_slow)]
         fast_args = ModelArgs(dim=sc.dim, n_head=sc.n_head, n_local_heads=sc.n_local_heads, head_dim=sc.head_dim,
-                              intermediate_size=sc.intermediate_size, max_seq_len=16, n_layer=cfg.n_fast_layer)
-        self.fast = [random_block(fast_args, device=self.device, seed=seed * 1000 + 500 + i)
-                     for i in range(cfg.n_fast_layer)]
+                              intermediate_size=sc.intermediate_size, max_seq_len=16, n_layer=cfg.n_fast_layer,
+                              attention_qk_norm=sc.attention_qk_norm, norm_eps=sc.norm_eps, rope_base=sc.rope_base)
+        self.fast_args = fast_args
+        if state_dict is None:
+            self.slow = [random_block(sc, device=self.device, seed=seed * 1000 + i) for i in range(n_slow)]
+            self.fast = [random_block(fast_args, device=self.device, seed=seed * 1000 + 500 + i)
+                         for i in range(cfg.n_fast_layer)]
+        else:
+            self.slow = [checkpoint.load_block(state_dict, f"layers.{i}", sc, self.device) for i in range(n_slow)]
+            self.fast = [checkpoint.load_block(state_dict, f"fast_layers.{i}", fast_args, self.device)
+                         for i in range(cfg.n_fast_layer)]
         for blk in self.slow + self.fast:
             for lin in (blk.attention.wqkv, blk.attention.wo, blk.feed_forward.w1, blk.feed_forward.w3,
                         blk.feed_forward.w2):
@@ -81,6 +92,8 @@ class DualARDecoder:
         self.sem_emb = randn(cfg.vocab, sc.dim)
         self.cb_emb = randn(cfg.num_codebooks, cfg.codebook_size, sc.dim)
         self.fast_emb = randn(cfg.codebook_size, sc.dim)
+        if state_dict is not None:
+            self._load_dense(state_dict)
         self.freqs = precompute_freqs_cis(sc.max_seq_len, sc.head_dim, sc.rope_base, device=self.device)
         self.fast_freqs = precompute_freqs_cis(16, sc.head_dim, sc.rope_base, device=self.device)
         self.mask = torch.ones(1, 1, 1, sc.max_seq_len, dtype=torch.bool, device=self.device)
@@ -95,6 +108,53 @@ class DualARDecoder:
         self.tokens = torch.zeros(cfg.num_codebooks + 1, dtype=torch.long, device=self.device)
         self.recent = torch.full((cfg.ras_window,), -1, dtype=torch.long, device=self.device)
         self.graph = None
+
+    # ------------------------------------------------------------------ checkpoint
+    # Names: the fork's module lists model.layers / model.fast_layers
+    # (app/engine/graphs.py:86-88, app/engine/cpu.py:236-252) and its tables
+    # model.embeddings and model.codebook_embeddings, flat
+    # [num_codebooks * codebook_size, dim] (app/engine/hostembed.py:3-4,
+    # app/engine/streamgen.py:269); the rest are this decoder's: fast_embeddings,
+    # norm, fast_norm, output (the LM head) and fast_output.{i} (codebook i's head).
+    def state_dict(self) -> dict:
+        """The model as a checkpoint state dict (NF4 blocks in bitsandbytes'
+        serialisation, dense tensors as they are)."""
+        cfg = self.cfg
+        sd = {}
+        for i, blk in enumerate(self.slow):
+            sd.update(checkpoint.block_state_dict(blk, f"layers.{i}"))
+        for i, blk in enumerate(self.fast):
+            sd.update(checkpoint.block_state_dict(blk, f"fast_layers.{i}"))
+        sd["embeddings.weight"] = self.sem_emb
+        sd["codebook_embeddings.weight"] = self.cb_emb.reshape(cfg.num_codebooks * cfg.codebook_size, -1)
+        sd["fast_embeddings.weight"] = self.fast_emb
+        sd["norm.weight"] = self.norm_w
+        sd["fast_norm.weight"] = self.fast_norm_w
+        sd["output.weight"] = self.lm_head
+        for i, h in enumerate(self.cb_heads):
+            sd[f"fast_output.{i}.weight"] = h
+        return sd
+
+    @torch.no_grad()
+    def _load_dense(self, sd) -> None:
+        cfg, dim = self.cfg, self.cfg.slow.dim
+
+        def take(name, shape):
+            t = sd.get(name)
+            if t is None:
+                raise ValueError(f"missing {name}")
+            if tuple(t.shape) != tuple(shape):
+                raise ValueError(f"{name} is {tuple(t.shape)}, expected {tuple(shape)}")
+            return t.to(self.device, torch.bfloat16).contiguous()
+
+        self.sem_emb = take("embeddings.weight", (cfg.vocab, dim))
+        self.cb_emb = take("codebook_embeddings.weight", (cfg.num_codebooks * cfg.codebook_size, dim)).view(
+            cfg.num_codebooks, cfg.codebook_size, dim)
+        self.fast_emb = take("fast_embeddings.weight", (cfg.codebook_size, dim))
+        self.norm_w = take("norm.weight", (dim,))
+        self.fast_norm_w = take("fast_norm.weight", (dim,))
+        self.lm_head = take("output.weight", (cfg.vocab, dim))
+        self.cb_heads = [take(f"fast_output.{i}.weight", (cfg.codebook_size, dim)) for i in range(cfg.num_codebooks)]
 
     # ------------------------------------------------------------------ prompt
     @torch.no_grad()
