@@ -294,7 +294,9 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
   p.M = rows;
   p.epi = epi;
   // split-K when the caller's workspace holds the partial sums (else one pass)
-  int splits = gemm_splits(w->n_out, rows, w->k_in, current_sm_count());
+  const int sms = current_sm_count();
+  p.bt = gemm_bt(w->n_out, rows, sms);
+  int splits = gemm_splits(w->n_out, rows, w->k_in, sms);
   const size_t need = splits > 1 ? GEMM_COUNTER_BYTES + (size_t)splits * rows * w->n_out * sizeof(float) : 0;
   if (splits > 1 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256))) splits = 1;
   p.splits = splits;

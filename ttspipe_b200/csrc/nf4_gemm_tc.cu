@@ -399,8 +399,6 @@ cudaError_t launch_bt(const GemmParams& p, cudaStream_t stream) {
 
 }  // namespace
 
-// Activation rows per tile for M rows.
-static int gemm_bt(int M) { return M <= 64 ? 64 : (M <= 128 ? 128 : 256); }
 
 template <int BT, bool kSplit>
 static int gemm_ctas_per_sm() {
@@ -424,12 +422,25 @@ static int gemm_ctas_per_sm() {
   return occ[i];
 }
 
-// Split the k range when the output tiles alone cannot fill the GPU: as many
-// splits as keep every resident CTA slot busy, each of at least 4 k blocks.
-// Only 64-row tiles (M <= 64): measured, the partial sums' traffic costs more
-// than the extra CTAs win for 128- and 256-row tiles.
+// Activation rows per tile. 64-row tiles (split over k when still too few)
+// whenever their grid fits in one wave of resident CTAs: measured faster for
+// the narrow projections up to M = 1024 (1024x2560 at M = 256: 25.4 -> 16.6 us)
+// even though each weight tile is then dequantised M / 64 times; beyond one
+// wave 128 (M <= 128) or 256-row tiles are faster. Split-K is never used for
+// 128- and 256-row tiles (measured slower: the partial sums' traffic outweighs
+// the extra CTAs).
+int gemm_bt(int N, int M, int sms) {
+  if (M <= 64) return 64;
+  const long long tiles64 = (long long)((N + BM - 1) / BM) * ((M + 63) / 64);
+  if (tiles64 <= (long long)sms * gemm_ctas_per_sm<64, true>()) return 64;
+  return M <= 128 ? 128 : 256;
+}
+
+// Split the k range of 64-row tiles when the output tiles alone cannot fill
+// the GPU: as many splits as keep every resident CTA slot busy, each of at
+// least 4 k blocks.
 int gemm_splits(int N, int M, int K, int sms) {
-  const int bt = gemm_bt(M);
+  const int bt = gemm_bt(N, M, sms);
   if (bt != 64) return 1;
   const long long tiles = (long long)((N + BM - 1) / BM) * ((M + bt - 1) / bt);
   if (tiles * (long long)sizeof(int) > (long long)GEMM_COUNTER_BYTES) return 1;
@@ -447,7 +458,7 @@ size_t gemm_workspace_bytes(int N, int M, int K, int sms) {
 }
 
 cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream) {
-  const int bt = gemm_bt(p.M);
+  const int bt = p.bt;
   if (bt == 64) return p.splits > 1 ? launch_bt<64, true>(p, stream) : launch_bt<64, false>(p, stream);
   if (bt == 128) return launch_bt<128, false>(p, stream);
   return launch_bt<256, false>(p, stream);
