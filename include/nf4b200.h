@@ -197,9 +197,12 @@ int nf4b_gemm_noalloc(const nf4b_weight* w, const void* x, void* y, int rows, in
  * and one activation row x[k_in], fp32 accumulation - the fork's bf16 output
  * heads (the slow AR's LM head, the fast AR's codebook heads), which the
  * reference runs through torch. k_in in {1024, 2048, 2560, 4096}; w and x
- * 16-byte aligned.
+ * 16-byte aligned. A non-NULL bf16 `norm_weight` [k_in] RMS-normalises x first
+ * (with norm_eps), exactly as nf4b_rms_norm, inside the launch: the final norm
+ * before a head. No reference counterpart as a single call.
  */
-int nf4b_dense_gemv(const void* w, const void* x, void* y, int n_out, int k_in, void* stream);
+int nf4b_dense_gemv(const void* w, const void* x, void* y, int n_out, int k_in, const void* norm_weight,
+                    float norm_eps, void* stream);
 
 /*
  * Draw one token id from a bf16 logit row, on the device (graph-capturable):

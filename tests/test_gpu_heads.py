@@ -29,6 +29,19 @@ def test_dense_head_matches_the_exact_product(n, k):
     assert np.all(np.abs(got - want) <= ulp + 1e-6 * np.sqrt((want ** 2).mean()))
 
 
+@pytest.mark.parametrize("n,k", [(4096, 2560), (155136, 2560), (100, 1024)])
+def test_dense_head_with_fused_norm_equals_norm_then_head(n, k):
+    from ttspipe_b200 import fusedops
+
+    w = randn_bf16((n, k), seed=n + 3 * k, device="cuda", std=0.02)
+    x = randn_bf16((k,), seed=k + 1, device="cuda") * 4
+    g = torch.Generator().manual_seed(k)
+    nw = (1.0 + 0.1 * torch.randn(k, generator=g)).to(torch.bfloat16).cuda()
+    want = heads.dense_linear(w, fusedops.rms_norm(x.view(1, k), nw, 1e-6))
+    got = heads.dense_linear(w, x, norm=(nw, 1e-6))
+    assert torch.equal(got, want)
+
+
 @pytest.mark.parametrize("vocab,scale", [(155136, 3.0), (4096, 2.0), (100, 1.0), (2049, 5.0)])
 def test_sampler_draws_the_oracles_token(vocab, scale):
     logits = randn_bf16((vocab,), seed=vocab, device="cuda", std=scale)

@@ -109,7 +109,7 @@ def _declare(lib) -> None:
         "nf4b_gemm_ex": (i32, [wp, vp, vp, i32, i32, vp, vp, sz, ctypes.POINTER(GemmOpts), vp]),
         "nf4b_gemm_gated": (i32, [wp, wp, vp, vp, i32, vp, sz, ctypes.POINTER(GemmOpts), vp]),
         "nf4b_gemv_chain": (i32, [ctypes.POINTER(ChainJob), i32, i32, vp, sz, vp]),
-        "nf4b_dense_gemv": (i32, [vp, vp, vp, i32, i32, vp]),
+        "nf4b_dense_gemv": (i32, [vp, vp, vp, i32, i32, vp, f32, vp]),
         "nf4b_sample": (i32, [vp, i32, ctypes.c_float, ctypes.c_float, i32, ctypes.c_uint64, vp, vp, vp, sz, vp]),
         "nf4b_sample_workspace_size": (sz, [i32]),
         "nf4b_gemv_chain_workspace_size": (sz, [ctypes.POINTER(ChainJob), i32, i32]),

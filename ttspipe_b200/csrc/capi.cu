@@ -418,8 +418,11 @@ extern "C" int nf4b_gemv_chain(const nf4b_chain_job* jobs, int n_jobs, int rows,
   return launch_status(launch_gemv_chain(cp, reinterpret_cast<cudaStream_t>(stream)), "nf4 gemv chain launch");
 }
 
-extern "C" int nf4b_dense_gemv(const void* w, const void* x, void* y, int n_out, int k_in, void* stream) {
+extern "C" int nf4b_dense_gemv(const void* w, const void* x, void* y, int n_out, int k_in, const void* norm_weight,
+                               float norm_eps, void* stream) {
   if (w == nullptr || x == nullptr || y == nullptr) return fail(NF4B_ERR_ARG, "null pointer");
+  if (norm_weight != nullptr && (!aligned(norm_weight, 2) || !(norm_eps >= 0.f)))
+    return fail(NF4B_ERR_ARG, "norm weight not 2-byte aligned or eps < 0");
   if (n_out <= 0) return fail(NF4B_ERR_SHAPE, "n_out must be positive (got %d)", n_out);
   if (k_in != 1024 && k_in != 2048 && k_in != 2560 && k_in != 4096)
     return fail(NF4B_ERR_SHAPE, "k_in %d is not one of 1024, 2048, 2560, 4096", k_in);
@@ -428,6 +431,7 @@ extern "C" int nf4b_dense_gemv(const void* w, const void* x, void* y, int n_out,
   if (st) return st;
   return launch_status(launch_dense_gemv(static_cast<const uint16_t*>(w), static_cast<const uint16_t*>(x),
                                          static_cast<uint16_t*>(y), n_out, k_in, current_sm_count(),
+                                         static_cast<const uint16_t*>(norm_weight), norm_eps,
                                          reinterpret_cast<cudaStream_t>(stream)),
                        "dense gemv launch");
 }

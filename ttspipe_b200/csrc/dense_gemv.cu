@@ -8,7 +8,9 @@
 // lane reading 16 contiguous bytes per load so a warp's load covers 512
 // contiguous bytes of the row. Each warp keeps the next row's loads in flight
 // while it reduces the current one (register double buffer); x is staged in
-// shared memory (k_in <= 8192).
+// shared memory (k_in <= 4096), RMS-normalised there first when a norm weight
+// is given (nf4b_rms_norm's arithmetic: the fast AR's norm before each
+// codebook head, app/engine/graphs.py:205-217).
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -23,8 +25,11 @@ constexpr int kDThreads = kDWarps * 32;
 template <int C>  // 512-byte column chunks per row: k_in = 256 * C
 __global__ void __launch_bounds__(kDThreads, 1) dense_gemv_kernel(const uint16_t* __restrict__ w,
                                                                   const uint16_t* __restrict__ x,
-                                                                  uint16_t* __restrict__ y, int n_out) {
+                                                                  uint16_t* __restrict__ y, int n_out,
+                                                                  const uint16_t* __restrict__ norm_w,
+                                                                  float norm_eps) {
   __shared__ __align__(16) uint4 xs[C * 32];
+  __shared__ double red[kDWarps];
   const int lane = threadIdx.x & 31;
   const long long gw = (long long)blockIdx.x * kDWarps + (threadIdx.x >> 5);
   const long long W = (long long)gridDim.x * kDWarps;
@@ -41,6 +46,7 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_gemv_kernel(const uint16_t
   pdl_wait();
   for (int i = threadIdx.x; i < C * 32; i += kDThreads) xs[i] = reinterpret_cast<const uint4*>(x)[i];
   __syncthreads();
+  if (norm_w != nullptr) rms_normalise_staged<kDThreads>(reinterpret_cast<uint16_t*>(xs), 1, K, norm_w, norm_eps, red);
   pdl_launch_dependents();
   for (; r < n_out; r += W) {
     const long long rn = r + W;
@@ -69,7 +75,8 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_gemv_kernel(const uint16_t
 }
 
 template <int C>
-cudaError_t launch_c(const uint16_t* w, const uint16_t* x, uint16_t* y, int n_out, int sms, cudaStream_t stream) {
+cudaError_t launch_c(const uint16_t* w, const uint16_t* x, uint16_t* y, int n_out, int sms, const uint16_t* norm_w,
+                     float norm_eps, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   long long ctas = ((long long)n_out + kDWarps - 1) / kDWarps;
   if (ctas > sms) ctas = sms;
@@ -81,18 +88,18 @@ cudaError_t launch_c(const uint16_t* w, const uint16_t* x, uint16_t* y, int n_ou
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, dense_gemv_kernel<C>, w, x, y, n_out);
+  return cudaLaunchKernelEx(&cfg, dense_gemv_kernel<C>, w, x, y, n_out, norm_w, norm_eps);
 }
 
 }  // namespace
 
 cudaError_t launch_dense_gemv(const uint16_t* w, const uint16_t* x, uint16_t* y, int n_out, int k_in, int sms,
-                              cudaStream_t stream) {
+                              const uint16_t* norm_w, float norm_eps, cudaStream_t stream) {
   switch (k_in / 256) {
-    case 4: return launch_c<4>(w, x, y, n_out, sms, stream);
-    case 8: return launch_c<8>(w, x, y, n_out, sms, stream);
-    case 10: return launch_c<10>(w, x, y, n_out, sms, stream);
-    case 16: return launch_c<16>(w, x, y, n_out, sms, stream);
+    case 4: return launch_c<4>(w, x, y, n_out, sms, norm_w, norm_eps, stream);
+    case 8: return launch_c<8>(w, x, y, n_out, sms, norm_w, norm_eps, stream);
+    case 10: return launch_c<10>(w, x, y, n_out, sms, norm_w, norm_eps, stream);
+    case 16: return launch_c<16>(w, x, y, n_out, sms, norm_w, norm_eps, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -188,7 +188,7 @@ cudaError_t launch_gemv_chain(const ChainParams& p, cudaStream_t stream);
 // ---- dense bf16 GEMV for the output heads (dense_gemv.cu) -----------------
 // k_in in {1024, 2048, 2560, 4096}; one activation row.
 cudaError_t launch_dense_gemv(const uint16_t* w, const uint16_t* x, uint16_t* y, int n_out, int k_in, int sms,
-                              cudaStream_t stream);
+                              const uint16_t* norm_w, float norm_eps, cudaStream_t stream);
 
 // ---- fused top-k / top-p sampler (sampler.cu) -------------------------------
 // V <= 8192 * 2048 / 64 logits (the last CTA sorts <= 8192 slice winners).

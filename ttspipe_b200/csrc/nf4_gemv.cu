@@ -233,44 +233,6 @@ __device__ __forceinline__ uint16_t gate_bf16(float v1, float v3) {
   return f2bf(__fmul_rn(s, round_bf(v3)));
 }
 
-__device__ __forceinline__ float rms_rsqrt(double ss, int width, float eps) {
-  const float t = __fadd_rn((float)(ss / (double)width), eps);
-  return (float)(1.0 / sqrt((double)t));
-}
-
-// RMS-normalise the M rows of K bf16 values staged at xr (shared memory) in
-// place with weight w, with the arithmetic of nf4b_rms_norm: fp64 sum of
-// squares (exact for bf16 inputs, so its order does not matter),
-// r = 1 / sqrt(fp32(ss / K) + eps), y = bf16(bf16(x * r) * w). Called by every
-// thread of the CTA after a barrier that made x visible; ends with a barrier.
-// `red` holds one double per warp.
-template <int THREADS>
-__device__ __forceinline__ void rms_normalise_staged(uint16_t* xr, int M, int K, const uint16_t* __restrict__ w,
-                                                     float eps, double* red) {
-  constexpr int NW = THREADS / 32;
-  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-  for (int m = 0; m < M; ++m) {
-    double ss = 0.0;
-    for (int i = threadIdx.x; i < K; i += THREADS) {
-      const double v = bf2f(xr[m * K + i]);
-      ss += v * v;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    if (lane == 0) red[wib] = ss;
-    __syncthreads();
-    double tot = 0.0;
-#pragma unroll
-    for (int k = 0; k < NW; ++k) tot += red[k];
-    const float r = rms_rsqrt(tot, K, eps);
-    for (int i = threadIdx.x; i < K; i += THREADS) {
-      const float normed = round_bf(__fmul_rn(bf2f(xr[m * K + i]), r));
-      xr[m * K + i] = f2bf(__fmul_rn(normed, bf2f(__ldg(w + i))));
-    }
-    __syncthreads();
-  }
-}
-
 // cp.async helpers (sm_80+ asynchronous global -> shared copies, tracked per
 // thread in commit groups).
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {

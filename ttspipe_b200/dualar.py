@@ -229,8 +229,8 @@ class DualARDecoder:
             for blk in self.fast:
                 y = fusedlayer.decode_block(blk, y, self.fast_freqs[i:i + 1], self.fast_mask, self.fast_pos[i])
                 assert y is not None, "a fast block fell back"
-            yn = fusedops.rms_norm(y, self.fast_norm_w, cfg.slow.norm_eps)
-            logits_i = heads.dense_linear(self.cb_heads[i], yn)
+            # fast_norm folded into the codebook head's launch
+            logits_i = heads.dense_linear(self.cb_heads[i], y, norm=(self.fast_norm_w, cfg.slow.norm_eps))
             a = heads.sample(logits_i, temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k,
                              seed=self.seed * 7919 + 10 + i, step=self.step)
             self.tokens[i + 1:i + 2].copy_(a)

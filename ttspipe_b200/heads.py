@@ -11,17 +11,20 @@ from ttspipe_b200 import _lib
 _workspaces: dict = {}
 
 
-def dense_linear(weight, x, out=None):
+def dense_linear(weight, x, out=None, norm=None):
     """``x @ weight.T`` for a bf16 weight [N, K] (K in 1024, 2048, 2560, 4096)
-    and one bf16 row x [K]; returns bf16 [N] (or writes `out`)."""
+    and one bf16 row x [K]; returns bf16 [N] (or writes `out`). `norm` =
+    (weight, eps): ``rms_norm(x) @ weight.T`` in the same launch, bit-exact to
+    ``fusedops.rms_norm`` first."""
     import torch
 
     n, k = weight.shape
     xf = x.reshape(-1)
     if out is None:
         out = torch.empty(n, dtype=torch.bfloat16, device=x.device)
+    nw, eps = (norm[0].data_ptr(), float(norm[1])) if norm is not None else (None, 0.0)
     st = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
-    _lib.check(_lib.lib().nf4b_dense_gemv(weight.data_ptr(), xf.data_ptr(), out.data_ptr(), n, k, st))
+    _lib.check(_lib.lib().nf4b_dense_gemv(weight.data_ptr(), xf.data_ptr(), out.data_ptr(), n, k, nw, eps, st))
     return out
 
 
