@@ -203,6 +203,11 @@ int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* 
   p.offset3 = gated ? w3->offset : 0.f;
   p.gated = gated ? 1 : 0;
   p.su = su;
+  // The register-fed pair kernel reads 32-byte pieces of the packed weights.
+  p.reg = (pairs && su == 2 && rows <= 2 && aligned(w->packed, 32) && (!gated || aligned(w3->packed, 32)) &&
+           (long long)w->n_out * (w->k_in / 64) < (1LL << 31))
+              ? 1
+              : 0;
   p.x_staged = (pairs && (long long)rows * w->k_in * 2 <= GEMV_PAIR_X_MAX) ? 1 : 0;
   p.norm_w = opts ? static_cast<const uint16_t*>(opts->norm_weight) : nullptr;
   p.norm_eps = opts ? opts->norm_eps : 0.f;
@@ -332,6 +337,9 @@ int build_chain(const nf4b_chain_job* jobs, int n_jobs, int rows, ChainParams* c
   if (rows < 1 || rows > 4) return fail(NF4B_ERR_SHAPE, "the GEMV chain serves 1..4 rows (got %d)", rows);
   cp->n_jobs = n_jobs;
   cp->M = rows;
+  // The register-fed chain (as the separate calls it must equal) serves rows
+  // <= 2 when every job's packed weights are 32-byte aligned.
+  cp->reg = rows <= 2 ? 1 : 0;
   for (int i = 0; i < n_jobs; ++i) {
     const nf4b_chain_job& jb = jobs[i];
     int st = check_weight(jb.w);
@@ -369,6 +377,11 @@ int build_chain(const nf4b_chain_job* jobs, int n_jobs, int rows, ChainParams* c
         (J.gated && !make_map_2d(&J.wmap3, CU_TENSOR_MAP_DATA_TYPE_UINT8, jb.w3->packed, rb, (uint64_t)w->n_out,
                                  rb, 128, 16, CU_TENSOR_MAP_SWIZZLE_NONE)))
       return fail(NF4B_ERR_ARG, "job %d: cannot describe the weight to the TMA unit", i);
+    J.packed = w->packed;
+    J.packed3 = J.gated ? jb.w3->packed : nullptr;
+    if (!aligned(w->packed, 32) || (J.gated && !aligned(jb.w3->packed, 32)) ||
+        (long long)w->n_out * (w->k_in / 64) >= (1LL << 31))
+      cp->reg = 0;
     J.a8 = w->absmax_code;
     J.absmax = w->absmax;
     J.code2 = w->code2;

@@ -135,16 +135,19 @@ __device__ __forceinline__ float rsqrt_exact(double ss, int width, float eps) {
 // squares (exact for bf16 inputs, so its order does not matter),
 // r = 1 / sqrt(fp32(ss / K) + eps), y = bf16(bf16(x * r) * w). Called by every
 // thread of the CTA after a barrier that made x visible; ends with a barrier.
-// `red` holds one double per warp.
-template <int THREADS>
+// `red` holds one double per warp. kPadded: row m starts at element
+// m * row_stride and every 64 elements are followed by 8 elements of padding.
+template <int THREADS, bool kPadded = false>
 __device__ __forceinline__ void rms_normalise_staged(uint16_t* xr, int M, int K, const uint16_t* __restrict__ w,
-                                                     float eps, double* red) {
+                                                     float eps, double* red, int row_stride = 0) {
   constexpr int NW = THREADS / 32;
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int rs = kPadded ? row_stride : K;
+  auto at = [&](int m, int i) -> uint16_t& { return xr[m * rs + (kPadded ? i + ((i >> 6) << 3) : i)]; };
   for (int m = 0; m < M; ++m) {
     double ss = 0.0;
     for (int i = threadIdx.x; i < K; i += THREADS) {
-      const double v = bf2f(xr[m * K + i]);
+      const double v = bf2f(at(m, i));
       ss += v * v;
     }
 #pragma unroll
@@ -156,8 +159,8 @@ __device__ __forceinline__ void rms_normalise_staged(uint16_t* xr, int M, int K,
     for (int k = 0; k < NW; ++k) tot += red[k];
     const float r = rsqrt_exact(tot, K, eps);
     for (int i = threadIdx.x; i < K; i += THREADS) {
-      const float normed = round_bf(__fmul_rn(bf2f(xr[m * K + i]), r));
-      xr[m * K + i] = f2bf(__fmul_rn(normed, bf2f(__ldg(w + i))));
+      const float normed = round_bf(__fmul_rn(bf2f(at(m, i)), r));
+      at(m, i) = f2bf(__fmul_rn(normed, bf2f(__ldg(w + i))));
     }
     __syncthreads();
   }

@@ -45,6 +45,10 @@ constexpr int GEMV_PAIR_X_MAX = NF4B_GEMV_PAIR_X_KB * 1024;
 constexpr int GEMV_PAIR_SMEM_MAX = GEMV_PAIR_X_OFFSET + GEMV_PAIR_X_MAX;
 static_assert(GEMV_PAIR_W_OFFSET % 1024 == 0, "TMA boxes must be aligned");
 static_assert(GEMV_PAIR_SMEM_MAX <= 227 * 1024, "pair kernel shared memory exceeds one CTA's limit");
+// Register-fed pair kernel: the pair table, then x of <= 2 rows with 16 bytes
+// of padding per 128 and 64 per row.
+constexpr int GEMV_REG_SMEM_MAX = GEMV_LUT_BYTES + GEMV_PAIR_X_MAX * 9 / 8 + 128;
+static_assert(GEMV_REG_SMEM_MAX <= 227 * 1024, "register-fed pair kernel shared memory exceeds one CTA's limit");
 constexpr int GEMV_MAX_ROWS = 32;              // activation rows one launch takes
 // The workspace starts with a fixed-size region of per-tile arrival counters,
 // so calls on weights of different shapes never alias one another's counters
@@ -93,6 +97,7 @@ struct alignas(64) GemvParams {
   float offset3;
   int gated;
   int su;        // pair kernel: 128-code sub-units per unit (1 or 2)
+  int reg;       // su == 2, rows <= 2: the register-fed pair kernel (weights loaded straight into registers)
   int x_staged;  // pair kernel: x is copied whole into shared memory first
   const uint16_t* norm_w;  // pair kernel, staged x: RMS-normalise x with this weight first (or null)
   float norm_eps;
@@ -153,6 +158,8 @@ constexpr long long CHAIN_MAX_TILES = GEMV_MAX_TILES - CHAIN_DONE_INTS;
 struct alignas(64) ChainJob {
   CUtensorMap wmap;   // packed W, boxes of 128 bytes x 16 rows
   CUtensorMap wmap3;  // gated pair: W3
+  const uint8_t* packed;   // the register-fed chain reads the packed weights directly
+  const uint8_t* packed3;
   const uint8_t* a8;
   const float* absmax;
   const float* code2;
@@ -174,6 +181,7 @@ struct alignas(64) ChainJob {
 struct alignas(64) ChainParams {
   int n_jobs;
   int M;
+  int reg;  // rows <= 2 and every job's weights 32-byte aligned: the register-fed chain
   int warps_total;
   float* partial;
   int* counters;

@@ -35,6 +35,8 @@
 // the first weight loads are issued before `griddepcontrol.wait`, overlapping
 // the previous kernel's tail; x, the workspace and y are touched only after it.
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "tmap.cuh"
@@ -747,6 +749,271 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
 }
 
 // ---------------------------------------------------------------------------
+// register-fed pair kernel: units of 16 rows x 256 codes, activation rows <= 2
+// ---------------------------------------------------------------------------
+//
+// The decode case (1 or 2 activation rows, blocksize 64, k_in % 256 == 0). The
+// units, runs and the split-tile protocol are the pair kernel's (SU = 2), but
+// the weights skip shared memory: lane (g, t) loads 64-block t of the unit for
+// rows g and g + 8 with one 256-bit load each straight into registers, three
+// units in flight per warp. Shared memory then carries only the pair table,
+// the scale codes' code2 values and x, which is what bounds the pair kernel's
+// consumer (its TMA ring costs a shared-memory write and a read per weight byte).
+//
+// MMA columns are (activation row, block): column 4m + b carries x of row m
+// over block b of the unit, so one MMA chain keeps the four blocks' sums apart
+// and each gets its own scale after the unit. Lane (g, t) holds columns 2t and
+// 2t + 1 - activation row t >> 1, blocks 2(t & 1) and 2(t & 1) + 1 - and
+// supplies x for column g (row g >> 2, block g & 3) when g & 3 == t. Lanes t
+// and t ^ 1 hold a row's two half-sums; they are added when a tile is finished.
+//
+// Shared memory: the pair table (entry e's 32 per-lane copies at e * 256), the
+// code2 value of scale code e at e * 256 + 128 + 4 * (2g + (t & 1)) (16 copies,
+// so a warp's lookups never conflict; W3's at + 192), then x with 16 bytes of
+// padding after every 128 (one 64-block), so the four x lanes of a load hit
+// different banks.
+constexpr int kRegDepth = 3;  // units in flight per warp
+
+__host__ __device__ constexpr int reg_x_row_bytes(int K) { return K * 9 / 4 + 64; }
+
+struct RegSlot {
+  uint32_t wa[8], wb[8];  // block t of the unit, rows g and g + 8
+  uint32_t qa, qb;        // nested: the unit's four scale codes of rows g, g + 8; plain: block 2(t & 1)'s scale
+  uint32_t sa, sb;        // nested: the rows' second-level scale; plain: block 2(t & 1) + 1's scale
+};
+
+__device__ __forceinline__ void ld_stream_u8(const void* p, uint32_t (&v)[8]) {
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "l"(p));
+}
+
+template <bool kGated, bool kNested>
+__global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
+    nf4_gemv_reg_kernel(const __grid_constant__ GemvParams p) {
+  constexpr int kT = GEMV_PAIR_WARPS * 32;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ double norm_red[GEMV_PAIR_WARPS];
+  const uint8_t* lut = smem;
+  uint8_t* xs = smem + GEMV_LUT_BYTES;
+
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * GEMV_PAIR_WARPS + (threadIdx.x >> 5);
+  const bool active = gw < p.warps_total;
+  const int u0 = active ? gw * p.uq + min(gw, p.ur) : 0;
+  const int u1 = active ? u0 + p.uq + (gw < p.ur ? 1 : 0) : 0;
+  const int g = lane >> 2, t = lane & 3;
+  const int B = p.blocks_per_tile;  // 256-code units per row tile and half
+  const int per_tile = kGated ? 2 * B : B;
+  const int N = p.N, K = p.K, M = p.M;
+  const int nblk = K >> 6;  // 64-blocks per weight row
+  const int bs2 = p.bs2_shift;
+  constexpr bool nested = kNested;
+  const int xrow = reg_x_row_bytes(K);
+
+  // Load cursor: tile lt, half lh, unit lk; rows past n_out re-read row
+  // n_out - 1 (their outputs are never stored).
+  int lt = u0 / per_tile, lk = u0 - lt * per_tile, lh = 0;
+  if (kGated && lk >= B) {
+    lh = 1;
+    lk -= B;
+  }
+  int ct = lt, ck = lk, ch = lh;
+  // first 64-block of rows g and g + 8 (n_out * k_in / 64 < 2^31 is checked on the host)
+  int oa = 0, ob = 0;
+  auto set_rows = [&](int rt) {
+    oa = min(rt * 16 + g, N - 1) * nblk;
+    ob = min(rt * 16 + g + 8, N - 1) * nblk;
+  };
+  set_rows(lt);
+  auto load = [&](RegSlot& s) {
+    const uint8_t* pw = (kGated && lh) ? p.packed3 : p.packed;
+    const uint8_t* pq = (kGated && lh) ? p.a8_3 : p.a8;
+    const float* ps = (kGated && lh) ? p.absmax3 : p.absmax;
+    const int ba = oa + lk * 4, bb = ob + lk * 4;  // the unit's first block in rows g, g + 8
+    ld_stream_u8(pw + (size_t)ba * 32 + t * 32, s.wa);
+    ld_stream_u8(pw + (size_t)bb * 32 + t * 32, s.wb);
+    if (nested) {
+      s.qa = __ldg(reinterpret_cast<const uint32_t*>(pq + ba));
+      s.qb = __ldg(reinterpret_cast<const uint32_t*>(pq + bb));
+      s.sa = __float_as_uint(__ldg(ps + (ba >> bs2)));
+      s.sb = __float_as_uint(__ldg(ps + (bb >> bs2)));
+    } else {
+      const float2 fa = __ldg(reinterpret_cast<const float2*>(ps + ba + 2 * (t & 1)));
+      const float2 fb = __ldg(reinterpret_cast<const float2*>(ps + bb + 2 * (t & 1)));
+      s.qa = __float_as_uint(fa.x);
+      s.sa = __float_as_uint(fa.y);
+      s.qb = __float_as_uint(fb.x);
+      s.sb = __float_as_uint(fb.y);
+    }
+    if (++lk == B) {
+      lk = 0;
+      if (kGated && lh == 0) {
+        lh = 1;
+      } else {
+        lh = 0;
+        ++lt;
+        set_rows(lt);
+      }
+    }
+  };
+
+  RegSlot sl[kRegDepth];
+#pragma unroll
+  for (int d = 0; d < kRegDepth; ++d)
+    if (u0 + d < u1) load(sl[d]);
+
+  // The pair table, built while the first units are in flight. Thread i
+  // (< 512) owns half i & 1 of entry i >> 1 and that entry's code2 copies (W,
+  // or W3 of a gated pair): the code2 value is requested now and its copies
+  // stored after the dependency wait, so no thread reaches the wait behind a
+  // global load.
+  static_assert(kT == 512, "one table entry half per thread");
+  const int le = threadIdx.x >> 1, lhalf = threadIdx.x & 1;
+  const float* lc2 = lhalf ? p.code2_3 : p.code2;
+  const bool c2_mine = nested && lc2 != nullptr;
+  const float c2v = c2_mine ? __ldg(lc2 + le) : 0.f;
+  {
+    const uint32_t v = pack_bf16x2(nf4_code_imm((uint32_t)le >> 4), nf4_code_imm((uint32_t)le & 15u));
+    uint4* dst = reinterpret_cast<uint4*>(smem + le * 256 + lhalf * 64);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(v, v, v, v);
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+  if (c2_mine) {
+    float4* cd = reinterpret_cast<float4*>(smem + le * 256 + 128 + lhalf * 64);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) cd[j] = make_float4(c2v, c2v, c2v, c2v);
+  }
+  // x, written by earlier work on the stream, staged with the padding.
+  {
+    const int n16 = K >> 3;
+    for (int m = 0; m < M; ++m) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.x) + (size_t)m * n16;
+      for (int c = threadIdx.x; c < n16; c += kT)
+        *reinterpret_cast<uint4*>(xs + m * xrow + c * 16 + (c >> 3) * 16) = __ldcg(src + c);
+    }
+  }
+  __syncthreads();
+  if (p.norm_w != nullptr)
+    rms_normalise_staged<kT, true>(reinterpret_cast<uint16_t*>(xs), M, K, p.norm_w, p.norm_eps, norm_red,
+                                   xrow / 2);
+
+  const uint32_t lane_base = (uint32_t)lane * 4u;
+  const uint32_t c2_base = 128u + (uint32_t)(2 * g + (t & 1)) * 4u;
+  const uint32_t qsel0 = 0x5504u | ((uint32_t)(2 * (t & 1)) << 4);
+  const uint32_t qsel1 = 0x5504u | ((uint32_t)(2 * (t & 1) + 1) << 4);
+  const int xtok = g >> 2;
+  const bool xlane = (xtok < M) && ((g & 3) == t);
+  const uint8_t* xb = xs + (xlane ? xtok : 0) * xrow + t * 144;
+  const int tok = (t & 1) ? 7 : (t >> 1);  // the activation row this lane publishes (7: none)
+
+  float acc_a = 0.f, acc_b = 0.f;    // W (or W1): rows g, g + 8
+  float acc3_a = 0.f, acc3_b = 0.f;  // gated pair: W3
+  int split_a = -1, split_b = -1, old_a = 0, old_b = 0;
+  auto compute = [&](const RegSlot& s, int u) {
+    const int rt = ct, kb = ck, hh = ch;
+    if (++ck == B) {
+      ck = 0;
+      if (kGated && ch == 0) {
+        ch = 1;
+      } else {
+        ch = 0;
+        ++ct;
+      }
+    }
+    float s0a, s1a, s0b, s1b;
+    if (nested) {
+      const uint32_t cb = c2_base + ((kGated && hh) ? 64u : 0u);
+      const float off = (kGated && hh) ? p.offset3 : p.offset;
+      const float s2a = __uint_as_float(s.sa), s2b = __uint_as_float(s.sb);
+      s0a = nested_scale(*reinterpret_cast<const float*>(lut + __byte_perm(s.qa, cb, qsel0)), s2a, off);
+      s1a = nested_scale(*reinterpret_cast<const float*>(lut + __byte_perm(s.qa, cb, qsel1)), s2a, off);
+      s0b = nested_scale(*reinterpret_cast<const float*>(lut + __byte_perm(s.qb, cb, qsel0)), s2b, off);
+      s1b = nested_scale(*reinterpret_cast<const float*>(lut + __byte_perm(s.qb, cb, qsel1)), s2b, off);
+    } else {
+      s0a = __uint_as_float(s.qa);
+      s1a = __uint_as_float(s.sa);
+      s0b = __uint_as_float(s.qb);
+      s1b = __uint_as_float(s.sb);
+    }
+    // Two independent MMA chains (even and odd k steps); x in two halves of
+    // 64 bytes (fewer live registers).
+    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+    uint4 xv[4];
+#pragma unroll
+    for (int st = 0; st < 16; ++st) {
+      if ((st & 7) == 0) {
+        if (xlane) {
+          const uint4* xr = reinterpret_cast<const uint4*>(xb + kb * 576 + (st >> 3) * 64);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) xv[j] = xr[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) xv[j] = make_uint4(0, 0, 0, 0);
+        }
+      }
+      const uint32_t w0 = s.wa[st >> 1], w1 = s.wb[st >> 1];
+      const int j0 = 2 * (st & 1);
+      const uint32_t a0 = lut_lookup(lut, w0, lut_sel(j0), lane_base);
+      const uint32_t a2 = lut_lookup(lut, w0, lut_sel(j0 + 1), lane_base);
+      const uint32_t a1 = lut_lookup(lut, w1, lut_sel(j0), lane_base);
+      const uint32_t a3 = lut_lookup(lut, w1, lut_sel(j0 + 1), lane_base);
+      const uint4& xq = xv[(st >> 1) & 3];
+      const uint32_t b0 = (st & 1) ? xq.z : xq.x;
+      const uint32_t b1 = (st & 1) ? xq.w : xq.y;
+      if (st & 1)
+        mma_bf16_16816(d1, a0, a1, a2, a3, b0, b1);
+      else
+        mma_bf16_16816(d0, a0, a1, a2, a3, b0, b1);
+    }
+    // d[0] = (row g, block 2(t & 1)), d[1] = its successor; d[2], d[3] for row g + 8.
+    const float ya = fmaf(s1a, d0[1] + d1[1], (d0[0] + d1[0]) * s0a);
+    const float yb = fmaf(s1b, d0[3] + d1[3], (d0[2] + d1[2]) * s0b);
+    if (kGated && hh) {
+      acc3_a += ya;
+      acc3_b += yb;
+    } else {
+      acc_a += ya;
+      acc_b += yb;
+    }
+    if ((kb == B - 1 && (!kGated || hh == 1)) || u == u1 - 1) {
+      acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 1);
+      acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 1);
+      if (kGated) {
+        acc3_a += __shfl_xor_sync(0xffffffffu, acc3_a, 1);
+        acc3_b += __shfl_xor_sync(0xffffffffu, acc3_b, 1);
+      }
+      const float v[2][2] = {{acc_a, acc_b}, {acc3_a, acc3_b}};
+      int old = 0;
+      if (publish_pair_tile<kGated>(p, rt, u0, u1, gw, g, tok, lane, v, old)) {
+        if (split_a < 0) {
+          split_a = rt;
+          old_a = old;
+        } else {
+          split_b = rt;
+          old_b = old;
+        }
+      }
+      acc_a = acc_b = acc3_a = acc3_b = 0.f;
+    }
+  };
+
+  for (int u = u0; u < u1; u += kRegDepth) {
+#pragma unroll
+    for (int d = 0; d < kRegDepth; ++d) {
+      if (u + d < u1) {
+        compute(sl[d], u + d);
+        if (u + d + kRegDepth < u1) load(sl[d]);
+      }
+    }
+  }
+  if (split_a >= 0) finish_split_tile<kGated>(p, split_a, old_a, g, tok, lane);
+  if (split_b >= 0) finish_split_tile<kGated>(p, split_b, old_b, g, tok, lane);
+}
+
+// ---------------------------------------------------------------------------
 // block kernel: units of 16 rows x 64 codes, up to 4 column tiles of 8 rows
 // ---------------------------------------------------------------------------
 
@@ -1248,6 +1515,330 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Register-fed GEMV chain (rows <= 2): the register-fed pair kernel's unit
+// body, runs and split tiles per job - so every job equals the separate call
+// bit for bit - with each warp's three register slots running straight
+// across job boundaries. At one activation row a warp owns 1-5 units of a
+// decode projection, so most of the next job's weights are in flight while
+// the CTA waits at the boundary. Job boundaries as in the chain above (one
+// release add per CTA and job, a bounded wait for the grid, x and the code2
+// copies staged in one round trip). A warp's unit count per job varies, so
+// the slot of a job's first unit is only known at run time; the unit loop
+// dispatches on it to one of three copies of the body, which keeps the slots
+// in registers.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
+    nf4_gemv_reg_chain_kernel(const __grid_constant__ ChainParams p) {
+  constexpr int kT = GEMV_PAIR_WARPS * 32;
+  constexpr int XR = (GEMV_PAIR_X_MAX / 16 + kT - 1) / kT;  // x uint4s per thread at most
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ double red[GEMV_PAIR_WARPS];
+  __shared__ int s_ok;
+  const uint8_t* lut = smem;
+  uint8_t* xs = smem + GEMV_LUT_BYTES;
+
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * GEMV_PAIR_WARPS + (threadIdx.x >> 5);
+  const int g = lane >> 2, t = lane & 3;
+  const int M = p.M, n_jobs = p.n_jobs;
+  int* done = p.counters + (GEMV_MAX_TILES - CHAIN_DONE_INTS);
+  int* exit_ctr = done + (CHAIN_DONE_INTS - 1);
+  if (threadIdx.x == 0) s_ok = 1;
+
+  auto run_of = [&](int j, int& a, int& b) {
+    const ChainJob& J = p.jobs[j];
+    a = gw * J.uq + min(gw, J.ur);
+    b = a + J.uq + (gw < J.ur ? 1 : 0);
+  };
+
+  // Load cursor: job lj, unit lu of this warp's run [lu, lend) in it, and the
+  // unit's tile lt, half lh, k unit lk; oa / ob = first 64-block of rows g, g + 8.
+  int lj = -1, lu = 0, lend = 0, lt = 0, lh = 0, lk = 0, oa = 0, ob = 0;
+  auto set_rows = [&]() {
+    const ChainJob& J = p.jobs[lj];
+    const int nblk = J.K >> 6;
+    oa = min(lt * 16 + g, J.N - 1) * nblk;
+    ob = min(lt * 16 + g + 8, J.N - 1) * nblk;
+  };
+  auto next_job = [&]() {
+    while (++lj < n_jobs) {
+      run_of(lj, lu, lend);
+      if (lu < lend) {
+        const ChainJob& J = p.jobs[lj];
+        const int per_tile = J.gated ? 2 * J.B : J.B;
+        lt = lu / per_tile;
+        lk = lu - lt * per_tile;
+        lh = 0;
+        if (J.gated && lk >= J.B) {
+          lh = 1;
+          lk -= J.B;
+        }
+        set_rows();
+        return;
+      }
+    }
+  };
+  next_job();
+  auto load = [&](RegSlot& s) {
+    if (lj >= n_jobs) return;
+    const ChainJob& J = p.jobs[lj];
+    const bool h3 = J.gated && lh;
+    const uint8_t* pw = h3 ? J.packed3 : J.packed;
+    const int ba = oa + lk * 4, bb = ob + lk * 4;
+    ld_stream_u8(pw + (size_t)ba * 32 + t * 32, s.wa);
+    ld_stream_u8(pw + (size_t)bb * 32 + t * 32, s.wb);
+    const float* ps = h3 ? J.absmax3 : J.absmax;
+    if (J.nested) {
+      const uint8_t* pq = h3 ? J.a8_3 : J.a8;
+      s.qa = __ldg(reinterpret_cast<const uint32_t*>(pq + ba));
+      s.qb = __ldg(reinterpret_cast<const uint32_t*>(pq + bb));
+      s.sa = __float_as_uint(__ldg(ps + (ba >> J.bs2_shift)));
+      s.sb = __float_as_uint(__ldg(ps + (bb >> J.bs2_shift)));
+    } else {
+      const float2 fa = __ldg(reinterpret_cast<const float2*>(ps + ba + 2 * (t & 1)));
+      const float2 fb = __ldg(reinterpret_cast<const float2*>(ps + bb + 2 * (t & 1)));
+      s.qa = __float_as_uint(fa.x);
+      s.sa = __float_as_uint(fa.y);
+      s.qb = __float_as_uint(fb.x);
+      s.sb = __float_as_uint(fb.y);
+    }
+    if (++lu == lend) {
+      next_job();
+      return;
+    }
+    if (++lk == J.B) {
+      lk = 0;
+      if (J.gated && lh == 0) {
+        lh = 1;
+      } else {
+        lh = 0;
+        ++lt;
+        set_rows();
+      }
+    }
+  };
+
+  RegSlot sl[kRegDepth];
+#pragma unroll
+  for (int d = 0; d < kRegDepth; ++d)
+    if (lj == 0) load(sl[d]);
+  for (int i = threadIdx.x; i < 512; i += kT) {
+    const int e = i >> 1, half = i & 1;
+    const uint32_t v = pack_bf16x2(nf4_code_imm((uint32_t)e >> 4), nf4_code_imm((uint32_t)e & 15u));
+    uint4* dst = reinterpret_cast<uint4*>(smem + e * 256 + half * 64);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(v, v, v, v);
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+
+  const uint32_t lane_base = (uint32_t)lane * 4u;
+  const uint32_t c2_base = 128u + (uint32_t)(2 * g + (t & 1)) * 4u;
+  const uint32_t qsel0 = 0x5504u | ((uint32_t)(2 * (t & 1)) << 4);
+  const uint32_t qsel1 = 0x5504u | ((uint32_t)(2 * (t & 1) + 1) << 4);
+  const int xtok = g >> 2;
+  const bool xlane = (xtok < M) && ((g & 3) == t);
+  const int tok = (t & 1) ? 7 : (t >> 1);
+  for (int j = 0; j < n_jobs; ++j) {
+    const ChainJob& J = p.jobs[j];
+    // ---- job boundary: every CTA has stored its tiles of job j - 1
+    if (j > 0 && threadIdx.x == 0) {
+      if (!mbar_free_wait_count(done + (j - 1), (int)gridDim.x)) s_ok = 0;
+    }
+    __syncthreads();
+    if (!s_ok) break;
+    const int K = J.K, xrow = reg_x_row_bytes(K);
+    {
+      // x (padded) and the code2 copies in one round trip
+      const int n16 = K >> 3, tot16 = M * n16;
+      const uint4* src = reinterpret_cast<const uint4*>(J.x);
+      const int e = threadIdx.x >> 1, half = threadIdx.x & 1;
+      const float* c2 = half ? J.code2_3 : J.code2;
+      const bool c2_here = J.nested && threadIdx.x < 512 && (half == 0 || J.gated);
+      const float c = c2_here ? __ldcg(c2 + e) : 0.f;
+      for (int r0 = 0; r0 < XR; r0 += 3) {  // three x loads in flight per thread (24 KB per CTA)
+        uint4 xv[3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+          const int i = threadIdx.x + (r0 + r) * kT;
+          if (i < tot16) xv[r] = __ldcg(src + i);
+        }
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+          const int i = threadIdx.x + (r0 + r) * kT;
+          if (i < tot16) {
+            const int m = i / n16, cc = i - m * n16;
+            *reinterpret_cast<uint4*>(xs + m * xrow + cc * 16 + (cc >> 3) * 16) = xv[r];
+          }
+        }
+      }
+      if (c2_here) {
+        float4* cd = reinterpret_cast<float4*>(smem + e * 256 + 128 + half * 64);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) cd[jj] = make_float4(c, c, c, c);
+      }
+    }
+    __syncthreads();
+    if (J.norm_w != nullptr)
+      rms_normalise_staged<kT, true>(reinterpret_cast<uint16_t*>(xs), M, K, J.norm_w, J.norm_eps, red, xrow / 2);
+
+    // ---- this warp's units of job j (the register-fed pair kernel's body),
+    // compiled separately for gated and plain jobs (fewer live registers)
+    int u0, u1;
+    run_of(j, u0, u1);
+    auto run_job = [&](auto gated_c) {
+    constexpr bool gated = decltype(gated_c)::value;
+    const int B = J.B, per_tile = gated ? 2 * B : B;
+    const bool nested = J.nested;
+    int ct = u0 / per_tile, ck = u0 - ct * per_tile, ch = 0;
+    if (gated && ck >= B) {
+      ch = 1;
+      ck -= B;
+    }
+    const uint8_t* xb = xs + (xlane ? xtok : 0) * xrow + t * 144;
+    float acc_a = 0.f, acc_b = 0.f, acc3_a = 0.f, acc3_b = 0.f;
+    int split_a = -1, split_b = -1, old_a = 0, old_b = 0;
+    auto compute = [&](const RegSlot& sv, int u) {
+      const int rt = ct, kb = ck, hh = ch;
+      if (++ck == B) {
+        ck = 0;
+        if (gated && ch == 0) {
+          ch = 1;
+        } else {
+          ch = 0;
+          ++ct;
+        }
+      }
+      float s0a, s1a, s0b, s1b;
+      if (nested) {
+        const uint32_t cb = c2_base + ((gated && hh) ? 64u : 0u);
+        const float off = (gated && hh) ? J.offset3 : J.offset;
+        const float s2a = __uint_as_float(sv.sa), s2b = __uint_as_float(sv.sb);
+        s0a = nested_scale(*reinterpret_cast<const float*>(lut + __byte_perm(sv.qa, cb, qsel0)), s2a, off);
+        s1a = nested_scale(*reinterpret_cast<const float*>(lut + __byte_perm(sv.qa, cb, qsel1)), s2a, off);
+        s0b = nested_scale(*reinterpret_cast<const float*>(lut + __byte_perm(sv.qb, cb, qsel0)), s2b, off);
+        s1b = nested_scale(*reinterpret_cast<const float*>(lut + __byte_perm(sv.qb, cb, qsel1)), s2b, off);
+      } else {
+        s0a = __uint_as_float(sv.qa);
+        s1a = __uint_as_float(sv.sa);
+        s0b = __uint_as_float(sv.qb);
+        s1b = __uint_as_float(sv.sb);
+      }
+      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+      uint4 xv[4];
+#pragma unroll
+      for (int st = 0; st < 16; ++st) {
+        if ((st & 7) == 0) {
+          if (xlane) {
+            const uint4* xr = reinterpret_cast<const uint4*>(xb + kb * 576 + (st >> 3) * 64);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) xv[jj] = xr[jj];
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) xv[jj] = make_uint4(0, 0, 0, 0);
+          }
+        }
+        const uint32_t w0 = sv.wa[st >> 1], w1 = sv.wb[st >> 1];
+        const int j0 = 2 * (st & 1);
+        const uint32_t a0 = lut_lookup(lut, w0, lut_sel(j0), lane_base);
+        const uint32_t a2 = lut_lookup(lut, w0, lut_sel(j0 + 1), lane_base);
+        const uint32_t a1 = lut_lookup(lut, w1, lut_sel(j0), lane_base);
+        const uint32_t a3 = lut_lookup(lut, w1, lut_sel(j0 + 1), lane_base);
+        const uint4& xq = xv[(st >> 1) & 3];
+        const uint32_t b0 = (st & 1) ? xq.z : xq.x;
+        const uint32_t b1 = (st & 1) ? xq.w : xq.y;
+        if (st & 1)
+          mma_bf16_16816(d1, a0, a1, a2, a3, b0, b1);
+        else
+          mma_bf16_16816(d0, a0, a1, a2, a3, b0, b1);
+      }
+      const float ya = fmaf(s1a, d0[1] + d1[1], (d0[0] + d1[0]) * s0a);
+      const float yb = fmaf(s1b, d0[3] + d1[3], (d0[2] + d1[2]) * s0b);
+      if (gated && hh) {
+        acc3_a += ya;
+        acc3_b += yb;
+      } else {
+        acc_a += ya;
+        acc_b += yb;
+      }
+      if ((kb == B - 1 && (!gated || hh == 1)) || u == u1 - 1) {
+        acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 1);
+        acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 1);
+        acc3_a += __shfl_xor_sync(0xffffffffu, acc3_a, 1);
+        acc3_b += __shfl_xor_sync(0xffffffffu, acc3_b, 1);
+        const float v[2][2] = {{acc_a, acc_b}, {acc3_a, acc3_b}};
+        int old = 0;
+        GemvParams q;  // the split-tile helpers' view of the job, built where it is used
+        chain_as_params(J, p, q);
+        const bool split = gated ? publish_pair_tile<true>(q, rt, u0, u1, gw, g, tok, lane, v, old)
+                                 : publish_pair_tile<false>(q, rt, u0, u1, gw, g, tok, lane, v, old);
+        if (split) {
+          if (split_a < 0) {
+            split_a = rt;
+            old_a = old;
+          } else {
+            split_b = rt;
+            old_b = old;
+          }
+        }
+        acc_a = acc_b = acc3_a = acc3_b = 0.f;
+      }
+    };
+    // Slots 0..2 hold this warp's next units in order. Inside the job a slot
+    // is refilled only with a unit of the same job; the next job's units are
+    // requested after the split tiles are finished (below), so the finish
+    // never holds three slots' registers, and still in flight during the
+    // boundary wait.
+    for (int u = u0; u < u1; u += kRegDepth) {
+#pragma unroll
+      for (int d = 0; d < kRegDepth; ++d) {
+        if (u + d < u1) {
+          compute(sl[d], u + d);
+          if (u + d + kRegDepth < u1) load(sl[d]);
+        }
+      }
+    }
+    GemvParams q;
+    chain_as_params(J, p, q);
+    if (gated) {
+      if (split_a >= 0) finish_split_tile<true>(q, split_a, old_a, g, tok, lane);
+      if (split_b >= 0) finish_split_tile<true>(q, split_b, old_b, g, tok, lane);
+    } else {
+      if (split_a >= 0) finish_split_tile<false>(q, split_a, old_a, g, tok, lane);
+      if (split_b >= 0) finish_split_tile<false>(q, split_b, old_b, g, tok, lane);
+    }
+    };
+    if (J.gated)
+      run_job(std::true_type{});
+    else
+      run_job(std::false_type{});
+    // The next job's first units (up to three, into slots 0..2 in order),
+    // requested now that every slot is free: they are in flight during the
+    // boundary wait, and no slot is live while a split tile is finished.
+#pragma unroll
+    for (int d = 0; d < kRegDepth; ++d)
+      if (lj == j + 1) load(sl[d]);
+    // ---- this CTA is done with job j: count it in (release after the barrier)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(done + j) : "memory");
+    }
+  }
+  // The last CTA out re-zeroes the completion counts for the next launch.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int old = atomicAdd(exit_ctr, 1);
+    if (old == (int)gridDim.x - 1) {
+      __threadfence();
+      for (int j = 0; j < n_jobs; ++j) done[j] = 0;
+      *exit_ctr = 0;
+    }
+  }
+}
+
 template <typename Kernel>
 cudaError_t launch_kernel(Kernel kernel, const GemvParams& p, int grid, cudaStream_t stream,
                           bool* configured, int smem = GEMV_SMEM_BYTES, int smem_max = GEMV_SMEM_BYTES,
@@ -1343,33 +1934,49 @@ size_t chain_plan(ChainParams* p, int sm_count) {
 }
 
 cudaError_t launch_gemv_chain(const ChainParams& p, cudaStream_t stream) {
-  static bool configured[64] = {};
+  static bool configured[64] = {}, configured_reg[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(nf4_gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         GEMV_PAIR_SMEM_MAX);
+  if (dev >= 0 && dev < 64 && !(p.reg ? configured_reg : configured)[dev]) {
+    cudaError_t e = p.reg ? cudaFuncSetAttribute(nf4_gemv_reg_chain_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_REG_SMEM_MAX)
+                          : cudaFuncSetAttribute(nf4_gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 GEMV_PAIR_SMEM_MAX);
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    (p.reg ? configured_reg : configured)[dev] = true;
   }
   int kmax = 0;
   for (int i = 0; i < p.n_jobs; ++i) kmax = p.jobs[i].K > kmax ? p.jobs[i].K : kmax;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(p.warps_total / GEMV_PAIR_WARPS));
   cfg.blockDim = dim3(GEMV_PAIR_WARPS * 32);
-  cfg.dynamicSmemBytes = GEMV_PAIR_X_OFFSET + p.M * kmax * 2;
+  cfg.dynamicSmemBytes = p.reg ? GEMV_LUT_BYTES + p.M * reg_x_row_bytes(kmax) : GEMV_PAIR_X_OFFSET + p.M * kmax * 2;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, nf4_gemv_chain_kernel, p);
+  return p.reg ? cudaLaunchKernelEx(&cfg, nf4_gemv_reg_chain_kernel, p) : cudaLaunchKernelEx(&cfg, nf4_gemv_chain_kernel, p);
 }
 
 cudaError_t launch_gemv(const GemvParams& p, int grid, bool pairs, cudaStream_t stream) {
   static bool cfg_pair[64] = {}, cfg_gated[64] = {}, cfg_pair2[64] = {}, cfg_gated2[64] = {};
+  static bool cfg_reg[64] = {}, cfg_reg_gated[64] = {}, cfg_reg_plain[64] = {}, cfg_reg_gated_plain[64] = {};
   static bool cfg1[64] = {}, cfg2[64] = {}, cfg4[64] = {};
+  if (pairs && p.reg) {
+    const int smem = GEMV_LUT_BYTES + p.M * reg_x_row_bytes(p.K);
+    const int nt = GEMV_PAIR_WARPS * 32;
+    if (p.nested)
+      return p.gated ? launch_kernel(nf4_gemv_reg_kernel<true, true>, p, grid, stream, cfg_reg_gated, smem,
+                                     GEMV_REG_SMEM_MAX, nt)
+                     : launch_kernel(nf4_gemv_reg_kernel<false, true>, p, grid, stream, cfg_reg, smem,
+                                     GEMV_REG_SMEM_MAX, nt);
+    return p.gated ? launch_kernel(nf4_gemv_reg_kernel<true, false>, p, grid, stream, cfg_reg_gated_plain, smem,
+                                   GEMV_REG_SMEM_MAX, nt)
+                   : launch_kernel(nf4_gemv_reg_kernel<false, false>, p, grid, stream, cfg_reg_plain, smem,
+                                   GEMV_REG_SMEM_MAX, nt);
+  }
   if (pairs) {
     GemvParams q = p;
     const uint64_t rb = (uint64_t)p.K / 2;
