@@ -115,6 +115,43 @@ __device__ __forceinline__ void build_pair_lut(uint8_t* smem) {
   }
 }
 
+// The pair table with conflict-free stores: the 8 threads of a quarter warp
+// write the 8 16-byte pieces of one entry (128 contiguous bytes); the 16 code
+// values come from lanes 0..15 by shuffle. Called by whole warps.
+template <int THREADS>
+__device__ __forceinline__ void build_pair_lut_fast(uint8_t* smem) {
+  const float code = nf4_code_imm((uint32_t)(threadIdx.x & 15));
+#pragma unroll
+  for (int r = 0; r < 2048 / THREADS; ++r) {
+    const int idx = threadIdx.x + r * THREADS, e = idx >> 3, c = idx & 7;
+    const float hi_nib = __shfl_sync(0xffffffffu, code, e >> 4);
+    const float lo_nib = __shfl_sync(0xffffffffu, code, e & 15);
+    const uint32_t v = pack_bf16x2(hi_nib, lo_nib);
+    *reinterpret_cast<uint4*>(smem + e * 256 + c * 16) = make_uint4(v, v, v, v);
+  }
+}
+
+// The code2 copies of the register-fed kernels, stored conflict-free: entry
+// e's 128 bytes at e * 256 + 128 hold 16 copies of code2[e] (W), then 16 of
+// code2_3[e] (W3; W's again when there is no W3). `vals` are this thread's
+// values, loaded by load_code2_copies.
+template <int THREADS>
+__device__ __forceinline__ void load_code2_copies(const float* c2, const float* c2_3, float (&vals)[2048 / THREADS]) {
+#pragma unroll
+  for (int r = 0; r < 2048 / THREADS; ++r) {
+    const int idx = threadIdx.x + r * THREADS, e = idx >> 3, c = idx & 7;
+    vals[r] = __ldg(((c >= 4 && c2_3 != nullptr) ? c2_3 : c2) + e);
+  }
+}
+template <int THREADS>
+__device__ __forceinline__ void store_code2_copies(uint8_t* smem, const float (&vals)[2048 / THREADS]) {
+#pragma unroll
+  for (int r = 0; r < 2048 / THREADS; ++r) {
+    const int idx = threadIdx.x + r * THREADS, e = idx >> 3, c = idx & 7;
+    *reinterpret_cast<float4*>(smem + e * 256 + 128 + c * 16) = make_float4(vals[r], vals[r], vals[r], vals[r]);
+  }
+}
+
 template <int THREADS = kThreads>
 __device__ __forceinline__ void build_tables(uint8_t* smem, const GemvParams& p) {
   for (int i = threadIdx.x; i < 256 * 8; i += THREADS) {
@@ -863,29 +900,15 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   for (int d = 0; d < kRegDepth; ++d)
     if (u0 + d < u1) load(sl[d]);
 
-  // The pair table, built while the first units are in flight. Thread i
-  // (< 512) owns half i & 1 of entry i >> 1 and that entry's code2 copies (W,
-  // or W3 of a gated pair): the code2 value is requested now and its copies
-  // stored after the dependency wait, so no thread reaches the wait behind a
-  // global load.
-  static_assert(kT == 512, "one table entry half per thread");
-  const int le = threadIdx.x >> 1, lhalf = threadIdx.x & 1;
-  const float* lc2 = lhalf ? p.code2_3 : p.code2;
-  const bool c2_mine = nested && lc2 != nullptr;
-  const float c2v = c2_mine ? __ldg(lc2 + le) : 0.f;
-  {
-    const uint32_t v = pack_bf16x2(nf4_code_imm((uint32_t)le >> 4), nf4_code_imm((uint32_t)le & 15u));
-    uint4* dst = reinterpret_cast<uint4*>(smem + le * 256 + lhalf * 64);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(v, v, v, v);
-  }
+  // The pair table, built while the first units are in flight; the code2
+  // values are requested now and their copies stored after the dependency
+  // wait, so no thread reaches the wait behind a global load.
+  float c2v[2048 / kT];
+  if (nested) load_code2_copies<kT>(p.code2, kGated ? p.code2_3 : nullptr, c2v);
+  build_pair_lut_fast<kT>(smem);
   pdl_launch_dependents();
   pdl_wait();
-  if (c2_mine) {
-    float4* cd = reinterpret_cast<float4*>(smem + le * 256 + 128 + lhalf * 64);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) cd[j] = make_float4(c2v, c2v, c2v, c2v);
-  }
+  if (nested) store_code2_copies<kT>(smem, c2v);
   // x, written by earlier work on the stream, staged with the padding.
   {
     const int n16 = K >> 3;
@@ -1623,13 +1646,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
 #pragma unroll
   for (int d = 0; d < kRegDepth; ++d)
     if (lj == 0) load(sl[d]);
-  for (int i = threadIdx.x; i < 512; i += kT) {
-    const int e = i >> 1, half = i & 1;
-    const uint32_t v = pack_bf16x2(nf4_code_imm((uint32_t)e >> 4), nf4_code_imm((uint32_t)e & 15u));
-    uint4* dst = reinterpret_cast<uint4*>(smem + e * 256 + half * 64);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(v, v, v, v);
-  }
+  build_pair_lut_fast<kT>(smem);
   pdl_launch_dependents();
   pdl_wait();
 
@@ -1653,10 +1670,8 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       // x (padded) and the code2 copies in one round trip
       const int n16 = K >> 3, tot16 = M * n16;
       const uint4* src = reinterpret_cast<const uint4*>(J.x);
-      const int e = threadIdx.x >> 1, half = threadIdx.x & 1;
-      const float* c2 = half ? J.code2_3 : J.code2;
-      const bool c2_here = J.nested && threadIdx.x < 512 && (half == 0 || J.gated);
-      const float c = c2_here ? __ldcg(c2 + e) : 0.f;
+      float c2v[2048 / kT];
+      if (J.nested) load_code2_copies<kT>(J.code2, J.gated ? J.code2_3 : nullptr, c2v);
       for (int r0 = 0; r0 < XR; r0 += 3) {  // three x loads in flight per thread (24 KB per CTA)
         uint4 xv[3];
 #pragma unroll
@@ -1673,11 +1688,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
           }
         }
       }
-      if (c2_here) {
-        float4* cd = reinterpret_cast<float4*>(smem + e * 256 + 128 + half * 64);
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) cd[jj] = make_float4(c, c, c, c);
-      }
+      if (J.nested) store_code2_copies<kT>(smem, c2v);
     }
     __syncthreads();
     if (J.norm_w != nullptr)
