@@ -249,7 +249,9 @@ def step_workspace(layers, io, device):
 
 MODES = {
     "decode": "per layer wqkv, wo(+res), the gated w1/w3 pair in one launch (nf4b_gemm_gated), w2(+res): "
-              "4 launches per layer in stream order, each naming the weights of a later launch for L2 prefetch",
+              "4 launches per layer in stream order, each waiting for the previous one (programmatic "
+              "dependent launch) as dependent matmuls would; with --prefetch-distance > 0 each also names "
+              "the weights of a later launch for L2 prefetch",
     "single": "one launch per projection (w1, then w3 with the silu-gate epilogue on w1's output): "
               "5 launches per layer",
     "chain": "the same 4 matmuls per layer with the same data dependencies, issued as nf4b_gemv_chain "
@@ -553,8 +555,9 @@ def run_gpu(args):
                          "frac": round(achieved / hbm, 4), "peak_source": peak_kind,
                          "traffic": traffic,
                          "algorithmic_bytes_per_launch": STEP_BYTES // len(plan),
-                         "kernel": "nf4_gemv_pair_kernel, plain and gated (every launch of the step; "
-                                   "achieved = step bytes / step time, i.e. launch gaps included)"},
+                         "kernel": "nf4_gemv_reg_kernel (register-fed pair GEMV), plain and gated (every "
+                                   "launch of the step; achieved = step bytes / step time, i.e. launch gaps "
+                                   "included)"},
             "clocks": clock,
             "per_rank_GBps": round(per_rank, 1),
         }
