@@ -223,6 +223,36 @@ int nf4b_sample(const void* logits, int vocab, float temperature, float top_p, i
 size_t nf4b_sample_workspace_size(int vocab);
 
 /*
+ * Dual-AR frame bookkeeping on the device (graph-capturable; one small
+ * launch each instead of the framework's compare / gather / copy kernels).
+ * The token logic of the reference's decode step (app/engine/graphs.py:105-127).
+ * Embedding tables are bf16 [rows, dim] with dim % 8 == 0, 16-byte aligned;
+ * token ids are int64 and clamped to their table.
+ *
+ * nf4b_embed_rows: out row r = table row ids[r], r < n_ids.
+ *
+ * nf4b_frame_select: the repetition-aware choice of the semantic token and
+ * the fast AR's first input. main' = *high when *main is a semantic id
+ * (sem_begin <= *main < sem_begin + codebook_size) that occurs in
+ * recent[0..n_recent), else *main; tokens[0] = main'; tokens[1] = a =
+ * clamp(main' - sem_begin, 0, codebook_size - 1); h = fast_emb row a.
+ *
+ * nf4b_frame_advance: the next frame's input and counters. x = bf16(
+ * float(sem_emb row tokens[0]) + s), s = the fp32 sum in codebook order of
+ * float(cb_emb[i] row tokens[1 + i]) for i < n_codebooks (cb_emb is
+ * [n_codebooks, codebook_size, dim]); recent <- [tokens[0], recent[0..n-2]];
+ * *pos += 1; *step += 1. n_codebooks <= 32.
+ */
+int nf4b_embed_rows(const void* table, long long rows, const int64_t* ids, int n_ids, int dim, void* out,
+                    void* stream);
+int nf4b_frame_select(const int64_t* main_tok, const int64_t* high_tok, const int64_t* recent, int n_recent,
+                      long long sem_begin, long long codebook_size, int64_t* tokens, const void* fast_emb, int dim,
+                      void* h, void* stream);
+int nf4b_frame_advance(const void* sem_emb, long long vocab, const void* cb_emb, long long codebook_size,
+                       int n_codebooks, const int64_t* tokens, int dim, void* x, int64_t* recent, int n_recent,
+                       int64_t* pos, int64_t* step, void* stream);
+
+/*
  * out[n_out, k_in] = RNE_bf16(NF4[q] * scale) - bitsandbytes' dequantize_4bit
  * to bf16 (the per-element value of app/engine/nf4gemv.py:185-188 in bf16).
  */

@@ -36,6 +36,9 @@ EXPORTS = (
     "nf4b_dense_gemv",
     "nf4b_sample",
     "nf4b_sample_workspace_size",
+    "nf4b_embed_rows",
+    "nf4b_frame_select",
+    "nf4b_frame_advance",
     "nf4b_gemv_chain_workspace_size",
     "nf4b_dequantize",
     "nf4b_rms_norm",
@@ -112,6 +115,10 @@ def _declare(lib) -> None:
         "nf4b_dense_gemv": (i32, [vp, vp, vp, i32, i32, vp, f32, vp]),
         "nf4b_sample": (i32, [vp, i32, ctypes.c_float, ctypes.c_float, i32, ctypes.c_uint64, vp, vp, vp, sz, vp]),
         "nf4b_sample_workspace_size": (sz, [i32]),
+        "nf4b_embed_rows": (i32, [vp, ctypes.c_longlong, vp, i32, i32, vp, vp]),
+        "nf4b_frame_select": (i32, [vp, vp, vp, i32, ctypes.c_longlong, ctypes.c_longlong, vp, vp, i32, vp, vp]),
+        "nf4b_frame_advance": (i32, [vp, ctypes.c_longlong, vp, ctypes.c_longlong, i32, vp, i32, vp, vp, i32, vp, vp,
+                                     vp]),
         "nf4b_gemv_chain_workspace_size": (sz, [ctypes.POINTER(ChainJob), i32, i32]),
         "nf4b_gemm_workspace_size": (sz, [wp, i32]),
         "nf4b_gemm_noalloc": (i32, [wp, vp, vp, i32, i32, vp, vp]),

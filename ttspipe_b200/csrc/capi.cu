@@ -476,6 +476,58 @@ extern "C" int nf4b_sample(const void* logits, int vocab, float temperature, flo
                        "sampler launch");
 }
 
+extern "C" int nf4b_embed_rows(const void* table, long long rows, const int64_t* ids, int n_ids, int dim, void* out,
+                               void* stream) {
+  if (table == nullptr || ids == nullptr || out == nullptr) return fail(NF4B_ERR_ARG, "null pointer");
+  if (rows <= 0 || n_ids <= 0 || dim <= 0 || dim % 8)
+    return fail(NF4B_ERR_SHAPE, "embedding of %lld rows, %d ids, dim %d (dim %% 8 == 0)", rows, n_ids, dim);
+  if (!aligned(table, 16) || !aligned(out, 16) || !aligned(ids, 8))
+    return fail(NF4B_ERR_ALIGN, "table/out not 16-byte aligned or ids not 8-byte aligned");
+  int st = check_device();
+  if (st) return st;
+  return launch_status(launch_embed_rows(static_cast<const uint16_t*>(table), rows, ids, n_ids, dim,
+                                         static_cast<uint16_t*>(out), reinterpret_cast<cudaStream_t>(stream)),
+                       "embedding gather launch");
+}
+
+extern "C" int nf4b_frame_select(const int64_t* main_tok, const int64_t* high_tok, const int64_t* recent,
+                                 int n_recent, long long sem_begin, long long codebook_size, int64_t* tokens,
+                                 const void* fast_emb, int dim, void* h, void* stream) {
+  if (main_tok == nullptr || high_tok == nullptr || tokens == nullptr || fast_emb == nullptr || h == nullptr ||
+      (n_recent > 0 && recent == nullptr))
+    return fail(NF4B_ERR_ARG, "null pointer");
+  if (n_recent < 0 || codebook_size <= 0 || dim <= 0 || dim % 8)
+    return fail(NF4B_ERR_SHAPE, "recent window %d, codebook size %lld, dim %d (dim %% 8 == 0)", n_recent,
+                codebook_size, dim);
+  if (!aligned(fast_emb, 16) || !aligned(h, 16)) return fail(NF4B_ERR_ALIGN, "fast_emb/h not 16-byte aligned");
+  int st = check_device();
+  if (st) return st;
+  return launch_status(launch_frame_select(main_tok, high_tok, recent, n_recent, sem_begin, codebook_size, tokens,
+                                           static_cast<const uint16_t*>(fast_emb), dim, static_cast<uint16_t*>(h),
+                                           reinterpret_cast<cudaStream_t>(stream)),
+                       "frame select launch");
+}
+
+extern "C" int nf4b_frame_advance(const void* sem_emb, long long vocab, const void* cb_emb, long long codebook_size,
+                                  int n_codebooks, const int64_t* tokens, int dim, void* x, int64_t* recent,
+                                  int n_recent, int64_t* pos, int64_t* step, void* stream) {
+  if (sem_emb == nullptr || cb_emb == nullptr || tokens == nullptr || x == nullptr || pos == nullptr ||
+      step == nullptr || (n_recent > 0 && recent == nullptr))
+    return fail(NF4B_ERR_ARG, "null pointer");
+  if (vocab <= 0 || codebook_size <= 0 || n_codebooks < 0 || n_codebooks > FRAME_MAX_CODEBOOKS || dim <= 0 ||
+      n_recent < 0)
+    return fail(NF4B_ERR_SHAPE, "vocab %lld, codebooks %d x %lld, dim %d, recent %d", vocab, n_codebooks,
+                codebook_size, dim, n_recent);
+  if (!aligned(sem_emb, 2) || !aligned(cb_emb, 2) || !aligned(x, 2)) return fail(NF4B_ERR_ALIGN, "bf16 misaligned");
+  int st = check_device();
+  if (st) return st;
+  return launch_status(launch_frame_advance(static_cast<const uint16_t*>(sem_emb), vocab,
+                                            static_cast<const uint16_t*>(cb_emb), codebook_size, n_codebooks, tokens,
+                                            dim, static_cast<uint16_t*>(x), recent, n_recent, pos, step,
+                                            reinterpret_cast<cudaStream_t>(stream)),
+                       "frame advance launch");
+}
+
 extern "C" int nf4b_dequantize(const nf4b_weight* w, void* out, void* stream) {
   int st = check_weight(w);
   if (st) return st;

@@ -198,6 +198,17 @@ cudaError_t launch_gemv_chain(const ChainParams& p, cudaStream_t stream);
 cudaError_t launch_dense_gemv(const uint16_t* w, const uint16_t* x, uint16_t* y, int n_out, int k_in, int sms,
                               const uint16_t* norm_w, float norm_eps, cudaStream_t stream);
 
+// ---- Dual-AR frame bookkeeping (frame_ops.cu) -------------------------------
+constexpr int FRAME_MAX_CODEBOOKS = 32;
+cudaError_t launch_embed_rows(const uint16_t* table, long long rows, const int64_t* ids, int n_ids, int dim,
+                              uint16_t* out, cudaStream_t stream);
+cudaError_t launch_frame_select(const int64_t* main_tok, const int64_t* high_tok, const int64_t* recent,
+                                int n_recent, long long sem_begin, long long cb_size, int64_t* tokens,
+                                const uint16_t* fast_emb, int dim, uint16_t* h, cudaStream_t stream);
+cudaError_t launch_frame_advance(const uint16_t* sem_emb, long long vocab, const uint16_t* cb_emb, long long cb_size,
+                                 int n_cb, const int64_t* tokens, int dim, uint16_t* x, int64_t* recent,
+                                 int n_recent, int64_t* pos, int64_t* step, cudaStream_t stream);
+
 // ---- fused top-k / top-p sampler (sampler.cu) -------------------------------
 // V <= 8192 * 2048 / 64 logits (the last CTA sorts <= 8192 slice winners).
 constexpr int SAMPLER_MAX_VOCAB = 262144;

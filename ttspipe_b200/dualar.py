@@ -107,6 +107,9 @@ class DualARDecoder:
         self.x = torch.zeros(1, 1, sc.dim, dtype=torch.bfloat16, device=self.device)
         self.tokens = torch.zeros(cfg.num_codebooks + 1, dtype=torch.long, device=self.device)
         self.recent = torch.full((cfg.ras_window,), -1, dtype=torch.long, device=self.device)
+        self.main_tok = torch.zeros(1, dtype=torch.long, device=self.device)   # the two semantic draws
+        self.high_tok = torch.zeros(1, dtype=torch.long, device=self.device)
+        self.h = torch.zeros(1, 1, sc.dim, dtype=torch.bfloat16, device=self.device)  # the fast AR's input
         self.graph = None
 
     # ------------------------------------------------------------------ checkpoint
@@ -212,38 +215,36 @@ class DualARDecoder:
         x = self.slow_stack(self.x)
         hidden = fusedops.rms_norm(x, self.norm_w, cfg.slow.norm_eps)
         logits = heads.dense_linear(self.lm_head, hidden)
-        main = heads.sample(logits, temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k,
-                            seed=self.seed * 7919 + 1, step=self.step)
-        high = heads.sample(logits, temperature=cfg.high_temperature, top_p=cfg.high_top_p, top_k=cfg.top_k,
-                            seed=self.seed * 7919 + 2, step=self.step)
-        semantic = (main >= cfg.semantic_begin_id) & (main < cfg.semantic_begin_id + cfg.codebook_size)
-        repeat = (self.recent == main).any() & semantic
-        main = torch.where(repeat, high, main)
-        self.tokens[0:1].copy_(main)
+        heads.sample(logits, temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k,
+                     seed=self.seed * 7919 + 1, step=self.step, out=self.main_tok)
+        heads.sample(logits, temperature=cfg.high_temperature, top_p=cfg.high_top_p, top_k=cfg.top_k,
+                     seed=self.seed * 7919 + 2, step=self.step, out=self.high_tok)
+        L = _lib.lib()
+        st = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        dim = self.h.shape[-1]
+        # the repetition-aware choice (app/engine/graphs.py:111-116), tokens[0..1]
+        # and the fast AR's first input, in one launch
+        _lib.check(L.nf4b_frame_select(self.main_tok.data_ptr(), self.high_tok.data_ptr(), self.recent.data_ptr(),
+                                       self.recent.numel(), cfg.semantic_begin_id, cfg.codebook_size,
+                                       self.tokens.data_ptr(), self.fast_emb.data_ptr(), dim, self.h.data_ptr(), st))
         self._fast_prime(hidden)
-        a = torch.clamp(main - cfg.semantic_begin_id, min=0, max=cfg.codebook_size - 1)
-        self.tokens[1:2].copy_(a)
-        h = self.fast_emb.index_select(0, a).view(1, 1, -1)
         for i in range(1, cfg.num_codebooks):
-            y = h
+            y = self.h
             for blk in self.fast:
                 y = fusedlayer.decode_block(blk, y, self.fast_freqs[i:i + 1], self.fast_mask, self.fast_pos[i])
                 assert y is not None, "a fast block fell back"
             # fast_norm folded into the codebook head's launch
             logits_i = heads.dense_linear(self.cb_heads[i], y, norm=(self.fast_norm_w, cfg.slow.norm_eps))
-            a = heads.sample(logits_i, temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k,
-                             seed=self.seed * 7919 + 10 + i, step=self.step)
-            self.tokens[i + 1:i + 2].copy_(a)
-            h = self.fast_emb.index_select(0, a).view(1, 1, -1)
-        # next frame's input and counters
-        emb = self.sem_emb.index_select(0, self.tokens[0:1]).float()
-        codes = self.tokens[1:]
-        emb = emb + self.cb_emb[torch.arange(cfg.num_codebooks, device=self.device), codes].float().sum(0, keepdim=True)
-        self.x.copy_(emb.to(torch.bfloat16).view(1, 1, -1))
-        self.recent.copy_(torch.roll(self.recent, 1))
-        self.recent[0:1].copy_(self.tokens[0:1])
-        self.pos.add_(1)
-        self.step.add_(1)
+            tok = self.tokens[i + 1:i + 2]
+            heads.sample(logits_i, temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k,
+                         seed=self.seed * 7919 + 10 + i, step=self.step, out=tok)
+            _lib.check(L.nf4b_embed_rows(self.fast_emb.data_ptr(), self.fast_emb.shape[0], tok.data_ptr(), 1, dim,
+                                         self.h.data_ptr(), st))
+        # next frame's input (semantic + codebook embeddings) and counters, one launch
+        _lib.check(L.nf4b_frame_advance(self.sem_emb.data_ptr(), self.sem_emb.shape[0], self.cb_emb.data_ptr(),
+                                        cfg.codebook_size, cfg.num_codebooks, self.tokens.data_ptr(), dim,
+                                        self.x.data_ptr(), self.recent.data_ptr(), self.recent.numel(),
+                                        self.pos.data_ptr(), self.step.data_ptr(), st))
 
     def capture(self) -> None:
         """Record one frame as a CUDA graph (state lives in device tensors)."""
