@@ -1,7 +1,7 @@
 """Regenerate the golden fixtures in this directory from the reference itself.
 
-Runs ONLY in a container that has the read-only reference checkout (default
-/root/reference) and the reference's CPU extension built by
+Runs ONLY where the read-only reference checkout is present (``REFERENCE``
+below) and the reference's CPU extension has been built by
 ``oracle/build_ref.py``. Every output below is computed by reference code:
 
 * ``nf4_code.npz``      - ``NF4_CODE`` as the reference states it
