@@ -479,16 +479,19 @@ def run_gpu(args):
     stream.synchronize()
 
     def timed(fn, steps):
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        """Seconds for `steps` calls (first to last event), and each step's ms
+        (an event after every step; the same bracket)."""
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
         barrier()
         torch.cuda.synchronize(device)
-        start.record(stream)
-        for _ in range(steps):
+        evs[0].record(stream)
+        for i in range(steps):
             fn()
-        end.record(stream)
+            evs[i + 1].record(stream)
         torch.cuda.synchronize(device)
         barrier()
-        return start.elapsed_time(end) / 1e3  # seconds
+        per_step = [evs[i].elapsed_time(evs[i + 1]) for i in range(steps)]
+        return evs[0].elapsed_time(evs[-1]) / 1e3, per_step
 
     def step_graph():
         with torch.cuda.stream(stream):
@@ -506,12 +509,12 @@ def run_gpu(args):
 
     with ClockSampler([local] if world == 1 else list(range(world))) as clocks:
         torch.cuda.profiler.start()   # bounds an `ncu --profile-from-start off` launch list to the timed steps
-        secs = timed(step_graph, args.steps)
+        secs, step_ms = timed(step_graph, args.steps)
         torch.cuda.profiler.stop()
     clock = clocks.summary()
     for _ in range(max(1, args.warmup)):
         step_e2e()
-    e2e_secs = timed(step_e2e, args.steps)
+    e2e_secs, _ = timed(step_e2e, args.steps)
 
     secs_max = max_over_ranks(secs, device)
     e2e_max = max_over_ranks(e2e_secs, device)
@@ -534,6 +537,8 @@ def run_gpu(args):
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(secs_max / args.steps * 1e3, 4),
+            "step_ms_quantiles": {q: round(statistics.quantiles(step_ms, n=10)[i], 4) if len(step_ms) >= 2
+                                  else round(step_ms[0], 4) for q, i in (("p10", 0), ("p50", 4), ("p90", 8))},
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init NF4 weights N(0,0.02), activations N(0,1), seeded per rank)",
             "config": {"workload": "S2-Pro slow-AR decode matmuls: 36 layers x [wqkv 6144x2560, "
