@@ -7,7 +7,8 @@ so that an `ncu --set full -k <kernel> -c 3` capture of it ends in a minute or
 two. With `--time` it instead replays the launches from a CUDA graph and
 prints CUDA-event timings (never under a profiler).
 
-kernels: gemv (M rows <= 32), gated (the W1/W3 gate, M <= 4), gemm (tcgen05, M > 32), attention (decode,
+kernels: gemv (M rows <= 32), gated (the W1/W3 gate, M <= 4), gemm (tcgen05, M > 32), head (a bf16
+output head, `--n` ids x `--k`), attention (decode,
 qk_rope_kv + split-KV attention at a given cache length), prefill (the seven
 S2-Pro projections at M rows through the GEMM, TFLOP/s), dualar (the config-5
 frame graph: `--frames` replays between cudaProfilerStart/Stop, for an
@@ -172,9 +173,35 @@ def run_dualar(frames: int, timed: bool) -> None:
     dec.release()
 
 
+def run_head(n: int, k: int, copies: int, launches: int, timed: bool) -> None:
+    """A bf16 output head (the LM head 155136 x 2560, or a codebook head 4096 x
+    2560) on one activation row: `heads.dense_linear`."""
+    from ttspipe_b200 import heads
+
+    copies = max(1, min(copies, (1 << 30) // (n * k * 2) + 1))  # >= 1 GB of distinct weights in all
+    ws = [(torch.randn(n, k, device="cuda") * 0.02).to(torch.bfloat16) for _ in range(copies)]
+    x = torch.randn(k, device="cuda").to(torch.bfloat16)
+    out = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+
+    def go(i):
+        heads.dense_linear(ws[i % copies], x, out=out)
+
+    for i in range(copies):
+        go(i)
+    torch.cuda.synchronize()
+    if timed:
+        reps = max(copies, 4)
+        us = _graph_time(lambda: [go(i) for i in range(reps)]) / reps
+        print(f"dense head {n}x{k}: {us:.2f} us/launch, {n * k * 2 / us / 1e3:.0f} GB/s")
+        return
+    for i in range(launches):
+        go(i)
+    torch.cuda.synchronize()
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemv", "gated", "gemm", "attention", "prefill", "dualar"])
+    ap.add_argument("kernel", choices=["gemv", "gated", "gemm", "attention", "prefill", "dualar", "head"])
     ap.add_argument("--n", type=int, default=9728)
     ap.add_argument("--k", type=int, default=2560)
     ap.add_argument("--rows", type=int, default=1)
@@ -197,6 +224,8 @@ def main(argv=None) -> None:
         run_gated(a.n, a.k, a.rows, a.copies, a.launches, a.time)
     elif a.kernel == "dualar":
         run_dualar(a.frames, a.time)
+    elif a.kernel == "head":
+        run_head(a.n, a.k, a.copies, a.launches, a.time)
     else:
         run_attention(a.length, a.launches, a.time)
     print("ok", file=sys.stderr)
