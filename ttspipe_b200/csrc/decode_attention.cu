@@ -368,6 +368,27 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
   const uint32_t rank = cluster_rank(), C = cluster_size();
 
   pdl_wait();  // the new K/V row and q come from the previous kernel
+  // A window of one chunk read by one CTA (the fast AR's): its rows' copies go
+  // out before the position is read - the whole window, rows past the live
+  // length are never used - saving a round trip.
+  const bool whole_window = C == 1 && window <= ATTN_CHUNK;
+  if (whole_window && threadIdx.x == 0) {
+    const uint32_t bytes = (uint32_t)window * kD * 2;
+    const uint32_t bar = sm_u32(&sm.bar[0]);
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&sm.bar[1])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     sm_u32(sm.kv[0][0])),
+                 "l"(kc + (size_t)kh * max_len * kD), "r"(bytes), "r"(bar)
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     sm_u32(sm.kv[0][1])),
+                 "l"(vc + (size_t)kh * max_len * kD), "r"(bytes), "r"(bar)
+                 : "memory");
+  }
   long long L = (pos_ptr != nullptr) ? pos_ptr[0] + 1 : (long long)window;
   if (L > window) L = window;
   if (L < 1) L = 1;
@@ -397,7 +418,7 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
                  "l"(vbase + j0 * kD), "r"(bytes), "r"(bar)
                  : "memory");
   };
-  if (tid == 0) {
+  if (tid == 0 && !whole_window) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&sm.bar[0])) : "memory");
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&sm.bar[1])) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -640,18 +661,21 @@ cudaError_t launch_cluster_g(const uint16_t* q, const uint16_t* kc, const uint16
   cfg.blockDim = dim3(kCThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
+  // One CTA per KV head (a one-chunk window) needs no cluster: a plain launch
+  // is an implicit cluster of one for the kernel's cluster operations.
   cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = C;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = C;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = C > 1 ? 2 : 1;
   int clusters = 1;
-  if (check && (cudaOccupancyMaxActiveClusters(&clusters, decode_attention_cluster_kernel<G>, &cfg) != cudaSuccess ||
-                clusters < 1)) {
+  if (check && C > 1 &&
+      (cudaOccupancyMaxActiveClusters(&clusters, decode_attention_cluster_kernel<G>, &cfg) != cudaSuccess ||
+       clusters < 1)) {
     (void)cudaGetLastError();
     return cudaErrorNotSupported;
   }
