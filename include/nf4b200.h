@@ -124,6 +124,32 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
                  const nf4b_gemm_opts* opts, void* stream);
 
 /*
+ * The wqkv projection of one token with the rotary + KV-cache write fused into
+ * its store (qk_rope_kv without q/k norm, app/engine/fusedlayer.py:56-92):
+ * y = x W^T (bf16, as nf4b_gemm), q heads rotated into q_out, k heads rotated
+ * into k_cache row *pos, v heads copied into v_cache row *pos (a *pos outside
+ * [0, max_len) writes no cache row) - bit-identical to nf4b_gemm followed by
+ * nf4b_qk_rope_kv with no norm weights. Output features are n_head query
+ * heads, then n_kv key heads, then n_kv value heads, 128 wide; freqs is this
+ * token's rotary row (128 values, (cos, sin) pairs). Serves one row on the
+ * register-fed decode GEMV (blocksize 64, k_in % 256 == 0, 32-byte aligned
+ * packed weight); anything else returns NF4B_ERR_SHAPE (make the two calls).
+ * opts as nf4b_gemm_ex (a fused RMSNorm of x is allowed).
+ */
+typedef struct nf4b_rope_kv {
+  const void* freqs;
+  int freqs_dtype; /* NF4B_F32 / NF4B_F16 / NF4B_BF16 */
+  const int64_t* pos;
+  void* q_out;     /* [n_head * 128] bf16 */
+  void* k_cache;   /* (n_kv, max_len, 128) bf16 */
+  void* v_cache;
+  int n_head, n_kv, max_len;
+} nf4b_rope_kv;
+
+int nf4b_gemm_qkv_rope(const nf4b_weight* w, const void* x, void* y, const nf4b_rope_kv* rk, void* workspace,
+                       size_t workspace_bytes, const nf4b_gemm_opts* opts, void* stream);
+
+/*
  * The FeedForward gate of a W1/W3 pair sharing x in ONE launch:
  * y = bf16(bf16(silu(bf16(x W1^T))) * bf16(x W3^T)), the rounding points of the
  * fork's w2(F.silu(w1(x)) * w3(x)) (app/engine/fusedlayer.py:265-266, where it

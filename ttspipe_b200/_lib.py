@@ -32,6 +32,7 @@ EXPORTS = (
     "nf4b_gemm_workspace_size",
     "nf4b_gemm_noalloc",
     "nf4b_gemm_gated",
+    "nf4b_gemm_qkv_rope",
     "nf4b_gemv_chain",
     "nf4b_dense_gemv",
     "nf4b_sample",
@@ -89,6 +90,14 @@ class GemmOpts(ctypes.Structure):
                 ("norm_weight", ctypes.c_void_p), ("norm_eps", ctypes.c_float)]
 
 
+class RopeKv(ctypes.Structure):
+    """`nf4b_rope_kv`: the rotary + KV-cache store fused into a wqkv GEMV."""
+
+    _fields_ = [("freqs", ctypes.c_void_p), ("freqs_dtype", ctypes.c_int), ("pos", ctypes.c_void_p),
+                ("q_out", ctypes.c_void_p), ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
+                ("n_head", ctypes.c_int), ("n_kv", ctypes.c_int), ("max_len", ctypes.c_int)]
+
+
 class Nf4bError(RuntimeError):
     """A non-zero status from the library, with its message."""
 
@@ -111,6 +120,7 @@ def _declare(lib) -> None:
         "nf4b_gemm": (i32, [wp, vp, vp, i32, i32, vp, vp, sz, vp]),
         "nf4b_gemm_ex": (i32, [wp, vp, vp, i32, i32, vp, vp, sz, ctypes.POINTER(GemmOpts), vp]),
         "nf4b_gemm_gated": (i32, [wp, wp, vp, vp, i32, vp, sz, ctypes.POINTER(GemmOpts), vp]),
+        "nf4b_gemm_qkv_rope": (i32, [wp, vp, vp, ctypes.POINTER(RopeKv), vp, sz, ctypes.POINTER(GemmOpts), vp]),
         "nf4b_gemv_chain": (i32, [ctypes.POINTER(ChainJob), i32, i32, vp, sz, vp]),
         "nf4b_dense_gemv": (i32, [vp, vp, vp, i32, i32, vp, f32, vp]),
         "nf4b_sample": (i32, [vp, i32, ctypes.c_float, ctypes.c_float, i32, ctypes.c_uint64, vp, vp, vp, sz, vp]),

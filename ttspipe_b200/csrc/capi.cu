@@ -173,7 +173,7 @@ int current_sm_count() {
 // workspace and the GEMV-specific limits.
 int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* y, int rows, int epi,
               const void* operand, void* workspace, size_t workspace_bytes, const nf4b_gemm_opts* opts,
-              cudaStream_t s) {
+              cudaStream_t s, const nf4b_rope_kv* rk = nullptr) {
   if ((long long)(w->n_out + 15) / 16 > GEMV_MAX_TILES)
     return fail(NF4B_ERR_SHAPE, "n_out %d exceeds the GEMV's %lld-row limit", w->n_out, GEMV_MAX_TILES * 16);
   const bool pairs = use_pairs(w, rows);
@@ -208,6 +208,19 @@ int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* 
            (long long)w->n_out * (w->k_in / 64) < (1LL << 31))
               ? 1
               : 0;
+  if (rk != nullptr) {
+    if (!p.reg || gated || rows != 1 || epi != NF4B_EPI_NONE)
+      return fail(NF4B_ERR_SHAPE, "the fused rotary store serves one row on the register-fed decode GEMV");
+    p.rk_freqs = rk->freqs;
+    p.rk_ftype = rk->freqs_dtype;
+    p.rk_pos = rk->pos;
+    p.rk_q = static_cast<uint16_t*>(rk->q_out);
+    p.rk_k = static_cast<uint16_t*>(rk->k_cache);
+    p.rk_v = static_cast<uint16_t*>(rk->v_cache);
+    p.rk_nh = rk->n_head;
+    p.rk_nkv = rk->n_kv;
+    p.rk_max_len = rk->max_len;
+  }
   p.x_staged = (pairs && (long long)rows * w->k_in * 2 <= GEMV_PAIR_X_MAX) ? 1 : 0;
   p.norm_w = opts ? static_cast<const uint16_t*>(opts->norm_weight) : nullptr;
   p.norm_eps = opts ? opts->norm_eps : 0.f;
@@ -308,6 +321,28 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
   p.counters = static_cast<int*>(workspace);
   p.partial = splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + GEMM_COUNTER_BYTES) : nullptr;
   return launch_status(launch_gemm_tc(p, s), "nf4 tcgen05 gemm launch");
+}
+
+extern "C" int nf4b_gemm_qkv_rope(const nf4b_weight* w, const void* x, void* y, const nf4b_rope_kv* rk,
+                                  void* workspace, size_t workspace_bytes, const nf4b_gemm_opts* opts, void* stream) {
+  int st = check_weight(w);
+  if (st) return st;
+  if (x == nullptr || y == nullptr || rk == nullptr) return fail(NF4B_ERR_ARG, "x, y or the rotary store is null");
+  if (rk->freqs == nullptr || rk->pos == nullptr || rk->q_out == nullptr || rk->k_cache == nullptr ||
+      rk->v_cache == nullptr)
+    return fail(NF4B_ERR_ARG, "a rotary store pointer is null");
+  if (rk->freqs_dtype < NF4B_F32 || rk->freqs_dtype > NF4B_BF16)
+    return fail(NF4B_ERR_DTYPE, "unknown rotary table dtype %d", rk->freqs_dtype);
+  if (rk->n_head <= 0 || rk->n_kv <= 0 || rk->n_head % rk->n_kv || rk->max_len <= 0 ||
+      (long long)(rk->n_head + 2 * rk->n_kv) * 128 != w->n_out)
+    return fail(NF4B_ERR_SHAPE, "n_out %d is not (%d + 2 x %d) heads of 128", w->n_out, rk->n_head, rk->n_kv);
+  if (!aligned(x, 16)) return fail(NF4B_ERR_ALIGN, "x is not 16-byte aligned");
+  if (!aligned(y, 2) || !aligned(rk->q_out, 2) || !aligned(rk->k_cache, 2) || !aligned(rk->v_cache, 2) ||
+      !aligned(rk->pos, 8))
+    return fail(NF4B_ERR_ALIGN, "y/q/cache not 2-byte aligned or pos not 8-byte aligned");
+  if ((st = check_device())) return st;
+  return gemv_call(w, nullptr, x, y, 1, NF4B_EPI_NONE, nullptr, workspace, workspace_bytes, opts,
+                   reinterpret_cast<cudaStream_t>(stream), rk);
 }
 
 int nf4b_gemm_gated(const nf4b_weight* w1, const nf4b_weight* w3, const void* x, void* y, int rows,

@@ -66,7 +66,8 @@ __global__ void __launch_bounds__(kFrameThreads)
 
 // x = bf16(float(sem_emb[tokens[0]]) + s), s = the fp32 sum, in codebook
 // order, of float(cb_emb[i][tokens[1 + i]]) for i < n_cb; recent <-
-// [tokens[0], recent[0..n_recent-2]]; pos += 1; step += 1.
+// [tokens[0], recent[0..n_recent-2]]; pos += 1; step += 1. One thread per
+// dimension (CTA b takes dimensions b * 256 ..); CTA 0 moves the counters.
 __global__ void __launch_bounds__(kFrameThreads)
     frame_advance_kernel(const uint16_t* __restrict__ sem_emb, long long vocab, const uint16_t* __restrict__ cb_emb,
                          long long cb_size, int n_cb, const int64_t* __restrict__ tokens, int dim,
@@ -77,12 +78,21 @@ __global__ void __launch_bounds__(kFrameThreads)
   if (threadIdx.x <= n_cb)
     s_tok[threadIdx.x] = clamp_ll(tokens[threadIdx.x], 0, (threadIdx.x == 0 ? vocab : cb_size) - 1);
   __syncthreads();
-  for (int d = threadIdx.x; d < dim; d += kFrameThreads) {
+  const int d = blockIdx.x * kFrameThreads + threadIdx.x;
+  if (d < dim) {
+    // every row's element requested before the sum (one round trip)
+    float e[FRAME_MAX_CODEBOOKS];
+#pragma unroll
+    for (int i = 0; i < FRAME_MAX_CODEBOOKS; ++i)
+      e[i] = i < n_cb ? bf2f(cb_emb[((size_t)i * cb_size + s_tok[1 + i]) * dim + d]) : 0.f;
+    const float sem = bf2f(sem_emb[(size_t)s_tok[0] * dim + d]);
     float s = 0.f;
-    for (int i = 0; i < n_cb; ++i) s += bf2f(cb_emb[((size_t)i * cb_size + s_tok[1 + i]) * dim + d]);
-    x[d] = f2bf(__fadd_rn(bf2f(sem_emb[(size_t)s_tok[0] * dim + d]), s));
+#pragma unroll
+    for (int i = 0; i < FRAME_MAX_CODEBOOKS; ++i)
+      if (i < n_cb) s += e[i];
+    x[d] = f2bf(__fadd_rn(sem, s));
   }
-  if (threadIdx.x == 0) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
     for (int j = n_recent - 1; j > 0; --j) recent[j] = recent[j - 1];
     if (n_recent > 0) recent[0] = s_tok[0];
     pos[0] += 1;
@@ -125,7 +135,8 @@ cudaError_t launch_frame_advance(const uint16_t* sem_emb, long long vocab, const
                                  int n_recent, int64_t* pos, int64_t* step, cudaStream_t stream) {
   void* args[] = {(void*)&sem_emb, (void*)&vocab, (void*)&cb_emb, (void*)&cb_size,  (void*)&n_cb, (void*)&tokens,
                   (void*)&dim,     (void*)&x,     (void*)&recent, (void*)&n_recent, (void*)&pos,  (void*)&step};
-  return launch_frame_kernel((const void*)frame_advance_kernel, 1, args, stream);
+  return launch_frame_kernel((const void*)frame_advance_kernel, (dim + kFrameThreads - 1) / kFrameThreads, args,
+                             stream);
 }
 
 }  // namespace nf4b

@@ -125,6 +125,16 @@ struct alignas(64) GemvParams {
   // Optional L2 prefetch of the weight the NEXT call reads (packed codes and
   // its first-level scales), issued by each warp once its own loads are done.
   PrefetchHint pf;
+  // Rotary + KV-cache write fused into the store (register-fed kernel, one
+  // activation row, no q/k norm; rk_q null otherwise). Output rows are rk_nh
+  // query heads, then rk_nkv key heads, then rk_nkv value heads of 128.
+  const void* rk_freqs;  // this token's rotary row: 128 values, (cos, sin) pairs
+  int rk_ftype;
+  const int64_t* rk_pos;
+  uint16_t* rk_q;
+  uint16_t* rk_k;
+  uint16_t* rk_v;
+  int rk_nh, rk_nkv, rk_max_len;
 };
 
 struct GemvPlan {

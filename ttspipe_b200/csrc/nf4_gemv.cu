@@ -363,11 +363,53 @@ __device__ __forceinline__ bool mbar_free_wait_count(const int* ctr, int need) {
   }
 }
 
+// A fused wqkv store's rotary row (staged in shared memory: (cos, sin) pairs,
+// 128 values) and the cache row it writes.
+struct RopeKv {
+  const float* f;
+  long long pos;
+};
+
+// Output feature r (bf16 y) and its rotary partner r ^ 1 (yp), with the
+// arithmetic of qk_rope_kv without q/k norm (app/engine/fusedlayer.py:56-92):
+// a q feature rotated into rk_q, a k feature rotated into the key cache at
+// pos, a v feature copied into the value cache at pos (rows outside the
+// cache are not written).
+__device__ __forceinline__ void rope_kv_row(const GemvParams& p, const RopeKv& rk, int r, bf16_t y, bf16_t yp) {
+  const int head = r >> 7, d = r & 127;
+  const int nh = p.rk_nh, nkv = p.rk_nkv;
+  const bool in_cache = rk.pos >= 0 && rk.pos < p.rk_max_len;
+  if (head < nh + nkv) {
+    const float x = bf2f(y), xp = bf2f(yp);
+    const float x0 = (d & 1) ? xp : x, x1 = (d & 1) ? x : xp;
+    const float c = rk.f[d & ~1], sn = rk.f[d | 1];
+    const float o = (d & 1) ? __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn))
+                            : __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+    if (head < nh)
+      p.rk_q[r] = f2bf(o);
+    else if (in_cache)
+      p.rk_k[((size_t)(head - nh) * p.rk_max_len + rk.pos) * 128 + d] = f2bf(o);
+  } else if (in_cache) {
+    p.rk_v[((size_t)(head - nh - nkv) * p.rk_max_len + rk.pos) * 128 + d] = y;
+  }
+}
+
+// Both rows of a lane (ra, rb) with their partners from lane ^ 4 (row g ^ 1):
+// called by the 8 lanes of activation row 0 (t == 0) together.
+__device__ __forceinline__ void rope_kv_rows(const GemvParams& p, const RopeKv& rk, int ra, int rb, bf16_t ya,
+                                             bf16_t yb) {
+  const bf16_t pa = (bf16_t)__shfl_xor_sync(0x11111111u, (unsigned)ya, 4);
+  const bf16_t pb = (bf16_t)__shfl_xor_sync(0x11111111u, (unsigned)yb, 4);
+  rope_kv_row(p, rk, ra, ya, pa);
+  rope_kv_row(p, rk, rb, yb, pb);
+}
+
 // Store the outputs of row tile `rt` (rows g, g + 8 of activation row t):
-// the gate of the two halves for a gated pair, else the epilogue of half 0.
+// the gate of the two halves for a gated pair, else the epilogue of half 0
+// (and, given `rk`, the fused rotary + KV-cache write).
 template <bool kGated>
 __device__ __forceinline__ void store_pair_tile(const GemvParams& p, int rt, int g, int t,
-                                                const float (&v)[2][2]) {
+                                                const float (&v)[2][2], const RopeKv* rk = nullptr) {
   const int N = p.N;
   const int ra = rt * 16 + g, rb = ra + 8;
   if (t >= p.M) return;
@@ -375,6 +417,11 @@ __device__ __forceinline__ void store_pair_tile(const GemvParams& p, int rt, int
   if (kGated) {
     if (ra < N) p.y[oa] = gate_bf16(v[0][0], v[1][0]);
     if (rb < N) p.y[ob] = gate_bf16(v[0][1], v[1][1]);
+  } else if (rk != nullptr) {  // one activation row, n_out % 16 == 0
+    const bf16_t ya = epilogue(v[0][0], p.epi, p.operand, oa), yb = epilogue(v[0][1], p.epi, p.operand, ob);
+    p.y[oa] = ya;
+    p.y[ob] = yb;
+    rope_kv_rows(p, *rk, ra, rb, ya, yb);
   } else {
     if (ra < N) p.y[oa] = epilogue(v[0][0], p.epi, p.operand, oa);
     if (rb < N) p.y[ob] = epilogue(v[0][1], p.epi, p.operand, ob);
@@ -392,12 +439,13 @@ __device__ __forceinline__ void store_pair_tile(const GemvParams& p, int rt, int
 // measured slower: the first tile's reduction then no longer overlaps the run.)
 template <bool kGated>
 __device__ __forceinline__ bool publish_pair_tile(const GemvParams& p, int rt, int u0, int u1, int gw, int g,
-                                                  int t, int lane, const float (&v)[2][2], int& old) {
+                                                  int t, int lane, const float (&v)[2][2], int& old,
+                                                  const RopeKv* rk = nullptr) {
   constexpr int H = kGated ? 2 : 1;
   const int per_tile = p.blocks_per_tile * H;
   const int t0 = rt * per_tile, t1 = t0 + per_tile - 1;
   if (t0 >= u0 && t1 < u1) {
-    store_pair_tile<kGated>(p, rt, g, t, v);
+    store_pair_tile<kGated>(p, rt, g, t, v, rk);
     return false;
   }
   const int w_lo = warp_of(t0, p.uq, p.ur);
@@ -423,7 +471,8 @@ __device__ __forceinline__ bool publish_pair_tile(const GemvParams& p, int rt, i
 // the residual or gate operand is fetched in the same round trip as the
 // slots - then re-zero the counter for the next launch.
 template <bool kGated>
-__device__ __forceinline__ void finish_split_tile(const GemvParams& p, int rt, int old, int g, int t, int lane) {
+__device__ __forceinline__ void finish_split_tile(const GemvParams& p, int rt, int old, int g, int t, int lane,
+                                                  const RopeKv* rk = nullptr) {
   constexpr int H = kGated ? 2 : 1;
   const int per_tile = p.blocks_per_tile * H;
   const int t0 = rt * per_tile;
@@ -444,6 +493,11 @@ __device__ __forceinline__ void finish_split_tile(const GemvParams& p, int rt, i
   if (kGated) {
     if (ra < N) p.y[oa] = gate_bf16(v[0][0], v[1][0]);
     if (rb < N) p.y[ob] = gate_bf16(v[0][1], v[1][1]);
+  } else if (rk != nullptr) {  // one activation row, n_out % 16 == 0
+    const bf16_t ya = epilogue_value(v[0][0], p.epi, bf2f(opa)), yb = epilogue_value(v[0][1], p.epi, bf2f(opb));
+    p.y[oa] = ya;
+    p.y[ob] = yb;
+    rope_kv_rows(p, *rk, ra, rb, ya, yb);
   } else {
     if (ra < N) p.y[oa] = epilogue_value(v[0][0], p.epi, bf2f(opa));
     if (rb < N) p.y[ob] = epilogue_value(v[0][1], p.epi, bf2f(opb));
@@ -825,12 +879,16 @@ __device__ __forceinline__ void ld_stream_u8(const void* p, uint32_t (&v)[8]) {
                : "l"(p));
 }
 
-template <bool kGated, bool kNested>
+// kRope: the fused rotary + KV-cache store of a wqkv projection (one
+// activation row, not gated).
+template <bool kGated, bool kNested, bool kRope = false>
 __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     nf4_gemv_reg_kernel(const __grid_constant__ GemvParams p) {
   constexpr int kT = GEMV_PAIR_WARPS * 32;
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ double norm_red[GEMV_PAIR_WARPS];
+  __shared__ float rk_f[kRope ? 128 : 1];  // kRope: this token's rotary row
+  static_assert(!(kRope && kGated), "the fused rotary store serves a plain projection");
   const uint8_t* lut = smem;
   uint8_t* xs = smem + GEMV_LUT_BYTES;
 
@@ -909,6 +967,14 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   pdl_launch_dependents();
   pdl_wait();
   if (nested) store_code2_copies<kT>(smem, c2v);
+  // kRope: the rotary row and the cache position (both written before this
+  // launch) are requested with x and stored after x's loads are out.
+  long long rk_pos = 0;
+  float rk_val = 0.f;
+  if (kRope) {
+    if (threadIdx.x < 128) rk_val = load_freq(p.rk_freqs, threadIdx.x, p.rk_ftype);
+    rk_pos = p.rk_pos[0];
+  }
   // x, written by earlier work on the stream, staged with the padding.
   {
     const int n16 = K >> 3;
@@ -918,6 +984,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
         *reinterpret_cast<uint4*>(xs + m * xrow + c * 16 + (c >> 3) * 16) = __ldcg(src + c);
     }
   }
+  if (kRope && threadIdx.x < 128) rk_f[threadIdx.x] = rk_val;
   __syncthreads();
   if (p.norm_w != nullptr)
     rms_normalise_staged<kT, true>(reinterpret_cast<uint16_t*>(xs), M, K, p.norm_w, p.norm_eps, norm_red,
@@ -1010,7 +1077,8 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       }
       const float v[2][2] = {{acc_a, acc_b}, {acc3_a, acc3_b}};
       int old = 0;
-      if (publish_pair_tile<kGated>(p, rt, u0, u1, gw, g, tok, lane, v, old)) {
+      const RopeKv rk{rk_f, rk_pos};
+      if (publish_pair_tile<kGated>(p, rt, u0, u1, gw, g, tok, lane, v, old, kRope ? &rk : nullptr)) {
         if (split_a < 0) {
           split_a = rt;
           old_a = old;
@@ -1032,8 +1100,9 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       }
     }
   }
-  if (split_a >= 0) finish_split_tile<kGated>(p, split_a, old_a, g, tok, lane);
-  if (split_b >= 0) finish_split_tile<kGated>(p, split_b, old_b, g, tok, lane);
+  const RopeKv rk{rk_f, rk_pos};
+  if (split_a >= 0) finish_split_tile<kGated>(p, split_a, old_a, g, tok, lane, kRope ? &rk : nullptr);
+  if (split_b >= 0) finish_split_tile<kGated>(p, split_b, old_b, g, tok, lane, kRope ? &rk : nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -1978,6 +2047,12 @@ cudaError_t launch_gemv(const GemvParams& p, int grid, bool pairs, cudaStream_t 
   if (pairs && p.reg) {
     const int smem = GEMV_LUT_BYTES + p.M * reg_x_row_bytes(p.K);
     const int nt = GEMV_PAIR_WARPS * 32;
+    static bool cfg_rope[64] = {}, cfg_rope_plain[64] = {};
+    if (p.rk_q != nullptr)
+      return p.nested ? launch_kernel(nf4_gemv_reg_kernel<false, true, true>, p, grid, stream, cfg_rope, smem,
+                                      GEMV_REG_SMEM_MAX, nt)
+                      : launch_kernel(nf4_gemv_reg_kernel<false, false, true>, p, grid, stream, cfg_rope_plain, smem,
+                                      GEMV_REG_SMEM_MAX, nt);
     if (p.nested)
       return p.gated ? launch_kernel(nf4_gemv_reg_kernel<true, true>, p, grid, stream, cfg_reg_gated, smem,
                                      GEMV_REG_SMEM_MAX, nt)

@@ -26,6 +26,14 @@ HEAD_DIM = 128
 #: instead of nf4b_qk_rope_kv then nf4b_decode_attention. Off: measured 3% slower
 #: per Dual-AR frame than the two launches chained by programmatic dependent launch.
 FUSED_QKV_ATTENTION = False
+#: Without q/k norm, run the rotary and the KV-cache write in the wqkv GEMV's
+#: store (nf4b_gemm_qkv_rope, one launch less per block); "one_chunk": only
+#: where the attention that follows is a plain launch (a window of <= 64 rows).
+#: Off: per Dual-AR frame, True measured 4.63 ms and "one_chunk" 4.42-4.43
+#: against 4.41-4.43 ms with nf4b_qk_rope_kv as its own launch - that launch is
+#: hidden behind the GEMV's tail by programmatic dependent launch, while the
+#: 8-CTA attention clusters that follow a whole-GPU GEMV start later.
+ROPE_IN_WQKV = False
 #: Pass L2 prefetch hints (the next weight of the block) to each matmul: off,
 #: measured 1.5% slower per Dual-AR frame with them.
 PREFETCH = False
@@ -68,6 +76,36 @@ def _eligible(block, x, mask, input_pos) -> bool:
     return True
 
 
+def _attention(a, qkv, freqs_cis, input_pos, mask, y, nh: int, nkv: int, max_len: int) -> None:
+    """From the wqkv output: q/k norm, rotary and the KV write, then the
+    attention into `y` - nf4b_qk_rope_kv and the attention kernel, or both in
+    one launch (FUSED_QKV_ATTENTION)."""
+    import torch
+
+    from ttspipe_b200 import fastpath
+
+    qn = getattr(a, "q_norm", None) if a.attention_qk_norm else None
+    kn = getattr(a, "k_norm", None) if a.attention_qk_norm else None
+    eps = float(qn.eps if qn is not None and qn.eps is not None else 1e-6)
+    if not FUSED_QKV_ATTENTION:
+        q = torch.empty(nh * HEAD_DIM, dtype=torch.bfloat16, device=qkv.device)
+        _lib.check(_lib.lib().nf4b_qk_rope_kv(
+            qkv.data_ptr(), None if qn is None else qn.weight.data_ptr(),
+            None if kn is None else kn.weight.data_ptr(), eps, freqs_cis.data_ptr(),
+            _FTYPE[str(freqs_cis.dtype)], input_pos.data_ptr(), q.data_ptr(),
+            a.kv_cache.k_cache.data_ptr(), a.kv_cache.v_cache.data_ptr(), nh, nkv, HEAD_DIM, max_len,
+            torch.cuda.current_stream(qkv.device).cuda_stream))
+        fastpath.kernel_attention(q, a.kv_cache.k_cache, a.kv_cache.v_cache, y, n_head=nh, n_kv=nkv,
+                                  pos=input_pos, mask=None, window=int(mask.shape[-1]), max_len=max_len)
+        return
+    # q/k norm, rotary, the KV write and the attention itself: one launch
+    fastpath.qkv_attention(qkv, a.kv_cache.k_cache, a.kv_cache.v_cache, y, n_head=nh, n_kv=nkv, pos=input_pos,
+                           window=int(mask.shape[-1]), max_len=max_len, freqs=freqs_cis,
+                           freqs_dtype=_FTYPE[str(freqs_cis.dtype)],
+                           q_norm_w=None if qn is None else qn.weight,
+                           k_norm_w=None if kn is None else kn.weight, eps=eps)
+
+
 def decode_block(block, x, freqs_cis, mask, input_pos, next_block=None):
     """`TransformerBlock.forward` for one position, or None if it cannot.
 
@@ -85,38 +123,32 @@ def decode_block(block, x, freqs_cis, mask, input_pos, next_block=None):
     a, ff = block.attention, block.feed_forward
     pf = (lambda m: m) if PREFETCH else (lambda m: None)
     an, fn = block.attention_norm, block.ffn_norm
-    # attention_norm fused into the wqkv launch (x staged, normalised in shared memory)
-    qkv = nf4gemv.matmul(a.wqkv, x, prefetch=pf(a.wo), norm=(an.weight, an.eps))
-    if qkv is None:
-        xn = fusedops.rms_norm(x, an.weight, an.eps)
-        if xn is None:
-            return None
-        qkv = nf4gemv.matmul(a.wqkv, xn, prefetch=pf(a.wo))
-        if qkv is None:
-            return None
     nh, nkv = a.n_head, a.n_local_heads
     max_len = a.kv_cache.k_cache.shape[2]
-    qn = getattr(a, "q_norm", None) if a.attention_qk_norm else None
-    kn = getattr(a, "k_norm", None) if a.attention_qk_norm else None
-    eps = float(qn.eps if qn is not None and qn.eps is not None else 1e-6)
     y = torch.empty((1, 1, nh * HEAD_DIM), dtype=torch.bfloat16, device=x.device)
-    if not FUSED_QKV_ATTENTION:
+    q = None
+    rope_here = ROPE_IN_WQKV is True or (ROPE_IN_WQKV == "one_chunk" and int(mask.shape[-1]) <= 64)
+    if rope_here and not FUSED_QKV_ATTENTION and not a.attention_qk_norm:
+        # attention_norm, wqkv, the rotary and the KV write in one launch
         q = torch.empty(nh * HEAD_DIM, dtype=torch.bfloat16, device=x.device)
-        _lib.check(_lib.lib().nf4b_qk_rope_kv(
-            qkv.data_ptr(), None if qn is None else qn.weight.data_ptr(),
-            None if kn is None else kn.weight.data_ptr(), eps, freqs_cis.data_ptr(),
-            _FTYPE[str(freqs_cis.dtype)], input_pos.data_ptr(), q.data_ptr(),
-            a.kv_cache.k_cache.data_ptr(), a.kv_cache.v_cache.data_ptr(), nh, nkv, HEAD_DIM, max_len,
-            torch.cuda.current_stream(x.device).cuda_stream))
+        if nf4gemv.matmul_qkv_rope(a.wqkv, x, freqs=freqs_cis, pos=input_pos, q_out=q, k_cache=a.kv_cache.k_cache,
+                                   v_cache=a.kv_cache.v_cache, n_head=nh, n_kv=nkv,
+                                   norm=(an.weight, an.eps)) is None:
+            q = None
+    if q is not None:
         fastpath.kernel_attention(q, a.kv_cache.k_cache, a.kv_cache.v_cache, y, n_head=nh, n_kv=nkv,
                                   pos=input_pos, mask=None, window=int(mask.shape[-1]), max_len=max_len)
     else:
-        # q/k norm, rotary, the KV write and the attention itself: one launch
-        fastpath.qkv_attention(qkv, a.kv_cache.k_cache, a.kv_cache.v_cache, y, n_head=nh, n_kv=nkv, pos=input_pos,
-                               window=int(mask.shape[-1]), max_len=max_len, freqs=freqs_cis,
-                               freqs_dtype=_FTYPE[str(freqs_cis.dtype)],
-                               q_norm_w=None if qn is None else qn.weight,
-                               k_norm_w=None if kn is None else kn.weight, eps=eps)
+        # attention_norm fused into the wqkv launch (x staged, normalised in shared memory)
+        qkv = nf4gemv.matmul(a.wqkv, x, prefetch=pf(a.wo), norm=(an.weight, an.eps))
+        if qkv is None:
+            xn = fusedops.rms_norm(x, an.weight, an.eps)
+            if xn is None:
+                return None
+            qkv = nf4gemv.matmul(a.wqkv, xn, prefetch=pf(a.wo))
+            if qkv is None:
+                return None
+        _attention(a, qkv, freqs_cis, input_pos, mask, y, nh, nkv, max_len)
     h = nf4gemv.matmul(a.wo, y, epi=nf4gemv.EPI_RESIDUAL, operand=x, prefetch=pf(ff.w1))
     # w1 and w3 read the same input: one launch normalises h (ffn_norm) and
     # computes the gate silu(hn W1^T) * (hn W3^T) without writing hn or hn W1^T out.

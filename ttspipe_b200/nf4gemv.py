@@ -275,6 +275,56 @@ def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None, norm=
     return out.view(*x.shape[:-1], N)
 
 
+def matmul_qkv_rope(module, x, *, freqs, pos, q_out, k_cache, v_cache, n_head: int, n_kv: int, norm=None):
+    """The wqkv projection of one token with the rotary + KV-cache write in
+    its store (an extension): ``y = x @ W.T`` as ``matmul``, the query heads
+    rotated into `q_out`, the key heads rotated into ``k_cache[.., pos]`` and
+    the value heads copied into ``v_cache[.., pos]`` - bit-identical to
+    ``matmul`` then ``nf4b_qk_rope_kv`` without q/k norm. `freqs` is the
+    token's rotary row (128 values, fp32/fp16/bf16), `pos` an int64 device
+    tensor [1], the caches (.., n_kv, max_len, 128) bf16. Returns y, or None
+    where the fused store does not serve the call (the two launches then).
+    """
+    import torch
+
+    fast = getattr(module, "_nf4_fast", None)
+    if fast is None or x.dtype != torch.bfloat16 or x.device.type != "cuda":
+        return None
+    K, N = fast["K"], fast["M"]
+    flat = x.reshape(-1, K) if x.shape[-1] == K else None
+    if flat is None or flat.shape[0] != 1 or not flat.is_contiguous() or flat.data_ptr() % 16:
+        return None
+    if N != (n_head + 2 * n_kv) * 128 or freqs.numel() != 128 or not freqs.is_contiguous():
+        return None
+    ftype = {torch.float32: _lib.NF4B_F32, torch.float16: _lib.NF4B_F16, torch.bfloat16: _lib.NF4B_BF16}.get(
+        freqs.dtype)
+    if ftype is None or norm is not None and not _norm_ok(norm, 1, K, x.device):
+        return None
+    max_len = k_cache.shape[-2]
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous() and q_out.is_contiguous()
+            and k_cache.dtype == torch.bfloat16 and v_cache.dtype == torch.bfloat16 and q_out.dtype == torch.bfloat16
+            and q_out.numel() == n_head * 128 and k_cache.numel() == n_kv * max_len * 128
+            and v_cache.shape == k_cache.shape and k_cache.shape[-1] == 128):
+        return None
+    if not available():
+        raise RuntimeError(f"nf4 kernels unavailable: {_unavailable}")
+    out = torch.empty((1, N), dtype=torch.bfloat16, device=x.device)
+    L = _lib.lib()
+    desc = fast["desc"]
+    need = int(L.nf4b_gemm_workspace_size(ctypes.byref(desc), 1))
+    ws = _workspace(x.device, need, "gemv") if need > 0 else None
+    rk = _lib.RopeKv(freqs.data_ptr(), ftype, pos.data_ptr(), q_out.data_ptr(), k_cache.data_ptr(),
+                     v_cache.data_ptr(), int(n_head), int(n_kv), int(max_len))
+    st = L.nf4b_gemm_qkv_rope(ctypes.byref(desc), flat.data_ptr(), out.data_ptr(), ctypes.byref(rk),
+                              ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+                              _opts(None, norm), ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream))
+    if st == _lib.NF4B_ERR_SHAPE:   # outside the fused store's envelope (e.g. a 16-byte aligned weight)
+        return None
+    _lib.check(st)
+    _stats["fast"] += 1
+    return out.view(*x.shape[:-1], N)
+
+
 def matmul_gated(w1, w3, x, *, prefetch=None, norm=None):
     """``silu(x @ w1.weight.T) * (x @ w3.weight.T)`` in ONE launch, with the
     fork's rounding points (app/engine/fusedlayer.py:265-266: two ``matmul``
