@@ -10,7 +10,7 @@
 //
 //   warp 0     TMA producer: X tile [BT x 64] bf16 (128-byte swizzle) and the
 //              packed weight tile [128 x 32 B] per 64-wide k block, into a
-//              STAGES-deep ring, completion via mbarrier transaction counts.
+//              ring_stages<BT>()-deep ring, completion via mbarrier transaction counts.
 //   warp 1     allocates TMEM (BT fp32 columns) and, from one thread, issues
 //              4 x tcgen05.mma (M=128, N=BT, K=16) per k block, committing each
 //              stage back to the producer and the whole tile to the epilogue.
@@ -41,22 +41,39 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int STAGES = 4;
 // Warp 0: TMA producer; warp 1: TMEM owner + MMA issuer; then DQ groups of
 // four dequantisation/epilogue warps (group g serves k blocks g, g + DQ, ...).
+// The dequantisation is the kernel's critical path: per 64-block each thread
+// builds its row's scaled table and runs ~170 dependent byte-permute
+// instructions, so more groups in flight raise the tile rate (measured
+// against two groups: the S2-Pro layer 7-11% faster from M = 64 to 1024).
 template <int DQ>
 constexpr int gemm_threads() { return 64 + 128 * DQ; }
-constexpr int kDequantGroups = 2;
+constexpr int kDequantGroups = 4;
+// Ring depth: 4 stages (8 for the 64-row tiles, which fit twice as many in
+// the same shared memory; deeper rings measured no faster). The depth must be
+// a multiple of DQ: group g then meets every phase of its stages in order
+// (block j's previous use of stage j % STAGES, block j - STAGES, was the
+// group's own), so a parity wait can never be satisfied by the phase two
+// rounds back - with more groups than stages it could, and a group would
+// read a stale tile.
+template <int BT>
+__host__ __device__ constexpr int ring_stages() { return BT >= 128 ? 4 : 8; }
+static_assert(ring_stages<256>() % kDequantGroups == 0 && ring_stages<128>() % kDequantGroups == 0 &&
+                  ring_stages<64>() % kDequantGroups == 0,
+              "ring depth must be a multiple of the dequantisation groups");
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 
 template <int BT>
 struct __align__(1024) TileSmem {
+  static constexpr int STAGES = ring_stages<BT>();
   uint8_t x[STAGES][BT * 128];
   uint8_t a[STAGES][BM * 128];
   uint8_t w[STAGES][BM * 32];
   float code2[256];
   float nf4[16];
-  unsigned long long tma_full[STAGES];
+  unsigned long long w_full[STAGES];  // packed weight tile landed (dequantisers wait)
+  unsigned long long x_full[STAGES];  // activation tile landed (MMA issuer waits)
   unsigned long long a_full[STAGES];
   unsigned long long mma_done[STAGES];
   unsigned long long accum_full;
@@ -64,6 +81,11 @@ struct __align__(1024) TileSmem {
   int abort_flag;
   int last;  // split-K: this CTA finishes its tile
 };
+
+// Each ring (plus 1 KB of alignment slack) fits the 227 KB of shared memory a CTA may use.
+static_assert(sizeof(TileSmem<64>) + 1024 <= 232448, "64-row ring too deep");
+static_assert(sizeof(TileSmem<128>) + 1024 <= 232448, "128-row ring too deep");
+static_assert(sizeof(TileSmem<256>) + 1024 <= 232448, "256-row ring too deep");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -115,6 +137,33 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Bounded wait for a phase that must complete whether or not the CTA is
+// aborting (copies and MMAs already issued): the CTA may not release its
+// shared memory or TMEM while they are in flight.
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
+  unsigned long long start = 0;
+  for (uint32_t i = 0;; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return;
+    if ((i & 255u) == 0u) {
+      const unsigned long long now = globaltimer();
+      if (i == 0) {
+        start = now;
+      } else if (now - start > kWaitNs) {
+        atomicOr(&g_device_error, 1);
+        return;
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
                                             uint32_t bar) {
   asm volatile(
@@ -148,6 +197,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
     nf4_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                        const __grid_constant__ CUtensorMap tmap_w, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
+  constexpr int STAGES = ring_stages<BT>();
   TileSmem<BT>& sm = *reinterpret_cast<TileSmem<BT>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -163,7 +213,8 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
   if (tid == 0) {
     sm.abort_flag = 0;
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(smem_u32(&sm.tma_full[s]), 1);
+      mbar_init(smem_u32(&sm.w_full[s]), 1);
+      mbar_init(smem_u32(&sm.x_full[s]), 1);
       mbar_init(smem_u32(&sm.a_full[s]), 4);
       mbar_init(smem_u32(&sm.mma_done[s]), 1);
     }
@@ -189,15 +240,26 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
 
   if (warp == 0) {
     if (lane == 0) {
+      int issued = 0;
       for (int i = 0; i < nkb; ++i) {
         const int kb = kb_lo + i, s = i % STAGES;
         if (i >= STAGES &&
             !mbar_wait(smem_u32(&sm.mma_done[s]), ((i / STAGES) - 1) & 1, abort_flag))
           break;
-        const uint32_t bar = smem_u32(&sm.tma_full[s]);
-        mbar_expect_tx(bar, BT * 128 + BM * 32);
-        tma_load_2d(smem_u32(sm.x[s]), &tmap_x, kb * BK, tok0, bar);
-        tma_load_2d(smem_u32(sm.w[s]), &tmap_w, kb * (BK / 2), n0, bar);
+        // the small weight tile first, on its own barrier, so that its
+        // dequantisation starts before the activation tile has landed
+        const uint32_t wbar = smem_u32(&sm.w_full[s]), xbar = smem_u32(&sm.x_full[s]);
+        mbar_expect_tx(wbar, BM * 32);
+        tma_load_2d(smem_u32(sm.w[s]), &tmap_w, kb * (BK / 2), n0, wbar);
+        mbar_expect_tx(xbar, BT * 128);
+        tma_load_2d(smem_u32(sm.x[s]), &tmap_x, kb * BK, tok0, xbar);
+        issued = i + 1;
+      }
+      // every copy issued has landed before the CTA can exit (immediate on the
+      // normal path: the consumers have waited for them all)
+      for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i) {
+        mbar_drain(smem_u32(&sm.w_full[i % STAGES]), (i / STAGES) & 1);
+        mbar_drain(smem_u32(&sm.x_full[i % STAGES]), (i / STAGES) & 1);
       }
     }
   } else if (warp == 1) {
@@ -207,7 +269,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
       for (int i = 0; i < nkb && ok; ++i) {
         const int s = i % STAGES;
         const uint32_t ph = (i / STAGES) & 1;
-        ok = mbar_wait(smem_u32(&sm.tma_full[s]), ph, abort_flag) &&
+        ok = mbar_wait(smem_u32(&sm.x_full[s]), ph, abort_flag) &&
              mbar_wait(smem_u32(&sm.a_full[s]), ph, abort_flag);
         if (!ok) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -230,6 +292,8 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
       asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
                        "r"(smem_u32(&sm.accum_full))
                    : "memory");
+      // every MMA issued has completed before TMEM is released
+      mbar_drain(smem_u32(&sm.accum_full), 0);
     }
   } else {
     // Dequantise: thread r of group grp owns weight row n0 + r.
@@ -238,20 +302,36 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
     const int row = n0 + r;
     const bool valid = row < p.N;
     const int rsw = r & 7;
-    for (int i = grp; i < nkb; i += DQ) {
-      const int kb = kb_lo + i, s = i % STAGES;
-      float scale = 0.f;
-      if (valid) {
-        const size_t b = ((size_t)row * p.K + (size_t)kb * BK) >> p.bs_shift;
-        if (p.nested)
-          scale = nested_scale(sm.code2[__ldg(p.a8 + b)], __ldg(p.absmax + (b >> p.bs2_shift)),
-                               p.offset);
-        else
-          scale = __ldg(p.absmax + b);
+    // The block scale's global loads run one of this group's k blocks ahead,
+    // so their latency hides under the previous block's dequantisation.
+    uint32_t code_next = 0;
+    float am_next = 0.f;
+    auto fetch_scale = [&](int i) {
+      if (valid && i < nkb) {
+        const size_t b = ((size_t)row * p.K + (size_t)(kb_lo + i) * BK) >> p.bs_shift;
+        if (p.nested) {
+          code_next = __ldg(p.a8 + b);
+          am_next = __ldg(p.absmax + (b >> p.bs2_shift));
+        } else {
+          am_next = __ldg(p.absmax + b);
+        }
       }
-      if (!mbar_wait(smem_u32(&sm.tma_full[s]), (i / STAGES) & 1, abort_flag)) break;
+    };
+    fetch_scale(grp);
+    // Row r's 32 packed bytes, its two 16-byte halves read in an order that
+    // alternates every 4 rows: the warp's 16-byte reads then cover all 8
+    // bank groups of each 128 bytes (no 2-way conflict).
+    const int hfirst = (r >> 2) & 1;
+    for (int i = grp; i < nkb; i += DQ) {
+      const int s = i % STAGES;
+      const uint32_t code = code_next;
+      const float am = am_next;
+      fetch_scale(i + DQ);
+      const float scale = !valid ? 0.f : p.nested ? nested_scale(sm.code2[code], am, p.offset) : am;
+      if (!mbar_wait(smem_u32(&sm.w_full[s]), (i / STAGES) & 1, abort_flag)) break;
       const uint4* wp = reinterpret_cast<const uint4*>(sm.w[s] + r * 32);
-      const uint4 u0 = wp[0], u1 = wp[1];
+      const uint4 ua = wp[hfirst], ub = wp[hfirst ^ 1];
+      const uint4 u0 = hfirst ? ub : ua, u1 = hfirst ? ua : ub;
       const uint32_t words[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
       uint8_t* arow = sm.a[s] + (r >> 3) * 1024 + rsw * 128;
       const ScaledLut lut = scaled_lut(scale);
