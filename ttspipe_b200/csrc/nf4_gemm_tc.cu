@@ -14,7 +14,9 @@
 //   warp 1     allocates TMEM (BT fp32 columns) and, from one thread, issues
 //              4 x tcgen05.mma (M=128, N=BT, K=16) per k block, committing each
 //              stage back to the producer and the whole tile to the epilogue.
-//   warps 2-5  dequantise: thread r owns weight row r of the tile; it forms the
+//   warps 2-17 four groups of four warps, k blocks round-robin over the
+//              groups, dequantise: thread r of a group owns weight row r of the
+//              tile; it forms the
 //              block's scale (plain fp32, or code2[a8] * absmax2 + offset as two
 //              rounded fp32 ops) and writes bf16(NF4[q] * scale) - bit-exact to
 //              bitsandbytes' dequantisation - into the K-major 128-byte-swizzled
@@ -24,7 +26,9 @@
 //
 // Every mbarrier wait is bounded: a wait that outlives kWaitNs sets the
 // library's device error word and a CTA-wide abort flag, after which every
-// role drains out, TMEM is released and the kernel returns.
+// role leaves its loop; the producer waits (bounded) for the copies it issued
+// and the MMA thread for its last commit, then TMEM is released and the kernel
+// returns.
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
