@@ -342,6 +342,16 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
     }
   }
 }
+// After a bounded wait gave up: wait (bounded again) for the n copies still in
+// flight in stages st, st + 1, ... of an R-stage ring, so that no copy lands in
+// shared memory the CTA has released.
+template <int R>
+__device__ __forceinline__ void drain_ring(uint32_t bar_s, int st, int n, uint32_t phase) {
+  for (int d = 0; d < n; ++d) {
+    const int sd = (st + d) % R;
+    (void)mbar_wait_bounded(bar_s + 8 * sd, (phase >> sd) & 1u);
+  }
+}
 
 // Bounded wait (2 s by %globaltimer) until the global count at `ctr` reaches
 // `need`, acquire; false after recording the timeout in g_gemv_error (bit 2).
@@ -706,7 +716,10 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     cp_async_commit();
     st_fill = st_fill + 1 == R ? 0 : st_fill + 1;
     cp_async_wait<R - 1>();  // unit u's scales (this lane's copies)
-    if (!mbar_wait_bounded(bar_s + 8 * st_use, (phase >> st_use) & 1u)) break;
+    if (!mbar_wait_bounded(bar_s + 8 * st_use, (phase >> st_use) & 1u)) {
+      drain_ring<R>(bar_s, st_use, min(R, u1 - u), phase);  // units u .. u + R - 1 were requested
+      break;
+    }
     phase ^= 1u << st_use;
     __syncwarp();            // every lane's scale copies are visible
     const uint8_t* wst = wring + st_use * WB;
@@ -1401,11 +1414,13 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     }
   };
 
+  int inflight = 0;  // unit copies requested and not yet consumed
 #pragma unroll
   for (int i = 0; i < R - 1; ++i) {
     if (lj < n_jobs) {
       issue(i);
       step_load();
+      ++inflight;
     }
     cp_async_commit();
   }
@@ -1475,14 +1490,17 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       if (lj < n_jobs) {
         issue(st_fill);
         step_load();
+        ++inflight;
       }
       cp_async_commit();
       st_fill = st_fill + 1 == R ? 0 : st_fill + 1;
       cp_async_wait<R - 1>();
       if (!mbar_wait_bounded(bar_s + 8 * st_use, (phase >> st_use) & 1u)) {
+        drain_ring<R>(bar_s, st_use, inflight, phase);
         s_ok = 0;
         break;
       }
+      --inflight;
       phase ^= 1u << st_use;
       __syncwarp();
       const uint8_t* wst = wring + st_use * WB;
