@@ -522,14 +522,22 @@ int gemm_bt(int N, int M, int sms) {
 
 // Split the k range of 64-row tiles when the output tiles alone cannot fill
 // the GPU: as many splits as keep every resident CTA slot busy, each of at
-// least 4 k blocks.
+// least 4 k blocks. When that is one (more than half the slots, fewer than all
+// of them, hold a tile), three splits still fit in two rounds of the slots and
+// each keeps at least 32 k blocks, three: two rounds of third-size CTAs then
+// beat one round of whole tiles (2560x9728 at M = 256, 80 tiles on 148 SMs:
+// 70.9 -> 59.4 us). With shorter splits the extra round costs more than it
+// saves (9728x2560 at M = 64: 22.6 -> 27.2 us; 2560x4096 at M = 256: 33.4 ->
+// 34.5 us), so those stay whole.
 int gemm_splits(int N, int M, int K, int sms) {
   const int bt = gemm_bt(N, M, sms);
   if (bt != 64) return 1;
   const long long tiles = (long long)((N + BM - 1) / BM) * ((M + bt - 1) / bt);
   if (tiles * (long long)sizeof(int) > (long long)GEMM_COUNTER_BYTES) return 1;
   const int occ = gemm_ctas_per_sm<64, true>();
-  long long s = (long long)sms * occ / tiles;
+  const long long slots = (long long)sms * occ;
+  long long s = slots / tiles;
+  if (s < 2 && 3 * tiles <= 2 * slots && K / BK >= 3 * 32) s = 3;
   const long long kmax = (K / BK) / 4;
   if (s > kmax) s = kmax;
   if (s > 16) s = 16;
