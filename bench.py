@@ -589,6 +589,17 @@ def run_gpu(args):
 CPU_SHAPES = [(6144, 2560), (2560, 4096), (19456, 2560), (2560, 9728)]  # wqkv, wo, w13, w2
 
 
+def cpu_layer_bytes(rows: int = 1) -> int:
+    """Bytes one layer pass of the reference's CPU kernel moves: packed codes,
+    the bf16 absmax it reads (2 B per 64-block; it takes no double-quantised
+    scales), x and y. The w13 output is 2 x 9728 wide on the CPU path (it
+    returns both products); the residual adds are not part of its GEMV."""
+    return sum(n * k // 2 + 2 * (n * k // BS) + 2 * rows * k + 2 * rows * n for n, k in CPU_SHAPES)
+
+
+CPU_LAYER_BYTES = cpu_layer_bytes()
+
+
 def _cpu_layers(count: int):
     """Random packed NF4 bytes and bf16 absmax for `count` layers, generated
     directly as the reference's own CPU test does (tests/test_nf4cpu.py:31-35);
@@ -650,11 +661,13 @@ def cpu_baseline(seconds: float) -> dict:
     while time.perf_counter() - t0 < seconds:
         for p, a, n, k in layers[li % len(layers)]:
             run(xs[k], p, a, n)
-        done_bytes += LAYER_BYTES
+        done_bytes += CPU_LAYER_BYTES
         li += 1
     el = time.perf_counter() - t0
     return {"value": round(done_bytes / el / 1e9, 2), "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{li} layer passes (wqkv, wo, w13, w2 at M=1; 4 distinct layers cycled) in {el:.1f}s; {note}"}
+            "sample": f"{li} layer passes (wqkv, wo, w13, w2 at M=1; 4 distinct layers cycled) in {el:.1f}s, "
+                      f"credited with the bytes the CPU kernel reads ({CPU_LAYER_BYTES} B per layer: bf16 absmax); "
+                      f"{note}"}
 
 
 def run_reference(args):
@@ -681,7 +694,7 @@ def run_reference(args):
     for _ in range(args.steps):
         step()
     el = time.perf_counter() - t0
-    step_bytes = n_layers * LAYER_BYTES
+    step_bytes = n_layers * CPU_LAYER_BYTES
     value = step_bytes * args.steps / el / 1e9
     # n_gpus: the N of the run this line stands beside (the reference's NF4 path is
     # CPU-only: rank 0 times it on the host cores, the GPUs stay idle)
@@ -691,10 +704,246 @@ def run_reference(args):
             "data": "synthetic (random packed NF4 bytes, bf16 absmax, x N(0,1))",
             "config": {"workload": f"{n_layers} layers x [wqkv 6144x2560, wo 2560x4096, w13 19456x2560, "
                                    "w2 2560x9728], M=1, NF4 bs64 (bf16 absmax, as the reference's CPU path)",
-                       "bytes_per_step": step_bytes},
+                       "bytes_per_step": step_bytes,
+                       "bytes": "what the CPU kernel reads: packed codes, bf16 absmax, x, y"},
             "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads, "kind": kind,
                              "sample": f"{args.steps} steps of {n_layers} layers; {note}"},
             "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+
+# --------------------------------------------------------------------------
+# profiling cases (`--case <kernel>`): small, self-contained cases of each
+# hot-path kernel for ncu captures and graph-replay timings
+# --------------------------------------------------------------------------
+#
+# `python bench.py --case <kernel> [options]` builds a few distinct weight
+# copies or caches (enough to exceed the 126 MB L2, a few hundred MB at most on
+# the device), warms up, and issues a bounded number of launches - sized so
+# that an `ncu --set full -k <kernel> -c 3` capture of it ends in a minute or
+# two. With `--time` it instead replays the launches from a CUDA graph and
+# prints CUDA-event timings (never under a profiler).
+#
+# kernels: gemv (M rows <= 32), gated (the W1/W3 gate, M <= 4), gemm (tcgen05,
+# M > 32), head (a bf16 output head, `--n` ids x `--k`), attention (decode,
+# qk_rope_kv + attention at a given cache length), prefill (the seven S2-Pro
+# projections at M rows through the GEMM, TFLOP/s), dualar (the config-5 frame
+# graph: `--frames` replays between cudaProfilerStart/Stop, for an
+# `ncu --profile-from-start off` launch list; with --time, ms per frame).
+
+S2PRO = [("q", 4096, 2560), ("k", 1024, 2560), ("v", 1024, 2560), ("o", 2560, 4096),
+         ("gate", 9728, 2560), ("up", 9728, 2560), ("down", 2560, 9728)]
+
+
+def _weights(n: int, k: int, copies: int, nested: bool):
+    import torch
+
+    from ttspipe_b200 import nf4gemv
+    from ttspipe_b200.quant import Linear4bit
+
+    mods = []
+    for i in range(copies):
+        g = torch.Generator(device="cuda").manual_seed(i)
+        w = torch.randn(n, k, generator=g, device="cuda") * 0.02
+        lin = Linear4bit.from_float(w, double_quant=nested)
+        assert nf4gemv.prepare(lin)
+        mods.append(lin)
+    return mods
+
+
+def _graph_time(fn, reps: int = 5) -> float:
+    """Microseconds per call of `fn`, replayed from a CUDA graph."""
+    import torch
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            fn()
+        g.replay()
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record(s)
+        for _ in range(reps):
+            g.replay()
+        en.record(s)
+    torch.cuda.synchronize()
+    return st.elapsed_time(en) * 1e3 / reps
+
+
+def run_matmul(n: int, k: int, rows: int, copies: int, launches: int, nested: bool, timed: bool) -> None:
+    import torch
+
+    from ttspipe_b200 import nf4gemv
+
+    mods = _weights(n, k, copies, nested)
+    x = torch.randn(rows, k, device="cuda").to(torch.bfloat16)
+    for m in mods:                       # warm-up: one launch per copy
+        nf4gemv.matmul(m, x)
+    torch.cuda.synchronize()
+    if timed:
+        us = _graph_time(lambda: [nf4gemv.matmul(mods[i % copies], x) for i in range(launches)]) / launches
+        flops = 2.0 * rows * n * k
+        print(f"{n}x{k} rows={rows}: {us:.2f} us/launch, {flops / us / 1e6:.1f} TFLOP/s")
+        return
+    for i in range(launches):
+        nf4gemv.matmul(mods[i % copies], x)
+    torch.cuda.synchronize()
+
+
+def run_prefill(rows: int) -> None:
+    """The seven S2-Pro projections at `rows` activation rows."""
+    import torch
+
+    from ttspipe_b200 import nf4gemv
+
+    total_flops, total_us = 0.0, 0.0
+    for name, n, k in S2PRO:
+        mods = _weights(n, k, 2, True)
+        x = torch.randn(rows, k, device="cuda").to(torch.bfloat16)
+        us = _graph_time(lambda: [nf4gemv.matmul(mods[i % 2], x) for i in range(4)]) / 4
+        flops = 2.0 * rows * n * k
+        total_flops += flops
+        total_us += us
+        print(f"  {name} {n}x{k} M={rows}: {us:.1f} us, {flops / us / 1e6:.1f} TFLOP/s")
+    print(f"layer M={rows}: {total_us:.1f} us, {total_flops / total_us / 1e6:.1f} TFLOP/s")
+
+
+def run_gated(n: int, k: int, rows: int, copies: int, launches: int, timed: bool) -> None:
+    """The FeedForward gate silu(x W1^T) * (x W3^T) in one launch per pair."""
+    import torch
+
+    from ttspipe_b200 import nf4gemv
+
+    mods = _weights(n, k, 2 * copies, True)
+    x = torch.randn(rows, k, device="cuda").to(torch.bfloat16)
+    for i in range(copies):
+        nf4gemv.matmul_gated(mods[2 * i], mods[2 * i + 1], x)
+    torch.cuda.synchronize()
+
+    def go(i):
+        nf4gemv.matmul_gated(mods[2 * (i % copies)], mods[2 * (i % copies) + 1], x)
+
+    if timed:
+        us = _graph_time(lambda: [go(i) for i in range(launches)]) / launches
+        print(f"gated 2x{n}x{k} rows={rows}: {us:.2f} us/launch, {2 * n * k / 2 / us / 1e3:.0f} GB/s of codes")
+        return
+    for i in range(launches):
+        go(i)
+    torch.cuda.synchronize()
+
+
+def run_attention(length: int, launches: int, timed: bool) -> None:
+    import torch
+
+    from ttspipe_b200 import fastpath
+
+    nh, nkv, max_len = 32, 8, 2048
+    layers = 16   # 16 distinct caches of 8.4 MB = 134 MB > L2
+    ks = [torch.randn(nkv, max_len, 128, device="cuda").to(torch.bfloat16) for _ in range(layers)]
+    vs = [torch.randn(nkv, max_len, 128, device="cuda").to(torch.bfloat16) for _ in range(layers)]
+    q = torch.randn(nh, 128, device="cuda").to(torch.bfloat16)
+    out = torch.empty(nh, 128, device="cuda", dtype=torch.bfloat16)
+    pos = torch.tensor([length - 1], device="cuda")
+
+    def go(i):
+        fastpath.kernel_attention(q, ks[i % layers], vs[i % layers], out, n_head=nh, n_kv=nkv,
+                                  pos=pos, window=max_len, max_len=max_len)
+
+    for i in range(layers):
+        go(i)
+    torch.cuda.synchronize()
+    if timed:
+        us = _graph_time(lambda: [go(i) for i in range(layers)]) / layers
+        kv_bytes = 2 * nkv * length * 128 * 2
+        print(f"decode attention L={length}: {us:.2f} us/launch, {kv_bytes / us / 1e3:.0f} GB/s of KV")
+        return
+    for i in range(launches):
+        go(i)
+    torch.cuda.synchronize()
+
+
+def run_case_dualar(frames: int, timed: bool) -> None:
+    """The Dual-AR frame graph (random-init model, 512-token prompt, 3 warm replays)."""
+    import torch
+
+    from ttspipe_b200.dualar import DualARConfig, DualARDecoder
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    dec = DualARDecoder(DualARConfig(), dev, seed=17)
+    g = torch.Generator().manual_seed(0)
+    dec.prefill(torch.randint(0, dec.cfg.vocab, (512,), generator=g).to(dev))
+    dec.capture()
+    for _ in range(3):
+        dec.replay()
+    torch.cuda.synchronize()
+    if timed:
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        for _ in range(frames):
+            dec.replay()
+        en.record()
+        torch.cuda.synchronize()
+        print(f"dual-AR frame: {st.elapsed_time(en) / frames:.3f} ms")
+    else:
+        torch.cuda.profiler.start()
+        for _ in range(frames):
+            dec.replay()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+    dec.release()
+
+
+def run_head(n: int, k: int, copies: int, launches: int, timed: bool) -> None:
+    """A bf16 output head (the LM head 155136 x 2560, or a codebook head 4096 x
+    2560) on one activation row: `heads.dense_linear`."""
+    import torch
+
+    from ttspipe_b200 import heads
+
+    copies = max(1, min(copies, (1 << 30) // (n * k * 2) + 1))  # >= 1 GB of distinct weights in all
+    ws = [(torch.randn(n, k, device="cuda") * 0.02).to(torch.bfloat16) for _ in range(copies)]
+    x = torch.randn(k, device="cuda").to(torch.bfloat16)
+    out = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+
+    def go(i):
+        heads.dense_linear(ws[i % copies], x, out=out)
+
+    for i in range(copies):
+        go(i)
+    torch.cuda.synchronize()
+    if timed:
+        reps = max(copies, 4)
+        us = _graph_time(lambda: [go(i) for i in range(reps)]) / reps
+        print(f"dense head {n}x{k}: {us:.2f} us/launch, {n * k * 2 / us / 1e3:.0f} GB/s")
+        return
+    for i in range(launches):
+        go(i)
+    torch.cuda.synchronize()
+
+
+
+
+def run_case(a) -> None:
+    from ttspipe_b200 import nf4gemv
+
+    assert nf4gemv.available()
+    if a.case in ("gemv", "gemm"):
+        rows = a.rows if a.case == "gemv" else max(a.rows, 33)
+        run_matmul(a.n, a.k, rows, a.copies, a.launches, not a.plain, a.time)
+    elif a.case == "prefill":
+        run_prefill(a.rows)
+    elif a.case == "gated":
+        run_gated(a.n, a.k, a.rows, a.copies, a.launches, a.time)
+    elif a.case == "dualar":
+        run_case_dualar(a.frames, a.time)
+    elif a.case == "head":
+        run_head(a.n, a.k, a.copies, a.launches, a.time)
+    else:
+        run_attention(a.length, a.launches, a.time)
+    print("ok", file=sys.stderr)
 
 
 def main():
@@ -713,8 +962,23 @@ def main():
     ap.add_argument("--prefetch-distance", type=int, default=0,
                     help="launches ahead whose weights each launch streams into L2 (0: none; "
                          "measured slower at 1-3 on B200, so off by default)")
+    ap.add_argument("--case", default=None,
+                    choices=["gemv", "gated", "gemm", "attention", "prefill", "dualar", "head"],
+                    help="run one profiling case instead of the benchmark (see 'profiling cases')")
+    ap.add_argument("--n", type=int, default=9728)
+    ap.add_argument("--k", type=int, default=2560)
+    ap.add_argument("--rows", type=int, default=1)
+    ap.add_argument("--copies", type=int, default=12)
+    ap.add_argument("--launches", type=int, default=12)
+    ap.add_argument("--plain", action="store_true", help="--case: fp32 absmax instead of double quant")
+    ap.add_argument("--length", type=int, default=2048)
+    ap.add_argument("--time", action="store_true", help="--case: time from a CUDA graph instead")
+    ap.add_argument("--frames", type=int, default=2, help="--case dualar: frames replayed")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.case is not None:
+        run_case(args)
+        return
     if args.impl == "reference":
         res = run_reference(args)
     else:

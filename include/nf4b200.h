@@ -208,12 +208,17 @@ size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows);
  * device pointers from another runtime, a graph being recorded): the GEMV's
  * partial sums and counters live in a 4 MiB scratch array built into the
  * library, which every GPU that loads it keeps until exit. No counterpart in
- * the reference. Limits: calls whose scratch need (nf4b_gemm_workspace_size)
- * exceeds NF4B_NOALLOC_SCRATCH_BYTES fail with NF4B_ERR_WORKSPACE; more than
- * 32 rows run the GEMM, which needs no scratch. The first call on a device
- * looks the scratch's device address up, so make it before any stream
- * capture. All calls share the scratch: each clears its counters first, and
- * calls that overlap on the GPU (other streams or threads) race.
+ * the reference. Limits: GEMV calls (1..32 rows) whose scratch need
+ * (nf4b_gemm_workspace_size) exceeds NF4B_NOALLOC_SCRATCH_BYTES fail with
+ * NF4B_ERR_WORKSPACE. More than 32 rows run the tensor-core GEMM, which puts
+ * its split-K partial sums in the same scratch when they fit (so it splits
+ * exactly as nf4b_gemm with a workspace does) and otherwise runs unsplit;
+ * those calls share the scratch too. The first call on a device looks the
+ * scratch's device address up and keeps it for the life of the process, so
+ * make it before any stream capture, and do not reset the device
+ * (cudaDeviceReset) between calls. All calls share the scratch: each clears
+ * its counters first, and calls that overlap on the GPU (other streams or
+ * threads) race.
  */
 int nf4b_gemm_noalloc(const nf4b_weight* w, const void* x, void* y, int rows, int epi,
                       const void* operand, void* stream);

@@ -64,9 +64,16 @@ def load():
     return mod
 
 
-def reference_source(reference_root: str = "/root/reference") -> str:
+def reference_root() -> Path:
+    """The read-only reference checkout: ``$TTSPIPE_REFERENCE`` when set, else a
+    directory named ``reference`` beside this repository."""
+    env = os.environ.get("TTSPIPE_REFERENCE")
+    return Path(env) if env else HERE.parent.parent / "reference"
+
+
+def reference_source(reference_root_dir: str | None = None) -> str:
     """The C++ source string of the reference's nf4cpu module, read in place."""
-    root = Path(reference_root)
+    root = Path(reference_root_dir) if reference_root_dir else reference_root()
     if not (root / "app" / "engine" / "nf4cpu.py").exists():
         raise FileNotFoundError(f"reference checkout not found at {root}")
     sys.path.insert(0, str(root))
@@ -77,11 +84,11 @@ def reference_source(reference_root: str = "/root/reference") -> str:
         sys.path.remove(str(root))
 
 
-def build(reference_root: str = "/root/reference", verbose: bool = False) -> Path:
+def build(reference_root_dir: str | None = None, verbose: bool = False) -> Path:
     """Compile the reference's nf4cpu source into oracle/_ref/. Returns the .so path."""
     from torch.utils.cpp_extension import load_inline
 
-    source = reference_source(reference_root)
+    source = reference_source(reference_root_dir)
     os.environ["CXX"] = "/usr/bin/g++"
     REF_DIR.mkdir(parents=True, exist_ok=True)
     with tempfile.TemporaryDirectory(prefix="nf4cpu_ref_") as tmp:

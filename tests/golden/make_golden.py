@@ -16,9 +16,21 @@ below) and the reference's CPU extension has been built by
 * ``attention.npz``     - the reference's torch ``decode_attention``
                           (app/engine/fastpath.py:133-174) for decode and
                           short-prefill shapes.
+* ``sampler.npz``       - the reference's torch sampler ``_sample_torch``
+                          (app/engine/graphs.py:55-73): the kept set and the
+                          final probabilities of seeded logit rows. Its last
+                          line hands the probabilities to the fish-speech
+                          fork's ``multinomial_sample_one_no_sync``; the fork
+                          is not in the checkout, so a stand-in module returns
+                          the probabilities it is given instead of drawing.
+                          Every line that decides the kept set and the
+                          probabilities is the reference's own.
 
 Inputs are stored next to outputs so the tests need neither the reference nor
-a random generator to replay them. Run: ``python tests/golden/make_golden.py``.
+a random generator to replay them. Run: ``python tests/golden/make_golden.py
+[fixture ...]`` (all fixtures when none is named). The reference checkout is
+``$TTSPIPE_REFERENCE``, or a directory named ``reference`` next to this
+repository.
 """
 
 from __future__ import annotations
@@ -36,7 +48,7 @@ sys.path.insert(0, str(ROOT))
 from oracle import build_ref  # noqa: E402
 from oracle import nf4_oracle as orc  # noqa: E402
 
-REFERENCE = "/root/reference"
+REFERENCE = str(build_ref.reference_root())
 
 
 def bits(t: torch.Tensor) -> np.ndarray:
@@ -184,17 +196,117 @@ def attention() -> dict:
     return out
 
 
-def main() -> None:
-    if build_ref.so_path() is None:
-        build_ref.build()
-    ext = build_ref.load()
-    np.savez_compressed(HERE / "nf4_code.npz", **nf4_code())
-    np.savez_compressed(HERE / "gemv.npz", **gemv(ext))
-    np.savez_compressed(HERE / "decode_block.npz", **decode_blocks(ext))
-    np.savez_compressed(HERE / "attention.npz", **attention())
+def _fork_stand_in():
+    """Register a stand-in for the one fork function `_sample_torch` calls,
+    `multinomial_sample_one_no_sync(probs)`: it returns `probs` itself, so the
+    reference function hands back the probability row it would draw from."""
+    import types
+
+    names = ["fish_speech", "fish_speech.models", "fish_speech.models.text2semantic",
+             "fish_speech.models.text2semantic.inference"]
+    for n in names:
+        sys.modules.setdefault(n, types.ModuleType(n))
+    sys.modules[names[-1]].multinomial_sample_one_no_sync = lambda probs: probs
+
+
+def _bf16_below(b: int) -> int:
+    """The largest bf16 value below the bf16 bit pattern b (finite, not -max)."""
+    if b & 0x8000:
+        return b + 1                  # negative: one step further from zero
+    return 0x8001 if b == 0 else b - 1
+
+
+def _distinct_top(v: np.ndarray, top: int) -> np.ndarray:
+    """bf16 bits of the fp32 row v with no two equal values among its `top`
+    largest (ties would make the reference's unstable sort order matter):
+    walking down from the largest, a value equal to or above its predecessor
+    becomes the next bf16 value below it; every other value is then held
+    strictly below the last of them."""
+    b = orc.f32_to_bf16(v.astype(np.float32))
+    f = orc.bf16_to_f32(b)
+    idx = np.argsort(-f, kind="stable")
+    head, rest = idx[:top], idx[top:]
+    prev = None
+    for i in head:
+        if prev is not None and orc.bf16_to_f32(b[i:i + 1])[0] >= orc.bf16_to_f32(np.array([prev], np.uint16))[0]:
+            b[i] = _bf16_below(int(prev))
+        prev = int(b[i])
+    floor = _bf16_below(prev)
+    fl = orc.bf16_to_f32(np.array([floor], np.uint16))[0]
+    over = rest[orc.bf16_to_f32(b[rest]) > fl]
+    b[over] = floor
+    hv = np.sort(orc.bf16_to_f32(b))[::-1][:top + 1]
+    assert np.all(np.diff(hv) < 0), "the top values are not distinct"
+    return b
+
+
+def sampler() -> dict:
+    """Kept sets and probabilities of the reference's torch sampler."""
+    sys.path.insert(0, REFERENCE)
+    _fork_stand_in()
+    from app.engine.graphs import _sample_torch
+
+    out = {}
+    # (name, vocab, logit scale, temperature, top_p, top_k)
+    cases = [("flat", 4096, 1.0, 0.7, 0.8, 64), ("peaked", 4096, 4.0, 0.7, 0.8, 64),
+             ("high", 4096, 3.0, 1.0, 0.9, 64), ("topk5", 4096, 2.0, 0.7, 0.99, 5),
+             ("first", 4096, 2.0, 0.7, 0.01, 64), ("cold", 4096, 2.0, 1e-6, 0.8, 64),
+             ("wide", 32768, 5.0, 0.7, 0.8, 64), ("vocab", 155136, 6.0, 0.7, 0.8, 64)]
+    for ci, (name, vocab, scale, temp, top_p, top_k) in enumerate(cases):
+        rng = np.random.default_rng(500 + ci)
+        for attempt in range(50):
+            bits_row = _distinct_top(rng.standard_normal(vocab) * scale, 80)
+            logits = torch.from_numpy(orc.bf16_to_f32(bits_row)).view(1, 1, vocab)
+            probs = _sample_torch(logits, torch.tensor(temp), torch.tensor(top_p),
+                                  torch.tensor(top_k))
+            p = probs.reshape(-1).double().numpy()
+            # The kept set does not depend on the temperature (the reference
+            # cuts on the unscaled logits); at temperature 1 every kept entry
+            # has a nonzero probability, which shows the set even where a tiny
+            # temperature rounds the others' probabilities to zero.
+            p1 = _sample_torch(logits, torch.tensor(1.0), torch.tensor(top_p),
+                               torch.tensor(top_k)).reshape(-1).double().numpy()
+            # keep rows whose cumulative probabilities stay clear of top_p (fp32
+            # here, fp64 in the oracle) so the kept set cannot depend on rounding
+            sv = np.sort(orc.bf16_to_f32(bits_row).astype(np.float64))[::-1]
+            e = np.exp(sv - sv[0])
+            cum = np.cumsum(e / e.sum())[:top_k + 1]
+            if np.min(np.abs(cum - top_p)) > 1e-4:
+                break
+        else:
+            raise RuntimeError(f"no clear row for {name}")
+        kept = np.nonzero(p1 > 0)[0]
+        kept = kept[np.argsort(-p1[kept], kind="stable")]
+        out[f"{name}_logits"] = bits_row
+        out[f"{name}_params"] = np.array([temp, top_p, top_k], dtype=np.float64)
+        out[f"{name}_kept"] = kept.astype(np.int64)
+        out[f"{name}_probs"] = p[kept].astype(np.float32)
+    out["cases"] = np.array([c[0] for c in cases])
+    return out
+
+
+FIXTURES = ("nf4_code", "gemv", "decode_block", "attention", "sampler")
+
+
+def main(which=None) -> None:
+    which = list(which or FIXTURES)
+    if any(w in which for w in ("gemv", "decode_block")):
+        if build_ref.so_path() is None:
+            build_ref.build()
+        ext = build_ref.load()
+    if "nf4_code" in which:
+        np.savez_compressed(HERE / "nf4_code.npz", **nf4_code())
+    if "gemv" in which:
+        np.savez_compressed(HERE / "gemv.npz", **gemv(ext))
+    if "decode_block" in which:
+        np.savez_compressed(HERE / "decode_block.npz", **decode_blocks(ext))
+    if "attention" in which:
+        np.savez_compressed(HERE / "attention.npz", **attention())
+    if "sampler" in which:
+        np.savez_compressed(HERE / "sampler.npz", **sampler())
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])

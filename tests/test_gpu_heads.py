@@ -98,3 +98,28 @@ def test_sampler_replays_from_a_cuda_graph():
         torch.cuda.synchronize()
         assert int(out.item()) == orc.sample_token(bits, 0.7, 0.8, 64, 5, i)[0]
     del g
+
+
+_SAMPLER_GOLDEN = np.load(__import__("pathlib").Path(__file__).resolve().parent / "golden" / "sampler.npz")
+
+
+@pytest.mark.parametrize("case", [str(c) for c in _SAMPLER_GOLDEN["cases"]])
+def test_sampler_on_the_reference_sampler_rows(case):
+    """The rows whose kept sets and probabilities tests/golden/make_golden.py
+    took from the reference's own torch sampler (app/engine/graphs.py:55-73):
+    at every step the device draws the oracle's token, and the oracle's kept
+    set on these rows is the reference's (tests/test_oracle_golden.py), so
+    every token drawn lies in the reference's kept set."""
+    from tests.helpers import from_bits
+
+    bits = _SAMPLER_GOLDEN[f"{case}_logits"]
+    temp, top_p, top_k = _SAMPLER_GOLDEN[f"{case}_params"]
+    ref_kept = set(int(i) for i in _SAMPLER_GOLDEN[f"{case}_kept"])
+    logits = from_bits(bits, device="cuda")
+    step = torch.zeros(1, dtype=torch.int64, device="cuda")
+    for s in range(16):
+        step.fill_(s)
+        got = int(heads.sample(logits, temperature=float(temp), top_p=float(top_p), top_k=int(top_k), seed=99,
+                               step=step).item())
+        want = orc.sample_token(bits, float(temp), float(top_p), int(top_k), 99, s)[0]
+        assert got == want and got in ref_kept, (s, got, want)

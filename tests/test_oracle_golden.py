@@ -1,8 +1,9 @@
 """Pin the oracle against fixtures computed by the reference itself.
 
 The fixtures in tests/golden/ were produced by tests/golden/make_golden.py from
-the reference's own C++ CPU kernels (app/engine/nf4cpu.py) and its torch
-attention (app/engine/fastpath.py:133-174). The bars are the reference's own:
+the reference's own C++ CPU kernels (app/engine/nf4cpu.py), its torch
+attention (app/engine/fastpath.py:133-174) and its torch sampler
+(app/engine/graphs.py:55-73). The bars are the reference's own:
 tests/test_nf4cpu.py (norm-relative < 5e-3 for the GEMV, < 2e-2 for a block)
 and tests/test_nf4gemv.py (max-relative < 5e-3 for attention).
 """
@@ -123,3 +124,34 @@ def test_sampler_oracle_follows_the_reference_rule():
     tok, kept, _ = orc.sample_token(bits, 1.0, 1.0, 3, 0, 0)
     assert list(kept) == [4, 0, 1]   # top_k
     assert 0.0 <= orc.sample_uniform(7, 3) < 1.0
+
+
+SAMPLER = np.load(GOLDEN / "sampler.npz")
+
+
+@pytest.mark.parametrize("case", [str(c) for c in SAMPLER["cases"]])
+def test_sampler_oracle_matches_the_reference_sampler(case):
+    """The kept set and the final probabilities of the reference's own torch
+    sampler (sort, softmax of the unscaled row, the top-p / top-k cut that
+    always keeps position 0, temperature, softmax; app/engine/graphs.py:64-72),
+    run on seeded rows by tests/golden/make_golden.py. The reference works in
+    fp32 and the oracle in fp64: the kept set must be the same and the
+    probabilities agree to fp32 rounding. (The final draw cannot be compared
+    token for token: the reference races one torch.rand per vocabulary entry,
+    the device draws one counter-based uniform - both sample this distribution.)"""
+    logits = SAMPLER[f"{case}_logits"]
+    temp, top_p, top_k = SAMPLER[f"{case}_params"]
+    _, kept, q = orc.sample_token(logits, float(temp), float(top_p), int(top_k), seed=1, step=0)
+    assert list(kept) == list(SAMPLER[f"{case}_kept"])
+    np.testing.assert_allclose(q, SAMPLER[f"{case}_probs"], rtol=2e-6, atol=1e-7)
+
+
+def test_sampler_uniform_is_uniform():
+    """The draw's uniform over consecutive steps (one seed): a Kolmogorov-
+    Smirnov test against U(0, 1), so an inverse-CDF draw samples the kept
+    distribution, as the reference's exponential race does."""
+    from scipy import stats
+
+    u = np.array([orc.sample_uniform(12345, s) for s in range(20000)])
+    assert stats.kstest(u, "uniform").pvalue > 1e-3
+    assert abs(u.mean() - 0.5) < 0.01

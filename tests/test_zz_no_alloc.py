@@ -94,11 +94,43 @@ def test_noalloc_refuses_a_call_larger_than_its_scratch():
     assert torch.all(y == 7.0)   # nothing was launched
 
 
-def test_noalloc_hands_prefill_to_the_gemm_without_scratch():
+def test_noalloc_gemm_splits_its_k_range_in_the_scratch():
+    """More than 32 rows run the tensor-core GEMM. Where its split-K partial
+    sums fit the built-in scratch (1024x2560 at 64 rows splits the k range
+    across CTAs), it splits exactly as nf4b_gemm does with a workspace, so the
+    two give the same bits - twice in a row on the shared scratch."""
     layer = make_linear(1024, 2560, seed=21)
     desc = layer._nf4_fast["desc"]
-    x = randn_bf16((64, 2560), seed=22, device="cuda")
-    st, got = _noalloc(desc, x, 64, 1024)
-    assert st == 0, _lib.last_error()
-    assert torch.equal(got, nf4gemv.matmul(layer, x))
+    rows = 64
+    need = int(_lib.lib().nf4b_gemm_workspace_size(ctypes.byref(desc), rows))
+    assert 0 < need <= NOALLOC_SCRATCH_BYTES, "this call must take the split path"
+    x = randn_bf16((rows, 2560), seed=22, device="cuda")
+    want = _with_workspace(desc, x, rows, 1024)
+    for _ in range(2):
+        st, got = _noalloc(desc, x, rows, 1024)
+        assert st == 0, _lib.last_error()
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+    check_matmul(got, x, layer)
     assert np.isfinite(got.float().cpu().numpy()).all()
+
+
+def test_noalloc_gemm_too_large_for_the_scratch_runs_unsplit():
+    """A GEMM whose split-K sums would not fit the scratch (2560x9728 at 256
+    rows splits three ways, ~7.9 MB) is not refused: it runs unsplit, which is
+    what nf4b_gemm does when it is given no workspace."""
+    layer = make_linear(2560, 9728, seed=31)
+    desc = layer._nf4_fast["desc"]
+    rows = 256
+    L = _lib.lib()
+    assert int(L.nf4b_gemm_workspace_size(ctypes.byref(desc), rows)) > NOALLOC_SCRATCH_BYTES
+    x = randn_bf16((rows, 9728), seed=32, device="cuda")
+    want = torch.empty((rows, 2560), dtype=torch.bfloat16, device="cuda")
+    assert L.nf4b_gemm(ctypes.byref(desc), x.data_ptr(), want.data_ptr(), rows, 0, None, None, 0, None) == 0
+    for _ in range(2):
+        st, got = _noalloc(desc, x, rows, 2560)
+        assert st == 0, _lib.last_error()
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+    check_matmul(got, x, layer)
+    assert L.nf4b_device_error(0) == 0

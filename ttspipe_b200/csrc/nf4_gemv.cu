@@ -296,6 +296,12 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
 
 // TMA and mbarrier helpers for the pair kernel.
 __device__ int g_gemv_error = 0;  // a bounded wait gave up: bit 0 weight stream, bit 1 split-tile reduce
+// How long a bounded wait on another CTA or on a copy lasts before it gives up
+// (nanoseconds of %globaltimer). 2 s; nf4b_debug_set_wait_limit shortens it
+// for the failure-detection tests. The drain after a timeout keeps its own
+// fixed limit (kDrainNs), so copies still in flight always land first.
+__device__ unsigned long long g_gemv_wait_ns = 2000000000ull;
+constexpr unsigned long long kDrainNs = 2000000000ull;
 
 __device__ __forceinline__ unsigned long long gemv_globaltimer() {
   unsigned long long t;
@@ -333,23 +339,27 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
   if (mbar_try(bar, parity)) return true;
-  const unsigned long long start = gemv_globaltimer();
+  const unsigned long long start = gemv_globaltimer(), limit = g_gemv_wait_ns;
   for (uint32_t i = 1;; ++i) {
     if (mbar_try(bar, parity)) return true;
-    if ((i & 63u) == 0u && gemv_globaltimer() - start > 2000000000ull) {
+    if ((i & 63u) == 0u && gemv_globaltimer() - start > limit) {
       atomicOr(&g_gemv_error, 1);
       return false;
     }
   }
 }
-// After a bounded wait gave up: wait (bounded again) for the n copies still in
-// flight in stages st, st + 1, ... of an R-stage ring, so that no copy lands in
-// shared memory the CTA has released.
+// After a bounded wait gave up: wait for the n copies still in flight in
+// stages st, st + 1, ... of an R-stage ring, so that no copy lands in shared
+// memory the CTA has released - all of them within one deadline (kDrainNs
+// from the start of the drain), after which the rest are not waited for.
 template <int R>
 __device__ __forceinline__ void drain_ring(uint32_t bar_s, int st, int n, uint32_t phase) {
+  const unsigned long long deadline = gemv_globaltimer() + kDrainNs;
   for (int d = 0; d < n; ++d) {
     const int sd = (st + d) % R;
-    (void)mbar_wait_bounded(bar_s + 8 * sd, (phase >> sd) & 1u);
+    const uint32_t bar = bar_s + 8 * sd, par = (phase >> sd) & 1u;
+    for (uint32_t i = 0; !mbar_try(bar, par); ++i)
+      if ((i & 63u) == 63u && gemv_globaltimer() > deadline) return;
   }
 }
 
@@ -365,7 +375,7 @@ __device__ __forceinline__ bool mbar_free_wait_count(const int* ctr, int need) {
       const unsigned long long now = gemv_globaltimer();
       if (i == 0) {
         start = now;
-      } else if (now - start > 2000000000ull) {
+      } else if (now - start > g_gemv_wait_ns) {
         atomicOr(&g_gemv_error, 4);
         return false;
       }
@@ -511,6 +521,34 @@ __device__ __forceinline__ void finish_split_tile(const GemvParams& p, int rt, i
   } else {
     if (ra < N) p.y[oa] = epilogue_value(v[0][0], p.epi, bf2f(opa));
     if (rb < N) p.y[ob] = epilogue_value(v[0][1], p.epi, bf2f(opb));
+  }
+}
+
+// A warp that gave up on a wait while computing unit tile `rt_now` of its run
+// [u0, u1) still counts itself into the split tiles it has not published (the
+// current one and the run's last), with zero partial sums, so every tile
+// counter returns to zero after the last contributor's reduction and the
+// caller's workspace stays reusable. The outputs of such a call are invalid;
+// nf4b_device_error reports it.
+template <bool kGated>
+__device__ __forceinline__ void abort_split_tiles(const GemvParams& p, int rt_now, int u0, int u1, int gw, int g,
+                                                  int t, int lane, int& split_a, int& old_a, int& split_b,
+                                                  int& old_b) {
+  const int per_tile = p.blocks_per_tile * (kGated ? 2 : 1);
+  const int rt_last = (u1 - 1) / per_tile;
+  const float zero[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+  for (int rt = rt_now; rt <= rt_last; rt += (rt_last > rt_now ? rt_last - rt_now : 1)) {
+    const int t0 = rt * per_tile;
+    if (t0 >= u0 && t0 + per_tile - 1 < u1) continue;  // a whole tile: nobody waits on it
+    int old = 0;
+    publish_pair_tile<kGated>(p, rt, u0, u1, gw, g, t, lane, zero, old);
+    if (split_a < 0) {
+      split_a = rt;
+      old_a = old;
+    } else {
+      split_b = rt;
+      old_b = old;
+    }
   }
 }
 
@@ -718,6 +756,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     cp_async_wait<R - 1>();  // unit u's scales (this lane's copies)
     if (!mbar_wait_bounded(bar_s + 8 * st_use, (phase >> st_use) & 1u)) {
       drain_ring<R>(bar_s, st_use, min(R, u1 - u), phase);  // units u .. u + R - 1 were requested
+      abort_split_tiles<kGated>(p, ct, u0, u1, gw, g, t, lane, split_a, old_a, split_b, old_b);
       break;
     }
     phase ^= 1u << st_use;
@@ -1497,6 +1536,10 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       cp_async_wait<R - 1>();
       if (!mbar_wait_bounded(bar_s + 8 * st_use, (phase >> st_use) & 1u)) {
         drain_ring<R>(bar_s, st_use, inflight, phase);
+        if (J.gated)
+          abort_split_tiles<true>(q, ct, u0, u1, gw, g, t, lane, split_a, old_a, split_b, old_b);
+        else
+          abort_split_tiles<false>(q, ct, u0, u1, gw, g, t, lane, split_a, old_a, split_b, old_b);
         s_ok = 0;
         break;
       }
@@ -1595,7 +1638,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
         acc_a = acc_b = acc3_a = acc3_b = 0.f;
       }
     }
-    if (s_ok) {
+    {  // after an abort too: the last contributor still re-zeroes each counter
       if (J.gated) {
         if (split_a >= 0) finish_split_tile<true>(q, split_a, old_a, g, t, lane);
         if (split_b >= 0) finish_split_tile<true>(q, split_b, old_b, g, t, lane);

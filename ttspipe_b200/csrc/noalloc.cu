@@ -14,8 +14,10 @@
 // (4 MiB), so every GPU that loads the library holds it until the process
 // exits. Host code may not use the array's name as a device pointer: the
 // first call on each device looks its device address up with
-// cudaGetSymbolAddress (with that device current) and reuses it afterwards.
-// That first call should therefore happen before any stream capture.
+// cudaGetSymbolAddress (with that device current) and reuses it for the life
+// of the process. That first call should therefore happen before any stream
+// capture, and a device must not be reset (cudaDeviceReset, or destroying its
+// primary context) between calls: the kept address would then be stale.
 //
 // All calls on a device share the one array and it keeps whatever the last
 // call left in it. Each call clears the arrival counters it relies on
