@@ -1,24 +1,32 @@
 """Benchmark: NF4 decode GEMV GB/s on B200 (one replica per GPU).
 
 Workload (`config.workload`): the decode-time NF4 matmuls of the S2-Pro slow AR
-at M=1 (blocksize 64, double-quantised scales), per layer: wqkv 6144x2560,
-wo 2560x4096 (+residual), the FeedForward gate silu(x W1^T) * (x W3^T) with
-W1, W3 9728x2560, and w2 2560x9728 (+residual). A step is one pass over 36
-distinct layers (1.87 GB of NF4 weights, far larger than the 126 MB L2, so
-every step streams from HBM). Each layer issues its matmuls in stream order as
-a decode step does: wqkv, wo (+residual), the gate (one nf4b_gemm_gated
-launch), w2 (+residual) - 4 C-ABI launches per layer, captured once as a CUDA
-graph. Each launch names the weights of a later launch as an L2 prefetch hint
-(`--prefetch-distance`). Weights ~ N(0, 0.02) and activations ~ N(0, 1),
-seeded per layer and rank (synthetic; no checkpoint).
+at M=1 (blocksize 64, double-quantised scales), per layer in the order and with
+the data flow of the reference's decode block (app/engine/fusedlayer.py:212-269)
+minus attention: wqkv 6144x2560 on RMSNorm(h) (attention_norm fused), wo
+2560x4096 on the attention output (a seeded stand-in per layer) + h, the
+FeedForward gate silu(x W1^T) * (x W3^T) with W1, W3 9728x2560 on
+RMSNorm(wo's output) (ffn_norm fused), and w2 2560x9728 on the gate + wo's
+output; the next layer's h is w2's output. A step is one pass over 36 distinct
+layers (1.87 GB of NF4 weights, far larger than the 126 MB L2, so every step
+streams from HBM). Weights ~ N(0, 0.02), norm weights ~ N(1, 0.1), the first
+h and the attention stand-ins ~ N(0, 1), seeded per layer and rank
+(synthetic; no checkpoint).
+
+Schedules (`--mode`, see MODES): `step` runs the whole step as ONE
+nf4b_decode_step launch (the persistent decode-step kernel); `decode` issues
+the 4 matmuls of each layer as separate C-ABI launches (nf4b_gemm_ex /
+nf4b_gemm_gated with the fused norms), captured as one CUDA graph.
 
 value  = algorithmic bytes of all ranks' steps / max-over-ranks device time
 e2e    = the same metric through the C ABI with host buffers: every step
-         copies its inputs from pinned host memory, replays the calls and
-         reads every output back to pinned host memory, inside the timed region.
+         copies its inputs (the first h and the attention stand-ins) from
+         pinned host memory, replays the step and reads every output back to
+         pinned host memory, inside the timed region.
 
 `--impl reference` times the reference's own CPU NF4 kernel (nf4cpu.nf4_gemv,
 built into oracle/_ref) on the host cores over the same workload definition.
+`--case <kernel>` runs one profiling case instead (see "profiling cases").
 """
 
 from __future__ import annotations
@@ -61,13 +69,17 @@ def weight_bytes(n: int, k: int, nested: bool = True) -> int:
     return n * k // 2 + ((nb + 4 * math.ceil(nb / BS2) + 1024) if nested else 4 * nb)
 
 
+# the jobs whose x is RMS-normalised inside the launch (their norm weight is read)
+NORMED = {"wqkv", "w13"}
+
+
 def job_bytes(job, rows: int = 1) -> int:
-    """Weights + x + y (+ operand) of one job; a gated pair reads x once and
-    writes only the gated product."""
-    _, widx, epi = job
+    """Weights + x + y (+ operand, + the fused norm's weight) of one job; a
+    gated pair reads x once and writes only the gated product."""
+    name, widx, epi = job
     n, k = PROJ[widx[0]][1], PROJ[widx[0]][2]
     b = sum(weight_bytes(PROJ[i][1], PROJ[i][2]) for i in widx) + 2 * rows * k + 2 * rows * n
-    return b + (2 * rows * n if epi == 1 else 0)
+    return b + (2 * rows * n if epi == 1 else 0) + (2 * k if name in NORMED else 0)
 
 
 LAYER_BYTES = sum(job_bytes(j) for j in JOBS)
@@ -207,33 +219,56 @@ def make_layers(device, rank: int):
 
 
 class StepIO:
-    """All of a step's inputs and outputs in two flat device buffers (and
-    pinned host mirrors for the end-to-end measurement). Per layer and job:
-    x (and the residual operand) in `dev_in`, y in `dev_out`."""
+    """A step's inputs, outputs and norm weights, and the data flow between
+    its jobs. Inputs in `dev_in`: the first layer's h, then one attention
+    stand-in [4096] per layer. Outputs in `dev_out`, per layer: wqkv's, wo's,
+    the gate's and w2's (the next layer's h). Pinned host mirrors serve the
+    end-to-end measurement."""
 
     def __init__(self, device, rank: int):
         import torch
 
-        self.specs = []   # per (layer, job): (x_off, op_off or None, y_off, n, k)
-        off_in = off_out = 0
+        dim, attn = PROJ[1][1], PROJ[1][2]
+        self.h0_off = 0
+        self.attn_off = [dim + l * attn for l in range(N_LAYERS)]
+        n_in = dim + N_LAYERS * attn
+        widths = [PROJ[0][1], PROJ[1][1], PROJ[2][1], PROJ[4][1]]   # wqkv, wo, gate, w2 outputs
+        self.out_off = []
+        off = 0
         for _ in range(N_LAYERS):
-            for _, widx, epi in JOBS:
-                n, k = PROJ[widx[0]][1], PROJ[widx[0]][2]
-                x_off, off_in = off_in, off_in + k
-                op_off = None
-                if epi == 1:
-                    op_off, off_in = off_in, off_in + n
-                self.specs.append((x_off, op_off, off_out, n, k))
-                off_out += n
+            offs = []
+            for w in widths:
+                offs.append(off)
+                off += w
+            self.out_off.append(offs)
         g = torch.Generator(device=device).manual_seed(77 + rank)
-        self.dev_in = torch.randn(off_in, generator=g, device=device).to(torch.bfloat16)
-        self.dev_out = torch.zeros(off_out, dtype=torch.bfloat16, device=device)
-        self.scratch = torch.zeros(9728, dtype=torch.bfloat16, device=device)  # w1 output (single mode)
-        self.host_in = torch.empty(off_in, dtype=torch.bfloat16, pin_memory=True)
+        self.dev_in = torch.randn(n_in, generator=g, device=device).to(torch.bfloat16)
+        self.dev_out = torch.zeros(off, dtype=torch.bfloat16, device=device)
+        self.norms = (1.0 + 0.1 * torch.randn(N_LAYERS, 2, dim, generator=g, device=device)).to(torch.bfloat16)
+        self.scratch = torch.zeros(PROJ[2][1], dtype=torch.bfloat16, device=device)  # w1 output (single mode)
+        self.host_in = torch.empty(n_in, dtype=torch.bfloat16, pin_memory=True)
         self.host_in.copy_(self.dev_in.cpu())
-        self.host_out = torch.empty(off_out, dtype=torch.bfloat16, pin_memory=True)
+        self.host_out = torch.empty(off, dtype=torch.bfloat16, pin_memory=True)
         self.h2d_bytes = self.dev_in.numel() * 2
         self.d2h_bytes = self.dev_out.numel() * 2
+
+    def jobs(self, layers):
+        """Per layer and job: (name, descriptors, x, y, epilogue, operand, norm weight) as addresses."""
+        ib, ob = self.dev_in.data_ptr(), self.dev_out.data_ptr()
+        nb = self.norms.data_ptr()
+        dim = PROJ[1][1]
+        out = []
+        h = ib + 2 * self.h0_off
+        for l, mods in enumerate(layers):
+            qkv, wo, gate, w2 = (ob + 2 * o for o in self.out_off[l])
+            attn_norm, ffn_norm = nb + 2 * (2 * l) * dim, nb + 2 * (2 * l + 1) * dim
+            d = [m._nf4_fast["desc"] for m in mods]
+            out.append(("wqkv", [d[0]], h, qkv, 0, None, attn_norm))
+            out.append(("wo", [d[1]], ib + 2 * self.attn_off[l], wo, 1, h, None))
+            out.append(("w13", [d[2], d[3]], wo, gate, "gated", None, ffn_norm))
+            out.append(("w2", [d[4]], gate, w2, 1, wo, None))
+            h = w2
+        return out
 
 
 def step_workspace(layers, io, device):
@@ -248,15 +283,32 @@ def step_workspace(layers, io, device):
 
 
 MODES = {
-    "decode": "per layer wqkv, wo(+res), the gated w1/w3 pair in one launch (nf4b_gemm_gated), w2(+res): "
-              "4 launches per layer in stream order, each waiting for the previous one (programmatic "
-              "dependent launch) as dependent matmuls would; with --prefetch-distance > 0 each also names "
-              "the weights of a later launch for L2 prefetch",
+    "step": "the whole step (36 layers x [wqkv with attention_norm fused, wo + residual, the W1/W3 gate with "
+            "ffn_norm fused, w2 + residual] = 144 dependent matmuls) as ONE nf4b_decode_step launch: a persistent "
+            "kernel, one CTA per SM, that streams the next matmul's weights while the previous one's outputs are "
+            "handed over",
+    "decode": "the same 144 matmuls as 4 C-ABI launches per layer in stream order (nf4b_gemm_ex / nf4b_gemm_gated "
+              "with the fused norms; programmatic dependent launch between them), captured as one CUDA graph; "
+              "with --prefetch-distance > 0 each also names the weights of a later launch for L2 prefetch",
     "single": "one launch per projection (w1, then w3 with the silu-gate epilogue on w1's output): "
               "5 launches per layer",
-    "chain": "the same 4 matmuls per layer with the same data dependencies, issued as nf4b_gemv_chain "
+    "chain": "the same 4 matmuls per layer with the same data flow, issued as nf4b_gemv_chain "
              "launches of --chain-layers layers each (job j reads its inputs only after jobs < j are done)",
 }
+
+
+def _chain_array(jobs):
+    from ttspipe_b200 import _lib
+
+    arr = (_lib.ChainJob * len(jobs))()
+    for i, (name, descs, x, y, epi, op, nw) in enumerate(jobs):
+        arr[i].w = ctypes.pointer(descs[0])
+        arr[i].w3 = ctypes.pointer(descs[1]) if epi == "gated" else None
+        arr[i].x, arr[i].y = x, y
+        arr[i].operand = op if epi == 1 else None
+        arr[i].epi = 1 if epi == 1 else 0
+        arr[i].norm_weight, arr[i].norm_eps = (nw, 1e-6) if nw is not None else (None, 0.0)
+    return arr
 
 
 class StepPlan:
@@ -264,58 +316,57 @@ class StepPlan:
     kept alive here) and issued on a stream; CUDA-graph capturable.
 
     Each launch names the weights of the launch `distance` places later as an
-    L2 prefetch hint (0: no hints)."""
+    L2 prefetch hint (0: no hints; separate launches only)."""
 
-    def __init__(self, layers, io: StepIO, ws, mode: str = "decode", distance: int = 0, chain_layers: int = 9):
+    def __init__(self, layers, io: StepIO, ws, mode: str = "step", distance: int = 0, chain_layers: int = 9):
+        import torch
+
         from ttspipe_b200 import _lib
 
         self.L = _lib.lib()
         self.ws_ptr, self.ws_bytes = ws.data_ptr(), ws.numel()
         self.mode = mode
-        self.launches = []   # ("gemm", desc, x, y, epi, operand) | ("gated", d1, d3, x, y)
+        self.launches = []   # ("gemm", desc, x, y, epi, operand, norm) | ("gated", d1, d3, x, y, norm) | ...
         weights = []         # per launch: descriptors it reads
-        in_base, out_base = io.dev_in.data_ptr(), io.dev_out.data_ptr()
-        if mode == "chain":
-            for first in range(0, len(layers), chain_layers):
-                ids = list(range(first, min(first + chain_layers, len(layers))))
-                arr = (_lib.ChainJob * (len(ids) * len(JOBS)))()
-                i = 0
-                for li in ids:
-                    mods = layers[li]
-                    for ji, (_, widx, epi) in enumerate(JOBS):
-                        x_off, op_off, y_off, _, _ = io.specs[li * len(JOBS) + ji]
-                        arr[i].w = ctypes.pointer(mods[widx[0]]._nf4_fast["desc"])
-                        arr[i].w3 = ctypes.pointer(mods[widx[1]]._nf4_fast["desc"]) if epi == "gated" else None
-                        arr[i].x, arr[i].y = in_base + 2 * x_off, out_base + 2 * y_off
-                        arr[i].operand = in_base + 2 * op_off if op_off is not None else None
-                        arr[i].epi = 1 if epi == 1 else 0
-                        arr[i].norm_weight, arr[i].norm_eps = None, 0.0
-                        i += 1
-                self.launches.append(("chain", arr))
+        jobs = io.jobs(layers)
+        if mode == "step":
+            arr = _chain_array(jobs)
+            need = int(self.L.nf4b_decode_step_workspace_size(arr, len(jobs), 1))
+            if need == 0:
+                raise RuntimeError(f"decode step rejected: {_lib.last_error()}")
+            self.step_ws = torch.zeros(need, dtype=torch.uint8, device=ws.device)
+            self.launches.append(("step", arr))
+            weights.append([])
+        elif mode == "chain":
+            per = 4 * chain_layers
+            for first in range(0, len(jobs), per):
+                self.launches.append(("chain", _chain_array(jobs[first:first + per])))
                 weights.append([])
-        for li, mods in enumerate(layers if mode != "chain" else []):
-            for ji, (_, widx, epi) in enumerate(JOBS):
-                x_off, op_off, y_off, _, _ = io.specs[li * len(JOBS) + ji]
-                x, y = in_base + 2 * x_off, out_base + 2 * y_off
-                op = in_base + 2 * op_off if op_off is not None else None
-                descs = [mods[w]._nf4_fast["desc"] for w in widx]
+        else:
+            for name, descs, x, y, epi, op, nw in jobs:
                 if epi == "gated" and mode == "decode":
-                    self.launches.append(("gated", descs[0], descs[1], x, y))
+                    self.launches.append(("gated", descs[0], descs[1], x, y, nw))
                     weights.append(descs)
                 elif epi == "gated":
                     scratch = io.scratch.data_ptr()
-                    self.launches.append(("gemm", descs[0], x, scratch, 0, None))
+                    self.launches.append(("gemm", descs[0], x, scratch, 0, None, nw))
                     weights.append([descs[0]])
-                    self.launches.append(("gemm", descs[1], x, y, 2, scratch))
+                    self.launches.append(("gemm", descs[1], x, y, 2, scratch, nw))
                     weights.append([descs[1]])
                 else:
-                    self.launches.append(("gemm", descs[0], x, y, epi, op))
+                    self.launches.append(("gemm", descs[0], x, y, epi, op, nw))
                     weights.append(descs)
         n = len(self.launches)
         self.opts = []
         for i in range(n):
+            launch = self.launches[i]
             hint = weights[(i + distance) % n][:2] if distance > 0 else []
-            self.opts.append(_lib.GemmOpts(*[ctypes.pointer(d) for d in hint]) if hint else None)
+            nw = launch[-1] if launch[0] in ("gemm", "gated") else None
+            if hint or nw is not None:
+                ptrs = [ctypes.pointer(d) for d in hint] + [None] * (2 - len(hint))
+                self.opts.append(_lib.GemmOpts(ptrs[0], ptrs[1], nw, 1e-6 if nw is not None else 0.0))
+            else:
+                self.opts.append(None)
 
     def __len__(self):
         return len(self.launches)
@@ -326,15 +377,18 @@ class StepPlan:
         L = self.L
         for launch, opts in zip(self.launches, self.opts):
             o = ctypes.byref(opts) if opts is not None else None
-            if launch[0] == "chain":
+            if launch[0] == "step":
+                arr = launch[1]
+                st = L.nf4b_decode_step(arr, len(arr), 1, self.step_ws.data_ptr(), self.step_ws.numel(), stream_ptr)
+            elif launch[0] == "chain":
                 arr = launch[1]
                 st = L.nf4b_gemv_chain(arr, len(arr), 1, self.ws_ptr, self.ws_bytes, stream_ptr)
             elif launch[0] == "gated":
-                _, d1, d3, x, y = launch
+                _, d1, d3, x, y, _ = launch
                 st = L.nf4b_gemm_gated(ctypes.byref(d1), ctypes.byref(d3), x, y, 1, self.ws_ptr, self.ws_bytes,
                                        o, stream_ptr)
             else:
-                _, desc, x, y, epi, op = launch
+                _, desc, x, y, epi, op, _ = launch
                 st = L.nf4b_gemm_ex(ctypes.byref(desc), x, y, 1, epi, op, self.ws_ptr, self.ws_bytes, o,
                                     stream_ptr)
             if st != 0:
@@ -387,7 +441,7 @@ def detail(layers, io, ws, stream, device):
         torch.cuda.synchronize(device)
         return st.elapsed_time(en) / reps * 1e3  # us per replay
 
-    cases = [("decode", 0, 0), ("decode", 2, 0), ("single", 0, 0)] + [("chain", 0, c) for c in (1, 4, 9)]
+    cases = [("step", 0, 0), ("decode", 0, 0), ("decode", 2, 0), ("single", 0, 0)] + [("chain", 0, c) for c in (1, 9)]
     for mode, dist, cl in cases:
         plan = StepPlan(layers, io, ws, mode, dist, cl or 9)
         g = graph_of(lambda: plan.issue(stream.cuda_stream))
@@ -540,10 +594,12 @@ def run_gpu(args):
             "step_ms_quantiles": {q: round(statistics.quantiles(step_ms, n=10)[i], 4) if len(step_ms) >= 2
                                   else round(step_ms[0], 4) for q, i in (("p10", 0), ("p50", 4), ("p90", 8))},
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (random-init NF4 weights N(0,0.02), activations N(0,1), seeded per rank)",
-            "config": {"workload": "S2-Pro slow-AR decode matmuls: 36 layers x [wqkv 6144x2560, "
-                                   "wo 2560x4096 +res, silu(x W1)*(x W3) W1,W3 9728x2560, w2 2560x9728 +res], "
-                                   "M=1, NF4 bs64 + double-quant (bs2 256)",
+            "data": "synthetic (random-init NF4 weights N(0,0.02), norm weights N(1,0.1), first h and attention "
+                    "stand-ins N(0,1), seeded per rank)",
+            "config": {"workload": "S2-Pro slow-AR decode matmuls with the decode block's data flow: 36 layers x "
+                                   "[wqkv 6144x2560 on rmsnorm(h), wo 2560x4096 on attn + h, "
+                                   "silu(x W1)*(x W3) W1,W3 9728x2560 on rmsnorm(wo out), w2 2560x9728 on the "
+                                   "gate + wo out -> next h], M=1, NF4 bs64 + double-quant (bs2 256)",
                        "schedule": f"{args.mode}: {MODES[args.mode]}",
                        "prefetch_distance": args.prefetch_distance,
                        "chain_layers": args.chain_layers if args.mode == "chain" else None,
@@ -555,14 +611,16 @@ def run_gpu(args):
             "launches_per_step": len(plan),
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": io.h2d_bytes,
                     "d2h_bytes_per_step": io.d2h_bytes,
-                    "path": "C ABI nf4b_gemm calls (CUDA graph) + pinned H2D inputs + D2H outputs per step"},
+                    "path": ("C ABI nf4b_decode_step call" if args.mode == "step" else "C ABI nf4b_gemm calls")
+                            + " (CUDA graph) + pinned H2D inputs + D2H outputs per step"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "peak_source": peak_kind,
                          "traffic": traffic,
                          "algorithmic_bytes_per_launch": STEP_BYTES // len(plan),
-                         "kernel": "nf4_gemv_reg_kernel (register-fed pair GEMV), plain and gated (every "
-                                   "launch of the step; achieved = step bytes / step time, i.e. launch gaps "
-                                   "included)"},
+                         "kernel": ("nf4_decode_step_kernel (persistent decode step: the step's 144 matmuls "
+                                    "in one launch)" if args.mode == "step" else
+                                    "nf4_gemv_reg_kernel (register-fed pair GEMV), plain and gated")
+                                   + "; achieved = step bytes / step time (handoffs and launch gaps included)"},
             "clocks": clock,
             "per_rank_GBps": round(per_rank, 1),
         }

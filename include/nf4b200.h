@@ -78,7 +78,8 @@ const char* nf4b_last_error(void);
 /*
  * The library's device error word: non-zero after a kernel gave up on a
  * bounded wait (a pipeline barrier that never completed): bit 0 the GEMM,
- * bit 1 the GEMV, bit 2 decode attention's KV copies. Synchronises the device to read it; `clear`
+ * bit 1 the GEMV, bit 2 decode attention's KV copies, bit 3 a decode step's
+ * handoff. Synchronises the device to read it; `clear`
  * resets it; -1 if it cannot be read. No counterpart in the reference, whose
  * kernels have no waits.
  */
@@ -195,6 +196,47 @@ int nf4b_gemv_chain(const nf4b_chain_job* jobs, int n_jobs, int rows, void* work
                     size_t workspace_bytes, void* stream);
 
 size_t nf4b_gemv_chain_workspace_size(const nf4b_chain_job* jobs, int n_jobs, int rows);
+
+#define NF4B_MAX_STEP_JOBS 152
+
+/*
+ * A whole decode step's dependent matmuls in ONE launch: up to
+ * NF4B_MAX_STEP_JOBS jobs with nf4b_gemv_chain's semantics (job j reads its x
+ * and operand only after every output of jobs 0..j-1 is written; x and
+ * operand may be earlier jobs' y; a job's norm_weight RMS-normalises its x
+ * first, exactly as nf4b_rms_norm), for 1 or 2 activation rows. It replaces
+ * the sequence of nf4gemv.matmul launches the reference's decode_block issues
+ * per block (app/engine/fusedlayer.py:212-269; the graph of them that
+ * graphs.DecodeGraphs replays), e.g. 36 layers x (wqkv, wo + residual, the
+ * W1/W3 gate, w2 + residual) = 144 jobs.
+ * One CTA per SM (a cooperative launch) streams the weights of job j + 1
+ * into registers while job j's outputs are handed over; a job whose x is the
+ * previous job's y reads it from flag-tagged handoff words in the workspace
+ * (one L2 round trip), any other boundary is a full barrier. Each job equals
+ * nf4b_gemm (or nf4b_gemm_gated) up to fp32 summation order; results are
+ * deterministic. Serves blocksize-64 weights with k_in % 256 == 0,
+ * k_in <= 10240, n_out % 16 == 0, 32-byte aligned packed weights (NF4B_ERR_*
+ * otherwise). A job whose x (or operand) is the previous job's y must match
+ * its shape. The workspace (nf4b_decode_step_workspace_size) is zeroed once
+ * before its first use; the step keeps a launch counter in it and must have
+ * it to itself (one workspace per stream). No reference counterpart as a
+ * single call.
+ */
+int nf4b_decode_step(const nf4b_chain_job* jobs, int n_jobs, int rows, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+size_t nf4b_decode_step_workspace_size(const nf4b_chain_job* jobs, int n_jobs, int rows);
+
+/*
+ * Test hook for failure detection (not for production use): nf4b_decode_step
+ * whose waits give up after `wait_ns` nanoseconds, and whose boundary before
+ * job `stall_job` (-1: none) waits for a flag that is never written, so that
+ * boundary's wait runs out. The kernel then records bit 3 in
+ * nf4b_device_error and returns; nothing faults, and the next launch on the
+ * same workspace is unaffected.
+ */
+int nf4b_debug_decode_step(const nf4b_chain_job* jobs, int n_jobs, int rows, void* workspace,
+                           size_t workspace_bytes, int stall_job, unsigned long long wait_ns, void* stream);
 
 /* Bytes of workspace nf4b_gemm needs for this weight and row count. */
 size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows);

@@ -13,12 +13,17 @@ from the very same state (the KV caches the prompt left behind, the position,
 the draw counter, the repetition window) and seeds.
 
 What must agree:
-  * every drawn token. The device's matmuls accumulate in a different order
-    than the oracle's exact sums, so a logit can differ in its last bits; a
-    draw whose uniform lies within that much of a CDF boundary may then pick
-    the neighbouring token. Such a draw is accepted only when its margin is
-    below DRAW_MARGIN, and the oracle continues with the device's token, so
-    the rest of the frame is still compared like for like;
+  * every logit row the frame samples from (the LM head's and each codebook
+    head's, which the frame keeps in place), within LOGIT_TOL of the oracle's;
+  * every drawn token, exactly, given the device's own logit row: the device
+    sampler and the oracle's `sample_token` apply the same rule to the same
+    row. On the oracle's row the oracle draws the same token too, unless the
+    draw's uniform lies closer to a CDF boundary than the logit difference can
+    move it (|dF| <= 2 max|dL| / T): the device's matmuls accumulate in a
+    different order than the oracle's exact sums, and a token whose
+    probabilities nearly tie may then flip. The frame continues with the
+    device's token either way, so everything after it is compared like for
+    like;
   * the KV-cache rows the frame writes (every slow layer at the position,
     every fast layer at fast positions 0..3), within the block tolerance;
   * the next frame's input, bit for bit (a sum of embedding rows in a fixed
@@ -39,7 +44,7 @@ from ttspipe_b200.dualar import DualARConfig, DualARDecoder
 pytestmark = pytest.mark.gpu
 
 CACHE_TOL = 2e-2     # a KV row after up to 4 blocks of GEMV rounding (one block: 8e-3)
-DRAW_MARGIN = 2e-3   # how close to a CDF boundary a draw may be to pick a neighbour
+LOGIT_TOL = 2e-2     # max|dL| / max|L| of a logit row after the frame's blocks
 
 
 def _cfg():
@@ -89,15 +94,22 @@ class OracleFrame:
         nh, nkv, hd, eps = self.dims
         return orc.decode_block(x, w, kc, vc, pos, freqs_row, nh, nkv, hd, eps, eps)
 
-    def _draw(self, logits, temp, top_p, seed, step, device_tok, mismatches, what):
+    def _draw(self, logits, dev_logits, temp, top_p, seed, step, device_tok, mismatches, what):
+        """The oracle's draw on its own row `logits`, checked against the
+        device's token and the device's row `dev_logits` (bf16 bits)."""
+        lo, lg = orc.bf16_to_f32(logits).astype(np.float64), orc.bf16_to_f32(dev_logits).astype(np.float64)
+        assert orc.relative_error(lg, lo) < LOGIT_TOL, what
+        # the same rule on the same row: the same token, exactly
+        assert orc.sample_token(dev_logits, temp, top_p, self.c.top_k, seed, step)[0] == device_tok, what
         tok = orc.sample_token(logits, temp, top_p, self.c.top_k, seed, step)[0]
         if tok != device_tok:
             margin = _draw_margin(logits, temp, top_p, self.c.top_k, seed, step)
-            assert margin < DRAW_MARGIN, f"{what}: device drew {device_tok}, oracle {tok}, margin {margin:.2e}"
-            mismatches.append((what, margin))
+            bound = 2.0 * float(np.max(np.abs(lg - lo))) / max(temp, 1e-5)
+            assert margin < bound, f"{what}: device drew {device_tok}, oracle {tok}, margin {margin:.2e} > {bound:.2e}"
+            mismatches.append((what, margin, bound))
         return device_tok   # teacher-forced: the frame continues with the device's choice
 
-    def run(self, st, dev_tokens, dev_main, dev_high):
+    def run(self, st, dev_tokens, dev_main, dev_high, dev_logits, dev_cb_logits):
         """One frame from state `st` (dict of bit arrays, modified in place);
         returns (tokens, draw mismatches within the margin)."""
         c = self.c
@@ -109,9 +121,10 @@ class OracleFrame:
             x = self._block(x, w, st["slow_k"][i], st["slow_v"][i], pos, self.freqs[pos])
         hidden = orc.rms_norm(x.reshape(1, -1), self.norm_w, eps)
         logits = orc.f32_to_bf16(orc.dense_gemv_exact(hidden, self.lm_head).astype(np.float32))
-        main = self._draw(logits, c.temperature, c.top_p, self.seed * 7919 + 1, step, dev_main, mism, "main")
-        high = self._draw(logits, c.high_temperature, c.high_top_p, self.seed * 7919 + 2, step, dev_high, mism,
-                          "high")
+        main = self._draw(logits, dev_logits, c.temperature, c.top_p, self.seed * 7919 + 1, step, dev_main, mism,
+                          "main")
+        high = self._draw(logits, dev_logits, c.high_temperature, c.high_top_p, self.seed * 7919 + 2, step, dev_high,
+                          mism, "high")
         semantic = c.semantic_begin_id <= main < c.semantic_begin_id + c.codebook_size
         chosen = high if (semantic and main in list(st["recent"])) else main
         a = min(max(chosen - c.semantic_begin_id, 0), c.codebook_size - 1)
@@ -136,8 +149,8 @@ class OracleFrame:
                 y = self._block(y, w, st["fast_k"][li], st["fast_v"][li], i, self.fast_freqs[i])
             yn = orc.rms_norm(y.reshape(1, -1), self.fast_norm_w, eps)
             lg = orc.f32_to_bf16(orc.dense_gemv_exact(yn, self.cb_heads[i]).astype(np.float32))
-            tok = self._draw(lg, c.temperature, c.top_p, self.seed * 7919 + 10 + i, step, dev_tokens[i + 1], mism,
-                             f"codebook {i}")
+            tok = self._draw(lg, dev_cb_logits[i], c.temperature, c.top_p, self.seed * 7919 + 10 + i, step,
+                             dev_tokens[i + 1], mism, f"codebook {i}")
             tokens.append(tok)
             h = self.fast_emb[tok]
         # next input: bf16(float(semantic row) + fp32 sum of the codebook rows in order)
@@ -173,8 +186,13 @@ def test_frame_matches_the_oracle_frame(seed, repeat):
     dec = DualARDecoder(_cfg(), "cuda", seed=seed)
     c = dec.cfg
     with torch.no_grad():
-        # favour codebook-0 ids so the main draw is a semantic token, as in real decoding
+        # favour codebook-0 ids so the main draw is a semantic token, as in real
+        # decoding, and give the heads a trained model's peaked rows instead of
+        # random-init's nearly uniform ones (with 64 near-equal probabilities
+        # almost every draw sits near a CDF boundary)
         dec.lm_head[c.semantic_begin_id:] *= 4
+        for h in dec.cb_heads:
+            h *= 4
     g = torch.Generator().manual_seed(seed)
     dec.prefill(torch.randint(0, c.vocab, (16,), generator=g).cuda())
     orf = OracleFrame(dec)
@@ -198,22 +216,25 @@ def test_frame_matches_the_oracle_frame(seed, repeat):
         dev_tokens = [int(t) for t in dec.tokens.cpu()]
         dev_main, dev_high = int(dec.main_tok.item()), int(dec.high_tok.item())
         pos = st["pos"]
-        tokens, mism = orf.run(st, dev_tokens, dev_main, dev_high)
-        assert tokens == dev_tokens, (frame, tokens, dev_tokens)
-        assert len(mism) <= 1, mism
-        if repeat and frame == 1:
-            assert c.semantic_begin_id <= dev_main < c.semantic_begin_id + c.codebook_size
-            assert dev_tokens[0] == dev_high
-        # the rows this frame wrote
+        tokens, mism = orf.run(st, dev_tokens, dev_main, dev_high, to_bits(dec.logits), to_bits(dec.cb_logits))
+        # the rows this frame wrote: every slow layer at pos, every fast layer
+        # at fast positions 0 (the prime) .. 3
         for i, b in enumerate(dec.slow):
             gk, gv = to_bits(b.attention.kv_cache.k_cache)[0], to_bits(b.attention.kv_cache.v_cache)[0]
             assert _close(gk[:, pos], st["slow_k"][i][:, pos], CACHE_TOL), (frame, "slow k", i)
             assert _close(gv[:, pos], st["slow_v"][i][:, pos], CACHE_TOL), (frame, "slow v", i)
         for i, b in enumerate(dec.fast):
             gk, gv = to_bits(b.attention.kv_cache.k_cache)[0], to_bits(b.attention.kv_cache.v_cache)[0]
-            for r in range(c.num_codebooks):   # fast position 0 (the prime) and 1..3
+            for r in range(c.num_codebooks):
                 assert _close(gk[:, r], st["fast_k"][i][:, r], CACHE_TOL), (frame, "fast k", i, r)
                 assert _close(gv[:, r], st["fast_v"][i][:, r], CACHE_TOL), (frame, "fast v", i, r)
+        assert tokens == dev_tokens, (frame, tokens, dev_tokens)
+        # a near-tie may flip a draw (each checked against its bound above);
+        # most draws must match outright
+        assert len(mism) <= (c.num_codebooks + 1) // 2, mism
+        if repeat and frame == 1:
+            assert c.semantic_begin_id <= dev_main < c.semantic_begin_id + c.codebook_size
+            assert dev_tokens[0] == dev_high
         # the next frame's input and counters, exactly
         assert np.array_equal(to_bits(dec.x).reshape(-1), st["x"])
         assert list(dec.recent.cpu().numpy()) == list(st["recent"])

@@ -48,6 +48,9 @@ EXPORTS = (
     "nf4b_decode_attention",
     "nf4b_decode_attention_workspace_size",
     "nf4b_qkv_attention",
+    "nf4b_decode_step",
+    "nf4b_decode_step_workspace_size",
+    "nf4b_debug_decode_step",
 )
 
 
@@ -130,6 +133,9 @@ def _declare(lib) -> None:
         "nf4b_frame_advance": (i32, [vp, ctypes.c_longlong, vp, ctypes.c_longlong, i32, vp, i32, vp, vp, i32, vp, vp,
                                      vp]),
         "nf4b_gemv_chain_workspace_size": (sz, [ctypes.POINTER(ChainJob), i32, i32]),
+        "nf4b_decode_step": (i32, [ctypes.POINTER(ChainJob), i32, i32, vp, sz, vp]),
+        "nf4b_decode_step_workspace_size": (sz, [ctypes.POINTER(ChainJob), i32, i32]),
+        "nf4b_debug_decode_step": (i32, [ctypes.POINTER(ChainJob), i32, i32, vp, sz, i32, ctypes.c_ulonglong, vp]),
         "nf4b_gemm_workspace_size": (sz, [wp, i32]),
         "nf4b_gemm_noalloc": (i32, [wp, vp, vp, i32, i32, vp, vp]),
         "nf4b_dequantize": (i32, [wp, vp, vp]),

@@ -259,8 +259,9 @@ const char* nf4b_last_error(void) { return g_err; }
 
 int nf4b_device_error(int clear) {
   const int gemm = read_device_error(clear), gemv = read_gemv_error(clear), attn = read_attn_error(clear);
-  if (gemm < 0 || gemv < 0 || attn < 0) return -1;
-  return (gemm ? 1 : 0) | (gemv ? 2 : 0) | (attn ? 4 : 0);
+  const int step = read_step_error(clear);
+  if (gemm < 0 || gemv < 0 || attn < 0 || step < 0) return -1;
+  return (gemm ? 1 : 0) | (gemv ? 2 : 0) | (attn ? 4 : 0) | (step ? 8 : 0);
 }
 
 size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows) {
@@ -464,6 +465,123 @@ extern "C" int nf4b_gemv_chain(const nf4b_chain_job* jobs, int n_jobs, int rows,
   cp.counters = static_cast<int*>(workspace);
   cp.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + GEMV_COUNTER_BYTES);
   return launch_status(launch_gemv_chain(cp, reinterpret_cast<cudaStream_t>(stream)), "nf4 gemv chain launch");
+}
+
+namespace {
+
+// Validate a decode step and fill the kernel parameters.
+int build_step(const nf4b_chain_job* jobs, int n_jobs, int rows, StepParams* sp, size_t* bytes) {
+  if (jobs == nullptr || n_jobs <= 0) return fail(NF4B_ERR_ARG, "empty job list");
+  if (n_jobs > STEP_MAX_JOBS)
+    return fail(NF4B_ERR_SHAPE, "%d jobs exceed the decode step limit of %d", n_jobs, STEP_MAX_JOBS);
+  if (rows < 1 || rows > 2) return fail(NF4B_ERR_SHAPE, "the decode step serves 1 or 2 rows (got %d)", rows);
+  sp->n_jobs = n_jobs;
+  sp->M = rows;
+  sp->stall_job = -1;
+  sp->wait_ns = 2000000000ull;
+  for (int i = 0; i < n_jobs; ++i) {
+    const nf4b_chain_job& jb = jobs[i];
+    int st = check_weight(jb.w);
+    if (st) return st;
+    const nf4b_weight* w = jb.w;
+    if (w->blocksize != 64 || w->k_in % 256 || w->k_in > STEP_MAX_K || w->n_out % 16)
+      return fail(NF4B_ERR_SHAPE,
+                  "job %d: the decode step needs blocksize 64, k_in %% 256 == 0, k_in <= %d, n_out %% 16 == 0", i,
+                  STEP_MAX_K);
+    if ((long long)w->n_out * (w->k_in / 64) >= (1LL << 31)) return fail(NF4B_ERR_SHAPE, "job %d too large", i);
+    if (!aligned(w->packed, 32) || !use_pairs(w, rows))
+      return fail(NF4B_ERR_ALIGN, "job %d: packed weight not 32-byte aligned or scales not aligned", i);
+    if (jb.x == nullptr || jb.y == nullptr) return fail(NF4B_ERR_ARG, "job %d: x or y is null", i);
+    if (!aligned(jb.x, 16)) return fail(NF4B_ERR_ALIGN, "job %d: x is not 16-byte aligned", i);
+    if (!aligned(jb.y, 4) || (jb.operand && !aligned(jb.operand, 2)) || (jb.norm_weight && !aligned(jb.norm_weight, 16)))
+      return fail(NF4B_ERR_ALIGN, "job %d: y not 4-byte, operand not 2-byte or norm weight not 16-byte aligned", i);
+    if (jb.norm_weight != nullptr && !(jb.norm_eps >= 0.f))
+      return fail(NF4B_ERR_ARG, "job %d: norm eps must be >= 0", i);
+    StepJob& J = sp->jobs[i];
+    J = StepJob{};
+    J.gated = jb.w3 != nullptr ? 1 : 0;
+    if (J.gated) {
+      const nf4b_weight* w3 = jb.w3;
+      if ((st = check_weight(w3))) return st;
+      if (w3->n_out != w->n_out || w3->k_in != w->k_in || w3->blocksize != w->blocksize ||
+          w3->nested != w->nested || (w->nested && w3->blocksize2 != w->blocksize2) || !use_pairs(w3, rows) ||
+          !aligned(w3->packed, 32))
+        return fail(NF4B_ERR_SHAPE, "job %d: the gated pair's weights differ in shape, quantisation or alignment", i);
+    } else {
+      if (jb.epi < NF4B_EPI_NONE || jb.epi > NF4B_EPI_SILU_GATE)
+        return fail(NF4B_ERR_ARG, "job %d: unknown epilogue %d", i, jb.epi);
+      if (jb.epi != NF4B_EPI_NONE && jb.operand == nullptr)
+        return fail(NF4B_ERR_ARG, "job %d: epilogue %d needs an operand", i, jb.epi);
+    }
+    if (i > 0) {
+      const nf4b_chain_job& pv = jobs[i - 1];
+      if (jb.x == pv.y && w->k_in != pv.w->n_out)
+        return fail(NF4B_ERR_SHAPE, "job %d: x is job %d's y but k_in %d != its n_out %d", i, i - 1, w->k_in,
+                    pv.w->n_out);
+      if (jb.operand != nullptr && jb.operand == pv.y && w->n_out != pv.w->n_out)
+        return fail(NF4B_ERR_SHAPE, "job %d: the operand is job %d's y of another width", i, i - 1);
+    }
+    J.packed = w->packed;
+    J.a8 = w->absmax_code;
+    J.absmax = w->absmax;
+    J.code2 = w->code2;
+    J.offset = w->offset;
+    J.packed3 = J.gated ? jb.w3->packed : nullptr;
+    J.a8_3 = J.gated ? jb.w3->absmax_code : nullptr;
+    J.absmax3 = J.gated ? jb.w3->absmax : nullptr;
+    J.code2_3 = J.gated ? jb.w3->code2 : nullptr;
+    J.offset3 = J.gated ? jb.w3->offset : 0.f;
+    J.x = static_cast<const uint16_t*>(jb.x);
+    J.y = static_cast<uint16_t*>(jb.y);
+    J.operand = static_cast<const uint16_t*>(jb.operand);
+    J.norm_w = static_cast<const uint16_t*>(jb.norm_weight);
+    J.norm_eps = jb.norm_eps;
+    J.N = w->n_out;
+    J.K = w->k_in;
+    J.nested = w->nested ? 1 : 0;
+    J.bs2_shift = w->nested ? log2i(w->blocksize2) : 0;
+    J.epi = J.gated ? NF4B_EPI_NONE : jb.epi;
+  }
+  *bytes = step_plan(sp, current_sm_count());
+  return NF4B_OK;
+}
+
+int decode_step_call(const nf4b_chain_job* jobs, int n_jobs, int rows, void* workspace, size_t workspace_bytes,
+                     int stall_job, unsigned long long wait_ns, void* stream) {
+  static thread_local StepParams sp;
+  size_t need = 0;
+  int st = build_step(jobs, n_jobs, rows, &sp, &need);
+  if (st) return st;
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(NF4B_ERR_WORKSPACE, "decode step workspace of %zu bytes needed, %zu given", need,
+                workspace ? workspace_bytes : (size_t)0);
+  if (!aligned(workspace, 256)) return fail(NF4B_ERR_ALIGN, "workspace is not 256-byte aligned");
+  if ((st = check_device())) return st;
+  sp.stall_job = stall_job;
+  sp.wait_ns = wait_ns;
+  return launch_status(launch_decode_step(sp, workspace, reinterpret_cast<cudaStream_t>(stream)),
+                       "nf4 decode step launch");
+}
+
+}  // namespace
+
+extern "C" size_t nf4b_decode_step_workspace_size(const nf4b_chain_job* jobs, int n_jobs, int rows) {
+  static thread_local StepParams sp;
+  size_t need = 0;
+  if (build_step(jobs, n_jobs, rows, &sp, &need)) return 0;
+  return need;
+}
+
+extern "C" int nf4b_decode_step(const nf4b_chain_job* jobs, int n_jobs, int rows, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  return decode_step_call(jobs, n_jobs, rows, workspace, workspace_bytes, -1, 2000000000ull, stream);
+}
+
+extern "C" int nf4b_debug_decode_step(const nf4b_chain_job* jobs, int n_jobs, int rows, void* workspace,
+                                      size_t workspace_bytes, int stall_job, unsigned long long wait_ns,
+                                      void* stream) {
+  if (wait_ns == 0 || wait_ns > 2000000000ull) return fail(NF4B_ERR_ARG, "wait_ns must be in (0, 2e9]");
+  return decode_step_call(jobs, n_jobs, rows, workspace, workspace_bytes, stall_job, wait_ns, stream);
 }
 
 extern "C" int nf4b_dense_gemv(const void* w, const void* x, void* y, int n_out, int k_in, const void* norm_weight,

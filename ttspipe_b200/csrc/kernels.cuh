@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "nf4b200.h"
+
 namespace nf4b {
 
 // ---- streaming GEMV (nf4_gemv.cu) ----------------------------------------
@@ -202,6 +204,59 @@ struct alignas(64) ChainParams {
 // partial-sum bytes the split tiles need (the largest job's).
 size_t chain_plan(ChainParams* p, int sm_count);
 cudaError_t launch_gemv_chain(const ChainParams& p, cudaStream_t stream);
+
+// ---- persistent decode step (decode_step.cu): dependent decode GEMVs in one
+// cooperative launch, handing outputs over through flag-tagged 64-bit words
+
+constexpr int STEP_WARPS = 16;
+constexpr int STEP_MAX_JOBS = NF4B_MAX_STEP_JOBS;
+constexpr int STEP_MAX_K = 10240;            // x of 2 rows staged whole in shared memory
+constexpr size_t STEP_CONTROL_BYTES = 256;   // epoch (u32) and exit counter (i32), padded
+
+struct StepJob {
+  const uint8_t* packed;
+  const uint8_t* a8;
+  const float* absmax;
+  const float* code2;
+  const uint8_t* packed3;  // gated pair: W3 (same shape and quantisation)
+  const uint8_t* a8_3;
+  const float* absmax3;
+  const float* code2_3;
+  const uint16_t* x;
+  uint16_t* y;
+  const uint16_t* operand;
+  const uint16_t* norm_w;
+  float offset, offset3, norm_eps;
+  int N, K;
+  int nested, gated, epi, bs2_shift;
+  // derived by step_plan
+  int B;        // 256-code units per row tile and half
+  int tiles;    // row tiles of 16
+  int units;    // tiles * B * (gated ? 2 : 1)
+  int smax;     // the most CTAs one tile meets
+  int x_ll;     // x is the previous job's y: staged from its handoff words
+  int op_ll;    // 1 / 2: the epilogue operand is job j - op_ll's y, read from its handoff words (0: memory)
+  int barrier;  // the boundary after this job is a full barrier (arrival words)
+};
+
+struct alignas(16) StepParams {
+  int n_jobs;
+  int M;
+  int grid;
+  int stall_job;                  // test hook: the boundary before this job never completes (-1: none)
+  unsigned long long wait_ns;     // how long a wait lasts before it gives up
+  long long ll_words;             // 64-bit handoff words per region
+  uint64_t* ll[3];                // handoff regions, job j's in region j % 3
+  uint64_t* arrive;               // [2][grid] arrival words
+  unsigned* epoch;
+  int* exit_ctr;
+  StepJob jobs[STEP_MAX_JOBS];
+};
+
+// Fills the derived job fields and returns the workspace bytes the step needs.
+size_t step_plan(StepParams* p, int sm_count);
+cudaError_t launch_decode_step(StepParams& p, void* workspace, cudaStream_t stream);
+int read_step_error(int clear);
 
 // ---- dense bf16 GEMV for the output heads (dense_gemv.cu) -----------------
 // k_in in {1024, 2048, 2560, 4096}; one activation row.

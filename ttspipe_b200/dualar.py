@@ -110,6 +110,10 @@ class DualARDecoder:
         self.main_tok = torch.zeros(1, dtype=torch.long, device=self.device)   # the two semantic draws
         self.high_tok = torch.zeros(1, dtype=torch.long, device=self.device)
         self.h = torch.zeros(1, 1, sc.dim, dtype=torch.bfloat16, device=self.device)  # the fast AR's input
+        # the frame's logit rows (the LM head's and each codebook head's), kept
+        # in place so a replayed graph writes the same buffers every frame
+        self.logits = torch.zeros(cfg.vocab, dtype=torch.bfloat16, device=self.device)
+        self.cb_logits = torch.zeros(cfg.num_codebooks, cfg.codebook_size, dtype=torch.bfloat16, device=self.device)
         self.graph = None
 
     # ------------------------------------------------------------------ checkpoint
@@ -214,7 +218,7 @@ class DualARDecoder:
         cfg = self.cfg
         x = self.slow_stack(self.x)
         hidden = fusedops.rms_norm(x, self.norm_w, cfg.slow.norm_eps)
-        logits = heads.dense_linear(self.lm_head, hidden)
+        logits = heads.dense_linear(self.lm_head, hidden, out=self.logits)
         heads.sample(logits, temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k,
                      seed=self.seed * 7919 + 1, step=self.step, out=self.main_tok)
         heads.sample(logits, temperature=cfg.high_temperature, top_p=cfg.high_top_p, top_k=cfg.top_k,
@@ -234,7 +238,8 @@ class DualARDecoder:
                 y = fusedlayer.decode_block(blk, y, self.fast_freqs[i:i + 1], self.fast_mask, self.fast_pos[i])
                 assert y is not None, "a fast block fell back"
             # fast_norm folded into the codebook head's launch
-            logits_i = heads.dense_linear(self.cb_heads[i], y, norm=(self.fast_norm_w, cfg.slow.norm_eps))
+            logits_i = heads.dense_linear(self.cb_heads[i], y, out=self.cb_logits[i],
+                                          norm=(self.fast_norm_w, cfg.slow.norm_eps))
             tok = self.tokens[i + 1:i + 2]
             heads.sample(logits_i, temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k,
                          seed=self.seed * 7919 + 10 + i, step=self.step, out=tok)

@@ -365,24 +365,13 @@ def matmul_gated(w1, w3, x, *, prefetch=None, norm=None):
     return out.view(*x.shape[:-1], N)
 
 
-def matmul_chain(steps):
-    """Dependent decode matmuls in ONE launch (an extension of the reference's
-    API, which launches each matmul, norm and gate separately,
-    app/engine/fusedlayer.py:212-269).
-
-    `steps`: a list of dicts, run in order, each with
-      ``w`` (prepared linear), ``x`` (bf16 tensor [..., in] or the int index of
-      an earlier step, whose output is then the input), optional ``w3`` (the
-      FeedForward gate silu(x W^T) * (x W3^T)), ``epi`` / ``operand`` (tensor
-      or step index) as for ``matmul``, and ``norm`` = (weight, eps) to
-      RMS-normalise x first exactly as ``fusedops.rms_norm``.
-    Returns the list of step outputs, or None if any step is outside the
-    chain's envelope (1..4 rows, blocksize 64, in_features % 256 == 0,
-    rows * in_features * 2 <= 40 KB); then nothing was launched.
-    """
+def _chain_jobs(steps, max_jobs: int):
+    """The C job array for a chain of steps (see matmul_chain), their output
+    tensors and the tensors the array points into; None if a step is outside
+    the envelope of the calls below."""
     import torch
 
-    if not steps or len(steps) > 40:
+    if not steps or len(steps) > max_jobs:
         return None
     arr = (_lib.ChainJob * len(steps))()
     outs, keep = [], []
@@ -434,6 +423,31 @@ def matmul_chain(steps):
             arr[i].norm_weight, arr[i].norm_eps = None, 0.0
         keep += [flat, operand]
         outs.append(out)
+    return arr, outs, keep, rows, dev
+
+
+def matmul_chain(steps):
+    """Dependent decode matmuls in ONE launch (an extension of the reference's
+    API, which launches each matmul, norm and gate separately,
+    app/engine/fusedlayer.py:212-269).
+
+    `steps`: a list of dicts, run in order, each with
+      ``w`` (prepared linear), ``x`` (bf16 tensor [..., in] or the int index of
+      an earlier step, whose output is then the input), optional ``w3`` (the
+      FeedForward gate silu(x W^T) * (x W3^T)), ``epi`` / ``operand`` (tensor
+      or step index) as for ``matmul``, and ``norm`` = (weight, eps) to
+      RMS-normalise x first exactly as ``fusedops.rms_norm``.
+    Returns the list of step outputs, or None if any step is outside the
+    chain's envelope (1..4 rows, blocksize 64, in_features % 256 == 0,
+    rows * in_features * 2 <= 40 KB); then nothing was launched. Every output
+    equals the separate call's bit for bit.
+    """
+    import torch
+
+    built = _chain_jobs(steps, 40)
+    if built is None:
+        return None
+    arr, outs, keep, rows, dev = built
     if not available():
         raise RuntimeError(f"nf4 kernels unavailable: {_unavailable}")
     L = _lib.lib()
@@ -444,6 +458,54 @@ def matmul_chain(steps):
     stream = torch.cuda.current_stream(dev)
     _lib.check(L.nf4b_gemv_chain(arr, len(steps), rows, ws.data_ptr(), ws.numel(),
                                  ctypes.c_void_p(stream.cuda_stream)))
+    _stats["fast"] += len(steps)
+    return outs
+
+
+_step_workspaces: dict = {}
+
+
+def step_workspace(device, need: int):
+    """The decode step's own workspace on `device` (it keeps a launch counter
+    there, so it is never shared with the other kernels' workspaces)."""
+    import torch
+
+    idx = torch.device(device).index
+    ws = _step_workspaces.get(idx)
+    if ws is None or ws.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("the decode step's workspace must be sized before graph capture")
+        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=device)
+        _step_workspaces[idx] = ws
+    return ws
+
+
+def decode_step(steps):
+    """A whole decode step's dependent matmuls in ONE persistent launch
+    (``nf4b_decode_step``): the steps of ``matmul_chain`` (same dict format),
+    up to 152 of them, for 1 or 2 activation rows. The weights of step i + 1
+    stream while step i's outputs are handed over. Each output equals the
+    separate call up to fp32 summation order. Returns the outputs, or None
+    outside the envelope (blocksize 64, in_features % 256 == 0 and <= 10240,
+    out_features % 16 == 0); then nothing was launched."""
+    import torch
+
+    built = _chain_jobs(steps, 152)
+    if built is None:
+        return None
+    arr, outs, keep, rows, dev = built
+    if rows > 2 or any(o.shape[1] % 16 for o in outs):
+        return None
+    if not available():
+        raise RuntimeError(f"nf4 kernels unavailable: {_unavailable}")
+    L = _lib.lib()
+    need = int(L.nf4b_decode_step_workspace_size(arr, len(steps), rows))
+    if need == 0:
+        return None
+    ws = step_workspace(dev, need)
+    stream = torch.cuda.current_stream(dev)
+    _lib.check(L.nf4b_decode_step(arr, len(steps), rows, ws.data_ptr(), ws.numel(),
+                                  ctypes.c_void_p(stream.cuda_stream)))
     _stats["fast"] += len(steps)
     return outs
 
