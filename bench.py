@@ -492,9 +492,10 @@ def run_dualar(args, device, rank: int, world: int):
     del dec
     torch.cuda.empty_cache()
     return {
-        "workload": "config 5: random-init NF4 Dual-AR (36 slow layers + bf16 LM head 2560x155136, 4 fast layers x 9 "
-                    "steps + 2560x4096 codebook heads), 512-token prompt, frames 516.., temperature 0.7, top-p 0.8, "
-                    "top-k 64, repetition-aware resample; one CUDA graph per frame",
+        "workload": f"config 5: random-init NF4 Dual-AR (36 slow layers + bf16 LM head 2560x155136, 4 fast layers x 9 "
+                    f"steps + 2560x4096 codebook heads), 512-token prompt, {n} frames timed (positions from 515 on, "
+                    f"after 3 untimed), temperature 0.7, top-p 0.8, top-k 64, repetition-aware resample; one CUDA "
+                    f"graph per frame",
         "frames": n, "frames_per_s_per_replica": round(fps, 1), "frames_per_s": round(world * fps, 1),
         "codebook_tokens_per_s": round(world * fps * 10, 1), "ms_per_frame": round(1e3 / fps, 3),
         "bytes_per_frame": int(frame_bytes),
@@ -502,6 +503,253 @@ def run_dualar(args, device, rank: int, world: int):
                      "frac": round(frame_bytes * fps / 1e9 / float(peaks["hbm_gbs"]), 4), "peak_source": kind},
         "setup_s": round(build_s, 1),
     }
+
+
+def _replay_us(issue, stream, reps: int = 5) -> float:
+    """Microseconds per replay of a CUDA graph of `issue()` (its launches, in
+    stream order), after one warm replay; CUDA events on the capturing stream."""
+    import torch
+
+    with torch.cuda.stream(stream):
+        issue()
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        g.capture_begin()
+        issue()
+        g.capture_end()
+        g.replay()
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record(stream)
+        for _ in range(reps):
+            g.replay()
+        en.record(stream)
+    stream.synchronize()
+    us = st.elapsed_time(en) * 1e3 / reps
+    del g
+    return us
+
+
+def _frac(achieved: float, peak: float) -> float:
+    return round(achieved / peak, 4) if peak else None
+
+
+def run_config1(device, stream, peaks) -> dict:
+    """one 9728x2560 GEMV at M=1 with plain fp32 absmax,
+    cold L2 (48 distinct weight copies, 672 MB, launched in turn)."""
+    import torch
+
+    from ttspipe_b200 import _lib
+    from ttspipe_b200.quant import Linear4bit
+
+    n, k, copies = 9728, 2560, 48
+    mods = []
+    for i in range(copies):
+        g = torch.Generator(device=device).manual_seed(i)
+        lin = Linear4bit.from_float(torch.randn(n, k, generator=g, device=device) * 0.02, double_quant=False)
+        mods.append(lin)
+    from ttspipe_b200 import nf4gemv
+
+    for m in mods:
+        assert nf4gemv.prepare(m)
+    L = _lib.lib()
+    x = torch.randn(1, k, device=device).to(torch.bfloat16)
+    y = torch.empty(1, n, device=device, dtype=torch.bfloat16)
+    ws = torch.zeros(int(L.nf4b_gemm_workspace_size(ctypes.byref(mods[0]._nf4_fast["desc"]), 1)),
+                     dtype=torch.uint8, device=device)
+
+    def issue():
+        for m in mods:
+            _lib.check(L.nf4b_gemm(ctypes.byref(m._nf4_fast["desc"]), x.data_ptr(), y.data_ptr(), 1, 0, None,
+                                   ws.data_ptr(), ws.numel(), stream.cuda_stream))
+
+    us = _replay_us(issue, stream) / copies
+    byts = algorithmic_bytes(n, k, 1, 0, nested=False)
+    gbs = byts / us / 1e3
+    del mods
+    return {"workload": "config 1: one 9728x2560 NF4 GEMV, M=1, blocksize 64, plain fp32 absmax; 48 distinct "
+                        "weight copies launched in turn (672 MB > L2: cold)",
+            "us_per_launch": round(us, 2), "bytes_per_launch": byts, "value": round(gbs, 1), "unit": "GB/s",
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": _frac(gbs, float(peaks["hbm_gbs"]))},
+            "kernel": "nf4_gemv_reg_kernel (plain scales)"}
+
+
+def _layer_weights(layers):
+    """Per layer: the five NF4 weights (wqkv = q, k, v fused; wo; w1; w3; w2)."""
+    return [[m._nf4_fast["desc"] for m in mods] for mods in layers]
+
+
+def run_config3(layers, device, stream, peaks) -> dict:
+    """the layer's projections at batched decode M in
+    {1, 8, 32, 64} (GB/s over all 36 layers: cold) and prefill M in
+    {256, 512, 1024} (TFLOP/s over 8 layers, 417 MB of weights)."""
+    import torch
+
+    from ttspipe_b200 import _lib
+
+    L = _lib.lib()
+    descs = _layer_weights(layers)
+    shapes = [(PROJ[i][1], PROJ[i][2]) for i in range(5)]
+    ws = torch.zeros(64 << 20, dtype=torch.uint8, device=device)
+    out = {"workload": "config 3: the S2-Pro layer's projections (q, k, v fused as wqkv 6144x2560; o 2560x4096; "
+                       "gate, up 9728x2560; down 2560x9728), NF4 bs64 + double quant, one launch per projection; "
+                       "decode rows over all 36 layers (1.87 GB: cold L2), prefill rows over 8 layers",
+           "decode": [], "prefill": []}
+    for rows, n_layers, kind in ((1, 36, "decode"), (8, 36, "decode"), (32, 36, "decode"), (64, 36, "decode"),
+                                 (256, 8, "prefill"), (512, 8, "prefill"), (1024, 8, "prefill")):
+        xs = {kk: torch.randn(rows, kk, device=device).to(torch.bfloat16) for _, kk in shapes}
+        ys = {nn: torch.empty(rows, nn, device=device, dtype=torch.bfloat16) for nn, _ in shapes}
+
+        def issue():
+            for li in range(n_layers):
+                for d, (nn, kk) in zip(descs[li], shapes):
+                    _lib.check(L.nf4b_gemm(ctypes.byref(d), xs[kk].data_ptr(), ys[nn].data_ptr(), rows, 0, None,
+                                           ws.data_ptr(), ws.numel(), stream.cuda_stream))
+
+        us = _replay_us(issue, stream, reps=3)
+        byts = n_layers * sum(algorithmic_bytes(nn, kk, rows) for nn, kk in shapes)
+        flops = n_layers * sum(2.0 * rows * nn * kk for nn, kk in shapes)
+        gbs, tfs = byts / us / 1e3, flops / us / 1e6
+        rec = {"rows": rows, "us_per_layer": round(us / n_layers, 2), "GBps": round(gbs, 1),
+               "TFLOPps": round(tfs, 2), "kernel": "GEMV (nf4_gemv_*)" if rows <= 32 else "tcgen05 GEMM"}
+        if kind == "decode":
+            rec["roofline"] = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                               "frac": _frac(gbs, float(peaks["hbm_gbs"]))}
+        else:
+            rec["roofline"] = {"bound": "tensor", "achieved": round(tfs, 1), "peak": peaks.get("bf16_tflops"),
+                               "unit": "TFLOP/s", "frac": _frac(tfs, float(peaks.get("bf16_tflops") or 0)),
+                               "frac_of_sustained": _frac(tfs, float(peaks.get("bf16_tflops_sustained") or 0))}
+        out[kind].append(rec)
+        del xs, ys
+    return out
+
+
+def run_config4(device, stream, peaks) -> dict:
+    """RMSNorm over 2560, q/k norm-free rotary + KV write of
+    one position (32 q / 8 kv heads x 128, theta 1e6), decode attention over a
+    2048-row cache; 16 distinct caches (134 MB > L2) launched in turn."""
+    import torch
+
+    from ttspipe_b200 import _lib, fastpath, fusedops, model
+
+    nh, nkv, max_len, layers = 32, 8, 2048, 16
+    ks = [torch.randn(nkv, max_len, 128, device=device).to(torch.bfloat16) for _ in range(layers)]
+    vs = [torch.randn(nkv, max_len, 128, device=device).to(torch.bfloat16) for _ in range(layers)]
+    q = torch.randn(nh, 128, device=device).to(torch.bfloat16)
+    o = torch.empty(nh, 128, device=device, dtype=torch.bfloat16)
+    pos = torch.tensor([max_len - 1], device=device)
+    hidden = torch.randn(1, 2560, device=device).to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(2560, device=device)).to(torch.bfloat16)
+    qkv = torch.randn((nh + 2 * nkv) * 128, device=device).to(torch.bfloat16)
+    freqs = model.precompute_freqs_cis(4096, 128, 1e6, device=device)
+    L = _lib.lib()
+
+    def attention():
+        for i in range(layers):
+            fastpath.kernel_attention(q, ks[i], vs[i], o, n_head=nh, n_kv=nkv, pos=pos, window=max_len,
+                                      max_len=max_len)
+
+    def norm():
+        for _ in range(layers):
+            fusedops.rms_norm(hidden, nw, 1e-6)
+
+    def rope_kv():
+        for i in range(layers):
+            _lib.check(L.nf4b_qk_rope_kv(qkv.data_ptr(), None, None, 1e-6, freqs.data_ptr(), _lib.NF4B_BF16,
+                                         pos.data_ptr(), o.data_ptr(), ks[i].data_ptr(), vs[i].data_ptr(), nh, nkv,
+                                         128, max_len, stream.cuda_stream))
+
+    att_us = _replay_us(attention, stream) / layers
+    norm_us = _replay_us(norm, stream) / layers
+    rope_us = _replay_us(rope_kv, stream) / layers
+    kv_bytes = 2 * nkv * max_len * 128 * 2
+    gbs = kv_bytes / att_us / 1e3
+    return {"workload": "config 4: RMSNorm (hidden 2560, eps 1e-6), rotary + KV write of one position "
+                        "(32 q / 8 kv heads x 128, theta 1e6, bf16 freqs), GQA decode attention over L = 2048 "
+                        "cached rows; 16 distinct caches (134 MB > L2) in turn",
+            "attention_us": round(att_us, 2), "attention_GBps_of_kv": round(gbs, 1), "kv_bytes": kv_bytes,
+            "rms_norm_us": round(norm_us, 2), "rope_kv_us": round(rope_us, 2),
+            "launches_per_layer_step": 3,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": _frac(gbs, float(peaks["hbm_gbs"])),
+                         "kernel": "decode attention (8-CTA cluster per KV head)"}}
+
+
+def run_reference_gpu(layers, device, stream, peaks) -> dict:
+    """The reference's own GPU kernel, nf4_mma (app/engine/nf4gemv.py:94-231,
+    fp16 only), compiled from its source by oracle/build_ref.py into
+    oracle/_ref/nf4mma_ref.so and launched as its matmul does, on the same 36
+    layers of NF4 weights at M in {1, 8, 32} (one launch per projection, no
+    epilogue): GB/s beside this build's GEMV on the same launches (config 3)."""
+    import numpy as np
+    import torch
+
+    from oracle import build_ref
+    from ttspipe_b200 import _lib
+
+    path = build_ref.gpu_so_path()
+    if path is None:
+        return {"unavailable": "oracle/_ref/nf4mma_ref.so was not built (the reference checkout is needed to build it)"}
+    ref = ctypes.CDLL(str(path))
+    ref.nf4mma_ref_launch.restype = ctypes.c_int
+    vp, i32 = ctypes.c_void_p, ctypes.c_int
+    ref.nf4mma_ref_launch.argtypes = [i32, i32, vp, vp, vp, vp, vp, vp, vp, ctypes.c_float, i32, i32, i32, i32,
+                                      i32, vp, i32, vp]
+    from oracle import nf4_oracle as orc
+
+    lut = torch.tensor(orc.NF4_CODE, dtype=torch.float32, device=device)
+    descs = _layer_weights(layers)
+    shapes = [(PROJ[i][1], PROJ[i][2]) for i in range(5)]
+    out = {"workload": "the reference's nf4_mma (fp16; NVRTC source compiled with nvcc --use_fast_math for "
+                       "sm_100a, launched with its own grid/block choice) on the config-2 layer's projections "
+                       "at M rows, 36 layers in turn (cold L2)", "rows": []}
+    L = _lib.lib()
+    ws = torch.zeros(64 << 20, dtype=torch.uint8, device=device)
+    for rows in (1, 8, 32):
+        xs = {kk: torch.randn(rows, kk, device=device).to(torch.float16) for _, kk in shapes}
+        ys = {nn: torch.empty(rows, nn, device=device, dtype=torch.float16) for nn, _ in shapes}
+
+        def call(d, nn, kk):
+            st = ref.nf4mma_ref_launch(rows, 1, xs[kk].data_ptr(), d.packed, d.absmax_code, d.absmax, d.code2,
+                                       ys[nn].data_ptr(), lut.data_ptr(), d.offset, nn, kk, kk // 64, 6,
+                                       int(d.blocksize2).bit_length() - 1, None, 0, stream.cuda_stream)
+            if st != 0:
+                raise RuntimeError(f"reference nf4_mma launch failed ({st})")
+
+        def issue():
+            for li in range(N_LAYERS):
+                for d, (nn, kk) in zip(descs[li], shapes):
+                    call(d, nn, kk)
+
+        us = _replay_us(issue, stream, reps=3)
+        byts = N_LAYERS * sum(algorithmic_bytes(nn, kk, rows) for nn, kk in shapes)
+        gbs = byts / us / 1e3
+        # the same products through this build (bf16), for a like-for-like rate and a check
+        xb = {kk: v.to(torch.bfloat16) for kk, v in xs.items()}
+        yb = {nn: torch.empty(rows, nn, device=device, dtype=torch.bfloat16) for nn, _ in shapes}
+
+        def ours():
+            for li in range(N_LAYERS):
+                for d, (nn, kk) in zip(descs[li], shapes):
+                    _lib.check(L.nf4b_gemm(ctypes.byref(d), xb[kk].data_ptr(), yb[nn].data_ptr(), rows, 0, None,
+                                           ws.data_ptr(), ws.numel(), stream.cuda_stream))
+
+        ours_us = _replay_us(ours, stream, reps=3)
+        d, (nn, kk) = descs[0][0], shapes[0]
+        call(d, nn, kk)
+        _lib.check(L.nf4b_gemm(ctypes.byref(d), xb[kk].data_ptr(), yb[nn].data_ptr(), rows, 0, None, ws.data_ptr(),
+                               ws.numel(), stream.cuda_stream))
+        stream.synchronize()
+        a, b2 = ys[nn].float().cpu().numpy(), yb[nn].float().cpu().numpy()
+        rel = float(np.abs(a - b2).max() / (np.sqrt((b2 ** 2).mean()) + 1e-12))
+        out["rows"].append({"rows": rows, "reference_us_per_layer": round(us / N_LAYERS, 2),
+                            "reference_GBps": round(gbs, 1),
+                            "reference_frac_of_hbm": _frac(gbs, float(peaks["hbm_gbs"])),
+                            "ours_us_per_layer": round(ours_us / N_LAYERS, 2),
+                            "ours_GBps": round(byts / ours_us / 1e3, 1),
+                            "speedup": round(us / ours_us, 2),
+                            "max_abs_diff_over_rms_vs_ours": round(rel, 4)})
+    return out
 
 
 def run_gpu(args):
@@ -627,6 +875,14 @@ def run_gpu(args):
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     del graph
+    if not args.no_configs:
+        peaks_d = peaks
+        configs = {"config1": run_config1(device, stream, peaks_d),
+                   "config3": run_config3(layers, device, stream, peaks_d),
+                   "config4": run_config4(device, stream, peaks_d),
+                   "reference_gpu_kernel": run_reference_gpu(layers, device, stream, peaks_d)}
+        if rank == 0:
+            result.update(configs)
     if args.dualar_frames > 0:
         dual = run_dualar(args, device, rank, world)
         if rank == 0:
@@ -1015,8 +1271,10 @@ def main():
     ap.add_argument("--detail", action="store_true")
     ap.add_argument("--mode", default="decode", choices=sorted(MODES))
     ap.add_argument("--chain-layers", type=int, default=9, help="layers per nf4b_gemv_chain launch (--mode chain)")
-    ap.add_argument("--dualar-frames", type=int, default=128,
-                    help="Dual-AR frames timed after the GEMV step (config 5; 0: skip)")
+    ap.add_argument("--dualar-frames", type=int, default=1024,
+                    help="Dual-AR frames timed after the GEMV step (config 5: 1024 slow steps; 0: skip)")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the config 1 / 3 / 4 and reference-GPU-kernel objects of the JSON line")
     ap.add_argument("--prefetch-distance", type=int, default=0,
                     help="launches ahead whose weights each launch streams into L2 (0: none; "
                          "measured slower at 1-3 on B200, so off by default)")
