@@ -282,9 +282,14 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(
 
 constexpr int kCThreads = 256;
 
+// Stages of the cluster kernel's K/V ring: every chunk of a CTA's share is in
+// flight at once up to this depth (a 2048-row window over 8 CTAs is 4 chunks
+// each), so the chunks' copy latencies overlap instead of adding up.
+constexpr int kCStages = 4;
+
 template <int G>
 struct ClusterSmem {
-  alignas(128) uint16_t kv[2][2][ATTN_CHUNK * kD];  // [stage][K, V][rows x 128]
+  alignas(128) uint16_t kv[kCStages][2][ATTN_CHUNK * kD];  // [stage][K, V][rows x 128]
   float q[G][kD];
   float sc[G][ATTN_CHUNK];
   float red[kCThreads / 32][G][kD];
@@ -292,7 +297,7 @@ struct ClusterSmem {
   float part_m[G], part_l[G];
   float alpha[G];
   float run_m[G], run_l[G];
-  unsigned long long bar[2];
+  unsigned long long bar[kCStages];
   // the fused q/k norm + rotary prologue (QkvIn)
   float sx[2][kD];
   double nred[kCThreads / 32];
@@ -368,6 +373,11 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
   const uint32_t rank = cluster_rank(), C = cluster_size();
 
   pdl_wait();  // the new K/V row and q come from the previous kernel
+  // The next kernel (the wo GEMV) may be scheduled now: its CTAs load their
+  // first weights on the SMs this grid leaves free; it reads this kernel's
+  // output only after its own dependency wait, which waits for this grid to
+  // complete.
+  pdl_launch_dependents();
   // A window of one chunk read by one CTA (the fast AR's): its rows' copies go
   // out before the position is read - the whole window, rows past the live
   // length are never used - saving a round trip.
@@ -402,27 +412,28 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
   const bf16_t* kbase = kc + (size_t)kh * max_len * kD;
   const bf16_t* vbase = vc + (size_t)kh * max_len * kD;
 
-  auto issue = [&](int ci) {  // thread 0: chunk ci into stage ci & 1
+  auto issue = [&](int ci) {  // thread 0: chunk ci into stage ci % kCStages
     const long long j0 = r0 + (long long)ci * ATTN_CHUNK;
     const long long n = (r1 - j0 < ATTN_CHUNK) ? r1 - j0 : ATTN_CHUNK;
     const uint32_t bytes = (uint32_t)n * kD * 2;
-    const uint32_t bar = sm_u32(&sm.bar[ci & 1]);
+    const int stg = ci % kCStages;
+    const uint32_t bar = sm_u32(&sm.bar[stg]);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     sm_u32(sm.kv[ci & 1][0])),
+                     sm_u32(sm.kv[stg][0])),
                  "l"(kbase + j0 * kD), "r"(bytes), "r"(bar)
                  : "memory");
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     sm_u32(sm.kv[ci & 1][1])),
+                     sm_u32(sm.kv[stg][1])),
                  "l"(vbase + j0 * kD), "r"(bytes), "r"(bar)
                  : "memory");
   };
   if (tid == 0 && !whole_window) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&sm.bar[0])) : "memory");
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&sm.bar[1])) : "memory");
+    for (int i = 0; i < kCStages; ++i)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&sm.bar[i])) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int ci = 0; ci < 2 && ci < my_chunks; ++ci) issue(ci);
+    for (int ci = 0; ci < kCStages && ci < my_chunks; ++ci) issue(ci);
   }
   const bool fused = in.qkv != nullptr;  // q/k/v from the wqkv output (pos given, no mask)
   const long long p_new = fused ? pos_ptr[0] : -1;
@@ -468,6 +479,18 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
   __syncthreads();
 
   const int dg = tid & 15, pg = tid >> 4;  // P.V: dimensions dg*8 .. +7, chunk rows pg*4 .. +3
+  // This lane's slice of every query head for the scores (dimensions
+  // (lane & 7) * 16 .. +15), held in registers as bf16 pairs - the values are
+  // bf16 already - instead of re-reading shared memory for every key row.
+  uint32_t qr[G][8];
+  {
+    const int li = lane & 7;
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        qr[h][e] = (uint32_t)f2bf(sm.q[h][li * 16 + 2 * e]) | ((uint32_t)f2bf(sm.q[h][li * 16 + 2 * e + 1]) << 16);
+  }
   float acc[G][8];
 #pragma unroll
   for (int h = 0; h < G; ++h)
@@ -475,17 +498,29 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
     for (int e = 0; e < 8; ++e) acc[h][e] = 0.f;
   bool ok = true;
   for (int ci = 0; ci < my_chunks; ++ci) {
-    ok = ok && wait_bar_parity(sm_u32(&sm.bar[ci & 1]), (uint32_t)(ci >> 1) & 1u);
+    const int stg = ci % kCStages;
+    // one decision for the whole CTA: a chunk whose copy never lands stops it
+    if (!__syncthreads_and(wait_bar_parity(sm_u32(&sm.bar[stg]), (uint32_t)(ci / kCStages) & 1u))) {
+      ok = false;
+      if (tid == 0) {
+        // the copies still in flight (chunks ci .. the last issued) land before the
+        // CTA releases its shared memory - within one more bounded wait each
+        for (int cj = ci; cj < my_chunks && cj < ci + kCStages; ++cj)
+          if (!wait_bar_parity(sm_u32(&sm.bar[cj % kCStages]), (uint32_t)(cj / kCStages) & 1u)) break;
+      }
+      __syncthreads();
+      break;
+    }
     const long long j0 = r0 + (long long)ci * ATTN_CHUNK;
     const int rows = (int)((r1 - j0 < ATTN_CHUNK) ? r1 - j0 : ATTN_CHUNK);
     if (fused && p_new >= j0 && p_new < j0 + rows) {
       // the copy may predate rank 0's store of the new row: use the computed one
       const int d = tid & (kD - 1), half = tid >> 7;
-      sm.kv[ci & 1][half][(int)(p_new - j0) * kD + d] = (half ? sm.vnew : sm.knew)[d];
+      sm.kv[stg][half][(int)(p_new - j0) * kD + d] = (half ? sm.vnew : sm.knew)[d];
       __syncthreads();
     }
-    const uint16_t* ks = sm.kv[ci & 1][0];
-    const uint16_t* vs = sm.kv[ci & 1][1];
+    const uint16_t* ks = sm.kv[stg][0];
+    const uint16_t* vs = sm.kv[stg][1];
     // Scores: a warp takes 8 rows, four at a time, eight lanes per row.
     {
       const int gi = lane >> 3, li = lane & 7;
@@ -504,8 +539,8 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
             const float ka = __uint_as_float(kw[e] << 16), kb = __uint_as_float(kw[e] & 0xFFFF0000u);
 #pragma unroll
             for (int h = 0; h < G; ++h) {
-              dot[h] = fmaf(sm.q[h][li * 16 + 2 * e], ka, dot[h]);
-              dot[h] = fmaf(sm.q[h][li * 16 + 2 * e + 1], kb, dot[h]);
+              dot[h] = fmaf(__uint_as_float(qr[h][e] << 16), ka, dot[h]);
+              dot[h] = fmaf(__uint_as_float(qr[h][e] & 0xFFFF0000u), kb, dot[h]);
             }
           }
         }
@@ -570,7 +605,7 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
       }
     }
     __syncthreads();  // every thread is done with this stage
-    if (tid == 0 && ci + 2 < my_chunks) issue(ci + 2);
+    if (tid == 0 && ci + kCStages < my_chunks) issue(ci + kCStages);
   }
   // This CTA's partial: sum the 16 row groups in a fixed order.
 #pragma unroll
@@ -619,7 +654,6 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
     }
   }
   cluster_sync();  // partials stay alive until CTA 0 has read them
-  pdl_launch_dependents();
 }
 
 }  // namespace
@@ -689,10 +723,11 @@ cudaError_t launch_cluster_g(const uint16_t* q, const uint16_t* kc, const uint16
 cudaError_t launch_cluster_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int64_t* pos,
                                      const uint8_t* mask, uint16_t* out, int nh, int nkv, int max_len, int window,
                                      cudaStream_t stream, const QkvIn& in) {
-  // Clusters of 8 (the portable size): measured as fast as 16 at 2048 rows
-  // and faster below; fewer when the window has fewer 64-row chunks (a
-  // window of one chunk - the fast AR's - runs one CTA per KV head, no
-  // cross-CTA merge). chosen: 0 unknown, 1 launches, -1 cannot be resident.
+  // Clusters of 8 (the portable size; 16 measured slower at every window
+  // length, 18.6 against 9.3 us at 512 rows, 24.4 against 17.1 at 2048);
+  // fewer when the window has fewer 64-row chunks (a window of one chunk -
+  // the fast AR's - runs one CTA per KV head, no cross-CTA merge). chosen:
+  // 0 unknown, 1 launches, -1 cannot be resident.
   static int chosen[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
