@@ -724,31 +724,38 @@ def run_reference_gpu(layers, device, stream, peaks) -> dict:
         us = _replay_us(issue, stream, reps=3)
         byts = N_LAYERS * sum(algorithmic_bytes(nn, kk, rows) for nn, kk in shapes)
         gbs = byts / us / 1e3
-        # the same products through this build (bf16), for a like-for-like rate and a check
+        # the same products through this build: in fp16 on the very same inputs
+        # (like for like, and a check of the outputs), and in bf16
+        f16 = ctypes.byref(_lib.GemmOpts(None, None, None, 0.0, _lib.NF4B_F16))
+        yh = {nn: torch.empty(rows, nn, device=device, dtype=torch.float16) for nn, _ in shapes}
         xb = {kk: v.to(torch.bfloat16) for kk, v in xs.items()}
         yb = {nn: torch.empty(rows, nn, device=device, dtype=torch.bfloat16) for nn, _ in shapes}
 
-        def ours():
+        def ours(x, y, opts):
             for li in range(N_LAYERS):
                 for d, (nn, kk) in zip(descs[li], shapes):
-                    _lib.check(L.nf4b_gemm(ctypes.byref(d), xb[kk].data_ptr(), yb[nn].data_ptr(), rows, 0, None,
-                                           ws.data_ptr(), ws.numel(), stream.cuda_stream))
+                    _lib.check(L.nf4b_gemm_ex(ctypes.byref(d), x[kk].data_ptr(), y[nn].data_ptr(), rows, 0, None,
+                                              ws.data_ptr(), ws.numel(), opts, stream.cuda_stream))
 
-        ours_us = _replay_us(ours, stream, reps=3)
+        ours_us = _replay_us(lambda: ours(xs, yh, f16), stream, reps=3)
+        ours_bf_us = _replay_us(lambda: ours(xb, yb, None), stream, reps=3)
         d, (nn, kk) = descs[0][0], shapes[0]
         call(d, nn, kk)
-        _lib.check(L.nf4b_gemm(ctypes.byref(d), xb[kk].data_ptr(), yb[nn].data_ptr(), rows, 0, None, ws.data_ptr(),
-                               ws.numel(), stream.cuda_stream))
+        _lib.check(L.nf4b_gemm_ex(ctypes.byref(d), xs[kk].data_ptr(), yh[nn].data_ptr(), rows, 0, None,
+                                  ws.data_ptr(), ws.numel(), f16, stream.cuda_stream))
         stream.synchronize()
-        a, b2 = ys[nn].float().cpu().numpy(), yb[nn].float().cpu().numpy()
-        rel = float(np.abs(a - b2).max() / (np.sqrt((b2 ** 2).mean()) + 1e-12))
+        a, b2 = ys[nn].double().cpu().numpy(), yh[nn].double().cpu().numpy()
+        rel = float(np.abs(a - b2).max() / (np.sqrt((a ** 2).mean()) + 1e-12))
         out["rows"].append({"rows": rows, "reference_us_per_layer": round(us / N_LAYERS, 2),
                             "reference_GBps": round(gbs, 1),
                             "reference_frac_of_hbm": _frac(gbs, float(peaks["hbm_gbs"])),
-                            "ours_us_per_layer": round(ours_us / N_LAYERS, 2),
-                            "ours_GBps": round(byts / ours_us / 1e3, 1),
-                            "speedup": round(us / ours_us, 2),
-                            "max_abs_diff_over_rms_vs_ours": round(rel, 4)})
+                            "ours_f16_us_per_layer": round(ours_us / N_LAYERS, 2),
+                            "ours_f16_GBps": round(byts / ours_us / 1e3, 1),
+                            "speedup_f16": round(us / ours_us, 2),
+                            "ours_bf16_us_per_layer": round(ours_bf_us / N_LAYERS, 2),
+                            "ours_bf16_GBps": round(byts / ours_bf_us / 1e3, 1),
+                            "speedup_bf16": round(us / ours_bf_us, 2),
+                            "f16_max_abs_diff_over_rms": round(rel, 5)})
     return out
 
 

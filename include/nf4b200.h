@@ -117,6 +117,17 @@ typedef struct nf4b_gemm_opts {
    * k_in % 128 == 0, rows * k_in * 2 <= 40 KB); NF4B_ERR_SHAPE otherwise. */
   const void* norm_weight;
   float norm_eps;
+  /* Activation type of x, operand, y and norm_weight: 0 or NF4B_BF16 = bf16,
+   * NF4B_F16 = fp16 (the reference's own kernel serves fp16 only,
+   * app/engine/nf4gemv.py:439; its TTS_HALF default, app/config.py:107). fp16
+   * runs the register-fed decode GEMV for 1..2 rows (blocksize 64,
+   * k_in % 256 == 0, 32-byte aligned packed codes; a fused RMSNorm and the
+   * gated pair as for bf16) and the tcgen05 GEMM for every other row count,
+   * with the reference's rounding points in fp16 (fp32 accumulation; the
+   * matmul output and each epilogue op rounded to fp16). The fused rotary
+   * store and the chain / decode-step launches are bf16 only. Any other value:
+   * NF4B_ERR_DTYPE. */
+  int dtype;
 } nf4b_gemm_opts;
 
 /* nf4b_gemm with options (opts may be NULL). */
@@ -395,6 +406,32 @@ int nf4b_qkv_attention(const void* qkv, const void* q_norm_w, const void* k_norm
                        const void* freqs, int freqs_dtype, const int64_t* pos, void* q_scratch,
                        void* k_cache, void* v_cache, void* out, int n_head, int n_kv, int head_dim, int max_len,
                        int window, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * The elementwise calls above with the activation type as an argument: dtype
+ * NF4B_BF16 (what the calls without _ex do) or NF4B_F16 - the reference's own
+ * kernels are fp16 (app/engine/fusedops.py:61-132, app/engine/fusedlayer.py:
+ * 56-157) - for x / y / weights / q / caches / out alike; the rotary table
+ * keeps its own freqs_dtype. fp16 uses the same formulas with fp16 at every
+ * rounding point. Any other dtype: NF4B_ERR_DTYPE.
+ */
+int nf4b_rms_norm_ex(const void* x, const void* weight, void* y, int rows, int width, float eps, int dtype,
+                     void* stream);
+int nf4b_rope_ex(const void* x, const void* freqs, int freqs_dtype, void* y, int batch, int seq,
+                 int heads, int head_dim, int dtype, void* stream);
+int nf4b_qk_rope_kv_ex(const void* qkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                       const void* freqs, int freqs_dtype, const int64_t* pos, void* q_out,
+                       void* k_cache, void* v_cache, int n_head, int n_kv, int head_dim, int max_len,
+                       int dtype, void* stream);
+int nf4b_decode_attention_ex(const void* q, const void* k_cache, const void* v_cache,
+                             const int64_t* pos, const uint8_t* mask, void* out, int n_head, int n_kv,
+                             int head_dim, int max_len, int window, void* workspace,
+                             size_t workspace_bytes, int dtype, void* stream);
+int nf4b_qkv_attention_ex(const void* qkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                          const void* freqs, int freqs_dtype, const int64_t* pos, void* q_scratch,
+                          void* k_cache, void* v_cache, void* out, int n_head, int n_kv, int head_dim,
+                          int max_len, int window, void* workspace, size_t workspace_bytes, int dtype,
+                          void* stream);
 
 #ifdef __cplusplus
 }

@@ -6,7 +6,9 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` leg of
 path fails loudly instead of falling back here.
 
 Everything is plain NumPy on bf16 *bit patterns* (uint16) so that every
-rounding point is explicit. Each function names the reference file:line whose
+rounding point is explicit; the functions with an ``f16`` switch take and
+return fp16 bit patterns instead, with the same formulas and fp16 at every
+rounding point (the reference's GPU dtype). Each function names the reference file:line whose
 arithmetic it restates (paths relative to the ttspipe repository root).
 
 Pinning: the restatement is checked against fixtures produced by running the
@@ -55,6 +57,37 @@ def bf16_to_f32(b) -> np.ndarray:
 def round_bf(a) -> np.ndarray:
     """fp32 -> bf16 -> fp32 (app/engine/nf4cpu.py:77)."""
     return bf16_to_f32(f32_to_bf16(a))
+
+
+def f32_to_f16(a) -> np.ndarray:
+    """Round fp32 to fp16 (nearest-even, overflow to infinity, as the
+    reference's `f2h` = __float2half_rn) and return the uint16 bit patterns."""
+    return np.ascontiguousarray(a, dtype=np.float32).astype(np.float16).view(np.uint16)
+
+
+def f16_to_f32(b) -> np.ndarray:
+    """Widen fp16 bit patterns to fp32 (exact)."""
+    return np.ascontiguousarray(b, dtype=np.uint16).view(np.float16).astype(np.float32)
+
+
+def round_f16(a) -> np.ndarray:
+    """fp32 -> fp16 -> fp32."""
+    return f16_to_f32(f32_to_f16(a))
+
+
+def act_to_f32(b, f16: bool = False) -> np.ndarray:
+    """Widen bit patterns of the activation type (bf16, or fp16 if `f16`)."""
+    return f16_to_f32(b) if f16 else bf16_to_f32(b)
+
+
+def f32_to_act(a, f16: bool = False) -> np.ndarray:
+    """Round fp32 to the activation type's bit patterns."""
+    return f32_to_f16(a) if f16 else f32_to_bf16(a)
+
+
+def round_act(a, f16: bool = False) -> np.ndarray:
+    """fp32 -> activation type -> fp32."""
+    return act_to_f32(f32_to_act(a, f16), f16)
 
 
 # --------------------------------------------------------------------------
@@ -196,6 +229,17 @@ def dequantize_bf16(packed, scales, blocksize: int = 64) -> np.ndarray:
     return f32_to_bf16(vals.reshape(n, k))
 
 
+def dequantize_f16(packed, scales, blocksize: int = 64) -> np.ndarray:
+    """Dequantised weight as fp16 bits [N, K]: RNE_f16(NF4[q] * scale), the
+    per-element value of the reference GPU kernel's A fragments
+    (app/engine/nf4gemv.py:185-188, `pack2` of the fp32 products)."""
+    q = nf4_unpack(packed)
+    n, k = q.shape
+    s = np.asarray(scales, dtype=np.float32).reshape(n, k // blocksize)
+    vals = (NF4_CODE[q].reshape(n, k // blocksize, blocksize) * s[:, :, None]).astype(np.float32)
+    return f32_to_f16(vals.reshape(n, k))
+
+
 # --------------------------------------------------------------------------
 # matmul with the fused epilogues (a4-a7)
 # --------------------------------------------------------------------------
@@ -203,47 +247,47 @@ def dequantize_bf16(packed, scales, blocksize: int = 64) -> np.ndarray:
 EPI_NONE, EPI_RESIDUAL, EPI_SILU_GATE = 0, 1, 2
 
 
-def silu_bf16(a_bits) -> np.ndarray:
+def silu_bf16(a_bits, f16: bool = False) -> np.ndarray:
     """bf16(silu(a)) with the division done in fp32 (app/engine/nf4gemv.py:224-226,
-    app/engine/nf4cpu.py:249-251)."""
-    a = bf16_to_f32(a_bits)
+    app/engine/nf4cpu.py:249-251); fp16 in and out if `f16`."""
+    a = act_to_f32(a_bits, f16)
     with np.errstate(over="ignore"):
         s = (a / (np.float32(1.0) + np.exp(-a).astype(np.float32))).astype(np.float32)
-    return f32_to_bf16(s)
+    return f32_to_act(s, f16)
 
 
-def epilogue(acc, epi: int = EPI_NONE, operand=None) -> np.ndarray:
-    """The matmul's store: its own output rounded to bf16 first, then each
-    fused elementwise op rounded where the fork rounds it
-    (app/engine/nf4gemv.py:212-228)."""
-    y = round_bf(np.asarray(acc, dtype=np.float32))
+def epilogue(acc, epi: int = EPI_NONE, operand=None, f16: bool = False) -> np.ndarray:
+    """The matmul's store: its own output rounded to the activation type
+    first, then each fused elementwise op rounded where the fork rounds it
+    (app/engine/nf4gemv.py:212-228, which is this with f16)."""
+    y = round_act(np.asarray(acc, dtype=np.float32), f16)
     if epi == EPI_NONE:
-        return f32_to_bf16(y)
+        return f32_to_act(y, f16)
     r = np.asarray(operand, dtype=np.uint16).reshape(y.shape)
-    if epi == EPI_RESIDUAL:
-        return f32_to_bf16((bf16_to_f32(r) + y).astype(np.float32))
-    if epi == EPI_SILU_GATE:
-        return f32_to_bf16((bf16_to_f32(silu_bf16(r)) * y).astype(np.float32))
+    with np.errstate(over="ignore", invalid="ignore"):
+        if epi == EPI_RESIDUAL:
+            return f32_to_act((act_to_f32(r, f16) + y).astype(np.float32), f16)
+        if epi == EPI_SILU_GATE:
+            return f32_to_act((act_to_f32(silu_bf16(r, f16), f16) * y).astype(np.float32), f16)
     raise ValueError(f"unknown epilogue {epi}")
 
 
-def matmul_exact(x_bits, w_bits) -> np.ndarray:
-    """X @ Wᵀ of bf16 inputs, accumulated in fp64 and NOT rounded: the value a
-    bf16-output kernel approximates (its error = accumulation + its own final
-    rounding, at most half a bf16 ulp when the accumulation is exact)."""
-    x = bf16_to_f32(x_bits).astype(np.float64)
-    w = bf16_to_f32(w_bits).astype(np.float64)
+def matmul_exact(x_bits, w_bits, f16: bool = False) -> np.ndarray:
+    """X @ Wᵀ of bf16 (fp16 if `f16`) inputs, accumulated in fp64 and NOT
+    rounded: the value a kernel with outputs of that type approximates (its
+    error = accumulation + its own final rounding, at most half an ulp when
+    the accumulation is exact)."""
+    x = act_to_f32(x_bits, f16).astype(np.float64)
+    w = act_to_f32(w_bits, f16).astype(np.float64)
     return x.reshape(-1, w.shape[1]) @ w.T
 
 
-def matmul_dequant(x_bits, w_bits, epi: int = EPI_NONE, operand=None) -> np.ndarray:
-    """Y = X @ Wᵀ from the dequantised bf16 weight, accumulated exactly (fp64)
+def matmul_dequant(x_bits, w_bits, epi: int = EPI_NONE, operand=None, f16: bool = False) -> np.ndarray:
+    """Y = X @ Wᵀ from the dequantised weight, accumulated exactly (fp64)
     and rounded once: the reference's "dequantise then matmul"
     (app/engine/nf4gemv.py:36-41; tests/test_nf4gemv.py:119-141)."""
-    x = bf16_to_f32(x_bits).astype(np.float64)
-    w = bf16_to_f32(w_bits).astype(np.float64)
-    acc = x.reshape(-1, w.shape[1]) @ w.T
-    return epilogue(acc.astype(np.float32), epi, operand)
+    acc = matmul_exact(x_bits, w_bits, f16)
+    return epilogue(acc.astype(np.float32), epi, operand, f16)
 
 
 def nf4cpu_gemv(x_bits, packed, absmax_bf16_bits, code_bf16_bits) -> np.ndarray:
@@ -267,44 +311,45 @@ def nf4cpu_gemv(x_bits, packed, absmax_bf16_bits, code_bf16_bits) -> np.ndarray:
 # --------------------------------------------------------------------------
 
 
-def rms_norm(x_bits, w_bits, eps: float) -> np.ndarray:
+def rms_norm(x_bits, w_bits, eps: float, f16: bool = False) -> np.ndarray:
     """The fork's RMSNorm in bf16: y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w)
     (fork formula app/engine/fusedops.py:9-13; bf16 rounding points as
-    app/engine/nf4cpu.py:456-461). The sum of squares is exact (fp64); the
-    reciprocal square root is correctly rounded fp32."""
-    x = bf16_to_f32(x_bits)
+    app/engine/nf4cpu.py:456-461; with `f16`, fp16 at both points as the
+    reference kernel app/engine/fusedops.py:61-95). The sum of squares is
+    exact (fp64); the reciprocal square root is correctly rounded fp32."""
+    x = act_to_f32(x_bits, f16)
     d = x.shape[-1]
     xf = x.reshape(-1, d)
     ms = (xf.astype(np.float64) ** 2).sum(-1) / d
     t = (ms.astype(np.float32) + np.float32(eps)).astype(np.float32)
     r = (1.0 / np.sqrt(t.astype(np.float64))).astype(np.float32)
-    y1 = round_bf((xf * r[:, None]).astype(np.float32))
-    w = bf16_to_f32(w_bits)
-    return f32_to_bf16((y1 * w[None, :]).astype(np.float32)).reshape(np.shape(x_bits))
+    y1 = round_act((xf * r[:, None]).astype(np.float32), f16)
+    w = act_to_f32(w_bits, f16)
+    return f32_to_act((y1 * w[None, :]).astype(np.float32), f16).reshape(np.shape(x_bits))
 
 
-def head_rms_norm(x_f32, w_bits, eps: float) -> np.ndarray:
+def head_rms_norm(x_f32, w_bits, eps: float, f16: bool = False) -> np.ndarray:
     """Per-head q/k RMSNorm over head_dim with ONE rounding of x*r*w, as both
     reference kernels do it (app/engine/fusedlayer.py:74-84,
-    app/engine/nf4cpu.py:501-510). Input fp32 [..., D] (already bf16 values);
-    returns fp32 values that are bf16-exact."""
+    app/engine/nf4cpu.py:501-510). Input fp32 [..., D] (already bf16 values,
+    fp16 with `f16`); returns fp32 values exact in that type."""
     x = np.asarray(x_f32, dtype=np.float32)
     d = x.shape[-1]
     ss = (x.astype(np.float64) ** 2).sum(-1, keepdims=True)
     t = ((ss / d).astype(np.float32) + np.float32(eps)).astype(np.float32)
     r = (1.0 / np.sqrt(t.astype(np.float64))).astype(np.float32)
-    w = bf16_to_f32(w_bits)
-    return round_bf(((x * r).astype(np.float32) * w).astype(np.float32))
+    w = act_to_f32(w_bits, f16)
+    return round_act(((x * r).astype(np.float32) * w).astype(np.float32), f16)
 
 
-def rope(x_bits, freqs) -> np.ndarray:
+def rope(x_bits, freqs, f16: bool = False) -> np.ndarray:
     """Interleaved-pair rotary: (x0*c - x1*s, x1*c + x0*s), each product and the
-    sum rounded in fp32 (no FMA contraction), then bf16
+    sum rounded in fp32 (no FMA contraction), then bf16 (fp16 with `f16`)
     (app/engine/fusedops.py:103-132; pairs (2i, 2i+1), freqs (S, D/2, 2)).
 
     x: bf16 bits (B, S, H, D); freqs: float array (S, D/2, 2) of fp32 values.
     """
-    x = bf16_to_f32(x_bits)
+    x = act_to_f32(x_bits, f16)
     b, s, h, d = x.shape
     f = np.asarray(freqs, dtype=np.float32).reshape(s, d // 2, 2)
     x0 = x[..., 0::2]
@@ -316,7 +361,7 @@ def rope(x_bits, freqs) -> np.ndarray:
     out = np.empty_like(x)
     out[..., 0::2] = y0
     out[..., 1::2] = y1
-    return f32_to_bf16(out)
+    return f32_to_act(out, f16)
 
 
 def precompute_freqs_cis(seq_len: int, n_elem: int, base: float = 1e6) -> np.ndarray:
@@ -334,7 +379,8 @@ def precompute_freqs_cis(seq_len: int, n_elem: int, base: float = 1e6) -> np.nda
     return f32_to_bf16(cache.astype(np.float32))
 
 
-def attention(q_bits, k_cache_bits, v_cache_bits, length: int, n_head: int, n_kv: int) -> np.ndarray:
+def attention(q_bits, k_cache_bits, v_cache_bits, length: int, n_head: int, n_kv: int,
+              f16: bool = False) -> np.ndarray:
     """Grouped decode attention of ONE query position over keys [0, length).
 
     Follows the fork's rounding points as `decode_attention`
@@ -344,11 +390,11 @@ def attention(q_bits, k_cache_bits, v_cache_bits, length: int, n_head: int, n_kv
     sum(p * v) rounded to bf16. Query head h reads KV head h // (n_head/n_kv).
 
     q: bf16 bits [n_head, D]; caches: bf16 bits [n_kv, max_len, D].
-    Returns bf16 bits [n_head, D].
+    Returns bf16 bits [n_head, D]. With `f16` every bf16 above is fp16.
     """
-    q = bf16_to_f32(q_bits).reshape(n_head, -1).astype(np.float64)
-    kc = bf16_to_f32(k_cache_bits)
-    vc = bf16_to_f32(v_cache_bits)
+    q = act_to_f32(q_bits, f16).reshape(n_head, -1).astype(np.float64)
+    kc = act_to_f32(k_cache_bits, f16)
+    vc = act_to_f32(v_cache_bits, f16)
     d = q.shape[1]
     groups = n_head // n_kv
     scale = np.float32(1.0 / math.sqrt(d))
@@ -357,24 +403,25 @@ def attention(q_bits, k_cache_bits, v_cache_bits, length: int, n_head: int, n_kv
         kh = h // groups
         k = kc[kh, :length].astype(np.float64)
         v = vc[kh, :length].astype(np.float64)
-        sc = (round_bf((k @ q[h]).astype(np.float32)) * scale).astype(np.float32)
+        sc = (round_act((k @ q[h]).astype(np.float32), f16) * scale).astype(np.float32)
         mx = sc.max()
         e = np.exp((sc - mx).astype(np.float64))
-        p = round_bf((e / e.sum()).astype(np.float32)).astype(np.float64)
+        p = round_act((e / e.sum()).astype(np.float32), f16).astype(np.float64)
         out[h] = (p @ v).astype(np.float32)
-    return f32_to_bf16(out)
+    return f32_to_act(out, f16)
 
 
-def attention_masked(q_bits, k_bits, v_bits, mask, n_head: int, n_kv: int) -> np.ndarray:
+def attention_masked(q_bits, k_bits, v_bits, mask, n_head: int, n_kv: int, f16: bool = False) -> np.ndarray:
     """`attention` for S query rows under an explicit visibility mask.
 
     q: bf16 bits [n_head, S, D]; k/v: [n_kv, L, D]; mask: bool [S, L] (True =
     visible), the (B, 1, S, L) mask of app/engine/fastpath.py:152-166 without
-    its unit axes. Masked keys are never read. Returns bf16 bits [n_head, S, D].
+    its unit axes. Masked keys are never read. Returns bf16 bits [n_head, S, D]
+    (fp16 throughout with `f16`).
     """
-    q = bf16_to_f32(q_bits).astype(np.float64)
-    kc = bf16_to_f32(k_bits).astype(np.float64)
-    vc = bf16_to_f32(v_bits).astype(np.float64)
+    q = act_to_f32(q_bits, f16).astype(np.float64)
+    kc = act_to_f32(k_bits, f16).astype(np.float64)
+    vc = act_to_f32(v_bits, f16).astype(np.float64)
     nh, S, d = q.shape
     groups = n_head // n_kv
     scale = np.float32(1.0 / math.sqrt(d))
@@ -387,11 +434,11 @@ def attention_masked(q_bits, k_bits, v_bits, mask, n_head: int, n_kv: int) -> np
             if vis.size == 0:
                 out[h, s] = np.nan
                 continue
-            sc = (round_bf((kc[kh, vis] @ q[h, s]).astype(np.float32)) * scale).astype(np.float32)
+            sc = (round_act((kc[kh, vis] @ q[h, s]).astype(np.float32), f16) * scale).astype(np.float32)
             e = np.exp((sc - sc.max()).astype(np.float64))
-            p = round_bf((e / e.sum()).astype(np.float32)).astype(np.float64)
+            p = round_act((e / e.sum()).astype(np.float32), f16).astype(np.float64)
             out[h, s] = (p @ vc[kh, vis]).astype(np.float32)
-    return f32_to_bf16(out)
+    return f32_to_act(out, f16)
 
 
 # --------------------------------------------------------------------------
@@ -401,7 +448,7 @@ def attention_masked(q_bits, k_bits, v_bits, mask, n_head: int, n_kv: int) -> np
 
 def decode_block(x_bits, weights: dict, k_cache_bits, v_cache_bits, pos: int, freqs_row,
                  n_head: int, n_kv: int, head_dim: int, eps: float, qk_eps: float | None,
-                 length: int | None = None):
+                 length: int | None = None, f16: bool = False):
     """`TransformerBlock.forward` for one position with the fork's rounding
     points, in the order of app/engine/fusedlayer.py:212-269 and
     app/engine/nf4cpu.py:479-617:
@@ -412,29 +459,30 @@ def decode_block(x_bits, weights: dict, k_cache_bits, v_cache_bits, pos: int, fr
 
     `weights` holds dequantised bf16 bits for "wqkv", "wo", "w1", "w3", "w2",
     norm weights "attn_norm", "ffn_norm" and optional "q_norm", "k_norm".
-    Caches are modified in place. Returns bf16 bits of the block output.
+    Caches are modified in place. Returns bf16 bits of the block output; with
+    `f16` every bf16 here (weights, norms, caches, output) is fp16.
     """
     length = pos + 1 if length is None else length
     qs, kvs = n_head * head_dim, n_kv * head_dim
-    xn = rms_norm(x_bits.reshape(1, -1), weights["attn_norm"], eps)
-    qkv = bf16_to_f32(matmul_dequant(xn, weights["wqkv"]))[0]
+    xn = rms_norm(x_bits.reshape(1, -1), weights["attn_norm"], eps, f16)
+    qkv = act_to_f32(matmul_dequant(xn, weights["wqkv"], f16=f16), f16)[0]
     q = qkv[:qs].reshape(n_head, head_dim)
     k = qkv[qs:qs + kvs].reshape(n_kv, head_dim)
     v = qkv[qs + kvs:].reshape(n_kv, head_dim)
     if weights.get("q_norm") is not None:
-        q = head_rms_norm(q, weights["q_norm"], qk_eps)
-        k = head_rms_norm(k, weights["k_norm"], qk_eps)
+        q = head_rms_norm(q, weights["q_norm"], qk_eps, f16)
+        k = head_rms_norm(k, weights["k_norm"], qk_eps, f16)
     f = np.asarray(freqs_row, dtype=np.float32).reshape(1, head_dim // 2, 2)
-    qr = rope(f32_to_bf16(q).reshape(1, 1, n_head, head_dim), f).reshape(n_head, head_dim)
-    kr = rope(f32_to_bf16(k).reshape(1, 1, n_kv, head_dim), f).reshape(n_kv, head_dim)
+    qr = rope(f32_to_act(q, f16).reshape(1, 1, n_head, head_dim), f, f16).reshape(n_head, head_dim)
+    kr = rope(f32_to_act(k, f16).reshape(1, 1, n_kv, head_dim), f, f16).reshape(n_kv, head_dim)
     k_cache_bits[:, pos] = kr
-    v_cache_bits[:, pos] = f32_to_bf16(v)
-    att = attention(qr, k_cache_bits, v_cache_bits, length, n_head, n_kv).reshape(1, qs)
-    h = matmul_dequant(att, weights["wo"], EPI_RESIDUAL, x_bits.reshape(1, -1))
-    hn = rms_norm(h, weights["ffn_norm"], eps)
-    g1 = matmul_dequant(hn, weights["w1"])
-    g = matmul_dequant(hn, weights["w3"], EPI_SILU_GATE, g1)
-    return matmul_dequant(g, weights["w2"], EPI_RESIDUAL, h)
+    v_cache_bits[:, pos] = f32_to_act(v, f16)
+    att = attention(qr, k_cache_bits, v_cache_bits, length, n_head, n_kv, f16).reshape(1, qs)
+    h = matmul_dequant(att, weights["wo"], EPI_RESIDUAL, x_bits.reshape(1, -1), f16)
+    hn = rms_norm(h, weights["ffn_norm"], eps, f16)
+    g1 = matmul_dequant(hn, weights["w1"], f16=f16)
+    g = matmul_dequant(hn, weights["w3"], EPI_SILU_GATE, g1, f16)
+    return matmul_dequant(g, weights["w2"], EPI_RESIDUAL, h, f16)
 
 
 # --------------------------------------------------------------------------

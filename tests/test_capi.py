@@ -109,3 +109,24 @@ def test_other_entry_points_reject_bad_arguments():
     assert L.nf4b_decode_attention(p, p, p, p, None, p, 32, 8, 128, 16, 32, p, 1 << 20, None) == -2
     assert L.nf4b_decode_attention(p, p, p, p, None, p, 32, 8, 128, 16, 16, p, 16, None) == -5
     assert L.nf4b_dequantize(None, p, None) == -1
+
+
+def test_activation_dtypes_are_checked_on_the_host():
+    """bf16 (0 or NF4B_BF16) and fp16 (NF4B_F16) are the activation types;
+    anything else is NF4B_ERR_DTYPE before any device work."""
+    w, _keep = _weight()
+    L = _lib.lib()
+    buf = ctypes.create_string_buffer(4096 + 16)
+    p = (ctypes.addressof(buf) + 15) // 16 * 16
+    opts = _lib.GemmOpts(None, None, None, 0.0, 3)    # 0 (zeroed options) means bf16
+    assert L.nf4b_gemm_ex(ctypes.byref(w), p, p, 1, 0, None, None, 0, ctypes.byref(opts), None) == -4
+    opts.dtype = 9
+    assert L.nf4b_gemm_ex(ctypes.byref(w), p, p, 1, 0, None, None, 0, ctypes.byref(opts), None) == -4
+    assert L.nf4b_rms_norm_ex(p, p, p, 1, 8, 1e-6, _lib.NF4B_F32, None) == -4
+    assert L.nf4b_rope_ex(p, p, 0, p, 1, 1, 1, 8, 3, None) == -4
+    assert L.nf4b_qk_rope_kv_ex(p, None, None, 1e-6, p, 2, p, p, p, p, 32, 8, 128, 16, 0, None) == -4
+    assert L.nf4b_decode_attention_ex(p, p, p, p, None, p, 32, 8, 128, 16, 16, p, 1 << 20, -1, None) == -4
+    assert L.nf4b_qkv_attention_ex(p, None, None, 1e-6, p, 2, p, p, p, p, p, 32, 8, 128, 16, 16, p, 1 << 20, 0,
+                                   None) == -4
+    # the argument checks still come first for a valid dtype
+    assert L.nf4b_rms_norm_ex(None, p, p, 1, 8, 1e-6, _lib.NF4B_F16, None) == -1

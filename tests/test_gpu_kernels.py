@@ -197,7 +197,7 @@ def test_declines_are_counted_and_do_not_launch():
     assert nf4gemv.matmul(layer, randn_bf16((1, 2560), seed=1, device="cuda")) is None
     good = make_linear(256, 2560, seed=2)
     assert nf4gemv.prepare(good)
-    assert nf4gemv.matmul(good, randn_bf16((1, 2560), seed=1, device="cuda").half()) is None
+    assert nf4gemv.matmul(good, randn_bf16((1, 2560), seed=1, device="cuda").float()) is None   # fp32 x
     assert nf4gemv.matmul(good, randn_bf16((1, 2048), seed=1, device="cuda")) is None
 
 

@@ -22,6 +22,14 @@ NF4B_ERR_WORKSPACE, NF4B_ERR_LAUNCH, NF4B_ERR_DEVICE = -5, -6, -7
 NF4B_EPI_NONE, NF4B_EPI_RESIDUAL, NF4B_EPI_SILU_GATE = 0, 1, 2
 NF4B_F32, NF4B_F16, NF4B_BF16 = 0, 1, 2
 
+
+def act_type(dtype):
+    """The library's activation-type code of a torch dtype: NF4B_BF16 for
+    bfloat16, NF4B_F16 for float16, None for anything else."""
+    import torch
+
+    return {torch.bfloat16: NF4B_BF16, torch.float16: NF4B_F16}.get(dtype)
+
 #: Every symbol the header declares; the CPU tests check the library exports all of them.
 EXPORTS = (
     "nf4b_version",
@@ -51,6 +59,11 @@ EXPORTS = (
     "nf4b_decode_step",
     "nf4b_decode_step_workspace_size",
     "nf4b_debug_decode_step",
+    "nf4b_rms_norm_ex",
+    "nf4b_rope_ex",
+    "nf4b_qk_rope_kv_ex",
+    "nf4b_decode_attention_ex",
+    "nf4b_qkv_attention_ex",
 )
 
 
@@ -90,7 +103,7 @@ class GemmOpts(ctypes.Structure):
     """`nf4b_gemm_opts`."""
 
     _fields_ = [("prefetch_next", ctypes.POINTER(Nf4Weight)), ("prefetch_next2", ctypes.POINTER(Nf4Weight)),
-                ("norm_weight", ctypes.c_void_p), ("norm_eps", ctypes.c_float)]
+                ("norm_weight", ctypes.c_void_p), ("norm_eps", ctypes.c_float), ("dtype", ctypes.c_int)]
 
 
 class RopeKv(ctypes.Structure):
@@ -146,6 +159,12 @@ def _declare(lib) -> None:
         "nf4b_decode_attention_workspace_size": (sz, [i32, i32, i32]),
         "nf4b_qkv_attention": (i32, [vp, vp, vp, f32, vp, i32, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, sz,
                                      vp]),
+        "nf4b_rms_norm_ex": (i32, [vp, vp, vp, i32, i32, f32, i32, vp]),
+        "nf4b_rope_ex": (i32, [vp, vp, i32, vp, i32, i32, i32, i32, i32, vp]),
+        "nf4b_qk_rope_kv_ex": (i32, [vp, vp, vp, f32, vp, i32, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+        "nf4b_decode_attention_ex": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, sz, i32, vp]),
+        "nf4b_qkv_attention_ex": (i32, [vp, vp, vp, f32, vp, i32, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp,
+                                        sz, i32, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -168,6 +168,27 @@ int current_sm_count() {
   return gemv_sm_count(dev);
 }
 
+// The activation type named by the options: 0 / NF4B_BF16 = bf16 (the
+// default of zeroed options), NF4B_F16 = fp16. Returns the status.
+int act_type(const nf4b_gemm_opts* opts, bool* f16) {
+  *f16 = false;
+  if (opts == nullptr || opts->dtype == 0 || opts->dtype == NF4B_BF16) return NF4B_OK;
+  if (opts->dtype != NF4B_F16) return fail(NF4B_ERR_DTYPE, "unknown activation dtype %d", opts->dtype);
+  *f16 = true;
+  return NF4B_OK;
+}
+
+// Whether the register-fed pair GEMV serves this weight (pair) at `rows`:
+// blocksize-64 units of 256 codes with their scale data in one aligned copy,
+// 32-byte aligned packed codes, 1..2 rows.
+bool reg_eligible(const nf4b_weight* w, const nf4b_weight* w3, int rows) {
+  auto one = [&](const nf4b_weight* v) {
+    return use_pairs(v, rows) && pair_su(v, rows) == 2 && aligned(v->packed, 32) &&
+           (long long)v->n_out * (v->k_in / 64) < (1LL << 31);
+  };
+  return rows >= 1 && rows <= 2 && one(w) && (w3 == nullptr || one(w3));
+}
+
 // One GEMV launch (rows <= GEMV_MAX_ROWS): plain, or the gated pair (w, w3)
 // of the pair kernel. Arguments already checked by the caller except the
 // workspace and the GEMV-specific limits.
@@ -204,10 +225,14 @@ int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* 
   p.gated = gated ? 1 : 0;
   p.su = su;
   // The register-fed pair kernel reads 32-byte pieces of the packed weights.
-  p.reg = (pairs && su == 2 && rows <= 2 && aligned(w->packed, 32) && (!gated || aligned(w3->packed, 32)) &&
-           (long long)w->n_out * (w->k_in / 64) < (1LL << 31))
-              ? 1
-              : 0;
+  p.reg = (pairs && su == 2 && reg_eligible(w, w3, rows)) ? 1 : 0;
+  bool f16 = false;
+  int st = act_type(opts, &f16);
+  if (st) return st;
+  if (f16 && (!p.reg || rk != nullptr))
+    return fail(NF4B_ERR_SHAPE, "fp16 is served here on the register-fed decode GEMV only (1..2 rows, blocksize 64, "
+                                "k_in %% 256 == 0, 32-byte aligned packed codes)");
+  p.f16 = f16 ? 1 : 0;
   if (rk != nullptr) {
     if (!p.reg || gated || rows != 1 || epi != NF4B_EPI_NONE)
       return fail(NF4B_ERR_SHAPE, "the fused rotary store serves one row on the register-fed decode GEMV");
@@ -253,7 +278,7 @@ int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* 
 
 extern "C" {
 
-int nf4b_version(void) { return 100; }
+int nf4b_version(void) { return 200; }
 
 const char* nf4b_last_error(void) { return g_err; }
 
@@ -266,8 +291,12 @@ int nf4b_device_error(int clear) {
 
 size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows) {
   if (w == nullptr || rows <= 0 || w->n_out <= 0 || w->k_in <= 0) return 0;
-  if (rows > GEMV_MAX_ROWS) return gemm_workspace_bytes(w->n_out, rows, w->k_in, current_sm_count());
-  return gemv_workspace_bytes(w, rows, current_sm_count());
+  const int sms = current_sm_count();
+  if (rows > GEMV_MAX_ROWS) return gemm_workspace_bytes(w->n_out, rows, w->k_in, sms);
+  // 1..32 rows: the GEMV's, or the GEMM's where an fp16 call goes there
+  const size_t a = gemv_workspace_bytes(w, rows, sms);
+  const size_t b = reg_eligible(w, nullptr, rows) ? 0 : gemm_workspace_bytes(w->n_out, rows, w->k_in, sms);
+  return a > b ? a : b;
 }
 
 int nf4b_gemm(const nf4b_weight* w, const void* x, void* y, int rows, int epi, const void* operand,
@@ -288,13 +317,17 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
   if (!aligned(x, 16)) return fail(NF4B_ERR_ALIGN, "x is not 16-byte aligned");
   if (!aligned(y, 2) || (operand && !aligned(operand, 2)))
     return fail(NF4B_ERR_ALIGN, "y/operand not 2-byte aligned");
+  bool f16 = false;
+  if ((st = act_type(opts, &f16))) return st;
   if ((st = check_device())) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
-  if (rows <= GEMV_MAX_ROWS)
+  // fp16: the register-fed GEMV for 1..2 rows where it applies, else the GEMM
+  // at any row count (the bf16-only GEMV kernels are not instantiated in fp16).
+  if (f16 ? reg_eligible(w, nullptr, rows) : rows <= GEMV_MAX_ROWS)
     return gemv_call(w, nullptr, x, y, rows, epi, operand, workspace, workspace_bytes, opts, s);
   if (opts != nullptr && opts->norm_weight != nullptr)
-    return fail(NF4B_ERR_SHAPE, "a fused RMSNorm is served for 1..4 rows (got %d)", rows);
+    return fail(NF4B_ERR_SHAPE, "a fused RMSNorm is served for 1..4 rows (fp16: 1..2 rows) (got %d)", rows);
 
   GemmParams p = {};
   p.packed = w->packed;
@@ -312,6 +345,7 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
   p.operand = static_cast<const uint16_t*>(operand);
   p.M = rows;
   p.epi = epi;
+  p.f16 = f16 ? 1 : 0;
   // split-K when the caller's workspace holds the partial sums (else one pass)
   const int sms = current_sm_count();
   p.bt = gemm_bt(w->n_out, rows, sms);
@@ -702,8 +736,28 @@ extern "C" int nf4b_dequantize(const nf4b_weight* w, void* out, void* stream) {
   return launch_status(launch_dequant(p, reinterpret_cast<cudaStream_t>(stream)), "nf4 dequantize launch");
 }
 
-int nf4b_rms_norm(const void* x, const void* weight, void* y, int rows, int width, float eps,
-                  void* stream) {
+}  // extern "C"
+
+namespace {
+// The activation type argument of the elementwise _ex calls: NF4B_BF16 or NF4B_F16.
+int elem_type(int dtype, bool* f16) {
+  *f16 = dtype == NF4B_F16;
+  if (dtype != NF4B_BF16 && dtype != NF4B_F16)
+    return fail(NF4B_ERR_DTYPE, "activation dtype %d is not served (NF4B_BF16 or NF4B_F16)", dtype);
+  return NF4B_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int nf4b_rms_norm(const void* x, const void* weight, void* y, int rows, int width, float eps, void* stream) {
+  return nf4b_rms_norm_ex(x, weight, y, rows, width, eps, NF4B_BF16, stream);
+}
+
+int nf4b_rms_norm_ex(const void* x, const void* weight, void* y, int rows, int width, float eps, int dtype,
+                     void* stream) {
+  bool f16 = false;
+  if (int e = elem_type(dtype, &f16)) return e;
   if (x == nullptr || weight == nullptr || y == nullptr) return fail(NF4B_ERR_ARG, "null pointer");
   if (rows <= 0 || width <= 0) return fail(NF4B_ERR_SHAPE, "empty input %dx%d", rows, width);
   if (!(eps >= 0.f)) return fail(NF4B_ERR_ARG, "eps must be >= 0");
@@ -712,12 +766,19 @@ int nf4b_rms_norm(const void* x, const void* weight, void* y, int rows, int widt
   return launch_status(
       launch_rms_norm(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(weight),
                       static_cast<uint16_t*>(y), rows, width, eps,
-                      reinterpret_cast<cudaStream_t>(stream)),
+                      reinterpret_cast<cudaStream_t>(stream), f16),
       "rms_norm launch");
 }
 
 int nf4b_rope(const void* x, const void* freqs, int freqs_dtype, void* y, int batch, int seq,
               int heads, int head_dim, void* stream) {
+  return nf4b_rope_ex(x, freqs, freqs_dtype, y, batch, seq, heads, head_dim, NF4B_BF16, stream);
+}
+
+int nf4b_rope_ex(const void* x, const void* freqs, int freqs_dtype, void* y, int batch, int seq,
+                 int heads, int head_dim, int dtype, void* stream) {
+  bool f16 = false;
+  if (int e = elem_type(dtype, &f16)) return e;
   if (x == nullptr || freqs == nullptr || y == nullptr) return fail(NF4B_ERR_ARG, "null pointer");
   if (batch <= 0 || seq <= 0 || heads <= 0 || head_dim <= 0 || head_dim % 2)
     return fail(NF4B_ERR_SHAPE, "bad rotary shape (%d,%d,%d,%d)", batch, seq, heads, head_dim);
@@ -728,7 +789,7 @@ int nf4b_rope(const void* x, const void* freqs, int freqs_dtype, void* y, int ba
   const long long pairs = (long long)batch * seq * heads * head_dim / 2;
   return launch_status(launch_rope(static_cast<const uint16_t*>(x), freqs, freqs_dtype,
                                    static_cast<uint16_t*>(y), pairs, head_dim / 2, heads, seq,
-                                   reinterpret_cast<cudaStream_t>(stream)),
+                                   reinterpret_cast<cudaStream_t>(stream), f16),
                        "rope launch");
 }
 
@@ -736,6 +797,16 @@ int nf4b_qk_rope_kv(const void* qkv, const void* q_norm_w, const void* k_norm_w,
                     const void* freqs, int freqs_dtype, const int64_t* pos, void* q_out,
                     void* k_cache, void* v_cache, int n_head, int n_kv, int head_dim, int max_len,
                     void* stream) {
+  return nf4b_qk_rope_kv_ex(qkv, q_norm_w, k_norm_w, eps, freqs, freqs_dtype, pos, q_out, k_cache, v_cache, n_head,
+                            n_kv, head_dim, max_len, NF4B_BF16, stream);
+}
+
+int nf4b_qk_rope_kv_ex(const void* qkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                       const void* freqs, int freqs_dtype, const int64_t* pos, void* q_out,
+                       void* k_cache, void* v_cache, int n_head, int n_kv, int head_dim, int max_len,
+                       int dtype, void* stream) {
+  bool f16 = false;
+  if (int e = elem_type(dtype, &f16)) return e;
   if (!qkv || !freqs || !pos || !q_out || !k_cache || !v_cache)
     return fail(NF4B_ERR_ARG, "null pointer");
   if (head_dim != 128) return fail(NF4B_ERR_SHAPE, "head_dim must be 128 (got %d)", head_dim);
@@ -751,7 +822,7 @@ int nf4b_qk_rope_kv(const void* qkv, const void* q_norm_w, const void* k_norm_w,
                         static_cast<const uint16_t*>(k_norm_w), eps, freqs, freqs_dtype, pos,
                         static_cast<uint16_t*>(q_out), static_cast<uint16_t*>(k_cache),
                         static_cast<uint16_t*>(v_cache), n_head, n_kv, max_len,
-                        reinterpret_cast<cudaStream_t>(stream)),
+                        reinterpret_cast<cudaStream_t>(stream), f16),
       "qk_rope_kv launch");
 }
 
@@ -766,6 +837,16 @@ int nf4b_decode_attention(const void* q, const void* k_cache, const void* v_cach
                           const int64_t* pos, const uint8_t* mask, void* out, int n_head, int n_kv,
                           int head_dim, int max_len, int window, void* workspace,
                           size_t workspace_bytes, void* stream) {
+  return nf4b_decode_attention_ex(q, k_cache, v_cache, pos, mask, out, n_head, n_kv, head_dim, max_len, window,
+                                  workspace, workspace_bytes, NF4B_BF16, stream);
+}
+
+int nf4b_decode_attention_ex(const void* q, const void* k_cache, const void* v_cache,
+                             const int64_t* pos, const uint8_t* mask, void* out, int n_head, int n_kv,
+                             int head_dim, int max_len, int window, void* workspace,
+                             size_t workspace_bytes, int dtype, void* stream) {
+  bool f16 = false;
+  if (int e = elem_type(dtype, &f16)) return e;
   if (!q || !k_cache || !v_cache || !out) return fail(NF4B_ERR_ARG, "null pointer");
   if (head_dim != 128) return fail(NF4B_ERR_SHAPE, "head_dim must be 128 (got %d)", head_dim);
   if (n_head <= 0 || n_kv <= 0 || n_head % n_kv)
@@ -791,7 +872,7 @@ int nf4b_decode_attention(const void* q, const void* k_cache, const void* v_cach
       launch_decode_attention(static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k_cache),
                               static_cast<const uint16_t*>(v_cache), pos, mask, static_cast<uint16_t*>(out),
                               n_head, n_kv, max_len, window, partial, static_cast<int*>(workspace),
-                              reinterpret_cast<cudaStream_t>(stream)),
+                              reinterpret_cast<cudaStream_t>(stream), f16),
       "decode attention launch");
 }
 
@@ -799,6 +880,18 @@ int nf4b_qkv_attention(const void* qkv, const void* q_norm_w, const void* k_norm
                        const void* freqs, int freqs_dtype, const int64_t* pos, void* q_scratch,
                        void* k_cache, void* v_cache, void* out, int n_head, int n_kv, int head_dim, int max_len,
                        int window, void* workspace, size_t workspace_bytes, void* stream) {
+  return nf4b_qkv_attention_ex(qkv, q_norm_w, k_norm_w, eps, freqs, freqs_dtype, pos, q_scratch, k_cache, v_cache,
+                               out, n_head, n_kv, head_dim, max_len, window, workspace, workspace_bytes, NF4B_BF16,
+                               stream);
+}
+
+int nf4b_qkv_attention_ex(const void* qkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                          const void* freqs, int freqs_dtype, const int64_t* pos, void* q_scratch,
+                          void* k_cache, void* v_cache, void* out, int n_head, int n_kv, int head_dim,
+                          int max_len, int window, void* workspace, size_t workspace_bytes, int dtype,
+                          void* stream) {
+  bool f16 = false;
+  if (int e = elem_type(dtype, &f16)) return e;
   if (!qkv || !freqs || !pos || !q_scratch || !k_cache || !v_cache || !out) return fail(NF4B_ERR_ARG, "null pointer");
   if (head_dim != 128) return fail(NF4B_ERR_SHAPE, "head_dim must be 128 (got %d)", head_dim);
   if (n_head <= 0 || n_kv <= 0 || n_head % n_kv)
@@ -835,7 +928,8 @@ int nf4b_qkv_attention(const void* qkv, const void* q_norm_w, const void* k_norm
   return launch_status(
       launch_qkv_attention(in, pos, static_cast<uint16_t*>(q_scratch), static_cast<uint16_t*>(k_cache),
                            static_cast<uint16_t*>(v_cache), static_cast<uint16_t*>(out), n_head, n_kv, max_len,
-                           window, partial, static_cast<int*>(workspace), reinterpret_cast<cudaStream_t>(stream)),
+                           window, partial, static_cast<int*>(workspace), reinterpret_cast<cudaStream_t>(stream),
+                           f16),
       "qkv attention launch");
 }
 

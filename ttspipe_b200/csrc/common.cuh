@@ -29,11 +29,59 @@ __device__ __forceinline__ bf16_t f2bf(float f) {
 
 __device__ __forceinline__ float round_bf(float f) { return bf2f(f2bf(f)); }
 
+// fp16 (binary16) bit patterns, for the fp16 activations the reference serves
+// by default: widening is exact, narrowing rounds to nearest even (cvt.rn),
+// overflow goes to infinity as in torch.
+__device__ __forceinline__ float h2f(uint16_t h) {
+  float f;
+  asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
+  return f;
+}
+__device__ __forceinline__ uint16_t f2h(float f) {
+  uint16_t h;
+  asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(f));
+  return h;
+}
+
+// The activation type of a kernel instantiation: bf16 (F16 = false) or fp16.
+template <bool F16>
+__device__ __forceinline__ float act2f(uint16_t v) {
+  return F16 ? h2f(v) : bf2f(v);
+}
+template <bool F16>
+__device__ __forceinline__ uint16_t f2act(float f) {
+  return F16 ? f2h(f) : f2bf(f);
+}
+template <bool F16>
+__device__ __forceinline__ float round_act(float f) {
+  return act2f<F16>(f2act<F16>(f));
+}
+
+// The low / high 16-bit value of a packed pair of the activation type, widened
+// (exact). For bf16 a shift or a mask is the whole conversion.
+template <bool F16>
+__device__ __forceinline__ float act_lo(uint32_t w) {
+  return F16 ? h2f((uint16_t)(w & 0xFFFFu)) : __uint_as_float(w << 16);
+}
+template <bool F16>
+__device__ __forceinline__ float act_hi(uint32_t w) {
+  return F16 ? h2f((uint16_t)(w >> 16)) : __uint_as_float(w & 0xFFFF0000u);
+}
+
 // Two fp32 -> one bf16x2 register, `lo` in the low half (lower address).
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+template <bool F16>
+__device__ __forceinline__ uint32_t pack_act2(float lo, float hi) {
+  return F16 ? pack_f16x2(lo, hi) : pack_bf16x2(lo, hi);
 }
 
 // Streaming read of data used once (packed weights): no L1 allocation, and a
@@ -81,11 +129,12 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return r;
 }
 
+template <bool F16 = false>
 __device__ __forceinline__ ScaledLut scaled_lut(float scale) {
   uint32_t pair[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
-    pair[i] = pack_bf16x2(__fmul_rn(c_nf4_code[2 * i], scale), __fmul_rn(c_nf4_code[2 * i + 1], scale));
+    pair[i] = pack_act2<F16>(__fmul_rn(c_nf4_code[2 * i], scale), __fmul_rn(c_nf4_code[2 * i + 1], scale));
   ScaledLut t;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -137,7 +186,7 @@ __device__ __forceinline__ float rsqrt_exact(double ss, int width, float eps) {
 // thread of the CTA after a barrier that made x visible; ends with a barrier.
 // `red` holds one double per warp. kPadded: row m starts at element
 // m * row_stride and every 64 elements are followed by 8 elements of padding.
-template <int THREADS, bool kPadded = false>
+template <int THREADS, bool kPadded = false, bool F16 = false>
 __device__ __forceinline__ void rms_normalise_staged(uint16_t* xr, int M, int K, const uint16_t* __restrict__ w,
                                                      float eps, double* red, int row_stride = 0) {
   constexpr int NW = THREADS / 32;
@@ -147,7 +196,7 @@ __device__ __forceinline__ void rms_normalise_staged(uint16_t* xr, int M, int K,
   for (int m = 0; m < M; ++m) {
     double ss = 0.0;
     for (int i = threadIdx.x; i < K; i += THREADS) {
-      const double v = bf2f(at(m, i));
+      const double v = act2f<F16>(at(m, i));
       ss += v * v;
     }
 #pragma unroll
@@ -159,35 +208,30 @@ __device__ __forceinline__ void rms_normalise_staged(uint16_t* xr, int M, int K,
     for (int k = 0; k < NW; ++k) tot += red[k];
     const float r = rsqrt_exact(tot, K, eps);
     for (int i = threadIdx.x; i < K; i += THREADS) {
-      const float normed = round_bf(__fmul_rn(bf2f(at(m, i)), r));
-      at(m, i) = f2bf(__fmul_rn(normed, bf2f(__ldg(w + i))));
+      const float normed = round_act<F16>(__fmul_rn(act2f<F16>(at(m, i)), r));
+      at(m, i) = f2act<F16>(__fmul_rn(normed, act2f<F16>(__ldg(w + i))));
     }
     __syncthreads();
   }
 }
 
-// The epilogue with the operand value already loaded (ignored for NF4B_EPI_NONE).
-__device__ __forceinline__ bf16_t epilogue_value(float acc, int epi, float opv) {
-  const float y = round_bf(acc);
+// The epilogue with the operand value already loaded (ignored for NF4B_EPI_NONE),
+// at the activation type's rounding points.
+template <bool F16 = false>
+__device__ __forceinline__ uint16_t epilogue_value(float acc, int epi, float opv) {
+  const float y = round_act<F16>(acc);
   if (epi == NF4B_EPI_RESIDUAL) {
-    return f2bf(__fadd_rn(opv, y));
+    return f2act<F16>(__fadd_rn(opv, y));
   } else if (epi == NF4B_EPI_SILU_GATE) {
-    const float s = round_bf(__fdiv_rn(opv, __fadd_rn(1.0f, expf(-opv))));
-    return f2bf(__fmul_rn(s, y));
+    const float s = round_act<F16>(__fdiv_rn(opv, __fadd_rn(1.0f, expf(-opv))));
+    return f2act<F16>(__fmul_rn(s, y));
   }
-  return f2bf(y);
+  return f2act<F16>(y);
 }
 
-__device__ __forceinline__ bf16_t epilogue(float acc, int epi, const bf16_t* operand, size_t idx) {
-  const float y = round_bf(acc);
-  if (epi == NF4B_EPI_RESIDUAL) {
-    return f2bf(__fadd_rn(bf2f(operand[idx]), y));
-  } else if (epi == NF4B_EPI_SILU_GATE) {
-    const float a = bf2f(operand[idx]);
-    const float s = round_bf(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))));
-    return f2bf(__fmul_rn(s, y));
-  }
-  return f2bf(y);
+template <bool F16 = false>
+__device__ __forceinline__ uint16_t epilogue(float acc, int epi, const uint16_t* operand, size_t idx) {
+  return epilogue_value<F16>(acc, epi, epi == NF4B_EPI_NONE ? 0.f : act2f<F16>(operand[idx]));
 }
 
 }  // namespace nf4b

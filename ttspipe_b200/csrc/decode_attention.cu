@@ -1,4 +1,5 @@
-// Grouped-query decode attention for one query position over a bf16 KV cache.
+// Grouped-query decode attention for one query position over a bf16 (or, F16,
+// fp16) KV cache.
 //
 // Replaces the reference's split-K pair attn_partial + attn_combine
 // (app/engine/fusedlayer.py:95-157) with one launch. Grid (n_kv, chunks): each
@@ -11,7 +12,8 @@
 // device-side position (*pos + 1), so one captured graph serves every position
 // up to `window`; chunks past the live length exit at once.
 //
-// Scores follow the fork's rounding: bf16(q.k) * head_dim^-0.5 in fp32.
+// Scores follow the fork's rounding: act(q.k) * head_dim^-0.5 in fp32, act the
+// activation type.
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -89,7 +91,7 @@ struct AttnSmem {
   int last;
 };
 
-template <int G>
+template <int G, bool F16>
 __global__ void __launch_bounds__(kThreads) decode_attention_kernel(
     const bf16_t* __restrict__ q, const bf16_t* __restrict__ kc, const bf16_t* __restrict__ vc,
     const int64_t* __restrict__ pos_ptr, const uint8_t* __restrict__ mask, bf16_t* __restrict__ out,
@@ -130,7 +132,7 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(
                  "l"(vsrc), "r"(bytes), "r"(bar)
                  : "memory");
   }
-  for (int i = tid; i < G * kD; i += kThreads) sm.q[i / kD][i % kD] = bf2f(q[(size_t)kh * G * kD + i]);
+  for (int i = tid; i < G * kD; i += kThreads) sm.q[i / kD][i % kD] = act2f<F16>(q[(size_t)kh * G * kD + i]);
   __syncthreads();  // the barrier's initialisation is visible before anyone waits on it
   const bool ok = wait_bar0(bar);
 
@@ -151,7 +153,7 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(
         const uint32_t kw[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float ka = __uint_as_float(kw[e] << 16), kb = __uint_as_float(kw[e] & 0xFFFF0000u);
+          const float ka = act_lo<F16>(kw[e]), kb = act_hi<F16>(kw[e]);
 #pragma unroll
           for (int h = 0; h < G; ++h) {
             dot[h] = fmaf(sm.q[h][li * 16 + 2 * e], ka, dot[h]);
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(
         v += __shfl_xor_sync(0xffffffffu, v, 4);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
         v += __shfl_xor_sync(0xffffffffu, v, 1);
-        if (li == 0) sm.sc[h][jl] = vis ? __fmul_rn(round_bf(v), scale) : -INFINITY;
+        if (li == 0) sm.sc[h][jl] = vis ? __fmul_rn(round_act<F16>(v), scale) : -INFINITY;
       }
     }
   }
@@ -212,8 +214,8 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(
         const float p = sm.sc[h][jl];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          acc[h][2 * e] = fmaf(p, __uint_as_float(vw[e] << 16), acc[h][2 * e]);
-          acc[h][2 * e + 1] = fmaf(p, __uint_as_float(vw[e] & 0xFFFF0000u), acc[h][2 * e + 1]);
+          acc[h][2 * e] = fmaf(p, act_lo<F16>(vw[e]), acc[h][2 * e]);
+          acc[h][2 * e + 1] = fmaf(p, act_hi<F16>(vw[e]), acc[h][2 * e + 1]);
         }
       }
     }
@@ -264,7 +266,7 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(
       den = fmaf(__ldcg(ml + 2 * cc + 1), w, den);
       num = fmaf(__ldcg(part_acc + ((size_t)qh * chunks + cc) * kD + d), w, num);
     }
-    out[(size_t)qh * kD + d] = f2bf(num / den);
+    out[(size_t)qh * kD + d] = f2act<F16>(num / den);
   }
   pdl_launch_dependents();
 }
@@ -330,7 +332,7 @@ __device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t ran
 // null) - fp64 sum of squares, reduced exactly as block_sum over 4 warps -
 // then the rotary pair (x0 c - x1 s, x1 c + x0 s) at the freqs row when
 // `rope`. Every thread calls it (uniform barriers); `any_norm` is uniform.
-template <int G>
+template <int G, bool F16>
 __device__ __forceinline__ float norm_rope_half(ClusterSmem<G>& sm, float x, bool has_w, float wd, bool rope,
                                                 bool any_norm, float eps, float c, float sn) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -346,7 +348,7 @@ __device__ __forceinline__ float norm_rope_half(ClusterSmem<G>& sm, float x, boo
     for (int i = 0; i < 4; ++i) ss += sm.nred[4 * half + i];
     if (has_w) {
       const float r = rsqrt_exact(ss, kD, eps);
-      x = round_bf(__fmul_rn(__fmul_rn(x, r), wd));
+      x = round_act<F16>(__fmul_rn(__fmul_rn(x, r), wd));
     }
     __syncthreads();
   }
@@ -361,7 +363,7 @@ __device__ __forceinline__ float norm_rope_half(ClusterSmem<G>& sm, float x, boo
   return y;
 }
 
-template <int G>
+template <int G, bool F16>
 __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
     const bf16_t* __restrict__ q, const bf16_t* __restrict__ kc, const bf16_t* __restrict__ vc,
     const int64_t* __restrict__ pos_ptr, const uint8_t* __restrict__ mask, bf16_t* __restrict__ out,
@@ -438,7 +440,7 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
   const bool fused = in.qkv != nullptr;  // q/k/v from the wqkv output (pos given, no mask)
   const long long p_new = fused ? pos_ptr[0] : -1;
   if (!fused) {
-    for (int i = tid; i < G * kD; i += kCThreads) sm.q[i / kD][i % kD] = bf2f(q[(size_t)kh * G * kD + i]);
+    for (int i = tid; i < G * kD; i += kCThreads) sm.q[i / kD][i % kD] = act2f<F16>(q[(size_t)kh * G * kD + i]);
   } else {
     // This KV head's query heads, two per pass, then k (half 0) and v (half 1):
     // the arithmetic of qk_rope_kv. The new rows reach the cache through rank 0;
@@ -452,20 +454,20 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
 #pragma unroll
     for (int i = 0; i < P; ++i) {
       const int h = 2 * i + half;
-      xq[i] = h < G ? bf2f(qkv[(size_t)(kh * G + h) * kD + d]) : 0.f;
+      xq[i] = h < G ? act2f<F16>(qkv[(size_t)(kh * G + h) * kD + d]) : 0.f;
     }
     const int nkv = (int)gridDim.x;
-    const float xkv = bf2f(qkv[(size_t)(in.n_head + (half ? nkv : 0) + kh) * kD + d]);
+    const float xkv = act2f<F16>(qkv[(size_t)(in.n_head + (half ? nkv : 0) + kh) * kD + d]);
     const float c = load_freq(in.freqs, d & ~1, in.ftype), sn = load_freq(in.freqs, d | 1, in.ftype);
-    const float qwd = norm ? bf2f(in.qw[d]) : 0.f, kwd = norm ? bf2f(in.kw[d]) : 0.f;
+    const float qwd = norm ? act2f<F16>(in.qw[d]) : 0.f, kwd = norm ? act2f<F16>(in.kw[d]) : 0.f;
 #pragma unroll
     for (int i = 0; i < P; ++i) {
       const int h = 2 * i + half;
-      const float y = norm_rope_half<G>(sm, xq[i], norm, qwd, true, norm, in.eps, c, sn);
-      if (h < G) sm.q[h][d] = bf2f(f2bf(y));
+      const float y = norm_rope_half<G, F16>(sm, xq[i], norm, qwd, true, norm, in.eps, c, sn);
+      if (h < G) sm.q[h][d] = round_act<F16>(y);
     }
-    const float y = norm_rope_half<G>(sm, xkv, norm && half == 0, kwd, half == 0, norm, in.eps, c, sn);
-    const bf16_t nb = f2bf(y);
+    const float y = norm_rope_half<G, F16>(sm, xkv, norm && half == 0, kwd, half == 0, norm, in.eps, c, sn);
+    const bf16_t nb = f2act<F16>(y);
     (half ? sm.vnew : sm.knew)[d] = nb;
     if (rank == 0 && p_new < max_len) {
       bf16_t* cache = const_cast<bf16_t*>(half ? vc : kc);
@@ -480,8 +482,9 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
 
   const int dg = tid & 15, pg = tid >> 4;  // P.V: dimensions dg*8 .. +7, chunk rows pg*4 .. +3
   // This lane's slice of every query head for the scores (dimensions
-  // (lane & 7) * 16 .. +15), held in registers as bf16 pairs - the values are
-  // bf16 already - instead of re-reading shared memory for every key row.
+  // (lane & 7) * 16 .. +15), held in registers as pairs of the activation
+  // type - the values are of that type already - instead of re-reading shared
+  // memory for every key row.
   uint32_t qr[G][8];
   {
     const int li = lane & 7;
@@ -489,7 +492,7 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
     for (int h = 0; h < G; ++h)
 #pragma unroll
       for (int e = 0; e < 8; ++e)
-        qr[h][e] = (uint32_t)f2bf(sm.q[h][li * 16 + 2 * e]) | ((uint32_t)f2bf(sm.q[h][li * 16 + 2 * e + 1]) << 16);
+        qr[h][e] = pack_act2<F16>(sm.q[h][li * 16 + 2 * e], sm.q[h][li * 16 + 2 * e + 1]);
   }
   float acc[G][8];
 #pragma unroll
@@ -536,11 +539,11 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
           const uint32_t kw[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const float ka = __uint_as_float(kw[e] << 16), kb = __uint_as_float(kw[e] & 0xFFFF0000u);
+            const float ka = act_lo<F16>(kw[e]), kb = act_hi<F16>(kw[e]);
 #pragma unroll
             for (int h = 0; h < G; ++h) {
-              dot[h] = fmaf(__uint_as_float(qr[h][e] << 16), ka, dot[h]);
-              dot[h] = fmaf(__uint_as_float(qr[h][e] & 0xFFFF0000u), kb, dot[h]);
+              dot[h] = fmaf(act_lo<F16>(qr[h][e]), ka, dot[h]);
+              dot[h] = fmaf(act_hi<F16>(qr[h][e]), kb, dot[h]);
             }
           }
         }
@@ -550,7 +553,7 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
           v += __shfl_xor_sync(0xffffffffu, v, 4);
           v += __shfl_xor_sync(0xffffffffu, v, 2);
           v += __shfl_xor_sync(0xffffffffu, v, 1);
-          if (li == 0) sm.sc[h][jl] = vis ? __fmul_rn(round_bf(v), scale) : -INFINITY;
+          if (li == 0) sm.sc[h][jl] = vis ? __fmul_rn(round_act<F16>(v), scale) : -INFINITY;
         }
       }
     }
@@ -599,8 +602,8 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
         const float p = sm.sc[h][jl];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          acc[h][2 * e] = fmaf(p, __uint_as_float(vw[e] << 16), acc[h][2 * e]);
-          acc[h][2 * e + 1] = fmaf(p, __uint_as_float(vw[e] & 0xFFFF0000u), acc[h][2 * e + 1]);
+          acc[h][2 * e] = fmaf(p, act_lo<F16>(vw[e]), acc[h][2 * e]);
+          acc[h][2 * e + 1] = fmaf(p, act_hi<F16>(vw[e]), acc[h][2 * e + 1]);
         }
       }
     }
@@ -650,7 +653,7 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
         den = fmaf(lr[r], w, den);
         num = fmaf(ar[r], w, num);
       }
-      out[(size_t)(kh * G + h) * kD + d] = f2bf(num / den);
+      out[(size_t)(kh * G + h) * kD + d] = f2act<F16>(num / den);
     }
   }
   cluster_sync();  // partials stay alive until CTA 0 has read them
@@ -676,7 +679,7 @@ void attn_plan(int n_head, int head_dim, int window, AttnPlan* plan) {
 
 namespace {
 
-template <int G>
+template <int G, bool F16>
 cudaError_t launch_cluster_g(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int64_t* pos,
                              const uint8_t* mask, uint16_t* out, int nkv, int max_len, int window, int C,
                              bool check, const QkvIn& in, cudaStream_t stream) {
@@ -685,7 +688,7 @@ cudaError_t launch_cluster_g(const uint16_t* q, const uint16_t* kc, const uint16
   cudaGetDevice(&dev);
   const int smem = (int)sizeof(ClusterSmem<G>);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(decode_attention_cluster_kernel<G>,
+    cudaError_t e = cudaFuncSetAttribute(decode_attention_cluster_kernel<G, F16>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
@@ -708,13 +711,13 @@ cudaError_t launch_cluster_g(const uint16_t* q, const uint16_t* kc, const uint16
   cfg.numAttrs = C > 1 ? 2 : 1;
   int clusters = 1;
   if (check && C > 1 &&
-      (cudaOccupancyMaxActiveClusters(&clusters, decode_attention_cluster_kernel<G>, &cfg) != cudaSuccess ||
+      (cudaOccupancyMaxActiveClusters(&clusters, decode_attention_cluster_kernel<G, F16>, &cfg) != cudaSuccess ||
        clusters < 1)) {
     (void)cudaGetLastError();
     return cudaErrorNotSupported;
   }
   const float scale = 1.0f / sqrtf((float)kD);
-  return cudaLaunchKernelEx(&cfg, decode_attention_cluster_kernel<G>, (const bf16_t*)q, (const bf16_t*)kc,
+  return cudaLaunchKernelEx(&cfg, decode_attention_cluster_kernel<G, F16>, (const bf16_t*)q, (const bf16_t*)kc,
                             (const bf16_t*)vc, pos, mask, (bf16_t*)out, max_len, window, scale, in);
 }
 
@@ -722,7 +725,7 @@ cudaError_t launch_cluster_g(const uint16_t* q, const uint16_t* kc, const uint16
 
 cudaError_t launch_cluster_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int64_t* pos,
                                      const uint8_t* mask, uint16_t* out, int nh, int nkv, int max_len, int window,
-                                     cudaStream_t stream, const QkvIn& in) {
+                                     cudaStream_t stream, const QkvIn& in, bool f16) {
   // Clusters of 8 (the portable size; 16 measured slower at every window
   // length, 18.6 against 9.3 us at 512 rows, 24.4 against 17.1 at 2048);
   // fewer when the window has fewer 64-row chunks (a window of one chunk -
@@ -740,10 +743,22 @@ cudaError_t launch_cluster_attention(const uint16_t* q, const uint16_t* kc, cons
     const bool check = chosen[idx] == 0;
     cudaError_t e;
     switch (groups) {
-      case 1: e = launch_cluster_g<1>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream); break;
-      case 2: e = launch_cluster_g<2>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream); break;
-      case 4: e = launch_cluster_g<4>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream); break;
-      case 8: e = launch_cluster_g<8>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream); break;
+      case 1:
+        e = f16 ? launch_cluster_g<1, true>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream)
+                : launch_cluster_g<1, false>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream);
+        break;
+      case 2:
+        e = f16 ? launch_cluster_g<2, true>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream)
+                : launch_cluster_g<2, false>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream);
+        break;
+      case 4:
+        e = f16 ? launch_cluster_g<4, true>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream)
+                : launch_cluster_g<4, false>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream);
+        break;
+      case 8:
+        e = f16 ? launch_cluster_g<8, true>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream)
+                : launch_cluster_g<8, false>(q, kc, vc, pos, mask, out, nkv, max_len, window, C, check, in, stream);
+        break;
       default: return cudaErrorInvalidValue;
     }
     if (e == cudaSuccess) {
@@ -759,14 +774,14 @@ cudaError_t launch_cluster_attention(const uint16_t* q, const uint16_t* kc, cons
 cudaError_t launch_decode_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
                                     const int64_t* pos, const uint8_t* mask, uint16_t* out, int nh, int nkv,
                                     int max_len, int window, float* partial, int* counters,
-                                    cudaStream_t stream) {
+                                    cudaStream_t stream, bool f16) {
   const int groups = nh / nkv;
   const int chunks = (window + ATTN_CHUNK - 1) / ATTN_CHUNK;
   {
     // One cluster of 8 CTAs per KV head; the split-KV kernel below if the
     // device cannot make such a cluster resident.
     const QkvIn none = {};
-    cudaError_t e = launch_cluster_attention(q, kc, vc, pos, mask, out, nh, nkv, max_len, window, stream, none);
+    cudaError_t e = launch_cluster_attention(q, kc, vc, pos, mask, out, nh, nkv, max_len, window, stream, none, f16);
     if (e == cudaSuccess) return e;
     (void)cudaGetLastError();
   }
@@ -777,7 +792,7 @@ cudaError_t launch_decode_attention(const uint16_t* q, const uint16_t* kc, const
   cfg.gridDim = dim3(nkv, chunks);
   cfg.blockDim = dim3(kThreads);
   cfg.stream = stream;
-  static bool configured[4][64] = {};
+  static bool configured[2][4][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   cudaLaunchAttribute attr[1];
@@ -785,19 +800,21 @@ cudaError_t launch_decode_attention(const uint16_t* q, const uint16_t* kc, const
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-#define NF4B_ATTN_CASE(GG)                                                                      \
-  case GG:                                                                                      \
-    cfg.dynamicSmemBytes = sizeof(AttnSmem<GG>);                                                \
-    if (dev >= 0 && dev < 64 && !configured[GG == 1 ? 0 : GG == 2 ? 1 : GG == 4 ? 2 : 3][dev]) {      \
-      cudaError_t e = cudaFuncSetAttribute(decode_attention_kernel<GG>,                         \
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,         \
-                                           (int)sizeof(AttnSmem<GG>));                          \
-      if (e != cudaSuccess) return e;                                                           \
-      configured[GG == 1 ? 0 : GG == 2 ? 1 : GG == 4 ? 2 : 3][dev] = true;                      \
-    }                                                                                           \
-    return cudaLaunchKernelEx(&cfg, decode_attention_kernel<GG>, (const bf16_t*)q,             \
-                              (const bf16_t*)kc, (const bf16_t*)vc, pos, mask, (bf16_t*)out, max_len, \
-                              window, chunks, scale, part_acc, part_ml, counters);
+  const int gi = groups == 1 ? 0 : groups == 2 ? 1 : groups == 4 ? 2 : 3;
+  auto launch = [&](auto kernel, size_t smem) -> cudaError_t {
+    cfg.dynamicSmemBytes = smem;
+    if (dev >= 0 && dev < 64 && !configured[f16][gi][dev]) {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      configured[f16][gi][dev] = true;
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, (const bf16_t*)q, (const bf16_t*)kc, (const bf16_t*)vc, pos, mask,
+                              (bf16_t*)out, max_len, window, chunks, scale, part_acc, part_ml, counters);
+  };
+#define NF4B_ATTN_CASE(GG)                                                                       \
+  case GG:                                                                                       \
+    return f16 ? launch(decode_attention_kernel<GG, true>, sizeof(AttnSmem<GG>))                  \
+               : launch(decode_attention_kernel<GG, false>, sizeof(AttnSmem<GG>));
   switch (groups) {
     NF4B_ATTN_CASE(1)
     NF4B_ATTN_CASE(2)
@@ -811,15 +828,16 @@ cudaError_t launch_decode_attention(const uint16_t* q, const uint16_t* kc, const
 
 cudaError_t launch_qkv_attention(const QkvIn& in, const int64_t* pos, uint16_t* q_scratch, uint16_t* kc,
                                  uint16_t* vc, uint16_t* out, int nh, int nkv, int max_len, int window,
-                                 float* partial, int* counters, cudaStream_t stream) {
-  cudaError_t e = launch_cluster_attention(nullptr, kc, vc, pos, nullptr, out, nh, nkv, max_len, window, stream, in);
+                                 float* partial, int* counters, cudaStream_t stream, bool f16) {
+  cudaError_t e =
+      launch_cluster_attention(nullptr, kc, vc, pos, nullptr, out, nh, nkv, max_len, window, stream, in, f16);
   if (e == cudaSuccess) return e;
   (void)cudaGetLastError();
   e = launch_qk_rope_kv(in.qkv, in.qw, in.kw, in.eps, in.freqs, in.ftype, pos, q_scratch, kc, vc, nh, nkv, max_len,
-                        stream);
+                        stream, f16);
   if (e != cudaSuccess) return e;
   return launch_decode_attention(q_scratch, kc, vc, pos, nullptr, out, nh, nkv, max_len, window, partial, counters,
-                                 stream);
+                                 stream, f16);
 }
 
 }  // namespace nf4b

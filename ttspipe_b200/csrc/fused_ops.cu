@@ -2,8 +2,8 @@
 //
 // Same formulas and rounding points as the reference kernels
 // (app/engine/fusedops.py:61-132, app/engine/fusedlayer.py:56-92) with bf16
-// activations. The sum of squares is accumulated in fp64: every term is an
-// exact square of a bf16 value, so the sum is exact in any order and the norm
+// activations, or fp16 (F16) as the reference's own kernels. The sum of squares is accumulated in fp64: every term is an
+// exact square of a bf16 / fp16 value, so the sum is exact in any order and the norm
 // does not depend on the reduction tree; the reciprocal square root is the
 // correctly rounded fp32 value. Rotary is spelled with the _rn intrinsics so
 // no multiply-add is contracted: (x0*c - x1*s, x1*c + x0*s), each product and
@@ -34,6 +34,7 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
 
 constexpr int kNormThreads = 256;
 
+template <bool F16>
 __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const bf16_t* __restrict__ x,
                                                                 const bf16_t* __restrict__ w,
                                                                 bf16_t* __restrict__ y, int width,
@@ -43,18 +44,19 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const bf16_t* __
   const size_t base = (size_t)blockIdx.x * width;
   double ss = 0.0;
   for (int i = threadIdx.x; i < width; i += kNormThreads) {
-    const double v = bf2f(x[base + i]);
+    const double v = act2f<F16>(x[base + i]);
     ss += v * v;
   }
   ss = block_sum<kNormThreads>(ss, red);
   const float r = rsqrt_exact(ss, width, eps);
   for (int i = threadIdx.x; i < width; i += kNormThreads) {
-    const float normed = round_bf(__fmul_rn(bf2f(x[base + i]), r));
-    y[base + i] = f2bf(__fmul_rn(normed, bf2f(w[i])));
+    const float normed = round_act<F16>(__fmul_rn(act2f<F16>(x[base + i]), r));
+    y[base + i] = f2act<F16>(__fmul_rn(normed, act2f<F16>(w[i])));
   }
   pdl_launch_dependents();
 }
 
+template <bool F16>
 __global__ void __launch_bounds__(256) rope_kernel(const bf16_t* __restrict__ x,
                                                    const void* __restrict__ f, int ftype,
                                                    bf16_t* __restrict__ y, long long pairs,
@@ -66,9 +68,9 @@ __global__ void __launch_bounds__(256) rope_kernel(const bf16_t* __restrict__ x,
     const long long s = (i / half_dim / heads) % seq;
     const long long fi = (s * half_dim + p) * 2;
     const float c = load_freq(f, fi, ftype), sn = load_freq(f, fi + 1, ftype);
-    const float x0 = bf2f(x[2 * i]), x1 = bf2f(x[2 * i + 1]);
-    y[2 * i] = f2bf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
-    y[2 * i + 1] = f2bf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
+    const float x0 = act2f<F16>(x[2 * i]), x1 = act2f<F16>(x[2 * i + 1]);
+    y[2 * i] = f2act<F16>(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+    y[2 * i + 1] = f2act<F16>(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
   }
   pdl_launch_dependents();
 }
@@ -77,6 +79,7 @@ __global__ void __launch_bounds__(256) rope_kernel(const bf16_t* __restrict__ x,
 // heads), one thread per dimension of a 128-wide head.
 constexpr int kHeadDim = 128;
 
+template <bool F16>
 __global__ void __launch_bounds__(kHeadDim) qk_rope_kv_kernel(
     const bf16_t* __restrict__ qkv, const bf16_t* __restrict__ qw, const bf16_t* __restrict__ kw,
     float eps, const void* __restrict__ f, int ftype, const int64_t* __restrict__ pos_ptr,
@@ -94,13 +97,13 @@ __global__ void __launch_bounds__(kHeadDim) qk_rope_kv_kernel(
     return;
   }
   const bool is_q = head < nh;
-  float x = bf2f(qkv[(size_t)head * kHeadDim + d]);
+  float x = act2f<F16>(qkv[(size_t)head * kHeadDim + d]);
   const bf16_t* w = is_q ? qw : kw;
   if (w != nullptr) {
     const double sq = (double)x * (double)x;
     const double ss = block_sum<kHeadDim>(sq, red);
     const float r = rsqrt_exact(ss, kHeadDim, eps);
-    x = round_bf(__fmul_rn(__fmul_rn(x, r), bf2f(w[d])));
+    x = round_act<F16>(__fmul_rn(__fmul_rn(x, r), act2f<F16>(w[d])));
   }
   sx[d] = x;
   __syncthreads();
@@ -109,9 +112,9 @@ __global__ void __launch_bounds__(kHeadDim) qk_rope_kv_kernel(
   const float r = (d & 1) ? __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn))
                           : __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
   if (is_q)
-    q_out[(size_t)head * kHeadDim + d] = f2bf(r);
+    q_out[(size_t)head * kHeadDim + d] = f2act<F16>(r);
   else
-    kc[((size_t)(head - nh) * max_len + pos) * kHeadDim + d] = f2bf(r);
+    kc[((size_t)(head - nh) * max_len + pos) * kHeadDim + d] = f2act<F16>(r);
   pdl_launch_dependents();
 }
 
@@ -131,28 +134,30 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, void** args, cudaS
 }  // namespace
 
 cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows,
-                            int width, float eps, cudaStream_t stream) {
+                            int width, float eps, cudaStream_t stream, bool f16) {
   void* args[] = {(void*)&x, (void*)&w, (void*)&y, (void*)&width, (void*)&eps};
-  return launch_pdl((const void*)rms_norm_kernel, dim3(rows), dim3(kNormThreads), args, stream);
+  return launch_pdl(f16 ? (const void*)rms_norm_kernel<true> : (const void*)rms_norm_kernel<false>, dim3(rows),
+                    dim3(kNormThreads), args, stream);
 }
 
 cudaError_t launch_rope(const uint16_t* x, const void* freqs, int ftype, uint16_t* y,
-                        long long pairs, int half_dim, int heads, int seq, cudaStream_t stream) {
+                        long long pairs, int half_dim, int heads, int seq, cudaStream_t stream, bool f16) {
   const long long blocks = (pairs + 255) / 256;
   void* args[] = {(void*)&x, (void*)&freqs, (void*)&ftype, (void*)&y,
                   (void*)&pairs, (void*)&half_dim, (void*)&heads, (void*)&seq};
-  return launch_pdl((const void*)rope_kernel, dim3((unsigned)blocks), dim3(256), args, stream);
+  return launch_pdl(f16 ? (const void*)rope_kernel<true> : (const void*)rope_kernel<false>, dim3((unsigned)blocks),
+                    dim3(256), args, stream);
 }
 
 cudaError_t launch_qk_rope_kv(const uint16_t* qkv, const uint16_t* qw, const uint16_t* kw,
                               float eps, const void* freqs, int ftype, const int64_t* pos,
                               uint16_t* q_out, uint16_t* kc, uint16_t* vc, int nh, int nkv,
-                              int max_len, cudaStream_t stream) {
+                              int max_len, cudaStream_t stream, bool f16) {
   void* args[] = {(void*)&qkv, (void*)&qw, (void*)&kw, (void*)&eps, (void*)&freqs,
                   (void*)&ftype, (void*)&pos, (void*)&q_out, (void*)&kc, (void*)&vc,
                   (void*)&nh, (void*)&nkv, (void*)&max_len};
-  return launch_pdl((const void*)qk_rope_kv_kernel, dim3(nh + 2 * nkv), dim3(kHeadDim), args,
-                    stream);
+  return launch_pdl(f16 ? (const void*)qk_rope_kv_kernel<true> : (const void*)qk_rope_kv_kernel<false>,
+                    dim3(nh + 2 * nkv), dim3(kHeadDim), args, stream);
 }
 
 }  // namespace nf4b

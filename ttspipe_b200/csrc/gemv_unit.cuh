@@ -28,6 +28,24 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
+                                              uint32_t a2, uint32_t a3, uint32_t b0,
+                                              uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// The MMA of the activation type (both operands of one type, as kind::f16 requires).
+template <bool F16>
+__device__ __forceinline__ void mma_act(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  if (F16)
+    mma_f16_16816(d, a0, a1, a2, a3, b0, b1);
+  else
+    mma_bf16_16816(d, a0, a1, a2, a3, b0, b1);
+}
 
 
 // NF4 code point q (0..15) from immediates (a select tree): the tables below
@@ -50,8 +68,9 @@ __device__ __forceinline__ float nf4_code_imm(uint32_t q) {
 
 // The pair table with conflict-free stores: the 8 threads of a quarter warp
 // write the 8 16-byte pieces of one entry (128 contiguous bytes); the 16 code
-// values come from lanes 0..15 by shuffle. Called by whole warps.
-template <int THREADS>
+// values come from lanes 0..15 by shuffle. Called by whole warps. Entries are
+// code pairs of the activation type (F16: fp16, else bf16).
+template <int THREADS, bool F16 = false>
 __device__ __forceinline__ void build_pair_lut_fast(uint8_t* smem) {
   const float code = nf4_code_imm((uint32_t)(threadIdx.x & 15));
 #pragma unroll
@@ -59,7 +78,7 @@ __device__ __forceinline__ void build_pair_lut_fast(uint8_t* smem) {
     const int idx = threadIdx.x + r * THREADS, e = idx >> 3, c = idx & 7;
     const float hi_nib = __shfl_sync(0xffffffffu, code, e >> 4);
     const float lo_nib = __shfl_sync(0xffffffffu, code, e & 15);
-    const uint32_t v = pack_bf16x2(hi_nib, lo_nib);
+    const uint32_t v = pack_act2<F16>(hi_nib, lo_nib);
     *reinterpret_cast<uint4*>(smem + e * 256 + c * 16) = make_uint4(v, v, v, v);
   }
 }
@@ -88,10 +107,11 @@ __device__ __forceinline__ void store_code2_copies(uint8_t* smem, const float (&
 
 // The gate of a W1/W3 pair at the fork's rounding points:
 // bf16(bf16(silu(bf16(x W1))) * bf16(x W3)) (app/engine/fusedlayer.py:265-266).
+template <bool F16 = false>
 __device__ __forceinline__ uint16_t gate_bf16(float v1, float v3) {
-  const float a = round_bf(v1);
-  const float s = round_bf(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))));
-  return f2bf(__fmul_rn(s, round_bf(v3)));
+  const float a = round_act<F16>(v1);
+  const float s = round_act<F16>(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))));
+  return f2act<F16>(__fmul_rn(s, round_act<F16>(v3)));
 }
 
 

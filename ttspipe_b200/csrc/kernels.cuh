@@ -100,6 +100,7 @@ struct alignas(64) GemvParams {
   int gated;
   int su;        // pair kernel: 128-code sub-units per unit (1 or 2)
   int reg;       // su == 2, rows <= 2: the register-fed pair kernel (weights loaded straight into registers)
+  int f16;       // fp16 x, operand, y and norm weight (register-fed kernel only); else bf16
   int x_staged;  // pair kernel: x is copied whole into shared memory first
   const uint16_t* norm_w;  // pair kernel, staged x: RMS-normalise x with this weight first (or null)
   float norm_eps;
@@ -323,6 +324,7 @@ struct GemmParams {
   float* partial;
   int* counters;
   int bt;  // activation rows per tile: gemm_bt(N, M, sms)
+  int f16;  // fp16 x, operand and y; else bf16
 };
 constexpr size_t GEMM_COUNTER_BYTES = 4096;  // tile counters of a split-K launch (<= 1024 tiles)
 // Split-K factor the GEMM would use for this shape on `sms` SMs (1: none), and
@@ -333,15 +335,17 @@ size_t gemm_workspace_bytes(int N, int M, int K, int sms);
 cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream);
 
 // ---- fused elementwise (fused_ops.cu) -------------------------------------
+// f16: fp16 activations and weights (the reference's dtype); else bf16.
 
 cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows,
-                            int width, float eps, cudaStream_t stream);
+                            int width, float eps, cudaStream_t stream, bool f16 = false);
 cudaError_t launch_rope(const uint16_t* x, const void* freqs, int ftype, uint16_t* y,
-                        long long pairs, int half_dim, int heads, int seq, cudaStream_t stream);
+                        long long pairs, int half_dim, int heads, int seq, cudaStream_t stream,
+                        bool f16 = false);
 cudaError_t launch_qk_rope_kv(const uint16_t* qkv, const uint16_t* qw, const uint16_t* kw,
                               float eps, const void* freqs, int ftype, const int64_t* pos,
                               uint16_t* q_out, uint16_t* kc, uint16_t* vc, int nh, int nkv,
-                              int max_len, cudaStream_t stream);
+                              int max_len, cudaStream_t stream, bool f16 = false);
 
 // ---- decode attention (decode_attention.cu) ---------------------------------
 
@@ -358,11 +362,11 @@ void attn_plan(int n_head, int head_dim, int window, AttnPlan* plan);
 struct QkvIn;
 cudaError_t launch_cluster_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int64_t* pos,
                                      const uint8_t* mask, uint16_t* out, int nh, int nkv, int max_len, int window,
-                                     cudaStream_t stream, const QkvIn& in);
+                                     cudaStream_t stream, const QkvIn& in, bool f16 = false);
 cudaError_t launch_decode_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
                                     const int64_t* pos, const uint8_t* mask, uint16_t* out, int nh, int nkv,
                                     int max_len, int window, float* partial, int* counters,
-                                    cudaStream_t stream);
+                                    cudaStream_t stream, bool f16 = false);
 // The decode step's q/k norm + rotary + KV write (qk_rope_kv's arithmetic)
 // taken by the cluster attention kernel from the wqkv output directly.
 struct QkvIn {
@@ -378,6 +382,6 @@ struct QkvIn {
 // q_scratch then launch_decode_attention (needs partial/counters).
 cudaError_t launch_qkv_attention(const QkvIn& in, const int64_t* pos, uint16_t* q_scratch, uint16_t* kc,
                                  uint16_t* vc, uint16_t* out, int nh, int nkv, int max_len, int window,
-                                 float* partial, int* counters, cudaStream_t stream);
+                                 float* partial, int* counters, cudaStream_t stream, bool f16 = false);
 
 }  // namespace nf4b

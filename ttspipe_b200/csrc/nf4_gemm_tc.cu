@@ -187,16 +187,18 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   return d;
 }
 
-template <int BT>
+// kind::f16 instruction descriptor: A and B both bf16 (format 1) or both
+// fp16 (format 0), fp32 accumulator.
+template <int BT, bool kF16 = false>
 __host__ __device__ constexpr uint32_t instr_desc() {
   return (1u << 4)                      // D: fp32
-         | (1u << 7)                    // A: bf16
-         | (1u << 10)                   // B: bf16
+         | ((kF16 ? 0u : 1u) << 7)      // A: bf16 / fp16
+         | ((kF16 ? 0u : 1u) << 10)     // B: bf16 / fp16
          | ((uint32_t)(BT >> 3) << 17)  // N
          | ((uint32_t)(BM >> 4) << 24); // M
 }
 
-template <int BT, int DQ, bool kSplit>
+template <int BT, int DQ, bool kSplit, bool kF16 = false>
 __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
     nf4_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                        const __grid_constant__ CUtensorMap tmap_w, const GemmParams p) {
@@ -268,7 +270,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc<BT>();
+      constexpr uint32_t idesc = instr_desc<BT, kF16>();
       bool ok = true;
       for (int i = 0; i < nkb && ok; ++i) {
         const int s = i % STAGES;
@@ -338,7 +340,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
       const uint4 u0 = hfirst ? ub : ua, u1 = hfirst ? ua : ub;
       const uint32_t words[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
       uint8_t* arow = sm.a[s] + (r >> 3) * 1024 + rsw * 128;
-      const ScaledLut lut = scaled_lut(scale);
+      const ScaledLut lut = scaled_lut<kF16>(scale);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint32_t o[4];
@@ -376,7 +378,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
             const int tok = tok0 + cb * 32 + i;
             if (tok < p.M) {
               const size_t o = (size_t)tok * p.N + n;
-              p.y[o] = epilogue(__uint_as_float(v[i]), p.epi, p.operand, o);
+              p.y[o] = epilogue<kF16>(__uint_as_float(v[i]), p.epi, p.operand, o);
             }
           }
         } else if (n < p.N) {
@@ -444,15 +446,15 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
       }
 #pragma unroll
       for (int e = 0; e < 4; ++e)
-        if (live[e]) p.y[o[e]] = epilogue(acc[e], p.epi, p.operand, o[e]);
+        if (live[e]) p.y[o[e]] = epilogue<kF16>(acc[e], p.epi, p.operand, o[e]);
     }
   }
 }
 
-template <int BT, bool kSplit>
+template <int BT, bool kSplit, bool kF16 = false>
 cudaError_t launch_bt(const GemmParams& p, cudaStream_t stream) {
   CUtensorMap mx, mw;
-  if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.x, (uint64_t)p.K, (uint64_t)p.M,
+  if (!make_map_2d(&mx, kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.x, (uint64_t)p.K, (uint64_t)p.M,
                    (uint64_t)p.K * 2, BK, BT, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   if (!make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.packed, (uint64_t)p.K / 2, (uint64_t)p.N,
@@ -463,7 +465,7 @@ cudaError_t launch_bt(const GemmParams& p, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(nf4_gemm_tc_kernel<BT, kDequantGroups, kSplit>,
+    cudaError_t e = cudaFuncSetAttribute(nf4_gemm_tc_kernel<BT, kDequantGroups, kSplit, kF16>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
@@ -478,7 +480,7 @@ cudaError_t launch_bt(const GemmParams& p, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, nf4_gemm_tc_kernel<BT, kDequantGroups, kSplit>, mx, mw, p);
+  return cudaLaunchKernelEx(&cfg, nf4_gemm_tc_kernel<BT, kDequantGroups, kSplit, kF16>, mx, mw, p);
 }
 
 }  // namespace
@@ -549,11 +551,17 @@ size_t gemm_workspace_bytes(int N, int M, int K, int sms) {
   return s > 1 ? GEMM_COUNTER_BYTES + (size_t)s * M * N * sizeof(float) : 0;
 }
 
-cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream) {
+template <bool kF16>
+static cudaError_t launch_gemm_act(const GemmParams& p, cudaStream_t stream) {
   const int bt = p.bt;
-  if (bt == 64) return p.splits > 1 ? launch_bt<64, true>(p, stream) : launch_bt<64, false>(p, stream);
-  if (bt == 128) return launch_bt<128, false>(p, stream);
-  return launch_bt<256, false>(p, stream);
+  if (bt == 64)
+    return p.splits > 1 ? launch_bt<64, true, kF16>(p, stream) : launch_bt<64, false, kF16>(p, stream);
+  if (bt == 128) return launch_bt<128, false, kF16>(p, stream);
+  return launch_bt<256, false, kF16>(p, stream);
+}
+
+cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream) {
+  return p.f16 ? launch_gemm_act<true>(p, stream) : launch_gemm_act<false>(p, stream);
 }
 
 int read_device_error(int clear) {

@@ -341,7 +341,7 @@ __device__ __forceinline__ void rope_kv_rows(const GemvParams& p, const RopeKv& 
 // Store the outputs of row tile `rt` (rows g, g + 8 of activation row t):
 // the gate of the two halves for a gated pair, else the epilogue of half 0
 // (and, given `rk`, the fused rotary + KV-cache write).
-template <bool kGated>
+template <bool kGated, bool kF16 = false>
 __device__ __forceinline__ void store_pair_tile(const GemvParams& p, int rt, int g, int t,
                                                 const float (&v)[2][2], const RopeKv* rk = nullptr) {
   const int N = p.N;
@@ -349,16 +349,16 @@ __device__ __forceinline__ void store_pair_tile(const GemvParams& p, int rt, int
   if (t >= p.M) return;
   const size_t oa = (size_t)t * N + ra, ob = (size_t)t * N + rb;
   if (kGated) {
-    if (ra < N) p.y[oa] = gate_bf16(v[0][0], v[1][0]);
-    if (rb < N) p.y[ob] = gate_bf16(v[0][1], v[1][1]);
-  } else if (rk != nullptr) {  // one activation row, n_out % 16 == 0
+    if (ra < N) p.y[oa] = gate_bf16<kF16>(v[0][0], v[1][0]);
+    if (rb < N) p.y[ob] = gate_bf16<kF16>(v[0][1], v[1][1]);
+  } else if (rk != nullptr) {  // one activation row, n_out % 16 == 0 (bf16 only)
     const bf16_t ya = epilogue(v[0][0], p.epi, p.operand, oa), yb = epilogue(v[0][1], p.epi, p.operand, ob);
     p.y[oa] = ya;
     p.y[ob] = yb;
     rope_kv_rows(p, *rk, ra, rb, ya, yb);
   } else {
-    if (ra < N) p.y[oa] = epilogue(v[0][0], p.epi, p.operand, oa);
-    if (rb < N) p.y[ob] = epilogue(v[0][1], p.epi, p.operand, ob);
+    if (ra < N) p.y[oa] = epilogue<kF16>(v[0][0], p.epi, p.operand, oa);
+    if (rb < N) p.y[ob] = epilogue<kF16>(v[0][1], p.epi, p.operand, ob);
   }
 }
 
@@ -371,7 +371,7 @@ __device__ __forceinline__ void store_pair_tile(const GemvParams& p, int rt, int
 // by finish_split_tile: no warp waits for another, and the last to arrive
 // reduces (returns true). (Publishing every split tile only after the run was
 // measured slower: the first tile's reduction then no longer overlaps the run.)
-template <bool kGated>
+template <bool kGated, bool kF16 = false>
 __device__ __forceinline__ bool publish_pair_tile(const GemvParams& p, int rt, int u0, int u1, int gw, int g,
                                                   int t, int lane, const float (&v)[2][2], int& old,
                                                   const RopeKv* rk = nullptr) {
@@ -379,7 +379,7 @@ __device__ __forceinline__ bool publish_pair_tile(const GemvParams& p, int rt, i
   const int per_tile = p.blocks_per_tile * H;
   const int t0 = rt * per_tile, t1 = t0 + per_tile - 1;
   if (t0 >= u0 && t1 < u1) {
-    store_pair_tile<kGated>(p, rt, g, t, v, rk);
+    store_pair_tile<kGated, kF16>(p, rt, g, t, v, rk);
     return false;
   }
   const int w_lo = warp_of(t0, p.uq, p.ur);
@@ -404,7 +404,7 @@ __device__ __forceinline__ bool publish_pair_tile(const GemvParams& p, int rt, i
 // arrive, sum every slot in slot order, (((0 + s0) + s1) + ...), and store -
 // the residual or gate operand is fetched in the same round trip as the
 // slots - then re-zero the counter for the next launch.
-template <bool kGated>
+template <bool kGated, bool kF16 = false>
 __device__ __forceinline__ void finish_split_tile(const GemvParams& p, int rt, int old, int g, int t, int lane,
                                                   const RopeKv* rk = nullptr) {
   constexpr int H = kGated ? 2 : 1;
@@ -425,16 +425,16 @@ __device__ __forceinline__ void finish_split_tile(const GemvParams& p, int rt, i
   float v[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
   sum_tile_slots<H>(p.partial + (size_t)t * N, MN, H * MN, n, ra, rb, N, v);
   if (kGated) {
-    if (ra < N) p.y[oa] = gate_bf16(v[0][0], v[1][0]);
-    if (rb < N) p.y[ob] = gate_bf16(v[0][1], v[1][1]);
-  } else if (rk != nullptr) {  // one activation row, n_out % 16 == 0
+    if (ra < N) p.y[oa] = gate_bf16<kF16>(v[0][0], v[1][0]);
+    if (rb < N) p.y[ob] = gate_bf16<kF16>(v[0][1], v[1][1]);
+  } else if (rk != nullptr) {  // one activation row, n_out % 16 == 0 (bf16 only)
     const bf16_t ya = epilogue_value(v[0][0], p.epi, bf2f(opa)), yb = epilogue_value(v[0][1], p.epi, bf2f(opb));
     p.y[oa] = ya;
     p.y[ob] = yb;
     rope_kv_rows(p, *rk, ra, rb, ya, yb);
   } else {
-    if (ra < N) p.y[oa] = epilogue_value(v[0][0], p.epi, bf2f(opa));
-    if (rb < N) p.y[ob] = epilogue_value(v[0][1], p.epi, bf2f(opb));
+    if (ra < N) p.y[oa] = epilogue_value<kF16>(v[0][0], p.epi, act2f<kF16>(opa));
+    if (rb < N) p.y[ob] = epilogue_value<kF16>(v[0][1], p.epi, act2f<kF16>(opb));
   }
 }
 
@@ -830,8 +830,9 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
 // padding after every 128 (one 64-block), so the four x lanes of a load hit
 // different banks.
 // kRope: the fused rotary + KV-cache store of a wqkv projection (one
-// activation row, not gated).
-template <bool kGated, bool kNested, bool kRope = false>
+// activation row, not gated, bf16). kF16: fp16 activations and outputs (the
+// pair table holds fp16 code pairs and the MMA is f16 x f16).
+template <bool kGated, bool kNested, bool kRope = false, bool kF16 = false>
 __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     nf4_gemv_reg_kernel(const __grid_constant__ GemvParams p) {
   constexpr int kT = GEMV_PAIR_WARPS * 32;
@@ -839,6 +840,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   __shared__ double norm_red[GEMV_PAIR_WARPS];
   __shared__ float rk_f[kRope ? 128 : 1];  // kRope: this token's rotary row
   static_assert(!(kRope && kGated), "the fused rotary store serves a plain projection");
+  static_assert(!(kRope && kF16), "the fused rotary store is bf16");
   const uint8_t* lut = smem;
   uint8_t* xs = smem + GEMV_LUT_BYTES;
 
@@ -913,7 +915,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   // wait, so no thread reaches the wait behind a global load.
   float c2v[2048 / kT];
   if (nested) load_code2_copies<kT>(p.code2, kGated ? p.code2_3 : nullptr, c2v);
-  build_pair_lut_fast<kT>(smem);
+  build_pair_lut_fast<kT, kF16>(smem);
   pdl_launch_dependents();
   pdl_wait();
   if (nested) store_code2_copies<kT>(smem, c2v);
@@ -937,8 +939,8 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   if (kRope && threadIdx.x < 128) rk_f[threadIdx.x] = rk_val;
   __syncthreads();
   if (p.norm_w != nullptr)
-    rms_normalise_staged<kT, true>(reinterpret_cast<uint16_t*>(xs), M, K, p.norm_w, p.norm_eps, norm_red,
-                                   xrow / 2);
+    rms_normalise_staged<kT, true, kF16>(reinterpret_cast<uint16_t*>(xs), M, K, p.norm_w, p.norm_eps, norm_red,
+                                         xrow / 2);
 
   const uint32_t lane_base = (uint32_t)lane * 4u;
   const uint32_t c2_base = 128u + (uint32_t)(2 * g + (t & 1)) * 4u;
@@ -1004,9 +1006,9 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       const uint32_t b0 = (st & 1) ? xq.z : xq.x;
       const uint32_t b1 = (st & 1) ? xq.w : xq.y;
       if (st & 1)
-        mma_bf16_16816(d1, a0, a1, a2, a3, b0, b1);
+        mma_act<kF16>(d1, a0, a1, a2, a3, b0, b1);
       else
-        mma_bf16_16816(d0, a0, a1, a2, a3, b0, b1);
+        mma_act<kF16>(d0, a0, a1, a2, a3, b0, b1);
     }
     // d[0] = (row g, block 2(t & 1)), d[1] = its successor; d[2], d[3] for row g + 8.
     const float ya = fmaf(s1a, d0[1] + d1[1], (d0[0] + d1[0]) * s0a);
@@ -1028,7 +1030,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       const float v[2][2] = {{acc_a, acc_b}, {acc3_a, acc3_b}};
       int old = 0;
       const RopeKv rk{rk_f, rk_pos};
-      if (publish_pair_tile<kGated>(p, rt, u0, u1, gw, g, tok, lane, v, old, kRope ? &rk : nullptr)) {
+      if (publish_pair_tile<kGated, kF16>(p, rt, u0, u1, gw, g, tok, lane, v, old, kRope ? &rk : nullptr)) {
         if (split_a < 0) {
           split_a = rt;
           old_a = old;
@@ -1051,8 +1053,8 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     }
   }
   const RopeKv rk{rk_f, rk_pos};
-  if (split_a >= 0) finish_split_tile<kGated>(p, split_a, old_a, g, tok, lane, kRope ? &rk : nullptr);
-  if (split_b >= 0) finish_split_tile<kGated>(p, split_b, old_b, g, tok, lane, kRope ? &rk : nullptr);
+  if (split_a >= 0) finish_split_tile<kGated, kF16>(p, split_a, old_a, g, tok, lane, kRope ? &rk : nullptr);
+  if (split_b >= 0) finish_split_tile<kGated, kF16>(p, split_b, old_b, g, tok, lane, kRope ? &rk : nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -2003,6 +2005,22 @@ cudaError_t launch_gemv(const GemvParams& p, int grid, bool pairs, cudaStream_t 
   static bool cfg_pair[64] = {}, cfg_gated[64] = {}, cfg_pair2[64] = {}, cfg_gated2[64] = {};
   static bool cfg_reg[64] = {}, cfg_reg_gated[64] = {}, cfg_reg_plain[64] = {}, cfg_reg_gated_plain[64] = {};
   static bool cfg1[64] = {}, cfg2[64] = {}, cfg4[64] = {};
+  if (pairs && p.reg && p.f16) {
+    const int smem = GEMV_LUT_BYTES + p.M * reg_x_row_bytes(p.K);
+    const int nt = GEMV_PAIR_WARPS * 32;
+    static bool h_reg[64] = {}, h_gated[64] = {}, h_plain[64] = {}, h_gated_plain[64] = {};
+    if (p.rk_q != nullptr) return cudaErrorInvalidValue;
+    if (p.nested)
+      return p.gated ? launch_kernel(nf4_gemv_reg_kernel<true, true, false, true>, p, grid, stream, h_gated, smem,
+                                     GEMV_REG_SMEM_MAX, nt)
+                     : launch_kernel(nf4_gemv_reg_kernel<false, true, false, true>, p, grid, stream, h_reg, smem,
+                                     GEMV_REG_SMEM_MAX, nt);
+    return p.gated ? launch_kernel(nf4_gemv_reg_kernel<true, false, false, true>, p, grid, stream, h_gated_plain,
+                                   smem, GEMV_REG_SMEM_MAX, nt)
+                   : launch_kernel(nf4_gemv_reg_kernel<false, false, false, true>, p, grid, stream, h_plain, smem,
+                                   GEMV_REG_SMEM_MAX, nt);
+  }
+  if (p.f16) return cudaErrorInvalidValue;  // fp16 is served by the register-fed kernel only
   if (pairs && p.reg) {
     const int smem = GEMV_LUT_BYTES + p.M * reg_x_row_bytes(p.K);
     const int nt = GEMV_PAIR_WARPS * 32;

@@ -5,10 +5,11 @@
 L, D) - possibly views of a longer cache - and a boolean mask (B, 1, S, L),
 True = visible; query head i reads KV head i // groups. One query position of
 batch 1 (every decode step) runs the split-KV kernel of ``libnf4b200.so``
-with the mask applied row by row (masked rows are never read). A multi-
-position prefill uses the reference's own grouped torch formulation
-(bf16 scores, fp32 softmax, bf16 probabilities), as the reference does for
-spans up to ``GROUPED_MAX_QUERY``.
+with the mask applied row by row (masked rows are never read), in bf16 or in
+the reference's fp16. A multi-position prefill uses the reference's own
+grouped torch formulation (scores of the activation type, fp32 softmax,
+probabilities of the activation type), as the reference does for spans up
+to ``GROUPED_MAX_QUERY``.
 """
 
 from __future__ import annotations
@@ -46,18 +47,21 @@ def kernel_attention(q, k_cache, v_cache, out, *, n_head: int, n_kv: int, pos=No
                      window: int, max_len: int):
     """Launch the decode-attention kernel on raw tensors (one query position).
 
-    q [n_head, 128] bf16; caches [n_kv, max_len, 128] bf16 (head stride
-    max_len rows); pos: int64 device tensor (rows [0, pos]) or None; mask:
-    uint8/bool device tensor of `window` entries or None.
+    q [n_head, 128] bf16 or fp16; caches [n_kv, max_len, 128] of q's dtype
+    (head stride max_len rows); pos: int64 device tensor (rows [0, pos]) or
+    None; mask: uint8/bool device tensor of `window` entries or None.
     """
     import torch
 
+    dt = _lib.act_type(q.dtype)
+    if dt is None or k_cache.dtype != q.dtype or v_cache.dtype != q.dtype or out.dtype != q.dtype:
+        raise ValueError(f"attention dtypes {q.dtype}/{k_cache.dtype}/{v_cache.dtype}/{out.dtype} are not served")
     ws = attention_workspace(q.device, n_head, 128, window)
     st = torch.cuda.current_stream(q.device)
-    _lib.check(_lib.lib().nf4b_decode_attention(
+    _lib.check(_lib.lib().nf4b_decode_attention_ex(
         q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
         None if pos is None else pos.data_ptr(), None if mask is None else mask.data_ptr(),
-        out.data_ptr(), n_head, n_kv, 128, max_len, window, ws.data_ptr(), ws.numel(),
+        out.data_ptr(), n_head, n_kv, 128, max_len, window, ws.data_ptr(), ws.numel(), dt,
         ctypes.c_void_p(st.cuda_stream)))
 
 
@@ -65,18 +69,22 @@ def qkv_attention(qkv, k_cache, v_cache, out, *, n_head: int, n_kv: int, pos, wi
                   freqs, freqs_dtype: int, q_norm_w=None, k_norm_w=None, eps: float = 1e-6, q_scratch=None):
     """q/k norm + rotary + KV write + decode attention in one launch
     (nf4b_qkv_attention) from the wqkv output `qkv` [n_head + 2 n_kv, 128];
-    `freqs` is the position's rotary row, `pos` the int64 device position."""
+    `freqs` is the position's rotary row, `pos` the int64 device position.
+    Activations, weights and caches are all bf16 or all fp16."""
     import torch
 
+    dt = _lib.act_type(qkv.dtype)
+    if dt is None or k_cache.dtype != qkv.dtype or v_cache.dtype != qkv.dtype or out.dtype != qkv.dtype:
+        raise ValueError(f"attention dtypes {qkv.dtype}/{k_cache.dtype}/{out.dtype} are not served")
     ws = attention_workspace(qkv.device, n_head, 128, window)
     if q_scratch is None:
-        q_scratch = torch.empty(n_head * 128, dtype=torch.bfloat16, device=qkv.device)
+        q_scratch = torch.empty(n_head * 128, dtype=qkv.dtype, device=qkv.device)
     st = torch.cuda.current_stream(qkv.device)
-    _lib.check(_lib.lib().nf4b_qkv_attention(
+    _lib.check(_lib.lib().nf4b_qkv_attention_ex(
         qkv.data_ptr(), None if q_norm_w is None else q_norm_w.data_ptr(),
         None if k_norm_w is None else k_norm_w.data_ptr(), float(eps), freqs.data_ptr(), int(freqs_dtype),
         pos.data_ptr(), q_scratch.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
-        n_head, n_kv, 128, max_len, window, ws.data_ptr(), ws.numel(), ctypes.c_void_p(st.cuda_stream)))
+        n_head, n_kv, 128, max_len, window, ws.data_ptr(), ws.numel(), dt, ctypes.c_void_p(st.cuda_stream)))
 
 
 def _grouped_torch(q, k, v, mask, n_head, n_local_heads, head_dim):
@@ -100,8 +108,8 @@ def decode_attention(q, k, v, mask, n_head, n_local_heads, head_dim):
     bsz, _, seqlen, _ = q.shape
     L = k.shape[2]
     served = (
-        q.is_cuda and bsz == 1 and seqlen == 1 and head_dim == 128 and q.dtype == torch.bfloat16
-        and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16
+        q.is_cuda and bsz == 1 and seqlen == 1 and head_dim == 128 and _lib.act_type(q.dtype) is not None
+        and k.dtype == q.dtype and v.dtype == q.dtype
         and n_head % n_local_heads == 0 and (n_head // n_local_heads) in (1, 2, 4, 8)
         and k.stride(-1) == 1 and k.stride(-2) == head_dim and v.stride() == k.stride()
         and k.stride(1) % head_dim == 0 and mask is not None and mask.shape[-1] == L
@@ -110,7 +118,7 @@ def decode_attention(q, k, v, mask, n_head, n_local_heads, head_dim):
         qc = q.reshape(n_head, head_dim).contiguous()
         m = mask.reshape(-1, L)[-1].to(torch.uint8).contiguous()
         if qc.data_ptr() % 16 == 0 and k.data_ptr() % 16 == 0 and v.data_ptr() % 16 == 0:
-            out = torch.empty((n_head, head_dim), dtype=torch.bfloat16, device=q.device)
+            out = torch.empty((n_head, head_dim), dtype=q.dtype, device=q.device)
             kernel_attention(qc, k, v, out, n_head=n_head, n_kv=n_local_heads, pos=None, mask=m,
                              window=L, max_len=k.stride(1) // head_dim)
             _stats["kernel"] += 1

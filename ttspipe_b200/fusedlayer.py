@@ -11,9 +11,10 @@ The reference's two attention launches (attn_partial + attn_combine) are one
 here (the last CTA of each KV head merges the partials), and so are its w1 and
 w3 launches (``nf4gemv.matmul_gated``, same rounding points). The position is read
 on the device from ``input_pos`` and the attended window is the mask's width,
-so one captured CUDA graph per window serves every position in it. Anything
-that is not a single bf16 position of an eligible block returns None and
-runs the block's own forward.
+so one captured CUDA graph per window serves every position in it. A block
+runs in bf16 or in the reference's fp16 (activations, norm weights and KV
+cache of one type). Anything that is not a single position of an eligible
+block returns None and runs the block's own forward.
 """
 
 from __future__ import annotations
@@ -55,7 +56,7 @@ def _eligible(block, x, mask, input_pos) -> bool:
     from ttspipe_b200 import nf4gemv
 
     a, ff = block.attention, block.feed_forward
-    if x.dim() != 3 or x.shape[0] != 1 or x.shape[1] != 1 or x.dtype != torch.bfloat16 or not x.is_cuda:
+    if x.dim() != 3 or x.shape[0] != 1 or x.shape[1] != 1 or _lib.act_type(x.dtype) is None or not x.is_cuda:
         return False
     if mask is None or input_pos is None or input_pos.numel() != 1 or a.kv_cache is None:
         return False
@@ -66,7 +67,8 @@ def _eligible(block, x, mask, input_pos) -> bool:
     if (a.n_head // a.n_local_heads) not in (1, 2, 4, 8):
         return False
     kc = a.kv_cache.k_cache
-    if kc.dtype != torch.bfloat16 or not kc.is_contiguous() or not a.kv_cache.v_cache.is_contiguous():
+    if kc.dtype != x.dtype or a.kv_cache.v_cache.dtype != x.dtype or not kc.is_contiguous() \
+            or not a.kv_cache.v_cache.is_contiguous():
         return False
     if mask.shape[-1] > kc.shape[2]:
         return False
@@ -88,13 +90,13 @@ def _attention(a, qkv, freqs_cis, input_pos, mask, y, nh: int, nkv: int, max_len
     kn = getattr(a, "k_norm", None) if a.attention_qk_norm else None
     eps = float(qn.eps if qn is not None and qn.eps is not None else 1e-6)
     if not FUSED_QKV_ATTENTION:
-        q = torch.empty(nh * HEAD_DIM, dtype=torch.bfloat16, device=qkv.device)
-        _lib.check(_lib.lib().nf4b_qk_rope_kv(
+        q = torch.empty(nh * HEAD_DIM, dtype=qkv.dtype, device=qkv.device)
+        _lib.check(_lib.lib().nf4b_qk_rope_kv_ex(
             qkv.data_ptr(), None if qn is None else qn.weight.data_ptr(),
             None if kn is None else kn.weight.data_ptr(), eps, freqs_cis.data_ptr(),
             _FTYPE[str(freqs_cis.dtype)], input_pos.data_ptr(), q.data_ptr(),
             a.kv_cache.k_cache.data_ptr(), a.kv_cache.v_cache.data_ptr(), nh, nkv, HEAD_DIM, max_len,
-            torch.cuda.current_stream(qkv.device).cuda_stream))
+            _lib.act_type(qkv.dtype), torch.cuda.current_stream(qkv.device).cuda_stream))
         fastpath.kernel_attention(q, a.kv_cache.k_cache, a.kv_cache.v_cache, y, n_head=nh, n_kv=nkv,
                                   pos=input_pos, mask=None, window=int(mask.shape[-1]), max_len=max_len)
         return
@@ -125,10 +127,10 @@ def decode_block(block, x, freqs_cis, mask, input_pos, next_block=None):
     an, fn = block.attention_norm, block.ffn_norm
     nh, nkv = a.n_head, a.n_local_heads
     max_len = a.kv_cache.k_cache.shape[2]
-    y = torch.empty((1, 1, nh * HEAD_DIM), dtype=torch.bfloat16, device=x.device)
+    y = torch.empty((1, 1, nh * HEAD_DIM), dtype=x.dtype, device=x.device)
     q = None
     rope_here = ROPE_IN_WQKV is True or (ROPE_IN_WQKV == "one_chunk" and int(mask.shape[-1]) <= 64)
-    if rope_here and not FUSED_QKV_ATTENTION and not a.attention_qk_norm:
+    if rope_here and not FUSED_QKV_ATTENTION and not a.attention_qk_norm and x.dtype == torch.bfloat16:
         # attention_norm, wqkv, the rotary and the KV write in one launch
         q = torch.empty(nh * HEAD_DIM, dtype=torch.bfloat16, device=x.device)
         if nf4gemv.matmul_qkv_rope(a.wqkv, x, freqs=freqs_cis, pos=input_pos, q_out=q, k_cache=a.kv_cache.k_cache,

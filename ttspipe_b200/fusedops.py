@@ -1,10 +1,10 @@
 """Fused RMSNorm and rotary embedding, one sm_100a kernel each.
 
 Drop-in for the reference's ``app/engine/fusedops.py`` (``rms_norm``,
-``rope``, ``install``, ``stats``, ``note_rope_fallback``) in bf16. Same
-formulas and rounding points (:61-132): the norm rounds to bf16 after the
-normalisation and again after the weight multiply; rotary is bit-exact to the
-unfused fp32 formula. The norm's sum of squares is exact (fp64 on the device),
+``rope``, ``install``, ``stats``, ``note_rope_fallback``) in bf16 and in the
+reference's fp16. Same formulas and rounding points (:61-132): the norm rounds
+to the activation type after the normalisation and again after the weight
+multiply; rotary is bit-exact to the unfused fp32 formula. The norm's sum of squares is exact (fp64 on the device),
 so unlike the reference's fp32 tree sum it does not depend on reduction order.
 Shapes these kernels do not serve return None (the caller uses its own code).
 """
@@ -37,7 +37,8 @@ def rms_norm(x, weight, eps: float):
 
     if not enabled:
         return None
-    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+    dt = _lib.act_type(x.dtype)
+    if dt is None or weight.dtype != x.dtype:
         return None
     if x.device.type != "cuda" or not x.is_contiguous() or not weight.is_contiguous():
         return None
@@ -45,8 +46,8 @@ def rms_norm(x, weight, eps: float):
     if width != weight.numel() or width == 0 or x.numel() == 0:
         return None
     out = torch.empty_like(x)
-    _lib.check(_lib.lib().nf4b_rms_norm(x.data_ptr(), weight.data_ptr(), out.data_ptr(),
-                                        x.numel() // width, width, float(eps), _stream(x)))
+    _lib.check(_lib.lib().nf4b_rms_norm_ex(x.data_ptr(), weight.data_ptr(), out.data_ptr(),
+                                           x.numel() // width, width, float(eps), dt, _stream(x)))
     _stats["norm"] += 1
     return out
 
@@ -57,7 +58,8 @@ def rope(x, freqs_cis):
 
     if not enabled:
         return None
-    if x.dtype != torch.bfloat16 or x.device.type != "cuda" or not x.is_contiguous():
+    dt = _lib.act_type(x.dtype)
+    if dt is None or x.device.type != "cuda" or not x.is_contiguous():
         return None
     if not freqs_cis.is_contiguous() or x.dim() != 4 or freqs_cis.device != x.device:
         return None
@@ -68,8 +70,8 @@ def rope(x, freqs_cis):
     if head_dim % 2 or freqs_cis.numel() != seq * (head_dim // 2) * 2 or x.numel() == 0:
         return None
     out = torch.empty_like(x)
-    _lib.check(_lib.lib().nf4b_rope(x.data_ptr(), freqs_cis.data_ptr(), ftype, out.data_ptr(),
-                                    bsz, seq, heads, head_dim, _stream(x)))
+    _lib.check(_lib.lib().nf4b_rope_ex(x.data_ptr(), freqs_cis.data_ptr(), ftype, out.data_ptr(),
+                                       bsz, seq, heads, head_dim, dt, _stream(x)))
     _stats["rope"] += 1
     return out
 

@@ -13,10 +13,15 @@ are nvcc-built sm_100a code in ``libnf4b200.so`` behind a C ABI
   memory, TMEM accumulators) - one launch for the whole prompt, where the
   reference slices it into 32-row launches (app/engine/nf4gemv.py:460-478).
 
-Activations are bf16 (the reference's GPU path is fp16-only; this build's
-primary dtype is bf16, see app/engine/nf4cpu.py for the bf16 rounding points).
-fp16 inputs are declined (None), as the reference declines non-fp16 ones.
-There is no CPU or bitsandbytes fallback inside: a missing library raises.
+Activations are bf16 or fp16. fp16 is the reference's only GPU dtype
+(app/engine/nf4gemv.py:439, its TTS_HALF default): ``matmul`` serves it with
+the same rounding points as its kernel (fp32 accumulation, the output and each
+epilogue op rounded to fp16) - on the register-fed decode GEMV for 1..2 rows
+and on the tcgen05 GEMM for every other row count. bf16 follows the bf16
+rounding points of app/engine/nf4cpu.py; ``matmul_qkv_rope``, the chain and the
+decode step are bf16 only. Other dtypes are declined (None), as the reference
+declines non-fp16 ones. There is no CPU or bitsandbytes fallback inside: a
+missing library raises.
 """
 
 from __future__ import annotations
@@ -193,48 +198,56 @@ def prepare(module) -> bool:
 NORM_X_MAX = 40 * 1024
 
 
-def _norm_ok(norm, rows: int, K: int, device) -> bool:
+def _norm_ok(norm, rows: int, K: int, device, dtype=None) -> bool:
     """Whether `norm` = (weight, eps) can be fused into a decode GEMV of this shape."""
     import torch
 
     w = norm[0]
-    return (1 <= rows <= 4 and K % 128 == 0 and rows * K * 2 <= NORM_X_MAX and w.dtype == torch.bfloat16
+    dtype = torch.bfloat16 if dtype is None else dtype
+    max_rows = 2 if dtype == torch.float16 else 4
+    return (1 <= rows <= max_rows and K % 128 == 0 and rows * K * 2 <= NORM_X_MAX and w.dtype == dtype
             and w.is_contiguous() and w.numel() == K and w.device == device)
 
 
-def _opts(prefetch=None, norm=None):
-    """`nf4b_gemm_opts`: up to two prepared linears to stream into L2 and a
-    fused RMSNorm (weight, eps) of x; None when neither is given."""
+def _opts(prefetch=None, norm=None, dtype=None):
+    """`nf4b_gemm_opts`: up to two prepared linears to stream into L2, a fused
+    RMSNorm (weight, eps) of x and the activation dtype; None when none is
+    given (bf16, nothing fused)."""
+    import torch
+
     descs = []
     if prefetch is not None:
         mods = list(prefetch) if isinstance(prefetch, (list, tuple)) else [prefetch]
         descs = [m._nf4_fast["desc"] for m in mods[:2] if getattr(m, "_nf4_fast", None) is not None]
-    if not descs and norm is None:
+    f16 = dtype == torch.float16
+    if not descs and norm is None and not f16:
         return None
     ptrs = [ctypes.pointer(d) for d in descs] + [None] * (2 - len(descs))
     nw, eps = (norm[0].data_ptr(), float(norm[1])) if norm is not None else (None, 0.0)
-    return ctypes.byref(_lib.GemmOpts(ptrs[0], ptrs[1], nw, eps))
+    return ctypes.byref(_lib.GemmOpts(ptrs[0], ptrs[1], nw, eps, _lib.NF4B_F16 if f16 else 0))
 
 
 def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None, norm=None):
     """``x @ module.weight.T`` for any number of input rows, or None if not applicable.
 
-    `epi` fuses ``operand + xW`` (EPI_RESIDUAL) or ``silu(operand) * xW``
-    (EPI_SILU_GATE); `operand` has the output's shape, bf16, on x's device.
+    x is bf16 or fp16 (the output has x's dtype). `epi` fuses
+    ``operand + xW`` (EPI_RESIDUAL) or ``silu(operand) * xW`` (EPI_SILU_GATE);
+    `operand` has the output's shape and x's dtype, on x's device.
     `prefetch` (an extension; None in the reference's API) names one or two
     prepared linears that later calls will read: their weights are streamed
     into L2 while this call runs. `norm` (an extension) = (weight, eps):
     ``rms_norm(x) @ W.T`` in the same launch, bit-exact to
-    ``fusedops.rms_norm`` then ``matmul``; served for 1..4 rows with
-    in_features % 128 == 0 and x within NORM_X_MAX bytes (None otherwise).
-    Launches on ``torch.cuda.current_stream()``.
+    ``fusedops.rms_norm`` then ``matmul``; served for 1..4 rows (fp16: 1..2
+    rows on the register-fed GEMV) with in_features % 128 == 0 and x within
+    NORM_X_MAX bytes (None otherwise). Launches on
+    ``torch.cuda.current_stream()``.
     """
     import torch
 
     fast = getattr(module, "_nf4_fast", None)
     if fast is None:
         return None
-    if x.dtype != torch.bfloat16 or x.device.type != "cuda":
+    if _lib.act_type(x.dtype) is None or x.device.type != "cuda":
         return None
     K, N = fast["K"], fast["M"]
     if x.shape[-1] != K:
@@ -247,11 +260,11 @@ def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None, norm=
     rows = flat.shape[0]
     if rows == 0:
         return x.new_empty((*x.shape[:-1], N))
-    if norm is not None and not _norm_ok(norm, rows, K, x.device):
+    if norm is not None and not _norm_ok(norm, rows, K, x.device, x.dtype):
         return None
     op_ptr = None
     if epi != EPI_NONE:
-        if operand is None or operand.numel() != rows * N or operand.dtype != torch.bfloat16:
+        if operand is None or operand.numel() != rows * N or operand.dtype != x.dtype:
             return None
         operand = operand.reshape(rows, N)
         if not operand.is_contiguous():
@@ -259,7 +272,7 @@ def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None, norm=
         op_ptr = operand.data_ptr()
     if not available():
         raise RuntimeError(f"nf4 kernels unavailable: {_unavailable}")
-    out = torch.empty((rows, N), dtype=torch.bfloat16, device=x.device)
+    out = torch.empty((rows, N), dtype=x.dtype, device=x.device)
     stream = torch.cuda.current_stream(x.device)
     L = _lib.lib()
     desc = fast["desc"]
@@ -268,9 +281,12 @@ def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None, norm=
     if need > 0:
         ws = _workspace(x.device, need, "gemv" if rows <= MAX_N else "gemm")
         ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
-    opts = _opts(prefetch, norm)
-    _lib.check(L.nf4b_gemm_ex(ctypes.byref(desc), flat.data_ptr(), out.data_ptr(), rows, int(epi),
-                              op_ptr, ws_ptr, ws_bytes, opts, ctypes.c_void_p(stream.cuda_stream)))
+    opts = _opts(prefetch, norm, x.dtype)
+    st = L.nf4b_gemm_ex(ctypes.byref(desc), flat.data_ptr(), out.data_ptr(), rows, int(epi),
+                        op_ptr, ws_ptr, ws_bytes, opts, ctypes.c_void_p(stream.cuda_stream))
+    if st == _lib.NF4B_ERR_SHAPE and norm is not None and x.dtype == torch.float16:
+        return None     # an fp16 RMSNorm fuses into the register-fed GEMV only
+    _lib.check(st)
     _stats["fast"] += 1
     return out.view(*x.shape[:-1], N)
 
@@ -332,11 +348,12 @@ def matmul_gated(w1, w3, x, *, prefetch=None, norm=None):
     out. An extension of the reference's API. Serves 1..4 rows with
     in_features % 128 == 0; returns None otherwise (the caller then issues the
     two matmuls) or if either linear is not prepared. `norm` as in ``matmul``.
+    fp16 x is served for 1..2 rows on the register-fed GEMV (None otherwise).
     """
     import torch
 
     f1, f3 = getattr(w1, "_nf4_fast", None), getattr(w3, "_nf4_fast", None)
-    if f1 is None or f3 is None or x.dtype != torch.bfloat16 or x.device.type != "cuda":
+    if f1 is None or f3 is None or _lib.act_type(x.dtype) is None or x.device.type != "cuda":
         return None
     K, N = f1["K"], f1["M"]
     if (f3["K"], f3["M"]) != (K, N) or x.shape[-1] != K or K % 128:
@@ -347,20 +364,23 @@ def matmul_gated(w1, w3, x, *, prefetch=None, norm=None):
         if flat.data_ptr() % 16:
             return None
     rows = flat.shape[0]
-    if rows < 1 or rows > 4:
+    if rows < 1 or rows > (2 if x.dtype == torch.float16 else 4):
         return None
-    if norm is not None and not _norm_ok(norm, rows, K, x.device):
+    if norm is not None and not _norm_ok(norm, rows, K, x.device, x.dtype):
         return None
     if not available():
         raise RuntimeError(f"nf4 kernels unavailable: {_unavailable}")
     L = _lib.lib()
     need = int(L.nf4b_gemm_workspace_size(ctypes.byref(f1["desc"]), rows))
     ws = _workspace(x.device, need)
-    out = torch.empty((rows, N), dtype=torch.bfloat16, device=x.device)
+    out = torch.empty((rows, N), dtype=x.dtype, device=x.device)
     stream = torch.cuda.current_stream(x.device)
-    _lib.check(L.nf4b_gemm_gated(ctypes.byref(f1["desc"]), ctypes.byref(f3["desc"]), flat.data_ptr(),
-                                 out.data_ptr(), rows, ws.data_ptr(), ws.numel(), _opts(prefetch, norm),
-                                 ctypes.c_void_p(stream.cuda_stream)))
+    st = L.nf4b_gemm_gated(ctypes.byref(f1["desc"]), ctypes.byref(f3["desc"]), flat.data_ptr(),
+                           out.data_ptr(), rows, ws.data_ptr(), ws.numel(), _opts(prefetch, norm, x.dtype),
+                           ctypes.c_void_p(stream.cuda_stream))
+    if st == _lib.NF4B_ERR_SHAPE and x.dtype == torch.float16:
+        return None     # fp16 gates run on the register-fed GEMV only
+    _lib.check(st)
     _stats["fast"] += 1
     return out.view(*x.shape[:-1], N)
 
