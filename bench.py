@@ -611,7 +611,8 @@ def run_config3(layers, device, stream, peaks) -> dict:
         flops = n_layers * sum(2.0 * rows * nn * kk for nn, kk in shapes)
         gbs, tfs = byts / us / 1e3, flops / us / 1e6
         rec = {"rows": rows, "us_per_layer": round(us / n_layers, 2), "GBps": round(gbs, 1),
-               "TFLOPps": round(tfs, 2), "kernel": "GEMV (nf4_gemv_*)" if rows <= 32 else "tcgen05 GEMM"}
+               "TFLOPps": round(tfs, 2),
+               "kernel": "register-fed GEMV (nf4_gemv_reg_kernel)" if rows <= 8 else "tcgen05 GEMM"}
         if kind == "decode":
             rec["roofline"] = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                                "frac": _frac(gbs, float(peaks["hbm_gbs"]))}

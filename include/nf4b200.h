@@ -88,8 +88,10 @@ int nf4b_device_error(int clear);
 /*
  * Y[rows, n_out] = epi(X[rows, k_in] . dequant(W)^T).
  * Replaces the `nf4_mma` launch of nf4gemv.matmul (app/engine/nf4gemv.py:427-479):
- * rows <= 32 (decode and batched decode) run the streaming GEMV, larger row
- * counts the tcgen05 GEMM. `operand` has Y's shape (epi != NONE).
+ * 1..8 rows (decode and batched decode) run the streaming GEMV - the
+ * register-fed kernel for blocksize-64 weights with k_in % 256 == 0, which
+ * decodes each weight once for all rows - and larger row counts the tcgen05
+ * GEMM. `operand` has Y's shape (epi != NONE).
  * `workspace` must hold nf4b_gemm_workspace_size(w, rows) bytes and be zeroed
  * once before its first use; every call leaves it zeroed again. One workspace
  * per stream: calls that overlap on the GPU must not share one. For the GEMM
@@ -113,14 +115,16 @@ typedef struct nf4b_gemm_opts {
    * norm_eps inside the launch, with exactly the arithmetic of nf4b_rms_norm,
    * and the matmul reads the normalised x (it is never written out): the
    * reference's attention_norm / ffn_norm before wqkv / w1,w3 as one launch.
-   * Served when x fits the decode GEMV's shared-memory staging (1..4 rows,
+   * Served when x fits the decode GEMV's shared-memory staging: the
+   * register-fed kernel's (1..8 rows, blocksize 64, k_in % 256 == 0,
+   * rows * k_in * 2 <= 162 KB), else the pair kernel's (1..4 rows,
    * k_in % 128 == 0, rows * k_in * 2 <= 40 KB); NF4B_ERR_SHAPE otherwise. */
   const void* norm_weight;
   float norm_eps;
   /* Activation type of x, operand, y and norm_weight: 0 or NF4B_BF16 = bf16,
    * NF4B_F16 = fp16 (the reference's own kernel serves fp16 only,
    * app/engine/nf4gemv.py:439; its TTS_HALF default, app/config.py:107). fp16
-   * runs the register-fed decode GEMV for 1..2 rows (blocksize 64,
+   * runs the register-fed decode GEMV for 1..8 rows (blocksize 64,
    * k_in % 256 == 0, 32-byte aligned packed codes; a fused RMSNorm and the
    * gated pair as for bf16) and the tcgen05 GEMM for every other row count,
    * with the reference's rounding points in fp16 (fp32 accumulation; the
@@ -166,8 +170,10 @@ int nf4b_gemm_qkv_rope(const nf4b_weight* w, const void* x, void* y, const nf4b_
  * y = bf16(bf16(silu(bf16(x W1^T))) * bf16(x W3^T)), the rounding points of the
  * fork's w2(F.silu(w1(x)) * w3(x)) (app/engine/fusedlayer.py:265-266, where it
  * is two nf4gemv.matmul launches, the second with EPI_SILU_GATE). x W1^T is
- * never written out. Serves 1..4 rows with k_in % 128 == 0 (NF4B_ERR_SHAPE
- * otherwise: the caller then issues the two matmuls). w1 and w3 must agree in
+ * never written out. Serves 1..8 rows on the register-fed kernel (blocksize
+ * 64, k_in % 256 == 0) and 1..4 rows with k_in % 128 == 0 otherwise
+ * (NF4B_ERR_SHAPE beyond: the caller then issues the two matmuls; fp16: the
+ * register-fed kernel only). w1 and w3 must agree in
  * shape and quantisation. Workspace as nf4b_gemm (nf4b_gemm_workspace_size of
  * w1 covers it). No reference counterpart as a single call.
  */
@@ -261,9 +267,9 @@ size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows);
  * device pointers from another runtime, a graph being recorded): the GEMV's
  * partial sums and counters live in a 4 MiB scratch array built into the
  * library, which every GPU that loads it keeps until exit. No counterpart in
- * the reference. Limits: GEMV calls (1..32 rows) whose scratch need
+ * the reference. Limits: GEMV calls (1..8 rows) whose scratch need
  * (nf4b_gemm_workspace_size) exceeds NF4B_NOALLOC_SCRATCH_BYTES fail with
- * NF4B_ERR_WORKSPACE. More than 32 rows run the tensor-core GEMM, which puts
+ * NF4B_ERR_WORKSPACE. More than 8 rows run the tensor-core GEMM, which puts
  * its split-K partial sums in the same scratch when they fit (so it splits
  * exactly as nf4b_gemm with a workspace does) and otherwise runs unsplit;
  * those calls share the scratch too. The first call on a device looks the

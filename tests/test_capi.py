@@ -88,8 +88,8 @@ def test_workspace_size_grows_with_rows_and_is_zero_for_the_gemm_path():
     w, _keep = _weight(n_out=9728, k_in=2560)
     L = _lib.lib()
     s1 = L.nf4b_gemm_workspace_size(ctypes.byref(w), 1)
-    s32 = L.nf4b_gemm_workspace_size(ctypes.byref(w), 32)
-    assert 0 < s1 < s32
+    s8 = L.nf4b_gemm_workspace_size(ctypes.byref(w), 8)   # the decode GEMV's partial sums grow with rows
+    assert 0 < s1 < s8
     assert L.nf4b_gemm_workspace_size(ctypes.byref(w), 33) == 0
     assert L.nf4b_decode_attention_workspace_size(32, 128, 2048) > 0
 

@@ -6,7 +6,7 @@ deployment default is fp16 (TTS_HALF, app/config.py:107). Every kernel here is
 also instantiated for fp16 and checked against the oracle's fp16 restatement
 (`f16=True`: the same formulas with fp16 at every rounding point):
 
-* matmul: the register-fed decode GEMV (1..2 rows) and the tcgen05 GEMM
+* matmul: the register-fed decode GEMV (1..8 rows) and the tcgen05 GEMM
   (every other row count) against the exactly accumulated product of the
   bit-exact fp16 dequantised weight - max|err| <= 2e-2 x RMS and
   norm-relative < 5e-3, the bars of the bf16 tests; the fused epilogues bit
@@ -112,7 +112,7 @@ def _ulp16(v):
     return np.exp2(np.floor(np.log2(np.maximum(np.abs(v), 2.0 ** -14))) - 10)
 
 
-@pytest.mark.parametrize("rows", [1, 2])
+@pytest.mark.parametrize("rows", [1, 2, 5])
 @pytest.mark.parametrize("nested", [True, False])
 def test_gated_pair(rows, nested):
     """silu(x W1) * (x W3) in one launch: within the gate of the separate
@@ -136,7 +136,7 @@ def test_gated_pair(rows, nested):
     assert np.all((got >= lo) & (got <= hi))
 
 
-@pytest.mark.parametrize("rows", [1, 2])
+@pytest.mark.parametrize("rows", [1, 2, 3, 8])
 def test_fused_norm_equals_norm_then_matmul(rows):
     lin = make_linear(6144, 2560, seed=31 + rows)
     g = torch.Generator().manual_seed(rows)
@@ -145,8 +145,8 @@ def test_fused_norm_equals_norm_then_matmul(rows):
     want = nf4gemv.matmul(lin, fusedops.rms_norm(x, nw, 1e-6))
     got = nf4gemv.matmul(lin, x, norm=(nw, 1e-6))
     assert got is not None and torch.equal(got, want)
-    # a fused norm beyond the register-fed GEMV's rows is declined, not run in bf16
-    assert nf4gemv.matmul(lin, randn_f16((3, 2560), seed=1), norm=(nw, 1e-6)) is None
+    # beyond the register-fed GEMV's rows a fused norm is declined, not run in bf16
+    assert nf4gemv.matmul(lin, randn_f16((9, 2560), seed=1), norm=(nw, 1e-6)) is None
 
 
 @pytest.mark.parametrize("rows,width", [(1, 2560), (32, 128), (3, 2560), (1, 40)])
@@ -328,8 +328,7 @@ def test_against_the_references_own_fp16_kernel(rows, epi):
     register-fed GEMV rounds the code and scales the block sums in fp32) and
     in summation order, so the products agree to two fp16 ulps element by
     element. Each kernel's fused epilogue is then the oracle's fp16 epilogue
-    of its own product (the reference's fast-math exponential may move a
-    gate output by one ulp)."""
+    of its own product."""
     ref = _reference_kernel()
     if ref is None:
         pytest.skip("oracle/_ref/nf4mma_ref.so was not built here")
@@ -359,7 +358,20 @@ def test_against_the_references_own_fp16_kernel(rows, epi):
     assert np.linalg.norm(a - b) / np.linalg.norm(a) < 2e-3
     if epi == nf4gemv.EPI_NONE:
         return
-    for prod, out, one_ulp in ((y0_ref, y_ref, True), (y0, y, epi == nf4gemv.EPI_SILU_GATE)):
-        want = orc.epilogue(f32(prod), epi, to_bits(operand), f16=True)
-        diff = np.abs(to_bits(out).astype(np.int32) - want.astype(np.int32))
-        assert diff.max() <= (1 if one_ulp else 0) and (diff > 0).mean() < 1e-2
+    # this build: deterministic, so its fused store is the epilogue of its own
+    # product (the gate's exponential may move an output by one ulp)
+    want = orc.epilogue(f32(y0), epi, to_bits(operand), f16=True)
+    diff = np.abs(to_bits(y).astype(np.int32) - want.astype(np.int32))
+    assert diff.max() <= (1 if epi == nf4gemv.EPI_SILU_GATE else 0) and (diff > 0).mean() < 1e-2
+    # the reference: its blocks sum their warps' partials with shared-memory
+    # atomics (an order that changes from launch to launch), so its fused
+    # launch may round the product one ulp apart from its plain launch; with
+    # the residual's cancellation that is many output ulps, so the bar is the
+    # product's ulp carried through the epilogue plus the output's own ulp
+    y0r = f32(y0_ref).astype(np.float64)
+    factor = 1.0 if epi == nf4gemv.EPI_RESIDUAL else \
+        np.abs(orc.f16_to_f32(orc.silu_bf16(to_bits(operand), f16=True)).astype(np.float64))
+    want = orc.f16_to_f32(orc.epilogue(f32(y0_ref), epi, to_bits(operand), f16=True)).astype(np.float64)
+    out = f32(y_ref).astype(np.float64)
+    allowed = _ulp16(y0r) * factor + _ulp16(np.maximum(np.abs(out), np.abs(want)))
+    assert np.all(np.abs(out - want) <= allowed)

@@ -126,8 +126,8 @@ def test_declines_and_rejects():
     w1 = make_linear(256, 2560, seed=1)
     w3 = make_linear(256, 2560, seed=2)
     odd = make_linear(256, 1024 + 64, seed=3)
-    x5 = randn_bf16((5, 2560), seed=4, device="cuda")
-    assert nf4gemv.matmul_gated(w1, w3, x5) is None          # more than 4 rows
+    x5 = randn_bf16((9, 2560), seed=4, device="cuda")
+    assert nf4gemv.matmul_gated(w1, w3, x5) is None          # more than 8 rows
     assert nf4gemv.matmul_gated(w1, odd, x5[:1]) is None     # shapes differ
     L = _lib.lib()
     y = torch.empty((1, 256), dtype=torch.bfloat16, device="cuda")
@@ -136,8 +136,8 @@ def test_declines_and_rejects():
                            x5.data_ptr(), y.data_ptr(), 1, ws.data_ptr(), ws.numel(), None, None)
     assert st == -2 and "differ" in _lib.last_error()
     st = L.nf4b_gemm_gated(ctypes.byref(w1._nf4_fast["desc"]), ctypes.byref(w3._nf4_fast["desc"]),
-                           x5.data_ptr(), y.data_ptr(), 5, ws.data_ptr(), ws.numel(), None, None)
-    assert st == -2 and "1..4 rows" in _lib.last_error()
+                           x5.data_ptr(), y.data_ptr(), 9, ws.data_ptr(), ws.numel(), None, None)
+    assert st == -2 and "1..8 rows" in _lib.last_error()
     x_odd = randn_bf16((1, 1088), seed=5, device="cuda")
     st = L.nf4b_gemm_gated(ctypes.byref(odd._nf4_fast["desc"]), ctypes.byref(odd._nf4_fast["desc"]),
                            x_odd.data_ptr(), y.data_ptr(), 1, ws.data_ptr(), ws.numel(), None, None)

@@ -76,20 +76,23 @@ def test_fused_norm_repeated_launches_are_identical():
 
 
 def test_fused_norm_outside_the_staging_limit_is_declined():
-    lin = make_linear(256, 2560, seed=31)
     nw = norm_weight(2560, seed=32)
-    x8 = randn_bf16((8, 2560), seed=33, device="cuda")
-    assert nf4gemv.matmul(lin, x8, norm=(nw, 1e-6)) is None       # 8 rows: the block kernel
+    lin = make_linear(256, 2560, seed=31)
+    x9 = randn_bf16((9, 2560), seed=33, device="cuda")
+    assert nf4gemv.matmul(lin, x9, norm=(nw, 1e-6)) is None       # 9 rows: the GEMM
     lin_big = make_linear(256, 12288, seed=34)
-    x_big = randn_bf16((2, 12288), seed=35, device="cuda")           # 48 KB of x
+    x_big = randn_bf16((8, 12288), seed=35, device="cuda")           # 192 KB of x
     assert nf4gemv.matmul(lin_big, x_big, norm=(norm_weight(12288, 36), 1e-6)) is None
+    lin_odd = make_linear(256, 2688, seed=37)                        # k_in % 256 != 0: no register-fed kernel
+    x5 = randn_bf16((5, 2688), seed=38, device="cuda")               # 5 rows: the block kernel
+    assert nf4gemv.matmul(lin_odd, x5, norm=(norm_weight(2688, 39), 1e-6)) is None
     # the C ABI itself refuses rather than computing without the norm
     L = _lib.lib()
     desc = lin._nf4_fast["desc"]
-    need = int(L.nf4b_gemm_workspace_size(ctypes.byref(desc), 8))
-    ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
-    y = torch.empty(8, 256, dtype=torch.bfloat16, device="cuda")
+    need = int(L.nf4b_gemm_workspace_size(ctypes.byref(desc), 9))
+    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device="cuda")
+    y = torch.empty(9, 256, dtype=torch.bfloat16, device="cuda")
     opts = _lib.GemmOpts(None, None, nw.data_ptr(), 1e-6)
-    st = L.nf4b_gemm_ex(ctypes.byref(desc), x8.data_ptr(), y.data_ptr(), 8, 0, None, ws.data_ptr(), need,
+    st = L.nf4b_gemm_ex(ctypes.byref(desc), x9.data_ptr(), y.data_ptr(), 9, 0, None, ws.data_ptr(), ws.numel(),
                         ctypes.byref(opts), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert st == _lib.NF4B_ERR_SHAPE

@@ -80,12 +80,14 @@ def test_noalloc_residual_epilogue():
 
 
 def test_noalloc_refuses_a_call_larger_than_its_scratch():
-    layer = make_linear(9728, 2560, seed=5)
+    """A decode GEMV (1..8 rows) whose partial sums exceed the scratch: 32768
+    output features at 8 rows (~6.4 MB of slots)."""
+    layer = make_linear(32768, 4096, seed=5)
     desc = layer._nf4_fast["desc"]
-    rows = 32
+    rows = 8
     assert _lib.lib().nf4b_gemm_workspace_size(ctypes.byref(desc), rows) > NOALLOC_SCRATCH_BYTES
-    x = randn_bf16((rows, 2560), seed=6, device="cuda")
-    y = torch.full((rows, 9728), 7.0, dtype=torch.bfloat16, device="cuda")
+    x = randn_bf16((rows, 4096), seed=6, device="cuda")
+    y = torch.full((rows, 32768), 7.0, dtype=torch.bfloat16, device="cuda")
     st = _lib.lib().nf4b_gemm_noalloc(ctypes.byref(desc), x.data_ptr(), y.data_ptr(), rows, 0,
                                       None, None)
     assert st == -5
@@ -95,7 +97,7 @@ def test_noalloc_refuses_a_call_larger_than_its_scratch():
 
 
 def test_noalloc_gemm_splits_its_k_range_in_the_scratch():
-    """More than 32 rows run the tensor-core GEMM. Where its split-K partial
+    """More than 8 rows run the tensor-core GEMM. Where its split-K partial
     sums fit the built-in scratch (1024x2560 at 64 rows splits the k range
     across CTAs), it splits exactly as nf4b_gemm does with a workspace, so the
     two give the same bits - twice in a row on the shared scratch."""

@@ -147,18 +147,20 @@ bool use_pairs(const nf4b_weight* w, int rows) {
   return aligned(w->absmax, w->blocksize == 64 ? 8 : 4);
 }
 
+bool reg_eligible(const nf4b_weight* w, const nf4b_weight* w3, int rows);
+
 size_t gemv_workspace_bytes(const nf4b_weight* w, int rows, int sms) {
   GemvPlan a;
   gemv_plan(w->n_out, w->k_in, rows, sms, false, &a);
   size_t bytes = a.partial_bytes;
-  if (rows <= 4 && w->k_in % 128 == 0) {  // the pair kernel may serve this call, plain or gated
-    for (int gated = 0; gated < 2; ++gated)
-      for (int su = 1; su <= pair_su(w, rows); ++su) {
-        GemvPlan b;
-        gemv_plan(w->n_out, w->k_in, rows, sms, true, &b, gated != 0, su);
-        if (b.partial_bytes > bytes) bytes = b.partial_bytes;
-      }
-  }
+  // the pair or register-fed kernel may serve this call, plain or gated
+  const int su_max = reg_eligible(w, nullptr, rows) ? 2 : (rows <= 4 && w->k_in % 128 == 0) ? pair_su(w, rows) : 0;
+  for (int gated = 0; gated < 2; ++gated)
+    for (int su = 1; su <= su_max; ++su) {
+      GemvPlan b;
+      gemv_plan(w->n_out, w->k_in, rows, sms, true, &b, gated != 0, su);
+      if (b.partial_bytes > bytes) bytes = b.partial_bytes;
+    }
   return GEMV_COUNTER_BYTES + bytes;
 }
 
@@ -179,14 +181,21 @@ int act_type(const nf4b_gemm_opts* opts, bool* f16) {
 }
 
 // Whether the register-fed pair GEMV serves this weight (pair) at `rows`:
-// blocksize-64 units of 256 codes with their scale data in one aligned copy,
-// 32-byte aligned packed codes, 1..2 rows.
+// 1..GEMV_REG_MAX_ROWS rows whose x fits its shared-memory staging,
+// blocksize-64 units of 256 codes with their scale data in one aligned copy
+// (nested: the pair kernel's alignment, second-level blocks of >= 4; plain:
+// 16-byte aligned fp32 scales), 32-byte aligned packed codes.
 bool reg_eligible(const nf4b_weight* w, const nf4b_weight* w3, int rows) {
   auto one = [&](const nf4b_weight* v) {
-    return use_pairs(v, rows) && pair_su(v, rows) == 2 && aligned(v->packed, 32) &&
-           (long long)v->n_out * (v->k_in / 64) < (1LL << 31);
+    if (v->blocksize != 64 || v->k_in % 256 || !aligned(v->packed, 32) ||
+        (long long)v->n_out * (v->k_in / 64) >= (1LL << 31))
+      return false;
+    if (v->nested)
+      return aligned(v->absmax_code, 4) && aligned(v->absmax, 4) && aligned(v->code2, 16) && v->blocksize2 >= 4;
+    return aligned(v->absmax, 16);
   };
-  return rows >= 1 && rows <= 2 && one(w) && (w3 == nullptr || one(w3));
+  return rows >= 1 && rows <= GEMV_REG_MAX_ROWS && (long long)rows * w->k_in * 2 <= GEMV_REG_X_MAX && one(w) &&
+         (w3 == nullptr || one(w3));
 }
 
 // One GEMV launch (rows <= GEMV_MAX_ROWS): plain, or the gated pair (w, w3)
@@ -197,13 +206,20 @@ int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* 
               cudaStream_t s, const nf4b_rope_kv* rk = nullptr) {
   if ((long long)(w->n_out + 15) / 16 > GEMV_MAX_TILES)
     return fail(NF4B_ERR_SHAPE, "n_out %d exceeds the GEMV's %lld-row limit", w->n_out, GEMV_MAX_TILES * 16);
-  const bool pairs = use_pairs(w, rows);
   const bool gated = w3 != nullptr;
-  if (gated && !(pairs && use_pairs(w3, rows)))
-    return fail(NF4B_ERR_SHAPE, "the gated GEMV serves 1..4 rows with k_in %% 128 == 0 (got %d rows, k_in %d)",
+  // the register-fed kernel (1..8 rows) where it applies, else the TMA-ring
+  // pair kernel (1..4 rows), else the block kernel
+  const bool reg = reg_eligible(w, w3, rows);
+  const bool pairs = reg || use_pairs(w, rows);
+  if (gated && !(reg || (pairs && use_pairs(w3, rows))))
+    return fail(NF4B_ERR_SHAPE,
+                "the gated GEMV serves 1..8 rows on the register-fed kernel (blocksize 64, k_in %% 256 == 0) or 1..4 "
+                "rows with k_in %% 128 == 0 (got %d rows, k_in %d)",
                 rows, w->k_in);
   const int sms = current_sm_count();
-  const int su = pairs ? (gated ? (pair_su(w, rows) == 2 && pair_su(w3, rows) == 2 ? 2 : 1) : pair_su(w, rows)) : 1;
+  const int su = reg ? 2
+                     : pairs ? (gated ? (pair_su(w, rows) == 2 && pair_su(w3, rows) == 2 ? 2 : 1) : pair_su(w, rows))
+                             : 1;
   GemvPlan plan;
   gemv_plan(w->n_out, w->k_in, rows, sms, pairs, &plan, gated, su);
   const size_t need = gemv_workspace_bytes(w, rows, sms);
@@ -225,12 +241,12 @@ int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* 
   p.gated = gated ? 1 : 0;
   p.su = su;
   // The register-fed pair kernel reads 32-byte pieces of the packed weights.
-  p.reg = (pairs && su == 2 && reg_eligible(w, w3, rows)) ? 1 : 0;
+  p.reg = reg ? 1 : 0;
   bool f16 = false;
   int st = act_type(opts, &f16);
   if (st) return st;
   if (f16 && (!p.reg || rk != nullptr))
-    return fail(NF4B_ERR_SHAPE, "fp16 is served here on the register-fed decode GEMV only (1..2 rows, blocksize 64, "
+    return fail(NF4B_ERR_SHAPE, "fp16 is served here on the register-fed decode GEMV only (1..8 rows, blocksize 64, "
                                 "k_in %% 256 == 0, 32-byte aligned packed codes)");
   p.f16 = f16 ? 1 : 0;
   if (rk != nullptr) {
@@ -246,7 +262,7 @@ int gemv_call(const nf4b_weight* w, const nf4b_weight* w3, const void* x, void* 
     p.rk_nkv = rk->n_kv;
     p.rk_max_len = rk->max_len;
   }
-  p.x_staged = (pairs && (long long)rows * w->k_in * 2 <= GEMV_PAIR_X_MAX) ? 1 : 0;
+  p.x_staged = (reg || (pairs && (long long)rows * w->k_in * 2 <= GEMV_PAIR_X_MAX)) ? 1 : 0;
   p.norm_w = opts ? static_cast<const uint16_t*>(opts->norm_weight) : nullptr;
   p.norm_eps = opts ? opts->norm_eps : 0.f;
   if (p.norm_w != nullptr && !p.x_staged)
@@ -293,8 +309,8 @@ size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows) {
   if (w == nullptr || rows <= 0 || w->n_out <= 0 || w->k_in <= 0) return 0;
   const int sms = current_sm_count();
   if (rows > GEMV_MAX_ROWS) return gemm_workspace_bytes(w->n_out, rows, w->k_in, sms);
-  // 1..32 rows: the GEMV's, or the GEMM's where an fp16 call goes there
-  const size_t a = gemv_workspace_bytes(w, rows, sms);
+  // 1..32 rows: the GEMV's, or the GEMM's where the call goes there
+  const size_t a = rows <= GEMV_REG_MAX_ROWS ? gemv_workspace_bytes(w, rows, sms) : 0;
   const size_t b = reg_eligible(w, nullptr, rows) ? 0 : gemm_workspace_bytes(w->n_out, rows, w->k_in, sms);
   return a > b ? a : b;
 }
@@ -322,12 +338,16 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
   if ((st = check_device())) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
-  // fp16: the register-fed GEMV for 1..2 rows where it applies, else the GEMM
-  // at any row count (the bf16-only GEMV kernels are not instantiated in fp16).
-  if (f16 ? reg_eligible(w, nullptr, rows) : rows <= GEMV_MAX_ROWS)
+  // The register-fed GEMV for 1..8 rows where it applies; otherwise bf16
+  // 1..8 rows on the TMA-ring pair kernel or the block kernel, and every other
+  // call (9+ rows, or fp16 outside the register-fed kernel's envelope: the
+  // other GEMV kernels are bf16 only) on the tcgen05 GEMM, which from 9 rows
+  // on beats the block kernel (2560x9728 at M = 32: 99 against 181 us per
+  // layer of five projections).
+  if (reg_eligible(w, nullptr, rows) || (!f16 && rows <= GEMV_REG_MAX_ROWS))
     return gemv_call(w, nullptr, x, y, rows, epi, operand, workspace, workspace_bytes, opts, s);
   if (opts != nullptr && opts->norm_weight != nullptr)
-    return fail(NF4B_ERR_SHAPE, "a fused RMSNorm is served for 1..4 rows (fp16: 1..2 rows) (got %d)", rows);
+    return fail(NF4B_ERR_SHAPE, "a fused RMSNorm is served by the decode GEMV only (got %d rows)", rows);
 
   GemmParams p = {};
   p.packed = w->packed;

@@ -184,15 +184,24 @@ __device__ __forceinline__ float rsqrt_exact(double ss, int width, float eps) {
 // squares (exact for bf16 inputs, so its order does not matter),
 // r = 1 / sqrt(fp32(ss / K) + eps), y = bf16(bf16(x * r) * w). Called by every
 // thread of the CTA after a barrier that made x visible; ends with a barrier.
-// `red` holds one double per warp. kPadded: row m starts at element
-// m * row_stride and every 64 elements are followed by 8 elements of padding.
-template <int THREADS, bool kPadded = false, bool F16 = false>
+// `red` holds one double per warp. Row m starts at element m * row_stride
+// (K for kLayout 0). kLayout 0: contiguous; 1: every 64 elements are followed
+// by 8 elements of padding; 2: each 64-element block's eight 8-element chunks
+// are rotated, chunk c of block b at chunk (c + (b & 3) + 4 (m & 1)) & 7.
+template <int THREADS, int kLayout = 0, bool F16 = false>
 __device__ __forceinline__ void rms_normalise_staged(uint16_t* xr, int M, int K, const uint16_t* __restrict__ w,
                                                      float eps, double* red, int row_stride = 0) {
   constexpr int NW = THREADS / 32;
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-  const int rs = kPadded ? row_stride : K;
-  auto at = [&](int m, int i) -> uint16_t& { return xr[m * rs + (kPadded ? i + ((i >> 6) << 3) : i)]; };
+  const int rs = kLayout ? row_stride : K;
+  auto at = [&](int m, int i) -> uint16_t& {
+    if (kLayout == 1) return xr[m * rs + i + ((i >> 6) << 3)];
+    if (kLayout == 2) {
+      const int b = i >> 6, c = (((i >> 3) & 7) + (b & 3) + 4 * (m & 1)) & 7;
+      return xr[m * rs + (b << 6) + (c << 3) + (i & 7)];
+    }
+    return xr[m * rs + i];
+  };
   for (int m = 0; m < M; ++m) {
     double ss = 0.0;
     for (int i = threadIdx.x; i < K; i += THREADS) {

@@ -47,10 +47,14 @@ constexpr int GEMV_PAIR_X_MAX = NF4B_GEMV_PAIR_X_KB * 1024;
 constexpr int GEMV_PAIR_SMEM_MAX = GEMV_PAIR_X_OFFSET + GEMV_PAIR_X_MAX;
 static_assert(GEMV_PAIR_W_OFFSET % 1024 == 0, "TMA boxes must be aligned");
 static_assert(GEMV_PAIR_SMEM_MAX <= 227 * 1024, "pair kernel shared memory exceeds one CTA's limit");
-// Register-fed pair kernel: the pair table, then x of <= 2 rows with 16 bytes
-// of padding per 128 and 64 per row.
-constexpr int GEMV_REG_SMEM_MAX = GEMV_LUT_BYTES + GEMV_PAIR_X_MAX * 9 / 8 + 128;
-static_assert(GEMV_REG_SMEM_MAX <= 227 * 1024, "register-fed pair kernel shared memory exceeds one CTA's limit");
+// Register-fed pair kernel: the pair table, then x of <= GEMV_REG_MAX_ROWS
+// rows (rows * k_in * 2 <= GEMV_REG_X_MAX bytes, chunk-rotated, no padding).
+// The GEMV chain's register-fed variant stages x with 16 bytes of padding per
+// 128 and 64 per row (reg_x_row_bytes) under the same dynamic limit.
+constexpr int GEMV_REG_SMEM_MAX = 227 * 1024 - 1024;  // 1 KB left for static shared memory
+constexpr int GEMV_REG_X_MAX = GEMV_REG_SMEM_MAX - GEMV_LUT_BYTES;
+constexpr int GEMV_REG_MAX_ROWS = 8;
+static_assert(GEMV_LUT_BYTES + GEMV_PAIR_X_MAX * 9 / 8 + 128 <= GEMV_REG_SMEM_MAX, "chain staging exceeds the limit");
 constexpr int GEMV_MAX_ROWS = 32;              // activation rows one launch takes
 // The workspace starts with a fixed-size region of per-tile arrival counters,
 // so calls on weights of different shapes never alias one another's counters

@@ -150,45 +150,56 @@ __device__ __forceinline__ void prefetch_next(const GemvParams& p, int gw, int l
 // ---------------------------------------------------------------------------
 
 // Sums of the `n` partial slots (stride `stride` floats) of one split tile,
-// for rows ra and rb of each of the H halves (`base` = slot 0, half h at
-// + h * MN): v[h][e] = (((0 + s0) + s1) + ... + s(n-1)) + v[h][e], slot order
-// whatever n is. All loads of a chunk of CH slots are issued before the first
-// add, so a tile reduced over <= CH slots costs one L2 round trip.
-template <int H>
+// for rows ra and rb of each of the H halves and of each of the NT activation
+// rows this lane finishes (row j at + j * jstride; only the first `live` of
+// them exist) (`base` = slot 0, half h at + h * MN): v[j][h][e] =
+// (((0 + s0) + s1) + ... + s(n-1)) + v[j][h][e], slot order whatever n is. All
+// loads of a chunk of CH slots are issued before the first add, so a tile
+// reduced over <= CH slots costs one L2 round trip.
+template <int H, int NT = 1>
 __device__ __forceinline__ void sum_tile_slots(const float* base, size_t MN, size_t stride, int n, int ra, int rb,
-                                               int N, float (&v)[2][2]) {
-  constexpr int CH = 16 / H;
-  float acc[H][2];
+                                               int N, size_t jstride, int live, float (&v)[NT][2][2]) {
+  constexpr int CH = (16 / (H * NT)) > 1 ? 16 / (H * NT) : 1;
+  float acc[NT][H][2];
 #pragma unroll
-  for (int h = 0; h < H; ++h) acc[h][0] = acc[h][1] = 0.f;
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int h = 0; h < H; ++h) acc[j][h][0] = acc[j][h][1] = 0.f;
   for (int c0 = 0; c0 < n; c0 += CH) {
-    float s[H][2][CH];
+    float s[NT][H][2][CH];
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-      const bool live = c0 + c < n;
-      const float* q = base + (size_t)(c0 + c) * stride;
 #pragma unroll
-      for (int h = 0; h < H; ++h) {
-        s[h][0][c] = (live && ra < N) ? __ldcg(q + h * MN + ra) : 0.f;
-        s[h][1][c] = (live && rb < N) ? __ldcg(q + h * MN + rb) : 0.f;
+      for (int j = 0; j < NT; ++j) {
+        const bool in = c0 + c < n && j < live;
+        const float* q = base + (size_t)(c0 + c) * stride + (size_t)j * jstride;
+#pragma unroll
+        for (int h = 0; h < H; ++h) {
+          s[j][h][0][c] = (in && ra < N) ? __ldcg(q + h * MN + ra) : 0.f;
+          s[j][h][1][c] = (in && rb < N) ? __ldcg(q + h * MN + rb) : 0.f;
+        }
       }
     }
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
       if (c0 + c < n) {
 #pragma unroll
-        for (int h = 0; h < H; ++h) {
-          acc[h][0] += s[h][0][c];
-          acc[h][1] += s[h][1][c];
-        }
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int h = 0; h < H; ++h) {
+            acc[j][h][0] += s[j][h][0][c];
+            acc[j][h][1] += s[j][h][1][c];
+          }
       }
     }
   }
 #pragma unroll
-  for (int h = 0; h < H; ++h) {
-    if (ra < N) v[h][0] = acc[h][0] + v[h][0];
-    if (rb < N) v[h][1] = acc[h][1] + v[h][1];
-  }
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int h = 0; h < H; ++h) {
+      if (ra < N) v[j][h][0] = acc[j][h][0] + v[j][h][0];
+      if (rb < N) v[j][h][1] = acc[j][h][1] + v[j][h][1];
+    }
 }
 
 // cp.async helpers (sm_80+ asynchronous global -> shared copies, tracked per
@@ -363,35 +374,42 @@ __device__ __forceinline__ void store_pair_tile(const GemvParams& p, int rt, int
 }
 
 // Finish row tile `rt` of the pair kernel from this warp's partial sums
-// v[half][row g / g + 8]. A tile inside the warp's run is stored at once
-// (returns false). A split tile is published as soon as the warp's part of it
-// is done: the partial goes to this warp's slot (slot = warp - first
-// contributing warp) and lane 0 counts the warp in with an acquire-release
-// atomic whose result (`old`, lane 0) is only looked at after the warp's run,
-// by finish_split_tile: no warp waits for another, and the last to arrive
-// reduces (returns true). (Publishing every split tile only after the run was
+// v[j][half][row g / g + 8] of activation rows t + 2j (j < NT; NT > 1 is the
+// register-fed kernel's several column tiles, whose lane holds every other
+// activation row). A tile inside the warp's run is stored at once (returns
+// false). A split tile is published as soon as the warp's part of it is done:
+// the partial goes to this warp's slot (slot = warp - first contributing
+// warp) and lane 0 counts the warp in with an acquire-release atomic whose
+// result (`old`, lane 0) is only looked at after the warp's run, by
+// finish_tile_rows: no warp waits for another, and the last to arrive reduces
+// (returns true). (Publishing every split tile only after the run was
 // measured slower: the first tile's reduction then no longer overlaps the run.)
-template <bool kGated, bool kF16 = false>
-__device__ __forceinline__ bool publish_pair_tile(const GemvParams& p, int rt, int u0, int u1, int gw, int g,
-                                                  int t, int lane, const float (&v)[2][2], int& old,
+template <bool kGated, bool kF16 = false, int NT = 1>
+__device__ __forceinline__ bool publish_tile_rows(const GemvParams& p, int rt, int u0, int u1, int gw, int g,
+                                                  int t, int lane, const float (*v)[2][2], int& old,
                                                   const RopeKv* rk = nullptr) {
   constexpr int H = kGated ? 2 : 1;
   const int per_tile = p.blocks_per_tile * H;
   const int t0 = rt * per_tile, t1 = t0 + per_tile - 1;
   if (t0 >= u0 && t1 < u1) {
-    store_pair_tile<kGated, kF16>(p, rt, g, t, v, rk);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) store_pair_tile<kGated, kF16>(p, rt, g, t + 2 * j, v[j], rk);
     return false;
   }
   const int w_lo = warp_of(t0, p.uq, p.ur);
   const int N = p.N, M = p.M;
   const int ra = rt * 16 + g, rb = ra + 8;
   const size_t MN = (size_t)M * N;
-  float* slot = p.partial + (size_t)(gw - w_lo) * H * MN + (size_t)t * N;
-  if (t < M) {
 #pragma unroll
-    for (int h = 0; h < H; ++h) {
-      if (ra < N) __stcg(slot + h * MN + ra, v[h][0]);
-      if (rb < N) __stcg(slot + h * MN + rb, v[h][1]);
+  for (int j = 0; j < NT; ++j) {
+    const int row = t + (NT > 1 ? 2 * j : 0);
+    if (row < M) {
+      float* slot = p.partial + (size_t)(gw - w_lo) * H * MN + (size_t)row * N;
+#pragma unroll
+      for (int h = 0; h < H; ++h) {
+        if (ra < N) __stcg(slot + h * MN + ra, v[j][h][0]);
+        if (rb < N) __stcg(slot + h * MN + rb, v[j][h][1]);
+      }
     }
   }
   // The warp barrier orders every lane's partial before lane 0's release.
@@ -400,14 +418,23 @@ __device__ __forceinline__ bool publish_pair_tile(const GemvParams& p, int rt, i
   return true;
 }
 
+template <bool kGated, bool kF16 = false>
+__device__ __forceinline__ bool publish_pair_tile(const GemvParams& p, int rt, int u0, int u1, int gw, int g,
+                                                  int t, int lane, const float (&v)[2][2], int& old,
+                                                  const RopeKv* rk = nullptr) {
+  return publish_tile_rows<kGated, kF16, 1>(p, rt, u0, u1, gw, g, t, lane, &v, old, rk);
+}
+
 // After the warp's run: if it was the last of split tile rt's contributors to
 // arrive, sum every slot in slot order, (((0 + s0) + s1) + ...), and store -
 // the residual or gate operand is fetched in the same round trip as the
-// slots - then re-zero the counter for the next launch.
-template <bool kGated, bool kF16 = false>
-__device__ __forceinline__ void finish_split_tile(const GemvParams& p, int rt, int old, int g, int t, int lane,
-                                                  const RopeKv* rk = nullptr) {
+// slots - then re-zero the counter for the next launch. Rows as
+// publish_tile_rows.
+template <bool kGated, bool kF16 = false, int NT = 1>
+__device__ __forceinline__ void finish_tile_rows(const GemvParams& p, int rt, int old, int g, int t, int lane,
+                                                 const RopeKv* rk = nullptr) {
   constexpr int H = kGated ? 2 : 1;
+  constexpr int JS = NT > 1 ? 2 : 0;  // activation-row step between column tiles
   const int per_tile = p.blocks_per_tile * H;
   const int t0 = rt * per_tile;
   const int n = warp_of(t0 + per_tile - 1, p.uq, p.ur) - warp_of(t0, p.uq, p.ur) + 1;
@@ -418,24 +445,44 @@ __device__ __forceinline__ void finish_split_tile(const GemvParams& p, int rt, i
   const size_t MN = (size_t)M * N;
   if (lane == 0) p.counters[rt] = 0;
   if (t >= M) return;
-  const size_t oa = (size_t)t * N + ra, ob = (size_t)t * N + rb;
+  const int live = NT > 1 ? (M - t + 1) / 2 : 1;  // rows t, t + 2, ... below M
   const bool opnd = !kGated && p.epi != NF4B_EPI_NONE;
-  const uint16_t opa = (opnd && ra < N) ? __ldcg(p.operand + oa) : (uint16_t)0;
-  const uint16_t opb = (opnd && rb < N) ? __ldcg(p.operand + ob) : (uint16_t)0;
-  float v[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-  sum_tile_slots<H>(p.partial + (size_t)t * N, MN, H * MN, n, ra, rb, N, v);
-  if (kGated) {
-    if (ra < N) p.y[oa] = gate_bf16<kF16>(v[0][0], v[1][0]);
-    if (rb < N) p.y[ob] = gate_bf16<kF16>(v[0][1], v[1][1]);
-  } else if (rk != nullptr) {  // one activation row, n_out % 16 == 0 (bf16 only)
-    const bf16_t ya = epilogue_value(v[0][0], p.epi, bf2f(opa)), yb = epilogue_value(v[0][1], p.epi, bf2f(opb));
-    p.y[oa] = ya;
-    p.y[ob] = yb;
-    rope_kv_rows(p, *rk, ra, rb, ya, yb);
-  } else {
-    if (ra < N) p.y[oa] = epilogue_value<kF16>(v[0][0], p.epi, act2f<kF16>(opa));
-    if (rb < N) p.y[ob] = epilogue_value<kF16>(v[0][1], p.epi, act2f<kF16>(opb));
+  uint16_t opa[NT], opb[NT];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    const size_t oa = (size_t)(t + JS * j) * N + ra, ob = (size_t)(t + JS * j) * N + rb;
+    const bool in = opnd && j < live;
+    opa[j] = (in && ra < N) ? __ldcg(p.operand + oa) : (uint16_t)0;
+    opb[j] = (in && rb < N) ? __ldcg(p.operand + ob) : (uint16_t)0;
   }
+  float v[NT][2][2];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) v[j][0][0] = v[j][0][1] = v[j][1][0] = v[j][1][1] = 0.f;
+  sum_tile_slots<H, NT>(p.partial + (size_t)t * N, MN, H * MN, n, ra, rb, N, (size_t)JS * N, live, v);
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    if (j >= live) break;
+    const size_t oa = (size_t)(t + JS * j) * N + ra, ob = (size_t)(t + JS * j) * N + rb;
+    if (kGated) {
+      if (ra < N) p.y[oa] = gate_bf16<kF16>(v[j][0][0], v[j][1][0]);
+      if (rb < N) p.y[ob] = gate_bf16<kF16>(v[j][0][1], v[j][1][1]);
+    } else if (rk != nullptr) {  // one activation row, n_out % 16 == 0 (bf16 only)
+      const bf16_t ya = epilogue_value(v[j][0][0], p.epi, bf2f(opa[j]));
+      const bf16_t yb = epilogue_value(v[j][0][1], p.epi, bf2f(opb[j]));
+      p.y[oa] = ya;
+      p.y[ob] = yb;
+      rope_kv_rows(p, *rk, ra, rb, ya, yb);
+    } else {
+      if (ra < N) p.y[oa] = epilogue_value<kF16>(v[j][0][0], p.epi, act2f<kF16>(opa[j]));
+      if (rb < N) p.y[ob] = epilogue_value<kF16>(v[j][0][1], p.epi, act2f<kF16>(opb[j]));
+    }
+  }
+}
+
+template <bool kGated, bool kF16 = false>
+__device__ __forceinline__ void finish_split_tile(const GemvParams& p, int rt, int old, int g, int t, int lane,
+                                                  const RopeKv* rk = nullptr) {
+  finish_tile_rows<kGated, kF16, 1>(p, rt, old, g, t, lane, rk);
 }
 
 // A warp that gave up on a wait while computing unit tile `rt_now` of its run
@@ -805,42 +852,60 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   if (!NF4B_GEMV_PREFETCH_EARLY) prefetch_next(p, gw, lane);
 }
 
+// A 16-byte shared-memory load into v when `pred`; v keeps its value otherwise
+// (the destination registers are read-write, so no zero-fill is issued).
+__device__ __forceinline__ void ld_shared_u4_if(bool pred, uint32_t addr, uint4& v) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t@p ld.shared.v4.u32 {%0, %1, %2, %3}, [%5];\n\t}"
+      : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w)
+      : "r"((int)pred), "r"(addr));
+}
+
 // ---------------------------------------------------------------------------
-// register-fed pair kernel: units of 16 rows x 256 codes, activation rows <= 2
+// register-fed pair kernel: units of 16 rows x 256 codes, activation rows <= 8
 // ---------------------------------------------------------------------------
 //
-// The decode case (1 or 2 activation rows, blocksize 64, k_in % 256 == 0). The
+// The decode case (1..8 activation rows, blocksize 64, k_in % 256 == 0). The
 // units, runs and the split-tile protocol are the pair kernel's (SU = 2), but
 // the weights skip shared memory: lane (g, t) loads 64-block t of the unit for
 // rows g and g + 8 with one 256-bit load each straight into registers, three
-// units in flight per warp. Shared memory then carries only the pair table,
-// the scale codes' code2 values and x, which is what bounds the pair kernel's
-// consumer (its TMA ring costs a shared-memory write and a read per weight byte).
+// units in flight per warp (two with several column tiles). Shared memory then
+// carries only the pair table, the scale codes' code2 values and x, which is
+// what bounds the pair kernel's consumer (its TMA ring costs a shared-memory
+// write and a read per weight byte).
 //
-// MMA columns are (activation row, block): column 4m + b carries x of row m
-// over block b of the unit, so one MMA chain keeps the four blocks' sums apart
-// and each gets its own scale after the unit. Lane (g, t) holds columns 2t and
-// 2t + 1 - activation row t >> 1, blocks 2(t & 1) and 2(t & 1) + 1 - and
-// supplies x for column g (row g >> 2, block g & 3) when g & 3 == t. Lanes t
-// and t ^ 1 hold a row's two half-sums; they are added when a tile is finished.
+// MMA columns are (activation row, block): column 4m + b of column tile j
+// carries x of row 2j + m over block b of the unit, so one MMA chain per tile
+// keeps the unit's four block sums apart and each gets its own scale after the
+// unit. Lane (g, t) holds columns 2t and 2t + 1 of every tile - activation
+// rows 2j + (t >> 1), blocks 2(t & 1) and 2(t & 1) + 1 - and supplies x for
+// column g (row 2j + (g >> 2), block g & 3) when g & 3 == t. Lanes t and t ^ 1
+// hold a row's two half-sums; they are added when a tile is finished. NT = 1,
+// 2, 4 column tiles serve 1-2, 3-4 and 5-8 rows: the weights are decoded once
+// (the pair-table lookups are the same) whatever the row count.
 //
 // Shared memory: the pair table (entry e's 32 per-lane copies at e * 256), the
 // code2 value of scale code e at e * 256 + 128 + 4 * (2g + (t & 1)) (16 copies,
-// so a warp's lookups never conflict; W3's at + 192), then x with 16 bytes of
-// padding after every 128 (one 64-block), so the four x lanes of a load hit
-// different banks.
+// so a warp's lookups never conflict; W3's at + 192), then x, rows of k_in * 2
+// bytes, each 64-block's eight 16-byte chunks rotated: chunk c of block b of
+// row m sits at chunk (c + (b & 3) + 4 (m & 1)) & 7 of the block's 128 bytes,
+// so the eight x lanes of a load (four blocks, two rows) hit eight different
+// bank groups with no padding (rows * k_in * 2 <= GEMV_REG_X_MAX).
 // kRope: the fused rotary + KV-cache store of a wqkv projection (one
 // activation row, not gated, bf16). kF16: fp16 activations and outputs (the
 // pair table holds fp16 code pairs and the MMA is f16 x f16).
-template <bool kGated, bool kNested, bool kRope = false, bool kF16 = false>
+template <bool kGated, bool kNested, bool kRope = false, bool kF16 = false, int NT = 1>
 __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     nf4_gemv_reg_kernel(const __grid_constant__ GemvParams p) {
   constexpr int kT = GEMV_PAIR_WARPS * 32;
+  constexpr int kDepth = NT == 1 ? kRegDepth : 2;  // units in flight per warp
+  constexpr int CH = NT == 1 ? 2 : 1;              // MMA chains per column tile
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ double norm_red[GEMV_PAIR_WARPS];
   __shared__ float rk_f[kRope ? 128 : 1];  // kRope: this token's rotary row
   static_assert(!(kRope && kGated), "the fused rotary store serves a plain projection");
-  static_assert(!(kRope && kF16), "the fused rotary store is bf16");
+  static_assert(!(kRope && (kF16 || NT > 1)), "the fused rotary store is bf16, one row");
+  static_assert(NT == 1 || NT == 2 || NT == 4, "1, 2 or 4 column tiles");
   const uint8_t* lut = smem;
   uint8_t* xs = smem + GEMV_LUT_BYTES;
 
@@ -856,7 +921,7 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
   const int nblk = K >> 6;  // 64-blocks per weight row
   const int bs2 = p.bs2_shift;
   constexpr bool nested = kNested;
-  const int xrow = reg_x_row_bytes(K);
+  const int xrow = K * 2;
 
   // Load cursor: tile lt, half lh, unit lk; rows past n_out re-read row
   // n_out - 1 (their outputs are never stored).
@@ -905,9 +970,9 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     }
   };
 
-  RegSlot sl[kRegDepth];
+  RegSlot sl[kDepth];
 #pragma unroll
-  for (int d = 0; d < kRegDepth; ++d)
+  for (int d = 0; d < kDepth; ++d)
     if (u0 + d < u1) load(sl[d]);
 
   // The pair table, built while the first units are in flight; the code2
@@ -927,32 +992,60 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
     if (threadIdx.x < 128) rk_val = load_freq(p.rk_freqs, threadIdx.x, p.rk_ftype);
     rk_pos = p.rk_pos[0];
   }
-  // x, written by earlier work on the stream, staged with the padding.
+  // x, written by earlier work on the stream, staged in the rotated layout:
+  // x is [M, k_in] contiguous, so the rows form one run of 16-byte chunks,
+  // and each thread issues up to 8 of its chunks' loads before storing any
+  // (one L2 round trip per 8 x 8 KB instead of one per row).
   {
-    const int n16 = K >> 3;
-    for (int m = 0; m < M; ++m) {
-      const uint4* src = reinterpret_cast<const uint4*>(p.x) + (size_t)m * n16;
-      for (int c = threadIdx.x; c < n16; c += kT)
-        *reinterpret_cast<uint4*>(xs + m * xrow + c * 16 + (c >> 3) * 16) = __ldcg(src + c);
+    constexpr int kBatch = 8;
+    const int n16 = K >> 3, total = M * n16;
+    const uint4* src = reinterpret_cast<const uint4*>(p.x);
+    for (int base = threadIdx.x; base < total; base += kBatch * kT) {
+      uint4 v[kBatch];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b)
+        if (base + b * kT < total) v[b] = __ldcg(src + base + b * kT);
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int i = base + b * kT;
+        if (i < total) {
+          const int m = i / n16, c = i - m * n16;
+          const int blk = c >> 3, rot = ((c & 7) + (blk & 3) + 4 * (m & 1)) & 7;
+          *reinterpret_cast<uint4*>(xs + m * xrow + blk * 128 + rot * 16) = v[b];
+        }
+      }
     }
   }
   if (kRope && threadIdx.x < 128) rk_f[threadIdx.x] = rk_val;
   __syncthreads();
   if (p.norm_w != nullptr)
-    rms_normalise_staged<kT, true, kF16>(reinterpret_cast<uint16_t*>(xs), M, K, p.norm_w, p.norm_eps, norm_red,
-                                         xrow / 2);
+    rms_normalise_staged<kT, 2, kF16>(reinterpret_cast<uint16_t*>(xs), M, K, p.norm_w, p.norm_eps, norm_red,
+                                      xrow / 2);
 
   const uint32_t lane_base = (uint32_t)lane * 4u;
   const uint32_t c2_base = 128u + (uint32_t)(2 * g + (t & 1)) * 4u;
   const uint32_t qsel0 = 0x5504u | ((uint32_t)(2 * (t & 1)) << 4);
   const uint32_t qsel1 = 0x5504u | ((uint32_t)(2 * (t & 1) + 1) << 4);
-  const int xtok = g >> 2;
-  const bool xlane = (xtok < M) && ((g & 3) == t);
-  const uint8_t* xb = xs + (xlane ? xtok : 0) * xrow + t * 144;
-  const int tok = (t & 1) ? 7 : (t >> 1);  // the activation row this lane publishes (7: none)
+  // x lane: block t of rows 2j + (g >> 2); its chunks are rotated by xrot.
+  const bool xsup = (g & 3) == t;
+  const int xr0 = g >> 2;
+  const uint32_t xrot = (uint32_t)(t + 4 * xr0);
+  const uint32_t xb_s = smem_addr(xs + xr0 * xrow + t * 128);
+  // Lanes that supply no x for tile j keep zeros in its B registers: the
+  // loads are predicated, so the zeros are written once.
+  bool xld[NT];
+  uint4 xq[NT];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    xld[j] = xsup && 2 * j + xr0 < M;
+    xq[j] = make_uint4(0, 0, 0, 0);
+  }
+  const int tok = (t & 1) ? 64 : (t >> 1);  // the first activation row this lane publishes (64: none)
 
-  float acc_a = 0.f, acc_b = 0.f;    // W (or W1): rows g, g + 8
-  float acc3_a = 0.f, acc3_b = 0.f;  // gated pair: W3
+  float acc_a[NT], acc_b[NT];    // W (or W1): rows g, g + 8 of activation rows tok + 2j
+  float acc3_a[NT], acc3_b[NT];  // gated pair: W3
+#pragma unroll
+  for (int j = 0; j < NT; ++j) acc_a[j] = acc_b[j] = acc3_a[j] = acc3_b[j] = 0.f;
   int split_a = -1, split_b = -1, old_a = 0, old_b = 0;
   auto compute = [&](const RegSlot& s, int u) {
     const int rt = ct, kb = ck, hh = ch;
@@ -980,21 +1073,21 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       s0b = __uint_as_float(s.qb);
       s1b = __uint_as_float(s.sb);
     }
-    // Two independent MMA chains (even and odd k steps); x in two halves of
-    // 64 bytes (fewer live registers).
-    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-    uint4 xv[4];
+    // NT == 1: two independent MMA chains (even and odd k steps); several
+    // column tiles are independent chains already. x of a tile: one 16-byte
+    // chunk (8 codes) per two steps.
+    float d[NT][CH][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int c = 0; c < CH; ++c) d[j][c][0] = d[j][c][1] = d[j][c][2] = d[j][c][3] = 0.f;
+    const uint32_t xu = xb_s + (uint32_t)kb * 512u;
 #pragma unroll
     for (int st = 0; st < 16; ++st) {
-      if ((st & 7) == 0) {
-        if (xlane) {
-          const uint4* xr = reinterpret_cast<const uint4*>(xb + kb * 576 + (st >> 3) * 64);
+      if ((st & 1) == 0) {
+        const uint32_t off = (((uint32_t)(st >> 1) + xrot) & 7u) * 16u;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) xv[j] = xr[j];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) xv[j] = make_uint4(0, 0, 0, 0);
-        }
+        for (int j = 0; j < NT; ++j) ld_shared_u4_if(xld[j], xu + (uint32_t)(2 * j * xrow) + off, xq[j]);
       }
       const uint32_t w0 = s.wa[st >> 1], w1 = s.wb[st >> 1];
       const int j0 = 2 * (st & 1);
@@ -1002,35 +1095,50 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
       const uint32_t a2 = lut_lookup(lut, w0, lut_sel(j0 + 1), lane_base);
       const uint32_t a1 = lut_lookup(lut, w1, lut_sel(j0), lane_base);
       const uint32_t a3 = lut_lookup(lut, w1, lut_sel(j0 + 1), lane_base);
-      const uint4& xq = xv[(st >> 1) & 3];
-      const uint32_t b0 = (st & 1) ? xq.z : xq.x;
-      const uint32_t b1 = (st & 1) ? xq.w : xq.y;
-      if (st & 1)
-        mma_act<kF16>(d1, a0, a1, a2, a3, b0, b1);
-      else
-        mma_act<kF16>(d0, a0, a1, a2, a3, b0, b1);
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const uint32_t b0 = (st & 1) ? xq[j].z : xq[j].x;
+        const uint32_t b1 = (st & 1) ? xq[j].w : xq[j].y;
+        mma_act<kF16>(d[j][CH == 2 ? (st & 1) : 0], a0, a1, a2, a3, b0, b1);
+      }
     }
-    // d[0] = (row g, block 2(t & 1)), d[1] = its successor; d[2], d[3] for row g + 8.
-    const float ya = fmaf(s1a, d0[1] + d1[1], (d0[0] + d1[0]) * s0a);
-    const float yb = fmaf(s1b, d0[3] + d1[3], (d0[2] + d1[2]) * s0b);
-    if (kGated && hh) {
-      acc3_a += ya;
-      acc3_b += yb;
-    } else {
-      acc_a += ya;
-      acc_b += yb;
+    // d[.][0] = (row g, block 2(t & 1)), d[.][1] = its successor; d[.][2], d[.][3] for row g + 8.
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      float e0 = d[j][0][0], e1 = d[j][0][1], e2 = d[j][0][2], e3 = d[j][0][3];
+      if (CH == 2) {
+        e0 += d[j][CH - 1][0];
+        e1 += d[j][CH - 1][1];
+        e2 += d[j][CH - 1][2];
+        e3 += d[j][CH - 1][3];
+      }
+      const float ya = fmaf(s1a, e1, e0 * s0a);
+      const float yb = fmaf(s1b, e3, e2 * s0b);
+      if (kGated && hh) {
+        acc3_a[j] += ya;
+        acc3_b[j] += yb;
+      } else {
+        acc_a[j] += ya;
+        acc_b[j] += yb;
+      }
     }
     if ((kb == B - 1 && (!kGated || hh == 1)) || u == u1 - 1) {
-      acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 1);
-      acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 1);
-      if (kGated) {
-        acc3_a += __shfl_xor_sync(0xffffffffu, acc3_a, 1);
-        acc3_b += __shfl_xor_sync(0xffffffffu, acc3_b, 1);
+      float v[NT][2][2];
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        v[j][0][0] = acc_a[j] + __shfl_xor_sync(0xffffffffu, acc_a[j], 1);
+        v[j][0][1] = acc_b[j] + __shfl_xor_sync(0xffffffffu, acc_b[j], 1);
+        if (kGated) {
+          v[j][1][0] = acc3_a[j] + __shfl_xor_sync(0xffffffffu, acc3_a[j], 1);
+          v[j][1][1] = acc3_b[j] + __shfl_xor_sync(0xffffffffu, acc3_b[j], 1);
+        } else {
+          v[j][1][0] = v[j][1][1] = 0.f;
+        }
+        acc_a[j] = acc_b[j] = acc3_a[j] = acc3_b[j] = 0.f;
       }
-      const float v[2][2] = {{acc_a, acc_b}, {acc3_a, acc3_b}};
       int old = 0;
       const RopeKv rk{rk_f, rk_pos};
-      if (publish_pair_tile<kGated, kF16>(p, rt, u0, u1, gw, g, tok, lane, v, old, kRope ? &rk : nullptr)) {
+      if (publish_tile_rows<kGated, kF16, NT>(p, rt, u0, u1, gw, g, tok, lane, v, old, kRope ? &rk : nullptr)) {
         if (split_a < 0) {
           split_a = rt;
           old_a = old;
@@ -1039,22 +1147,21 @@ __global__ void __launch_bounds__(GEMV_PAIR_WARPS * 32, 1)
           old_b = old;
         }
       }
-      acc_a = acc_b = acc3_a = acc3_b = 0.f;
     }
   };
 
-  for (int u = u0; u < u1; u += kRegDepth) {
+  for (int u = u0; u < u1; u += kDepth) {
 #pragma unroll
-    for (int d = 0; d < kRegDepth; ++d) {
-      if (u + d < u1) {
-        compute(sl[d], u + d);
-        if (u + d + kRegDepth < u1) load(sl[d]);
+    for (int dd = 0; dd < kDepth; ++dd) {
+      if (u + dd < u1) {
+        compute(sl[dd], u + dd);
+        if (u + dd + kDepth < u1) load(sl[dd]);
       }
     }
   }
   const RopeKv rk{rk_f, rk_pos};
-  if (split_a >= 0) finish_split_tile<kGated, kF16>(p, split_a, old_a, g, tok, lane, kRope ? &rk : nullptr);
-  if (split_b >= 0) finish_split_tile<kGated, kF16>(p, split_b, old_b, g, tok, lane, kRope ? &rk : nullptr);
+  if (split_a >= 0) finish_tile_rows<kGated, kF16, NT>(p, split_a, old_a, g, tok, lane, kRope ? &rk : nullptr);
+  if (split_b >= 0) finish_tile_rows<kGated, kF16, NT>(p, split_b, old_b, g, tok, lane, kRope ? &rk : nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -2001,45 +2108,53 @@ cudaError_t launch_gemv_chain(const ChainParams& p, cudaStream_t stream) {
   return p.reg ? cudaLaunchKernelEx(&cfg, nf4_gemv_reg_chain_kernel, p) : cudaLaunchKernelEx(&cfg, nf4_gemv_chain_kernel, p);
 }
 
+// The register-fed kernel's instantiation for (gated, nested, fp16, column tiles).
+template <bool kGated, bool kNested, bool kF16, int NT>
+cudaError_t launch_reg_nt(const GemvParams& p, int grid, cudaStream_t stream, int smem) {
+  static bool configured[64] = {};
+  return launch_kernel(nf4_gemv_reg_kernel<kGated, kNested, false, kF16, NT>, p, grid, stream, configured, smem,
+                       GEMV_REG_SMEM_MAX, GEMV_PAIR_WARPS * 32);
+}
+
+template <bool kGated, bool kNested, bool kF16>
+cudaError_t launch_reg_tiles(const GemvParams& p, int grid, cudaStream_t stream, int smem, int tiles) {
+  if (tiles == 1) return launch_reg_nt<kGated, kNested, kF16, 1>(p, grid, stream, smem);
+  if (tiles == 2) return launch_reg_nt<kGated, kNested, kF16, 2>(p, grid, stream, smem);
+  return launch_reg_nt<kGated, kNested, kF16, 4>(p, grid, stream, smem);
+}
+
+template <bool kF16>
+cudaError_t launch_reg_act(const GemvParams& p, int grid, cudaStream_t stream, int smem, int tiles) {
+  if (p.gated)
+    return p.nested ? launch_reg_tiles<true, true, kF16>(p, grid, stream, smem, tiles)
+                    : launch_reg_tiles<true, false, kF16>(p, grid, stream, smem, tiles);
+  return p.nested ? launch_reg_tiles<false, true, kF16>(p, grid, stream, smem, tiles)
+                  : launch_reg_tiles<false, false, kF16>(p, grid, stream, smem, tiles);
+}
+
+cudaError_t launch_reg(const GemvParams& p, int grid, cudaStream_t stream, int smem, int tiles) {
+  return p.f16 ? launch_reg_act<true>(p, grid, stream, smem, tiles) : launch_reg_act<false>(p, grid, stream, smem, tiles);
+}
+
 cudaError_t launch_gemv(const GemvParams& p, int grid, bool pairs, cudaStream_t stream) {
   static bool cfg_pair[64] = {}, cfg_gated[64] = {}, cfg_pair2[64] = {}, cfg_gated2[64] = {};
-  static bool cfg_reg[64] = {}, cfg_reg_gated[64] = {}, cfg_reg_plain[64] = {}, cfg_reg_gated_plain[64] = {};
   static bool cfg1[64] = {}, cfg2[64] = {}, cfg4[64] = {};
-  if (pairs && p.reg && p.f16) {
-    const int smem = GEMV_LUT_BYTES + p.M * reg_x_row_bytes(p.K);
-    const int nt = GEMV_PAIR_WARPS * 32;
-    static bool h_reg[64] = {}, h_gated[64] = {}, h_plain[64] = {}, h_gated_plain[64] = {};
-    if (p.rk_q != nullptr) return cudaErrorInvalidValue;
-    if (p.nested)
-      return p.gated ? launch_kernel(nf4_gemv_reg_kernel<true, true, false, true>, p, grid, stream, h_gated, smem,
-                                     GEMV_REG_SMEM_MAX, nt)
-                     : launch_kernel(nf4_gemv_reg_kernel<false, true, false, true>, p, grid, stream, h_reg, smem,
-                                     GEMV_REG_SMEM_MAX, nt);
-    return p.gated ? launch_kernel(nf4_gemv_reg_kernel<true, false, false, true>, p, grid, stream, h_gated_plain,
-                                   smem, GEMV_REG_SMEM_MAX, nt)
-                   : launch_kernel(nf4_gemv_reg_kernel<false, false, false, true>, p, grid, stream, h_plain, smem,
-                                   GEMV_REG_SMEM_MAX, nt);
-  }
-  if (p.f16) return cudaErrorInvalidValue;  // fp16 is served by the register-fed kernel only
   if (pairs && p.reg) {
-    const int smem = GEMV_LUT_BYTES + p.M * reg_x_row_bytes(p.K);
+    // column tiles: 1 for 1-2 rows, 2 for 3-4, 4 for 5-8
+    const int smem = GEMV_LUT_BYTES + p.M * p.K * 2;
     const int nt = GEMV_PAIR_WARPS * 32;
-    static bool cfg_rope[64] = {}, cfg_rope_plain[64] = {};
-    if (p.rk_q != nullptr)
+    const int tiles = p.M <= 2 ? 1 : p.M <= 4 ? 2 : 4;
+    if (p.rk_q != nullptr) {
+      static bool cfg_rope[64] = {}, cfg_rope_plain[64] = {};
+      if (p.f16 || tiles != 1) return cudaErrorInvalidValue;
       return p.nested ? launch_kernel(nf4_gemv_reg_kernel<false, true, true>, p, grid, stream, cfg_rope, smem,
                                       GEMV_REG_SMEM_MAX, nt)
                       : launch_kernel(nf4_gemv_reg_kernel<false, false, true>, p, grid, stream, cfg_rope_plain, smem,
                                       GEMV_REG_SMEM_MAX, nt);
-    if (p.nested)
-      return p.gated ? launch_kernel(nf4_gemv_reg_kernel<true, true>, p, grid, stream, cfg_reg_gated, smem,
-                                     GEMV_REG_SMEM_MAX, nt)
-                     : launch_kernel(nf4_gemv_reg_kernel<false, true>, p, grid, stream, cfg_reg, smem,
-                                     GEMV_REG_SMEM_MAX, nt);
-    return p.gated ? launch_kernel(nf4_gemv_reg_kernel<true, false>, p, grid, stream, cfg_reg_gated_plain, smem,
-                                   GEMV_REG_SMEM_MAX, nt)
-                   : launch_kernel(nf4_gemv_reg_kernel<false, false>, p, grid, stream, cfg_reg_plain, smem,
-                                   GEMV_REG_SMEM_MAX, nt);
+    }
+    return launch_reg(p, grid, stream, smem, tiles);
   }
+  if (p.f16) return cudaErrorInvalidValue;  // fp16 is served by the register-fed kernel only
   if (pairs) {
     GemvParams q = p;
     const uint64_t rb = (uint64_t)p.K / 2;

@@ -24,8 +24,8 @@
 // (cudaMemsetAsync on the call's stream) before launching, so stale contents
 // are harmless for calls ordered on one stream; calls that overlap on the GPU
 // (other streams, other threads) race on the same bytes and must not be issued.
-// GEMV calls whose partial sums would not fit are rejected. More than 32
-// activation rows run the tensor-core GEMM: it takes the scratch for its
+// GEMV calls (1..8 activation rows) whose partial sums would not fit are
+// rejected. More rows run the tensor-core GEMM: it takes the scratch for its
 // split-K partial sums when they fit (so it splits exactly as nf4b_gemm with a
 // workspace does) and otherwise runs unsplit.
 
@@ -53,7 +53,7 @@ extern "C" int nf4b_gemm_noalloc(const nf4b_weight* w, const void* x, void* y, i
   const size_t need = nf4b_gemm_workspace_size(w, rows);
   if (need == 0)  // an unsplit GEMM, or an invalid weight / row count that nf4b_gemm reports
     return nf4b_gemm(w, x, y, rows, epi, operand, nullptr, 0, stream);
-  if (rows > nf4b::GEMV_MAX_ROWS && need > (size_t)NF4B_NOALLOC_SCRATCH_BYTES)  // GEMM: run unsplit
+  if (rows > nf4b::GEMV_REG_MAX_ROWS && need > (size_t)NF4B_NOALLOC_SCRATCH_BYTES)  // GEMM: run unsplit
     return nf4b_gemm(w, x, y, rows, epi, operand, nullptr, 0, stream);
   if (need > (size_t)NF4B_NOALLOC_SCRATCH_BYTES) {
     char msg[256];

@@ -7,16 +7,17 @@ declined" convention (app/engine/nf4gemv.py:315-376, :427-479). The kernels
 are nvcc-built sm_100a code in ``libnf4b200.so`` behind a C ABI
 (``include/nf4b200.h``) instead of NVRTC + ctypes driver launches:
 
-* up to ``MAX_N`` (32) activation rows: the streaming GEMV (mma.sync fragments
-  fed from a shared-memory NF4 pair table, persistent SM-balanced grid);
-* more rows: the tcgen05 GEMM (TMA, bit-exact bf16 dequantisation into shared
+* 1..8 activation rows: the streaming GEMV (mma.sync fragments fed from a
+  shared-memory NF4 pair table, persistent SM-balanced grid; the register-fed
+  kernel decodes each weight once for all rows);
+* more rows: the tcgen05 GEMM (TMA, bit-exact dequantisation into shared
   memory, TMEM accumulators) - one launch for the whole prompt, where the
   reference slices it into 32-row launches (app/engine/nf4gemv.py:460-478).
 
 Activations are bf16 or fp16. fp16 is the reference's only GPU dtype
 (app/engine/nf4gemv.py:439, its TTS_HALF default): ``matmul`` serves it with
 the same rounding points as its kernel (fp32 accumulation, the output and each
-epilogue op rounded to fp16) - on the register-fed decode GEMV for 1..2 rows
+epilogue op rounded to fp16) - on the register-fed decode GEMV for 1..8 rows
 and on the tcgen05 GEMM for every other row count. bf16 follows the bf16
 rounding points of app/engine/nf4cpu.py; ``matmul_qkv_rope``, the chain and the
 decode step are bf16 only. Other dtypes are declined (None), as the reference
@@ -193,19 +194,23 @@ def prepare(module) -> bool:
     return True
 
 
-#: Largest x (rows * in_features * 2 bytes) the decode GEMV stages in shared
-#: memory, and so the largest a fused RMSNorm serves.
+#: Largest x (rows * in_features * 2 bytes) the TMA-ring pair GEMV stages in
+#: shared memory (1..4 rows), and the register-fed GEMV's limits (1..8 rows of
+#: blocksize-64 weights with in_features % 256 == 0): a fused RMSNorm is
+#: served within them.
 NORM_X_MAX = 40 * 1024
+REG_MAX_ROWS = 8
+REG_X_MAX = 227 * 1024 - 1024 - 256 * 256
 
 
 def _norm_ok(norm, rows: int, K: int, device, dtype=None) -> bool:
-    """Whether `norm` = (weight, eps) can be fused into a decode GEMV of this shape."""
+    """Whether `norm` = (weight, eps) may be fused into a decode GEMV of this
+    shape; the library makes the final call (NF4B_ERR_SHAPE = declined)."""
     import torch
 
     w = norm[0]
     dtype = torch.bfloat16 if dtype is None else dtype
-    max_rows = 2 if dtype == torch.float16 else 4
-    return (1 <= rows <= max_rows and K % 128 == 0 and rows * K * 2 <= NORM_X_MAX and w.dtype == dtype
+    return (1 <= rows <= REG_MAX_ROWS and K % 128 == 0 and rows * K * 2 <= REG_X_MAX and w.dtype == dtype
             and w.is_contiguous() and w.numel() == K and w.device == device)
 
 
@@ -237,10 +242,10 @@ def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None, norm=
     prepared linears that later calls will read: their weights are streamed
     into L2 while this call runs. `norm` (an extension) = (weight, eps):
     ``rms_norm(x) @ W.T`` in the same launch, bit-exact to
-    ``fusedops.rms_norm`` then ``matmul``; served for 1..4 rows (fp16: 1..2
-    rows on the register-fed GEMV) with in_features % 128 == 0 and x within
-    NORM_X_MAX bytes (None otherwise). Launches on
-    ``torch.cuda.current_stream()``.
+    ``fusedops.rms_norm`` then ``matmul``; served where x fits a decode GEMV's
+    staging (the register-fed kernel: 1..8 rows within REG_X_MAX bytes; the
+    pair kernel, bf16: 1..4 rows within NORM_X_MAX; None otherwise). Launches
+    on ``torch.cuda.current_stream()``.
     """
     import torch
 
@@ -284,8 +289,8 @@ def matmul(module, x, *, epi: int = EPI_NONE, operand=None, prefetch=None, norm=
     opts = _opts(prefetch, norm, x.dtype)
     st = L.nf4b_gemm_ex(ctypes.byref(desc), flat.data_ptr(), out.data_ptr(), rows, int(epi),
                         op_ptr, ws_ptr, ws_bytes, opts, ctypes.c_void_p(stream.cuda_stream))
-    if st == _lib.NF4B_ERR_SHAPE and norm is not None and x.dtype == torch.float16:
-        return None     # an fp16 RMSNorm fuses into the register-fed GEMV only
+    if st == _lib.NF4B_ERR_SHAPE and norm is not None:
+        return None     # outside the fused RMSNorm's staging envelope
     _lib.check(st)
     _stats["fast"] += 1
     return out.view(*x.shape[:-1], N)
@@ -345,10 +350,10 @@ def matmul_gated(w1, w3, x, *, prefetch=None, norm=None):
     """``silu(x @ w1.weight.T) * (x @ w3.weight.T)`` in ONE launch, with the
     fork's rounding points (app/engine/fusedlayer.py:265-266: two ``matmul``
     launches there, the second with EPI_SILU_GATE); x W1^T is never written
-    out. An extension of the reference's API. Serves 1..4 rows with
-    in_features % 128 == 0; returns None otherwise (the caller then issues the
-    two matmuls) or if either linear is not prepared. `norm` as in ``matmul``.
-    fp16 x is served for 1..2 rows on the register-fed GEMV (None otherwise).
+    out. An extension of the reference's API. Serves 1..8 rows on the
+    register-fed GEMV and (bf16) 1..4 rows with in_features % 128 == 0 on the
+    pair kernel; returns None otherwise (the caller then issues the two
+    matmuls) or if either linear is not prepared. `norm` as in ``matmul``.
     """
     import torch
 
@@ -364,7 +369,7 @@ def matmul_gated(w1, w3, x, *, prefetch=None, norm=None):
         if flat.data_ptr() % 16:
             return None
     rows = flat.shape[0]
-    if rows < 1 or rows > (2 if x.dtype == torch.float16 else 4):
+    if rows < 1 or rows > REG_MAX_ROWS:
         return None
     if norm is not None and not _norm_ok(norm, rows, K, x.device, x.dtype):
         return None
@@ -378,8 +383,8 @@ def matmul_gated(w1, w3, x, *, prefetch=None, norm=None):
     st = L.nf4b_gemm_gated(ctypes.byref(f1["desc"]), ctypes.byref(f3["desc"]), flat.data_ptr(),
                            out.data_ptr(), rows, ws.data_ptr(), ws.numel(), _opts(prefetch, norm, x.dtype),
                            ctypes.c_void_p(stream.cuda_stream))
-    if st == _lib.NF4B_ERR_SHAPE and x.dtype == torch.float16:
-        return None     # fp16 gates run on the register-fed GEMV only
+    if st == _lib.NF4B_ERR_SHAPE:
+        return None     # outside the gated launch's envelope: the caller issues two matmuls
     _lib.check(st)
     _stats["fast"] += 1
     return out.view(*x.shape[:-1], N)
