@@ -282,7 +282,16 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(
 // partials, no atomics.
 // ---------------------------------------------------------------------------
 
-constexpr int kCThreads = 256;
+// 8 warps. (16 warps for groups of <= 4 query heads measured 0.6 us faster
+// at 2048 rows, four chunks per CTA, but 0.8-1 us slower for windows of one
+// or two chunks per CTA, which the fast AR and most slow-AR positions use.)
+template <int G>
+__host__ __device__ constexpr int cthreads() { return 256; }
+template <int G>
+__host__ __device__ constexpr int rows_per_warp() { return ATTN_CHUNK / (cthreads<G>() / 32); }  // score rows
+template <int G>
+__host__ __device__ constexpr int pv_rows() { return ATTN_CHUNK / (cthreads<G>() / 16); }  // P.V rows per thread
+static_assert(rows_per_warp<4>() % 4 == 0 && rows_per_warp<8>() % 4 == 0 && pv_rows<4>() >= 1, "chunk split");
 
 // Stages of the cluster kernel's K/V ring: every chunk of a CTA's share is in
 // flight at once up to this depth (a 2048-row window over 8 CTAs is 4 chunks
@@ -294,7 +303,7 @@ struct ClusterSmem {
   alignas(128) uint16_t kv[kCStages][2][ATTN_CHUNK * kD];  // [stage][K, V][rows x 128]
   float q[G][kD];
   float sc[G][ATTN_CHUNK];
-  float red[kCThreads / 32][G][kD];
+  float red[cthreads<G>() / 32][G][kD];
   float part_acc[G][kD];
   float part_m[G], part_l[G];
   float alpha[G];
@@ -302,7 +311,7 @@ struct ClusterSmem {
   unsigned long long bar[kCStages];
   // the fused q/k norm + rotary prologue (QkvIn)
   float sx[2][kD];
-  double nred[kCThreads / 32];
+  double nred[cthreads<G>() / 32];
   uint16_t knew[kD], vnew[kD];
 };
 
@@ -327,7 +336,8 @@ __device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t ran
   return v;
 }
 
-// One 128-wide row per half-CTA (threads 0-127: half 0, 128-255: half 1)
+// One 128-wide row per half of the first 256 threads (threads 0-127: half 0,
+// 128-255: half 1; the others only join the barriers)
 // with qk_rope_kv's arithmetic: RMSNorm with this half's weight w (none when
 // null) - fp64 sum of squares, reduced exactly as block_sum over 4 warps -
 // then the rotary pair (x0 c - x1 s, x1 c + x0 s) at the freqs row when
@@ -336,7 +346,8 @@ template <int G, bool F16>
 __device__ __forceinline__ float norm_rope_half(ClusterSmem<G>& sm, float x, bool has_w, float wd, bool rope,
                                                 bool any_norm, float eps, float c, float sn) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int d = tid & (kD - 1), half = tid >> 7;
+  const int d = tid & (kD - 1), half = (tid >> 7) & 1;
+  const bool mine = tid < 2 * kD;
   if (any_norm) {
     double sq = has_w ? (double)x * (double)x : 0.0;
 #pragma unroll
@@ -352,7 +363,7 @@ __device__ __forceinline__ float norm_rope_half(ClusterSmem<G>& sm, float x, boo
     }
     __syncthreads();
   }
-  sm.sx[half][d] = x;
+  if (mine) sm.sx[half][d] = x;
   __syncthreads();
   float y = x;
   if (rope) {
@@ -364,10 +375,11 @@ __device__ __forceinline__ float norm_rope_half(ClusterSmem<G>& sm, float x, boo
 }
 
 template <int G, bool F16>
-__global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
+__global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel(
     const bf16_t* __restrict__ q, const bf16_t* __restrict__ kc, const bf16_t* __restrict__ vc,
     const int64_t* __restrict__ pos_ptr, const uint8_t* __restrict__ mask, bf16_t* __restrict__ out,
     int max_len, int window, float scale, const QkvIn in) {
+  constexpr int kCT = cthreads<G>(), kRPW = rows_per_warp<G>(), kPVR = pv_rows<G>();
   extern __shared__ __align__(128) uint8_t smem_raw[];
   ClusterSmem<G>& sm = *reinterpret_cast<ClusterSmem<G>*>(smem_raw);
   const int kh = blockIdx.x;
@@ -440,12 +452,13 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
   const bool fused = in.qkv != nullptr;  // q/k/v from the wqkv output (pos given, no mask)
   const long long p_new = fused ? pos_ptr[0] : -1;
   if (!fused) {
-    for (int i = tid; i < G * kD; i += kCThreads) sm.q[i / kD][i % kD] = act2f<F16>(q[(size_t)kh * G * kD + i]);
+    for (int i = tid; i < G * kD; i += kCT) sm.q[i / kD][i % kD] = act2f<F16>(q[(size_t)kh * G * kD + i]);
   } else {
     // This KV head's query heads, two per pass, then k (half 0) and v (half 1):
     // the arithmetic of qk_rope_kv. The new rows reach the cache through rank 0;
     // the CTA whose chunk holds row p_new patches them into its shared copy.
-    const int d = tid & (kD - 1), half = tid >> 7;
+    const int d = tid & (kD - 1), half = (tid >> 7) & 1;
+    const bool mine = tid < 2 * kD;  // threads 256+ only join the barriers
     const bf16_t* qkv = in.qkv;
     const bool norm = in.qw != nullptr;  // q and k norm weights come together
     // every global load first (one round trip), then the passes
@@ -464,12 +477,12 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
     for (int i = 0; i < P; ++i) {
       const int h = 2 * i + half;
       const float y = norm_rope_half<G, F16>(sm, xq[i], norm, qwd, true, norm, in.eps, c, sn);
-      if (h < G) sm.q[h][d] = round_act<F16>(y);
+      if (h < G && mine) sm.q[h][d] = round_act<F16>(y);
     }
     const float y = norm_rope_half<G, F16>(sm, xkv, norm && half == 0, kwd, half == 0, norm, in.eps, c, sn);
     const bf16_t nb = f2act<F16>(y);
-    (half ? sm.vnew : sm.knew)[d] = nb;
-    if (rank == 0 && p_new < max_len) {
+    if (mine) (half ? sm.vnew : sm.knew)[d] = nb;
+    if (mine && rank == 0 && p_new < max_len) {
       bf16_t* cache = const_cast<bf16_t*>(half ? vc : kc);
       cache[((size_t)kh * max_len + p_new) * kD + d] = nb;
     }
@@ -480,19 +493,22 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
   }
   __syncthreads();
 
-  const int dg = tid & 15, pg = tid >> 4;  // P.V: dimensions dg*8 .. +7, chunk rows pg*4 .. +3
+  const int dg = tid & 15, pg = tid >> 4;  // P.V: dimensions dg*8 .. +7, chunk rows pg*kPVR .. +kPVR-1
   // This lane's slice of every query head for the scores (dimensions
-  // (lane & 7) * 16 .. +15), held in registers as pairs of the activation
-  // type - the values are of that type already - instead of re-reading shared
-  // memory for every key row.
+  // (lane & 7) * 8 .. +7 and 64 + (lane & 7) * 8 .. +7, so that the eight lanes
+  // of a key row read 128 contiguous bytes per load: no bank conflicts), held
+  // in registers as pairs of the activation type - the values are of that
+  // type already - instead of re-reading shared memory for every key row.
   uint32_t qr[G][8];
   {
     const int li = lane & 7;
 #pragma unroll
     for (int h = 0; h < G; ++h)
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        qr[h][e] = pack_act2<F16>(sm.q[h][li * 16 + 2 * e], sm.q[h][li * 16 + 2 * e + 1]);
+      for (int e = 0; e < 8; ++e) {
+        const int d0 = (e < 4 ? 0 : 64) + li * 8 + 2 * (e & 3);
+        qr[h][e] = pack_act2<F16>(sm.q[h][d0], sm.q[h][d0 + 1]);
+      }
   }
   float acc[G][8];
 #pragma unroll
@@ -519,7 +535,7 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
     if (fused && p_new >= j0 && p_new < j0 + rows) {
       // the copy may predate rank 0's store of the new row: use the computed one
       const int d = tid & (kD - 1), half = tid >> 7;
-      sm.kv[stg][half][(int)(p_new - j0) * kD + d] = (half ? sm.vnew : sm.knew)[d];
+      if (half < 2) sm.kv[stg][half][(int)(p_new - j0) * kD + d] = (half ? sm.vnew : sm.knew)[d];
       __syncthreads();
     }
     const uint16_t* ks = sm.kv[stg][0];
@@ -527,15 +543,15 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
     // Scores: a warp takes 8 rows, four at a time, eight lanes per row.
     {
       const int gi = lane >> 3, li = lane & 7;
-      for (int it = 0; it < 2; ++it) {
-        const int jl = warp * 8 + it * 4 + gi;
+      for (int it = 0; it < kRPW / 4; ++it) {
+        const int jl = warp * kRPW + it * 4 + gi;
         float dot[G];
 #pragma unroll
         for (int h = 0; h < G; ++h) dot[h] = 0.f;
         const bool vis = ok && jl < rows && (mask == nullptr || mask[j0 + jl] != 0);
         if (vis) {
-          const uint4* kr = reinterpret_cast<const uint4*>(ks + jl * kD + li * 16);
-          const uint4 k0 = kr[0], k1 = kr[1];
+          const uint4* kr = reinterpret_cast<const uint4*>(ks + jl * kD);
+          const uint4 k0 = kr[li], k1 = kr[8 + li];
           const uint32_t kw[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
@@ -559,7 +575,7 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
     }
     __syncthreads();
     // Online softmax update per head (a warp per head).
-    for (int h = warp; h < G; h += kCThreads / 32) {
+    for (int h = warp; h < G; h += kCT / 32) {
       const float a = sm.sc[h][lane], b = sm.sc[h][lane + 32];
       float mc = fmaxf(a, b);
 #pragma unroll
@@ -591,8 +607,8 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
       for (int e = 0; e < 8; ++e) acc[h][e] *= al;
     }
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int jl = pg * 4 + r;
+    for (int r = 0; r < kPVR; ++r) {
+      const int jl = pg * kPVR + r;
       if (!ok || jl >= rows) continue;
       if (mask != nullptr && mask[j0 + jl] == 0) continue;
       const uint4 vv = *reinterpret_cast<const uint4*>(vs + jl * kD + dg * 8);
@@ -619,21 +635,34 @@ __global__ void __launch_bounds__(kCThreads) decode_attention_cluster_kernel(
       if ((lane & 16) == 0) sm.red[warp][h][dg * 8 + e] = v;
     }
   __syncthreads();
-  for (int i = tid; i < G * kD; i += kCThreads) {
+  for (int i = tid; i < G * kD; i += kCT) {
     const int h = i / kD, d = i % kD;
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < kCThreads / 32; ++w) v += sm.red[w][h][d];
+    for (int w = 0; w < kCT / 32; ++w) v += sm.red[w][h][d];
     sm.part_acc[h][d] = v;
   }
   if (tid < G) {
     sm.part_m[tid] = sm.run_m[tid];
     sm.part_l[tid] = sm.run_l[tid];
   }
+  if (C == 1) {
+    // One CTA per KV head: its partial is the result (the merge below with a
+    // single partial has weight exp(0) = 1, so this is bit for bit the same).
+    __syncthreads();
+    for (int i = tid; i < G * kD; i += kCT) {
+      const int h = i / kD, d = i % kD;
+      const float w = (sm.part_m[h] == -INFINITY) ? 0.f : 1.f;
+      out[(size_t)(kh * G + h) * kD + d] = f2act<F16>(fmaf(sm.part_acc[h][d], w, 0.f) / fmaf(sm.part_l[h], w, 0.f));
+    }
+    return;
+  }
   cluster_sync();
-  if (rank == 0) {
-    // All remote loads are issued before any is used (one round trip).
-    for (int i = tid; i < G * kD; i += kCThreads) {
+  {
+    // Each CTA of the cluster merges its share of the (head, dimension)
+    // outputs: all remote loads are issued before any is used (one round trip).
+    const int E = G * kD, lo = (int)(rank * E / C), hi = (int)((rank + 1) * E / C);
+    for (int i = lo + tid; i < hi; i += kCT) {
       const int h = i / kD, d = i % kD;
       float mr[16], lr[16], ar[16];
 #pragma unroll
@@ -695,7 +724,7 @@ cudaError_t launch_cluster_g(const uint16_t* q, const uint16_t* kc, const uint16
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nkv, C);
-  cfg.blockDim = dim3(kCThreads);
+  cfg.blockDim = dim3(cthreads<G>());
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   // One CTA per KV head (a one-chunk window) needs no cluster: a plain launch
