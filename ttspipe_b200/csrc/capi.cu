@@ -368,7 +368,7 @@ int nf4b_gemm_ex(const nf4b_weight* w, const void* x, void* y, int rows, int epi
   p.f16 = f16 ? 1 : 0;
   // split-K when the caller's workspace holds the partial sums (else one pass)
   const int sms = current_sm_count();
-  p.bt = gemm_bt(w->n_out, rows, sms);
+  p.bt = gemm_bt(w->n_out, rows, w->k_in, sms);
   int splits = gemm_splits(w->n_out, rows, w->k_in, sms);
   const size_t need = splits > 1 ? GEMM_COUNTER_BYTES + (size_t)splits * rows * w->n_out * sizeof(float) : 0;
   if (splits > 1 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256))) splits = 1;

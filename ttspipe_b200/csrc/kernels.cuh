@@ -327,13 +327,13 @@ struct GemmParams {
   int splits;
   float* partial;
   int* counters;
-  int bt;  // activation rows per tile: gemm_bt(N, M, sms)
+  int bt;  // activation rows per tile: gemm_bt(N, M, K, sms)
   int f16;  // fp16 x, operand and y; else bf16
 };
 constexpr size_t GEMM_COUNTER_BYTES = 4096;  // tile counters of a split-K launch (<= 1024 tiles)
 // Split-K factor the GEMM would use for this shape on `sms` SMs (1: none), and
 // the workspace it then needs (0 when 1).
-int gemm_bt(int N, int M, int sms);
+int gemm_bt(int N, int M, int K, int sms);
 int gemm_splits(int N, int M, int K, int sms);
 size_t gemm_workspace_bytes(int N, int M, int K, int sms);
 cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream);

@@ -416,10 +416,57 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
     __syncthreads();
     if (!sm.last || *abort_flag) return;
     __threadfence();
-    // four elements per thread in flight, each with all its splits' loads issued
-    // before the in-order sum
+    // The tile's BT x 128 sums, read as float4 runs along n (when n_out % 4 == 0)
+    // with every split's loads of a thread's elements issued before the
+    // in-order sums: a few L2 round trips for the whole tile.
     const size_t MN = (size_t)p.M * p.N;
     constexpr int T = gemm_threads<DQ>();
+    if ((p.N & 3) == 0) {
+      constexpr int V = 2;  // float4s per thread per split in flight
+      for (int base = tid; base < BT * (BM / 4); base += V * T) {
+        float4 acc[V];
+        size_t o[V];
+        bool live[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          const int idx = base + e * T;
+          const int tok = tok0 + idx / (BM / 4), n = n0 + (idx % (BM / 4)) * 4;
+          live[e] = idx < BT * (BM / 4) && tok < p.M && n < p.N;
+          o[e] = live[e] ? (size_t)tok * p.N + n : 0;
+          acc[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        for (int z0 = 0; z0 < S; z0 += 4) {
+          float4 v[4][V];
+#pragma unroll
+          for (int zz = 0; zz < 4; ++zz)
+#pragma unroll
+            for (int e = 0; e < V; ++e)
+              v[zz][e] = (live[e] && z0 + zz < S)
+                             ? __ldcg(reinterpret_cast<const float4*>(p.partial + (z0 + zz) * MN + o[e]))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int zz = 0; zz < 4; ++zz)
+            if (z0 + zz < S)
+#pragma unroll
+              for (int e = 0; e < V; ++e) {
+                acc[e].x += v[zz][e].x;
+                acc[e].y += v[zz][e].y;
+                acc[e].z += v[zz][e].z;
+                acc[e].w += v[zz][e].w;
+              }
+        }
+#pragma unroll
+        for (int e = 0; e < V; ++e)
+          if (live[e]) {
+            const float a[4] = {acc[e].x, acc[e].y, acc[e].z, acc[e].w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) p.y[o[e] + c] = epilogue<kF16>(a[c], p.epi, p.operand, o[e] + c);
+          }
+      }
+      return;
+    }
+    // four elements per thread in flight, each with all its splits' loads issued
+    // before the in-order sum
     for (int base = tid; base < BT * BM; base += 4 * T) {
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
       size_t o[4];
@@ -486,65 +533,53 @@ cudaError_t launch_bt(const GemmParams& p, cudaStream_t stream) {
 }  // namespace
 
 
-template <int BT, bool kSplit>
-static int gemm_ctas_per_sm() {
-  static int occ[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int i = (dev >= 0 && dev < 64) ? dev : 0;
-  if (occ[i] == 0) {
-    const int smem = (int)(sizeof(TileSmem<BT>) + 1024);
-    int n = 0;
-    if (cudaFuncSetAttribute(nf4_gemm_tc_kernel<BT, kDequantGroups, kSplit>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             smem) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, nf4_gemm_tc_kernel<BT, kDequantGroups, kSplit>,
-                                                      gemm_threads<kDequantGroups>(), smem) != cudaSuccess ||
-        n < 1) {
-      (void)cudaGetLastError();
-      n = 1;
+// Tile rows (BT) and k splits of a GEMM, from a cost model fitted to a sweep of
+// the S2-Pro projections at 32..1024 rows over BT in {64, 128, 256} and 1..8
+// splits: a CTA costs ~6 k-block times of fixed work (pipeline fill, epilogue)
+// plus its k blocks at a rate set by the dequantisation (relative cost 0.7,
+// 0.75, 1 per k block for 64-, 128-, 256-row tiles); CTAs beyond one per SM run
+// in further rounds (a second resident CTA shares the SM's dequantisation
+// rate, so it does not count as free); each split adds its partial sums'
+// write and reduction (1.5, 3, 10 k-block times). Examples it reproduces:
+// 2560x9728 at M = 256, 6 splits of 256-row tiles (a 128-row 3-split within
+// 5%) where a 64-row 3-split took 58 us against 33; 2560x4096 at M = 256,
+// 128-row tiles in 3 splits (21 against 33 us); the 9728-row gate and up
+// projections unsplit 256-row tiles (one CTA per tile is cheapest there).
+struct GemmShape {
+  int bt, splits;
+};
+
+static GemmShape gemm_choose(int N, int M, int K, int sms) {
+  const long long tn = (N + BM - 1) / BM;
+  const int KB = K / BK;
+  const int bts[3] = {64, 128, 256};
+  const double cost_kb[3] = {0.7, 0.75, 1.0}, cost_split[3] = {1.5, 3.0, 10.0};
+  const int splits[6] = {1, 2, 3, 4, 6, 8};
+  GemmShape best = {64, 1};
+  double best_t = 1e30;
+  for (int bi = 0; bi < 3; ++bi) {
+    const int bt = bts[bi];
+    if (bt > 64 && M <= bt / 2) continue;  // a tile at most half full
+    const long long tiles = tn * ((M + bt - 1) / bt);
+    for (int si = 0; si < 6; ++si) {
+      const int sp = splits[si];
+      if (sp > 1 && (KB / sp < 4 || tiles * (long long)sizeof(int) > (long long)GEMM_COUNTER_BYTES)) continue;
+      const long long ctas = tiles * sp;
+      const long long rounds = (ctas + sms - 1) / sms;
+      const double t = (double)rounds * ((double)((KB + sp - 1) / sp) * cost_kb[bi] + 6.0) +
+                       (sp > 1 ? sp * cost_split[bi] : 0.0);
+      if (t < best_t - 1e-9) {
+        best_t = t;
+        best = {bt, sp};
+      }
     }
-    occ[i] = n;
   }
-  return occ[i];
+  return best;
 }
 
-// Activation rows per tile. 64-row tiles (split over k when still too few)
-// whenever their grid fits in one wave of resident CTAs: measured faster for
-// the narrow projections up to M = 1024 (1024x2560 at M = 256: 25.4 -> 16.6 us)
-// even though each weight tile is then dequantised M / 64 times; beyond one
-// wave 128 (M <= 128) or 256-row tiles are faster. Split-K is never used for
-// 128- and 256-row tiles (measured slower: the partial sums' traffic outweighs
-// the extra CTAs).
-int gemm_bt(int N, int M, int sms) {
-  if (M <= 64) return 64;
-  const long long tiles64 = (long long)((N + BM - 1) / BM) * ((M + 63) / 64);
-  if (tiles64 <= (long long)sms * gemm_ctas_per_sm<64, true>()) return 64;
-  return M <= 128 ? 128 : 256;
-}
+int gemm_bt(int N, int M, int K, int sms) { return gemm_choose(N, M, K, sms).bt; }
 
-// Split the k range of 64-row tiles when the output tiles alone cannot fill
-// the GPU: as many splits as keep every resident CTA slot busy, each of at
-// least 4 k blocks. When that is one (more than half the slots, fewer than all
-// of them, hold a tile), three splits still fit in two rounds of the slots and
-// each keeps at least 32 k blocks, three: two rounds of third-size CTAs then
-// beat one round of whole tiles (2560x9728 at M = 256, 80 tiles on 148 SMs:
-// 70.9 -> 59.4 us). With shorter splits the extra round costs more than it
-// saves (9728x2560 at M = 64: 22.6 -> 27.2 us; 2560x4096 at M = 256: 33.4 ->
-// 34.5 us), so those stay whole.
-int gemm_splits(int N, int M, int K, int sms) {
-  const int bt = gemm_bt(N, M, sms);
-  if (bt != 64) return 1;
-  const long long tiles = (long long)((N + BM - 1) / BM) * ((M + bt - 1) / bt);
-  if (tiles * (long long)sizeof(int) > (long long)GEMM_COUNTER_BYTES) return 1;
-  const int occ = gemm_ctas_per_sm<64, true>();
-  const long long slots = (long long)sms * occ;
-  long long s = slots / tiles;
-  if (s < 2 && 3 * tiles <= 2 * slots && K / BK >= 3 * 32) s = 3;
-  const long long kmax = (K / BK) / 4;
-  if (s > kmax) s = kmax;
-  if (s > 16) s = 16;
-  return s >= 2 ? (int)s : 1;
-}
+int gemm_splits(int N, int M, int K, int sms) { return gemm_choose(N, M, K, sms).splits; }
 
 size_t gemm_workspace_bytes(int N, int M, int K, int sms) {
   const int s = gemm_splits(N, M, K, sms);
@@ -556,8 +591,9 @@ static cudaError_t launch_gemm_act(const GemmParams& p, cudaStream_t stream) {
   const int bt = p.bt;
   if (bt == 64)
     return p.splits > 1 ? launch_bt<64, true, kF16>(p, stream) : launch_bt<64, false, kF16>(p, stream);
-  if (bt == 128) return launch_bt<128, false, kF16>(p, stream);
-  return launch_bt<256, false, kF16>(p, stream);
+  if (bt == 128)
+    return p.splits > 1 ? launch_bt<128, true, kF16>(p, stream) : launch_bt<128, false, kF16>(p, stream);
+  return p.splits > 1 ? launch_bt<256, true, kF16>(p, stream) : launch_bt<256, false, kF16>(p, stream);
 }
 
 cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream) {
