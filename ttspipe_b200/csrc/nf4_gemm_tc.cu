@@ -15,12 +15,15 @@
 //              4 x tcgen05.mma (M=128, N=BT, K=16) per k block, committing each
 //              stage back to the producer and the whole tile to the epilogue.
 //   warps 2-17 four groups of four warps, k blocks round-robin over the
-//              groups, dequantise: thread r of a group owns weight row r of the
-//              tile; it forms the
+//              groups, dequantise: lane l of warp w owns weight row
+//              32 (w % 4) + l of the tile; it forms the
 //              block's scale (plain fp32, or code2[a8] * absmax2 + offset as two
 //              rounded fp32 ops) and writes bf16(NF4[q] * scale) - bit-exact to
-//              bitsandbytes' dequantisation - into the K-major 128-byte-swizzled
-//              A tile the MMA reads. After the last k block the same warps read
+//              bitsandbytes' dequantisation - into its row's lane of the A ring
+//              in tensor memory (tcgen05.st), which the MMA reads as its A
+//              operand: the weights never pass through shared memory, whose
+//              bandwidth the X tiles' copies and the MMA's B reads already
+//              use. After the last k block the same warps read
 //              the accumulator back (tcgen05.ld, 32 lanes x 32 columns at a
 //              time), round to bf16, apply the epilogue and store Y.
 //
@@ -63,6 +66,15 @@ constexpr int kDequantGroups = 4;
 // read a stale tile.
 template <int BT>
 __host__ __device__ constexpr int ring_stages() { return BT >= 128 ? 4 : 8; }
+// Tensor memory per CTA: the fp32 accumulator (BT columns), then the A ring -
+// the dequantised weight tiles, 128 lanes (weight rows) x 32 columns (64 bf16
+// or fp16 codes, two per column) per stage, which the MMA reads straight from
+// tensor memory, so A never passes through shared memory. Allocated as the
+// next power of two.
+template <int BT>
+__host__ __device__ constexpr uint32_t tmem_cols() {
+  return (BT + ring_stages<BT>() * 32) <= 256 ? 256u : 512u;
+}
 static_assert(ring_stages<256>() % kDequantGroups == 0 && ring_stages<128>() % kDequantGroups == 0 &&
                   ring_stages<64>() % kDequantGroups == 0,
               "ring depth must be a multiple of the dequantisation groups");
@@ -72,7 +84,6 @@ template <int BT>
 struct __align__(1024) TileSmem {
   static constexpr int STAGES = ring_stages<BT>();
   uint8_t x[STAGES][BT * 128];
-  uint8_t a[STAGES][BM * 128];
   uint8_t w[STAGES][BM * 32];
   float code2[256];
   float nf4[16];
@@ -230,7 +241,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&sm.tmem_base)),
-                 "r"((uint32_t)BT)
+                 "r"(tmem_cols<BT>())
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -279,16 +290,17 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
              mbar_wait(smem_u32(&sm.a_full[s]), ph, abort_flag);
         if (!ok) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a_addr = smem_u32(sm.a[s]), x_addr = smem_u32(sm.x[s]);
+        const uint32_t a_tmem = tmem + (uint32_t)BT + (uint32_t)s * 32u, x_addr = smem_u32(sm.x[s]);
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k) {
-          const uint64_t ad = smem_desc(a_addr + k * 32), bd = smem_desc(x_addr + k * 32);
+          const uint64_t bd = smem_desc(x_addr + k * 32);
           const uint32_t accumulate = (i > 0 || k > 0) ? 1u : 0u;
+          // A: 128 lanes x 8 columns (16 codes) of the stage in tensor memory
           asm volatile(
               "{\n\t.reg .pred p;\n\t"
               "setp.ne.b32 p, %4, 0;\n\t"
-              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
-              "l"(ad), "l"(bd), "r"(idesc), "r"(accumulate)
+              "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem),
+              "r"(a_tmem + (uint32_t)k * 8u), "l"(bd), "r"(idesc), "r"(accumulate)
               : "memory");
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
@@ -302,12 +314,13 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
       mbar_drain(smem_u32(&sm.accum_full), 0);
     }
   } else {
-    // Dequantise: thread r of group grp owns weight row n0 + r.
+    // Dequantise: lane l of a warp owns weight row r = 32 (warp % 4) + l of the
+    // tile - its tensor-memory lane, the only lane quarter the warp may write.
     const int grp = (warp - 2) >> 2;
-    const int r = (tid - 64) & 127;
+    const int r = (warp & 3) * 32 + lane;
     const int row = n0 + r;
     const bool valid = row < p.N;
-    const int rsw = r & 7;
+    const uint32_t a_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)BT;
     // The block scale's global loads run one of this group's k blocks ahead,
     // so their latency hides under the previous block's dequantisation.
     uint32_t code_next = 0;
@@ -335,19 +348,34 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
       fetch_scale(i + DQ);
       const float scale = !valid ? 0.f : p.nested ? nested_scale(sm.code2[code], am, p.offset) : am;
       if (!mbar_wait(smem_u32(&sm.w_full[s]), (i / STAGES) & 1, abort_flag)) break;
+      // the stage's previous MMAs completed before this tile's copy was issued:
+      // order the tensor-memory store below after that
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint4* wp = reinterpret_cast<const uint4*>(sm.w[s] + r * 32);
       const uint4 ua = wp[hfirst], ub = wp[hfirst ^ 1];
       const uint4 u0 = hfirst ? ub : ua, u1 = hfirst ? ua : ub;
       const uint32_t words[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-      uint8_t* arow = sm.a[s] + (r >> 3) * 1024 + rsw * 128;
       const ScaledLut lut = scaled_lut<kF16>(scale);
+      // the row's 64 codes as 32 pairs in k order -> columns 0..31 of its lane
+      uint32_t o[32];
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        uint32_t o[4];
-        lut_dequant8(lut, words[c], o);
-        *reinterpret_cast<uint4*>(arow + ((c ^ rsw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        uint32_t q4[4];
+        lut_dequant8(lut, words[c], q4);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[4 * c + e] = q4[e];
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile(
+          "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+          "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+          "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(a_lane + (uint32_t)s * 32u),
+          "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3]), "r"(o[4]), "r"(o[5]), "r"(o[6]), "r"(o[7]), "r"(o[8]),
+          "r"(o[9]), "r"(o[10]), "r"(o[11]), "r"(o[12]), "r"(o[13]), "r"(o[14]), "r"(o[15]), "r"(o[16]),
+          "r"(o[17]), "r"(o[18]), "r"(o[19]), "r"(o[20]), "r"(o[21]), "r"(o[22]), "r"(o[23]), "r"(o[24]),
+          "r"(o[25]), "r"(o[26]), "r"(o[27]), "r"(o[28]), "r"(o[29]), "r"(o[30]), "r"(o[31])
+          : "memory");
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&sm.a_full[s]));
     }
@@ -400,7 +428,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"((uint32_t)BT)
+                 "r"(tmem_cols<BT>())
                  : "memory");
   }
   if (kSplit) {
