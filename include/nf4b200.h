@@ -80,8 +80,12 @@ const char* nf4b_last_error(void);
  * bounded wait (a pipeline barrier that never completed): bit 0 the GEMM,
  * bit 1 the GEMV, bit 2 decode attention's KV copies, bit 3 a decode step's
  * handoff. Synchronises the device to read it; `clear`
- * resets it; -1 if it cannot be read. No counterpart in the reference, whose
- * kernels have no waits.
+ * resets it; -1 if it cannot be read. The outputs of a call that set it are
+ * invalid. The abort paths still count every CTA / warp into the workspace
+ * counters (so the last arriver returns them to zero) and the decode step takes
+ * a new flag space per launch; a caller that wants certainty zeroes a workspace
+ * again after a non-zero word before reusing it. No counterpart in the
+ * reference, whose kernels have no waits.
  */
 int nf4b_device_error(int clear);
 
