@@ -543,29 +543,33 @@ __global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel
     // Scores: a warp takes 8 rows, four at a time, eight lanes per row.
     {
       const int gi = lane >> 3, li = lane & 7;
+#pragma unroll
       for (int it = 0; it < kRPW / 4; ++it) {
         const int jl = warp * kRPW + it * 4 + gi;
-        float dot[G];
+        // Every row's loads and products are computed (no branch, so the loads
+        // issue together); rows that are masked or past the live length are
+        // stored as -inf below, whatever their stage bytes hold. Two
+        // accumulators per head halve the dependent FMA chain.
+        float dot[G], dot2[G];
 #pragma unroll
-        for (int h = 0; h < G; ++h) dot[h] = 0.f;
+        for (int h = 0; h < G; ++h) dot[h] = dot2[h] = 0.f;
         const bool vis = ok && jl < rows && (mask == nullptr || mask[j0 + jl] != 0);
-        if (vis) {
-          const uint4* kr = reinterpret_cast<const uint4*>(ks + jl * kD);
-          const uint4 k0 = kr[li], k1 = kr[8 + li];
-          const uint32_t kw[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+        const uint4* kr = reinterpret_cast<const uint4*>(ks + jl * kD);
+        const uint4 k0 = kr[li], k1 = kr[8 + li];
+        const uint32_t kw[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float ka = act_lo<F16>(kw[e]), kb = act_hi<F16>(kw[e]);
+        for (int e = 0; e < 8; ++e) {
+          const float ka = act_lo<F16>(kw[e]), kb = act_hi<F16>(kw[e]);
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
-              dot[h] = fmaf(act_lo<F16>(qr[h][e]), ka, dot[h]);
-              dot[h] = fmaf(act_hi<F16>(qr[h][e]), kb, dot[h]);
-            }
+          for (int h = 0; h < G; ++h) {
+            float& d = (e & 1) ? dot2[h] : dot[h];
+            d = fmaf(act_lo<F16>(qr[h][e]), ka, d);
+            d = fmaf(act_hi<F16>(qr[h][e]), kb, d);
           }
         }
 #pragma unroll
         for (int h = 0; h < G; ++h) {
-          float v = dot[h];
+          float v = dot[h] + dot2[h];
           v += __shfl_xor_sync(0xffffffffu, v, 4);
           v += __shfl_xor_sync(0xffffffffu, v, 2);
           v += __shfl_xor_sync(0xffffffffu, v, 1);
@@ -598,8 +602,10 @@ __global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel
       }
     }
     __syncthreads();
-    // P.V for this chunk; masked and past-the-end rows are skipped, never
-    // multiplied by a zero weight.
+    // P.V for this chunk. Masked and past-the-end rows contribute exact zeros:
+    // their V words are replaced by zero before any multiply (their weights
+    // are zero too), so whatever the stage bytes hold (NaN included) never
+    // reaches the sums; all rows' loads issue together.
 #pragma unroll
     for (int h = 0; h < G; ++h) {
       const float al = sm.alpha[h];
@@ -609,9 +615,9 @@ __global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel
 #pragma unroll
     for (int r = 0; r < kPVR; ++r) {
       const int jl = pg * kPVR + r;
-      if (!ok || jl >= rows) continue;
-      if (mask != nullptr && mask[j0 + jl] == 0) continue;
-      const uint4 vv = *reinterpret_cast<const uint4*>(vs + jl * kD + dg * 8);
+      const bool live = jl < rows && (mask == nullptr || mask[j0 + jl] != 0);
+      const uint4 raw = *reinterpret_cast<const uint4*>(vs + jl * kD + dg * 8);
+      const uint4 vv = live ? raw : make_uint4(0u, 0u, 0u, 0u);
       const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
 #pragma unroll
       for (int h = 0; h < G; ++h) {
