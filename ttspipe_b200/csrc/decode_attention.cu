@@ -452,7 +452,19 @@ __global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel
   const bool fused = in.qkv != nullptr;  // q/k/v from the wqkv output (pos given, no mask)
   const long long p_new = fused ? pos_ptr[0] : -1;
   if (!fused) {
-    for (int i = tid; i < G * kD; i += kCT) sm.q[i / kD][i % kD] = act2f<F16>(q[(size_t)kh * G * kD + i]);
+    // every load first (one round trip), then the stores
+    constexpr int QN = (G * kD + kCT - 1) / kCT;
+    uint16_t qv[QN];
+#pragma unroll
+    for (int j = 0; j < QN; ++j) {
+      const int i = tid + j * kCT;
+      qv[j] = i < G * kD ? __ldg(q + (size_t)kh * G * kD + i) : (uint16_t)0;
+    }
+#pragma unroll
+    for (int j = 0; j < QN; ++j) {
+      const int i = tid + j * kCT;
+      if (i < G * kD) sm.q[i / kD][i % kD] = act2f<F16>(qv[j]);
+    }
   } else {
     // This KV head's query heads, two per pass, then k (half 0) and v (half 1):
     // the arithmetic of qk_rope_kv. The new rows reach the cache through rank 0;
