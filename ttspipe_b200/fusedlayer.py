@@ -24,9 +24,10 @@ from ttspipe_b200 import _lib
 
 HEAD_DIM = 128
 #: One launch for q/k norm + rotary + KV write + attention (nf4b_qkv_attention)
-#: instead of nf4b_qk_rope_kv then nf4b_decode_attention. Off: measured 3% slower
-#: per Dual-AR frame than the two launches chained by programmatic dependent launch.
-FUSED_QKV_ATTENTION = False
+#: instead of nf4b_qk_rope_kv then nf4b_decode_attention. On: with the current
+#: attention kernel the Dual-AR frame takes 3.88 ms against 4.00 ms with the two
+#: launches (it was 3% slower against an earlier, slower attention kernel).
+FUSED_QKV_ATTENTION = True
 #: Without q/k norm, run the rotary and the KV-cache write in the wqkv GEMV's
 #: store (nf4b_gemm_qkv_rope, one launch less per block); "one_chunk": only
 #: where the attention that follows is a plain launch (a window of <= 64 rows).
