@@ -10,7 +10,9 @@
 //
 //   warp 0     TMA producer: X tile [BT x 64] bf16 (128-byte swizzle) and the
 //              packed weight tile [128 x 32 B] per 64-wide k block, into a
-//              ring_stages<BT>()-deep ring, completion via mbarrier transaction counts.
+//              ring_stages<BT>()-deep ring, completion via mbarrier transaction
+//              counts; the first ring's weight tiles are requested before the
+//              dependency wait (weights are not the previous launch's output).
 //   warp 1     allocates TMEM (BT fp32 columns) and, from one thread, issues
 //              4 x tcgen05.mma (M=128, N=BT, K=16) per k block, committing each
 //              stage back to the producer and the whole tile to the epilogue.
@@ -23,9 +25,11 @@
 //              in tensor memory (tcgen05.st), which the MMA reads as its A
 //              operand: the weights never pass through shared memory, whose
 //              bandwidth the X tiles' copies and the MMA's B reads already
-//              use. After the last k block the same warps read
-//              the accumulator back (tcgen05.ld, 32 lanes x 32 columns at a
-//              time), round to bf16, apply the epilogue and store Y.
+//              use (the dequantised tiles never do). After the last k block
+//              the same warps read the accumulator back (tcgen05.ld, 32 lanes
+//              x 32 columns at a time), round to bf16, apply the epilogue and
+//              store Y, through the then idle X ring for split-K and 64-row
+//              tiles.
 //
 // Every mbarrier wait is bounded: a wait that outlives kWaitNs sets the
 // library's device error word and a CTA-wide abort flag, after which every
@@ -50,10 +54,10 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 // Warp 0: TMA producer; warp 1: TMEM owner + MMA issuer; then DQ groups of
 // four dequantisation/epilogue warps (group g serves k blocks g, g + DQ, ...).
-// The dequantisation is the kernel's critical path: per 64-block each thread
-// builds its row's scaled table and runs ~170 dependent byte-permute
-// instructions, so more groups in flight raise the tile rate (measured
-// against two groups: the S2-Pro layer 7-11% faster from M = 64 to 1024).
+// Per 64-block each dequantisation thread builds its row's scaled table and
+// runs ~170 byte-permute instructions (~1000 cycles per group and block); four
+// groups measured faster than two or three, and five or six (more threads,
+// fewer registers each) slower again.
 template <int DQ>
 constexpr int gemm_threads() { return 64 + 128 * DQ; }
 constexpr int kDequantGroups = 4;
@@ -79,6 +83,10 @@ static_assert(ring_stages<256>() % kDequantGroups == 0 && ring_stages<128>() % k
                   ring_stages<64>() % kDequantGroups == 0,
               "ring depth must be a multiple of the dequantisation groups");
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
+// A waiting thread asks to be suspended for up to this long per try (it wakes
+// when the phase completes): spinning waiters would take issue slots from the
+// dequantisation warps (measured 3-4% on the S2-Pro layer at 256-4096 rows).
+constexpr uint32_t kSuspendNs = 1000;
 
 template <int BT>
 struct __align__(1024) TileSmem {
@@ -86,10 +94,9 @@ struct __align__(1024) TileSmem {
   uint8_t x[STAGES][BT * 128];
   uint8_t w[STAGES][BM * 32];
   float code2[256];
-  float nf4[16];
   unsigned long long w_full[STAGES];  // packed weight tile landed (dequantisers wait)
-  unsigned long long x_full[STAGES];  // activation tile landed (MMA issuer waits)
-  unsigned long long a_full[STAGES];
+  unsigned long long x_full[STAGES];  // activation tile landed (one dequantisation warp waits)
+  unsigned long long a_full[STAGES];  // A stage written and X seen landed (MMA issuer waits)
   unsigned long long mma_done[STAGES];
   unsigned long long accum_full;
   uint32_t tmem_base;
@@ -97,6 +104,10 @@ struct __align__(1024) TileSmem {
   int last;  // split-K: this CTA finishes its tile
 };
 
+// The epilogue stages the fp32 tile [BT][BM] in the X ring.
+static_assert(ring_stages<64>() * 64 * 128 >= 64 * BM * 4 && ring_stages<128>() * 128 * 128 >= 128 * BM * 4 &&
+                  ring_stages<256>() * 256 * 128 >= 256 * BM * 4,
+              "the X ring cannot hold the output tile");
 // Each ring (plus 1 KB of alignment slack) fits the 227 KB of shared memory a CTA may use.
 static_assert(sizeof(TileSmem<64>) + 1024 <= 232448, "64-row ring too deep");
 static_assert(sizeof(TileSmem<128>) + 1024 <= 232448, "128-row ring too deep");
@@ -132,10 +143,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(done)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "n"(kSuspendNs)
         : "memory");
     if (done) return true;
     if ((i & 255u) == 0u) {
@@ -245,64 +256,75 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (tid < 16) sm.nf4[tid] = c_nf4_code[tid];
-  if (p.nested)
-    for (int i = tid; i < 256; i += gemm_threads<DQ>()) sm.code2[i] = p.code2[i];
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = sm.tmem_base;
 
-  pdl_wait();  // X and Y belong to the stream's previous work
-
+  // Only X, Y, the epilogue operand and the split-K scratch belong to the
+  // stream's previous work: the producer requests the first weight tiles
+  // before its dependency wait, and the dequantisation warps wait only
+  // before their epilogue.
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < nkb; ++i) {
-        const int kb = kb_lo + i, s = i % STAGES;
-        if (i >= STAGES &&
-            !mbar_wait(smem_u32(&sm.mma_done[s]), ((i / STAGES) - 1) & 1, abort_flag))
-          break;
-        // the small weight tile first, on its own barrier, so that its
-        // dequantisation starts before the activation tile has landed
-        const uint32_t wbar = smem_u32(&sm.w_full[s]), xbar = smem_u32(&sm.x_full[s]);
+      int issued_w = 0, issued = 0;
+      auto load_w = [&](int i) {
+        const uint32_t wbar = smem_u32(&sm.w_full[i % STAGES]);
         mbar_expect_tx(wbar, BM * 32);
-        tma_load_2d(smem_u32(sm.w[s]), &tmap_w, kb * (BK / 2), n0, wbar);
+        tma_load_2d(smem_u32(sm.w[i % STAGES]), &tmap_w, (kb_lo + i) * (BK / 2), n0, wbar);
+        issued_w = i + 1;
+      };
+      for (int i = 0; i < nkb && i < STAGES; ++i) load_w(i);
+      pdl_wait();
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % STAGES;
+        if (i >= STAGES) {
+          if (!mbar_wait(smem_u32(&sm.mma_done[s]), ((i / STAGES) - 1) & 1, abort_flag)) break;
+          // the small weight tile first, on its own barrier, so that its
+          // dequantisation starts before the activation tile has landed
+          load_w(i);
+        }
+        const uint32_t xbar = smem_u32(&sm.x_full[s]);
         mbar_expect_tx(xbar, BT * 128);
-        tma_load_2d(smem_u32(sm.x[s]), &tmap_x, kb * BK, tok0, xbar);
+        tma_load_2d(smem_u32(sm.x[s]), &tmap_x, (kb_lo + i) * BK, tok0, xbar);
         issued = i + 1;
       }
       // every copy issued has landed before the CTA can exit (immediate on the
       // normal path: the consumers have waited for them all)
-      for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i) {
+      for (int i = issued_w > STAGES ? issued_w - STAGES : 0; i < issued_w; ++i)
         mbar_drain(smem_u32(&sm.w_full[i % STAGES]), (i / STAGES) & 1);
+      for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i)
         mbar_drain(smem_u32(&sm.x_full[i % STAGES]), (i / STAGES) & 1);
-      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = instr_desc<BT, kF16>();
-      bool ok = true;
-      for (int i = 0; i < nkb && ok; ++i) {
+      // This thread's loop is the kernel's serial path (every barrier wait,
+      // MMA issue and commit here costs tens to ~150 cycles even when its
+      // operands are long ready), so it waits on ONE barrier per k block:
+      // a_full completes when the block's group has written the A stage and
+      // one of its warps has seen the X tile land.
+      for (int i = 0; i < nkb; ++i) {
         const int s = i % STAGES;
-        const uint32_t ph = (i / STAGES) & 1;
-        ok = mbar_wait(smem_u32(&sm.x_full[s]), ph, abort_flag) &&
-             mbar_wait(smem_u32(&sm.a_full[s]), ph, abort_flag);
-        if (!ok) break;
+        if (!mbar_wait(smem_u32(&sm.a_full[s]), (i / STAGES) & 1, abort_flag)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a_tmem = tmem + (uint32_t)BT + (uint32_t)s * 32u, x_addr = smem_u32(sm.x[s]);
-#pragma unroll
-        for (int k = 0; k < BK / 16; ++k) {
-          const uint64_t bd = smem_desc(x_addr + k * 32);
-          const uint32_t accumulate = (i > 0 || k > 0) ? 1u : 0u;
-          // A: 128 lanes x 8 columns (16 codes) of the stage in tensor memory
-          asm volatile(
-              "{\n\t.reg .pred p;\n\t"
-              "setp.ne.b32 p, %4, 0;\n\t"
-              "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem),
-              "r"(a_tmem + (uint32_t)k * 8u), "l"(bd), "r"(idesc), "r"(accumulate)
-              : "memory");
-        }
+        // A: 128 lanes x 8 columns (16 codes) of the stage in tensor memory per
+        // MMA; B: the X stage, 32 bytes further per 16-wide k step (+2 in the
+        // descriptor's 16-byte address field, which cannot carry: shared
+        // addresses are below 2^18)
+        const uint32_t a_tmem = tmem + (uint32_t)BT + (uint32_t)s * 32u;
+        const uint64_t bd = smem_desc(smem_u32(sm.x[s]));
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "setp.eq.b32 q, %4, %4;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %6, %3, q;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %8, %3, q;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%9], %10, %3, q;\n\t}" ::"r"(tmem),
+            "r"(a_tmem), "l"(bd), "r"(idesc), "r"((uint32_t)i), "r"(a_tmem + 8u), "l"(bd + 2), "r"(a_tmem + 16u),
+            "l"(bd + 4), "r"(a_tmem + 24u), "l"(bd + 6)
+            : "memory");
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
                          "r"(smem_u32(&sm.mma_done[s]))
                      : "memory");
@@ -337,6 +359,11 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
       }
     };
     fetch_scale(grp);
+    // code2 (a weight table) into shared memory while the first copies land;
+    // the dequantisation threads alone meet at this barrier
+    if (p.nested)
+      for (int i = tid - 64; i < 256; i += DQ * 128) sm.code2[i] = p.code2[i];
+    asm volatile("bar.sync 1, %0;" ::"n"(DQ * 128) : "memory");
     // Row r's 32 packed bytes, its two 16-byte halves read in an order that
     // alternates every 4 rows: the warp's 16-byte reads then cover all 8
     // bank groups of each 128 bytes (no 2-way conflict).
@@ -376,15 +403,62 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
           : "memory");
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      // the group's first warp also sees the block's X tile land, so that
+      // a_full alone tells the MMA issuer both operands are ready
+      if ((warp & 3) == 0 && !mbar_wait(smem_u32(&sm.x_full[s]), (i / STAGES) & 1, abort_flag)) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&sm.a_full[s]));
     }
 
-    // Epilogue: TMEM lane quarter (warp % 4) holds weight rows 32q..32q+31.
+    // Epilogue. TMEM lane quarter (warp % 4) holds weight rows 32q..32q+31;
+    // each warp reads its column blocks (32 activation rows) with tcgen05.ld.
+    // Unsplit 128- and 256-row tiles store Y straight from those registers
+    // (a warp's store is 32 consecutive outputs of one activation row). The
+    // split-K partial sums and 64-row tiles go through the X ring (free once
+    // every MMA has completed) instead: stored transposed as fp32 [BT][BM],
+    // read back along n four outputs per thread and written as whole 8-byte
+    // (16-byte) runs of each activation row (measured on the S2-Pro
+    // projections: 2-14% faster on those launches, 7-11% slower on unsplit
+    // 128- and 256-row tiles).
+    float* stage = reinterpret_cast<float*>(&sm.x[0][0]);
+    pdl_wait();
+    constexpr bool kStaged = kSplit || BT == 64;
+    if (!kStaged) {
+      if (mbar_wait(smem_u32(&sm.accum_full), 0, abort_flag)) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int q = warp & 3;
+        const int n = n0 + q * 32 + lane;
+        for (int cb = grp; cb < BT / 32; cb += DQ) {
+          uint32_t v[32];
+          const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * 32);
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+              "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+              "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+              : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+                "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
+                "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
+                "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+                "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
+                "=r"(v[30]), "=r"(v[31])
+              : "r"(taddr));
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if (n < p.N) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int tok = tok0 + cb * 32 + i;
+              if (tok < p.M) {
+                const size_t o = (size_t)tok * p.N + n;
+                p.y[o] = epilogue<kF16>(__uint_as_float(v[i]), p.epi, p.operand, o);
+              }
+            }
+          }
+        }
+      }
+    } else {
     if (mbar_wait(smem_u32(&sm.accum_full), 0, abort_flag)) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int q = warp & 3;
-      const int n = n0 + q * 32 + lane;
       for (int cb = grp; cb < BT / 32; cb += DQ) {
         uint32_t v[32];
         const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * 32);
@@ -400,29 +474,55 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
               "=r"(v[30]), "=r"(v[31])
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (n < p.N && !kSplit) {
+        float* col = stage + (size_t)(cb * 32) * BM + q * 32 + lane;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int tok = tok0 + cb * 32 + i;
-            if (tok < p.M) {
-              const size_t o = (size_t)tok * p.N + n;
-              p.y[o] = epilogue<kF16>(__uint_as_float(v[i]), p.epi, p.operand, o);
-            }
+        for (int i = 0; i < 32; ++i) col[i * BM] = __uint_as_float(v[i]);
+      }
+    }
+    // every dequantisation thread reaches this barrier, aborting or not
+    asm volatile("bar.sync 1, %0;" ::"n"(DQ * 128) : "memory");
+    if (!*abort_flag) {
+      const int t = tid - 64;
+      const bool vec = (p.N & 3) == 0 && (kSplit || (((uintptr_t)p.y | (uintptr_t)p.operand) & 7) == 0);
+      float* part = kSplit ? p.partial + (size_t)z * p.M * p.N : nullptr;
+      for (int e = t; e < BT * (BM / 4); e += DQ * 128) {
+        const int tok = tok0 + e / (BM / 4), n = n0 + (e % (BM / 4)) * 4;
+        if (tok >= p.M || n >= p.N) continue;
+        const float4 a = *reinterpret_cast<const float4*>(stage + (size_t)e * 4);
+        const size_t o = (size_t)tok * p.N + n;
+        if (vec && kSplit) {
+          __stcg(reinterpret_cast<float4*>(part + o), a);
+        } else if (vec) {
+          float opv[4] = {0.f, 0.f, 0.f, 0.f};
+          if (p.epi != NF4B_EPI_NONE) {
+            const uint2 ov = *reinterpret_cast<const uint2*>(p.operand + o);
+            opv[0] = act2f<kF16>((uint16_t)(ov.x & 0xFFFFu));
+            opv[1] = act2f<kF16>((uint16_t)(ov.x >> 16));
+            opv[2] = act2f<kF16>((uint16_t)(ov.y & 0xFFFFu));
+            opv[3] = act2f<kF16>((uint16_t)(ov.y >> 16));
           }
-        } else if (n < p.N) {
-          float* part = p.partial + (size_t)z * p.M * p.N + n;
+          const uint32_t y0 = epilogue_value<kF16>(a.x, p.epi, opv[0]), y1 = epilogue_value<kF16>(a.y, p.epi, opv[1]);
+          const uint32_t y2 = epilogue_value<kF16>(a.z, p.epi, opv[2]), y3 = epilogue_value<kF16>(a.w, p.epi, opv[3]);
+          *reinterpret_cast<uint2*>(p.y + o) = make_uint2(y0 | (y1 << 16), y2 | (y3 << 16));
+        } else {
+          const float av[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int tok = tok0 + cb * 32 + i;
-            if (tok < p.M) __stcg(part + (size_t)tok * p.N, __uint_as_float(v[i]));
+          for (int c = 0; c < 4; ++c) {
+            if (n + c >= p.N) break;
+            if (kSplit)
+              __stcg(part + o + c, av[c]);
+            else
+              p.y[o + c] = epilogue<kF16>(av[c], p.epi, p.operand, o + c);
           }
         }
       }
+    }
     }
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   if (kSplit) __threadfence();  // this thread's partial stores, before the tile's count below
+  if (warp < 2) pdl_wait();  // the split's counters below belong to the previous work as well
   __syncthreads();
   pdl_launch_dependents();
   if (warp == 1) {
