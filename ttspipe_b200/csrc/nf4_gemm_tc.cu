@@ -13,10 +13,12 @@
 //              ring_stages<BT>()-deep ring, completion via mbarrier transaction
 //              counts; the first ring's weight tiles are requested before the
 //              dependency wait (weights are not the previous launch's output).
-//   warp 1     allocates TMEM (BT fp32 columns) and, from one thread, issues
-//              4 x tcgen05.mma (M=128, N=BT, K=16) per k block, committing each
-//              stage back to the producer and the whole tile to the epilogue.
-//   warps 2-17 four groups of four warps, k blocks round-robin over the
+//   warps 1-2  warp 1 allocates TMEM; one thread of each (of warp 1 only for
+//              256-row tiles) issues 4 x tcgen05.mma (M=128, N=BT, K=16) per
+//              k block of its share, into its own fp32 accumulator (BT
+//              columns), committing each stage back to the producer and the
+//              whole tile to the epilogue.
+//   warps 3-18 four groups of four warps, k blocks round-robin over the
 //              groups, dequantise: lane l of warp w owns weight row
 //              32 (w % 4) + l of the tile; it forms the
 //              block's scale (plain fp32, or code2[a8] * absmax2 + offset as two
@@ -58,8 +60,20 @@ constexpr int BK = 64;
 // runs ~170 byte-permute instructions (~1000 cycles per group and block); four
 // groups measured faster than two or three, and five or six (more threads,
 // fewer registers each) slower again.
+// Warps 0-2 are the producer and the MMA issuers; the dequantisation warps
+// follow.
+constexpr int kControlWarps = 3;
 template <int DQ>
-constexpr int gemm_threads() { return 64 + 128 * DQ; }
+constexpr int gemm_threads() { return 32 * kControlWarps + 128 * DQ; }
+// MMA issuing threads: each thread's issue loop (barrier wait, fence, four
+// MMAs, commit: ~630 cycles per k block, whatever the tile's width) is the
+// kernel's serial path for narrow tiles, so 64- and 128-row tiles use two,
+// in different warps, taking alternate k blocks into two accumulators that
+// the epilogue adds (even blocks' sum + odd blocks' sum). 256-row tiles have
+// no tensor memory for a second accumulator, and their MMAs take about as
+// long as the issue loop.
+template <int BT>
+__host__ __device__ constexpr int mma_issuers() { return BT <= 128 ? 2 : 1; }
 constexpr int kDequantGroups = 4;
 // Ring depth: 4 stages (8 for the 64-row tiles, which fit twice as many in
 // the same shared memory; deeper rings measured no faster). The depth must be
@@ -77,8 +91,10 @@ __host__ __device__ constexpr int ring_stages() { return BT >= 128 ? 4 : 8; }
 // next power of two.
 template <int BT>
 __host__ __device__ constexpr uint32_t tmem_cols() {
-  return (BT + ring_stages<BT>() * 32) <= 256 ? 256u : 512u;
+  return (mma_issuers<BT>() * BT + ring_stages<BT>() * 32) <= 256 ? 256u : 512u;
 }
+static_assert(2 * 128 + 4 * 32 <= 512 && 2 * 64 + 8 * 32 <= 512 && 256 + 4 * 32 <= 512,
+              "accumulators and A ring exceed tensor memory");
 static_assert(ring_stages<256>() % kDequantGroups == 0 && ring_stages<128>() % kDequantGroups == 0 &&
                   ring_stages<64>() % kDequantGroups == 0,
               "ring depth must be a multiple of the dequantisation groups");
@@ -199,6 +215,36 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// 32 consecutive fp32 columns of this warp's tensor-memory lane quarter.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// The tile's accumulated sums for 32 activation rows (columns c0..c0+31) of
+// this warp's 32 weight rows: the first accumulator, plus the second one's
+// (at column offset `second`) when two issuers wrote it.
+template <int NI>
+__device__ __forceinline__ void acc_columns(uint32_t taddr, uint32_t second, bool use_second, float (&a)[32]) {
+  uint32_t v[32];
+  tmem_ld32(taddr, v);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) a[i] = __uint_as_float(v[i]);
+  if (NI == 2 && use_second) {
+    tmem_ld32(taddr + second, v);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) a[i] = __fadd_rn(a[i], __uint_as_float(v[i]));
+  }
+}
+
 // K-major, 128-byte-swizzled operand: rows of 128 B, 8-row atoms of 1024 B.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   uint64_t d = (uint64_t)((addr >> 4) & 0x3FFFu);
@@ -246,7 +292,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
       mbar_init(smem_u32(&sm.a_full[s]), 4);
       mbar_init(smem_u32(&sm.mma_done[s]), 1);
     }
-    mbar_init(smem_u32(&sm.accum_full), 1);
+    mbar_init(smem_u32(&sm.accum_full), mma_issuers<BT>());
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -296,15 +342,18 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
       for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i)
         mbar_drain(smem_u32(&sm.x_full[i % STAGES]), (i / STAGES) & 1);
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
+  } else if (warp < kControlWarps) {
+    constexpr int NI = mma_issuers<BT>();
+    const int j = warp - 1;  // issuer j takes k blocks j, j + NI, ... into accumulator j
+    if (lane == 0 && j < NI) {
       constexpr uint32_t idesc = instr_desc<BT, kF16>();
       // This thread's loop is the kernel's serial path (every barrier wait,
       // MMA issue and commit here costs tens to ~150 cycles even when its
       // operands are long ready), so it waits on ONE barrier per k block:
       // a_full completes when the block's group has written the A stage and
       // one of its warps has seen the X tile land.
-      for (int i = 0; i < nkb; ++i) {
+      const uint32_t d_tmem = tmem + (uint32_t)(j * BT);
+      for (int i = j; i < nkb; i += NI) {
         const int s = i % STAGES;
         if (!mbar_wait(smem_u32(&sm.a_full[s]), (i / STAGES) & 1, abort_flag)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -312,7 +361,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
         // MMA; B: the X stage, 32 bytes further per 16-wide k step (+2 in the
         // descriptor's 16-byte address field, which cannot carry: shared
         // addresses are below 2^18)
-        const uint32_t a_tmem = tmem + (uint32_t)BT + (uint32_t)s * 32u;
+        const uint32_t a_tmem = tmem + (uint32_t)(NI * BT) + (uint32_t)s * 32u;
         const uint64_t bd = smem_desc(smem_u32(sm.x[s]));
         asm volatile(
             "{\n\t.reg .pred p, q;\n\t"
@@ -321,8 +370,8 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
             "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
             "tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %6, %3, q;\n\t"
             "tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %8, %3, q;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%9], %10, %3, q;\n\t}" ::"r"(tmem),
-            "r"(a_tmem), "l"(bd), "r"(idesc), "r"((uint32_t)i), "r"(a_tmem + 8u), "l"(bd + 2), "r"(a_tmem + 16u),
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%9], %10, %3, q;\n\t}" ::"r"(d_tmem),
+            "r"(a_tmem), "l"(bd), "r"(idesc), "r"((uint32_t)(i - j)), "r"(a_tmem + 8u), "l"(bd + 2), "r"(a_tmem + 16u),
             "l"(bd + 4), "r"(a_tmem + 24u), "l"(bd + 6)
             : "memory");
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
@@ -338,11 +387,11 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
   } else {
     // Dequantise: lane l of a warp owns weight row r = 32 (warp % 4) + l of the
     // tile - its tensor-memory lane, the only lane quarter the warp may write.
-    const int grp = (warp - 2) >> 2;
+    const int grp = (warp - kControlWarps) >> 2;
     const int r = (warp & 3) * 32 + lane;
     const int row = n0 + r;
     const bool valid = row < p.N;
-    const uint32_t a_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)BT;
+    const uint32_t a_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(mma_issuers<BT>() * BT);
     // The block scale's global loads run one of this group's k blocks ahead,
     // so their latency hides under the previous block's dequantisation.
     uint32_t code_next = 0;
@@ -362,7 +411,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
     // code2 (a weight table) into shared memory while the first copies land;
     // the dequantisation threads alone meet at this barrier
     if (p.nested)
-      for (int i = tid - 64; i < 256; i += DQ * 128) sm.code2[i] = p.code2[i];
+      for (int i = tid - 32 * kControlWarps; i < 256; i += DQ * 128) sm.code2[i] = p.code2[i];
     asm volatile("bar.sync 1, %0;" ::"n"(DQ * 128) : "memory");
     // Row r's 32 packed bytes, its two 16-byte halves read in an order that
     // alternates every 4 rows: the warp's 16-byte reads then cover all 8
@@ -429,27 +478,16 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
         const int q = warp & 3;
         const int n = n0 + q * 32 + lane;
         for (int cb = grp; cb < BT / 32; cb += DQ) {
-          uint32_t v[32];
-          const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * 32);
-          asm volatile(
-              "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-              "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-              "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-              : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
-                "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
-                "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
-                "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-                "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
-                "=r"(v[30]), "=r"(v[31])
-              : "r"(taddr));
-          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          float a[32];
+          acc_columns<mma_issuers<BT>()>(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * 32), (uint32_t)BT,
+                                         nkb > 1, a);
           if (n < p.N) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               const int tok = tok0 + cb * 32 + i;
               if (tok < p.M) {
                 const size_t o = (size_t)tok * p.N + n;
-                p.y[o] = epilogue<kF16>(__uint_as_float(v[i]), p.epi, p.operand, o);
+                p.y[o] = epilogue<kF16>(a[i], p.epi, p.operand, o);
               }
             }
           }
@@ -460,29 +498,18 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int q = warp & 3;
       for (int cb = grp; cb < BT / 32; cb += DQ) {
-        uint32_t v[32];
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * 32);
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-            "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
-              "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
-              "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
-              "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-              "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
-              "=r"(v[30]), "=r"(v[31])
-            : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        float a[32];
+        acc_columns<mma_issuers<BT>()>(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * 32), (uint32_t)BT,
+                                       nkb > 1, a);
         float* col = stage + (size_t)(cb * 32) * BM + q * 32 + lane;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) col[i * BM] = __uint_as_float(v[i]);
+        for (int i = 0; i < 32; ++i) col[i * BM] = a[i];
       }
     }
     // every dequantisation thread reaches this barrier, aborting or not
     asm volatile("bar.sync 1, %0;" ::"n"(DQ * 128) : "memory");
     if (!*abort_flag) {
-      const int t = tid - 64;
+      const int t = tid - 32 * kControlWarps;
       const bool vec = (p.N & 3) == 0 && (kSplit || (((uintptr_t)p.y | (uintptr_t)p.operand) & 7) == 0);
       float* part = kSplit ? p.partial + (size_t)z * p.M * p.N : nullptr;
       for (int e = t; e < BT * (BM / 4); e += DQ * 128) {
@@ -522,7 +549,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   if (kSplit) __threadfence();  // this thread's partial stores, before the tile's count below
-  if (warp < 2) pdl_wait();  // the split's counters below belong to the previous work as well
+  if (warp < kControlWarps) pdl_wait();  // the split's counters below belong to the previous work as well
   __syncthreads();
   pdl_launch_dependents();
   if (warp == 1) {
