@@ -689,17 +689,17 @@ cudaError_t launch_bt(const GemmParams& p, cudaStream_t stream) {
 
 
 // Tile rows (BT) and k splits of a GEMM, from a cost model fitted to a sweep of
-// the S2-Pro projections at 32..1024 rows over BT in {64, 128, 256} and 1..8
-// splits: a CTA costs ~6 k-block times of fixed work (pipeline fill, epilogue)
-// plus its k blocks at a rate set by the dequantisation (relative cost 0.7,
-// 0.75, 1 per k block for 64-, 128-, 256-row tiles); CTAs beyond one per SM run
-// in further rounds (a second resident CTA shares the SM's dequantisation
-// rate, so it does not count as free); each split adds its partial sums'
-// write and reduction (1.5, 3, 10 k-block times). Examples it reproduces:
-// 2560x9728 at M = 256, 6 splits of 256-row tiles (a 128-row 3-split within
-// 5%) where a 64-row 3-split took 58 us against 33; 2560x4096 at M = 256,
-// 128-row tiles in 3 splits (21 against 33 us); the 9728-row gate and up
-// projections unsplit 256-row tiles (one CTA per tile is cheapest there).
+// the S2-Pro projections (6144x2560, 2560x4096, 9728x2560, 2560x9728) at 32..4096
+// rows over BT in {64, 128, 256} and 1..8 splits: a CTA costs ~10 k-block
+// times of fixed work (pipeline fill, epilogue) plus its k blocks (relative
+// cost 0.8, 1, 1 per k block for 64-, 128-, 256-row tiles: the MMA issue loop
+// and the dequantisation, not the tile's MMA width, set a k block's time);
+// CTAs beyond one per SM run in further rounds; each split adds its partial
+// sums' write and reduction (1.5, 3, 15 k-block times). On that sweep its pick
+// is the fastest measured (bt, splits) or within 7% of it for every shape and
+// row count (e.g. 2560x9728: 6 splits of 64-row tiles at M = 32-64, 3 splits
+// of 128-row tiles at M = 256, unsplit 256-row tiles from M = 1024; the
+// 9728-row gate and up projections unsplit, one CTA per tile).
 struct GemmShape {
   int bt, splits;
 };
@@ -708,7 +708,7 @@ static GemmShape gemm_choose(int N, int M, int K, int sms) {
   const long long tn = (N + BM - 1) / BM;
   const int KB = K / BK;
   const int bts[3] = {64, 128, 256};
-  const double cost_kb[3] = {0.7, 0.75, 1.0}, cost_split[3] = {1.5, 3.0, 10.0};
+  const double cost_kb[3] = {0.8, 1.0, 1.0}, cost_split[3] = {1.5, 3.0, 15.0};
   const int splits[6] = {1, 2, 3, 4, 6, 8};
   GemmShape best = {64, 1};
   double best_t = 1e30;
@@ -721,7 +721,7 @@ static GemmShape gemm_choose(int N, int M, int K, int sms) {
       if (sp > 1 && (KB / sp < 4 || tiles * (long long)sizeof(int) > (long long)GEMM_COUNTER_BYTES)) continue;
       const long long ctas = tiles * sp;
       const long long rounds = (ctas + sms - 1) / sms;
-      const double t = (double)rounds * ((double)((KB + sp - 1) / sp) * cost_kb[bi] + 6.0) +
+      const double t = (double)rounds * ((double)((KB + sp - 1) / sp) * cost_kb[bi] + 10.0) +
                        (sp > 1 ? sp * cost_split[bi] : 0.0);
       if (t < best_t - 1e-9) {
         best_t = t;
