@@ -14,7 +14,7 @@
 //              counts; the first ring's weight tiles are requested before the
 //              dependency wait (weights are not the previous launch's output).
 //   warps 1-2  warp 1 allocates TMEM; one thread of each (of warp 1 only for
-//              256-row tiles) issues 4 x tcgen05.mma (M=128, N=BT, K=16) per
+//              128- and 256-row tiles) issues 4 x tcgen05.mma (M=128, N=BT, K=16) per
 //              k block of its share, into its own fp32 accumulator (BT
 //              columns), committing each stage back to the producer and the
 //              whole tile to the epilogue.
@@ -54,9 +54,8 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-// Warp 0: TMA producer; warp 1: TMEM owner + MMA issuer; then DQ groups of
-// four dequantisation/epilogue warps (group g serves k blocks g, g + DQ, ...).
-// Per 64-block each dequantisation thread builds its row's scaled table and
+// DQ groups of four dequantisation/epilogue warps (group g serves k blocks
+// g, g + DQ, ...) follow the control warps. Per 64-block each dequantisation thread builds its row's scaled table and
 // runs ~170 byte-permute instructions (~1000 cycles per group and block); four
 // groups measured faster than two or three, and five or six (more threads,
 // fewer registers each) slower again.
@@ -67,13 +66,14 @@ template <int DQ>
 constexpr int gemm_threads() { return 32 * kControlWarps + 128 * DQ; }
 // MMA issuing threads: each thread's issue loop (barrier wait, fence, four
 // MMAs, commit: ~630 cycles per k block, whatever the tile's width) is the
-// kernel's serial path for narrow tiles, so 64- and 128-row tiles use two,
+// kernel's serial path for 64-row tiles (batched decode), so those use two,
 // in different warps, taking alternate k blocks into two accumulators that
-// the epilogue adds (even blocks' sum + odd blocks' sum). 256-row tiles have
-// no tensor memory for a second accumulator, and their MMAs take about as
-// long as the issue loop.
+// the epilogue adds (even blocks' sum + odd blocks' sum). Wider tiles keep one:
+// with weights streamed cold from HBM a second issuer on 128-row tiles measured
+// 3.5% slower at M = 256 (nothing gained with warm weights), and 256-row tiles
+// have no tensor memory for a second accumulator.
 template <int BT>
-__host__ __device__ constexpr int mma_issuers() { return BT <= 128 ? 2 : 1; }
+__host__ __device__ constexpr int mma_issuers() { return BT <= 64 ? 2 : 1; }
 constexpr int kDequantGroups = 4;
 // Ring depth: 4 stages (8 for the 64-row tiles, which fit twice as many in
 // the same shared memory; deeper rings measured no faster). The depth must be
@@ -84,7 +84,8 @@ constexpr int kDequantGroups = 4;
 // read a stale tile.
 template <int BT>
 __host__ __device__ constexpr int ring_stages() { return BT >= 128 ? 4 : 8; }
-// Tensor memory per CTA: the fp32 accumulator (BT columns), then the A ring -
+// Tensor memory per CTA: the fp32 accumulators (one per MMA issuer, BT
+// columns each), then the A ring -
 // the dequantised weight tiles, 128 lanes (weight rows) x 32 columns (64 bf16
 // or fp16 codes, two per column) per stage, which the MMA reads straight from
 // tensor memory, so A never passes through shared memory. Allocated as the
