@@ -17,6 +17,8 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "gemv_unit.cuh"
+#include "tmap.cuh"
 
 namespace nf4b {
 
@@ -285,13 +287,10 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(
 // 8 warps. (16 warps for groups of <= 4 query heads measured 0.6 us faster
 // at 2048 rows, four chunks per CTA, but 0.8-1 us slower for windows of one
 // or two chunks per CTA, which the fast AR and most slow-AR positions use.)
+// Warp w takes key rows 8w .. 8w + 7 of every 64-row chunk.
 template <int G>
 __host__ __device__ constexpr int cthreads() { return 256; }
-template <int G>
-__host__ __device__ constexpr int rows_per_warp() { return ATTN_CHUNK / (cthreads<G>() / 32); }  // score rows
-template <int G>
-__host__ __device__ constexpr int pv_rows() { return ATTN_CHUNK / (cthreads<G>() / 16); }  // P.V rows per thread
-static_assert(rows_per_warp<4>() % 4 == 0 && rows_per_warp<8>() % 4 == 0 && pv_rows<4>() >= 1, "chunk split");
+static_assert(ATTN_CHUNK == 8 * (256 / 32), "a chunk is 8 key rows per warp");
 
 // Stages of the cluster kernel's K/V ring: every chunk of a CTA's share is in
 // flight at once up to this depth (a 2048-row window over 8 CTAs is 4 chunks
@@ -300,20 +299,44 @@ constexpr int kCStages = 4;
 
 template <int G>
 struct ClusterSmem {
-  alignas(128) uint16_t kv[kCStages][2][ATTN_CHUNK * kD];  // [stage][K, V][rows x 128]
+  // [stage][K, V]: 64 rows x 128 dims as two 8 KB boxes (dims 0-63, 64-127),
+  // each written by a 2-D TMA copy in the 128-byte swizzle: row r's 16-byte
+  // chunk c sits at chunk c ^ (r & 7) of its 128-byte line (kv_off).
+  alignas(1024) uint16_t kv[kCStages][2][ATTN_CHUNK * kD];
   float q[G][kD];
-  float sc[G][ATTN_CHUNK];
-  float red[cthreads<G>() / 32][G][kD];
+  float red[cthreads<G>() / 32][G][kD];  // each warp's partial output
+  float wm[cthreads<G>() / 32][G], wl[cthreads<G>() / 32][G];  // and its max and sum
   float part_acc[G][kD];
   float part_m[G], part_l[G];
-  float alpha[G];
-  float run_m[G], run_l[G];
   unsigned long long bar[kCStages];
   // the fused q/k norm + rotary prologue (QkvIn)
   float sx[2][kD];
   double nred[cthreads<G>() / 32];
   uint16_t knew[kD], vnew[kD];
 };
+
+// Byte offset of (row r, dimension d) in a K or V stage (see ClusterSmem::kv).
+__device__ __forceinline__ uint32_t kv_off(int r, int d) {
+  return (uint32_t)((d >> 6) * 8192 + r * 128 + ((((d >> 3) & 7) ^ (r & 7)) << 4) + ((d & 7) << 1));
+}
+
+// One 64-dimension x 64-row box of a K or V cache (a 2-D map over
+// [n_kv * max_len rows, 128 dims]; rows past the end are zero-filled).
+__device__ __forceinline__ void tma_box(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Four 8x8 16-bit matrices, transposed (MMA B fragments of a [k][n] row-major tile).
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -378,10 +401,14 @@ template <int G, bool F16>
 __global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel(
     const bf16_t* __restrict__ q, const bf16_t* __restrict__ kc, const bf16_t* __restrict__ vc,
     const int64_t* __restrict__ pos_ptr, const uint8_t* __restrict__ mask, bf16_t* __restrict__ out,
-    int max_len, int window, float scale, const QkvIn in) {
-  constexpr int kCT = cthreads<G>(), kRPW = rows_per_warp<G>(), kPVR = pv_rows<G>();
+    int max_len, int window, float scale, const QkvIn in, const __grid_constant__ CUtensorMap tmk,
+    const __grid_constant__ CUtensorMap tmv) {
+  constexpr int kCT = cthreads<G>();
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  ClusterSmem<G>& sm = *reinterpret_cast<ClusterSmem<G>*>(smem_raw);
+  // 1024-byte aligned for the swizzled boxes (the launch adds 1 KB of slack);
+  // the same offset in every CTA of a cluster, as the merge's mapa needs
+  ClusterSmem<G>& sm = *reinterpret_cast<ClusterSmem<G>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                          ~(uintptr_t)1023);
   const int kh = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t rank = cluster_rank(), C = cluster_size();
@@ -396,22 +423,23 @@ __global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel
   // out before the position is read - the whole window, rows past the live
   // length are never used - saving a round trip.
   const bool whole_window = C == 1 && window <= ATTN_CHUNK;
+  // Every chunk is four whole boxes (K and V, two 64-dimension halves each),
+  // 32 KB of transaction bytes whatever its live rows.
+  auto copy_chunk = [&](int stg, long long row0) {  // one thread
+    const uint32_t bar = sm_u32(&sm.bar[stg]);
+    const int y = (int)((long long)kh * max_len + row0);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(4 * 8192) : "memory");
+    tma_box(sm_u32(sm.kv[stg][0]), &tmk, 0, y, bar);
+    tma_box(sm_u32(sm.kv[stg][0]) + 8192, &tmk, 64, y, bar);
+    tma_box(sm_u32(sm.kv[stg][1]), &tmv, 0, y, bar);
+    tma_box(sm_u32(sm.kv[stg][1]) + 8192, &tmv, 64, y, bar);
+  };
   if (whole_window && threadIdx.x == 0) {
-    const uint32_t bytes = (uint32_t)window * kD * 2;
-    const uint32_t bar = sm_u32(&sm.bar[0]);
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&sm.bar[0])) : "memory");
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&sm.bar[1])) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     sm_u32(sm.kv[0][0])),
-                 "l"(kc + (size_t)kh * max_len * kD), "r"(bytes), "r"(bar)
-                 : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     sm_u32(sm.kv[0][1])),
-                 "l"(vc + (size_t)kh * max_len * kD), "r"(bytes), "r"(bar)
-                 : "memory");
+    copy_chunk(0, 0);
   }
   long long L = (pos_ptr != nullptr) ? pos_ptr[0] + 1 : (long long)window;
   if (L > window) L = window;
@@ -423,26 +451,8 @@ __global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel
   long long r1 = r0 + per * ATTN_CHUNK;
   if (r1 > L) r1 = L;
   const int my_chunks = r1 > r0 ? (int)((r1 - r0 + ATTN_CHUNK - 1) / ATTN_CHUNK) : 0;
-  const bf16_t* kbase = kc + (size_t)kh * max_len * kD;
-  const bf16_t* vbase = vc + (size_t)kh * max_len * kD;
-
-  auto issue = [&](int ci) {  // thread 0: chunk ci into stage ci % kCStages
-    const long long j0 = r0 + (long long)ci * ATTN_CHUNK;
-    const long long n = (r1 - j0 < ATTN_CHUNK) ? r1 - j0 : ATTN_CHUNK;
-    const uint32_t bytes = (uint32_t)n * kD * 2;
-    const int stg = ci % kCStages;
-    const uint32_t bar = sm_u32(&sm.bar[stg]);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     sm_u32(sm.kv[stg][0])),
-                 "l"(kbase + j0 * kD), "r"(bytes), "r"(bar)
-                 : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     sm_u32(sm.kv[stg][1])),
-                 "l"(vbase + j0 * kD), "r"(bytes), "r"(bar)
-                 : "memory");
-  };
+  // thread 0: chunk ci into stage ci % kCStages
+  auto issue = [&](int ci) { copy_chunk(ci % kCStages, r0 + (long long)ci * ATTN_CHUNK); };
   if (tid == 0 && !whole_window) {
     for (int i = 0; i < kCStages; ++i)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_u32(&sm.bar[i])) : "memory");
@@ -499,34 +509,30 @@ __global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel
       cache[((size_t)kh * max_len + p_new) * kD + d] = nb;
     }
   }
-  if (tid < G) {
-    sm.run_m[tid] = -INFINITY;
-    sm.run_l[tid] = 0.f;
-  }
   __syncthreads();
 
-  const int dg = tid & 15, pg = tid >> 4;  // P.V: dimensions dg*8 .. +7, chunk rows pg*kPVR .. +kPVR-1
-  // This lane's slice of every query head for the scores (dimensions
-  // (lane & 7) * 8 .. +7 and 64 + (lane & 7) * 8 .. +7, so that the eight lanes
-  // of a key row read 128 contiguous bytes per load: no bank conflicts), held
-  // in registers as pairs of the activation type - the values are of that
-  // type already - instead of re-reading shared memory for every key row.
-  uint32_t qr[G][8];
-  {
-    const int li = lane & 7;
+  // Tensor-core form (mma.sync m16n8k16, fp32 accumulators): the query heads
+  // are the A rows (G of 16 used), warp w's 8 key rows of a chunk the score
+  // tile's columns, so lane (g, t) = (lane / 4, lane % 4) gets head g's
+  // scores for keys 8w + 2t and 8w + 2t + 1, and those two values, rounded to
+  // the activation type, are already its A fragment for the P.V product
+  // (keys as k, the 128 dimensions as 16 column tiles). Each warp keeps its own
+  // online softmax (max, sum, output) for its rows; the eight are merged once
+  // at the end.
+  const int g = lane >> 2, t = lane & 3;
+  uint32_t qa[8][2];  // A fragments of the 8 k steps: dims 16s + 2t (+1) and 16s + 2t + 8 (+9)
 #pragma unroll
-    for (int h = 0; h < G; ++h)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int d0 = (e < 4 ? 0 : 64) + li * 8 + 2 * (e & 3);
-        qr[h][e] = pack_act2<F16>(sm.q[h][d0], sm.q[h][d0 + 1]);
-      }
+  for (int st = 0; st < 8; ++st) {
+    const int d0 = 16 * st + 2 * t;
+    qa[st][0] = g < G ? pack_act2<F16>(sm.q[g < G ? g : 0][d0], sm.q[g < G ? g : 0][d0 + 1]) : 0u;
+    qa[st][1] = g < G ? pack_act2<F16>(sm.q[g < G ? g : 0][d0 + 8], sm.q[g < G ? g : 0][d0 + 9]) : 0u;
   }
-  float acc[G][8];
+  float acc[16][4];  // output tile j: head g, dimensions 8j + 2t, 8j + 2t + 1 (and unused head g + 8)
 #pragma unroll
-  for (int h = 0; h < G; ++h)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[h][e] = 0.f;
+  for (int j = 0; j < 16; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  float wmax = -INFINITY, wsum = 0.f;  // this warp's running max and sum for head g
+  const int kr = 8 * warp + g;         // the key row of this lane's score B fragments
+  const int vr = 8 * warp + (lane & 7);  // the key row whose address this lane gives ldmatrix
   bool ok = true;
   for (int ci = 0; ci < my_chunks; ++ci) {
     const int stg = ci % kCStages;
@@ -544,125 +550,105 @@ __global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel
     }
     const long long j0 = r0 + (long long)ci * ATTN_CHUNK;
     const int rows = (int)((r1 - j0 < ATTN_CHUNK) ? r1 - j0 : ATTN_CHUNK);
+    uint8_t* kst = reinterpret_cast<uint8_t*>(sm.kv[stg][0]);
+    uint8_t* vst = reinterpret_cast<uint8_t*>(sm.kv[stg][1]);
     if (fused && p_new >= j0 && p_new < j0 + rows) {
       // the copy may predate rank 0's store of the new row: use the computed one
       const int d = tid & (kD - 1), half = tid >> 7;
-      if (half < 2) sm.kv[stg][half][(int)(p_new - j0) * kD + d] = (half ? sm.vnew : sm.knew)[d];
+      if (half < 2)
+        *reinterpret_cast<uint16_t*>((half ? vst : kst) + kv_off((int)(p_new - j0), d)) =
+            (half ? sm.vnew : sm.knew)[d];
       __syncthreads();
     }
-    const uint16_t* ks = sm.kv[stg][0];
-    const uint16_t* vs = sm.kv[stg][1];
-    // Scores: a warp takes 8 rows, four at a time, eight lanes per row.
-    {
-      const int gi = lane >> 3, li = lane & 7;
+    // Rows that are masked or past the live length: their V rows are zeroed
+    // before the P.V product (their weights are zero, and whatever the stage
+    // holds - NaN included - must not reach the sums); their scores are
+    // replaced by -inf below, whatever the K bytes hold.
 #pragma unroll
-      for (int it = 0; it < kRPW / 4; ++it) {
-        const int jl = warp * kRPW + it * 4 + gi;
-        // Every row's loads and products are computed (no branch, so the loads
-        // issue together); rows that are masked or past the live length are
-        // stored as -inf below, whatever their stage bytes hold. Two
-        // accumulators per head halve the dependent FMA chain.
-        float dot[G], dot2[G];
-#pragma unroll
-        for (int h = 0; h < G; ++h) dot[h] = dot2[h] = 0.f;
-        const bool vis = ok && jl < rows && (mask == nullptr || mask[j0 + jl] != 0);
-        const uint4* kr = reinterpret_cast<const uint4*>(ks + jl * kD);
-        const uint4 k0 = kr[li], k1 = kr[8 + li];
-        const uint32_t kw[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float ka = act_lo<F16>(kw[e]), kb = act_hi<F16>(kw[e]);
-#pragma unroll
-          for (int h = 0; h < G; ++h) {
-            float& d = (e & 1) ? dot2[h] : dot[h];
-            d = fmaf(act_lo<F16>(qr[h][e]), ka, d);
-            d = fmaf(act_hi<F16>(qr[h][e]), kb, d);
-          }
-        }
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-          float v = dot[h] + dot2[h];
-          v += __shfl_xor_sync(0xffffffffu, v, 4);
-          v += __shfl_xor_sync(0xffffffffu, v, 2);
-          v += __shfl_xor_sync(0xffffffffu, v, 1);
-          if (li == 0) sm.sc[h][jl] = vis ? __fmul_rn(round_act<F16>(v), scale) : -INFINITY;
-        }
-      }
-    }
-    __syncthreads();
-    // Online softmax update per head (a warp per head).
-    for (int h = warp; h < G; h += kCT / 32) {
-      const float a = sm.sc[h][lane], b = sm.sc[h][lane + 32];
-      float mc = fmaxf(a, b);
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, off));
-      const float mo = sm.run_m[h];
-      const float mn = fmaxf(mo, mc);
-      const float al = (mn == -INFINITY) ? 1.f : expf(mo - mn);
-      const float pa = (a == -INFINITY) ? 0.f : expf(a - mn);
-      const float pb = (b == -INFINITY) ? 0.f : expf(b - mn);
-      sm.sc[h][lane] = pa;
-      sm.sc[h][lane + 32] = pb;
-      float l = pa + pb;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-      __syncwarp();
-      if (lane == 0) {
-        sm.alpha[h] = al;
-        sm.run_l[h] = sm.run_l[h] * al + l;
-        sm.run_m[h] = mn;
-      }
-    }
-    __syncthreads();
-    // P.V for this chunk. Masked and past-the-end rows contribute exact zeros:
-    // their V words are replaced by zero before any multiply (their weights
-    // are zero too), so whatever the stage bytes hold (NaN included) never
-    // reaches the sums; all rows' loads issue together.
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const float al = sm.alpha[h];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[h][e] *= al;
-    }
-#pragma unroll
-    for (int r = 0; r < kPVR; ++r) {
-      const int jl = pg * kPVR + r;
+    for (int i = 0; i < 8; ++i) {
+      const int jl = 8 * warp + i;
       const bool live = jl < rows && (mask == nullptr || mask[j0 + jl] != 0);
-      const uint4 raw = *reinterpret_cast<const uint4*>(vs + jl * kD + dg * 8);
-      const uint4 vv = live ? raw : make_uint4(0u, 0u, 0u, 0u);
-      const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
+      if (!live && lane < 16) *reinterpret_cast<uint4*>(vst + (lane >> 3) * 8192 + jl * 128 + (lane & 7) * 16) =
+          make_uint4(0u, 0u, 0u, 0u);
+    }
+    __syncwarp();
+    // Scores: 8 k steps of 16 dimensions; the B fragment words of key row kr
+    // (dims 16s + 2t, +1 and 16s + 2t + 8, +9) are conflict-free thanks to the swizzle.
+    float sd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float p = sm.sc[h][jl];
+    for (int st = 0; st < 8; ++st) {
+      const int d0 = 16 * st + 2 * t;
+      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kst + kv_off(kr, d0));
+      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kst + kv_off(kr, d0 + 8));
+      mma_act<F16>(sd, qa[st][0], 0u, qa[st][1], 0u, b0, b1);
+    }
+    const int k0 = 8 * warp + 2 * t;
+    const bool vis0 = k0 < rows && (mask == nullptr || mask[j0 + k0] != 0);
+    const bool vis1 = k0 + 1 < rows && (mask == nullptr || mask[j0 + k0 + 1] != 0);
+    const float s0 = vis0 ? __fmul_rn(round_act<F16>(sd[0]), scale) : -INFINITY;
+    const float s1 = vis1 ? __fmul_rn(round_act<F16>(sd[1]), scale) : -INFINITY;
+    // Online softmax of head g over this warp's rows (the quad t = 0..3).
+    float mc = fmaxf(s0, s1);
+    mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, 1));
+    mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, 2));
+    const float mn = fmaxf(wmax, mc);
+    const float al = (mn == -INFINITY) ? 1.f : expf(wmax - mn);
+    const float p0 = (s0 == -INFINITY) ? 0.f : expf(s0 - mn);
+    const float p1 = (s1 == -INFINITY) ? 0.f : expf(s1 - mn);
+    const uint32_t pa = pack_act2<F16>(p0, p1);  // the weights as the P.V product uses them
+    float ls = act_lo<F16>(pa) + act_hi<F16>(pa);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+    wsum = wsum * al + ls;
+    wmax = mn;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          acc[h][2 * e] = fmaf(p, act_lo<F16>(vw[e]), acc[h][2 * e]);
-          acc[h][2 * e + 1] = fmaf(p, act_hi<F16>(vw[e]), acc[h][2 * e + 1]);
-        }
-      }
+    for (int j = 0; j < 16; ++j) {
+      acc[j][0] *= al;
+      acc[j][1] *= al;
+    }
+    // P.V: four transposed ldmatrix loads (32 dimensions each) give the B
+    // fragments of the 16 column tiles; keys 8..15 of the k step are absent
+    // (zero A and B halves).
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) {
+      uint32_t b[4];
+      ldsm_x4_trans(b, sm_u32(vst) + kv_off(vr, 32 * q4 + 8 * (lane >> 3)));
+#pragma unroll
+      for (int m = 0; m < 4; ++m) mma_act<F16>(acc[4 * q4 + m], pa, 0u, 0u, 0u, b[m], 0u);
     }
     __syncthreads();  // every thread is done with this stage
     if (tid == 0 && ci + kCStages < my_chunks) issue(ci + kCStages);
   }
-  // This CTA's partial: sum the 16 row groups in a fixed order.
+  // This CTA's partial: the eight warps' partials merged in warp order.
+  if (g < G) {
 #pragma unroll
-  for (int h = 0; h < G; ++h)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float v = acc[h][e] + __shfl_xor_sync(0xffffffffu, acc[h][e], 16);
-      if ((lane & 16) == 0) sm.red[warp][h][dg * 8 + e] = v;
+    for (int j = 0; j < 16; ++j) {
+      sm.red[warp][g][8 * j + 2 * t] = acc[j][0];
+      sm.red[warp][g][8 * j + 2 * t + 1] = acc[j][1];
     }
+    if (t == 0) {
+      sm.wm[warp][g] = wmax;
+      sm.wl[warp][g] = wsum;
+    }
+  }
   __syncthreads();
   for (int i = tid; i < G * kD; i += kCT) {
     const int h = i / kD, d = i % kD;
-    float v = 0.f;
+    float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kCT / 32; ++w) v += sm.red[w][h][d];
-    sm.part_acc[h][d] = v;
-  }
-  if (tid < G) {
-    sm.part_m[tid] = sm.run_m[tid];
-    sm.part_l[tid] = sm.run_l[tid];
+    for (int w = 0; w < kCT / 32; ++w) M = fmaxf(M, sm.wm[w][h]);
+    float num = 0.f, den = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCT / 32; ++w) {
+      const float e = (sm.wm[w][h] == -INFINITY) ? 0.f : expf(sm.wm[w][h] - M);
+      num = fmaf(sm.red[w][h][d], e, num);
+      den = fmaf(sm.wl[w][h], e, den);
+    }
+    sm.part_acc[h][d] = num;
+    if (d == 0) {
+      sm.part_m[h] = M;
+      sm.part_l[h] = den;
+    }
   }
   if (C == 1) {
     // One CTA per KV head: its partial is the result (the merge below with a
@@ -733,7 +719,16 @@ cudaError_t launch_cluster_g(const uint16_t* q, const uint16_t* kc, const uint16
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  const int smem = (int)sizeof(ClusterSmem<G>);
+  const int smem = (int)sizeof(ClusterSmem<G>) + 1024;  // + slack for the 1024-byte alignment
+  // K and V caches as 2-D [n_kv * max_len rows, 128 dims] maps, 64 x 64 boxes
+  // in the 128-byte swizzle (base and row stride are 16-byte multiples).
+  CUtensorMap mk, mv;
+  const uint64_t rows = (uint64_t)nkv * (uint64_t)max_len;
+  if (!make_map_2d(&mk, CU_TENSOR_MAP_DATA_TYPE_UINT16, kc, kD, rows, kD * 2, 64, ATTN_CHUNK,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map_2d(&mv, CU_TENSOR_MAP_DATA_TYPE_UINT16, vc, kD, rows, kD * 2, 64, ATTN_CHUNK,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
   if (dev >= 0 && dev < 64 && !configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(decode_attention_cluster_kernel<G, F16>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -765,7 +760,7 @@ cudaError_t launch_cluster_g(const uint16_t* q, const uint16_t* kc, const uint16
   }
   const float scale = 1.0f / sqrtf((float)kD);
   return cudaLaunchKernelEx(&cfg, decode_attention_cluster_kernel<G, F16>, (const bf16_t*)q, (const bf16_t*)kc,
-                            (const bf16_t*)vc, pos, mask, (bf16_t*)out, max_len, window, scale, in);
+                            (const bf16_t*)vc, pos, mask, (bf16_t*)out, max_len, window, scale, in, mk, mv);
 }
 
 }  // namespace
