@@ -259,6 +259,18 @@ size_t nf4b_decode_step_workspace_size(const nf4b_chain_job* jobs, int n_jobs, i
 int nf4b_debug_decode_step(const nf4b_chain_job* jobs, int n_jobs, int rows, void* workspace,
                            size_t workspace_bytes, int stall_job, unsigned long long wait_ns, void* stream);
 
+/*
+ * Test hook for failure detection (not for production use), for the
+ * tcgen05 GEMM (more than 8 rows) of the current device: every later GEMM
+ * launch's waits give up after `wait_ns` nanoseconds, and with `skip_x0` = 1
+ * its producer leaves the first k block's activation tile unrequested, so the
+ * barrier that copy would complete never does and the waits on it run out.
+ * The launch then records bit 0 in nf4b_device_error and returns (its outputs
+ * are invalid); nothing faults. nf4b_debug_gemm_hook(0, 2000000000) restores
+ * normal operation. No counterpart in the reference, whose kernels have no waits.
+ */
+int nf4b_debug_gemm_hook(int skip_x0, unsigned long long wait_ns);
+
 /* Bytes of workspace nf4b_gemm needs for this weight and row count. */
 size_t nf4b_gemm_workspace_size(const nf4b_weight* w, int rows);
 

@@ -8,7 +8,9 @@ limit - through the test hook nf4b_debug_decode_step: the boundary before
 launch returned, that the error word says which wait gave up, that the CUDA
 context is still usable, and that the next launch on the same workspace gives
 the same bits as before the failure (the step's launch counter gives every
-launch a new flag space, so nothing the abandoned launch wrote is read).
+launch a new flag space, so nothing the abandoned launch wrote is read). The
+tcgen05 GEMM's waits are made to run out the same way through
+nf4b_debug_gemm_hook: an activation-tile copy that is never requested.
 """
 
 from __future__ import annotations
@@ -75,3 +77,57 @@ def test_the_hook_rejects_a_limit_outside_its_range():
     assert L.nf4b_debug_decode_step(arr, len(steps), rows, ws.data_ptr(), ws.numel(), 1, 3_000_000_000,
                                     None) == _lib.NF4B_ERR_ARG
     del keep
+
+
+GEMM_BIT = 1   # bit 0 of nf4b_device_error
+
+
+@pytest.mark.parametrize("n,k,rows", [(1024, 2560, 64), (9728, 2560, 256)])
+def test_a_gemm_whose_activation_copy_never_lands_gives_up_and_the_next_call_is_exact(n, k, rows):
+    """The tcgen05 GEMM (64-row tiles with split-K, two MMA issuers and the
+    staged epilogue; 256-row tiles, one issuer, direct stores) through the test
+    hook nf4b_debug_gemm_hook: the first k block's activation tile is never
+    requested, so the barrier it would complete never does, and with a 200 us
+    limit the waits on it run out. The launch returns by itself with bit 0 of
+    the error word set, the context stays usable, and after the workspace is
+    zeroed again (as the header asks after a non-zero error word) the next call
+    gives the same bits as before the failure."""
+    L = _lib.lib()
+    assert nf4gemv.available() and L.nf4b_device_error(1) == 0
+    lin = make_linear(n, k, seed=n + rows)
+    desc = lin._nf4_fast["desc"]
+    x = randn_bf16((rows, k), seed=rows, device="cuda")
+    need = int(L.nf4b_gemm_workspace_size(ctypes.byref(desc), rows))
+    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def call():
+        y = torch.empty(rows, n, dtype=torch.bfloat16, device="cuda")
+        st = L.nf4b_gemm(ctypes.byref(desc), x.data_ptr(), y.data_ptr(), rows, 0, None,
+                         ws.data_ptr() if need else None, need, stream)
+        assert st == 0, _lib.last_error()
+        return y
+
+    want = call()
+    torch.cuda.synchronize()
+    try:
+        assert L.nf4b_debug_gemm_hook(1, 200_000) == 0
+        call()
+        torch.cuda.synchronize()                  # the launch ended by itself
+    finally:
+        assert L.nf4b_debug_gemm_hook(0, 2_000_000_000) == 0
+    err = L.nf4b_device_error(1)                  # reads and clears the error word
+    assert err == GEMM_BIT, err
+    assert L.nf4b_device_error(0) == 0
+    ws.zero_()
+    again = call()
+    torch.cuda.synchronize()
+    assert torch.equal(again, want)
+    assert L.nf4b_device_error(0) == 0
+
+
+def test_the_gemm_hook_rejects_arguments_outside_their_range():
+    L = _lib.lib()
+    assert L.nf4b_debug_gemm_hook(1, 0) == _lib.NF4B_ERR_ARG
+    assert L.nf4b_debug_gemm_hook(1, 3_000_000_000) == _lib.NF4B_ERR_ARG
+    assert L.nf4b_debug_gemm_hook(2, 1_000_000) == _lib.NF4B_ERR_ARG

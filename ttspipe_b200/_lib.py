@@ -59,6 +59,7 @@ EXPORTS = (
     "nf4b_decode_step",
     "nf4b_decode_step_workspace_size",
     "nf4b_debug_decode_step",
+    "nf4b_debug_gemm_hook",
     "nf4b_rms_norm_ex",
     "nf4b_rope_ex",
     "nf4b_qk_rope_kv_ex",
@@ -149,6 +150,7 @@ def _declare(lib) -> None:
         "nf4b_decode_step": (i32, [ctypes.POINTER(ChainJob), i32, i32, vp, sz, vp]),
         "nf4b_decode_step_workspace_size": (sz, [ctypes.POINTER(ChainJob), i32, i32]),
         "nf4b_debug_decode_step": (i32, [ctypes.POINTER(ChainJob), i32, i32, vp, sz, i32, ctypes.c_ulonglong, vp]),
+        "nf4b_debug_gemm_hook": (i32, [i32, ctypes.c_ulonglong]),
         "nf4b_gemm_workspace_size": (sz, [wp, i32]),
         "nf4b_gemm_noalloc": (i32, [wp, vp, vp, i32, i32, vp, vp]),
         "nf4b_dequantize": (i32, [wp, vp, vp]),

@@ -16,6 +16,7 @@
 
 namespace nf4b {
 int read_device_error(int clear);
+int set_gemm_debug(int skip_x0, unsigned long long wait_ns);
 int read_gemv_error(int clear);
 int read_attn_error(int clear);
 }
@@ -636,6 +637,14 @@ extern "C" int nf4b_debug_decode_step(const nf4b_chain_job* jobs, int n_jobs, in
                                       void* stream) {
   if (wait_ns == 0 || wait_ns > 2000000000ull) return fail(NF4B_ERR_ARG, "wait_ns must be in (0, 2e9]");
   return decode_step_call(jobs, n_jobs, rows, workspace, workspace_bytes, stall_job, wait_ns, stream);
+}
+
+extern "C" int nf4b_debug_gemm_hook(int skip_x0, unsigned long long wait_ns) {
+  if (wait_ns == 0 || wait_ns > 2000000000ull) return fail(NF4B_ERR_ARG, "wait_ns must be in (0, 2e9]");
+  if (skip_x0 != 0 && skip_x0 != 1) return fail(NF4B_ERR_ARG, "skip_x0 must be 0 or 1");
+  int st = check_device();
+  if (st) return st;
+  return set_gemm_debug(skip_x0, wait_ns) == 0 ? 0 : fail(NF4B_ERR_LAUNCH, "setting the GEMM test hook failed");
 }
 
 extern "C" int nf4b_dense_gemv(const void* w, const void* x, void* y, int n_out, int k_in, const void* norm_weight,

@@ -33,7 +33,7 @@
 //              store Y, through the then idle X ring for split-K and 64-row
 //              tiles.
 //
-// Every mbarrier wait is bounded: a wait that outlives kWaitNs sets the
+// Every mbarrier wait is bounded: a wait that outlives g_gemm_wait_ns (2 s) sets the
 // library's device error word and a CTA-wide abort flag, after which every
 // role leaves its loop; the producer waits (bounded) for the copies it issued
 // and the MMA thread for its last commit, then TMEM is released and the kernel
@@ -49,6 +49,11 @@
 namespace nf4b {
 
 __device__ int g_device_error = 0;
+// Every wait's limit (2 s), and the test hook's switch: when set, the producer
+// leaves block 0's activation tile unrequested, so the barrier that copy would
+// complete never does and the waits on it run out (set_gemm_debug).
+__device__ unsigned long long g_gemm_wait_ns = 2000000000ull;
+__device__ int g_gemm_skip_x0 = 0;
 
 namespace {
 
@@ -99,7 +104,6 @@ static_assert(2 * 128 + 4 * 32 <= 512 && 2 * 64 + 8 * 32 <= 512 && 256 + 4 * 32 
 static_assert(ring_stages<256>() % kDequantGroups == 0 && ring_stages<128>() % kDequantGroups == 0 &&
                   ring_stages<64>() % kDequantGroups == 0,
               "ring depth must be a multiple of the dequantisation groups");
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 // A waiting thread asks to be suspended for up to this long per try (it wakes
 // when the phase completes): spinning waiters would take issue slots from the
 // dequantisation warps (measured 3-4% on the S2-Pro layer at 256-4096 rows).
@@ -171,7 +175,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       const unsigned long long now = globaltimer();
       if (i == 0) {
         start = now;
-      } else if (now - start > kWaitNs) {
+      } else if (now - start > g_gemm_wait_ns) {
         *abort_flag = 1;
         atomicOr(&g_device_error, 1);
         return false;
@@ -199,7 +203,7 @@ __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
       const unsigned long long now = globaltimer();
       if (i == 0) {
         start = now;
-      } else if (now - start > kWaitNs) {
+      } else if (now - start > g_gemm_wait_ns) {
         atomicOr(&g_device_error, 1);
         return;
       }
@@ -323,6 +327,7 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
       };
       for (int i = 0; i < nkb && i < STAGES; ++i) load_w(i);
       pdl_wait();
+      const bool skip_x0 = g_gemm_skip_x0 != 0;  // test hook only
       for (int i = 0; i < nkb; ++i) {
         const int s = i % STAGES;
         if (i >= STAGES) {
@@ -331,9 +336,11 @@ __global__ void __launch_bounds__(gemm_threads<DQ>(), 1)
           // dequantisation starts before the activation tile has landed
           load_w(i);
         }
-        const uint32_t xbar = smem_u32(&sm.x_full[s]);
-        mbar_expect_tx(xbar, BT * 128);
-        tma_load_2d(smem_u32(sm.x[s]), &tmap_x, (kb_lo + i) * BK, tok0, xbar);
+        if (!(skip_x0 && i == 0)) {
+          const uint32_t xbar = smem_u32(&sm.x_full[s]);
+          mbar_expect_tx(xbar, BT * 128);
+          tma_load_2d(smem_u32(sm.x[s]), &tmap_x, (kb_lo + i) * BK, tok0, xbar);
+        }
         issued = i + 1;
       }
       // every copy issued has landed before the CTA can exit (immediate on the
@@ -754,6 +761,12 @@ static cudaError_t launch_gemm_act(const GemmParams& p, cudaStream_t stream) {
 
 cudaError_t launch_gemm_tc(const GemmParams& p, cudaStream_t stream) {
   return p.f16 ? launch_gemm_act<true>(p, stream) : launch_gemm_act<false>(p, stream);
+}
+
+int set_gemm_debug(int skip_x0, unsigned long long wait_ns) {
+  if (cudaMemcpyToSymbol(g_gemm_skip_x0, &skip_x0, sizeof(int)) != cudaSuccess) return -1;
+  if (cudaMemcpyToSymbol(g_gemm_wait_ns, &wait_ns, sizeof(wait_ns)) != cudaSuccess) return -1;
+  return 0;
 }
 
 int read_device_error(int clear) {
