@@ -8,7 +8,8 @@
 //   divide the kept logits by max(temperature, 1e-5), softmax over them,
 //   draw one.
 //
-// One launch. CTA s takes a 2048-logit slice: each of its 32 warps sorts 64
+// One launch. CTA s takes a 2048-logit slice (a vocabulary of up to 4096, the
+// codebooks', is one CTA's, two slices, drawn at once): each of its 32 warps sorts 64
 // (value, index) keys (larger value first, then smaller index) in registers,
 // and the warps' lists are merged pairwise - the top 64 of two sorted lists
 // is max(A[i], B[63 - i]), a bitonic sequence, then a 6-stage bitonic merge -
@@ -135,7 +136,43 @@ __device__ __forceinline__ unsigned long long splitmix64(unsigned long long z) {
   return z ^ (z >> 31);
 }
 
-__global__ void __launch_bounds__(kSThreads) sample_kernel(const uint16_t* __restrict__ logits, int V,
+// Warp 0 of the deciding CTA: from the sorted top keys and the whole
+// vocabulary's softmax statistics (max M, sum Z of exp(v - M)), the kept
+// positions (i = 0, then up to the first i with cumsum(p)[i] > top_p, at most
+// top_k), the softmax of the kept logits / temperature and the inverse-CDF
+// draw of one of them.
+__device__ __forceinline__ void draw_token(const unsigned long long* keys, float M, float Z, int V,
+                                           float temperature, float top_p, int top_k, unsigned long long seed,
+                                           const int64_t* __restrict__ step, int64_t* __restrict__ out, int lane) {
+  const int kk = top_k < kTop ? (top_k < 1 ? 1 : top_k) : kTop;
+  const int n = kk < V ? kk : V;
+  const float inv_t = 1.0f / fmaxf(temperature, 1e-5f);
+  const float kv0 = key_value(keys[lane]), kv1 = key_value(keys[lane + 32]);
+  const float p0 = lane < n ? expf(kv0 - M) / Z : 0.f, p1 = lane + 32 < n ? expf(kv1 - M) / Z : 0.f;
+  const float c0 = warp_scan(p0, lane);
+  const float c1 = warp_scan(p1, lane) + __shfl_sync(0xffffffffu, c0, 31);
+  const int keep = first_set(__ballot_sync(0xffffffffu, lane >= 1 && lane < n && c0 > top_p),
+                             __ballot_sync(0xffffffffu, lane + 32 < n && c1 > top_p), n);
+  const float m0 = key_value(keys[0]) * inv_t;
+  const float q0 = lane < keep ? expf(kv0 * inv_t - m0) : 0.f;
+  const float q1 = lane + 32 < keep ? expf(kv1 * inv_t - m0) : 0.f;
+  const float a0 = warp_scan(q0, lane);
+  const float a1 = warp_scan(q1, lane) + __shfl_sync(0xffffffffu, a0, 31);
+  const float tot = __shfl_sync(0xffffffffu, a1, 31);
+  const unsigned long long st = step != nullptr ? (unsigned long long)step[0] : 0ull;
+  const float u = (float)(splitmix64(seed ^ (st * 0xD1B54A32D192ED03ull)) >> 40) * (1.0f / 16777216.0f);
+  const float target = u * tot;
+  const int pick = first_set(__ballot_sync(0xffffffffu, lane < keep && a0 > target),
+                             __ballot_sync(0xffffffffu, lane + 32 < keep && a1 > target), keep - 1);
+  if (lane == 0) out[0] = (int64_t)key_index(keys[pick]);
+}
+
+// `per` slices of 2048 logits per CTA: 1 when the vocabulary takes several
+// CTAs, up to kMaxPer for a vocabulary one CTA takes whole (the codebooks'
+// 4096), which then draws at once - no partial lists through global memory,
+// no last-CTA handoff (a 4096-entry draw took 13.4 us as two CTAs).
+constexpr int kMaxPer = 2;
+__global__ void __launch_bounds__(kSThreads) sample_kernel(const uint16_t* __restrict__ logits, int V, int per,
                                                            float temperature, float top_p, int top_k,
                                                            unsigned long long seed, const int64_t* __restrict__ step,
                                                            int64_t* __restrict__ out, unsigned long long* __restrict__ ws_keys,
@@ -147,25 +184,53 @@ __global__ void __launch_bounds__(kSThreads) sample_kernel(const uint16_t* __res
   pdl_wait();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int s = blockIdx.x, S = gridDim.x;
-  const int base = s * kSlice;
-  // this slice's keys (64 per warp, sorted in registers) and its max / sum of exp
-  const int j0 = base + warp * 64 + lane, j1 = j0 + 32;
-  const float v0 = j0 < V ? bf2f(logits[j0]) : -INFINITY, v1 = j1 < V ? bf2f(logits[j1]) : -INFINITY;
-  unsigned long long x0 = j0 < V ? make_key(v0, (uint32_t)j0) : 0ull;  // 0: below every real key
-  unsigned long long x1 = j1 < V ? make_key(v1, (uint32_t)j1) : 0ull;
-  float m = fmaxf(v0, v1);
+  const int base = s * kSlice * per;
+  // this CTA's keys (64 per warp and slice, sorted in registers, the slices'
+  // lists merged) and its max / sum of exp
+  float v[2 * kMaxPer];
+  unsigned long long x0 = 0ull, x1 = 0ull;  // 0: below every real key
+  float m = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < kMaxPer; ++c) {
+    v[2 * c] = v[2 * c + 1] = -INFINITY;
+    if (c >= per) continue;
+    const int j0 = base + c * kSlice + warp * 64 + lane, j1 = j0 + 32;
+    v[2 * c] = j0 < V ? bf2f(logits[j0]) : -INFINITY;
+    v[2 * c + 1] = j1 < V ? bf2f(logits[j1]) : -INFINITY;
+    unsigned long long y0 = j0 < V ? make_key(v[2 * c], (uint32_t)j0) : 0ull;
+    unsigned long long y1 = j1 < V ? make_key(v[2 * c + 1], (uint32_t)j1) : 0ull;
+    m = fmaxf(m, fmaxf(v[2 * c], v[2 * c + 1]));
+    warp_sort64(y0, y1, lane);
+    if (c == 0) {
+      x0 = y0;
+      x1 = y1;
+    } else {
+      warp_merge64(x0, x1, y0, y1, lane);
+    }
+  }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
   if (lane == 0) red_m[warp] = m;
-  warp_sort64(x0, x1, lane);
   __syncthreads();
   m = -INFINITY;
   for (int w = 0; w < kSThreads / 32; ++w) m = fmaxf(m, red_m[w]);
-  float sum = expf(v0 - m) + expf(v1 - m);  // exp(-inf) = 0 past the vocabulary
+  float sum = 0.f;
+#pragma unroll
+  for (int c = 0; c < 2 * kMaxPer; ++c) sum += expf(v[c] - m);  // exp(-inf) = 0 past the vocabulary
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
   if (lane == 0) red_s[warp] = sum;
-  block_merge(lists, x0, x1, warp, lane);
+  block_merge(lists, x0, x1, warp, lane);  // its barriers also publish red_s
+  if (S == 1) {
+    // the whole vocabulary in this CTA: draw now
+    if (warp == 0) {
+      float t = 0.f;
+      for (int w = 0; w < kSThreads / 32; ++w) t += red_s[w];  // fixed order
+      draw_token(lists[0], m, t, V, temperature, top_p, top_k, seed, step, out, lane);
+    }
+    pdl_launch_dependents();
+    return;
+  }
   if (warp == 0) {
     ws_keys[(size_t)s * kTop + lane] = x0;
     ws_keys[(size_t)s * kTop + lane + 32] = x1;
@@ -198,7 +263,6 @@ __global__ void __launch_bounds__(kSThreads) sample_kernel(const uint16_t* __res
   }
   for (int c = tid; c < S; c += kSThreads) sm_max[c] = __ldcg(ws_stats + 2 * c);
   block_merge(lists, x0, x1, warp, lane);  // its barriers also publish sm_max
-  const unsigned long long* keys = lists[0];
   if (warp == 0) {
     float M = -INFINITY;
     for (int c = lane; c < S; c += 32) M = fmaxf(M, sm_max[c]);
@@ -208,29 +272,7 @@ __global__ void __launch_bounds__(kSThreads) sample_kernel(const uint16_t* __res
     __syncwarp();
     float Z = 0.f;
     for (int c = 0; c < S; ++c) Z += sm_term[c];  // slice order (every lane, same value)
-    const int kk = top_k < kTop ? (top_k < 1 ? 1 : top_k) : kTop;
-    const int n = kk < V ? kk : V;
-    const float inv_t = 1.0f / fmaxf(temperature, 1e-5f);
-    const float kv0 = key_value(keys[lane]), kv1 = key_value(keys[lane + 32]);
-    // kept positions: i = 0, then up to the first i with cumsum(p)[i] > top_p
-    const float p0 = lane < n ? expf(kv0 - M) / Z : 0.f, p1 = lane + 32 < n ? expf(kv1 - M) / Z : 0.f;
-    const float c0 = warp_scan(p0, lane);
-    const float c1 = warp_scan(p1, lane) + __shfl_sync(0xffffffffu, c0, 31);
-    const int keep = first_set(__ballot_sync(0xffffffffu, lane >= 1 && lane < n && c0 > top_p),
-                               __ballot_sync(0xffffffffu, lane + 32 < n && c1 > top_p), n);
-    // softmax of the kept logits / temperature, then the inverse-CDF draw
-    const float m0 = key_value(keys[0]) * inv_t;
-    const float q0 = lane < keep ? expf(kv0 * inv_t - m0) : 0.f;
-    const float q1 = lane + 32 < keep ? expf(kv1 * inv_t - m0) : 0.f;
-    const float a0 = warp_scan(q0, lane);
-    const float a1 = warp_scan(q1, lane) + __shfl_sync(0xffffffffu, a0, 31);
-    const float tot = __shfl_sync(0xffffffffu, a1, 31);
-    const unsigned long long st = step != nullptr ? (unsigned long long)step[0] : 0ull;
-    const float u = (float)(splitmix64(seed ^ (st * 0xD1B54A32D192ED03ull)) >> 40) * (1.0f / 16777216.0f);
-    const float target = u * tot;
-    const int pick = first_set(__ballot_sync(0xffffffffu, lane < keep && a0 > target),
-                               __ballot_sync(0xffffffffu, lane + 32 < keep && a1 > target), keep - 1);
-    if (lane == 0) out[0] = (int64_t)key_index(keys[pick]);
+    draw_token(lists[0], M, Z, V, temperature, top_p, top_k, seed, step, out, lane);
   }
   pdl_launch_dependents();
 }
@@ -245,7 +287,9 @@ size_t sampler_workspace_bytes(int V) {
 cudaError_t launch_sampler(const uint16_t* logits, int V, float temperature, float top_p, int top_k,
                            unsigned long long seed, const int64_t* step, int64_t* out, void* workspace,
                            cudaStream_t stream) {
-  const int S = (V + kSlice - 1) / kSlice;
+  // a vocabulary of up to kMaxPer slices: one CTA, no handoff
+  const int per = V <= kMaxPer * kSlice ? (V + kSlice - 1) / kSlice : 1;
+  const int S = V <= kMaxPer * kSlice ? 1 : (V + kSlice - 1) / kSlice;
   int* counter = static_cast<int*>(workspace);
   unsigned long long* keys = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(workspace) + 256);
   float* stats = reinterpret_cast<float*>(keys + (size_t)S * kTop);
@@ -259,8 +303,8 @@ cudaError_t launch_sampler(const uint16_t* logits, int V, float temperature, flo
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, sample_kernel, logits, V, temperature, top_p, top_k, seed, step, out, keys, stats,
-                            counter);
+  return cudaLaunchKernelEx(&cfg, sample_kernel, logits, V, per < 1 ? 1 : per, temperature, top_p, top_k, seed, step,
+                            out, keys, stats, counter);
 }
 
 }  // namespace nf4b
