@@ -44,29 +44,53 @@ __device__ __forceinline__ float key_value(unsigned long long k) {
   return __uint_as_float(b);
 }
 __device__ __forceinline__ uint32_t key_index(unsigned long long k) { return 0xFFFFFFFFu - (uint32_t)k; }
+// The same order in 32 bits for a one-CTA vocabulary (indices below 65536): the
+// logit's bf16 bits (a bf16 value's low 16 fp32 bits are zero), then the index.
+// Half the shuffles of the 64-bit key in the sorts and merges, which bound them.
+__device__ __forceinline__ uint32_t make_key32(float v, uint32_t idx) {
+  uint32_t b = __float_as_uint(v) >> 16;
+  b = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+  return (b << 16) | (0xFFFFu - idx);
+}
+__device__ __forceinline__ float key_value(uint32_t k) {
+  uint32_t b = k >> 16;
+  b = (b & 0x8000u) ? (b & 0x7FFFu) : (~b & 0xFFFFu);
+  return __uint_as_float(b << 16);
+}
+__device__ __forceinline__ uint32_t key_index(uint32_t k) { return 0xFFFFu - (k & 0xFFFFu); }
+template <typename Key>
+__device__ __forceinline__ Key make_key_t(float v, uint32_t idx) {
+  if constexpr (sizeof(Key) == 4)
+    return make_key32(v, idx);
+  else
+    return make_key(v, idx);
+}
 
 // A sorted (descending) list of 64 keys held by one warp: lane l holds
 // L[l] in x0 and L[l + 32] in x1.
-__device__ __forceinline__ unsigned long long kmax(unsigned long long a, unsigned long long b) { return a > b ? a : b; }
-__device__ __forceinline__ unsigned long long kmin(unsigned long long a, unsigned long long b) { return a < b ? a : b; }
+template <typename Key>
+__device__ __forceinline__ Key kmax(Key a, Key b) { return a > b ? a : b; }
+template <typename Key>
+__device__ __forceinline__ Key kmin(Key a, Key b) { return a < b ? a : b; }
 
 // Sort 64 arbitrary keys into that layout (bitonic network; strides below 32
 // between lanes, stride 32 within a lane).
-__device__ __forceinline__ void warp_sort64(unsigned long long& x0, unsigned long long& x1, int lane) {
+template <typename Key>
+__device__ __forceinline__ void warp_sort64(Key& x0, Key& x1, int lane) {
 #pragma unroll
   for (int k = 2; k <= 64; k <<= 1) {
 #pragma unroll
     for (int j = k >> 1; j > 0; j >>= 1) {
       if (j == 32) {  // k == 64: element i against i + 32, descending
-        const unsigned long long hi = kmax(x0, x1), lo = kmin(x0, x1);
+        const Key hi = kmax(x0, x1), lo = kmin(x0, x1);
         x0 = hi;
         x1 = lo;
         continue;
       }
       const bool lower = (lane & j) == 0;
       const bool d0 = (lane & k) == 0, d1 = ((lane + 32) & k) == 0;  // block of element i sorted descending?
-      const unsigned long long p0 = __shfl_xor_sync(0xffffffffu, x0, j);
-      const unsigned long long p1 = __shfl_xor_sync(0xffffffffu, x1, j);
+      const Key p0 = __shfl_xor_sync(0xffffffffu, x0, j);
+      const Key p1 = __shfl_xor_sync(0xffffffffu, x1, j);
       x0 = (lower == d0) ? kmax(x0, p0) : kmin(x0, p0);
       x1 = (lower == d1) ? kmax(x1, p1) : kmin(x1, p1);
     }
@@ -74,19 +98,19 @@ __device__ __forceinline__ void warp_sort64(unsigned long long& x0, unsigned lon
 }
 
 // (a0, a1) <- the top 64 of the sorted lists A = (a0, a1) and B = (b0, b1), sorted.
-__device__ __forceinline__ void warp_merge64(unsigned long long& a0, unsigned long long& a1, unsigned long long b0,
-                                             unsigned long long b1, int lane) {
-  const unsigned long long r0 = __shfl_sync(0xffffffffu, b1, 31 - lane);  // B[63 - lane]
-  const unsigned long long r1 = __shfl_sync(0xffffffffu, b0, 31 - lane);  // B[31 - lane]
-  unsigned long long c0 = kmax(a0, r0), c1 = kmax(a1, r1);              // bitonic
-  const unsigned long long hi = kmax(c0, c1), lo = kmin(c0, c1);
+template <typename Key>
+__device__ __forceinline__ void warp_merge64(Key& a0, Key& a1, Key b0, Key b1, int lane) {
+  const Key r0 = __shfl_sync(0xffffffffu, b1, 31 - lane);  // B[63 - lane]
+  const Key r1 = __shfl_sync(0xffffffffu, b0, 31 - lane);  // B[31 - lane]
+  Key c0 = kmax(a0, r0), c1 = kmax(a1, r1);              // bitonic
+  const Key hi = kmax(c0, c1), lo = kmin(c0, c1);
   c0 = hi;
   c1 = lo;
 #pragma unroll
   for (int j = 16; j > 0; j >>= 1) {
     const bool lower = (lane & j) == 0;
-    const unsigned long long p0 = __shfl_xor_sync(0xffffffffu, c0, j);
-    const unsigned long long p1 = __shfl_xor_sync(0xffffffffu, c1, j);
+    const Key p0 = __shfl_xor_sync(0xffffffffu, c0, j);
+    const Key p1 = __shfl_xor_sync(0xffffffffu, c1, j);
     c0 = lower ? kmax(c0, p0) : kmin(c0, p0);
     c1 = lower ? kmax(c1, p1) : kmin(c1, p1);
   }
@@ -96,8 +120,8 @@ __device__ __forceinline__ void warp_merge64(unsigned long long& a0, unsigned lo
 
 // Merge the 32 warps' lists (registers) down to warp 0's; lists[32][64] is
 // shared scratch. Leaves the result in lists[0] too. Every thread calls it.
-__device__ __forceinline__ void block_merge(unsigned long long (*lists)[kTop], unsigned long long& x0,
-                                            unsigned long long& x1, int warp, int lane) {
+template <typename Key>
+__device__ __forceinline__ void block_merge(Key (*lists)[kTop], Key& x0, Key& x1, int warp, int lane) {
   lists[warp][lane] = x0;
   lists[warp][lane + 32] = x1;
 #pragma unroll
@@ -141,7 +165,8 @@ __device__ __forceinline__ unsigned long long splitmix64(unsigned long long z) {
 // positions (i = 0, then up to the first i with cumsum(p)[i] > top_p, at most
 // top_k), the softmax of the kept logits / temperature and the inverse-CDF
 // draw of one of them.
-__device__ __forceinline__ void draw_token(const unsigned long long* keys, float M, float Z, int V,
+template <typename Key>
+__device__ __forceinline__ void draw_token(const Key* keys, float M, float Z, int V,
                                            float temperature, float top_p, int top_k, unsigned long long seed,
                                            const int64_t* __restrict__ step, int64_t* __restrict__ out, int lane) {
   const int kk = top_k < kTop ? (top_k < 1 ? 1 : top_k) : kTop;
@@ -172,12 +197,14 @@ __device__ __forceinline__ void draw_token(const unsigned long long* keys, float
 // 4096), which then draws at once - no partial lists through global memory,
 // no last-CTA handoff (a 4096-entry draw took 13.4 us as two CTAs).
 constexpr int kMaxPer = 2;
+// Key: 32-bit keys for a one-CTA vocabulary, 64-bit otherwise.
+template <typename Key>
 __global__ void __launch_bounds__(kSThreads) sample_kernel(const uint16_t* __restrict__ logits, int V, int per,
                                                            float temperature, float top_p, int top_k,
                                                            unsigned long long seed, const int64_t* __restrict__ step,
                                                            int64_t* __restrict__ out, unsigned long long* __restrict__ ws_keys,
                                                            float* __restrict__ ws_stats, int* __restrict__ counter) {
-  __shared__ unsigned long long lists[kSThreads / 32][kTop];
+  __shared__ Key lists[kSThreads / 32][kTop];
   __shared__ float red_m[kSThreads / 32], red_s[kSThreads / 32];
   __shared__ float sm_max[kMaxSlices], sm_term[kMaxSlices];
   __shared__ int last;
@@ -188,7 +215,7 @@ __global__ void __launch_bounds__(kSThreads) sample_kernel(const uint16_t* __res
   // this CTA's keys (64 per warp and slice, sorted in registers, the slices'
   // lists merged) and its max / sum of exp
   float v[2 * kMaxPer];
-  unsigned long long x0 = 0ull, x1 = 0ull;  // 0: below every real key
+  Key x0 = 0, x1 = 0;  // 0: below every real key
   float m = -INFINITY;
 #pragma unroll
   for (int c = 0; c < kMaxPer; ++c) {
@@ -197,8 +224,8 @@ __global__ void __launch_bounds__(kSThreads) sample_kernel(const uint16_t* __res
     const int j0 = base + c * kSlice + warp * 64 + lane, j1 = j0 + 32;
     v[2 * c] = j0 < V ? bf2f(logits[j0]) : -INFINITY;
     v[2 * c + 1] = j1 < V ? bf2f(logits[j1]) : -INFINITY;
-    unsigned long long y0 = j0 < V ? make_key(v[2 * c], (uint32_t)j0) : 0ull;
-    unsigned long long y1 = j1 < V ? make_key(v[2 * c + 1], (uint32_t)j1) : 0ull;
+    Key y0 = j0 < V ? make_key_t<Key>(v[2 * c], (uint32_t)j0) : Key(0);
+    Key y1 = j1 < V ? make_key_t<Key>(v[2 * c + 1], (uint32_t)j1) : Key(0);
     m = fmaxf(m, fmaxf(v[2 * c], v[2 * c + 1]));
     warp_sort64(y0, y1, lane);
     if (c == 0) {
@@ -231,48 +258,50 @@ __global__ void __launch_bounds__(kSThreads) sample_kernel(const uint16_t* __res
     pdl_launch_dependents();
     return;
   }
-  if (warp == 0) {
-    ws_keys[(size_t)s * kTop + lane] = x0;
-    ws_keys[(size_t)s * kTop + lane + 32] = x1;
-  }
-  if (tid == 0) {
-    float t = 0.f;
-    for (int w = 0; w < kSThreads / 32; ++w) t += red_s[w];  // fixed order
-    ws_stats[2 * s] = m;
-    ws_stats[2 * s + 1] = t;
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int old = atomicAdd(counter, 1);
-    last = (old == S - 1);
-    if (last) *counter = 0;
-  }
-  __syncthreads();
-  if (!last) {
-    pdl_launch_dependents();
-    return;
-  }
-  __threadfence();
-  // ---- the last CTA: global top keys, full-vocabulary softmax statistics, draw
-  x0 = x1 = 0ull;
-  for (int c = warp; c < S; c += kSThreads / 32) {
-    const unsigned long long b0 = __ldcg(ws_keys + (size_t)c * kTop + lane);
-    const unsigned long long b1 = __ldcg(ws_keys + (size_t)c * kTop + lane + 32);
-    warp_merge64(x0, x1, b0, b1, lane);
-  }
-  for (int c = tid; c < S; c += kSThreads) sm_max[c] = __ldcg(ws_stats + 2 * c);
-  block_merge(lists, x0, x1, warp, lane);  // its barriers also publish sm_max
-  if (warp == 0) {
-    float M = -INFINITY;
-    for (int c = lane; c < S; c += 32) M = fmaxf(M, sm_max[c]);
+  if constexpr (sizeof(Key) == 8) {  // several CTAs: partial lists, the last CTA draws
+    if (warp == 0) {
+      ws_keys[(size_t)s * kTop + lane] = x0;
+      ws_keys[(size_t)s * kTop + lane + 32] = x1;
+    }
+    if (tid == 0) {
+      float t = 0.f;
+      for (int w = 0; w < kSThreads / 32; ++w) t += red_s[w];  // fixed order
+      ws_stats[2 * s] = m;
+      ws_stats[2 * s + 1] = t;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const int old = atomicAdd(counter, 1);
+      last = (old == S - 1);
+      if (last) *counter = 0;
+    }
+    __syncthreads();
+    if (!last) {
+      pdl_launch_dependents();
+      return;
+    }
+    __threadfence();
+    // ---- the last CTA: global top keys, full-vocabulary softmax statistics, draw
+    x0 = x1 = 0ull;
+    for (int c = warp; c < S; c += kSThreads / 32) {
+      const unsigned long long b0 = __ldcg(ws_keys + (size_t)c * kTop + lane);
+      const unsigned long long b1 = __ldcg(ws_keys + (size_t)c * kTop + lane + 32);
+      warp_merge64(x0, x1, b0, b1, lane);
+    }
+    for (int c = tid; c < S; c += kSThreads) sm_max[c] = __ldcg(ws_stats + 2 * c);
+    block_merge(lists, x0, x1, warp, lane);  // its barriers also publish sm_max
+    if (warp == 0) {
+      float M = -INFINITY;
+      for (int c = lane; c < S; c += 32) M = fmaxf(M, sm_max[c]);
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    for (int c = lane; c < S; c += 32) sm_term[c] = __ldcg(ws_stats + 2 * c + 1) * expf(sm_max[c] - M);
-    __syncwarp();
-    float Z = 0.f;
-    for (int c = 0; c < S; ++c) Z += sm_term[c];  // slice order (every lane, same value)
-    draw_token(lists[0], M, Z, V, temperature, top_p, top_k, seed, step, out, lane);
+      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      for (int c = lane; c < S; c += 32) sm_term[c] = __ldcg(ws_stats + 2 * c + 1) * expf(sm_max[c] - M);
+      __syncwarp();
+      float Z = 0.f;
+      for (int c = 0; c < S; ++c) Z += sm_term[c];  // slice order (every lane, same value)
+      draw_token(lists[0], M, Z, V, temperature, top_p, top_k, seed, step, out, lane);
+    }
   }
   pdl_launch_dependents();
 }
@@ -303,8 +332,11 @@ cudaError_t launch_sampler(const uint16_t* logits, int V, float temperature, flo
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, sample_kernel, logits, V, per < 1 ? 1 : per, temperature, top_p, top_k, seed, step,
-                            out, keys, stats, counter);
+  if (S == 1)
+    return cudaLaunchKernelEx(&cfg, sample_kernel<uint32_t>, logits, V, per < 1 ? 1 : per, temperature, top_p, top_k,
+                              seed, step, out, keys, stats, counter);
+  return cudaLaunchKernelEx(&cfg, sample_kernel<unsigned long long>, logits, V, per < 1 ? 1 : per, temperature, top_p,
+                            top_k, seed, step, out, keys, stats, counter);
 }
 
 }  // namespace nf4b
