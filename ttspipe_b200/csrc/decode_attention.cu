@@ -808,6 +808,10 @@ cudaError_t launch_cluster_attention(const uint16_t* q, const uint16_t* kc, cons
       return e;
     }
     (void)cudaGetLastError();
+    // Only a cluster that cannot be resident is a property of the device; a
+    // call whose caches the tensor maps reject (an argument of this call) falls
+    // back for this call alone.
+    if (e != cudaErrorNotSupported) return e;
   }
   chosen[idx] = -1;
   return cudaErrorNotSupported;
