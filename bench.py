@@ -673,7 +673,7 @@ def run_config4(device, stream, peaks) -> dict:
             "launches_per_layer_step": 3,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": _frac(gbs, float(peaks["hbm_gbs"])),
-                         "kernel": "decode attention (8-CTA cluster per KV head)"}}
+                         "kernel": "decode attention (8-CTA cluster per KV head, 2-D TMA chunks, mma.sync scores and P.V)"}}
 
 
 def run_reference_gpu(layers, device, stream, peaks) -> dict:
