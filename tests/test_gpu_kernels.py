@@ -299,6 +299,22 @@ def test_decode_attention_by_position(length):
     assert orc.relative_error(orc.bf16_to_f32(to_bits(out)), orc.bf16_to_f32(want)) < ATTN_TOL
 
 
+@pytest.mark.parametrize("nh,nkv", [(4, 4), (8, 4), (32, 4)])
+@pytest.mark.parametrize("length", [17, 300, 1100])
+def test_decode_attention_query_groups(nh, nkv, length):
+    """Groups of 1, 2 and 8 query heads per KV head (the kernel's tensor-core
+    tiles pad a group to 16 rows), at live lengths that occupy one, five and all
+    eight CTAs of a KV head's cluster."""
+    max_len = 1536
+    k, v = _cache(nkv, max_len, seed=nh * 31 + length)
+    q = randn_bf16((nh, 128), seed=length + nh, device="cuda")
+    out = torch.empty((nh, 128), dtype=torch.bfloat16, device="cuda")
+    pos = torch.tensor([length - 1], dtype=torch.long, device="cuda")
+    fastpath.kernel_attention(q, k, v, out, n_head=nh, n_kv=nkv, pos=pos, window=max_len, max_len=max_len)
+    want = orc.attention(to_bits(q), to_bits(k), to_bits(v), length, nh, nkv)
+    assert orc.relative_error(orc.bf16_to_f32(to_bits(out)), orc.bf16_to_f32(want)) < ATTN_TOL
+
+
 @pytest.mark.parametrize("max_len,length", [(16, 1), (16, 5), (16, 16), (100, 64), (100, 65), (100, 100),
                                             (300, 130), (300, 300)])
 def test_decode_attention_short_windows(max_len, length):
