@@ -308,6 +308,10 @@ struct ClusterSmem {
   float wm[cthreads<G>() / 32][G], wl[cthreads<G>() / 32][G];  // and its max and sum
   float part_acc[G][kD];
   float part_m[G], part_l[G];
+  // the cluster merge's inbox: slot r holds what rank r pushed (its output
+  // partial for this CTA's share of the outputs, its max and sum per head)
+  float in_acc[8][G * kD];
+  float in_m[8][G], in_l[8][G];
   unsigned long long bar[kCStages];
   // the fused q/k norm + rotary prologue (QkvIn)
   float sx[2][kD];
@@ -351,6 +355,13 @@ __device__ __forceinline__ uint32_t cluster_size() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Store v at the address `local` names in the shared memory of cluster rank `rank`.
+__device__ __forceinline__ void st_cluster_f32(float* local, uint32_t rank, float v) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(sm_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+
 __device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(sm_u32(local)), "r"(rank));
@@ -649,6 +660,17 @@ __global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel
       sm.part_m[h] = M;
       sm.part_l[h] = den;
     }
+    if (C > 1) {
+      // push this partial to the rank that merges output i, and the head's
+      // max and sum to every rank (they arrive before the cluster barrier)
+      // the owner of i: the largest q with floor(q E / C) <= i (the merge's shares)
+      st_cluster_f32(&sm.in_acc[rank][i], (uint32_t)(((long long)(i + 1) * C - 1) / (G * kD)), num);
+      if (d == 0)
+        for (uint32_t q = 0; q < C; ++q) {
+          st_cluster_f32(&sm.in_m[rank][h], q, M);
+          st_cluster_f32(&sm.in_l[rank][h], q, den);
+        }
+    }
   }
   if (C == 1) {
     // One CTA per KV head: its partial is the result (the merge below with a
@@ -661,35 +683,28 @@ __global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel
     }
     return;
   }
+  // Every rank's pushes land before the barrier completes (release / acquire);
+  // after it each CTA reads only its own shared memory, so no CTA waits for
+  // another to finish reading before it may exit.
   cluster_sync();
   {
     // Each CTA of the cluster merges its share of the (head, dimension)
-    // outputs: all remote loads are issued before any is used (one round trip).
+    // outputs from the partials the ranks pushed, in rank order.
     const int E = G * kD, lo = (int)(rank * E / C), hi = (int)((rank + 1) * E / C);
     for (int i = lo + tid; i < hi; i += kCT) {
       const int h = i / kD, d = i % kD;
-      float mr[16], lr[16], ar[16];
-#pragma unroll
-      for (uint32_t r = 0; r < 16; ++r) {
-        const bool in = r < C;
-        mr[r] = in ? ld_cluster_f32(&sm.part_m[h], r) : -INFINITY;
-        lr[r] = in ? ld_cluster_f32(&sm.part_l[h], r) : 0.f;
-        ar[r] = in ? ld_cluster_f32(&sm.part_acc[h][d], r) : 0.f;
-      }
       float M = -INFINITY;
-#pragma unroll
-      for (int r = 0; r < 16; ++r) M = fmaxf(M, mr[r]);
+      for (uint32_t r = 0; r < C; ++r) M = fmaxf(M, sm.in_m[r][h]);
       float num = 0.f, den = 0.f;
-#pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        const float w = (mr[r] == -INFINITY) ? 0.f : expf(mr[r] - M);
-        den = fmaf(lr[r], w, den);
-        num = fmaf(ar[r], w, num);
+      for (uint32_t r = 0; r < C; ++r) {
+        const float m = sm.in_m[r][h];
+        const float w = (m == -INFINITY) ? 0.f : expf(m - M);
+        den = fmaf(sm.in_l[r][h], w, den);
+        num = fmaf(sm.in_acc[r][i], w, num);
       }
       out[(size_t)(kh * G + h) * kD + d] = f2act<F16>(num / den);
     }
   }
-  cluster_sync();  // partials stay alive until CTA 0 has read them
 }
 
 }  // namespace
