@@ -111,6 +111,41 @@ def test_other_entry_points_reject_bad_arguments():
     assert L.nf4b_dequantize(None, p, None) == -1
 
 
+def test_misaligned_element_pointers_are_refused_on_the_host():
+    """Every pointer a kernel dereferences is checked for its element's
+    alignment (2 bytes for bf16/fp16, 4 for an fp32 rotary table, 8 for int64
+    positions, steps and token ids) and refused with NF4B_ERR_ALIGN before any
+    device work: a C caller's misaligned pointer becomes a status, not a fault.
+    Every call below is one the host must refuse."""
+    L = _lib.lib()
+    buf = ctypes.create_string_buffer(1 << 16)
+    p = (ctypes.addressof(buf) + 255) // 256 * 256          # 256-byte aligned
+    odd, two, four = p + 1, p + 2, p + 4                    # aligned to 1, 2 and 4 bytes
+    ALIGN = _lib_err("ALIGN")
+    assert L.nf4b_rms_norm(odd, p, p, 1, 8, 1e-6, None) == ALIGN
+    assert L.nf4b_rms_norm(p, odd, p, 1, 8, 1e-6, None) == ALIGN
+    assert L.nf4b_rope(p, two, _lib.NF4B_F32, p, 1, 1, 1, 8, None) == ALIGN       # fp32 table
+    assert L.nf4b_rope(p, odd, _lib.NF4B_BF16, p, 1, 1, 1, 8, None) == ALIGN
+    assert L.nf4b_qk_rope_kv(p, None, None, 1e-6, p, 2, four, p, p, p, 32, 8, 128, 16, None) == ALIGN  # pos
+    assert L.nf4b_qk_rope_kv(p, None, None, 1e-6, two, 0, p, p, p, p, 32, 8, 128, 16, None) == ALIGN  # freqs
+    assert L.nf4b_qk_rope_kv(odd, None, None, 1e-6, p, 2, p, p, p, p, 32, 8, 128, 16, None) == ALIGN  # qkv
+    assert L.nf4b_decode_attention(p, p, p, four, None, p, 32, 8, 128, 16, 16, p, 1 << 20, None) == ALIGN
+    assert L.nf4b_decode_attention(p, p, p, p, None, odd, 32, 8, 128, 16, 16, p, 1 << 20, None) == ALIGN
+    assert L.nf4b_qkv_attention(odd, None, None, 1e-6, p, 2, p, p, p, p, p, 32, 8, 128, 16, 16, p, 1 << 20,
+                                None) == ALIGN
+    assert L.nf4b_qkv_attention(p, None, None, 1e-6, p, 2, four, p, p, p, p, 32, 8, 128, 16, 16, p, 1 << 20,
+                                None) == ALIGN
+    need = L.nf4b_sample_workspace_size(1000)
+    assert 0 < need <= (1 << 16) - 512
+    assert L.nf4b_sample(p, 1000, 1.0, 0.9, 50, 1, four, p + 256, p + 256, need, None) == ALIGN  # step
+    assert L.nf4b_sample(p, 1000, 1.0, 0.9, 50, 1, p, four, p + 256, need, None) == ALIGN        # out
+    assert L.nf4b_frame_select(four, p, p, 4, 0, 16, p, p, 8, p, None) == ALIGN
+    assert L.nf4b_frame_select(p, p, p, 4, 0, 16, four, p, 8, p, None) == ALIGN
+    assert L.nf4b_frame_advance(p, 16, p, 16, 2, four, 8, p, p, 4, p, p, None) == ALIGN
+    assert L.nf4b_frame_advance(p, 16, p, 16, 2, p, 8, p, p, 4, p, four, None) == ALIGN
+    assert "aligned" in _lib.last_error()
+
+
 def test_activation_dtypes_are_checked_on_the_host():
     """bf16 (0 or NF4B_BF16) and fp16 (NF4B_F16) are the activation types;
     anything else is NF4B_ERR_DTYPE before any device work."""

@@ -57,6 +57,10 @@ int log2i(int v) {
   return s;
 }
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+// Rotary tables are read one element at a time: 4-byte fp32 or 2-byte fp16/bf16.
+bool freqs_aligned(const void* f, int freqs_dtype) { return aligned(f, freqs_dtype == NF4B_F32 ? 4 : 2); }
+// Device int64 scalars and vectors (positions, step counters, token ids); null passes.
+bool i64_aligned(const int64_t* p) { return aligned(p, 8); }
 
 int check_device() {
   static int checked[64] = {};  // 0 unknown, 1 ok, -1 bad
@@ -394,8 +398,8 @@ extern "C" int nf4b_gemm_qkv_rope(const nf4b_weight* w, const void* x, void* y, 
     return fail(NF4B_ERR_SHAPE, "n_out %d is not (%d + 2 x %d) heads of 128", w->n_out, rk->n_head, rk->n_kv);
   if (!aligned(x, 16)) return fail(NF4B_ERR_ALIGN, "x is not 16-byte aligned");
   if (!aligned(y, 2) || !aligned(rk->q_out, 2) || !aligned(rk->k_cache, 2) || !aligned(rk->v_cache, 2) ||
-      !aligned(rk->pos, 8))
-    return fail(NF4B_ERR_ALIGN, "y/q/cache not 2-byte aligned or pos not 8-byte aligned");
+      !i64_aligned(rk->pos) || !freqs_aligned(rk->freqs, rk->freqs_dtype))
+    return fail(NF4B_ERR_ALIGN, "y/q/cache not 2-byte aligned, pos not 8-byte aligned or freqs misaligned");
   if ((st = check_device())) return st;
   return gemv_call(w, nullptr, x, y, 1, NF4B_EPI_NONE, nullptr, workspace, workspace_bytes, opts,
                    reinterpret_cast<cudaStream_t>(stream), rk);
@@ -683,8 +687,8 @@ extern "C" int nf4b_sample(const void* logits, int vocab, float temperature, flo
   if (workspace == nullptr || workspace_bytes < need)
     return fail(NF4B_ERR_WORKSPACE, "sampler workspace of %zu bytes needed, %zu given", need,
                 workspace ? workspace_bytes : (size_t)0);
-  if (!aligned(workspace, 256) || !aligned(logits, 2) || !aligned(out, 8))
-    return fail(NF4B_ERR_ALIGN, "workspace/logits/out misaligned");
+  if (!aligned(workspace, 256) || !aligned(logits, 2) || !i64_aligned(out) || !i64_aligned(step))
+    return fail(NF4B_ERR_ALIGN, "workspace/logits/out/step misaligned");
   int st = check_device();
   if (st) return st;
   return launch_status(launch_sampler(static_cast<const uint16_t*>(logits), vocab, temperature, top_p, top_k, seed,
@@ -716,6 +720,8 @@ extern "C" int nf4b_frame_select(const int64_t* main_tok, const int64_t* high_to
     return fail(NF4B_ERR_SHAPE, "recent window %d, codebook size %lld, dim %d (dim %% 8 == 0)", n_recent,
                 codebook_size, dim);
   if (!aligned(fast_emb, 16) || !aligned(h, 16)) return fail(NF4B_ERR_ALIGN, "fast_emb/h not 16-byte aligned");
+  if (!i64_aligned(main_tok) || !i64_aligned(high_tok) || !i64_aligned(recent) || !i64_aligned(tokens))
+    return fail(NF4B_ERR_ALIGN, "token ids not 8-byte aligned");
   int st = check_device();
   if (st) return st;
   return launch_status(launch_frame_select(main_tok, high_tok, recent, n_recent, sem_begin, codebook_size, tokens,
@@ -735,6 +741,8 @@ extern "C" int nf4b_frame_advance(const void* sem_emb, long long vocab, const vo
     return fail(NF4B_ERR_SHAPE, "vocab %lld, codebooks %d x %lld, dim %d, recent %d", vocab, n_codebooks,
                 codebook_size, dim, n_recent);
   if (!aligned(sem_emb, 2) || !aligned(cb_emb, 2) || !aligned(x, 2)) return fail(NF4B_ERR_ALIGN, "bf16 misaligned");
+  if (!i64_aligned(tokens) || !i64_aligned(recent) || !i64_aligned(pos) || !i64_aligned(step))
+    return fail(NF4B_ERR_ALIGN, "tokens/recent/pos/step not 8-byte aligned");
   int st = check_device();
   if (st) return st;
   return launch_status(launch_frame_advance(static_cast<const uint16_t*>(sem_emb), vocab,
@@ -790,6 +798,8 @@ int nf4b_rms_norm_ex(const void* x, const void* weight, void* y, int rows, int w
   if (x == nullptr || weight == nullptr || y == nullptr) return fail(NF4B_ERR_ARG, "null pointer");
   if (rows <= 0 || width <= 0) return fail(NF4B_ERR_SHAPE, "empty input %dx%d", rows, width);
   if (!(eps >= 0.f)) return fail(NF4B_ERR_ARG, "eps must be >= 0");
+  if (!aligned(x, 2) || !aligned(weight, 2) || !aligned(y, 2))
+    return fail(NF4B_ERR_ALIGN, "x/weight/y not 2-byte aligned");
   int st = check_device();
   if (st) return st;
   return launch_status(
@@ -813,6 +823,8 @@ int nf4b_rope_ex(const void* x, const void* freqs, int freqs_dtype, void* y, int
     return fail(NF4B_ERR_SHAPE, "bad rotary shape (%d,%d,%d,%d)", batch, seq, heads, head_dim);
   if (freqs_dtype < NF4B_F32 || freqs_dtype > NF4B_BF16)
     return fail(NF4B_ERR_DTYPE, "unknown freqs dtype %d", freqs_dtype);
+  if (!aligned(x, 2) || !aligned(y, 2) || !freqs_aligned(freqs, freqs_dtype))
+    return fail(NF4B_ERR_ALIGN, "x/y not 2-byte aligned or freqs misaligned");
   int st = check_device();
   if (st) return st;
   const long long pairs = (long long)batch * seq * heads * head_dim / 2;
@@ -844,6 +856,9 @@ int nf4b_qk_rope_kv_ex(const void* qkv, const void* q_norm_w, const void* k_norm
     return fail(NF4B_ERR_ARG, "q and k norm weights must both be given or both be null");
   if (freqs_dtype < NF4B_F32 || freqs_dtype > NF4B_BF16)
     return fail(NF4B_ERR_DTYPE, "unknown freqs dtype %d", freqs_dtype);
+  if (!aligned(qkv, 2) || !aligned(q_norm_w, 2) || !aligned(k_norm_w, 2) || !aligned(q_out, 2) ||
+      !aligned(k_cache, 2) || !aligned(v_cache, 2) || !i64_aligned(pos) || !freqs_aligned(freqs, freqs_dtype))
+    return fail(NF4B_ERR_ALIGN, "activations/caches not 2-byte aligned, pos not 8-byte aligned or freqs misaligned");
   int st = check_device();
   if (st) return st;
   return launch_status(
@@ -888,6 +903,7 @@ int nf4b_decode_attention_ex(const void* q, const void* k_cache, const void* v_c
   if (window <= 0 || window > max_len) return fail(NF4B_ERR_SHAPE, "window %d outside [1, %d]", window, max_len);
   if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16))
     return fail(NF4B_ERR_ALIGN, "q / caches not 16-byte aligned");
+  if (!aligned(out, 2) || !i64_aligned(pos)) return fail(NF4B_ERR_ALIGN, "out not 2-byte or pos not 8-byte aligned");
   AttnPlan plan;
   attn_plan(n_head, head_dim, window, &plan);
   const size_t need = plan.counter_bytes + plan.partial_bytes;
@@ -937,6 +953,9 @@ int nf4b_qkv_attention_ex(const void* qkv, const void* q_norm_w, const void* k_n
     return fail(NF4B_ERR_DTYPE, "unknown freqs dtype %d", freqs_dtype);
   if (!aligned(q_scratch, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16))
     return fail(NF4B_ERR_ALIGN, "q scratch / caches not 16-byte aligned");
+  if (!aligned(qkv, 2) || !aligned(q_norm_w, 2) || !aligned(k_norm_w, 2) || !aligned(out, 2) || !i64_aligned(pos) ||
+      !freqs_aligned(freqs, freqs_dtype))
+    return fail(NF4B_ERR_ALIGN, "qkv/norm weights/out not 2-byte aligned, pos not 8-byte aligned or freqs misaligned");
   AttnPlan plan;
   attn_plan(n_head, head_dim, window, &plan);
   const size_t need = plan.counter_bytes + plan.partial_bytes;
