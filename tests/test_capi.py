@@ -144,6 +144,12 @@ def test_misaligned_element_pointers_are_refused_on_the_host():
     assert L.nf4b_frame_advance(p, 16, p, 16, 2, four, 8, p, p, 4, p, p, None) == ALIGN
     assert L.nf4b_frame_advance(p, 16, p, 16, 2, p, 8, p, p, 4, p, four, None) == ALIGN
     assert "aligned" in _lib.last_error()
+    # the wqkv GEMV's fused rotary store: 4 query heads + 2 x 1 KV head of 128 outputs
+    w, _keep = _weight(n_out=(4 + 2) * 128, k_in=256)
+    rk = _lib.RopeKv(two, _lib.NF4B_F32, p, p, p, p, 4, 1, 16)           # fp32 table on 2 bytes
+    assert L.nf4b_gemm_qkv_rope(ctypes.byref(w), p, p, ctypes.byref(rk), p, 1 << 16, None, None) == ALIGN
+    rk = _lib.RopeKv(p, _lib.NF4B_BF16, four, p, p, p, 4, 1, 16)         # pos on 4 bytes
+    assert L.nf4b_gemm_qkv_rope(ctypes.byref(w), p, p, ctypes.byref(rk), p, 1 << 16, None, None) == ALIGN
 
 
 def test_activation_dtypes_are_checked_on_the_host():
