@@ -423,6 +423,10 @@ __global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel
   const int kh = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t rank = cluster_rank(), C = cluster_size();
+  // A CTA may store into another CTA's shared memory only once every CTA of
+  // the cluster is running: every thread arrives here and waits just before
+  // the merge's first push, by when the others have long arrived.
+  if (C > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
   pdl_wait();  // the new K/V row and q come from the previous kernel
   // The next kernel (the wo GEMV) may be scheduled now: its CTAs load their
@@ -643,6 +647,7 @@ __global__ void __launch_bounds__(cthreads<G>()) decode_attention_cluster_kernel
     }
   }
   __syncthreads();
+  if (C > 1) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA is running
   for (int i = tid; i < G * kD; i += kCT) {
     const int h = i / kD, d = i % kD;
     float M = -INFINITY;
