@@ -362,14 +362,6 @@ __device__ __forceinline__ void st_cluster_f32(float* local, uint32_t rank, floa
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
 
-__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(sm_u32(local)), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
-}
-
 // One 128-wide row per half of the first 256 threads (threads 0-127: half 0,
 // 128-255: half 1; the others only join the barriers)
 // with qk_rope_kv's arithmetic: RMSNorm with this half's weight w (none when
