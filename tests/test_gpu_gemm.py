@@ -1,5 +1,7 @@
-"""The tcgen05 GEMM (more than 32 activation rows: batched decode M=64 and
-prefill M=256..1024) against the oracle (B200 only).
+"""The tcgen05 GEMM (every call of more than 8 activation rows; here 33..1024
+rows: batched decode M=64 and prefill M=256..1024, BASELINE config 3, and
+ragged counts) against the oracle (B200 only). 9-32 rows through the same
+GEMM are in test_gpu_kernels.py::test_rows_match_the_oracle.
 
 Its dequantised tiles are bit-exact bf16(NF4[q] * scale), so its outputs
 differ from the oracle's exactly-accumulated product only by fp32

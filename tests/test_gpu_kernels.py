@@ -72,7 +72,7 @@ def test_dequantize_is_bit_exact(shape, nested, bs):
 
 
 # --------------------------------------------------------------------------
-# streaming GEMV (rows <= 32) and tcgen05 GEMM (rows > 32)
+# streaming GEMV (rows <= 8) and tcgen05 GEMM (rows > 8)
 # --------------------------------------------------------------------------
 
 

@@ -305,8 +305,6 @@ cudaError_t launch_dequant(const DequantParams& p, cudaStream_t stream);
 
 // ---- tcgen05 GEMM (nf4_gemm_tc.cu) -----------------------------------------
 
-constexpr int GEMM_MIN_ROWS = 33;  // rows above GEMV_MAX_ROWS go to the GEMM
-
 struct GemmParams {
   const uint8_t* packed;
   const uint8_t* a8;
