@@ -1046,8 +1046,8 @@ def run_reference(args):
 # two. With `--time` it instead replays the launches from a CUDA graph and
 # prints CUDA-event timings (never under a profiler).
 #
-# kernels: gemv (M rows <= 32), gated (the W1/W3 gate, M <= 4), gemm (tcgen05,
-# M > 32), head (a bf16 output head, `--n` ids x `--k`), attention (decode,
+# kernels: gemv (M rows <= 8), gated (the W1/W3 gate, M <= 8), gemm (tcgen05,
+# M > 8), head (a bf16 output head, `--n` ids x `--k`), attention (decode,
 # qk_rope_kv + attention at a given cache length), prefill (the seven S2-Pro
 # projections at M rows through the GEMM, TFLOP/s), dualar (the config-5 frame
 # graph: `--frames` replays between cudaProfilerStart/Stop, for an
@@ -1253,7 +1253,7 @@ def run_case(a) -> None:
 
     assert nf4gemv.available()
     if a.case in ("gemv", "gemm"):
-        rows = a.rows if a.case == "gemv" else max(a.rows, 33)
+        rows = a.rows if a.case == "gemv" else max(a.rows, 9)
         run_matmul(a.n, a.k, rows, a.copies, a.launches, not a.plain, a.time)
     elif a.case == "prefill":
         run_prefill(a.rows)

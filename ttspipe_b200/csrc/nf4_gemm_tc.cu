@@ -1,4 +1,4 @@
-// NF4 GEMM for prefill and batched decode (more than 32 activation rows) on
+// NF4 GEMM for prefill and batched decode (more than 8 activation rows) on
 // the sm_100a tensor cores: tcgen05.mma with TMEM accumulators.
 //
 // The reference has no large-row kernel: it slices a prompt into 32-row
