@@ -94,6 +94,22 @@ def test_workspace_size_grows_with_rows_and_is_zero_for_the_gemm_path():
     assert L.nf4b_decode_attention_workspace_size(32, 128, 2048) > 0
 
 
+@pytest.mark.parametrize("n,k", [(1024, 2560), (9728, 2560), (6144, 2560), (2560, 9728)])
+def test_prepare_sizes_the_decode_workspace_for_every_decode_row_count(n, k):
+    """`prepare` sizes the shared decode workspace once, before any capture; it
+    must cover 1..MAX_N rows, whose largest need may come from the GEMV's
+    partial sums (few rows) rather than the GEMM's split-K sums (MAX_N rows)."""
+    from ttspipe_b200 import nf4gemv
+
+    w, _keep = _weight(n_out=n, k_in=k, nested=1)
+    w.absmax_code = w.code2 = w.absmax
+    size = _lib.lib().nf4b_gemm_workspace_size
+    needs = [int(size(ctypes.byref(w), r)) for r in range(1, nf4gemv.MAX_N + 1)]
+    assert nf4gemv.decode_workspace_bytes(w) == max(needs) > 0
+    if (n, k) in ((1024, 2560), (9728, 2560)):
+        assert max(needs) > needs[-1]       # sizing for MAX_N rows alone would fall short
+
+
 def test_other_entry_points_reject_bad_arguments():
     L = _lib.lib()
     buf = ctypes.create_string_buffer(4096 + 16)

@@ -36,7 +36,10 @@ from ttspipe_b200.quant import NF4_CODE  # noqa: F401 - part of the reference's 
 
 logger = logging.getLogger(__name__)
 
-#: Rows one GEMV launch takes; more rows go to the tensor-core GEMM in ONE launch.
+#: The reference's rows per launch (app/engine/nf4gemv.py:71, :460). Here any
+#: row count is one launch (1..8 rows the GEMV, more the tensor-core GEMM);
+#: MAX_N bounds the decode-sized calls, which share the workspace `prepare`
+#: sizes and captured decode graphs point at.
 MAX_N = 32
 
 #: Epilogues `matmul` can fold into the kernel's store (app/engine/nf4gemv.py:424).
@@ -75,6 +78,14 @@ def available() -> bool:
                 logger.warning("nf4 kernels unavailable: %s", exc)
             _checked = True
     return _unavailable is None
+
+
+def decode_workspace_bytes(desc) -> int:
+    """Workspace bytes that cover every decode-sized call (1..MAX_N rows) of
+    the weight `desc` describes: the GEMV's partial sums (1..8 rows) can
+    outgrow the GEMM's split-K sums at MAX_N rows."""
+    size = _lib.lib().nf4b_gemm_workspace_size
+    return max(int(size(ctypes.byref(desc), rows)) for rows in range(1, MAX_N + 1))
 
 
 def _workspace(device, nbytes: int, kind: str = "gemv"):
@@ -188,8 +199,7 @@ def prepare(module) -> bool:
     module._nf4_fast = {"desc": desc, "held": held, "M": out_f, "K": in_f,
                         "nested": bool(getattr(qs, "nested", False))}
     if available():
-        ws = _lib.lib().nf4b_gemm_workspace_size(ctypes.byref(desc), MAX_N)
-        _workspace(weight.device, int(ws))
+        _workspace(weight.device, decode_workspace_bytes(desc))
     _stats["layers"] += 1
     return True
 
