@@ -4,7 +4,8 @@ The reference ships its CPU NF4 path as a C++ source string inside
 ``app/engine/nf4cpu.py`` (``_SOURCE``, lines 51-781: ``nf4_gemv``, ``nf4_amx``,
 ``decode_block``, ``prefill_block``). This recipe reads that string from the
 read-only reference checkout, compiles it with ``g++`` through
-``torch.utils.cpp_extension.load_inline`` into a scratch directory under /tmp,
+``torch.utils.cpp_extension.load_inline`` into a scratch directory inside
+``oracle/_ref/`` (removed afterwards; the compilers' temporary files go there too),
 and copies only the resulting extension module into ``oracle/_ref/``. Nothing
 from the reference is written into the repository's tracked files.
 
@@ -38,6 +39,30 @@ HERE = Path(__file__).resolve().parent
 REF_DIR = HERE / "_ref"
 MODULE = "nf4cpu_ref"
 FUNCTIONS = ["nf4_gemv", "nf4_amx", "amx_available", "decode_block", "prefill_block"]
+
+
+class _scratch:
+    """A temporary build directory inside oracle/_ref/ that is also TMPDIR
+    while it lives, so neither the build nor the compilers write outside the
+    repository."""
+
+    def __init__(self, prefix: str):
+        REF_DIR.mkdir(parents=True, exist_ok=True)
+        self._dir = tempfile.TemporaryDirectory(prefix=prefix, dir=REF_DIR)
+        self._old = None
+
+    def __enter__(self) -> str:
+        path = self._dir.__enter__()
+        self._old = os.environ.get("TMPDIR")
+        os.environ["TMPDIR"] = path
+        return path
+
+    def __exit__(self, *exc):
+        if self._old is None:
+            os.environ.pop("TMPDIR", None)
+        else:
+            os.environ["TMPDIR"] = self._old
+        return self._dir.__exit__(*exc)
 
 
 def so_path() -> Path | None:
@@ -98,7 +123,7 @@ def build(reference_root_dir: str | None = None, verbose: bool = False) -> Path:
     source = reference_source(reference_root_dir)
     os.environ["CXX"] = "/usr/bin/g++"
     REF_DIR.mkdir(parents=True, exist_ok=True)
-    with tempfile.TemporaryDirectory(prefix="nf4cpu_ref_") as tmp:
+    with _scratch("nf4cpu_ref_") as tmp:
         ext = load_inline(
             name=MODULE,
             cpp_sources=source,
@@ -189,7 +214,7 @@ def build_gpu(reference_root_dir: str | None = None, verbose: bool = False) -> P
                             f"return (int)cudaGetLastError(); }}")
     launcher = _LAUNCHER.replace("@DECLS@", "\n".join(decls)).replace("@DISPATCH@", "\n  ".join(dispatch))
     REF_DIR.mkdir(parents=True, exist_ok=True)
-    with tempfile.TemporaryDirectory(prefix="nf4mma_ref_") as tmp:
+    with _scratch("nf4mma_ref_") as tmp:
         cu = Path(tmp) / "nf4mma_ref.cu"
         cu.write_text("\n".join(parts) + launcher)
         out = REF_DIR / f"{GPU_MODULE}.so"

@@ -17,6 +17,10 @@ if str(ROOT) not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 GPU and libnf4b200.so")
+    # tmp_path directories stay inside the checkout (git-ignored) unless the
+    # caller chooses another place with --basetemp
+    if config.option.basetemp is None:
+        config.option.basetemp = str(ROOT / ".pytest_tmp")
 
 
 def pytest_collection_modifyitems(config, items):
