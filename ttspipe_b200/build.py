@@ -59,13 +59,14 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     BUILD.mkdir(exist_ok=True)
     cc = nvcc()
     extra = ["-Xptxas", "-v"] if ptxas_info else []
+    env = dict(os.environ, TMPDIR=str(BUILD))  # nvcc's intermediate files stay in the build folder
 
     def compile_one(src: Path) -> tuple[Path, str]:
         obj = BUILD / (src.stem + ".o")
         cmd = [cc, *ARCH, *NVCC_FLAGS, *extra, f"-I{INCLUDE}", f"-I{CSRC}", "-c", str(src), "-o", str(obj)]
         if verbose:
             print(" ".join(cmd), flush=True)
-        r = subprocess.run(cmd, capture_output=True, text=True)
+        r = subprocess.run(cmd, capture_output=True, text=True, env=env)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stdout}\n{r.stderr}")
         return obj, r.stderr
@@ -78,7 +79,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     objs = [str(o) for o, _ in results]
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [cc, *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *objs]
-    r = subprocess.run(cmd, capture_output=True, text=True)
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
     os.replace(tmp, LIB)
