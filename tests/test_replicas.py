@@ -7,6 +7,9 @@ from __future__ import annotations
 
 import os
 import socket
+import subprocess
+import sys
+from pathlib import Path
 
 import pytest
 import torch
@@ -72,3 +75,15 @@ def test_seconds_are_reduced_as_the_max_over_ranks():
 def test_a_dead_replica_surfaces_as_an_error_not_a_hang():
     out = _spawn("dies")
     assert out[0].startswith("error:")
+
+
+def test_the_reference_arm_runs_on_rank_0_only():
+    """Launched under torchrun, `bench.py --impl reference` works on rank 0
+    alone: every other rank exits 0 at once, prints nothing and joins no
+    rendezvous (an unreachable master port would fail it)."""
+    root = Path(__file__).resolve().parent.parent
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1", MASTER_ADDR="127.0.0.1", MASTER_PORT="1")
+    r = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference", "--steps", "1",
+                        "--warmup", "3"], capture_output=True, text=True, timeout=180, cwd=root, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip() == ""
