@@ -8,7 +8,12 @@
  *
  * Conventions shared by every entry point:
  *   - All tensor pointers are device pointers, contiguous, row-major.
- *   - Activations are bf16 (uint16 bit patterns); accumulation is fp32.
+ *   - Activations are bf16 (uint16 bit patterns) unless an _ex call or
+ *     nf4b_gemm_opts.dtype selects fp16; accumulation is fp32.
+ *   - Alignment is checked on the host (NF4B_ERR_ALIGN, nothing launched):
+ *     packed weights and matmul inputs 16 bytes, workspaces 256 bytes, other
+ *     bf16/fp16 arrays 2 bytes, fp32 rotary tables 4, int64 values 8; each
+ *     entry point notes any stricter rule.
  *   - `stream` is a cudaStream_t (NULL = legacy default stream). Nothing here
  *     synchronises the host or allocates device memory, so every call can be
  *     captured into a CUDA graph.
