@@ -168,6 +168,34 @@ def test_misaligned_element_pointers_are_refused_on_the_host():
     assert L.nf4b_gemm_qkv_rope(ctypes.byref(w), p, p, ctypes.byref(rk), p, 1 << 16, None, None) == ALIGN
 
 
+def test_empty_inputs_and_sizes_past_each_maximum_are_refused_on_the_host():
+    """Empty inputs and sizes past an entry point's maximum return a status
+    before any device work: a 262144-entry vocabulary, 32 codebooks, 1024 KV
+    heads, 40 chained and 152 decode-step jobs (the persistent launches'
+    parameter blocks) and the dense head's four input widths."""
+    L = _lib.lib()
+    buf = ctypes.create_string_buffer(1 << 16)
+    p = (ctypes.addressof(buf) + 255) // 256 * 256
+    SHAPE, ARG = _lib_err("SHAPE"), _lib_err("ARG")
+    assert L.nf4b_sample_workspace_size(0) == 0
+    assert L.nf4b_sample_workspace_size(262144) > 0
+    assert L.nf4b_sample_workspace_size(262145) == 0
+    assert L.nf4b_sample(p, 262145, 1.0, 0.9, 50, 1, p, p, p, 1 << 16, None) == SHAPE
+    assert L.nf4b_sample(p, 0, 1.0, 0.9, 50, 1, p, p, p, 1 << 16, None) == SHAPE
+    assert L.nf4b_frame_advance(p, 16, p, 16, 33, p, 8, p, p, 4, p, p, None) == SHAPE
+    assert L.nf4b_decode_attention(p, p, p, p, None, p, 1025, 1025, 128, 16, 16, p, 1 << 20, None) == SHAPE
+    jobs = (_lib.ChainJob * 153)()
+    assert L.nf4b_gemv_chain(jobs, 41, 1, p, 1 << 16, None) == SHAPE
+    assert L.nf4b_gemv_chain(jobs, 0, 1, p, 1 << 16, None) == ARG
+    assert L.nf4b_gemv_chain_workspace_size(jobs, 41, 1) == 0
+    assert L.nf4b_decode_step(jobs, 153, 1, p, 1 << 16, None) == SHAPE
+    assert L.nf4b_decode_step(None, 1, 1, p, 1 << 16, None) == ARG
+    assert L.nf4b_decode_step_workspace_size(jobs, 153, 1) == 0
+    assert L.nf4b_embed_rows(p, 16, p, 0, 8, p, None) == SHAPE
+    assert L.nf4b_dense_gemv(p, p, p, 16, 3072, None, 0.0, None) == SHAPE
+    assert L.nf4b_dense_gemv(p, p, p, 0, 2560, None, 0.0, None) == SHAPE
+
+
 def test_activation_dtypes_are_checked_on_the_host():
     """bf16 (0 or NF4B_BF16) and fp16 (NF4B_F16) are the activation types;
     anything else is NF4B_ERR_DTYPE before any device work."""
